@@ -1,0 +1,272 @@
+"""Index construction in the reference's exact on-device layout (build time, not the query path).
+
+The query kernels consume the dicts the reference builds (same keys, dtypes, byte layouts).  The reference builds them
+with CUDA, torch and faiss (`src/rev_fanardb.py:33-61`, `src/ideas_engine2.py:23-40`, `src/engine_cell.py:8-32`,
+`throughput/enginei8.py:19-27`, `throughput/s2lut.py:9-29`, `src/tiered.py:15-44`).  faiss is not available here, so the
+two places it is used (the 1-D Lloyd-Max codebooks behind `tiered.DIST`/`tiered.CB`, `src/tiered.py:6-10`) are computed
+from the Gaussian density directly; every other step follows the reference's recipe.  Layout produced:
+
+s1   : c [d] f32, off (numpy int64 [NC+1]), off_t int64 [NC+1], order int32 [N] (sorted position -> original id),
+       means16 [NC,d] f16, inv_mnorm [NC] f32, cen (= inv_mnorm)                              (`src/engine_cell.py:23,26-32`)
+i8   : Z int8 [N,R], zs f32 [N], Vr f32 [d,R], all in sorted-position order                  (`throughput/enginei8.py:19-27`)
+code : TS [(s,e,b)], rots [w x w f32], planes[t] uint8 [b,N,w/8] (bit 7-k of byte j = bit of coordinate 8j+k),
+       scale/sig f16 [T,N], V f32 [d,d], deltas {b: step}, cb_uniform {b: levels}            (`src/tiered.py:29-44`)
+trellis (optional): W1 f32 [d,R], tab f32 [2^L], alpha, words int32 [N,W], scale1 f16 [N]     (`src/rev_fanardb.py:33-61`)
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+G = 32  # coordinates per allocation group (`src/tiered.py:13`)
+
+
+# ----------------------------------------------------------------------------------------------- scalar quantisers
+def _phi(x):
+    return np.exp(-0.5 * x * x) / math.sqrt(2 * math.pi)
+
+
+def _Phi(x):
+    from scipy.special import ndtr
+    return ndtr(x)
+
+
+def lloyd_max(bits: int, iters: int = 20000):
+    """Lloyd-Max levels and MSE for a standard Gaussian (what `src/tiered.py:6-10` fits with faiss 1-D k-means)."""
+    n = 2 ** bits
+    from scipy.special import ndtri
+    lv = ndtri((np.arange(n) + 0.5) / n)
+    for _ in range(iters):
+        th = np.concatenate([[-np.inf], (lv[1:] + lv[:-1]) / 2, [np.inf]])
+        p = _Phi(th[1:]) - _Phi(th[:-1])
+        lv = (_phi(th[:-1]) - _phi(th[1:])) / np.maximum(p, 1e-300)
+    return lv.astype(np.float32), _gauss_mse(lv)
+
+
+def _gauss_mse(lv):
+    """E[(X - Q(X))^2] for X ~ N(0,1) with nearest-level quantiser lv (sorted)."""
+    lv = np.asarray(lv, np.float64)
+    th = np.concatenate([[-np.inf], (lv[1:] + lv[:-1]) / 2, [np.inf]])
+    a, b = th[:-1], th[1:]
+    Pa, Pb = _Phi(a), _Phi(b)
+    pa = np.where(np.isfinite(a), _phi(np.where(np.isfinite(a), a, 0)), 0.0)
+    pb = np.where(np.isfinite(b), _phi(np.where(np.isfinite(b), b, 0)), 0.0)
+    aa = np.where(np.isfinite(a), a, 0.0)
+    bb = np.where(np.isfinite(b), b, 0.0)
+    m0 = Pb - Pa                      # int phi
+    m1 = pa - pb                      # int x phi
+    m2 = (Pb - Pa) + aa * pa - bb * pb  # int x^2 phi
+    return float(np.sum(m2 - 2 * lv * m1 + lv * lv * m0))
+
+
+_LM_CACHE = {}
+
+
+def lloyd_table(bits: int):
+    """(levels, mse) of the Lloyd-Max quantiser, computed once per bit width."""
+    if bits not in _LM_CACHE:
+        _LM_CACHE[bits] = lloyd_max(bits)
+    return _LM_CACHE[bits]
+
+
+def dist(bits: int) -> float:
+    """Lloyd-Max MSE per bit width (the reference's `tiered.DIST`); DIST[0] = 1."""
+    return 1.0 if bits == 0 else lloyd_table(bits)[1]
+
+
+def uniform_delta(bits: int) -> float:
+    """Step of the MSE-best uniform quantiser on the reference's grid linspace(0.02, 2.5, 600) (`throughput/s2lut.py:9-16`);
+    the MSE is evaluated exactly on the Gaussian density instead of on 2M samples."""
+    mid = (2 ** bits - 1) / 2
+    best = None
+    for delta in np.linspace(0.02, 2.5, 600):
+        m = _gauss_mse((np.arange(2 ** bits) - mid) * delta)
+        if best is None or m < best[0]:
+            best = (m, float(delta))
+    return best[1]
+
+
+# ----------------------------------------------------------------------------------------------- building blocks
+def spherical_kmeans(X16, nlist, seed=0, sample=200_000, iters=15, chunk=50_000):
+    """Cell centroids as `src/ideas_engine2.py:27-33` (200k sample, random init, 15 iterations, argmax assignment)."""
+    dev = X16.device
+    N = X16.shape[0]
+    g = torch.Generator().manual_seed(seed)
+    samp = X16[torch.randperm(N, generator=g)[:min(sample, N)].to(dev)].float()
+    cen = samp[torch.randperm(len(samp), generator=g)[:nlist].to(dev)].clone()
+    for _ in range(iters):
+        a = torch.cat([(samp[j:j + chunk] @ cen.T).argmax(1) for j in range(0, len(samp), chunk)])
+        cen = torch.nn.functional.normalize(torch.zeros_like(cen).index_add_(0, a, samp) + 1e-9, dim=1)
+    return cen
+
+
+def assign_cells(X16, cen, chunk=100_000):
+    """order (sorted position -> id) and off (cell boundaries) as `src/ideas_engine2.py:35-36`."""
+    A = torch.cat([(X16[j:j + chunk].float() @ cen.T).argmax(1) for j in range(0, X16.shape[0], chunk)])
+    order = torch.argsort(A, stable=True)
+    off = torch.searchsorted(A[order], torch.arange(cen.shape[0] + 1, device=X16.device))
+    return order, off
+
+
+def cell_of_position(off_t, N):
+    return torch.searchsorted(off_t, torch.arange(N, device=off_t.device), right=True) - 1
+
+
+def cell_means(X16, order, off_t, chunk=65536):
+    """fp32 mean of each cell (`src/engine_cell.py:11-14`)."""
+    N, d = X16.shape
+    NC = len(off_t) - 1
+    cell = cell_of_position(off_t, N)
+    means = torch.zeros(NC, d, device=X16.device)
+    for j in range(0, N, chunk):
+        means.index_add_(0, cell[j:j + chunk], X16[order[j:j + chunk]].float())
+    means /= (off_t[1:] - off_t[:-1]).clamp(min=1).float()[:, None]
+    return means
+
+
+def pca_eigh(S):
+    ev, V = torch.linalg.eigh(torch.cov(S.T))
+    return ev.flip(0), V.flip(1).contiguous()
+
+
+def build_i8_codes(X16, order, off_t, means16, V, R=256, chunk=65536):
+    """int8 cell-residual codes (`throughput/enginei8.py:19-27`): Z = round(((x - m_c) @ Vr) / a), a = max|z| / 127."""
+    N = len(order)
+    means = means16.float()
+    cell = cell_of_position(off_t, N)
+    Vr = V[:, :R].contiguous()
+    Z = torch.empty(N, R, dtype=torch.int8, device=X16.device)
+    zs = torch.empty(N, device=X16.device)
+    for j in range(0, N, chunk):
+        x = X16[order[j:j + chunk]].float()
+        z = (x - means[cell[j:j + chunk]]) @ Vr
+        a = z.abs().amax(1).clamp(min=1e-12) / 127
+        Z[j:j + chunk] = torch.round(z / a[:, None]).clamp(-127, 127).to(torch.int8)
+        zs[j:j + chunk] = a
+    return Z, zs, Vr
+
+
+def allocate(lam, B, bmin=1, bmax=8):
+    """MSE water-filling bit allocation over 32-dim groups -> tiers (s, e, bits) (`src/tiered.py:19-27`)."""
+    d = len(lam)
+    NG = d // G
+    lamg = lam.reshape(NG, G).sum(1).cpu().numpy()
+    b = np.full(NG, bmin)
+    left = B - bmin * d
+    while left >= G:
+        gain = [lamg[i] * (dist(b[i]) - dist(b[i] + 1)) if b[i] < bmax else -1 for i in range(NG)]
+        i = int(np.argmax(gain))
+        b[i] += 1
+        left -= G
+    T, st = [], 0
+    for i in range(1, NG + 1):
+        if i == NG or b[i] != b[st]:
+            T.append((st * G, i * G, int(b[st])))
+            st = i
+    return T
+
+
+def pack_bits(bit):
+    """(n, w) bool -> (n, w/8) uint8, bit 7-k of byte j = coordinate 8j+k (`src/tiered.py:12`)."""
+    sh = torch.arange(7, -1, -1, device=bit.device, dtype=torch.uint8)
+    return ((bit.reshape(bit.shape[0], -1, 8).to(torch.uint8)) << sh).sum(2).to(torch.uint8)
+
+
+def tiered_build(X16, order, c, V, TS, CB, seed=0, chunk=16384):
+    """Tiered refinement code (`src/tiered.py:29-44`) with the codebook table CB[b] = (levels, thresholds)."""
+    dev = X16.device
+    N = len(order)
+    gen = torch.Generator(device=dev).manual_seed(100 + seed)
+    rots = [torch.linalg.qr(torch.randn(e - s, e - s, device=dev, generator=gen))[0] for s, e, _ in TS]
+    planes = [torch.empty(bb, N, (e - s) // 8, dtype=torch.uint8, device=dev) for s, e, bb in TS]
+    scale = torch.empty(len(TS), N, dtype=torch.float16, device=dev)
+    sig = torch.empty(len(TS), N, dtype=torch.float16, device=dev)
+    for j in range(0, N, chunk):
+        Z = (X16[order[j:j + chunk]].float() - c) @ V
+        n = len(Z)
+        for t, ((s, e, bb), P) in enumerate(zip(TS, rots)):
+            F = Z[:, s:e] @ P
+            nf = F.norm(dim=1).clamp(min=1e-12)
+            dt = e - s
+            Fu = F / nf[:, None] * dt ** 0.5
+            cb, th = CB[bb]
+            q = torch.bucketize(Fu, th)
+            Y = cb[q]
+            yn = Y.norm(dim=1)
+            ct = (Fu * Y).sum(1) / (yn * dt ** 0.5)
+            for p in range(bb):
+                planes[t][p, j:j + n] = pack_bits(((q >> (bb - 1 - p)) & 1).bool())
+            scale[t, j:j + n] = (nf / (ct * yn)).half()
+            sig[t, j:j + n] = (nf * torch.sqrt((1 - ct ** 2).clamp(min=0)) / (ct * (dt - 1) ** 0.5)).half()
+    nbytes = sum((e - s) * bb for s, e, bb in TS) / 8 + 4 * len(TS)
+    return dict(TS=TS, rots=rots, planes=planes, scale=scale, sig=sig, V=V, bytes=nbytes)
+
+
+def block_rotation(code):
+    """VP = V @ blockdiag(rots) (`throughput/s2lut.py:31-37`, `src/tiered_fused.py:46-52`)."""
+    V = code["V"]
+    d = V.shape[0]
+    D = torch.zeros(d, d, device=V.device)
+    for (s, e, _), P in zip(code["TS"], code["rots"]):
+        D[s:e, s:e] = P
+    return (V @ D).contiguous()
+
+
+# ----------------------------------------------------------------------------------------------- whole index
+def build_index(X16, nlist, R=256, refine_bits=None, seed=0, kmeans_sample=200_000, kmeans_iters=15,
+                uniform=True, lloyd=False):
+    """Build s1 + int8 codes + tiered refinement (uniform and/or Lloyd-Max codebooks) for base X16 [N,d] fp16.
+
+    Mirrors the reference's recipe end to end: global centre c from the first 50k rows (`src/rev_fanardb.py:37`),
+    spherical k-means cells (`src/ideas_engine2.py:27-36`), cell means and norms (`src/engine_cell.py:8-32`), int8 PCA
+    codes (`throughput/e_brute.py:8-10`, `throughput/enginei8.py:19-27`), tiered code over the PCA basis of normalised
+    residuals (`src/tiered.py:15-44`) with uniform codebooks (`throughput/s2lut.py:18-29`).
+    """
+    dev = X16.device
+    N, d = X16.shape
+    refine_bits = int(refine_bits or 2.5 * d)
+    with torch.no_grad():
+        c = X16[:50000].float().mean(0)
+        cen = spherical_kmeans(X16, nlist, seed, kmeans_sample, kmeans_iters)
+        order, off_t = assign_cells(X16, cen)
+        means = cell_means(X16, order, off_t)
+        means16 = means.half().contiguous()
+        nrm = means16.float().norm(dim=1).clamp(min=1e-12)
+        inv_mnorm = (1.0 / nrm).contiguous()
+        s1 = dict(c=c, off=off_t.cpu().numpy(), off_t=off_t, order=order.to(torch.int32).contiguous(),
+                  means16=means16, inv_mnorm=inv_mnorm, cen=inv_mnorm)
+        # int8 stage-1 codes over the PCA basis of mean-centred rows (every 10th row, mean of the first 200k)
+        mu = X16[:200000].float().mean(0)
+        _, Vp = pca_eigh(X16[::10].float() - mu)
+        Z, zs, Vr = build_i8_codes(X16, order, off_t, means16, Vp, R)
+        i8 = dict(Z=Z, zs=zs, Vr=Vr)
+        # tiered refinement: PCA of normalised residuals to c (first 50k rows)
+        S = X16[:50000].float() - c
+        S = S / S.norm(dim=1, keepdim=True)
+        lam, V = pca_eigh(S)
+        lam = lam.clamp(min=1e-12)
+        TS = allocate(lam, refine_bits)
+        codes = {}
+        if uniform:
+            deltas = {b: uniform_delta(b) for b in sorted({bb for _, _, bb in TS})}
+            CBu = {}
+            for b, dl in deltas.items():
+                lv = ((torch.arange(2 ** b, device=dev).float() - (2 ** b - 1) / 2) * dl)
+                CBu[b] = (lv, (lv[1:] + lv[:-1]) / 2)
+            cu = tiered_build(X16, order, c, V, TS, CBu, seed)
+            cu["deltas"] = deltas
+            cu["cb_uniform"] = {b: CBu[b][0] for b in deltas}
+            cu["VP"] = block_rotation(cu)
+            codes["uniform"] = cu
+        if lloyd:
+            CBl = {}
+            for b in sorted({bb for _, _, bb in TS}):
+                lv = torch.as_tensor(lloyd_table(b)[0], device=dev)
+                CBl[b] = (lv, (lv[1:] + lv[:-1]) / 2)
+            cl = tiered_build(X16, order, c, V, TS, CBl, seed)
+            cl["cbf"] = [CBl[bb][0].contiguous() for _, _, bb in TS]
+            cl["VP"] = block_rotation(cl)
+            codes["lloyd"] = cl
+    return s1, i8, codes
