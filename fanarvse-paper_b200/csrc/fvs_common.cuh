@@ -1,0 +1,155 @@
+// Shared device helpers of libfanar_b200 (sm_100a): order-preserving keys, block-wide radix select, bitonic sort.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
+
+#include "../../include/fanar_b200.h"
+
+#define FVS_CHECK_ARG(cond)            \
+    do {                               \
+        if (!(cond)) return FVS_EINVAL; \
+    } while (0)
+
+static inline int fvs_launch_status() {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? FVS_OK : (int)e;
+}
+
+// Raise a kernel's dynamic shared-memory limit once per (kernel, device); later calls (including calls made while a
+// stream is being captured into a CUDA graph) only read the cache.
+inline cudaError_t fvs_ensure_smem(const void* func, size_t bytes) {
+    if (bytes <= 48 * 1024) return cudaSuccess;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> done;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = done.find({func, dev});
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
+    e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (e == cudaSuccess) done[{func, dev}] = bytes;
+    return e;
+}
+
+namespace fvs {
+
+constexpr float kNeg = -1e30f;  // the reference's "empty" estimate (`throughput/enginei8.py:48,57`)
+
+// float -> uint32 with the same order (larger float, larger key); NaN is not expected on this path.
+__device__ __forceinline__ uint32_t f2o(float f) {
+    uint32_t u = __float_as_uint(f);
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float o2f(uint32_t k) {
+    uint32_t u = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
+    return __uint_as_float(u);
+}
+
+__device__ __forceinline__ int next_pow2(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+// Shared scratch of the block radix select: 256 histogram bins + the running (prefix, rank).
+struct SelectScratch {
+    unsigned hist[256];
+    unsigned long long prefix;
+    int rem;
+};
+
+// r-th largest (1-based, 1 <= r <= n) of n keys of KBITS bits (32 or 64) produced by key(i); MSB-first radix select,
+// 8 bits per pass.  All threads of the block must call it; returns the same key in every thread.
+template <int KBITS, typename KeyT, typename KeyFn>
+__device__ KeyT block_select_rth_largest(KeyFn key, int n, int r, SelectScratch& s) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    if (tid == 0) {
+        s.prefix = 0ull;
+        s.rem = r;
+    }
+    __syncthreads();
+#pragma unroll 1
+    for (int shift = KBITS - 8; shift >= 0; shift -= 8) {
+        for (int i = tid; i < 256; i += nt) s.hist[i] = 0;
+        __syncthreads();
+        const unsigned long long pre = s.prefix;
+        const unsigned long long hmask = (shift + 8 >= 64) ? 0ull : (~0ull << (shift + 8));
+        for (int i = tid; i < n; i += nt) {
+            unsigned long long k = (unsigned long long)key(i);
+            if ((k & hmask) == (pre & hmask)) atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+        }
+        __syncthreads();
+        if (tid < 32) {
+            // lane l owns bins 255-8l .. 248-8l (descending)
+            const int lane = tid;
+            unsigned c[8], sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                c[i] = s.hist[255 - 8 * lane - i];
+                sum += c[i];
+            }
+            unsigned incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const int rem = s.rem;
+            unsigned ball = __ballot_sync(0xffffffffu, incl >= (unsigned)rem);
+            int L = __ffs(ball) - 1;  // always found since the total equals the candidate count >= rem
+            if (lane == L) {
+                unsigned above = incl - sum;
+                int digit = 0;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    if (above + c[i] >= (unsigned)rem) {
+                        digit = 255 - 8 * lane - i;
+                        break;
+                    }
+                    above += c[i];
+                }
+                s.rem = rem - (int)above;
+                s.prefix = pre | ((unsigned long long)digit << shift);
+            }
+        }
+        __syncthreads();
+    }
+    KeyT res = (KeyT)s.prefix;
+    __syncthreads();  // every thread has read the result before the scratch is reused
+    return res;
+}
+
+// In-place descending bitonic sort of n (a power of two) 64-bit keys in shared memory.
+__device__ __forceinline__ void block_bitonic_desc(unsigned long long* a, int n) {
+    const int tid = threadIdx.x, nt = blockDim.x;
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = tid; i < n; i += nt) {
+                int ixj = i ^ j;
+                if (ixj > i) {
+                    unsigned long long x = a[i], y = a[ixj];
+                    bool desc = (i & k) == 0;
+                    if (desc ? (x < y) : (x > y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+}  // namespace fvs

@@ -1,0 +1,205 @@
+// Stage 2 of the throughput mode: per-query nibble lookup tables and the LUT-scored tiered refinement.
+//
+// `fvs_lut_build` replaces `_lut_kernel` + the tier sums of `luts_fused` (`throughput/s2lut.py:108-126`).
+// `fvs_lut_score` replaces `_score_lut` / `_tier_lut` (`throughput/s2lut.py:48-106`): one CTA per query holds the
+// query's table (D/4 x 16 entries, 12 KB at D = 1536 in fp16) in shared memory; each warp scores one candidate at a
+// time, its lanes striding over the tier's (plane, byte) pairs; the per-tier dot products are warp-reduced.
+#include <type_traits>
+
+#include "fvs_common.cuh"
+
+namespace fvs {
+
+constexpr int MAX_TIERS = 8;
+
+struct TierSet {
+    int T;
+    int s[MAX_TIERS], e[MAX_TIERS], bits[MAX_TIERS], kb[MAX_TIERS], loff[MAX_TIERS];
+    float delta[MAX_TIERS], mid[MAX_TIERS], pw[MAX_TIERS][8];
+    const uint8_t* planes[MAX_TIERS];
+};
+
+// ------------------------------------------------------------------------------------------------ LUT build
+template <bool HALF>
+__global__ void lut_build_kernel(const float* __restrict__ Zq, int ldz, int D, void* __restrict__ Lout, TierSet ts,
+                                 int B, float* __restrict__ qsum, float* __restrict__ qn2) {
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const float* z = Zq + (int64_t)q * ldz;
+    const int nent = (D / 4) * 16;
+    for (int idx = tid; idx < nent; idx += nt) {
+        const int n = idx >> 4, v = idx & 15;
+        // sum of the selected coordinates in order i = 0..3 (bits 3..0 of v), as acc += z_i * bit_i
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+            if ((v >> (3 - i)) & 1) acc = __fadd_rn(acc, z[4 * n + i]);
+        if (HALF)
+            reinterpret_cast<__half*>(Lout)[(int64_t)q * nent + idx] = __float2half_rn(acc);
+        else
+            reinterpret_cast<float*>(Lout)[(int64_t)q * nent + idx] = acc;
+    }
+    __shared__ float red[2][32];
+    const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+    for (int t = 0; t < ts.T; t++) {
+        float a = 0.f, b = 0.f;
+        for (int i = ts.s[t] + tid; i < ts.e[t]; i += nt) {
+            const float x = z[i];
+            a += x;
+            b += x * x;
+        }
+        a = warp_sum(a);
+        b = warp_sum(b);
+        if (lane == 0) {
+            red[0][warp] = a;
+            red[1][warp] = b;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            float sa = 0.f, sb = 0.f;
+            for (int w = 0; w < nw; w++) {
+                sa += red[0][w];
+                sb += red[1][w];
+            }
+            qsum[(int64_t)t * B + q] = sa;
+            qn2[(int64_t)t * B + q] = sb;
+        }
+        __syncthreads();
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ LUT score
+template <bool HALF>
+__global__ void __launch_bounds__(256) lut_score_kernel(const int64_t* __restrict__ pos, int B, int K,
+                                                        const float* __restrict__ qc, const void* __restrict__ L, int LW,
+                                                        TierSet ts, const __half* __restrict__ scale,
+                                                        const __half* __restrict__ sig, int64_t N,
+                                                        const float* __restrict__ qsum, const float* __restrict__ qn2,
+                                                        const int32_t* __restrict__ ncnt, float* __restrict__ est,
+                                                        float* __restrict__ sd) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const int lim = ncnt ? min(max(ncnt[q], 0), K) : K;
+    // dead candidates first (no table needed)
+    for (int i = lim + tid; i < K; i += blockDim.x) {
+        est[(int64_t)q * K + i] = kNeg;
+        sd[(int64_t)q * K + i] = 0.f;
+    }
+    if (lim == 0) return;
+    // stage the query's table
+    using E = typename std::conditional<HALF, __half, float>::type;
+    E* lut = reinterpret_cast<E*>(smem);
+    {
+        const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const E*>(L) + (int64_t)q * LW);
+        uint4* dst = reinterpret_cast<uint4*>(lut);
+        const int nv = LW * (int)sizeof(E) / 16;
+        for (int i = tid; i < nv; i += blockDim.x) dst[i] = src[i];
+    }
+    __syncthreads();
+    const float qcv = qc[q];
+    float qs_t[MAX_TIERS], qn_t[MAX_TIERS];
+#pragma unroll
+    for (int t = 0; t < MAX_TIERS; t++) {
+        qs_t[t] = t < ts.T ? qsum[(int64_t)t * B + q] : 0.f;
+        qn_t[t] = t < ts.T ? qn2[(int64_t)t * B + q] : 0.f;
+    }
+    for (int i = warp; i < lim; i += nw) {
+        const int64_t n = pos[(int64_t)q * K + i];
+        float acc = qcv, var = 0.f;
+#pragma unroll 1
+        for (int t = 0; t < ts.T; t++) {
+            const int kb = ts.kb[t], nbytes = ts.bits[t] * kb;
+            const uint8_t* pl = ts.planes[t];
+            const E* lt = lut + ts.loff[t];
+            float a = 0.f;
+            for (int idx = lane; idx < nbytes; idx += 32) {
+                const int p = idx / kb, j = idx - p * kb;
+                const uint32_t byt = __ldg(pl + ((int64_t)p * N + n) * kb + j);
+                const float h = (float)lt[(2 * j) * 16 + (byt >> 4)];
+                const float l = (float)lt[(2 * j + 1) * 16 + (byt & 15u)];
+                a += (h + l) * ts.pw[t][p];
+            }
+            a = warp_sum(a);
+            const float at = ts.delta[t] * (a - ts.mid[t] * qs_t[t]);
+            const float s = __half2float(scale[(int64_t)t * N + n]);
+            const float g = __half2float(sig[(int64_t)t * N + n]);
+            acc = acc + at * s;
+            var = var + qn_t[t] * g * g;
+        }
+        if (lane == 0) {
+            est[(int64_t)q * K + i] = acc;
+            sd[(int64_t)q * K + i] = sqrtf(var);
+        }
+    }
+}
+
+static int make_tiers(TierSet& ts, int T, const int32_t* s, const int32_t* e, const int32_t* bits,
+                      const float* delta, const uint8_t* const* planes) {
+    if (T < 1 || T > MAX_TIERS) return FVS_ERANGE;
+    ts.T = T;
+    int loff = 0;
+    for (int t = 0; t < T; t++) {
+        if (e[t] <= s[t] || (e[t] - s[t]) % 8 != 0) return FVS_EINVAL;
+        ts.s[t] = s[t];
+        ts.e[t] = e[t];
+        ts.bits[t] = bits ? bits[t] : 0;
+        if (bits && (bits[t] < 1 || bits[t] > 8)) return FVS_EINVAL;
+        ts.kb[t] = (e[t] - s[t]) / 8;
+        ts.loff[t] = loff;
+        loff += (e[t] - s[t]) / 4 * 16;
+        ts.delta[t] = delta ? delta[t] : 0.f;
+        ts.mid[t] = bits ? ((1 << bits[t]) - 1) * 0.5f : 0.f;
+        for (int p = 0; p < 8; p++) ts.pw[t][p] = (bits && p < bits[t]) ? (float)(1 << (bits[t] - 1 - p)) : 0.f;
+        ts.planes[t] = planes ? planes[t] : nullptr;
+    }
+    return FVS_OK;
+}
+
+}  // namespace fvs
+
+extern "C" int fvs_lut_build(fvs_stream_t stream, const float* Zq, int B, int ldz, int D, int half, void* L, int T,
+                             const int32_t* tier_s, const int32_t* tier_e, float* qsum, float* qn2) {
+    FVS_CHECK_ARG(Zq && L && tier_s && tier_e && qsum && qn2 && B >= 0 && D > 0 && D % 4 == 0 && ldz >= D);
+    fvs::TierSet ts;
+    int rc = fvs::make_tiers(ts, T, tier_s, tier_e, nullptr, nullptr, nullptr);
+    if (rc) return rc;
+    for (int t = 0; t < T; t++)
+        if (tier_e[t] > D) return FVS_EINVAL;
+    if (B == 0) return FVS_OK;
+    if (half)
+        fvs::lut_build_kernel<true><<<B, 256, 0, stream>>>(Zq, ldz, D, L, ts, B, qsum, qn2);
+    else
+        fvs::lut_build_kernel<false><<<B, 256, 0, stream>>>(Zq, ldz, D, L, ts, B, qsum, qn2);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_lut_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const void* L,
+                             int half, int LW, int T, const int32_t* tier_s, const int32_t* tier_e,
+                             const int32_t* tier_bits, const float* tier_delta, const uint8_t* const* tier_planes,
+                             const uint16_t* scale, const uint16_t* sig, int64_t N, const float* qsum, const float* qn2,
+                             const int32_t* ncnt, float* est, float* sd) {
+    FVS_CHECK_ARG(pos && qc && L && tier_s && tier_e && tier_bits && tier_delta && tier_planes && scale && sig);
+    FVS_CHECK_ARG(qsum && qn2 && est && sd && B >= 0 && K >= 1 && N > 0 && LW > 0);
+    fvs::TierSet ts;
+    int rc = fvs::make_tiers(ts, T, tier_s, tier_e, tier_bits, tier_delta, tier_planes);
+    if (rc) return rc;
+    for (int t = 0; t < T; t++) FVS_CHECK_ARG(tier_planes[t] != nullptr);
+    if (ts.loff[T - 1] + (tier_e[T - 1] - tier_s[T - 1]) / 4 * 16 > LW) return FVS_EINVAL;
+    const size_t esz = half ? 2 : 4;
+    if ((LW * esz) % 16 != 0) return FVS_EINVAL;
+    const size_t sm = (size_t)LW * esz;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    cudaError_t e;
+    if (half) {
+        e = fvs_ensure_smem((const void*)fvs::lut_score_kernel<true>, sm);
+        if (e != cudaSuccess) return (int)e;
+        fvs::lut_score_kernel<true><<<B, 256, sm, stream>>>(pos, B, K, qc, L, LW, ts, (const __half*)scale,
+                                                            (const __half*)sig, N, qsum, qn2, ncnt, est, sd);
+    } else {
+        e = fvs_ensure_smem((const void*)fvs::lut_score_kernel<false>, sm);
+        if (e != cudaSuccess) return (int)e;
+        fvs::lut_score_kernel<false><<<B, 256, sm, stream>>>(pos, B, K, qc, L, LW, ts, (const __half*)scale,
+                                                             (const __half*)sig, N, qsum, qn2, ncnt, est, sd);
+    }
+    return fvs_launch_status();
+}

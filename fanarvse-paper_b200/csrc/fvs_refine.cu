@@ -1,0 +1,122 @@
+// Classification, exact re-rank of the ambiguous candidates and final top-k, fused in one kernel (one CTA per query).
+//
+// Replaces `_finish` lines 92-95 (`throughput/enginei8.py`), `Engine8._s3` (`src/engine3.py:143-146`) and the zero-copy
+// stage-3 kernel `_stage3` (`src/stage3_zc.py:11-27`).  The fp16 store H stays in HBM (the reference reads it from
+// pinned host memory over PCIe): each ambiguous candidate's row (d x 2 bytes) is read once by one warp with 16-byte
+// loads and dotted with the fp32 query in fp32.
+#include "fvs_common.cuh"
+
+namespace fvs {
+
+constexpr int REF_THREADS = 256;
+
+__global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __restrict__ H, int d,
+                                                            const int32_t* __restrict__ order,
+                                                            const int64_t* __restrict__ pos,
+                                                            const float* __restrict__ est, const float* __restrict__ sd,
+                                                            int K, float z, int k, int kp, const float* __restrict__ Q,
+                                                            int ldq, int32_t* __restrict__ ids, int32_t* __restrict__ I,
+                                                            int32_t* __restrict__ reads, float* __restrict__ score_k) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ SelectScratch ss;
+    __shared__ int s_namb, s_fill;
+    uint32_t* klo = reinterpret_cast<uint32_t*>(smem);       // K
+    uint32_t* khi = klo + K;                                  // K
+    float* score = reinterpret_cast<float*>(khi + K);         // K
+    int32_t* cid = reinterpret_cast<int32_t*>(score + K);     // K candidate ids
+    int32_t* amb_list = cid + K;                              // K
+    unsigned long long* sb = reinterpret_cast<unsigned long long*>(amb_list + K + (K & 1));  // kp
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const int64_t qK = (int64_t)q * K;
+    for (int i = tid; i < K; i += nt) {
+        const float e = est[qK + i], s = sd[qK + i];
+        const float zs = __fmul_rn(z, s);
+        klo[i] = f2o(__fsub_rn(e, zs));
+        khi[i] = f2o(__fadd_rn(e, zs));
+        const int32_t id = order[pos[qK + i]];
+        cid[i] = id;
+        ids[qK + i] = id;
+    }
+    if (tid == 0) {
+        s_namb = 0;
+        s_fill = 0;
+    }
+    __syncthreads();
+    const uint32_t hk1 = block_select_rth_largest<32, uint32_t>([&](int i) { return khi[i]; }, K, k + 1, ss);
+    const uint32_t lk = block_select_rth_largest<32, uint32_t>([&](int i) { return klo[i]; }, K, k, ss);
+    // sure: lo > (k+1)-th hi; ambiguous: hi >= k-th lo and not sure (key order == float order)
+    for (int i = tid; i < K; i += nt) {
+        const bool sure = klo[i] > hk1;
+        const bool amb = !sure && khi[i] >= lk;
+        score[i] = sure ? __fadd_rn(est[qK + i], 10.f) : -1e9f;
+        if (amb) amb_list[atomicAdd(&s_namb, 1)] = i;
+    }
+    __syncthreads();
+    const int namb = s_namb;
+    // exact fp32 dot products of the ambiguous rows (one warp per row, 8 halves per lane per step)
+    const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
+    const float* qrow = Q + (int64_t)q * ldq;
+    for (int a = warp; a < namb; a += nw) {
+        const int i = amb_list[a];
+        const __half* h = H + (int64_t)cid[i] * d;
+        float acc = 0.f;
+        for (int c0 = lane * 8; c0 < d; c0 += 256) {
+            const uint4 hv = *reinterpret_cast<const uint4*>(h + c0);
+            const float4 qa = *reinterpret_cast<const float4*>(qrow + c0);
+            const float4 qb = *reinterpret_cast<const float4*>(qrow + c0 + 4);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&hv);
+            float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+            float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+            acc += f0.x * qa.x + f0.y * qa.y + f1.x * qa.z + f1.y * qa.w;
+            acc += f2.x * qb.x + f2.y * qb.y + f3.x * qb.z + f3.y * qb.w;
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) score[i] = acc;
+    }
+    __syncthreads();
+    // final top-k by (score desc, id asc)
+    auto key = [&](int i) {
+        return ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
+    };
+    const unsigned long long T = block_select_rth_largest<64, unsigned long long>(key, K, k, ss);
+    // keys above the k-th first (fewer than k of them), then equal keys up to k (fillers can repeat a key)
+    for (int i = tid; i < K; i += nt) {
+        const unsigned long long kk = key(i);
+        if (kk > T) sb[atomicAdd(&s_fill, 1)] = kk;
+    }
+    for (int i = k + tid; i < kp; i += nt) sb[i] = 0ull;
+    __syncthreads();
+    for (int i = tid; i < K; i += nt) {
+        const unsigned long long kk = key(i);
+        if (kk == T) {
+            const int slot = atomicAdd(&s_fill, 1);
+            if (slot < k) sb[slot] = kk;
+        }
+    }
+    __syncthreads();
+    block_bitonic_desc(sb, kp);
+    for (int i = tid; i < k; i += nt) {
+        I[(int64_t)q * k + i] = (int32_t)(0xffffffffu - (uint32_t)sb[i]);
+        if (score_k) score_k[(int64_t)q * k + i] = o2f((uint32_t)(sb[i] >> 32));
+    }
+    if (tid == 0) reads[q] = namb;
+}
+
+}  // namespace fvs
+
+extern "C" int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* order, const int64_t* pos,
+                          const float* est, const float* sd, int B, int K, float z, int k, const float* Q, int ldq,
+                          int32_t* ids, int32_t* I, int32_t* reads, float* score_k) {
+    FVS_CHECK_ARG(H && order && pos && est && sd && Q && ids && I && reads);
+    FVS_CHECK_ARG(d > 0 && d % 8 == 0 && ldq >= d && ldq % 4 == 0 && B >= 0 && k >= 1 && K > k);
+    if (K > 4096 || k > 256) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    int kp = 1;
+    while (kp < k) kp <<= 1;
+    const size_t sm = (size_t)K * 4 * 5 + 8 + (size_t)kp * 8;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::refine_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::refine_kernel<<<B, fvs::REF_THREADS, sm, stream>>>((const __half*)H, d, order, pos, est, sd, K, z, k, kp, Q,
+                                                             ldq, ids, I, reads, score_k);
+    return fvs_launch_status();
+}

@@ -1,0 +1,198 @@
+// Selection kernels: first-pass threshold, stage-1 top-K (+ delta rule), top-k merge across shards.
+// One CTA per query; candidates are staged in shared memory, the k-th bound is found by a block-wide MSB-first radix
+// select on order-preserving integer keys, the winners are compacted and sorted with a bitonic network.
+#include "fvs_common.cuh"
+
+namespace fvs {
+
+// ------------------------------------------------------------------------------------------------ threshold
+// t0[q] = r-th largest of the block maxima of q's first-pass pairs (`throughput/enginei8.py:53-55`).
+__global__ void threshold_kernel(const float* __restrict__ bmc, int MB, const int32_t* __restrict__ slot,
+                                 const int64_t* __restrict__ probe, int nprobe, int n1, const int64_t* __restrict__ off,
+                                 int r, float* __restrict__ t0) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ SelectScratch ss;
+    __shared__ int s_base[1024 + 1];
+    __shared__ int s_cnt_valid;
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
+    const int q = blockIdx.x, tid = threadIdx.x;
+    // exclusive prefix of block counts over the n1 first-pass cells (n1 <= 1024)
+    if (tid == 0) {
+        int acc = 0;
+        for (int j = 0; j < n1; j++) {
+            const int64_t c = probe[(int64_t)q * nprobe + j];
+            const int64_t s = off[c], e = off[c + 1];
+            s_base[j] = acc;
+            acc += (e > s) ? (int)((e - 1) / 32 - s / 32 + 1) : 0;
+        }
+        s_base[n1] = acc;
+        s_cnt_valid = 0;
+    }
+    __syncthreads();
+    const int n = s_base[n1];
+    int nvalid = 0;
+    for (int j = 0; j < n1; j++) {
+        const int b0 = s_base[j], nb = s_base[j + 1] - b0;
+        const float* row = bmc + (int64_t)slot[(int64_t)q * n1 + j] * MB;
+        for (int b = tid; b < nb; b += blockDim.x) {
+            const float v = row[b];
+            keys[b0 + b] = f2o(v);
+            nvalid += v > -1e29f;
+        }
+    }
+    atomicAdd(&s_cnt_valid, nvalid);
+    __syncthreads();
+    const int cv = s_cnt_valid;
+    float res;
+    if (cv >= r && r >= 1) {
+        res = o2f(block_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, n, r, ss));
+    } else if (cv > 0) {
+        // fewer valid maxima than r: the smallest valid one
+        __shared__ unsigned s_min;
+        if (tid == 0) s_min = 0xffffffffu;
+        __syncthreads();
+        unsigned m = 0xffffffffu;
+        for (int i = tid; i < n; i += blockDim.x)
+            if (o2f(keys[i]) > -1e29f) m = min(m, keys[i]);
+        atomicMin(&s_min, m);
+        __syncthreads();
+        res = o2f(s_min);
+    } else {
+        res = 1e30f;
+    }
+    if (tid == 0) t0[q] = res;
+}
+
+// ------------------------------------------------------------------------------------------------ stage-1 top-K
+constexpr int SEL_SMEM_KEYS = 6144;  // keys staged in shared memory; larger buffers are read from global memory
+
+__device__ __forceinline__ unsigned long long cand_key(float v, int32_t pos) {
+    return ((unsigned long long)f2o(v) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)pos);
+}
+
+__global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t* __restrict__ bpos,
+                                   const int32_t* __restrict__ cnt, int M, int K, int Kp, int64_t* __restrict__ pos,
+                                   float* __restrict__ est1, uint8_t* __restrict__ ok, int32_t* __restrict__ ncnt,
+                                   float delta, int didx) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ SelectScratch ss;
+    __shared__ int s_fill, s_ncnt;
+    unsigned long long* sb = reinterpret_cast<unsigned long long*>(smem);   // Kp sort buffer
+    unsigned long long* sk = sb + Kp;                                        // staged keys (<= SEL_SMEM_KEYS)
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const int c = cnt[q];
+    const int n = min(max(c, 0), M);
+    const float* bv = bval + (int64_t)q * M;
+    const int32_t* bp = bpos + (int64_t)q * M;
+    const bool staged = n <= SEL_SMEM_KEYS;
+    if (staged)
+        for (int i = tid; i < n; i += nt) sk[i] = cand_key(bv[i], bp[i]);
+    if (tid == 0) s_fill = 0;
+    __syncthreads();
+    auto key = [&](int i) { return staged ? sk[i] : cand_key(bv[i], bp[i]); };
+    const unsigned long long filler = cand_key(kNeg, 0);
+    if (n <= K) {
+        for (int i = tid; i < Kp; i += nt) sb[i] = i < n ? key(i) : (i < K ? filler : 0ull);
+        __syncthreads();
+    } else {
+        const unsigned long long T = block_select_rth_largest<64, unsigned long long>(key, n, K, ss);
+        for (int i = tid; i < n; i += nt) {
+            const unsigned long long k = key(i);
+            if (k >= T) {  // keys are unique (one entry per probed row): exactly K of them
+                const int slot = atomicAdd(&s_fill, 1);
+                if (slot < K) sb[slot] = k;
+            }
+        }
+        for (int i = K + tid; i < Kp; i += nt) sb[i] = 0ull;
+        __syncthreads();
+    }
+    block_bitonic_desc(sb, Kp);
+    for (int i = tid; i < K; i += nt) {
+        const unsigned long long k = sb[i];
+        est1[(int64_t)q * K + i] = o2f((uint32_t)(k >> 32));
+        pos[(int64_t)q * K + i] = (int64_t)(0xffffffffu - (uint32_t)k);
+    }
+    if (tid == 0) ok[q] = (c >= K && c <= M) ? 1 : 0;
+    if (ncnt != nullptr) {
+        if (tid == 0) s_ncnt = 0;
+        __syncthreads();
+        const float thr = __fsub_rn(o2f((uint32_t)(sb[didx] >> 32)), delta);
+        int m = 0;
+        for (int i = tid; i < K; i += nt) m += o2f((uint32_t)(sb[i] >> 32)) >= thr;
+        atomicAdd(&s_ncnt, m);
+        __syncthreads();
+        if (tid == 0) ncnt[q] = s_ncnt;
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ merge
+__global__ void merge_kernel(const int64_t* __restrict__ ids_g, const float* __restrict__ score_g, int G, int B,
+                             int kin, int k, int Kp, int64_t* __restrict__ I, float* __restrict__ S) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    unsigned long long* sb = reinterpret_cast<unsigned long long*>(smem);
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const int n = G * kin;
+    for (int i = tid; i < Kp; i += nt) {
+        if (i < n) {
+            const int g = i / kin, j = i - g * kin;
+            const int64_t o = ((int64_t)g * B + q) * kin + j;
+            sb[i] = ((unsigned long long)f2o(score_g[o]) << 32) | (0xffffffffu - (uint32_t)ids_g[o]);
+        } else {
+            sb[i] = 0ull;
+        }
+    }
+    __syncthreads();
+    block_bitonic_desc(sb, Kp);
+    for (int i = tid; i < k; i += nt) {
+        const unsigned long long key = sb[i];
+        I[(int64_t)q * k + i] = (int64_t)(0xffffffffu - (uint32_t)key);
+        if (S) S[(int64_t)q * k + i] = o2f((uint32_t)(key >> 32));
+    }
+}
+
+static int pow2_at_least(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+}  // namespace fvs
+
+extern "C" int fvs_threshold(fvs_stream_t stream, const float* bmc, int MB, const int32_t* slot, const int64_t* probe,
+                             int nprobe, int n1, const int64_t* off, int B, int r, float* t0) {
+    FVS_CHECK_ARG(bmc && slot && probe && off && t0 && MB > 0 && nprobe > 0 && B >= 0);
+    FVS_CHECK_ARG(n1 >= 1 && n1 <= nprobe && r >= 1);
+    if (n1 > 1024) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    const size_t sm = (size_t)n1 * MB * sizeof(uint32_t);
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::threshold_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::threshold_kernel<<<B, 256, sm, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int32_t* bpos, const int32_t* cnt, int B,
+                               int M, int K, int64_t* pos, float* est1, uint8_t* ok, int32_t* ncnt, float delta,
+                               int delta_idx) {
+    FVS_CHECK_ARG(bval && bpos && cnt && pos && est1 && ok && B >= 0 && M > 0 && K >= 1);
+    if (ncnt) FVS_CHECK_ARG(delta_idx >= 0 && delta_idx < K);
+    if (K > 4096) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    const int Kp = fvs::pow2_at_least(K);
+    const size_t sm = (size_t)(Kp + fvs::SEL_SMEM_KEYS) * 8;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::select_topk_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::select_topk_kernel<<<B, 512, sm, stream>>>(bval, bpos, cnt, M, K, Kp, pos, est1, ok, ncnt, delta, delta_idx);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_merge_topk(fvs_stream_t stream, const int64_t* ids_g, const float* score_g, int G, int B, int kin,
+                              int k, int64_t* I, float* S) {
+    FVS_CHECK_ARG(ids_g && score_g && I && G >= 1 && B >= 0 && kin >= 1 && k >= 1 && k <= G * kin);
+    if (G * kin > 4096) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    const int Kp = fvs::pow2_at_least(G * kin);
+    fvs::merge_kernel<<<B, 256, (size_t)Kp * 8, stream>>>(ids_g, score_g, G, B, kin, k, Kp, I, S);
+    return fvs_launch_status();
+}

@@ -1,0 +1,283 @@
+"""Throughput-mode search engine on the B200 C library: the drop-in for the reference's `EngineI8`.
+
+Mirrors `throughput/enginei8.py` (class EngineI8 with the final knobs of `throughput/e_v3final.py:28-32`):
+`search(Qb, K, z, nprobe, k) -> (I [B,k], reads [B], cand_ids [B,K])`, one CUDA graph per (B, K, z, nprobe, k), the
+exactness flag as the only host synchronisation, and the reference's recompute path for flagged queries.
+
+Host-side PyTorch keeps what the reference computes with cuBLAS / torch before the kernels (routing product and top-n_p,
+query quantisation, the pair CSR, the rotated LUT query); everything after that -- the int8 scan passes, threshold,
+stage-1 top-K with the delta rule, LUT build and scoring, classification, exact re-rank and final top-k -- runs in
+libfanar_b200 through its C ABI.  There is no CPU path: without the shared library (or without a GPU) `search` raises.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, ptr
+
+BN = 32
+
+
+def static_tiles(off, tile_rows):
+    """Static work list of the int8 scan: for every non-empty cell, tiles of `tile_rows` rows starting on the cell's
+    first global 32-row boundary (`src/s1cell.py:157-168` uses 32-row blocks; a tile here is tile_rows/32 of them).
+    Returns (tile_cell, tile_row0) int32 numpy arrays and MB (max blocks per cell + 1)."""
+    off = np.asarray(off, np.int64)
+    s, e = off[:-1], off[1:]
+    first = (s // BN) * BN
+    ntile = np.where(e > s, (e - first + tile_rows - 1) // tile_rows, 0)
+    cell = np.repeat(np.arange(len(s)), ntile)
+    k = np.arange(len(cell)) - np.repeat(np.cumsum(ntile) - ntile, ntile)
+    row0 = first[cell] + k * tile_rows
+    MB = int((int((e - s).max()) + BN - 1) // BN + 1)
+    return cell.astype(np.int32), row0.astype(np.int32), MB
+
+
+class IndexI8:
+    """Device-resident throughput-mode index in the reference's layout.
+
+    s1   : dict with off (NC+1), order (int32 [N]), c, means16, inv_mnorm          (`src/engine_cell.py:26-32`)
+    i8   : dict with Z (int8 [N,R]), zs (f32 [N]), Vr (f32 [d,R])                  (`throughput/enginei8.py:19-27`)
+    code : uniform tiered code: TS, planes, scale, sig, deltas and VP or VP16 (or V + rots)  (`throughput/s2lut.py`)
+    H16  : fp16 full-precision store [N, d] in original-id order (HBM-resident here; pinned host RAM in the reference)
+    """
+
+    def __init__(self, s1, i8, code, H16, device="cuda"):
+        dev = torch.device(device)
+        self.device = dev
+        f = lambda x, dt=None: torch.as_tensor(x).to(device=dev, dtype=dt).contiguous()
+        self.off_np = np.asarray(s1["off"] if "off" in s1 else s1["off_t"].cpu().numpy(), np.int64)
+        self.off = f(self.off_np, torch.int64)
+        self.NC = len(self.off_np) - 1
+        self.N = int(self.off_np[-1])
+        self.order = f(s1["order"], torch.int32)
+        self.c = f(s1["c"], torch.float32)
+        means16 = f(s1["means16"], torch.float16)
+        inv_mnorm = f(s1["inv_mnorm"], torch.float32)
+        self.meansN = (means16.float() * inv_mnorm[:, None]).half().contiguous()     # `throughput/enginei8.py:66`
+        self.mnorm = (1.0 / inv_mnorm).float().contiguous()
+        self.Z = f(i8["Z"], torch.int8)
+        self.zs = f(i8["zs"], torch.float32)
+        self.Vr = f(i8["Vr"], torch.float32)
+        self.R = self.Z.shape[1]
+        self.TS = [tuple(int(v) for v in t) for t in code["TS"]]
+        self.T = len(self.TS)
+        self.D = self.TS[-1][1]
+        self.planes = [f(p, torch.uint8) for p in code["planes"]]
+        self.scale = f(code["scale"], torch.float16)
+        self.sig = f(code["sig"], torch.float16)
+        self.deltas = [float(code["deltas"][b]) for _, _, b in self.TS]
+        if "VP16" in code:
+            VP16 = f(code["VP16"], torch.float16)
+        elif "VP" in code:
+            VP16 = f(code["VP"], torch.float32).half()
+        else:
+            V = f(code["V"], torch.float32)
+            Dm = torch.zeros(V.shape[0], V.shape[0], device=dev)
+            for (s, e, _), P in zip(self.TS, code["rots"]):
+                Dm[s:e, s:e] = f(P, torch.float32)
+            VP16 = (V @ Dm).half()
+        self.VP16 = VP16[:, :self.D].contiguous()
+        self.H16 = f(H16, torch.float16)
+        self.d = self.H16.shape[1]
+        tc, tr, self.MB = static_tiles(self.off_np, _lib.lib().fvs_i8_tile_rows())
+        self.tile_cell, self.tile_row0 = f(tc, torch.int32), f(tr, torch.int32)
+        self.ntiles = len(tc)
+        self.LW = self.D // 4 * 16
+        # host-side tier descriptors for the C ABI
+        self._ts_s = _lib.i32_array([s for s, _, _ in self.TS])
+        self._ts_e = _lib.i32_array([e for _, e, _ in self.TS])
+        self._ts_b = _lib.i32_array([b for _, _, b in self.TS])
+        self._ts_d = _lib.f32_array(self.deltas)
+        self._ts_p = _lib.ptr_array(self.planes)
+
+    def nbytes_per_vector(self):
+        return self.R + 4 + sum((e - s) * b for s, e, b in self.TS) / 8 + 4 * self.T
+
+
+def pairs_fast(probe, NC, QM, scale):
+    """CSR of (query, cell) pairs sorted by cell (`throughput/enginei8.py:11-16`): qid, coff, ccnt, qcp, o."""
+    B, npr = probe.shape
+    flat = probe.flatten().to(torch.int32)
+    _, o = torch.sort(flat, stable=True)
+    qid = (o // npr).to(torch.int32).contiguous()
+    cnt = torch.zeros(NC, dtype=torch.int32, device=probe.device).scatter_add_(0, flat.long(), torch.ones_like(flat))
+    off = torch.cumsum(cnt, 0) - cnt
+    fo = flat[o].long()
+    qc = QM[qid.long(), fo].float() * scale[fo]
+    return qid, off.to(torch.int32).contiguous(), cnt.contiguous(), qc.contiguous(), o
+
+
+class EngineB200I8:
+    """The reference's EngineI8 (FanarVSE-T) on libfanar_b200.  Knobs as in `throughput/e_v3final.py:28-32`."""
+    RHO = 0.6
+    MSZ = 3072
+    DELTA = 0.07
+    LUTH = True
+    BETA = None
+
+    def __init__(self, index: IndexI8):
+        self.ix = index
+        self.graphs = {}
+        self.nbad = 0
+        self.nbad2 = 0
+        self.L = _lib.lib()
+
+    # ------------------------------------------------------------------ stage 1
+    def quantize(self, Qb):
+        """q8, qs (`throughput/enginei8.py:38`)."""
+        z = Qb @ self.ix.Vr
+        qs = z.abs().amax(1).clamp(min=1e-12) / 127
+        q8 = torch.round(z / qs[:, None]).clamp(-127, 127).to(torch.int8).contiguous()
+        return q8, qs.float().contiguous()
+
+    def first_pass_cells(self, K, nprobe, rho_override=None):
+        beta = (1.1 if K <= 400 else 0.7) if not self.BETA else self.BETA
+        if rho_override:
+            beta = 1.5
+        return min(max(int(np.ceil(beta * K / (self.ix.N / self.ix.NC / BN + 1))), 1), nprobe)
+
+    def stage1_i8(self, Qb, QM, probe, K, rho_override=None, M_override=None, q8qs=None):
+        """`throughput/enginei8.py:36-60` on the C library: returns pos [B,K] int64, ok [B] bool, est1 [B,K], n1."""
+        ix, L = self.ix, self.L
+        B = Qb.shape[0]
+        dev = Qb.device
+        q8, qs = q8qs if q8qs is not None else self.quantize(Qb)
+        M = M_override or self.MSZ or max(4096, 16 * K)
+        rho = rho_override if rho_override else (self.RHO or (0.75 if K <= 400 else 0.5))
+        n1 = self.first_pass_cells(K, probe.shape[1], rho_override)
+        probe = probe.contiguous()
+        sh = _lib.stream_handle()
+        qid, coff, ccnt, qcp, o = pairs_fast(probe[:, :n1], ix.NC, QM, ix.mnorm)
+        bmc = torch.empty(B * n1 * ix.MB, device=dev)
+        check(L.fvs_i8_scan(sh, 0, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
+                            ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z), ptr(ix.zs),
+                            None, None, None, None, 0, ptr(bmc), ix.MB), "fvs_i8_scan(first pass)")
+        slot = torch.empty_like(o, dtype=torch.int32)
+        slot[o] = torch.arange(len(o), device=dev, dtype=torch.int32)
+        t0 = torch.empty(B, device=dev)
+        check(L.fvs_threshold(sh, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1, ptr(ix.off), B,
+                              int(np.ceil(rho * K)), ptr(t0)), "fvs_threshold")
+        qid, coff, ccnt, qcp, _ = pairs_fast(probe, ix.NC, QM, ix.mnorm)
+        cnt = torch.zeros(B, dtype=torch.int32, device=dev)
+        bval = torch.empty(B, M, device=dev)
+        bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
+        check(L.fvs_i8_scan(sh, 1, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
+                            ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z), ptr(ix.zs),
+                            ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, None, 0), "fvs_i8_scan(emit)")
+        pos = torch.empty(B, K, dtype=torch.int64, device=dev)
+        est1 = torch.empty(B, K, device=dev)
+        ok = torch.empty(B, dtype=torch.uint8, device=dev)
+        use_delta = self.DELTA is not None and not rho_override
+        ncnt = torch.empty(B, dtype=torch.int32, device=dev) if use_delta else None
+        check(L.fvs_select_topk(sh, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1), ptr(ok), ptr(ncnt),
+                                float(self.DELTA or 0.0), 9), "fvs_select_topk")
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs)
+        return pos, ok.bool(), est1, ncnt
+
+    # ------------------------------------------------------------------ stages 2-3
+    def luts(self, Qb, half, Zq=None):
+        ix = self.ix
+        B = Qb.shape[0]
+        if Zq is None:
+            Zq = (Qb.half() @ ix.VP16).float().contiguous()                # `throughput/s2lut.py:122`
+        Lt = torch.empty(B, ix.LW, device=Qb.device, dtype=torch.float16 if half else torch.float32)
+        qsum = torch.empty(ix.T, B, device=Qb.device)
+        qn2 = torch.empty(ix.T, B, device=Qb.device)
+        check(self.L.fvs_lut_build(_lib.stream_handle(), ptr(Zq), B, ix.D, ix.D, int(half), ptr(Lt), ix.T, ix._ts_s,
+                                   ix._ts_e, ptr(qsum), ptr(qn2)), "fvs_lut_build")
+        return Lt, qsum, qn2, Zq
+
+    def score_lut(self, QC, pos, pre, ncnt, half):
+        ix = self.ix
+        B, K = pos.shape
+        Lt, qsum, qn2 = pre[:3]
+        est = torch.empty(B, K, device=pos.device)
+        sd = torch.empty(B, K, device=pos.device)
+        check(self.L.fvs_lut_score(_lib.stream_handle(), ptr(pos), B, K, ptr(QC), ptr(Lt), int(half), ix.LW, ix.T,
+                                   ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N,
+                                   ptr(qsum), ptr(qn2), ptr(ncnt), ptr(est), ptr(sd)), "fvs_lut_score")
+        return est, sd
+
+    def refine(self, Qb, pos, est, sd, z, k):
+        ix = self.ix
+        B, K = pos.shape
+        ids = torch.empty(B, K, dtype=torch.int32, device=pos.device)
+        I = torch.empty(B, k, dtype=torch.int32, device=pos.device)
+        reads = torch.empty(B, dtype=torch.int32, device=pos.device)
+        score_k = torch.empty(B, k, device=pos.device)
+        Qf = Qb.float().contiguous()
+        check(self.L.fvs_refine(_lib.stream_handle(), ptr(ix.H16), ix.d, ptr(ix.order), ptr(pos), ptr(est), ptr(sd),
+                                B, K, float(z), k, ptr(Qf), Qf.shape[1], ptr(ids), ptr(I), ptr(reads), ptr(score_k)),
+              "fvs_refine")
+        return I, reads, ids, score_k
+
+    def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None):
+        """`throughput/enginei8.py:80-95`."""
+        half = self.LUTH if half is None else half
+        pre = self.luts(Qb, half)
+        est, sd = self.score_lut(QC, pos, pre, ncnt, half)
+        I, reads, ids, score_k = self.refine(Qb, pos, est, sd, z, k)
+        self._last.update(est=est, sd=sd, Zq=pre[3], score_k=score_k)
+        return ok, I, reads.long(), ids
+
+    def route(self, Qb, nprobe):
+        QM = Qb.half() @ self.ix.meansN.T                                   # `throughput/enginei8.py:67-68`
+        return QM, QM.topk(nprobe, 1).indices
+
+    def _gpu(self, Qb, K, z, nprobe, k):
+        """`throughput/enginei8.py:61-70` (NROUTE branch)."""
+        if K <= k or K < 10:
+            raise ValueError("need K > k and K >= 10 (the delta rule reads the 10th stage-1 estimate)")
+        QC = (Qb @ self.ix.c).contiguous()
+        QM, probe = self.route(Qb, nprobe)
+        pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K)
+        return self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
+
+    def _fallback(self, Qb, K, z, nprobe, k):
+        """`throughput/enginei8.py:112-120`: rho 1.0 (beta 1.5), M 65536, fp32 LUT, no delta rule."""
+        QC = (Qb @ self.ix.c).contiguous()
+        QM, probe = self.route(Qb, nprobe)
+        pos, ok, est1, _ = self.stage1_i8(Qb, QM, probe, K, rho_override=1.0, M_override=65536)
+        self.nbad2 += int((~ok).sum())
+        pre = self.luts(Qb, False)
+        est, sd = self.score_lut(QC, pos, pre, None, False)
+        I, reads, ids, _ = self.refine(Qb, pos, est, sd, z, k)
+        return I, reads.long(), ids
+
+    def search(self, Qb, K, z, nprobe, k, ret_est=False):
+        """`throughput/enginei8.py:96-111`: returns (I [B,k] int32, reads [B] int64, cand_ids [B,K] int32)."""
+        if not Qb.is_cuda:
+            raise RuntimeError("EngineB200I8.search needs CUDA queries (the B200 library has no CPU path)")
+        B = len(Qb)
+        key = (B, K, z, nprobe, k)
+        if key not in self.graphs:
+            qs = Qb.clone()
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                for _ in range(3):
+                    self._gpu(qs, K, z, nprobe, k)
+            torch.cuda.current_stream().wait_stream(st)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                outs = self._gpu(qs, K, z, nprobe, k)
+            self.graphs[key] = (g, qs, outs)
+        g, qs, (ok, I, nr, ids) = self.graphs[key]
+        qs.copy_(Qb)
+        g.replay()
+        I, nr, ids = I.clone(), nr.clone(), ids.clone()
+        if not bool(ok.all()):                                             # the only synchronisation
+            bad = torch.nonzero(~ok).flatten()
+            self.nbad += len(bad)
+            a, b, c = self._fallback(Qb[bad], K, z, nprobe, k)
+            I[bad], nr[bad] = a, b
+            ids[bad] = c[:, :ids.shape[1]]
+        return I, nr, ids
+
+    def search_eager(self, Qb, K, z, nprobe, k):
+        """One search without graph capture (same kernels); returns the intermediates for parity tests."""
+        ok, I, nr, ids = self._gpu(Qb, K, z, nprobe, k)
+        return dict(ok=ok, I=I, reads=nr, ids=ids, **self._last)

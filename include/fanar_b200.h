@@ -1,0 +1,122 @@
+/*
+ * libfanar_b200 -- the C ABI of the B200 (sm_100a) query path of FanarVSE.
+ *
+ * Conventions (all entry points):
+ *   - every pointer argument is a DEVICE pointer unless the comment says "host"; the caller allocates every buffer;
+ *   - kernels are enqueued on `stream` (a cudaStream_t); no entry point allocates, synchronises or reads device memory
+ *     on the host, so every call can be captured into a CUDA graph;
+ *   - return 0 on success, a negative FVS_E* code for a bad argument, or a positive cudaError_t from the launch;
+ *   - data conditions are not errors: overflow / underflow of the emit buffer is reported through cnt / ok exactly as
+ *     the reference reports it (`throughput/enginei8.py:60`), and handled by the caller's recompute path.
+ * Index layout is the reference's (sorted-position order; see `throughput/enginei8.py:19-27`, `src/tiered.py:29-44`).
+ */
+#ifndef FANAR_B200_H
+#define FANAR_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* fvs_stream_t; /* == cudaStream_t */
+
+#define FVS_OK 0
+#define FVS_EINVAL (-1)   /* null pointer, negative size, unsupported shape */
+#define FVS_ERANGE (-2)   /* a size above what the kernel supports (e.g. K > 4096) */
+
+/* Library version (major*10000 + minor*100 + patch) and build target ("sm_100a"). */
+int fvs_version(void);
+const char* fvs_arch(void);
+
+/* Rows per tile of the int8 scan (a multiple of the reference's 32-row block).  Host-side helper. */
+int fvs_i8_tile_rows(void);
+
+/*
+ * Int8 stage-1 scan over the probed cells: first pass (mode 0) or threshold emit (mode 1).
+ * Replaces the Triton kernels `_first8c` / `_emit8c` (`throughput/ivf8c_kern.py:2-36`) and the CUDA WMMA kernel
+ * `ivf8` (`throughput/civf8.py:15-91`, launched by `civf8.launch(mode, P, q8, qs, qid, coff, ccnt, pcell, pblk, ps, pe,
+ * Z, zs, qcp, t0, cnt, bval, bpos, bmc, CAP, MB)`).
+ *   q8 [B,R] int8, qs [B]           quantised queries and their scales (`throughput/enginei8.py:38`)
+ *   qid, qcp [npairs]; coff, ccnt [NC]  pairs sorted by cell (`throughput/enginei8.py:11-16`)
+ *   tile_cell, tile_row0 [ntiles]   static work list: tiles of fvs_i8_tile_rows() rows of one cell, row0 a multiple of 32
+ *   off [NC+1] int64                cell boundaries in sorted positions
+ *   Z [N,R] int8, zs [N] f32        stage-1 codes and scales
+ *   mode 0: bmc[(coff[c]+i)*MB + (blk - off[c]/32)] = max over the cell's rows of global 32-row block blk of
+ *           est = ((float(q8.z) * qs) * zs) + qcp; slots of blocks a cell does not have are not written.
+ *   mode 1: every (q, n) with est >= t0[q]: i = atomicAdd(cnt[q], 1); if i < M: bval[q*M+i] = est, bpos[q*M+i] = n.
+ *   R must be 256.  Unused outputs of a mode may be NULL.
+ */
+int fvs_i8_scan(fvs_stream_t stream, int mode,
+                const int8_t* q8, const float* qs, int B, int R,
+                const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
+                const int32_t* tile_cell, const int32_t* tile_row0, int ntiles,
+                const int64_t* off, int NC,
+                const int8_t* Z, const float* zs,
+                const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M,
+                float* bmc, int MB);
+
+/*
+ * First-pass threshold (`throughput/enginei8.py:53-55`): t0[q] = the r-th largest block maximum over the blocks of the
+ * n1 first-pass cells probe[q*nprobe + j] (j < n1) of query q, read at bmc[slot[q*n1+j]*MB + b]; the smallest one if
+ * there are fewer than r; 1e30 if none.  slot[q*n1+j] is the cell-sorted position of pair (q, j) (`inv` in the
+ * reference).
+ */
+int fvs_threshold(fvs_stream_t stream, const float* bmc, int MB, const int32_t* slot,
+                  const int64_t* probe, int nprobe, int n1, const int64_t* off, int B, int r, float* t0);
+
+/*
+ * Stage-1 top-K and exactness flag (`throughput/enginei8.py:60`, `bval.topk(K)` + `K <= cnt <= M`) fused with the
+ * delta rule (`throughput/enginei8.py:87-90`).  Per query: the K best of the first min(cnt, M) buffer entries by
+ * (est desc, pos asc), written sorted; slots beyond cnt read as (-1e30, position 0) as the reference's initialised
+ * buffers do.  ok[q] = K <= cnt[q] <= M.  If ncnt != NULL: ncnt[q] = #{i : est1[q,i] >= est1[q,delta_idx] - delta}.
+ * K <= 4096.
+ */
+int fvs_select_topk(fvs_stream_t stream, const float* bval, const int32_t* bpos, const int32_t* cnt, int B, int M,
+                    int K, int64_t* pos, float* est1, uint8_t* ok, int32_t* ncnt, float delta, int delta_idx);
+
+/*
+ * Per-query nibble lookup tables (`throughput/s2lut.py:108-126`, `_lut_kernel` + `luts_fused`):
+ *   L[q, n*16 + v] = sum_{i<4} Zq[q, 4n+i] * ((v >> (3-i)) & 1) over the leading D coordinates (fp16 if half else f32),
+ *   qsum[t*B+q] = sum Zq[q, s_t:e_t], qn2[t*B+q] = sum Zq[q, s_t:e_t]^2 for the T tiers (host arrays tier_s / tier_e).
+ */
+int fvs_lut_build(fvs_stream_t stream, const float* Zq, int B, int ldz, int D, int half, void* L,
+                  int T, const int32_t* tier_s, const int32_t* tier_e, float* qsum, float* qn2);
+
+/*
+ * LUT-scored tiered refinement (`throughput/s2lut.py:48-106`, `_score_lut` / `_tier_lut`).  For candidate i of query q
+ * (row n = pos[q*K+i]; live if i < ncnt[q], or all when ncnt == NULL):
+ *   est = qc[q] + sum_t delta_t (sum_p 2^(b_t-1-p) sum_j (L[2j][hi(byte)] + L[2j+1][lo(byte)]) - mid_t qsum[t,q])
+ *                   * scale[t*N+n],      sd = sqrt(sum_t qn2[t,q] sig[t*N+n]^2);   dead: est = -1e30, sd = 0.
+ * Host arrays of length T: tier_s, tier_e, tier_bits, tier_delta, tier_planes (device pointers to planes_t
+ * [b_t, N, (e_t-s_t)/8] uint8).  T <= 8.
+ */
+int fvs_lut_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc,
+                  const void* L, int half, int LW, int T, const int32_t* tier_s, const int32_t* tier_e,
+                  const int32_t* tier_bits, const float* tier_delta, const uint8_t* const* tier_planes,
+                  const uint16_t* scale, const uint16_t* sig, int64_t N, const float* qsum, const float* qn2,
+                  const int32_t* ncnt, float* est, float* sd);
+
+/*
+ * Classification, exact re-rank and final top-k (`throughput/enginei8.py:92-95`, `src/engine3.py:143-146`,
+ * `src/stage3_zc.py:11-27`):  lo/hi = est -/+ z*sd;  sure = lo > (k+1)-th largest hi;  amb = hi >= k-th largest lo
+ * and not sure;  score = est + 10 if sure, the exact fp32 dot <H[id], Q[q]> of the fp16 row id = order[pos] if
+ * ambiguous, -1e9 otherwise;  I[q] = the k ids of largest score (ties by smaller id).
+ * Outputs: ids [B,K] (candidate ids, int32), I [B,k] int32, reads [B] int32 (#ambiguous), score_k [B,k] (nullable).
+ * H [Nfull, d] fp16 in original-id order; d a multiple of 8.  K <= 4096, k <= 256.
+ */
+int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* order, const int64_t* pos,
+               const float* est, const float* sd, int B, int K, float z, int k, const float* Q, int ldq,
+               int32_t* ids, int32_t* I, int32_t* reads, float* score_k);
+
+/*
+ * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
+ * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.
+ */
+int fvs_merge_topk(fvs_stream_t stream, const int64_t* ids_g, const float* score_g, int G, int B, int kin, int k,
+                   int64_t* I, float* S);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FANAR_B200_H */
