@@ -27,6 +27,7 @@ SIGNATURES = {
     "fvs_lut_build": (I32, [P, P, I32, I32, I32, I32, P, I32, P, P, P, P]),
     "fvs_lut_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P, P, P]),
     "fvs_refine": (I32, [P, P, I32, P, P, P, P, I32, I32, F32, I32, P, I32, P, P, P, P]),
+    "fvs_exact_scores": (I32, [P, P, I32, P, I32, I32, P, I32, P]),
     "fvs_merge_topk": (I32, [P, P, P, I32, I32, I32, I32, P, P]),
 }
 

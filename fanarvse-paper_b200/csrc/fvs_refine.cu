@@ -102,7 +102,45 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
     if (tid == 0) reads[q] = namb;
 }
 
+// One warp per (query, listed id): exact fp32 dot of the fp16 row with the query.
+__global__ void exact_scores_kernel(const __half* __restrict__ H, int d, const int32_t* __restrict__ ids, int B, int k,
+                                    const float* __restrict__ Q, int ldq, float* __restrict__ score) {
+    const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (w >= B * k) return;
+    const int q = w / k;
+    const int32_t id = ids[w];
+    if (id < 0) {
+        if (lane == 0) score[w] = kNeg;
+        return;
+    }
+    const __half* h = H + (int64_t)id * d;
+    const float* qrow = Q + (int64_t)q * ldq;
+    float acc = 0.f;
+    for (int c0 = lane * 8; c0 < d; c0 += 256) {
+        const uint4 hv = *reinterpret_cast<const uint4*>(h + c0);
+        const float4 qa = *reinterpret_cast<const float4*>(qrow + c0);
+        const float4 qb = *reinterpret_cast<const float4*>(qrow + c0 + 4);
+        const __half2* h2 = reinterpret_cast<const __half2*>(&hv);
+        float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+        float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+        acc += f0.x * qa.x + f0.y * qa.y + f1.x * qa.z + f1.y * qa.w;
+        acc += f2.x * qb.x + f2.y * qb.y + f3.x * qb.z + f3.y * qb.w;
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) score[w] = acc;
+}
+
 }  // namespace fvs
+
+extern "C" int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ids, int B, int k,
+                                const float* Q, int ldq, float* score) {
+    FVS_CHECK_ARG(H && ids && Q && score && d > 0 && d % 8 == 0 && ldq >= d && ldq % 4 == 0 && B >= 0 && k >= 1);
+    if (B == 0) return FVS_OK;
+    const int64_t warps = (int64_t)B * k;
+    fvs::exact_scores_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>((const __half*)H, d, ids, B, k, Q, ldq,
+                                                                             score);
+    return fvs_launch_status();
+}
 
 extern "C" int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* order, const int64_t* pos,
                           const float* est, const float* sd, int B, int K, float z, int k, const float* Q, int ldq,

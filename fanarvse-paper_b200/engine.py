@@ -121,9 +121,26 @@ class EngineB200I8:
     def __init__(self, index: IndexI8):
         self.ix = index
         self.graphs = {}
+        self.graph_launches = {}
         self.nbad = 0
         self.nbad2 = 0
+        self.launches = 0          # library kernel launches issued (eager) or captured
+        self.timing = None         # dict name -> [(start, end) CUDA events] when timing library calls
         self.L = _lib.lib()
+
+    def _call(self, name, fn, *args):
+        """Call one C-ABI entry point on the current stream; count it; optionally bracket it with CUDA events."""
+        if self.timing is not None:
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            rc = fn(_lib.stream_handle(), *args)
+            b.record()
+            self.timing.setdefault(name, []).append((a, b))
+        else:
+            rc = fn(_lib.stream_handle(), *args)
+        check(rc, name)
+        self.launches += 1
 
     # ------------------------------------------------------------------ stage 1
     def quantize(self, Qb):
@@ -149,32 +166,31 @@ class EngineB200I8:
         rho = rho_override if rho_override else (self.RHO or (0.75 if K <= 400 else 0.5))
         n1 = self.first_pass_cells(K, probe.shape[1], rho_override)
         probe = probe.contiguous()
-        sh = _lib.stream_handle()
         qid, coff, ccnt, qcp, o = pairs_fast(probe[:, :n1], ix.NC, QM, ix.mnorm)
         bmc = torch.empty(B * n1 * ix.MB, device=dev)
-        check(L.fvs_i8_scan(sh, 0, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
-                            ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z), ptr(ix.zs),
-                            None, None, None, None, 0, ptr(bmc), ix.MB), "fvs_i8_scan(first pass)")
+        self._call("i8_scan_first", L.fvs_i8_scan, 0, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
+                   ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z),
+                   ptr(ix.zs), None, None, None, None, 0, ptr(bmc), ix.MB)
         slot = torch.empty_like(o, dtype=torch.int32)
         slot[o] = torch.arange(len(o), device=dev, dtype=torch.int32)
         t0 = torch.empty(B, device=dev)
-        check(L.fvs_threshold(sh, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1, ptr(ix.off), B,
-                              int(np.ceil(rho * K)), ptr(t0)), "fvs_threshold")
+        self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1,
+                   ptr(ix.off), B, int(np.ceil(rho * K)), ptr(t0))
         qid, coff, ccnt, qcp, _ = pairs_fast(probe, ix.NC, QM, ix.mnorm)
         cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
-        check(L.fvs_i8_scan(sh, 1, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
-                            ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z), ptr(ix.zs),
-                            ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, None, 0), "fvs_i8_scan(emit)")
+        self._call("i8_scan_emit", L.fvs_i8_scan, 1, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
+                   ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z),
+                   ptr(ix.zs), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, None, 0)
         pos = torch.empty(B, K, dtype=torch.int64, device=dev)
         est1 = torch.empty(B, K, device=dev)
         ok = torch.empty(B, dtype=torch.uint8, device=dev)
         use_delta = self.DELTA is not None and not rho_override
         ncnt = torch.empty(B, dtype=torch.int32, device=dev) if use_delta else None
-        check(L.fvs_select_topk(sh, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1), ptr(ok), ptr(ncnt),
-                                float(self.DELTA or 0.0), 9), "fvs_select_topk")
-        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs)
+        self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
+                   ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, npairs=int(qid.numel()))
         return pos, ok.bool(), est1, ncnt
 
     # ------------------------------------------------------------------ stages 2-3
@@ -186,8 +202,8 @@ class EngineB200I8:
         Lt = torch.empty(B, ix.LW, device=Qb.device, dtype=torch.float16 if half else torch.float32)
         qsum = torch.empty(ix.T, B, device=Qb.device)
         qn2 = torch.empty(ix.T, B, device=Qb.device)
-        check(self.L.fvs_lut_build(_lib.stream_handle(), ptr(Zq), B, ix.D, ix.D, int(half), ptr(Lt), ix.T, ix._ts_s,
-                                   ix._ts_e, ptr(qsum), ptr(qn2)), "fvs_lut_build")
+        self._call("lut_build", self.L.fvs_lut_build, ptr(Zq), B, ix.D, ix.D, int(half), ptr(Lt), ix.T, ix._ts_s,
+                   ix._ts_e, ptr(qsum), ptr(qn2))
         return Lt, qsum, qn2, Zq
 
     def score_lut(self, QC, pos, pre, ncnt, half):
@@ -196,9 +212,9 @@ class EngineB200I8:
         Lt, qsum, qn2 = pre[:3]
         est = torch.empty(B, K, device=pos.device)
         sd = torch.empty(B, K, device=pos.device)
-        check(self.L.fvs_lut_score(_lib.stream_handle(), ptr(pos), B, K, ptr(QC), ptr(Lt), int(half), ix.LW, ix.T,
-                                   ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N,
-                                   ptr(qsum), ptr(qn2), ptr(ncnt), ptr(est), ptr(sd)), "fvs_lut_score")
+        self._call("lut_score", self.L.fvs_lut_score, ptr(pos), B, K, ptr(QC), ptr(Lt), int(half), ix.LW, ix.T,
+                   ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N, ptr(qsum),
+                   ptr(qn2), ptr(ncnt), ptr(est), ptr(sd))
         return est, sd
 
     def refine(self, Qb, pos, est, sd, z, k):
@@ -209,9 +225,8 @@ class EngineB200I8:
         reads = torch.empty(B, dtype=torch.int32, device=pos.device)
         score_k = torch.empty(B, k, device=pos.device)
         Qf = Qb.float().contiguous()
-        check(self.L.fvs_refine(_lib.stream_handle(), ptr(ix.H16), ix.d, ptr(ix.order), ptr(pos), ptr(est), ptr(sd),
-                                B, K, float(z), k, ptr(Qf), Qf.shape[1], ptr(ids), ptr(I), ptr(reads), ptr(score_k)),
-              "fvs_refine")
+        self._call("refine", self.L.fvs_refine, ptr(ix.H16), ix.d, ptr(ix.order), ptr(pos), ptr(est), ptr(sd), B, K,
+                   float(z), k, ptr(Qf), Qf.shape[1], ptr(ids), ptr(I), ptr(reads), ptr(score_k))
         return I, reads, ids, score_k
 
     def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None):
@@ -262,12 +277,15 @@ class EngineB200I8:
                     self._gpu(qs, K, z, nprobe, k)
             torch.cuda.current_stream().wait_stream(st)
             g = torch.cuda.CUDAGraph()
+            n0 = self.launches
             with torch.cuda.graph(g):
                 outs = self._gpu(qs, K, z, nprobe, k)
+            self.graph_launches[key] = self.launches - n0
             self.graphs[key] = (g, qs, outs)
         g, qs, (ok, I, nr, ids) = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
+        self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         I, nr, ids = I.clone(), nr.clone(), ids.clone()
         if not bool(ok.all()):                                             # the only synchronisation
             bad = torch.nonzero(~ok).flatten()

@@ -1,0 +1,68 @@
+"""Row-sharded search over the GPUs of one node (new; the reference is single-GPU).
+
+Every rank holds its own index over a contiguous slice of the database rows [row_offset, row_offset + n) (built by the
+reference's recipe on that slice alone), searches the same query batch with the local engine, and returns its local
+top-k with EXACT scores (a "sure" candidate is ranked by est + 10 without a read, `src/engine3.py:144-145`, which is
+not comparable across shards, so the k winners are re-read with `fvs_exact_scores`).  One all-gather of the [B, k]
+(global id, score) pairs crosses NVLink (NCCL), and `fvs_merge_topk` keeps the global top-k by (score desc, id asc).
+
+The exchange is the only collective; every rank takes it once per batch, in the same order, also when its local search
+ran the recompute path.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+
+
+def exact_scores(engine, Qb, I):
+    """fp32 <H[id], q> for the local ids I [B, k] (int32) on the engine's device."""
+    ix = engine.ix
+    B, k = I.shape
+    S = torch.empty(B, k, device=I.device)
+    Qf = Qb.float().contiguous()
+    L = _lib.lib()
+    _lib.check(L.fvs_exact_scores(_lib.stream_handle(), _lib.ptr(ix.H16), ix.d, _lib.ptr(I.contiguous()), B, k,
+                                  _lib.ptr(Qf), Qf.shape[1], _lib.ptr(S)), "fvs_exact_scores")
+    return S
+
+
+def merge_topk(ids_g, score_g, k):
+    """Global top-k of [G, B, kin] (ids int64, scores f32) on the GPU."""
+    G, B, kin = ids_g.shape
+    I = torch.empty(B, k, dtype=torch.int64, device=ids_g.device)
+    S = torch.empty(B, k, device=ids_g.device)
+    L = _lib.lib()
+    _lib.check(L.fvs_merge_topk(_lib.stream_handle(), _lib.ptr(ids_g.contiguous()), _lib.ptr(score_g.contiguous()), G,
+                                B, kin, k, _lib.ptr(I), _lib.ptr(S)), "fvs_merge_topk")
+    return I, S
+
+
+class ShardedSearch:
+    """search(Qb, K, z, nprobe, k) -> (I [B,k] int64 global ids, S [B,k] exact scores, reads [B] local reads).
+
+    `local` is the rank's engine (EngineB200I8 on its shard); `row_offset` the global id of its first row.  The local
+    exact-score and merge steps can be replaced (CPU tests inject the oracle's restatements)."""
+
+    def __init__(self, local, row_offset, group=None, exact=None, merge=None):
+        self.local, self.row_offset, self.group = local, int(row_offset), group
+        self.exact = exact or (lambda Qb, I: exact_scores(self.local, Qb, I))
+        self.merge = merge or merge_topk
+
+    def search(self, Qb, K, z, nprobe, k):
+        I, reads, _ = self.local.search(Qb, K, z, nprobe, k)
+        S = self.exact(Qb, I)
+        gid = I.long() + self.row_offset
+        G = dist.get_world_size(self.group) if dist.is_initialized() else 1
+        if G == 1:
+            ids_all, s_all = gid[None], S[None]
+        else:
+            ids_l = [torch.empty_like(gid) for _ in range(G)]
+            s_l = [torch.empty_like(S) for _ in range(G)]
+            dist.all_gather(ids_l, gid.contiguous(), group=self.group)
+            dist.all_gather(s_l, S.contiguous(), group=self.group)
+            ids_all, s_all = torch.stack(ids_l), torch.stack(s_l)
+        Ig, Sg = self.merge(ids_all, s_all, k)
+        return Ig, Sg, reads

@@ -69,10 +69,13 @@ class Mixture:
         return out
 
 
-def make_dataset(spec: MixtureSpec, device="cpu", gt_k: int = 100, with_gt: bool = True):
-    """Returns dict(base16 [n,d] fp16, queries [nq,d] fp32, gt [nq,gt_k] int64 or None) on `device`."""
+def make_dataset(spec: MixtureSpec, device="cpu", gt_k: int = 100, with_gt: bool = True, shard: int = 0):
+    """Returns dict(base16 [n,d] fp16, queries [nq,d] fp32, gt [nq,gt_k] int64 or None) on `device`.
+
+    `shard` selects an independent stream of base rows from the same mixture (row-sharded multi-GPU data: every shard
+    shares the mixture and the queries)."""
     mix = Mixture(spec, device)
-    gb = torch.Generator(device=mix.device).manual_seed(spec.seed + 1)
+    gb = torch.Generator(device=mix.device).manual_seed(spec.seed + 1 + 1000 * shard)
     gq = torch.Generator(device=mix.device).manual_seed(spec.seed + 2)
     base16 = torch.empty(spec.n, spec.d, dtype=torch.float16, device=mix.device)
     for j in range(0, spec.n, 262144):
@@ -80,7 +83,13 @@ def make_dataset(spec: MixtureSpec, device="cpu", gt_k: int = 100, with_gt: bool
         base16[j:j + m] = mix.sample(m, gb).half()
     queries = mix.sample(spec.nq, gq)
     gt = brute_force_topk(base16, queries, gt_k) if with_gt else None
-    return dict(base16=base16, queries=queries, gt=gt, spec=spec)
+    return dict(base16=base16, queries=queries, gt=gt, spec=spec, mixture=mix)
+
+
+def extra_queries(ds, n: int, seed: int):
+    """n more queries from the dataset's mixture (timing batches beyond the recall batch)."""
+    mix = ds["mixture"]
+    return mix.sample(n, torch.Generator(device=mix.device).manual_seed(seed))
 
 
 def brute_force_topk(base16: torch.Tensor, queries: torch.Tensor, k: int, chunk: int = 131072) -> torch.Tensor:

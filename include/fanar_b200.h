@@ -110,6 +110,15 @@ int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ord
                int32_t* ids, int32_t* I, int32_t* reads, float* score_k);
 
 /*
+ * Exact fp32 inner products of given rows: score[q*k+i] = <H[ids[q*k+i]], Q[q]> (fp16 rows, fp32 accumulate), as the
+ * exact read of `src/stage3_zc.py:11-22` but for every listed id.  Used by the row-sharded search so that each shard's
+ * local top-k carries exact scores before the cross-shard merge (a "sure" candidate is ranked by est + 10 without a
+ * read, `src/engine3.py:144-145`, which is not comparable across shards).  ids < 0 give -1e30.
+ */
+int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ids, int B, int k, const float* Q,
+                     int ldq, float* score);
+
+/*
  * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
  * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.
  */
