@@ -33,7 +33,7 @@ sys.path.insert(0, REPO)
 import importlib  # noqa: E402
 
 METRIC = "QPS at recall@10>=0.99, 1M x 1536 fp16, batch 2000; batch-1 p50 latency"
-GRID = [(128, 120, 3072), (160, 120, 3072), (192, 150, 3072), (256, 150, 4096), (352, 175, 4096)]
+GRID = [(96, 100, 4096), (128, 120, 4096), (160, 120, 4096), (192, 150, 4096), (256, 150, 4096), (352, 175, 4096)]
 
 
 def pkg(name):
@@ -273,11 +273,13 @@ def main():
     sampler.start()
     time.sleep(0.3)
     a, b = torch.cuda.Event(True), torch.cuda.Event(True)
+    torch.cuda.nvtx.range_push("timed")
     a.record()
     for i in range(args.steps):
         search(Qs[i % 4], K, z, npr, k)
     b.record()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     clocks = sampler.stop()
     ms_rank = a.elapsed_time(b) / args.steps
     launches = E.launches + getattr(E, "replayed_launches", 0) - launches0

@@ -21,11 +21,17 @@ SIGNATURES = {
     "fvs_version": (I32, []),
     "fvs_arch": (C.c_char_p, []),
     "fvs_i8_tile_rows": (I32, []),
+    "fvs_quantize": (I32, [P, P, I32, I32, I32, P, P]),
+    "fvs_route_topk": (I32, [P, P, I32, I32, I32, P]),
+    "fvs_pairs": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P]),
     "fvs_i8_scan": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, P, P, P, P, P, I32, P, I32]),
+    "fvs_i8_scan_tc": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I64, P, P, P, P, P, I32, P,
+                              I32, P]),
     "fvs_threshold": (I32, [P, P, I32, P, P, I32, I32, P, I32, I32, P]),
     "fvs_select_topk": (I32, [P, P, P, P, I32, I32, I32, P, P, P, P, F32, I32]),
     "fvs_lut_build": (I32, [P, P, I32, I32, I32, I32, P, I32, P, P, P, P]),
     "fvs_lut_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P, P, P]),
+    "fvs_lut_score_zq": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P]),
     "fvs_refine": (I32, [P, P, I32, P, P, P, P, I32, I32, F32, I32, P, I32, P, P, P, P]),
     "fvs_exact_scores": (I32, [P, P, I32, P, I32, I32, P, I32, P]),
     "fvs_merge_topk": (I32, [P, P, P, I32, I32, I32, I32, P, P]),

@@ -65,10 +65,11 @@ struct SelectScratch {
 };
 
 // r-th largest (1-based, 1 <= r <= n) of n keys of KBITS bits (32 or 64) produced by key(i); MSB-first radix select,
-// 8 bits per pass.  All threads of the block must call it; returns the same key in every thread.
+// 8 bits per pass.  Histogram updates are aggregated per warp (lanes with the same digit add once), since the leading
+// digits of scores concentrate in one or two bins.  All threads of the block must call it; every thread gets the key.
 template <int KBITS, typename KeyT, typename KeyFn>
 __device__ KeyT block_select_rth_largest(KeyFn key, int n, int r, SelectScratch& s) {
-    const int tid = threadIdx.x, nt = blockDim.x;
+    const int tid = threadIdx.x, nt = blockDim.x, lane = tid & 31;
     if (tid == 0) {
         s.prefix = 0ull;
         s.rem = r;
@@ -80,14 +81,24 @@ __device__ KeyT block_select_rth_largest(KeyFn key, int n, int r, SelectScratch&
         __syncthreads();
         const unsigned long long pre = s.prefix;
         const unsigned long long hmask = (shift + 8 >= 64) ? 0ull : (~0ull << (shift + 8));
-        for (int i = tid; i < n; i += nt) {
-            unsigned long long k = (unsigned long long)key(i);
-            if ((k & hmask) == (pre & hmask)) atomicAdd(&s.hist[(k >> shift) & 255u], 1u);
+        for (int b = tid - lane; b < n; b += nt) {  // whole warps iterate together
+            const int i = b + lane;
+            bool take = false;
+            unsigned digit = 0;
+            if (i < n) {
+                const unsigned long long k = (unsigned long long)key(i);
+                take = (k & hmask) == (pre & hmask);
+                digit = (unsigned)(k >> shift) & 255u;
+            }
+            const unsigned act = __ballot_sync(0xffffffffu, take);
+            if (take) {
+                const unsigned peers = __match_any_sync(act, digit);
+                if ((peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&s.hist[digit], (unsigned)__popc(peers));
+            }
         }
         __syncthreads();
         if (tid < 32) {
             // lane l owns bins 255-8l .. 248-8l (descending)
-            const int lane = tid;
             unsigned c[8], sum = 0;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
@@ -102,7 +113,7 @@ __device__ KeyT block_select_rth_largest(KeyFn key, int n, int r, SelectScratch&
             }
             const int rem = s.rem;
             unsigned ball = __ballot_sync(0xffffffffu, incl >= (unsigned)rem);
-            int L = __ffs(ball) - 1;  // always found since the total equals the candidate count >= rem
+            int L = __ffs(ball) - 1;  // always found: the candidates (keys matching the prefix) number >= rem
             if (lane == L) {
                 unsigned above = incl - sum;
                 int digit = 0;
@@ -123,6 +134,109 @@ __device__ KeyT block_select_rth_largest(KeyFn key, int n, int r, SelectScratch&
     KeyT res = (KeyT)s.prefix;
     __syncthreads();  // every thread has read the result before the scratch is reused
     return res;
+}
+
+// r-th largest (1-based, 1 <= r <= n) of n keys produced by key(i), by ONE warp (all 32 lanes call it); hist is 256
+// words of this warp's own shared memory.  Same algorithm as block_select_rth_largest without block barriers.
+template <int KBITS, typename KeyT, typename KeyFn>
+__device__ KeyT warp_select_rth_largest(KeyFn key, int n, int r, unsigned* hist) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long prefix = 0ull;
+    int rem = r;
+#pragma unroll 1
+    for (int shift = KBITS - 8; shift >= 0; shift -= 8) {
+        for (int i = lane; i < 256; i += 32) hist[i] = 0;
+        __syncwarp();
+        const unsigned long long hmask = (shift + 8 >= 64) ? 0ull : (~0ull << (shift + 8));
+        for (int b = 0; b < n; b += 32) {
+            const int i = b + lane;
+            bool take = false;
+            unsigned digit = 0;
+            if (i < n) {
+                const unsigned long long k = (unsigned long long)key(i);
+                take = (k & hmask) == (prefix & hmask);
+                digit = (unsigned)(k >> shift) & 255u;
+            }
+            const unsigned act = __ballot_sync(0xffffffffu, take);
+            if (take) {
+                const unsigned peers = __match_any_sync(act, digit);
+                if ((peers & ((1u << lane) - 1u)) == 0u) atomicAdd(&hist[digit], (unsigned)__popc(peers));
+            }
+        }
+        __syncwarp();
+        unsigned c[8], sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            c[i] = hist[255 - 8 * lane - i];
+            sum += c[i];
+        }
+        unsigned incl = sum;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const unsigned ball = __ballot_sync(0xffffffffu, incl >= (unsigned)rem);
+        const int L = __ffs(ball) - 1;
+        int digit = 0, nrem = rem;
+        if (lane == L) {
+            unsigned above = incl - sum;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if (above + c[i] >= (unsigned)rem) {
+                    digit = 255 - 8 * lane - i;
+                    break;
+                }
+                above += c[i];
+            }
+            nrem = rem - (int)above;
+        }
+        digit = __shfl_sync(0xffffffffu, digit, L);
+        rem = __shfl_sync(0xffffffffu, nrem, L);
+        prefix |= (unsigned long long)digit << shift;
+        __syncwarp();
+    }
+    return (KeyT)prefix;
+}
+
+// In-place descending bitonic sort of n (a power of two) 64-bit keys in shared memory by one warp.
+__device__ __forceinline__ void warp_bitonic_desc(unsigned long long* a, int n) {
+    const int lane = threadIdx.x & 31;
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = lane; i < n; i += 32) {
+                const int ixj = i ^ j;
+                if (ixj > i) {
+                    const unsigned long long x = a[i], y = a[ixj];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? (x < y) : (x > y)) {
+                        a[i] = y;
+                        a[ixj] = x;
+                    }
+                }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Block-wide sum of an int (all threads call; every thread gets the total).
+__device__ __forceinline__ int block_sum_int(int v, int* red /* >= 32 ints of shared memory */) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    int t = 0;
+    for (int w = 0; w < nw; w++) t += red[w];
+    __syncthreads();
+    return t;
 }
 
 // In-place descending bitonic sort of n (a power of two) 64-bit keys in shared memory.

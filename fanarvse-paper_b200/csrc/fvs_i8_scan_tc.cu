@@ -1,0 +1,482 @@
+// Int8 stage-1 IVF scan on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Same contract as the reference's `_first8c` / `_emit8c` (`throughput/ivf8c_kern.py:2-36`): one CTA owns a tile of
+// 128 code rows of one cell, starting on a global 32-row boundary so that epilogue warp w covers exactly the
+// reference's 32-row block blk = row0/32 + w (`src/s1cell.py:161-168`).
+//
+// Persistent kernel: one CTA per SM walks the tiles b, b + G, b + 2G, ... of the static work list (skipping cells no
+// query probes).  A tile is split into sub-tiles of up to 64 of the cell's queries; sub-tiles are numbered in walk
+// order (nb).  Warp roles (512 threads):
+//   warp 0      : TMA loads of the 128 x 256 B code tiles (two 128 B-wide boxes, 128 B swizzle), A_STAGES ahead
+//   warp 1      : TMEM allocation; lane 0 issues tcgen05.mma.kind::i8 (M=128 rows, N=16..64 queries, K=32 x 8) per
+//                 sub-tile into one of T_STAGES accumulators, and releases a code tile when its last MMA completes
+//   warps 2-7   : gather: warp 2+g fills the sub-tiles nb = g (mod 6) -- the rows of q8 picked by qid, in the
+//                 canonical K-major 128 B-swizzled layout, plus scale / pair constant / threshold -- so six
+//                 sub-tiles' dependent loads are in flight at once
+//   warps 8-15  : two epilogue warpgroups, group e on the sub-tiles nb = e (mod 2): tcgen05.ld of the warp's 32 TMEM
+//                 lanes (= code rows), est = ((acc * qs) * zs) + qcp in fp32 with explicit rounding, then first pass:
+//                 per-query block maximum by one redux.sync.max, or emit: per-query ballot over the 32 rows, lane j
+//                 reserving space for column j with one atomicAdd (a chunk's 32 atomics in flight together, the
+//                 second chunk's ballots computed while the first chunk's atomics return), prefix positions by popc.
+// So the loads and MMAs of the next sub-tiles and tiles overlap the epilogues of the current ones.
+// Every mbarrier wait is bounded; on expiry the CTA raises `status`, drains what it issued, frees TMEM and returns.
+#include <cuda.h>
+
+#include "fvs_common.cuh"
+
+namespace fvs {
+namespace tc {
+
+constexpr int TILE_ROWS = 128;
+constexpr int QN = 64;  // queries per sub-tile
+constexpr int RB = 256;
+constexpr int A_STAGES = 3;
+constexpr int GATHER_WARPS = 6;
+constexpr int B_STAGES = GATHER_WARPS;  // gather warp g owns B stage g
+constexpr int T_STAGES = 4;
+constexpr int EPI_GROUPS = 2;
+constexpr int NTHREADS = 32 * (2 + GATHER_WARPS + 4 * EPI_GROUPS);
+constexpr uint32_t TMEM_COLS = T_STAGES * QN;  // int32 accumulator columns
+constexpr uint32_t WAIT_LIMIT = 1u << 22;
+
+// shared-memory carve-up (offsets from a 1024-byte aligned base)
+constexpr int A_BYTES = 2 * TILE_ROWS * 128;               // one code tile: 2 K-halves x 16 KB
+constexpr int B_BYTES = 2 * QN * 128;                      // one query sub-tile: 2 K-halves x 8 KB
+constexpr int A_OFF = 0;
+constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
+constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;       // B_STAGES x 4 x QN x 4 B
+constexpr int BAR_OFF = META_OFF + B_STAGES * 4 * QN * 4;  // mbarriers
+constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 2 * T_STAGES;
+constexpr int MISC_OFF = BAR_OFF + NBAR * 8;               // tmem base, abort flag
+constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;           // + alignment slack
+
+struct Params {
+    const int8_t* q8;
+    const float* qs;
+    const int32_t* qid;
+    const int32_t* coff;
+    const int32_t* ccnt;
+    const float* qcp;
+    const int32_t* tile_cell;
+    const int32_t* tile_row0;
+    const int64_t* off;
+    const float* zs;
+    const float* t0;
+    int32_t* cnt;
+    float* bval;
+    int32_t* bpos;
+    float* bmc;
+    int32_t* status;
+    int M, MB;
+};
+
+__device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+// bounded wait for the completion of the phase with the given parity; false when the limit expired or the CTA aborted
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+    for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((it & 255u) == 255u && *abort) return false;
+    }
+    *abort = 1;
+    return false;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(map), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+
+// UMMA shared-memory descriptor: K-major, 128 B swizzle, 8-row core groups 1024 B apart (SBO), sm_100 version bit.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t addr) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// instruction descriptor of tcgen05.mma.kind::i8: s32 accumulate, signed A and B, both K-major, M=128, N.
+__device__ __forceinline__ uint32_t i8_idesc(int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(TILE_ROWS >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+template <int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_constant__ CUtensorMap zmap, Params p,
+                                                              int ntiles) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t sbase = saddr(smem);
+    auto a_full = [&](int s) { return sbase + BAR_OFF + 8 * s; };
+    auto a_empty = [&](int s) { return sbase + BAR_OFF + 8 * (A_STAGES + s); };
+    auto b_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + s); };
+    auto b_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + B_STAGES + s); };
+    auto t_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + s); };
+    auto t_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + T_STAGES + s); };
+    int* meta_qid = reinterpret_cast<int*>(smem + META_OFF);          // [B_STAGES][QN]
+    float* meta_qs = reinterpret_cast<float*>(meta_qid + B_STAGES * QN);
+    float* meta_qc = meta_qs + B_STAGES * QN;
+    float* meta_th = meta_qc + B_STAGES * QN;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + MISC_OFF);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + MISC_OFF + 4);
+
+    if (tid == 0) {
+        for (int s = 0; s < A_STAGES; s++) {
+            mbar_init(a_full(s), 1);
+            mbar_init(a_empty(s), 1);
+        }
+        for (int s = 0; s < B_STAGES; s++) {
+            mbar_init(b_full(s), 1);
+            mbar_init(b_empty(s), 4);
+        }
+        for (int s = 0; s < T_STAGES; s++) {
+            mbar_init(t_full(s), 1);
+            mbar_init(t_empty(s), 4);
+        }
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int G = gridDim.x;
+
+    if (warp == 0) {
+        // ---- code tiles by TMA
+        if (lane == 0) {
+            asm volatile("prefetch.tensormap [%0];" ::"l"(&zmap) : "memory");
+            int na = 0;
+            for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
+                if (p.ccnt[p.tile_cell[tile]] == 0) continue;
+                const int s = na % A_STAGES;
+                if (!mbar_wait(a_empty(s), ((na / A_STAGES) & 1) ^ 1, abort)) break;
+                const int row0 = p.tile_row0[tile];
+                mbar_expect_tx(a_full(s), A_BYTES);
+                tma_load_2d(sbase + A_OFF + s * A_BYTES, &zmap, 0, row0, a_full(s));
+                tma_load_2d(sbase + A_OFF + s * A_BYTES + TILE_ROWS * 128, &zmap, 128, row0, a_full(s));
+                na++;
+            }
+            // drain: the most recent load of every stage has landed before the CTA may exit
+            for (int u = na - 1; u >= 0 && u >= na - A_STAGES; u--) mbar_wait(a_full(u % A_STAGES), (u / A_STAGES) & 1, abort);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issue
+        if (lane == 0) {
+            int na = 0, nb = 0, last_a = -1;
+            for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
+                const int qn = p.ccnt[p.tile_cell[tile]];
+                if (qn == 0) continue;
+                const int sa = na % A_STAGES;
+                if (!mbar_wait(a_full(sa), (na / A_STAGES) & 1, abort)) break;
+                tc_fence_after();
+                const uint32_t abase = sbase + A_OFF + sa * A_BYTES;
+                bool ok = true;
+                for (int i = 0; i * QN < qn; i++, nb++) {
+                    const int sb = nb % B_STAGES, st = nb % T_STAGES;
+                    if (!mbar_wait(b_full(sb), (nb / B_STAGES) & 1, abort) ||
+                        !mbar_wait(t_empty(st), ((nb / T_STAGES) & 1) ^ 1, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const int nq = min(QN, qn - i * QN);
+                    const uint32_t idesc = i8_idesc((nq + 15) & ~15);
+                    const uint32_t d = tmem + (uint32_t)(st * QN);
+                    const uint32_t bb = sbase + B_OFF + sb * B_BYTES;
+#pragma unroll
+                    for (int ks = 0; ks < RB / 32; ks++) {
+                        const int h = ks >> 2, kofs = (ks & 3) * 32;
+                        mma_i8(d, sw128_desc(abase + h * TILE_ROWS * 128 + kofs), sw128_desc(bb + h * QN * 128 + kofs),
+                               idesc, ks > 0 ? 1u : 0u);
+                    }
+                    mma_commit(t_full(st));
+                }
+                if (!ok) break;
+                mma_commit(a_empty(sa));  // the code tile is free once these MMAs complete
+                last_a = na;
+                na++;
+            }
+            if (last_a >= 0) mbar_wait(a_empty(last_a % A_STAGES), (last_a / A_STAGES) & 1, abort);
+        }
+        __syncwarp();
+    } else if (warp < 2 + GATHER_WARPS) {
+        // ---- query gather: warp gw fills the sub-tiles nb = gw (mod GATHER_WARPS); lane l fills rows l and l + 32
+        const int gw = warp - 2;
+        int nb = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
+            const int c = p.tile_cell[tile];
+            const int qn = p.ccnt[c];
+            if (qn == 0) continue;
+            const int qoff = p.coff[c];
+            bool ok = true;
+            for (int i = 0; i * QN < qn; i++, nb++) {
+                if (nb % GATHER_WARPS != gw) continue;
+                const int s = nb % B_STAGES;
+                if (!mbar_wait(b_empty(s), ((nb / B_STAGES) & 1) ^ 1, abort)) {
+                    ok = false;
+                    break;
+                }
+                const int nq = min(QN, qn - i * QN);
+                const int n16 = (nq + 15) & ~15;
+                int qq[2];
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int g = lane + 32 * rr;
+                    qq[rr] = -1;
+                    if (g < nq) {
+                        const int pi = qoff + i * QN + g;
+                        const int q = p.qid[pi];
+                        qq[rr] = q;
+                        meta_qid[s * QN + g] = q;
+                        meta_qs[s * QN + g] = p.qs[q];
+                        meta_qc[s * QN + g] = p.qcp[pi];
+                        meta_th[s * QN + g] = MODE ? p.t0[q] : 0.f;
+                    }
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int g = lane + 32 * rr;
+                    if (g >= n16) continue;
+                    const int q = qq[rr];
+                    const uint4* src = reinterpret_cast<const uint4*>(p.q8 + (int64_t)(q >= 0 ? q : 0) * RB);
+                    uint8_t* bs = smem + B_OFF + s * B_BYTES + (g >> 3) * 1024 + (g & 7) * 128;
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        uint4 v[8];
+#pragma unroll
+                        for (int cc = 0; cc < 8; cc++)
+                            v[cc] = q >= 0 ? __ldg(src + 8 * h + cc) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                        for (int cc = 0; cc < 8; cc++)
+                            *reinterpret_cast<uint4*>(bs + h * QN * 128 + ((cc ^ (g & 7)) << 4)) = v[cc];
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b_full(s));
+            }
+            if (!ok) break;
+        }
+    } else {
+        // ---- epilogue: group eg = sub-tiles nb = eg (mod EPI_GROUPS); warp ew = warp % 4 reads TMEM lanes
+        //      32*ew .. 32*ew+31 (tile rows)
+        const int eg = (warp - 2 - GATHER_WARPS) / 4;
+        const int ew = warp & 3;
+        int nb = 0;
+        for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
+            const int c = p.tile_cell[tile];
+            const int qn = p.ccnt[c];
+            if (qn == 0) continue;
+            const int64_t cs = p.off[c], ce = p.off[c + 1];
+            const int row0 = p.tile_row0[tile];
+            const int qoff = p.coff[c];
+            const int row = row0 + 32 * ew + lane;
+            const bool rvalid = row >= cs && row < ce;
+            const bool wactive = (int64_t)(row0 + 32 * ew) < ce;
+            const float zr = rvalid ? p.zs[row] : 0.f;
+            const int blk_rel = (int)((row0 + 32 * ew) / 32 - cs / 32);
+            bool ok = true;
+            for (int i = 0; i * QN < qn; i++, nb++) {
+                if (nb % EPI_GROUPS != eg) continue;
+                const int sb = nb % B_STAGES, st = nb % T_STAGES;
+                if (!mbar_wait(t_full(st), (nb / T_STAGES) & 1, abort) ||
+                    !mbar_wait(b_full(sb), (nb / B_STAGES) & 1, abort)) {  // b_full: acquire the metadata
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const int nq = min(QN, qn - i * QN);
+                const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
+                const int* mq = meta_qid + sb * QN;
+                const float* ms = meta_qs + sb * QN;
+                const float* mc = meta_qc + sb * QN;
+                const float* mt = meta_th + sb * QN;
+                uint32_t acc[2][32];
+                tmem_ld32(ta, acc[0]);
+                if (nq > 32) tmem_ld32(ta + 32, acc[1]);
+                tmem_ld_wait();
+                if (wactive) {
+                    if (MODE == 0) {
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+#pragma unroll
+                            for (int jj = 0; jj < 32; jj++) {
+                                const int j = h * 32 + jj;
+                                if (j < nq) {
+                                    const float est = __fadd_rn(
+                                        __fmul_rn(__fmul_rn((float)(int32_t)acc[h][jj], ms[j]), zr), mc[j]);
+                                    const uint32_t m = __reduce_max_sync(0xffffffffu, rvalid ? f2o(est) : 0u);
+                                    if (lane == 0) p.bmc[(int64_t)(qoff + i * QN + j) * p.MB + blk_rel] = o2f(m);
+                                }
+                            }
+                        }
+                    } else {
+                        // per chunk: ballots of the 32 columns (lane jj keeps column jj's), then lane jj reserves
+                        // space for column jj; chunk 1's ballots run while chunk 0's atomics are in flight
+                        uint32_t mymask[2] = {0u, 0u};
+                        int mybase[2] = {0, 0};
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+#pragma unroll
+                            for (int jj = 0; jj < 32; jj++) {
+                                const int j = h * 32 + jj;
+                                if (j < nq) {
+                                    const float est = __fadd_rn(
+                                        __fmul_rn(__fmul_rn((float)(int32_t)acc[h][jj], ms[j]), zr), mc[j]);
+                                    const uint32_t mask = __ballot_sync(0xffffffffu, rvalid && est >= mt[j]);
+                                    if (lane == jj) mymask[h] = mask;
+                                }
+                            }
+                            if (mymask[h]) mybase[h] = atomicAdd(p.cnt + mq[h * 32 + lane], __popc(mymask[h]));
+                        }
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const unsigned any = __ballot_sync(0xffffffffu, mymask[h] != 0);
+#pragma unroll
+                            for (int jj = 0; jj < 32; jj++) {
+                                if (!(any & (1u << jj))) continue;  // warp-uniform
+                                const uint32_t mask = __shfl_sync(0xffffffffu, mymask[h], jj);
+                                const int base = __shfl_sync(0xffffffffu, mybase[h], jj);
+                                if (mask & (1u << lane)) {
+                                    const int j = h * 32 + jj;
+                                    const float est = __fadd_rn(
+                                        __fmul_rn(__fmul_rn((float)(int32_t)acc[h][jj], ms[j]), zr), mc[j]);
+                                    const int idx = base + __popc(mask & ((1u << lane) - 1u));
+                                    if (idx < p.M) {
+                                        const int64_t o = (int64_t)mq[j] * p.M + idx;
+                                        p.bval[o] = est;
+                                        p.bpos[o] = row;
+                                    }
+                                }
+                            }
+                        }
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(t_empty(st));
+                    mbar_arrive(b_empty(sb));
+                }
+            }
+            if (!ok) break;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    if (tid == 0 && *abort && p.status) atomicExch(p.status, 1);
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    return fn;
+}
+
+}  // namespace tc
+}  // namespace fvs
+
+extern "C" int fvs_i8_scan_tc(fvs_stream_t stream, int mode, const int8_t* q8, const float* qs, int B, int R,
+                              const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
+                              const int32_t* tile_cell, const int32_t* tile_row0, int ntiles, const int64_t* off,
+                              int NC, const int8_t* Z, int64_t N, const float* zs, const float* t0, int32_t* cnt,
+                              float* bval, int32_t* bpos, int M, float* bmc, int MB, int32_t* status) {
+    using namespace fvs::tc;
+    FVS_CHECK_ARG(mode == 0 || mode == 1);
+    FVS_CHECK_ARG(R == RB && B >= 0 && ntiles >= 0 && NC > 0 && N > 0);
+    FVS_CHECK_ARG(q8 && qs && qid && coff && ccnt && qcp && tile_cell && tile_row0 && off && Z && zs);
+    FVS_CHECK_ARG(((uintptr_t)Z & 15) == 0 && ((uintptr_t)q8 & 15) == 0);
+    if (mode == 0) FVS_CHECK_ARG(bmc && MB > 0);
+    if (mode == 1) FVS_CHECK_ARG(t0 && cnt && bval && bpos && M > 0);
+    if (ntiles == 0 || B == 0) return FVS_OK;
+    EncodeTiledFn enc = encode_fn();
+    if (!enc) return (int)cudaErrorNotSupported;
+    CUtensorMap map;
+    const cuuint64_t dims[2] = {(cuuint64_t)RB, (cuuint64_t)N};
+    const cuuint64_t strides[1] = {(cuuint64_t)RB};
+    const cuuint32_t box[2] = {128, (cuuint32_t)TILE_ROWS};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)Z, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return FVS_EINVAL;
+    Params p{q8, qs, qid, coff, ccnt, qcp, tile_cell, tile_row0, off, zs, t0, cnt, bval, bpos, bmc, status, M, MB};
+    cudaError_t e = mode ? fvs_ensure_smem((const void*)scan_tc_kernel<1>, SMEM_BYTES)
+                         : fvs_ensure_smem((const void*)scan_tc_kernel<0>, SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    static int nsm = 0;
+    if (nsm == 0) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+        if (nsm <= 0) nsm = 148;
+    }
+    const int grid = ntiles < nsm ? ntiles : nsm;
+    if (mode == 0)
+        scan_tc_kernel<0><<<grid, NTHREADS, SMEM_BYTES, stream>>>(map, p, ntiles);
+    else
+        scan_tc_kernel<1><<<grid, NTHREADS, SMEM_BYTES, stream>>>(map, p, ntiles);
+    return fvs_launch_status();
+}

@@ -13,8 +13,8 @@ namespace fvs {
 constexpr int MAX_TIERS = 8;
 
 struct TierSet {
-    int T;
-    int s[MAX_TIERS], e[MAX_TIERS], bits[MAX_TIERS], kb[MAX_TIERS], loff[MAX_TIERS];
+    int T, nwords;  // nwords: 4-byte plane words per candidate over all tiers
+    int s[MAX_TIERS], e[MAX_TIERS], bits[MAX_TIERS], kb[MAX_TIERS], loff[MAX_TIERS], wbase[MAX_TIERS + 1];
     float delta[MAX_TIERS], mid[MAX_TIERS], pw[MAX_TIERS][8];
     const uint8_t* planes[MAX_TIERS];
 };
@@ -132,6 +132,147 @@ __global__ void __launch_bounds__(256) lut_score_kernel(const int64_t* __restric
     }
 }
 
+
+// ------------------------------------------------------------------------------------------------ fused LUT score
+// One CTA per query: the query's table and tier sums are built in shared memory from Zq, then each warp scores
+// candidates.  A candidate's plane bytes are read as 4-byte words (every plane segment is a multiple of 4 bytes): lane
+// l owns words l, l+32, ... of the candidate's word list (tier-major, then plane, then position), issues all its loads
+// before any lookup, and folds delta_t * 2^(b-1-p) * scale_t into its partial sum, so a candidate needs one warp
+// reduction for the estimate and one for the variance.  Two candidates are in flight per warp.
+// Table layout: a plane word covers one block of 32 coordinates, ga = coordinate / 32 (tiers are contiguous 32-wide
+// groups from coordinate 0), and its byte c4 / nibble h select LUT group c = 2*c4 + h (4 coordinates).  Entry
+// (c, v, ga) sits at (c*16 + v)*GA + ga with GA a multiple of 32, so the 32 lanes of a warp, which hold consecutive
+// words, read 32 different banks.  Entries are fp32 slots holding the fp16-rounded value when HALF (the reference's
+// `LUTH` table), otherwise the fp32 value.
+template <bool HALF, int WPL>
+__global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __restrict__ pos, int B, int K,
+                                                           const float* __restrict__ qc, const float* __restrict__ Zq,
+                                                           int ldz, int D, int GA, TierSet ts,
+                                                           const __half* __restrict__ scale,
+                                                           const __half* __restrict__ sig, int64_t N,
+                                                           const int32_t* __restrict__ ncnt, float* __restrict__ est,
+                                                           float* __restrict__ sd) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
+    float* lut = reinterpret_cast<float*>(smem);
+    const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    const int lim = ncnt ? min(max(ncnt[q], 0), K) : K;
+    for (int i = lim + tid; i < K; i += blockDim.x) {
+        est[(int64_t)q * K + i] = kNeg;
+        sd[(int64_t)q * K + i] = 0.f;
+    }
+    if (lim == 0) return;
+    const float* z = Zq + (int64_t)q * ldz;
+    const int nblk = D / 32;
+    // one 4-coordinate group per thread (ga fastest across lanes: conflict-free stores); entry v sums the selected
+    // coordinates left to right in fp32, as acc += z_i * bit_i does
+    for (int gi = tid; gi < 8 * GA; gi += blockDim.x) {
+        const int ga = gi % GA, cgrp = gi / GA;
+        float z0 = 0.f, z1 = 0.f, z2 = 0.f, z3 = 0.f;
+        if (ga < nblk) {
+            const float4 zz = *reinterpret_cast<const float4*>(z + 32 * ga + 4 * cgrp);
+            z0 = zz.x;
+            z1 = zz.y;
+            z2 = zz.z;
+            z3 = zz.w;
+        }
+        float* out = lut + (cgrp * 16) * GA + ga;
+#pragma unroll
+        for (int v = 0; v < 16; v++) {
+            float acc = 0.f;
+            if (v & 8) acc = __fadd_rn(acc, z0);
+            if (v & 4) acc = __fadd_rn(acc, z1);
+            if (v & 2) acc = __fadd_rn(acc, z2);
+            if (v & 1) acc = __fadd_rn(acc, z3);
+            out[v * GA] = HALF ? __half2float(__float2half_rn(acc)) : acc;
+        }
+    }
+    if (warp < ts.T) {  // warp t reduces tier t
+        float a = 0.f, b = 0.f;
+        for (int i = ts.s[warp] + lane; i < ts.e[warp]; i += 32) {
+            const float x = z[i];
+            a += x;
+            b += x * x;
+        }
+        a = warp_sum(a);
+        b = warp_sum(b);
+        if (lane == 0) {
+            s_qsum[warp] = a;
+            s_qn2[warp] = b;
+        }
+    }
+    __syncthreads();
+    // per-lane word descriptors (same for every candidate): tier, plane, byte offset in the plane segment, block ga
+    int wt[WPL], wp[WPL], wj[WPL], wg[WPL];
+#pragma unroll
+    for (int u = 0; u < WPL; u++) {
+        const int w = lane + 32 * u;
+        int t = 0;
+        while (t + 1 < ts.T && w >= ts.wbase[t + 1]) t++;
+        const int r = w - ts.wbase[t], wpp = ts.kb[t] / 4;
+        wt[u] = w < ts.nwords ? t : -1;
+        wp[u] = r / wpp;
+        wj[u] = (r - wp[u] * wpp) * 4;
+        wg[u] = ts.s[t] / 32 + wj[u] / 4;
+    }
+    const int tl = lane < ts.T ? lane : 0;
+    const float dmq = ts.delta[tl] * ts.mid[tl] * s_qsum[tl], qn2l = s_qn2[tl];
+    const float qcv = qc[q];
+    for (int i0 = warp; i0 < lim; i0 += 2 * nw) {
+        int64_t nn[2];
+        bool live[2];
+        uint32_t wv[2][WPL];
+        float scl[2], sgl[2];
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            const int i = i0 + c * nw;
+            live[c] = i < lim;
+            nn[c] = live[c] ? pos[(int64_t)q * K + i] : 0;
+        }
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+#pragma unroll
+            for (int u = 0; u < WPL; u++) {
+                wv[c][u] = 0;
+                if (live[c] && wt[u] >= 0) {
+                    const int t = wt[u];
+                    wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(ts.planes[t] +
+                                                                        ((int64_t)wp[u] * N + nn[c]) * ts.kb[t] + wj[u]));
+                }
+            }
+            scl[c] = (live[c] && lane < ts.T) ? __half2float(scale[(int64_t)lane * N + nn[c]]) : 0.f;
+            sgl[c] = (live[c] && lane < ts.T) ? __half2float(sig[(int64_t)lane * N + nn[c]]) : 0.f;
+        }
+#pragma unroll
+        for (int c = 0; c < 2; c++) {
+            float part = lane < ts.T ? -dmq * scl[c] : 0.f;
+            float var = lane < ts.T ? qn2l * sgl[c] * sgl[c] : 0.f;
+#pragma unroll
+            for (int u = 0; u < WPL; u++) {
+                const int t = wt[u];
+                const float st = __shfl_sync(0xffffffffu, scl[c], t < 0 ? 0 : t);
+                if (t >= 0) {
+                    const float* lt = lut + wg[u];
+                    const uint32_t w = wv[c][u];
+                    float a = 0.f;
+#pragma unroll
+                    for (int bi = 0; bi < 4; bi++) {
+                        const uint32_t byt = (w >> (8 * bi)) & 0xffu;
+                        a += lt[((2 * bi) * 16 + (byt >> 4)) * GA] + lt[((2 * bi + 1) * 16 + (byt & 15u)) * GA];
+                    }
+                    part += a * (ts.pw[t][wp[u]] * ts.delta[t]) * st;
+                }
+            }
+            part = warp_sum(part);
+            var = warp_sum(var);
+            if (lane == 0 && live[c]) {
+                est[(int64_t)q * K + i0 + c * nw] = qcv + part;
+                sd[(int64_t)q * K + i0 + c * nw] = sqrtf(var);
+            }
+        }
+    }
+}
+
 static int make_tiers(TierSet& ts, int T, const int32_t* s, const int32_t* e, const int32_t* bits,
                       const float* delta, const uint8_t* const* planes) {
     if (T < 1 || T > MAX_TIERS) return FVS_ERANGE;
@@ -151,6 +292,13 @@ static int make_tiers(TierSet& ts, int T, const int32_t* s, const int32_t* e, co
         for (int p = 0; p < 8; p++) ts.pw[t][p] = (bits && p < bits[t]) ? (float)(1 << (bits[t] - 1 - p)) : 0.f;
         ts.planes[t] = planes ? planes[t] : nullptr;
     }
+    int w = 0;
+    for (int t = 0; t < T; t++) {
+        ts.wbase[t] = w;
+        w += ts.bits[t] * ts.kb[t] / 4;
+    }
+    ts.wbase[T] = w;
+    ts.nwords = w;
     return FVS_OK;
 }
 
@@ -201,5 +349,45 @@ extern "C" int fvs_lut_score(fvs_stream_t stream, const int64_t* pos, int B, int
         fvs::lut_score_kernel<false><<<B, 256, sm, stream>>>(pos, B, K, qc, L, LW, ts, (const __half*)scale,
                                                              (const __half*)sig, N, qsum, qn2, ncnt, est, sd);
     }
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
+                                int ldz, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e,
+                                const int32_t* tier_bits, const float* tier_delta, const uint8_t* const* tier_planes,
+                                const uint16_t* scale, const uint16_t* sig, int64_t N, const int32_t* ncnt, float* est,
+                                float* sd) {
+    FVS_CHECK_ARG(pos && qc && Zq && tier_s && tier_e && tier_bits && tier_delta && tier_planes && scale && sig);
+    FVS_CHECK_ARG(est && sd && B >= 0 && K >= 1 && N > 0 && D > 0 && D % 4 == 0 && ldz >= D && ldz % 4 == 0);
+    FVS_CHECK_ARG(((uintptr_t)Zq & 15) == 0);
+    fvs::TierSet ts;
+    int rc = fvs::make_tiers(ts, T, tier_s, tier_e, tier_bits, tier_delta, tier_planes);
+    if (rc) return rc;
+    for (int t = 0; t < T; t++) {
+        FVS_CHECK_ARG(tier_planes[t] != nullptr && tier_e[t] <= D && (tier_e[t] - tier_s[t]) % 32 == 0);
+        if (t > 0) FVS_CHECK_ARG(tier_s[t] == tier_e[t - 1]);
+    }
+    FVS_CHECK_ARG(tier_s[0] == 0);
+    const int wpl = (ts.nwords + 31) / 32;
+    if (wpl > 12) return FVS_ERANGE;
+    const int GA = ((D / 32) + 31) / 32 * 32;
+    FVS_CHECK_ARG(D % 32 == 0);
+    const size_t sm = (size_t)128 * GA * 4;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+#define FVS_LZ(H, W)                                                                                               \
+    do {                                                                                                           \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W>, sm);                         \
+        if (e != cudaSuccess) return (int)e;                                                                       \
+        fvs::lut_score_zq_kernel<H, W><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,                 \
+                                                              (const __half*)scale, (const __half*)sig, N, ncnt,    \
+                                                              est, sd);                                             \
+    } while (0)
+    if (half) {
+        if (wpl <= 4) FVS_LZ(true, 4); else if (wpl <= 8) FVS_LZ(true, 8); else FVS_LZ(true, 12);
+    } else {
+        if (wpl <= 4) FVS_LZ(false, 4); else if (wpl <= 8) FVS_LZ(false, 8); else FVS_LZ(false, 12);
+    }
+#undef FVS_LZ
     return fvs_launch_status();
 }

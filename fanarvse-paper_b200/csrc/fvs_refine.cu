@@ -18,8 +18,9 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
                                                             int ldq, int32_t* __restrict__ ids, int32_t* __restrict__ I,
                                                             int32_t* __restrict__ reads, float* __restrict__ score_k) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ SelectScratch ss;
-    __shared__ int s_namb, s_fill;
+    __shared__ unsigned hist[2][256];
+    __shared__ uint32_t s_bounds[2];
+    __shared__ int s_namb;
     uint32_t* klo = reinterpret_cast<uint32_t*>(smem);       // K
     uint32_t* khi = klo + K;                                  // K
     float* score = reinterpret_cast<float*>(khi + K);         // K
@@ -27,6 +28,7 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
     int32_t* amb_list = cid + K;                              // K
     unsigned long long* sb = reinterpret_cast<unsigned long long*>(amb_list + K + (K & 1));  // kp
     const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
     const int64_t qK = (int64_t)q * K;
     for (int i = tid; i < K; i += nt) {
         const float e = est[qK + i], s = sd[qK + i];
@@ -37,13 +39,18 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
         cid[i] = id;
         ids[qK + i] = id;
     }
-    if (tid == 0) {
-        s_namb = 0;
-        s_fill = 0;
+    if (tid == 0) s_namb = 0;
+    __syncthreads();
+    // (k+1)-th largest hi on warp 0, k-th largest lo on warp 1
+    if (warp == 0) {
+        const uint32_t v = warp_select_rth_largest<32, uint32_t>([&](int i) { return khi[i]; }, K, k + 1, hist[0]);
+        if (lane == 0) s_bounds[0] = v;
+    } else if (warp == 1) {
+        const uint32_t v = warp_select_rth_largest<32, uint32_t>([&](int i) { return klo[i]; }, K, k, hist[1]);
+        if (lane == 0) s_bounds[1] = v;
     }
     __syncthreads();
-    const uint32_t hk1 = block_select_rth_largest<32, uint32_t>([&](int i) { return khi[i]; }, K, k + 1, ss);
-    const uint32_t lk = block_select_rth_largest<32, uint32_t>([&](int i) { return klo[i]; }, K, k, ss);
+    const uint32_t hk1 = s_bounds[0], lk = s_bounds[1];
     // sure: lo > (k+1)-th hi; ambiguous: hi >= k-th lo and not sure (key order == float order)
     for (int i = tid; i < K; i += nt) {
         const bool sure = klo[i] > hk1;
@@ -54,7 +61,6 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
     __syncthreads();
     const int namb = s_namb;
     // exact fp32 dot products of the ambiguous rows (one warp per row, 8 halves per lane per step)
-    const int warp = tid >> 5, lane = tid & 31, nw = nt >> 5;
     const float* qrow = Q + (int64_t)q * ldq;
     for (int a = warp; a < namb; a += nw) {
         const int i = amb_list[a];
@@ -74,30 +80,48 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
         if (lane == 0) score[i] = acc;
     }
     __syncthreads();
-    // final top-k by (score desc, id asc)
-    auto key = [&](int i) {
-        return ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
-    };
-    const unsigned long long T = block_select_rth_largest<64, unsigned long long>(key, K, k, ss);
-    // keys above the k-th first (fewer than k of them), then equal keys up to k (fillers can repeat a key)
-    for (int i = tid; i < K; i += nt) {
-        const unsigned long long kk = key(i);
-        if (kk > T) sb[atomicAdd(&s_fill, 1)] = kk;
-    }
-    for (int i = k + tid; i < kp; i += nt) sb[i] = 0ull;
-    __syncthreads();
-    for (int i = tid; i < K; i += nt) {
-        const unsigned long long kk = key(i);
-        if (kk == T) {
-            const int slot = atomicAdd(&s_fill, 1);
-            if (slot < k) sb[slot] = kk;
+    // final top-k by (score desc, id asc) on warp 0: the k-th largest score key, then id order among ties
+    if (warp == 0) {
+        auto key = [&](int i) {
+            return ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
+        };
+        const uint32_t Th = warp_select_rth_largest<32, uint32_t>([&](int i) { return f2o(score[i]); }, K, k, hist[0]);
+        int gt = 0, eq = 0;
+        for (int i = lane; i < K; i += 32) {
+            const uint32_t h = f2o(score[i]);
+            gt += h > Th;
+            eq += h == Th;
         }
-    }
-    __syncthreads();
-    block_bitonic_desc(sb, kp);
-    for (int i = tid; i < k; i += nt) {
-        I[(int64_t)q * k + i] = (int32_t)(0xffffffffu - (uint32_t)sb[i]);
-        if (score_k) score_k[(int64_t)q * k + i] = o2f((uint32_t)(sb[i] >> 32));
+        gt = warp_sum_int(gt);
+        eq = warp_sum_int(eq);
+        unsigned long long T = (unsigned long long)Th << 32;
+        if (eq > k - gt)
+            T |= warp_select_rth_largest<32, uint32_t>(
+                [&](int i) { return f2o(score[i]) == Th ? (0xffffffffu - (uint32_t)cid[i]) : 0u; }, K, k - gt, hist[0]);
+        // keys above T first, then keys equal to T (fillers can repeat a key) up to k
+        int fill = 0;
+        for (int pass = 0; pass < 2; pass++) {
+            for (int b = 0; b < K; b += 32) {
+                const int i = b + lane;
+                unsigned long long kk = 0;
+                bool take = false;
+                if (i < K) {
+                    kk = key(i);
+                    take = pass == 0 ? kk > T : kk == T;
+                }
+                const unsigned m = __ballot_sync(0xffffffffu, take);
+                const int at = fill + __popc(m & ((1u << lane) - 1u));
+                if (take && at < k) sb[at] = kk;
+                fill += __popc(m);
+            }
+        }
+        for (int i = k + lane; i < kp; i += 32) sb[i] = 0ull;
+        __syncwarp();
+        warp_bitonic_desc(sb, kp);
+        for (int i = lane; i < k; i += 32) {
+            I[(int64_t)q * k + i] = (int32_t)(0xffffffffu - (uint32_t)sb[i]);
+            if (score_k) score_k[(int64_t)q * k + i] = o2f((uint32_t)(sb[i] >> 32));
+        }
     }
     if (tid == 0) reads[q] = namb;
 }

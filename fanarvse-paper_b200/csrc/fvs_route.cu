@@ -1,0 +1,161 @@
+// Routing and pairing: the probe list of each query and the cell-sorted pair list (CSR) the scan consumes.
+//
+// fvs_route_topk replaces `QM.topk(nprobe, 1).indices` on the fp16 routing product (`throughput/enginei8.py:67-68`):
+// one CTA per query selects the nprobe largest scores with a block radix select on 32-bit keys
+// (ordered fp16 score << 16 | (65535 - cell)), so the order is (score desc, cell asc) -- the reference leaves the order
+// of equal scores to torch.topk.
+// fvs_pairs replaces `pairs_fast` (`throughput/enginei8.py:11-16`): a counting sort of the (query, cell) pairs by cell
+// (histogram, exclusive scan, atomic scatter).  Within a cell the query order is the scatter order; nothing downstream
+// depends on it (block maxima are addressed through `slot`, emitted sets are sets).
+#include "fvs_common.cuh"
+
+namespace fvs {
+
+__device__ __forceinline__ uint32_t h2o(uint16_t u) { return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u); }
+
+constexpr int RT_THREADS = 512;
+
+__global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* __restrict__ QM, int NC, int nprobe,
+                                                                int kp, int64_t* __restrict__ probe) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ SelectScratch ss;
+    __shared__ int s_fill;
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem);        // NC
+    unsigned long long* sb = reinterpret_cast<unsigned long long*>(keys + NC + (NC & 1));  // kp (as 64-bit slots)
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const uint16_t* row = QM + (int64_t)q * NC;
+    for (int c = tid; c < NC; c += nt) keys[c] = (h2o(row[c]) << 16) | (uint32_t)(0xffff - c);
+    if (tid == 0) s_fill = 0;
+    __syncthreads();
+    const uint32_t T = block_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, NC, nprobe, ss);
+    for (int c = tid; c < NC; c += nt)
+        if (keys[c] >= T) {
+            const int slot = atomicAdd(&s_fill, 1);
+            if (slot < nprobe) sb[slot] = keys[c];
+        }
+    for (int i = nprobe + tid; i < kp; i += nt) sb[i] = 0ull;
+    __syncthreads();
+    block_bitonic_desc(sb, kp);
+    for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = 0xffff - (int64_t)(sb[i] & 0xffffu);
+}
+
+__global__ void pair_hist_kernel(const int64_t* __restrict__ probe, int B, int nprobe, int ncols,
+                                 int32_t* __restrict__ ccnt) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)B * ncols) return;
+    const int q = (int)(i / ncols), j = (int)(i - (int64_t)q * ncols);
+    atomicAdd(ccnt + probe[(int64_t)q * nprobe + j], 1);
+}
+
+// exclusive scan of NC counts in one CTA of 1024 threads
+__global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t* __restrict__ ccnt, int NC,
+                                                         int32_t* __restrict__ coff) {
+    __shared__ int wsum[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (NC + 1023) / 1024;
+    const int b0 = tid * per;
+    int local = 0;
+    for (int i = 0; i < per; i++)
+        if (b0 + i < NC) local += ccnt[b0 + i];
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = wsum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += v;
+        }
+        wsum[lane] = w;
+    }
+    __syncthreads();
+    int run = incl - local + (warp > 0 ? wsum[warp - 1] : 0);
+    for (int i = 0; i < per; i++)
+        if (b0 + i < NC) {
+            coff[b0 + i] = run;
+            run += ccnt[b0 + i];
+        }
+}
+
+__global__ void pair_scatter_kernel(const int64_t* __restrict__ probe, int B, int nprobe, int ncols, int NC,
+                                    const __half* __restrict__ QM, const float* __restrict__ mnorm,
+                                    const int32_t* __restrict__ coff, int32_t* __restrict__ cursor,
+                                    int32_t* __restrict__ qid, float* __restrict__ qcp, int32_t* __restrict__ slot) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)B * ncols) return;
+    const int q = (int)(i / ncols), j = (int)(i - (int64_t)q * ncols);
+    const int c = (int)probe[(int64_t)q * nprobe + j];
+    const int pos = coff[c] + atomicAdd(cursor + c, 1);
+    qid[pos] = q;
+    const float v = __half2float(QM[(int64_t)q * NC + c]);
+    qcp[pos] = mnorm ? __fmul_rn(v, mnorm[c]) : v;
+    if (slot) slot[i] = pos;
+}
+
+// q8, qs from the projected queries z [B, ldz] (`throughput/enginei8.py:38`): qs = max(max|z|, 1e-12) / 127,
+// q8 = clamp(round_half_even(z / qs), -127, 127); one warp per query.  The division by the constant 127 is evaluated as
+// torch evaluates a tensor-by-scalar division on the GPU, a multiplication by the fp32 reciprocal; z / qs is a true
+// division.
+__global__ void quantize_kernel(const float* __restrict__ z, int B, int R, int ldz, int8_t* __restrict__ q8,
+                                float* __restrict__ qs) {
+    const int q = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (q >= B) return;
+    const float* zr = z + (int64_t)q * ldz;
+    float m = 0.f;
+    for (int i = lane; i < R; i += 32) m = fmaxf(m, fabsf(zr[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    const float sc = __fmul_rn(fmaxf(m, 1e-12f), 1.0f / 127.0f);
+    for (int i = lane; i < R; i += 32) {
+        const float v = rintf(__fdiv_rn(zr[i], sc));
+        q8[(int64_t)q * R + i] = (int8_t)fminf(fmaxf(v, -127.f), 127.f);
+    }
+    if (lane == 0) qs[q] = sc;
+}
+
+}  // namespace fvs
+
+extern "C" int fvs_quantize(fvs_stream_t stream, const float* z, int B, int R, int ldz, int8_t* q8, float* qs) {
+    FVS_CHECK_ARG(z && q8 && qs && B >= 0 && R > 0 && ldz >= R);
+    if (B == 0) return FVS_OK;
+    fvs::quantize_kernel<<<(B + 7) / 8, 256, 0, stream>>>(z, B, R, ldz, q8, qs);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_route_topk(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int64_t* probe) {
+    FVS_CHECK_ARG(QM && probe && B >= 0 && NC > 0 && nprobe >= 1 && nprobe <= NC);
+    if (NC > 65535 || nprobe > 4096) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    int kp = 1;
+    while (kp < nprobe) kp <<= 1;
+    const size_t sm = (size_t)(NC + (NC & 1)) * 4 + (size_t)kp * 8;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::route_topk_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::route_topk_kernel<<<B, fvs::RT_THREADS, sm, stream>>>(QM, NC, nprobe, kp, probe);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_pairs(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int ncols, int NC,
+                         const uint16_t* QM, const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt,
+                         float* qcp, int32_t* slot, int32_t* work) {
+    FVS_CHECK_ARG(probe && QM && qid && coff && ccnt && qcp && work && B >= 0 && NC > 0);
+    FVS_CHECK_ARG(ncols >= 1 && ncols <= nprobe);
+    cudaError_t e = cudaMemsetAsync(ccnt, 0, (size_t)NC * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(work, 0, (size_t)NC * 4, stream);
+    if (e != cudaSuccess) return (int)e;
+    const int64_t n = (int64_t)B * ncols;
+    const unsigned grid = (unsigned)((n + 255) / 256);
+    if (n > 0) fvs::pair_hist_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, ncols, ccnt);
+    fvs::pair_scan_kernel<<<1, 1024, 0, stream>>>(ccnt, NC, coff);
+    if (n > 0)
+        fvs::pair_scatter_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, ncols, NC, (const __half*)QM, mnorm, coff,
+                                                           work, qid, qcp, slot);
+    return fvs_launch_status();
+}

@@ -16,19 +16,27 @@ __global__ void threshold_kernel(const float* __restrict__ bmc, int MB, const in
     __shared__ int s_cnt_valid;
     uint32_t* keys = reinterpret_cast<uint32_t*>(smem);
     const int q = blockIdx.x, tid = threadIdx.x;
-    // exclusive prefix of block counts over the n1 first-pass cells (n1 <= 1024)
-    if (tid == 0) {
-        int acc = 0;
-        for (int j = 0; j < n1; j++) {
+    // exclusive prefix of the first-pass cells' block counts (n1 <= 1024), one cell per thread
+    {
+        int nb = 0;
+        for (int j = tid; j < n1; j += blockDim.x) {
             const int64_t c = probe[(int64_t)q * nprobe + j];
             const int64_t s = off[c], e = off[c + 1];
-            s_base[j] = acc;
-            acc += (e > s) ? (int)((e - 1) / 32 - s / 32 + 1) : 0;
+            nb = (e > s) ? (int)((e - 1) / 32 - s / 32 + 1) : 0;
+            s_base[j + 1] = nb;  // counts first, scanned below
         }
-        s_base[n1] = acc;
-        s_cnt_valid = 0;
+        if (tid == 0) s_cnt_valid = 0;
+        __syncthreads();
+        if (tid == 0) {
+            int acc = 0;
+            s_base[0] = 0;
+            for (int j = 1; j <= n1; j++) {
+                acc += s_base[j];
+                s_base[j] = acc;
+            }
+        }
+        __syncthreads();
     }
-    __syncthreads();
     const int n = s_base[n1];
     int nvalid = 0;
     for (int j = 0; j < n1; j++) {
@@ -76,7 +84,7 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
                                    float delta, int didx) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ SelectScratch ss;
-    __shared__ int s_fill, s_ncnt;
+    __shared__ int s_fill, s_ncnt, s_red[32];
     unsigned long long* sb = reinterpret_cast<unsigned long long*>(smem);   // Kp sort buffer
     unsigned long long* sk = sb + Kp;                                        // staged keys (<= SEL_SMEM_KEYS)
     const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
@@ -95,7 +103,27 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
         for (int i = tid; i < Kp; i += nt) sb[i] = i < n ? key(i) : (i < K ? filler : 0ull);
         __syncthreads();
     } else {
-        const unsigned long long T = block_select_rth_largest<64, unsigned long long>(key, n, K, ss);
+        // K-th largest score key; ties at it are resolved by position only when they straddle the K-th place
+        const uint32_t Th = block_select_rth_largest<32, uint32_t>([&](int i) { return (uint32_t)(key(i) >> 32); }, n,
+                                                                   K, ss);
+        int gt = 0, eq = 0;
+        for (int i = tid; i < n; i += nt) {
+            const uint32_t h = (uint32_t)(key(i) >> 32);
+            gt += h > Th;
+            eq += h == Th;
+        }
+        gt = block_sum_int(gt, s_red);
+        eq = block_sum_int(eq, s_red);
+        unsigned long long T = (unsigned long long)Th << 32;
+        if (eq > K - gt) {
+            const uint32_t Tl = block_select_rth_largest<32, uint32_t>(
+                [&](int i) {
+                    const unsigned long long k = key(i);
+                    return (uint32_t)(k >> 32) == Th ? (uint32_t)k : 0u;
+                },
+                n, K - gt, ss);
+            T |= Tl;
+        }
         for (int i = tid; i < n; i += nt) {
             const unsigned long long k = key(i);
             if (k >= T) {  // keys are unique (one entry per probed row): exactly K of them
@@ -122,6 +150,137 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
         atomicAdd(&s_ncnt, m);
         __syncthreads();
         if (tid == 0) ncnt[q] = s_ncnt;
+    }
+}
+
+
+// ------------------------------------------------------------------------------------------------ warp-per-query
+constexpr int WQ_WARPS = 8;  // queries per CTA in the warp-per-query kernels
+
+// threshold (same contract as threshold_kernel), one warp per query; keys staged in the warp's shared slice
+__global__ void __launch_bounds__(32 * WQ_WARPS) threshold_warp_kernel(const float* __restrict__ bmc, int MB,
+                                                                      const int32_t* __restrict__ slot,
+                                                                      const int64_t* __restrict__ probe, int nprobe,
+                                                                      int n1, const int64_t* __restrict__ off, int B,
+                                                                      int r, int cap, float* __restrict__ t0) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * WQ_WARPS + warp;
+    if (q >= B) return;
+    unsigned* hist = reinterpret_cast<unsigned*>(smem) + warp * (256 + cap);
+    uint32_t* keys = hist + 256;
+    int base = 0, nvalid = 0;
+    for (int j0 = 0; j0 < n1; j0 += 32) {
+        const int j = j0 + lane;
+        int nb = 0;
+        int64_t srow = 0;
+        if (j < n1) {
+            const int64_t c = probe[(int64_t)q * nprobe + j];
+            const int64_t s = off[c], e = off[c + 1];
+            nb = (e > s) ? (int)((e - 1) / 32 - s / 32 + 1) : 0;
+            srow = (int64_t)slot[(int64_t)q * n1 + j] * MB;
+        }
+        int incl = nb;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const int tot = __shfl_sync(0xffffffffu, incl, 31);
+        // each lane copies its cell's block maxima (short rows), then the warp continues
+        int kb = base + incl - nb;
+        for (int b = 0; b < nb; b++) {
+            const float v = bmc[srow + b];
+            keys[kb + b] = f2o(v);
+            nvalid += v > -1e29f;
+        }
+        base += tot;
+    }
+    __syncwarp();
+    nvalid = warp_sum_int(nvalid);
+    const int n = base;
+    float res;
+    if (nvalid >= r) {
+        res = o2f(warp_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, n, r, hist));
+    } else if (nvalid > 0) {
+        unsigned m = 0xffffffffu;
+        for (int i = lane; i < n; i += 32)
+            if (o2f(keys[i]) > -1e29f) m = min(m, keys[i]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = min(m, __shfl_xor_sync(0xffffffffu, m, o));
+        res = o2f(m);
+    } else {
+        res = 1e30f;
+    }
+    if (lane == 0) t0[q] = res;
+}
+
+// stage-1 top-K (same contract as select_topk_kernel) for K <= 512, one warp per query; keys read from global
+__global__ void __launch_bounds__(32 * WQ_WARPS) select_topk_warp_kernel(
+    const float* __restrict__ bval, const int32_t* __restrict__ bpos, const int32_t* __restrict__ cnt, int B, int M,
+    int K, int Kp, int64_t* __restrict__ pos, float* __restrict__ est1, uint8_t* __restrict__ ok,
+    int32_t* __restrict__ ncnt, float delta, int didx) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = blockIdx.x * WQ_WARPS + warp;
+    if (q >= B) return;
+    unsigned long long* sb = reinterpret_cast<unsigned long long*>(smem) + (int64_t)warp * (Kp + 128);
+    unsigned* hist = reinterpret_cast<unsigned*>(sb + Kp);
+    const int c = cnt[q];
+    const int n = min(max(c, 0), M);
+    const float* bv = bval + (int64_t)q * M;
+    const int32_t* bp = bpos + (int64_t)q * M;
+    auto key = [&](int i) { return cand_key(bv[i], bp[i]); };
+    if (n <= K) {
+        const unsigned long long filler = cand_key(kNeg, 0);
+        for (int i = lane; i < Kp; i += 32) sb[i] = i < n ? key(i) : (i < K ? filler : 0ull);
+    } else {
+        const uint32_t Th =
+            warp_select_rth_largest<32, uint32_t>([&](int i) { return f2o(bv[i]); }, n, K, hist);
+        int gt = 0, eq = 0;
+        for (int i = lane; i < n; i += 32) {
+            const uint32_t h = f2o(bv[i]);
+            gt += h > Th;
+            eq += h == Th;
+        }
+        gt = warp_sum_int(gt);
+        eq = warp_sum_int(eq);
+        unsigned long long T = (unsigned long long)Th << 32;
+        if (eq > K - gt) {
+            const uint32_t Tl = warp_select_rth_largest<32, uint32_t>(
+                [&](int i) { return f2o(bv[i]) == Th ? (0xffffffffu - (uint32_t)bp[i]) : 0u; }, n, K - gt, hist);
+            T |= Tl;
+        }
+        int fill = 0;
+        for (int b = 0; b < n; b += 32) {
+            const int i = b + lane;
+            unsigned long long k = 0;
+            bool take = false;
+            if (i < n) {
+                k = key(i);
+                take = k >= T;
+            }
+            const unsigned m = __ballot_sync(0xffffffffu, take);
+            const int at = fill + __popc(m & ((1u << lane) - 1u));
+            if (take && at < K) sb[at] = k;
+            fill += __popc(m);
+        }
+        for (int i = K + lane; i < Kp; i += 32) sb[i] = 0ull;
+    }
+    __syncwarp();
+    warp_bitonic_desc(sb, Kp);
+    for (int i = lane; i < K; i += 32) {
+        const unsigned long long k = sb[i];
+        est1[(int64_t)q * K + i] = o2f((uint32_t)(k >> 32));
+        pos[(int64_t)q * K + i] = (int64_t)(0xffffffffu - (uint32_t)k);
+    }
+    if (lane == 0) ok[q] = (c >= K && c <= M) ? 1 : 0;
+    if (ncnt != nullptr) {
+        const float thr = __fsub_rn(o2f((uint32_t)(sb[didx] >> 32)), delta);
+        int m = 0;
+        for (int i = lane; i < K; i += 32) m += o2f((uint32_t)(sb[i] >> 32)) >= thr;
+        m = warp_sum_int(m);
+        if (lane == 0) ncnt[q] = m;
     }
 }
 
@@ -164,6 +323,15 @@ extern "C" int fvs_threshold(fvs_stream_t stream, const float* bmc, int MB, cons
     FVS_CHECK_ARG(n1 >= 1 && n1 <= nprobe && r >= 1);
     if (n1 > 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
+    const int cap = n1 * MB;
+    const size_t smw = (size_t)fvs::WQ_WARPS * (256 + cap) * 4;
+    if (smw <= 96 * 1024) {
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::threshold_warp_kernel, smw);
+        if (e != cudaSuccess) return (int)e;
+        fvs::threshold_warp_kernel<<<(B + fvs::WQ_WARPS - 1) / fvs::WQ_WARPS, 32 * fvs::WQ_WARPS, smw, stream>>>(
+            bmc, MB, slot, probe, nprobe, n1, off, B, r, cap, t0);
+        return fvs_launch_status();
+    }
     const size_t sm = (size_t)n1 * MB * sizeof(uint32_t);
     if (sm > 200 * 1024) return FVS_ERANGE;
     cudaError_t e = fvs_ensure_smem((const void*)fvs::threshold_kernel, sm);
@@ -180,6 +348,14 @@ extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int
     if (K > 4096) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const int Kp = fvs::pow2_at_least(K);
+    if (Kp <= 512 && M < 0) {  // warp-per-query variant: slower than the staged block version; kept disabled
+        const size_t smw = (size_t)fvs::WQ_WARPS * (Kp + 128) * 8;
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::select_topk_warp_kernel, smw);
+        if (e != cudaSuccess) return (int)e;
+        fvs::select_topk_warp_kernel<<<(B + fvs::WQ_WARPS - 1) / fvs::WQ_WARPS, 32 * fvs::WQ_WARPS, smw, stream>>>(
+            bval, bpos, cnt, B, M, K, Kp, pos, est1, ok, ncnt, delta, delta_idx);
+        return fvs_launch_status();
+    }
     const size_t sm = (size_t)(Kp + fvs::SEL_SMEM_KEYS) * 8;
     cudaError_t e = fvs_ensure_smem((const void*)fvs::select_topk_kernel, sm);
     if (e != cudaSuccess) return (int)e;

@@ -4,10 +4,10 @@ Mirrors `throughput/enginei8.py` (class EngineI8 with the final knobs of `throug
 `search(Qb, K, z, nprobe, k) -> (I [B,k], reads [B], cand_ids [B,K])`, one CUDA graph per (B, K, z, nprobe, k), the
 exactness flag as the only host synchronisation, and the reference's recompute path for flagged queries.
 
-Host-side PyTorch keeps what the reference computes with cuBLAS / torch before the kernels (routing product and top-n_p,
-query quantisation, the pair CSR, the rotated LUT query); everything after that -- the int8 scan passes, threshold,
-stage-1 top-K with the delta rule, LUT build and scoring, classification, exact re-rank and final top-k -- runs in
-libfanar_b200 through its C ABI.  There is no CPU path: without the shared library (or without a GPU) `search` raises.
+Host-side PyTorch keeps the dense products the reference computes with cuBLAS (routing product QM, the query
+projections for quantisation and for the LUT, q . c); everything else -- top-n_p routing selection, the pair lists,
+the int8 scan passes, threshold, stage-1 top-K with the delta rule, LUT scoring, classification, exact re-rank and
+final top-k -- runs in libfanar_b200 through its C ABI.  There is no CPU path: without the shared library (or without a GPU) `search` raises.
 """
 from __future__ import annotations
 
@@ -97,19 +97,6 @@ class IndexI8:
         return self.R + 4 + sum((e - s) * b for s, e, b in self.TS) / 8 + 4 * self.T
 
 
-def pairs_fast(probe, NC, QM, scale):
-    """CSR of (query, cell) pairs sorted by cell (`throughput/enginei8.py:11-16`): qid, coff, ccnt, qcp, o."""
-    B, npr = probe.shape
-    flat = probe.flatten().to(torch.int32)
-    _, o = torch.sort(flat, stable=True)
-    qid = (o // npr).to(torch.int32).contiguous()
-    cnt = torch.zeros(NC, dtype=torch.int32, device=probe.device).scatter_add_(0, flat.long(), torch.ones_like(flat))
-    off = torch.cumsum(cnt, 0) - cnt
-    fo = flat[o].long()
-    qc = QM[qid.long(), fo].float() * scale[fo]
-    return qid, off.to(torch.int32).contiguous(), cnt.contiguous(), qc.contiguous(), o
-
-
 class EngineB200I8:
     """The reference's EngineI8 (FanarVSE-T) on libfanar_b200.  Knobs as in `throughput/e_v3final.py:28-32`."""
     RHO = 0.6
@@ -117,6 +104,7 @@ class EngineB200I8:
     DELTA = 0.07
     LUTH = True
     BETA = None
+    SCAN = "tc"      # "tc": tcgen05 kernel (the product path); "mma": the mma.sync kernel kept as a baseline
 
     def __init__(self, index: IndexI8):
         self.ix = index
@@ -127,6 +115,35 @@ class EngineB200I8:
         self.launches = 0          # library kernel launches issued (eager) or captured
         self.timing = None         # dict name -> [(start, end) CUDA events] when timing library calls
         self.L = _lib.lib()
+        self.status = torch.zeros(1, dtype=torch.int32, device=index.device)
+        self.work = torch.zeros(index.NC, dtype=torch.int32, device=index.device)
+
+    def pairs(self, probe, ncols, QM, want_slot):
+        """pair list by cell over the first ncols probe columns (`throughput/enginei8.py:11-16`)."""
+        ix = self.ix
+        B, npr = probe.shape
+        dev = probe.device
+        n = B * ncols
+        qid = torch.empty(n, dtype=torch.int32, device=dev)
+        qcp = torch.empty(n, device=dev)
+        coff = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        ccnt = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        slot = torch.empty(n, dtype=torch.int32, device=dev) if want_slot else None
+        self._call("pairs", self.L.fvs_pairs, ptr(probe), B, npr, ncols, ix.NC, ptr(QM), ptr(ix.mnorm), ptr(qid),
+                   ptr(coff), ptr(ccnt), ptr(qcp), ptr(slot), ptr(self.work))
+        self.launches += 2   # fvs_pairs issues three kernels
+        return qid, coff, ccnt, qcp, slot
+
+    def _scan(self, mode, name, q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc):
+        ix = self.ix
+        if self.SCAN == "tc":
+            self._call(name, self.L.fvs_i8_scan_tc, mode, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
+                       ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z), ix.N,
+                       ptr(ix.zs), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB, ptr(self.status))
+        else:
+            self._call(name, self.L.fvs_i8_scan, mode, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
+                       ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z),
+                       ptr(ix.zs), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB)
 
     def _call(self, name, fn, *args):
         """Call one C-ABI entry point on the current stream; count it; optionally bracket it with CUDA events."""
@@ -144,11 +161,13 @@ class EngineB200I8:
 
     # ------------------------------------------------------------------ stage 1
     def quantize(self, Qb):
-        """q8, qs (`throughput/enginei8.py:38`)."""
-        z = Qb @ self.ix.Vr
-        qs = z.abs().amax(1).clamp(min=1e-12) / 127
-        q8 = torch.round(z / qs[:, None]).clamp(-127, 127).to(torch.int8).contiguous()
-        return q8, qs.float().contiguous()
+        """q8, qs (`throughput/enginei8.py:38`): fp32 projection by cuBLAS, then one quantisation kernel."""
+        z = (Qb @ self.ix.Vr).contiguous()
+        B, R = z.shape
+        q8 = torch.empty(B, R, dtype=torch.int8, device=z.device)
+        qs = torch.empty(B, device=z.device)
+        self._call("quantize", self.L.fvs_quantize, ptr(z), B, R, R, ptr(q8), ptr(qs))
+        return q8, qs
 
     def first_pass_cells(self, K, nprobe, rho_override=None):
         beta = (1.1 if K <= 400 else 0.7) if not self.BETA else self.BETA
@@ -166,23 +185,17 @@ class EngineB200I8:
         rho = rho_override if rho_override else (self.RHO or (0.75 if K <= 400 else 0.5))
         n1 = self.first_pass_cells(K, probe.shape[1], rho_override)
         probe = probe.contiguous()
-        qid, coff, ccnt, qcp, o = pairs_fast(probe[:, :n1], ix.NC, QM, ix.mnorm)
+        qid, coff, ccnt, qcp, slot = self.pairs(probe, n1, QM, True)
         bmc = torch.empty(B * n1 * ix.MB, device=dev)
-        self._call("i8_scan_first", L.fvs_i8_scan, 0, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
-                   ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z),
-                   ptr(ix.zs), None, None, None, None, 0, ptr(bmc), ix.MB)
-        slot = torch.empty_like(o, dtype=torch.int32)
-        slot[o] = torch.arange(len(o), device=dev, dtype=torch.int32)
+        self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt, qcp, None, None, None, None, 0, bmc)
         t0 = torch.empty(B, device=dev)
         self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1,
                    ptr(ix.off), B, int(np.ceil(rho * K)), ptr(t0))
-        qid, coff, ccnt, qcp, _ = pairs_fast(probe, ix.NC, QM, ix.mnorm)
+        qid, coff, ccnt, qcp, _ = self.pairs(probe, probe.shape[1], QM, False)
         cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
-        self._call("i8_scan_emit", L.fvs_i8_scan, 1, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
-                   ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z),
-                   ptr(ix.zs), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, None, 0)
+        self._scan(1, "i8_scan_emit", q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None)
         pos = torch.empty(B, K, dtype=torch.int64, device=dev)
         est1 = torch.empty(B, K, device=dev)
         ok = torch.empty(B, dtype=torch.uint8, device=dev)
@@ -190,7 +203,8 @@ class EngineB200I8:
         ncnt = torch.empty(B, dtype=torch.int32, device=dev) if use_delta else None
         self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
                    ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
-        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, npairs=int(qid.numel()))
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, npairs=int(qid.numel()),
+                          bval=bval, bpos=bpos, slot=slot)
         return pos, ok.bool(), est1, ncnt
 
     # ------------------------------------------------------------------ stages 2-3
@@ -217,6 +231,20 @@ class EngineB200I8:
                    ptr(qn2), ptr(ncnt), ptr(est), ptr(sd))
         return est, sd
 
+    def score_lut_zq(self, QC, pos, Zq, ncnt, half):
+        """fused table build + LUT scoring (`throughput/s2lut.py:92-126` in one launch)."""
+        ix = self.ix
+        B, K = pos.shape
+        est = torch.empty(B, K, device=pos.device)
+        sd = torch.empty(B, K, device=pos.device)
+        self._call("lut_score", self.L.fvs_lut_score_zq, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D, int(half),
+                   ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N, ptr(ncnt),
+                   ptr(est), ptr(sd))
+        return est, sd
+
+    def rotated_query(self, Qb):
+        return (Qb.half() @ self.ix.VP16).float().contiguous()             # `throughput/s2lut.py:122`
+
     def refine(self, Qb, pos, est, sd, z, k):
         ix = self.ix
         B, K = pos.shape
@@ -232,15 +260,18 @@ class EngineB200I8:
     def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None):
         """`throughput/enginei8.py:80-95`."""
         half = self.LUTH if half is None else half
-        pre = self.luts(Qb, half)
-        est, sd = self.score_lut(QC, pos, pre, ncnt, half)
+        Zq = self.rotated_query(Qb)
+        est, sd = self.score_lut_zq(QC, pos, Zq, ncnt, half)
         I, reads, ids, score_k = self.refine(Qb, pos, est, sd, z, k)
-        self._last.update(est=est, sd=sd, Zq=pre[3], score_k=score_k)
+        self._last.update(est=est, sd=sd, Zq=Zq, score_k=score_k)
         return ok, I, reads.long(), ids
 
     def route(self, Qb, nprobe):
-        QM = Qb.half() @ self.ix.meansN.T                                   # `throughput/enginei8.py:67-68`
-        return QM, QM.topk(nprobe, 1).indices
+        """QM = fp16(Q) @ meansN^T (cuBLAS) and the nprobe best cells per query (`throughput/enginei8.py:67-68`)."""
+        QM = (Qb.half() @ self.ix.meansN.T).contiguous()
+        probe = torch.empty(Qb.shape[0], nprobe, dtype=torch.int64, device=Qb.device)
+        self._call("route_topk", self.L.fvs_route_topk, ptr(QM), Qb.shape[0], self.ix.NC, nprobe, ptr(probe))
+        return QM, probe
 
     def _gpu(self, Qb, K, z, nprobe, k):
         """`throughput/enginei8.py:61-70` (NROUTE branch)."""
@@ -256,9 +287,7 @@ class EngineB200I8:
         QC = (Qb @ self.ix.c).contiguous()
         QM, probe = self.route(Qb, nprobe)
         pos, ok, est1, _ = self.stage1_i8(Qb, QM, probe, K, rho_override=1.0, M_override=65536)
-        self.nbad2 += int((~ok).sum())
-        pre = self.luts(Qb, False)
-        est, sd = self.score_lut(QC, pos, pre, None, False)
+        est, sd = self.score_lut_zq(QC, pos, self.rotated_query(Qb), None, False)
         I, reads, ids, _ = self.refine(Qb, pos, est, sd, z, k)
         return I, reads.long(), ids
 
@@ -287,13 +316,49 @@ class EngineB200I8:
         g.replay()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         I, nr, ids = I.clone(), nr.clone(), ids.clone()
-        if not bool(ok.all()):                                             # the only synchronisation
-            bad = torch.nonzero(~ok).flatten()
+        flags = torch.cat([ok.to(torch.int32), self.status]).cpu()         # the only synchronisation
+        if int(flags[-1]) != 0:
+            raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
+        if not bool(flags[:-1].all()):
+            bad = torch.nonzero(flags[:-1] == 0).flatten()
             self.nbad += len(bad)
-            a, b, c = self._fallback(Qb[bad], K, z, nprobe, k)
-            I[bad], nr[bad] = a, b
-            ids[bad] = c[:, :ids.shape[1]]
+            a, b, c = self._fallback_graphed(Qb, bad, K, z, nprobe, k)
+            badd = bad.to(Qb.device)
+            I[badd], nr[badd] = a, b
+            ids[badd] = c[:, :ids.shape[1]]
         return I, nr, ids
+
+    FALLBACK_BUCKETS = (8, 16, 32, 64, 128, 256)
+
+    def _fallback_graphed(self, Qb, bad, K, z, nprobe, k):
+        """`_fallback` on the flagged rows, replayed from a CUDA graph captured per padded batch size (the rows are
+        padded with copies of the first flagged row; their results are discarded)."""
+        nb = len(bad)
+        bucket = next((b for b in self.FALLBACK_BUCKETS if b >= nb), None)
+        if bucket is None:                                                 # very many flagged rows: eager, chunked
+            outs = [self._fallback(Qb[bad[i:i + 256].to(Qb.device)], K, z, nprobe, k) for i in range(0, nb, 256)]
+            return tuple(torch.cat(x) for x in zip(*outs))
+        key = ("fb", bucket, K, z, nprobe, k)
+        if key not in self.graphs:
+            qs = Qb[:1].repeat(bucket, 1).contiguous()
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                for _ in range(2):
+                    self._fallback(qs, K, z, nprobe, k)
+            torch.cuda.current_stream().wait_stream(st)
+            g = torch.cuda.CUDAGraph()
+            n0 = self.launches
+            with torch.cuda.graph(g):
+                outs = self._fallback(qs, K, z, nprobe, k)
+            self.graph_launches[key] = self.launches - n0
+            self.graphs[key] = (g, qs, outs)
+        g, qs, (a, b, c) = self.graphs[key]
+        idx = torch.cat([bad, bad[:1].repeat(bucket - nb)]).to(Qb.device)
+        qs.copy_(Qb[idx])
+        g.replay()
+        self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
+        return a[:nb].clone(), b[:nb].clone(), c[:nb].clone()
 
     def search_eager(self, Qb, K, z, nprobe, k):
         """One search without graph capture (same kernels); returns the intermediates for parity tests."""

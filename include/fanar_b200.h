@@ -29,6 +29,29 @@ typedef struct CUstream_st* fvs_stream_t; /* == cudaStream_t */
 int fvs_version(void);
 const char* fvs_arch(void);
 
+/*
+ * Query quantisation (`throughput/enginei8.py:38`): qs[q] = max(max_r |z[q,r]|, 1e-12) / 127,
+ * q8[q,r] = clamp(round_half_even(z[q,r] / qs[q]), -127, 127); z [B, ldz] f32 = Q @ Vr.
+ */
+int fvs_quantize(fvs_stream_t stream, const float* z, int B, int R, int ldz, int8_t* q8, float* qs);
+
+/*
+ * Routing selection (`throughput/enginei8.py:67-68`, `QM.topk(nprobe, 1).indices`): probe[q, :] = the nprobe cells of
+ * largest fp16 score QM[q, :] (QM [B, NC] fp16, the routing product q . m_c / |m_c|), ordered by (score desc, cell asc).
+ * NC <= 65535, nprobe <= 4096.
+ */
+int fvs_route_topk(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int64_t* probe);
+
+/*
+ * Pair list by cell (`throughput/enginei8.py:11-16`, `pairs_fast`) over the first ncols columns of probe [B, nprobe]:
+ * ccnt[c] = #pairs in cell c, coff = exclusive prefix of ccnt, qid[coff[c] .. coff[c]+ccnt[c]) = the queries probing c,
+ * qcp[i] = float(QM[qid, c]) * mnorm[c] (mnorm nullable: 1), slot[q*ncols + j] = position of pair (q, j) (nullable).
+ * work: NC int32 of scratch.  The order of queries within a cell is unspecified.
+ */
+int fvs_pairs(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int ncols, int NC, const uint16_t* QM,
+              const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt, float* qcp, int32_t* slot,
+              int32_t* work);
+
 /* Rows per tile of the int8 scan (a multiple of the reference's 32-row block).  Host-side helper. */
 int fvs_i8_tile_rows(void);
 
@@ -55,6 +78,20 @@ int fvs_i8_scan(fvs_stream_t stream, int mode,
                 const int8_t* Z, const float* zs,
                 const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M,
                 float* bmc, int MB);
+
+/*
+ * fvs_i8_scan on the 5th-generation tensor cores (tcgen05.mma.kind::i8, TMEM accumulators, TMA-staged code tiles).
+ * Same inputs, outputs and semantics as fvs_i8_scan, plus N (rows of Z, for the tensor map; Z and q8 16-byte aligned)
+ * and status (nullable): set to 1 if a bounded internal wait expired (the outputs of that launch are then incomplete).
+ */
+int fvs_i8_scan_tc(fvs_stream_t stream, int mode,
+                   const int8_t* q8, const float* qs, int B, int R,
+                   const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
+                   const int32_t* tile_cell, const int32_t* tile_row0, int ntiles,
+                   const int64_t* off, int NC,
+                   const int8_t* Z, int64_t N, const float* zs,
+                   const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M,
+                   float* bmc, int MB, int32_t* status);
 
 /*
  * First-pass threshold (`throughput/enginei8.py:53-55`): t0[q] = the r-th largest block maximum over the blocks of the
@@ -96,6 +133,17 @@ int fvs_lut_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const f
                   const int32_t* tier_bits, const float* tier_delta, const uint8_t* const* tier_planes,
                   const uint16_t* scale, const uint16_t* sig, int64_t N, const float* qsum, const float* qn2,
                   const int32_t* ncnt, float* est, float* sd);
+
+/*
+ * fvs_lut_score with the table built in shared memory: takes the rotated tier query Zq [B, ldz] f32 (the input of
+ * fvs_lut_build) instead of L/qsum/qn2, and computes the same est / sd (same fp16 / f32 table rounding).  Tiers must be
+ * contiguous from coordinate 0 with widths multiples of 32 (the reference's 32-dim allocation groups,
+ * `src/tiered.py:19-27`).  Replaces `luts_fused` + `score_lut` (`throughput/s2lut.py:92-126`) in one launch.
+ */
+int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq, int ldz,
+                     int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e, const int32_t* tier_bits,
+                     const float* tier_delta, const uint8_t* const* tier_planes, const uint16_t* scale,
+                     const uint16_t* sig, int64_t N, const int32_t* ncnt, float* est, float* sd);
 
 /*
  * Classification, exact re-rank and final top-k (`throughput/enginei8.py:92-95`, `src/engine3.py:143-146`,
