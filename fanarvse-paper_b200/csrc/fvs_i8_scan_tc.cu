@@ -6,18 +6,18 @@
 //
 // Persistent kernel: one CTA per SM walks the tiles b, b + G, b + 2G, ... of the static work list (skipping cells no
 // query probes).  A tile is split into sub-tiles of up to 64 of the cell's queries; sub-tiles are numbered in walk
-// order (nb).  Warp roles (512 threads):
+// order (nb).  Warp roles (768 threads):
 //   warp 0      : TMA loads of the 128 x 256 B code tiles (two 128 B-wide boxes, 128 B swizzle), A_STAGES ahead
 //   warp 1      : TMEM allocation; lane 0 issues tcgen05.mma.kind::i8 (M=128 rows, N=16..64 queries, K=32 x 8) per
 //                 sub-tile into one of T_STAGES accumulators, and releases a code tile when its last MMA completes
 //   warps 2-7   : gather: warp 2+g fills the sub-tiles nb = g (mod 6) -- the rows of q8 picked by qid, in the
 //                 canonical K-major 128 B-swizzled layout, plus scale / pair constant / threshold -- so six
 //                 sub-tiles' dependent loads are in flight at once
-//   warps 8-15  : two epilogue warpgroups, group e on the sub-tiles nb = e (mod 2): tcgen05.ld of the warp's 32 TMEM
-//                 lanes (= code rows), est = ((acc * qs) * zs) + qcp in fp32 with explicit rounding, then first pass:
-//                 per-query block maximum by one redux.sync.max, or emit: per-query ballot over the 32 rows, lane j
-//                 reserving space for column j with one atomicAdd (a chunk's 32 atomics in flight together, the
-//                 second chunk's ballots computed while the first chunk's atomics return), prefix positions by popc.
+//   warps 8-23  : four epilogue warpgroups, group e on the sub-tiles nb = e (mod 4): tcgen05.ld of the warp's 32 TMEM
+//                 lanes (= code rows) 32 columns (queries) at a time, est = ((acc * qs) * zs) + qcp in fp32 with
+//                 explicit rounding, then first pass: per-query block maximum by one redux.sync.max, or emit:
+//                 per-query ballot over the 32 rows, lane j reserving space for column j with one atomicAdd (a chunk's
+//                 32 atomics in flight together), prefix positions by popc.
 // So the loads and MMAs of the next sub-tiles and tiles overlap the epilogues of the current ones.
 // Every mbarrier wait is bounded; on expiry the CTA raises `status`, drains what it issued, frees TMEM and returns.
 #include <cuda.h>
@@ -33,8 +33,8 @@ constexpr int RB = 256;
 constexpr int A_STAGES = 3;
 constexpr int GATHER_WARPS = 6;
 constexpr int B_STAGES = GATHER_WARPS;  // gather warp g owns B stage g
-constexpr int T_STAGES = 4;
-constexpr int EPI_GROUPS = 2;
+constexpr int T_STAGES = 8;
+constexpr int EPI_GROUPS = 4;
 constexpr int NTHREADS = 32 * (2 + GATHER_WARPS + 4 * EPI_GROUPS);
 constexpr uint32_t TMEM_COLS = T_STAGES * QN;  // int32 accumulator columns
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
@@ -45,10 +45,14 @@ constexpr int B_BYTES = 2 * QN * 128;                      // one query sub-tile
 constexpr int A_OFF = 0;
 constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
 constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;       // B_STAGES x 4 x QN x 4 B
-constexpr int BAR_OFF = META_OFF + B_STAGES * 4 * QN * 4;  // mbarriers
+constexpr int ZS_OFF = META_OFF + B_STAGES * 4 * QN * 4;   // B_STAGES x TILE_ROWS x 4 B (row scales of the sub-tile)
+constexpr int MAXT = 512;                                  // tiles of one round of a CTA's walk
+constexpr int LIST_OFF = ZS_OFF + B_STAGES * TILE_ROWS * 4; // 5 x MAXT int32: row0, cs, ce, qoff, qn
+constexpr int COL_OFF = LIST_OFF + 5 * MAXT * 4;           // per epilogue warp: 32 column masks + 32 bases
+constexpr int BAR_OFF = COL_OFF + 16 * 64 * 4;             // mbarriers
 constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 2 * T_STAGES;
-constexpr int MISC_OFF = BAR_OFF + NBAR * 8;               // tmem base, abort flag
-constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;           // + alignment slack
+constexpr int MISC_OFF = BAR_OFF + NBAR * 8;               // tmem base, abort flag, list length, scan scratch
+constexpr int SMEM_BYTES = MISC_OFF + 16 + 64 + 1024;      // + alignment slack
 
 struct Params {
     const int8_t* q8;
@@ -190,228 +194,293 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const int G = gridDim.x;
+    int* L_row0 = reinterpret_cast<int*>(smem + LIST_OFF);
+    int* L_cs = L_row0 + MAXT;
+    int* L_ce = L_cs + MAXT;
+    int* L_qoff = L_ce + MAXT;
+    int* L_qn = L_qoff + MAXT;
+    volatile int* L_len = reinterpret_cast<volatile int*>(smem + MISC_OFF + 8);
+    int* wsum = reinterpret_cast<int*>(smem + MISC_OFF + 16);  // 16 warps
+    float* zsm = reinterpret_cast<float*>(smem + ZS_OFF);
+    const int nlocal = ntiles > blockIdx.x ? (ntiles - blockIdx.x + G - 1) / G : 0;
 
-    if (warp == 0) {
-        // ---- code tiles by TMA
-        if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&zmap) : "memory");
-            int na = 0;
-            for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
-                if (p.ccnt[p.tile_cell[tile]] == 0) continue;
-                const int s = na % A_STAGES;
-                if (!mbar_wait(a_empty(s), ((na / A_STAGES) & 1) ^ 1, abort)) break;
-                const int row0 = p.tile_row0[tile];
-                mbar_expect_tx(a_full(s), A_BYTES);
-                tma_load_2d(sbase + A_OFF + s * A_BYTES, &zmap, 0, row0, a_full(s));
-                tma_load_2d(sbase + A_OFF + s * A_BYTES + TILE_ROWS * 128, &zmap, 128, row0, a_full(s));
-                na++;
+    // per-role pipeline counters persist across rounds
+    int na_tma = 0, na_mma = 0, nb_mma = 0, last_a = -1, nb_g = 0, nb_e = 0;
+    for (int r0 = 0; r0 < nlocal; r0 += MAXT) {
+        // ---- stage this round's tiles (skipping cells no query probes) in shared memory, in walk order
+        {
+            const int cnt_r = min(MAXT, nlocal - r0);
+            // NTHREADS >= MAXT is not required: loop in chunks of NTHREADS
+            int base = 0;
+            for (int c0 = 0; c0 < cnt_r; c0 += NTHREADS) {
+                const int li = c0 + tid;
+                int qn = 0, row0 = 0, cs = 0, ce = 0, qoff = 0;
+                if (li < cnt_r) {
+                    const int tile = blockIdx.x + (r0 + li) * G;
+                    const int c = p.tile_cell[tile];
+                    row0 = p.tile_row0[tile];
+                    qn = p.ccnt[c];
+                    cs = (int)p.off[c];
+                    ce = (int)p.off[c + 1];
+                    qoff = p.coff[c];
+                }
+                const bool act = qn > 0;
+                const unsigned bal = __ballot_sync(0xffffffffu, act);
+                if (lane == 0) wsum[warp] = __popc(bal);
+                __syncthreads();
+                int before = base;
+                for (int w = 0; w < warp; w++) before += wsum[w];
+                int tot = 0;
+                for (int w = 0; w < NTHREADS / 32; w++) tot += wsum[w];
+                if (act) {
+                    const int at = before + __popc(bal & ((1u << lane) - 1u));
+                    L_row0[at] = row0;
+                    L_cs[at] = cs;
+                    L_ce[at] = ce;
+                    L_qoff[at] = qoff;
+                    L_qn[at] = qn;
+                }
+                base += tot;
+                __syncthreads();
             }
-            // drain: the most recent load of every stage has landed before the CTA may exit
-            for (int u = na - 1; u >= 0 && u >= na - A_STAGES; u--) mbar_wait(a_full(u % A_STAGES), (u / A_STAGES) & 1, abort);
+            if (tid == 0) *L_len = base;
+            __syncthreads();
         }
-    } else if (warp == 1) {
-        // ---- MMA issue
-        if (lane == 0) {
-            int na = 0, nb = 0, last_a = -1;
-            for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
-                const int qn = p.ccnt[p.tile_cell[tile]];
-                if (qn == 0) continue;
-                const int sa = na % A_STAGES;
-                if (!mbar_wait(a_full(sa), (na / A_STAGES) & 1, abort)) break;
-                tc_fence_after();
-                const uint32_t abase = sbase + A_OFF + sa * A_BYTES;
+        const int len = *L_len;
+
+        if (warp == 0) {
+            // ---- code tiles by TMA
+            if (lane == 0) {
+                if (r0 == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&zmap) : "memory");
+                for (int t = 0; t < len && !*abort; t++) {
+                    const int s = na_tma % A_STAGES;
+                    if (!mbar_wait(a_empty(s), ((na_tma / A_STAGES) & 1) ^ 1, abort)) break;
+                    const int row0 = L_row0[t];
+                    mbar_expect_tx(a_full(s), A_BYTES);
+                    tma_load_2d(sbase + A_OFF + s * A_BYTES, &zmap, 0, row0, a_full(s));
+                    tma_load_2d(sbase + A_OFF + s * A_BYTES + TILE_ROWS * 128, &zmap, 128, row0, a_full(s));
+                    na_tma++;
+                }
+            }
+        } else if (warp == 1) {
+            // ---- MMA issue
+            if (lane == 0) {
+                for (int t = 0; t < len && !*abort; t++) {
+                    const int qn = L_qn[t];
+                    const int sa = na_mma % A_STAGES;
+                    if (!mbar_wait(a_full(sa), (na_mma / A_STAGES) & 1, abort)) break;
+                    tc_fence_after();
+                    const uint32_t abase = sbase + A_OFF + sa * A_BYTES;
+                    bool ok = true;
+                    for (int i = 0; i * QN < qn; i++, nb_mma++) {
+                        const int sb = nb_mma % B_STAGES, st = nb_mma % T_STAGES;
+                        if (!mbar_wait(b_full(sb), (nb_mma / B_STAGES) & 1, abort) ||
+                            !mbar_wait(t_empty(st), ((nb_mma / T_STAGES) & 1) ^ 1, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const int nq = min(QN, qn - i * QN);
+                        const uint32_t idesc = i8_idesc((nq + 15) & ~15);
+                        const uint32_t d = tmem + (uint32_t)(st * QN);
+                        const uint32_t bb = sbase + B_OFF + sb * B_BYTES;
+#pragma unroll
+                        for (int ks = 0; ks < RB / 32; ks++) {
+                            const int h = ks >> 2, kofs = (ks & 3) * 32;
+                            mma_i8(d, sw128_desc(abase + h * TILE_ROWS * 128 + kofs),
+                                   sw128_desc(bb + h * QN * 128 + kofs), idesc, ks > 0 ? 1u : 0u);
+                        }
+                        mma_commit(t_full(st));
+                    }
+                    if (!ok) break;
+                    mma_commit(a_empty(sa));  // the code tile is free once these MMAs complete
+                    last_a = na_mma;
+                    na_mma++;
+                }
+            }
+            __syncwarp();
+        } else if (warp < 2 + GATHER_WARPS) {
+            // ---- query gather: warp gw fills the sub-tiles nb = gw (mod GATHER_WARPS); lane l fills rows l, l + 32
+            const int gw = warp - 2;
+            for (int t = 0; t < len && !*abort; t++) {
+                const int qn = L_qn[t], qoff = L_qoff[t], row0 = L_row0[t], cs = L_cs[t], ce = L_ce[t];
                 bool ok = true;
-                for (int i = 0; i * QN < qn; i++, nb++) {
-                    const int sb = nb % B_STAGES, st = nb % T_STAGES;
-                    if (!mbar_wait(b_full(sb), (nb / B_STAGES) & 1, abort) ||
-                        !mbar_wait(t_empty(st), ((nb / T_STAGES) & 1) ^ 1, abort)) {
+                for (int i = 0; i * QN < qn; i++, nb_g++) {
+                    if (nb_g % GATHER_WARPS != gw) continue;
+                    const int s = nb_g % B_STAGES;
+                    if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort)) {
+                        ok = false;
+                        break;
+                    }
+                    const int nq = min(QN, qn - i * QN);
+                    const int n16 = (nq + 15) & ~15;
+                    // row scales of the tile (rows outside the cell read as 0)
+#pragma unroll
+                    for (int rr = 0; rr < TILE_ROWS / 32; rr++) {
+                        const int row = row0 + 32 * rr + lane;
+                        zsm[s * TILE_ROWS + 32 * rr + lane] = (row >= cs && row < ce) ? p.zs[row] : 0.f;
+                    }
+                    int qq[2];
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++) {
+                        const int g = lane + 32 * rr;
+                        qq[rr] = -1;
+                        if (g < nq) {
+                            const int pi = qoff + i * QN + g;
+                            const int q = p.qid[pi];
+                            qq[rr] = q;
+                            meta_qid[s * QN + g] = q;
+                            meta_qs[s * QN + g] = p.qs[q];
+                            meta_qc[s * QN + g] = p.qcp[pi];
+                            meta_th[s * QN + g] = MODE ? p.t0[q] : 0.f;
+                        }
+                    }
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++) {
+                        const int g = lane + 32 * rr;
+                        if (g >= n16) continue;
+                        const int q = qq[rr];
+                        const uint4* src = reinterpret_cast<const uint4*>(p.q8 + (int64_t)(q >= 0 ? q : 0) * RB);
+                        uint8_t* bs = smem + B_OFF + s * B_BYTES + (g >> 3) * 1024 + (g & 7) * 128;
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            uint4 v[8];
+#pragma unroll
+                            for (int cc = 0; cc < 8; cc++)
+                                v[cc] = q >= 0 ? __ldg(src + 8 * h + cc) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                            for (int cc = 0; cc < 8; cc++)
+                                *reinterpret_cast<uint4*>(bs + h * QN * 128 + ((cc ^ (g & 7)) << 4)) = v[cc];
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(b_full(s));
+                }
+                if (!ok) break;
+            }
+        } else {
+            // ---- epilogue: group eg = sub-tiles nb = eg (mod EPI_GROUPS); warp ew = warp % 4 reads TMEM lanes
+            //      32*ew .. 32*ew+31 (tile rows)
+            const int eg = (warp - 2 - GATHER_WARPS) / 4;
+            const int ew = warp & 3;
+            for (int t = 0; t < len && !*abort; t++) {
+                const int qn = L_qn[t], qoff = L_qoff[t], row0 = L_row0[t], cs = L_cs[t], ce = L_ce[t];
+                const int row = row0 + 32 * ew + lane;
+                const bool rvalid = row >= cs && row < ce;
+                const bool wactive = row0 + 32 * ew < ce;
+                const int blk_rel = (row0 + 32 * ew) / 32 - cs / 32;
+                bool ok = true;
+                for (int i = 0; i * QN < qn; i++, nb_e++) {
+                    if (nb_e % EPI_GROUPS != eg) continue;
+                    const int sb = nb_e % B_STAGES, st = nb_e % T_STAGES;
+                    if (!mbar_wait(t_full(st), (nb_e / T_STAGES) & 1, abort) ||
+                        !mbar_wait(b_full(sb), (nb_e / B_STAGES) & 1, abort)) {  // b_full: acquire the metadata
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const int nq = min(QN, qn - i * QN);
-                    const uint32_t idesc = i8_idesc((nq + 15) & ~15);
-                    const uint32_t d = tmem + (uint32_t)(st * QN);
-                    const uint32_t bb = sbase + B_OFF + sb * B_BYTES;
+                    const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
+                    const int* mq = meta_qid + sb * QN;
+                    const float* ms = meta_qs + sb * QN;
+                    const float* mc = meta_qc + sb * QN;
+                    const float* mt = meta_th + sb * QN;
+                    const float zr = zsm[sb * TILE_ROWS + 32 * ew + lane];
+                    uint32_t* colm = reinterpret_cast<uint32_t*>(smem + COL_OFF) + (warp - 2 - GATHER_WARPS) * 64;
+                    int* colb = reinterpret_cast<int*>(colm + 32);
+                    for (int h = 0; h * 32 < nq; h++) {
+                        uint32_t acc[32];
+                        tmem_ld32(ta + 32 * h, acc);
+                        tmem_ld_wait();
+                        if (!wactive) continue;
+                        const int nc = min(32, nq - h * 32);
+                        const float4* ms4 = reinterpret_cast<const float4*>(ms + 32 * h);
+                        const float4* mc4 = reinterpret_cast<const float4*>(mc + 32 * h);
+                        if (MODE == 0) {
 #pragma unroll
-                    for (int ks = 0; ks < RB / 32; ks++) {
-                        const int h = ks >> 2, kofs = (ks & 3) * 32;
-                        mma_i8(d, sw128_desc(abase + h * TILE_ROWS * 128 + kofs), sw128_desc(bb + h * QN * 128 + kofs),
-                               idesc, ks > 0 ? 1u : 0u);
-                    }
-                    mma_commit(t_full(st));
-                }
-                if (!ok) break;
-                mma_commit(a_empty(sa));  // the code tile is free once these MMAs complete
-                last_a = na;
-                na++;
-            }
-            if (last_a >= 0) mbar_wait(a_empty(last_a % A_STAGES), (last_a / A_STAGES) & 1, abort);
-        }
-        __syncwarp();
-    } else if (warp < 2 + GATHER_WARPS) {
-        // ---- query gather: warp gw fills the sub-tiles nb = gw (mod GATHER_WARPS); lane l fills rows l and l + 32
-        const int gw = warp - 2;
-        int nb = 0;
-        for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
-            const int c = p.tile_cell[tile];
-            const int qn = p.ccnt[c];
-            if (qn == 0) continue;
-            const int qoff = p.coff[c];
-            bool ok = true;
-            for (int i = 0; i * QN < qn; i++, nb++) {
-                if (nb % GATHER_WARPS != gw) continue;
-                const int s = nb % B_STAGES;
-                if (!mbar_wait(b_empty(s), ((nb / B_STAGES) & 1) ^ 1, abort)) {
-                    ok = false;
-                    break;
-                }
-                const int nq = min(QN, qn - i * QN);
-                const int n16 = (nq + 15) & ~15;
-                int qq[2];
+                            for (int j4 = 0; j4 < 8; j4++) {
+                                if (4 * j4 >= nc) break;
+                                const float4 sv = ms4[j4], cv = mc4[j4];
+                                const float s4[4] = {sv.x, sv.y, sv.z, sv.w}, c4[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int g = lane + 32 * rr;
-                    qq[rr] = -1;
-                    if (g < nq) {
-                        const int pi = qoff + i * QN + g;
-                        const int q = p.qid[pi];
-                        qq[rr] = q;
-                        meta_qid[s * QN + g] = q;
-                        meta_qs[s * QN + g] = p.qs[q];
-                        meta_qc[s * QN + g] = p.qcp[pi];
-                        meta_th[s * QN + g] = MODE ? p.t0[q] : 0.f;
-                    }
-                }
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int g = lane + 32 * rr;
-                    if (g >= n16) continue;
-                    const int q = qq[rr];
-                    const uint4* src = reinterpret_cast<const uint4*>(p.q8 + (int64_t)(q >= 0 ? q : 0) * RB);
-                    uint8_t* bs = smem + B_OFF + s * B_BYTES + (g >> 3) * 1024 + (g & 7) * 128;
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        uint4 v[8];
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            v[cc] = q >= 0 ? __ldg(src + 8 * h + cc) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            *reinterpret_cast<uint4*>(bs + h * QN * 128 + ((cc ^ (g & 7)) << 4)) = v[cc];
-                    }
-                }
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(b_full(s));
-            }
-            if (!ok) break;
-        }
-    } else {
-        // ---- epilogue: group eg = sub-tiles nb = eg (mod EPI_GROUPS); warp ew = warp % 4 reads TMEM lanes
-        //      32*ew .. 32*ew+31 (tile rows)
-        const int eg = (warp - 2 - GATHER_WARPS) / 4;
-        const int ew = warp & 3;
-        int nb = 0;
-        for (int tile = blockIdx.x; tile < ntiles && !*abort; tile += G) {
-            const int c = p.tile_cell[tile];
-            const int qn = p.ccnt[c];
-            if (qn == 0) continue;
-            const int64_t cs = p.off[c], ce = p.off[c + 1];
-            const int row0 = p.tile_row0[tile];
-            const int qoff = p.coff[c];
-            const int row = row0 + 32 * ew + lane;
-            const bool rvalid = row >= cs && row < ce;
-            const bool wactive = (int64_t)(row0 + 32 * ew) < ce;
-            const float zr = rvalid ? p.zs[row] : 0.f;
-            const int blk_rel = (int)((row0 + 32 * ew) / 32 - cs / 32);
-            bool ok = true;
-            for (int i = 0; i * QN < qn; i++, nb++) {
-                if (nb % EPI_GROUPS != eg) continue;
-                const int sb = nb % B_STAGES, st = nb % T_STAGES;
-                if (!mbar_wait(t_full(st), (nb / T_STAGES) & 1, abort) ||
-                    !mbar_wait(b_full(sb), (nb / B_STAGES) & 1, abort)) {  // b_full: acquire the metadata
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const int nq = min(QN, qn - i * QN);
-                const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
-                const int* mq = meta_qid + sb * QN;
-                const float* ms = meta_qs + sb * QN;
-                const float* mc = meta_qc + sb * QN;
-                const float* mt = meta_th + sb * QN;
-                uint32_t acc[2][32];
-                tmem_ld32(ta, acc[0]);
-                if (nq > 32) tmem_ld32(ta + 32, acc[1]);
-                tmem_ld_wait();
-                if (wactive) {
-                    if (MODE == 0) {
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-#pragma unroll
-                            for (int jj = 0; jj < 32; jj++) {
-                                const int j = h * 32 + jj;
-                                if (j < nq) {
-                                    const float est = __fadd_rn(
-                                        __fmul_rn(__fmul_rn((float)(int32_t)acc[h][jj], ms[j]), zr), mc[j]);
-                                    const uint32_t m = __reduce_max_sync(0xffffffffu, rvalid ? f2o(est) : 0u);
-                                    if (lane == 0) p.bmc[(int64_t)(qoff + i * QN + j) * p.MB + blk_rel] = o2f(m);
-                                }
-                            }
-                        }
-                    } else {
-                        // per chunk: ballots of the 32 columns (lane jj keeps column jj's), then lane jj reserves
-                        // space for column jj; chunk 1's ballots run while chunk 0's atomics are in flight
-                        uint32_t mymask[2] = {0u, 0u};
-                        int mybase[2] = {0, 0};
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-#pragma unroll
-                            for (int jj = 0; jj < 32; jj++) {
-                                const int j = h * 32 + jj;
-                                if (j < nq) {
-                                    const float est = __fadd_rn(
-                                        __fmul_rn(__fmul_rn((float)(int32_t)acc[h][jj], ms[j]), zr), mc[j]);
-                                    const uint32_t mask = __ballot_sync(0xffffffffu, rvalid && est >= mt[j]);
-                                    if (lane == jj) mymask[h] = mask;
-                                }
-                            }
-                            if (mymask[h]) mybase[h] = atomicAdd(p.cnt + mq[h * 32 + lane], __popc(mymask[h]));
-                        }
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const unsigned any = __ballot_sync(0xffffffffu, mymask[h] != 0);
-#pragma unroll
-                            for (int jj = 0; jj < 32; jj++) {
-                                if (!(any & (1u << jj))) continue;  // warp-uniform
-                                const uint32_t mask = __shfl_sync(0xffffffffu, mymask[h], jj);
-                                const int base = __shfl_sync(0xffffffffu, mybase[h], jj);
-                                if (mask & (1u << lane)) {
-                                    const int j = h * 32 + jj;
-                                    const float est = __fadd_rn(
-                                        __fmul_rn(__fmul_rn((float)(int32_t)acc[h][jj], ms[j]), zr), mc[j]);
-                                    const int idx = base + __popc(mask & ((1u << lane) - 1u));
-                                    if (idx < p.M) {
-                                        const int64_t o = (int64_t)mq[j] * p.M + idx;
-                                        p.bval[o] = est;
-                                        p.bpos[o] = row;
+                                for (int u = 0; u < 4; u++) {
+                                    const int jj = 4 * j4 + u;
+                                    if (jj < nc) {
+                                        const float est =
+                                            __fadd_rn(__fmul_rn(__fmul_rn((float)(int32_t)acc[jj], s4[u]), zr), c4[u]);
+                                        const uint32_t m = __reduce_max_sync(0xffffffffu, rvalid ? f2o(est) : 0u);
+                                        if (lane == 0)
+                                            p.bmc[(int64_t)(qoff + i * QN + 32 * h + jj) * p.MB + blk_rel] = o2f(m);
                                     }
                                 }
                             }
+                        } else {
+                            // ballots of the chunk's columns (lane jj keeps column jj's, every row its own kept
+                            // columns), then lane jj reserves space for column jj: the chunk's atomics are in flight
+                            // together; finally every row writes only its own kept entries
+                            const float4* mt4 = reinterpret_cast<const float4*>(mt + 32 * h);
+                            uint32_t mymask = 0, rowmask = 0;
+#pragma unroll
+                            for (int j4 = 0; j4 < 8; j4++) {
+                                if (4 * j4 >= nc) break;
+                                const float4 sv = ms4[j4], cv = mc4[j4], tv = mt4[j4];
+                                const float s4[4] = {sv.x, sv.y, sv.z, sv.w}, c4[4] = {cv.x, cv.y, cv.z, cv.w};
+                                const float t4[4] = {tv.x, tv.y, tv.z, tv.w};
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    const int jj = 4 * j4 + u;
+                                    if (jj < nc) {
+                                        const float est =
+                                            __fadd_rn(__fmul_rn(__fmul_rn((float)(int32_t)acc[jj], s4[u]), zr), c4[u]);
+                                        const bool keep = rvalid && est >= t4[u];
+                                        rowmask |= (uint32_t)keep << jj;
+                                        const uint32_t mask = __ballot_sync(0xffffffffu, keep);
+                                        if (lane == jj) mymask = mask;
+                                    }
+                                }
+                            }
+                            int mybase = 0;
+                            if (mymask) mybase = atomicAdd(p.cnt + mq[32 * h + lane], __popc(mymask));
+                            colm[lane] = mymask;
+                            colb[lane] = mybase;
+                            __syncwarp();
+                            while (rowmask) {
+                                const int jj = __ffs(rowmask) - 1;
+                                rowmask &= rowmask - 1;
+                                const int j = 32 * h + jj;
+                                float accj = 0.f;
+#pragma unroll
+                                for (int u = 0; u < 32; u++)
+                                    if (u == jj) accj = (float)(int32_t)acc[u];
+                                const float est = __fadd_rn(__fmul_rn(__fmul_rn(accj, ms[j]), zr), mc[j]);
+                                const int idx = colb[jj] + __popc(colm[jj] & ((1u << lane) - 1u));
+                                if (idx < p.M) {
+                                    const int64_t o = (int64_t)mq[j] * p.M + idx;
+                                    p.bval[o] = est;
+                                    p.bpos[o] = row;
+                                }
+                            }
+                            __syncwarp();
                         }
                     }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(t_empty(st));
+                        mbar_arrive(b_empty(sb));
+                    }
                 }
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(t_empty(st));
-                    mbar_arrive(b_empty(sb));
-                }
+                if (!ok) break;
             }
-            if (!ok) break;
         }
+        __syncthreads();  // the round's list is consumed by every role before it is overwritten
     }
+    // drain: the most recent load of every A stage has landed, the last code-tile release has arrived
+    if (warp == 0 && lane == 0)
+        for (int u = na_tma - 1; u >= 0 && u >= na_tma - A_STAGES; u--)
+            mbar_wait(a_full(u % A_STAGES), (u / A_STAGES) & 1, abort);
+    if (warp == 1 && lane == 0 && last_a >= 0) mbar_wait(a_empty(last_a % A_STAGES), (last_a / A_STAGES) & 1, abort);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
