@@ -159,3 +159,53 @@ extern "C" int fvs_pairs(fvs_stream_t stream, const int64_t* probe, int B, int n
                                                            work, qid, qcp, slot);
     return fvs_launch_status();
 }
+
+// ------------------------------------------------------------------------------------------------ allocation-free
+// fvs_pairs_noalloc: fvs_pairs for callers that cannot allocate device memory (the per-cell cursors live in this
+// file-scope array instead of a caller-provided `work` buffer).  The array is allocated once per GPU when the library
+// is loaded there and stays allocated until the process exits.
+static __device__ __align__(256) int32_t g_pairs_cursor[FVS_PAIRS_NOALLOC_MAX_CELLS];
+
+// Device address of g_pairs_cursor on the current device, looked up once per device.  The host-side symbol is only a
+// handle: a kernel must be given the address cudaGetSymbolAddress returns for the device it runs on.
+static cudaError_t pairs_cursor_address(int32_t** out) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    constexpr int MAXDEV = 256;
+    static std::mutex mu;
+    static int32_t* addr[MAXDEV] = {};
+    if (dev < 0 || dev >= MAXDEV) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_pairs_cursor);
+        if (e != cudaSuccess) return e;
+        addr[dev] = reinterpret_cast<int32_t*>(ptr);
+    }
+    *out = addr[dev];
+    return cudaSuccess;
+}
+
+extern "C" int fvs_pairs_noalloc(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int ncols, int NC,
+                                 const uint16_t* QM, const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt,
+                                 float* qcp, int32_t* slot) {
+    FVS_CHECK_ARG(probe && QM && qid && coff && ccnt && qcp && B >= 0 && NC > 0);
+    FVS_CHECK_ARG(ncols >= 1 && ncols <= nprobe);
+    if (NC > FVS_PAIRS_NOALLOC_MAX_CELLS) return FVS_ERANGE;
+    int32_t* cursor = nullptr;
+    cudaError_t e = pairs_cursor_address(&cursor);
+    if (e != cudaSuccess) return (int)e;
+    // the array keeps the previous call's cursors: clear the part this call uses
+    e = cudaMemsetAsync(ccnt, 0, (size_t)NC * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(cursor, 0, (size_t)NC * 4, stream);
+    if (e != cudaSuccess) return (int)e;
+    const int64_t n = (int64_t)B * ncols;
+    const unsigned grid = (unsigned)((n + 255) / 256);
+    if (n > 0) fvs::pair_hist_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, ncols, ccnt);
+    fvs::pair_scan_kernel<<<1, 1024, 0, stream>>>(ccnt, NC, coff);
+    if (n > 0)
+        fvs::pair_scatter_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, ncols, NC, (const __half*)QM, mnorm, coff,
+                                                           cursor, qid, qcp, slot);
+    return fvs_launch_status();
+}

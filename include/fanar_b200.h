@@ -52,6 +52,22 @@ int fvs_pairs(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int 
               const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt, float* qcp, int32_t* slot,
               int32_t* work);
 
+/*
+ * fvs_pairs without the `work` argument, for callers that cannot allocate device memory: host programs that drive
+ * the search through a foreign-function binding and own no CUDA allocator, or that must not call cudaMalloc while
+ * their stream is being captured into a CUDA graph.  No counterpart in the reference (its pairing is torch code that
+ * allocates freely).  The per-cell scratch is a file-scope device array of FVS_PAIRS_NOALLOC_MAX_CELLS int32 inside
+ * this library, held on every GPU that loads the library until the process exits; NC above that returns FVS_ERANGE.
+ * This call allocates nothing: it clears the part of the array it uses, then runs the same kernels as fvs_pairs.
+ * The first call on a device looks up the array's device address (once per device): make it before capturing a
+ * stream.  All calls share the one array, so calls whose kernels overlap on the GPU (concurrent streams, other host
+ * threads) race on it and must be serialised by the caller.
+ */
+#define FVS_PAIRS_NOALLOC_MAX_CELLS 65536
+int fvs_pairs_noalloc(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int ncols, int NC,
+                      const uint16_t* QM, const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt, float* qcp,
+                      int32_t* slot);
+
 /* Rows per tile of the int8 scan (a multiple of the reference's 32-row block).  Host-side helper. */
 int fvs_i8_tile_rows(void);
 
