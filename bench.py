@@ -196,11 +196,12 @@ def load_peaks():
 
 
 def load_traffic(kernel):
+    """DRAM bytes per launch of the kernel from the committed ncu summary (profiles/traffic.json), or None."""
     p = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(p):
         d = json.load(open(p)).get(kernel)
         if d:
-            return d
+            return d["bytes_per_launch"]
     return None
 
 

@@ -1,0 +1,131 @@
+"""Row-sharded search, host side, on CPU ranks (gloo, world size 2).
+
+The per-shard engine and the two device steps (exact scores of the local winners, cross-shard merge) are replaced by
+the oracle's restatements so that the plumbing -- row offsets, the all-gather of [B, k] (global id, score) pairs, the
+merge by (score desc, id asc) -- runs without a GPU.  A second test kills one rank before the exchange: the other rank
+must fail with an error from the process group instead of waiting forever."""
+import datetime
+import os
+import socket
+import sys
+import tempfile
+import traceback
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _shard(rank, n=2500, d=256, nq=24):
+    sys.path.insert(0, REPO)
+    import importlib
+    synth = importlib.import_module("fanarvse-paper_b200.synth")
+    ib = importlib.import_module("fanarvse-paper_b200.index_build")
+    import __graft_entry__ as ge
+    ds = synth.make_dataset(synth.MixtureSpec(n=n, d=d, comps=8, nq=nq, seed=4), "cpu", gt_k=10, shard=rank)
+    s1, i8, codes = ib.build_index(ds["base16"], 24, R=256, refine_bits=640, seed=4, kmeans_sample=n)
+    return ds, ge.oracle_index(s1, i8, codes["uniform"], ds["base16"])
+
+
+class _OracleLocal:
+    """stands in for the shard's EngineB200I8 (same search signature and outputs)."""
+
+    def __init__(self, oi):
+        from oracle import fvs_oracle as O
+        self.O, self.oi = O, oi
+
+    def search(self, Qb, K, z, nprobe, k):
+        out = self.O.search_i8(self.oi, Qb.numpy(), K, z, nprobe, k, self.O.I8Knobs, fallback=True)
+        return torch.from_numpy(out["I"].astype(np.int32)), torch.from_numpy(out["reads"]), torch.from_numpy(out["ids"])
+
+
+def _worker(rank, world, port, outdir, fail_rank):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    sys.path.insert(0, REPO)
+    import importlib
+    sharded = importlib.import_module("fanarvse-paper_b200.sharded")
+    from oracle import fvs_oracle as O
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    ds, oi = _shard(rank)
+    n = len(oi["order"])
+    H = oi["H16"].astype(np.float32)
+
+    def exact(Qb, I):
+        return torch.from_numpy((H[I.numpy()] * Qb.numpy()[:, None, :]).sum(2).astype(np.float32))
+
+    def merge(ids_g, s_g, k):
+        a, b = O.merge_topk(ids_g.numpy(), s_g.numpy(), k)
+        return torch.from_numpy(a), torch.from_numpy(b)
+
+    S = sharded.ShardedSearch(_OracleLocal(oi), rank * n, exact=exact, merge=merge)
+    Q = ds["queries"]
+    if rank == fail_rank:
+        os._exit(3)                       # dies before its first exchange
+    try:
+        I, Sc, reads = S.search(Q, 40, 1.25, 10, 10)
+        Il, _, _ = S.local.search(Q, 40, 1.25, 10, 10)
+        np.savez(os.path.join(outdir, f"r{rank}.npz"), I=I.numpy(), S=Sc.numpy(), local=Il.numpy() + rank * n,
+                 local_s=exact(Q, Il).numpy())
+        status = "ok"
+    except Exception as e:  # a peer vanished: the collective must raise, not hang
+        status = "raised: " + type(e).__name__ + ": " + str(e).splitlines()[0][:200]
+    open(os.path.join(outdir, f"r{rank}.status"), "w").write(status)
+    try:
+        dist.destroy_process_group()
+    except Exception:
+        pass
+
+
+def _run(world, fail_rank, timeout=240):
+    outdir = tempfile.mkdtemp()
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    ps = [ctx.Process(target=_worker, args=(r, world, port, outdir, fail_rank)) for r in range(world)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(timeout)
+    alive = [p for p in ps if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank did not finish"
+    return outdir, [p.exitcode for p in ps]
+
+
+def test_sharded_merge_two_ranks():
+    outdir, codes = _run(2, fail_rank=-1)
+    assert codes == [0, 0]
+    from oracle import fvs_oracle as O
+    r = [np.load(os.path.join(outdir, f"r{i}.npz")) for i in range(2)]
+    for i in range(2):
+        assert open(os.path.join(outdir, f"r{i}.status")).read() == "ok"
+    # both ranks hold the same global result ...
+    np.testing.assert_array_equal(r[0]["I"], r[1]["I"])
+    # ... which is the exact-score merge of the two shards' local top-k, in global ids
+    ids_g = np.stack([r[0]["local"], r[1]["local"]]).astype(np.int64)
+    s_g = np.stack([r[0]["local_s"], r[1]["local_s"]])
+    want_i, want_s = O.merge_topk(ids_g, s_g, 10)
+    np.testing.assert_array_equal(r[0]["I"], want_i)
+    np.testing.assert_array_equal(r[0]["S"], want_s)
+    # every result row draws from both shards' id ranges only through the merge
+    assert (r[0]["I"] >= 0).all() and (r[0]["I"] < 2 * 2500).all()
+
+
+def test_dead_rank_is_detected():
+    outdir, codes = _run(2, fail_rank=1)
+    assert codes[1] == 3
+    assert codes[0] == 0
+    st = open(os.path.join(outdir, "r0.status")).read()
+    assert st.startswith("raised"), st
