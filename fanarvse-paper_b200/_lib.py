@@ -34,6 +34,12 @@ SIGNATURES = {
     "fvs_lut_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P, P, P]),
     "fvs_lut_score_zq": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P]),
     "fvs_refine": (I32, [P, P, I32, P, P, P, P, I32, I32, F32, I32, P, I32, P, P, P, P]),
+    "fvs_trellis_tile_rows": (I32, []),
+    "fvs_trellis_scan": (I32, [P, I32, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I32, P, I32, P, P, P, P, P,
+                                I32, P, I32]),
+    "fvs_tiered_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P]),
+    "fvs_route_topk_scaled": (I32, [P, P, I32, I32, I32, P, P]),
+    "fvs_viterbi_encode": (I32, [P, P, I32, I32, P, I32, P]),
     "fvs_exact_scores": (I32, [P, P, I32, P, I32, I32, P, I32, P]),
     "fvs_merge_topk": (I32, [P, P, P, I32, I32, I32, I32, P, P]),
 }

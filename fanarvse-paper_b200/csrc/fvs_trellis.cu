@@ -1,0 +1,510 @@
+// Default engine (cell-residual trellis code): stage-1 scan, tiered gather stage 2, fp32-keyed routing, and the
+// build-time Viterbi encoder.
+//
+// fvs_trellis_scan replaces `_first_compact_s` / `_emit_loop_s` (`src/s1cell.py:121-154`) with the decoder of
+// `src/decode2.py:5-17`: value_j = tab[state_j], state_j = ((w[j/32] << 32 | w[j/32+1]) >> (64 - L - j%32)) & (2^L-1)
+// (bits MSB-first per uint32 word, `src/trellis_scan.py:10-18`), rounded to fp16 as the reference's `.to(fp16)`.
+// One CTA owns 128 code rows of one cell (four of the reference's 32-row blocks): each thread decodes one row through
+// the 1024-entry table held in shared memory into an fp16 tile; queries (fp16 Q @ W1) come in tiles of 64; the dot
+// products run on the tensor cores (mma m16n8k16, fp16 in, fp32 accumulate) and the epilogue computes
+// est = scale1[n] * dot + qcp (fp32, unfused) with the same first-pass / threshold-emit logic as the int8 scan.
+#include <cuda.h>
+
+#include "fvs_common.cuh"
+
+namespace fvs {
+namespace trellis {
+
+constexpr int TILE_ROWS = 128;
+constexpr int QT = 64;
+constexpr int R = 256;
+constexpr int RS = R * 2 + 16;  // fp16 row stride in bytes (ldmatrix bank-conflict free)
+constexpr int NTHREADS = 128;
+constexpr int MAXW = 16;         // words per row (R + L - 1 <= 512 bits)
+
+struct Params {
+    const __half* Qh;
+    const int32_t* qid;
+    const int32_t* coff;
+    const int32_t* ccnt;
+    const float* qcp;
+    const int32_t* tile_cell;
+    const int32_t* tile_row0;
+    const int64_t* off;
+    const uint32_t* words;
+    const float* tab;
+    const __half* scale1;
+    const float* t0;
+    int32_t* cnt;
+    float* bval;
+    int32_t* bpos;
+    float* bmc;
+    int W, L, M, MB;
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, const void* p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+                 : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void mma_f16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    uint8_t* vt = smem;                                        // TILE_ROWS x RS (decoded fp16 values)
+    uint8_t* qt = vt + TILE_ROWS * RS;                         // QT x RS (fp16 queries)
+    float* tab = reinterpret_cast<float*>(qt + QT * RS);       // 2^L
+    float* ssc = tab + (1 << p.L);                             // TILE_ROWS row scales
+    float* qcs = ssc + TILE_ROWS;                              // QT
+    float* thr = qcs + QT;                                     // QT
+    int* qids = reinterpret_cast<int*>(thr + QT);              // QT
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int c = p.tile_cell[blockIdx.x];
+    const int qn = p.ccnt[c];
+    if (qn == 0) return;
+    const int64_t cs = p.off[c], ce = p.off[c + 1];
+    const int64_t row0 = p.tile_row0[blockIdx.x];
+    const int qoff = p.coff[c];
+    const int L = p.L, W = p.W;
+
+    for (int i = tid; i < (1 << L); i += NTHREADS) tab[i] = p.tab[i];
+    __syncthreads();
+    // ---- decode one row per thread (rows outside the cell: zeros)
+    {
+        const int64_t n = row0 + tid;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(vt + tid * RS);
+        if (n >= cs && n < ce) {
+            uint32_t w[R / 32 + 1];
+#pragma unroll
+            for (int i = 0; i <= R / 32; i++) w[i] = (i < W) ? p.words[n * W + i] : 0u;
+            const uint32_t mask = (1u << L) - 1u;
+#pragma unroll
+            for (int wi = 0; wi < R / 32; wi++) {
+                const unsigned long long comb = ((unsigned long long)w[wi] << 32) | w[wi + 1];
+#pragma unroll
+                for (int o = 0; o < 32; o += 2) {
+                    const uint32_t s0 = (uint32_t)(comb >> (64 - L - o)) & mask;
+                    const uint32_t s1 = (uint32_t)(comb >> (64 - L - o - 1)) & mask;
+                    const uint32_t h0 = __half_as_ushort(__float2half_rn(tab[s0]));
+                    const uint32_t h1 = __half_as_ushort(__float2half_rn(tab[s1]));
+                    dst[(wi * 32 + o) >> 1] = h0 | (h1 << 16);
+                }
+            }
+            ssc[tid] = __half2float(p.scale1[n]);
+        } else {
+            for (int j = 0; j < R / 2; j++) dst[j] = 0u;
+            ssc[tid] = 0.f;
+        }
+    }
+    const int64_t wrow0 = row0 + 32 * warp;
+    const bool warp_active = wrow0 < ce;
+    const int blk_rel = (int)(wrow0 / 32 - cs / 32);
+    const int g = lane >> 2, t4 = lane & 3;
+
+    for (int qb = 0; qb < qn; qb += QT) {
+        const int nq = min(QT, qn - qb);
+        __syncthreads();
+        if (tid < QT) {
+            if (tid < nq) {
+                const int pi = qoff + qb + tid;
+                const int q = p.qid[pi];
+                qids[tid] = q;
+                qcs[tid] = p.qcp[pi];
+                thr[tid] = MODE ? p.t0[q] : 0.f;
+            } else {
+                qids[tid] = -1;
+            }
+        }
+        __syncthreads();
+        const int mt = (nq + 15) >> 4;
+        for (int i = tid; i < mt * 16 * (R * 2 / 16); i += NTHREADS) {
+            const int r = i >> 5, ch = i & 31;
+            const int q = qids[r];
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (q >= 0) v = reinterpret_cast<const uint4*>(p.Qh + (int64_t)q * R)[ch];
+            *reinterpret_cast<uint4*>(qt + r * RS + ch * 16) = v;
+        }
+        __syncthreads();
+        if (!warp_active) continue;
+
+        float acc[4][4][4];
+#pragma unroll
+        for (int m = 0; m < 4; m++)
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[m][j][e] = 0.f;
+#pragma unroll 4
+        for (int kb = 0; kb < R * 2; kb += 32) {  // 16 fp16 = 32 bytes per k-step
+            uint32_t b[4][2];
+#pragma unroll
+            for (int jp = 0; jp < 2; jp++) {
+                const int nrow = 32 * warp + 16 * jp + (lane & 7) + ((lane >> 4) << 3);
+                ldsm_x4(b[2 * jp][0], b[2 * jp][1], b[2 * jp + 1][0], b[2 * jp + 1][1],
+                        vt + nrow * RS + kb + ((lane >> 3) & 1) * 16);
+            }
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                if (m < mt) {
+                    uint32_t a[4];
+                    ldsm_x4(a[0], a[1], a[2], a[3], qt + (16 * m + (lane & 15)) * RS + kb + (lane >> 4) * 16);
+#pragma unroll
+                    for (int j = 0; j < 4; j++) mma_f16(acc[m][j], a, b[j][0], b[j][1]);
+                }
+            }
+        }
+        float sr[4][2];
+        bool rv[4][2];
+#pragma unroll
+        for (int j = 0; j < 4; j++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int r = 32 * warp + 8 * j + 2 * t4 + e;
+                const int64_t n = row0 + r;
+                rv[j][e] = n >= cs && n < ce;
+                sr[j][e] = ssc[r];
+            }
+#pragma unroll
+        for (int m = 0; m < 4; m++) {
+            if (m >= mt) break;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int ql = 16 * m + g + 8 * h;
+                const bool qv = ql < nq;
+                const float qcv = qv ? qcs[ql] : 0.f;
+                float est[4][2];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) est[j][e] = __fadd_rn(__fmul_rn(sr[j][e], acc[m][j][2 * h + e]), qcv);
+                if (MODE == 0) {
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+#pragma unroll
+                        for (int e = 0; e < 2; e++)
+                            if (rv[j][e]) mx = fmaxf(mx, est[j][e]);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                    if (qv && t4 == 0) p.bmc[(int64_t)(qoff + qb + ql) * p.MB + blk_rel] = mx;
+                } else {
+                    const float th = qv ? thr[ql] : INFINITY;
+                    unsigned kmask = 0;
+#pragma unroll
+                    for (int j = 0; j < 4; j++)
+#pragma unroll
+                        for (int e = 0; e < 2; e++)
+                            if (qv && rv[j][e] && est[j][e] >= th) kmask |= 1u << (2 * j + e);
+                    if (__any_sync(0xffffffffu, kmask != 0)) {
+                        const int s = __popc(kmask);
+                        int incl = s;
+                        int v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
+                        if (t4 >= 1) incl += v;
+                        v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
+                        if (t4 >= 2) incl += v;
+                        const int total = __shfl_sync(0xffffffffu, incl, 3, 4);
+                        int base = 0;
+                        const int q = qv ? qids[ql] : 0;
+                        if (t4 == 0 && total > 0) base = atomicAdd(p.cnt + q, total);
+                        base = __shfl_sync(0xffffffffu, base, 0, 4) + incl - s;
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+#pragma unroll
+                            for (int e = 0; e < 2; e++)
+                                if (kmask & (1u << (2 * j + e))) {
+                                    if (base < p.M) {
+                                        const int64_t o = (int64_t)q * p.M + base;
+                                        p.bval[o] = est[j][e];
+                                        p.bpos[o] = (int32_t)(row0 + 32 * warp + 8 * j + 2 * t4 + e);
+                                    }
+                                    base++;
+                                }
+                    }
+                }
+            }
+        }
+    }
+}
+
+constexpr size_t smem_bytes(int L) {
+    return (size_t)TILE_ROWS * RS + (size_t)QT * RS + ((size_t)1 << L) * 4 + TILE_ROWS * 4 + QT * 4 * 3;
+}
+
+}  // namespace trellis
+
+// ------------------------------------------------------------------------------------------------ tiered gather
+// est = qc + sum_t scale_t <q_t, cb_t[code]>, var = sum_t ||q_t||^2 sig_t^2 (`src/tiered_fused.py:8-41`); code of
+// coordinate 8j+k of tier t = sum_p bit(7-k) of byte j of plane p << (b-1-p).  One CTA per query holds the rotated
+// query (D floats) and every tier's codebook in shared memory; each warp scores one candidate at a time, lane l owning
+// byte positions l, l+32, ... of the candidate (all planes of a position are loaded together), folding scale_t into its
+// partial sum so that a candidate needs one reduction for the estimate and one for the variance.
+constexpr int TG_MAXT = 8;
+struct TieredSet {
+    int T, nbytes;  // nbytes: byte positions per candidate over all tiers = D / 8
+    int s[TG_MAXT], kb[TG_MAXT], bits[TG_MAXT], cboff[TG_MAXT], pbase[TG_MAXT + 1];
+    const uint8_t* planes[TG_MAXT];
+    const float* cb[TG_MAXT];
+};
+
+__global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __restrict__ pos, int B, int K,
+                                                          const float* __restrict__ qc, const float* __restrict__ Zq,
+                                                          int ldz, int D, TieredSet ts, const __half* __restrict__ scale,
+                                                          const __half* __restrict__ sig, int64_t N,
+                                                          float* __restrict__ est, float* __restrict__ sd) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_qn2[TG_MAXT];
+    __shared__ float s_scl[8][TG_MAXT];  // per warp: this candidate's scale of every tier
+    float* zq = reinterpret_cast<float*>(smem);  // D
+    float* cbs = zq + D;                         // sum_t 2^b_t
+    const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
+    for (int i = tid; i < D; i += blockDim.x) zq[i] = Zq[(int64_t)q * ldz + i];
+    for (int t = 0; t < ts.T; t++)
+        for (int i = tid; i < (1 << ts.bits[t]); i += blockDim.x) cbs[ts.cboff[t] + i] = ts.cb[t][i];
+    __syncthreads();
+    if (warp < ts.T) {
+        float a = 0.f;
+        for (int i = ts.s[warp] + lane; i < ts.s[warp] + 8 * ts.kb[warp]; i += 32) a += zq[i] * zq[i];
+        a = warp_sum(a);
+        if (lane == 0) s_qn2[warp] = a;
+    }
+    __syncthreads();
+    const float qcv = qc[q];
+    const int tl = lane < ts.T ? lane : 0;
+    const float qn2l = s_qn2[tl];
+    for (int i = warp; i < K; i += nw) {
+        const int64_t n = pos[(int64_t)q * K + i];
+        const float scl = lane < ts.T ? __half2float(scale[(int64_t)lane * N + n]) : 0.f;
+        const float sgl = lane < ts.T ? __half2float(sig[(int64_t)lane * N + n]) : 0.f;
+        if (lane < ts.T) s_scl[warp][lane] = scl;
+        __syncwarp();
+        float part = 0.f;
+        for (int gp = lane; gp < ts.nbytes; gp += 32) {
+            int t = 0;
+            while (t + 1 < ts.T && gp >= ts.pbase[t + 1]) t++;
+            const int j = gp - ts.pbase[t], b = ts.bits[t], kb = ts.kb[t];
+            uint32_t code[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            for (int pl = 0; pl < b; pl++) {
+                const uint32_t byt = __ldg(ts.planes[t] + ((int64_t)pl * N + n) * kb + j);
+#pragma unroll
+                for (int k = 0; k < 8; k++) code[k] |= ((byt >> (7 - k)) & 1u) << (b - 1 - pl);
+            }
+            const float* cbt = cbs + ts.cboff[t];
+            const float* z = zq + ts.s[t] + 8 * j;
+            float a = 0.f;
+#pragma unroll
+            for (int k = 0; k < 8; k++) a += cbt[code[k]] * z[k];
+            part += a * s_scl[warp][t];
+        }
+        __syncwarp();
+        part = warp_sum(part);
+        const float var = warp_sum(lane < ts.T ? qn2l * sgl * sgl : 0.f);
+        if (lane == 0) {
+            est[(int64_t)q * K + i] = qcv + part;
+            sd[(int64_t)q * K + i] = sqrtf(var);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------------------------------ routing (fp32)
+// probe = the nprobe largest float(QM[q, c]) * scale[c] (`src/engine_cell.py:40-42`), ordered (score desc, cell asc).
+__global__ void __launch_bounds__(512) route_topk_scaled_kernel(const __half* __restrict__ QM, const float* __restrict__ sc,
+                                                               int NC, int nprobe, int kp, int64_t* __restrict__ probe) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ SelectScratch ss;
+    __shared__ int s_fill;
+    unsigned long long* keys = reinterpret_cast<unsigned long long*>(smem);  // NC
+    unsigned long long* sb = keys + NC;                                      // kp
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    for (int c = tid; c < NC; c += nt) {
+        const float v = __fmul_rn(__half2float(QM[(int64_t)q * NC + c]), sc[c]);
+        keys[c] = ((unsigned long long)f2o(v) << 32) | (0xffffffffu - (uint32_t)c);
+    }
+    if (tid == 0) s_fill = 0;
+    __syncthreads();
+    const uint32_t Th = block_select_rth_largest<32, uint32_t>([&](int i) { return (uint32_t)(keys[i] >> 32); }, NC,
+                                                               nprobe, ss);
+    // ties at the boundary score: by cell index (keys are unique)
+    int gt = 0;
+    for (int c = tid; c < NC; c += nt) gt += (uint32_t)(keys[c] >> 32) > Th;
+    __shared__ int s_red[32];
+    gt = block_sum_int(gt, s_red);
+    const uint32_t Tl = block_select_rth_largest<32, uint32_t>(
+        [&](int i) { return (uint32_t)(keys[i] >> 32) == Th ? (uint32_t)keys[i] : 0u; }, NC, nprobe - gt, ss);
+    const unsigned long long T = ((unsigned long long)Th << 32) | Tl;
+    for (int c = tid; c < NC; c += nt)
+        if (keys[c] >= T) {
+            const int slot = atomicAdd(&s_fill, 1);
+            if (slot < nprobe) sb[slot] = keys[c];
+        }
+    for (int i = nprobe + tid; i < kp; i += nt) sb[i] = 0ull;
+    __syncthreads();
+    block_bitonic_desc(sb, kp);
+    for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = (int64_t)(0xffffffffu - (uint32_t)sb[i]);
+}
+
+// ------------------------------------------------------------------------------------------------ Viterbi (build)
+// Encoder of the bitshift trellis (k = 1) as `src/trellis_scan.py:21-32`: predecessors of state s are
+// (s >> 1) | (u << (L-1)); entering s emits vals[s]; ties keep predecessor u = 0 and the lowest final state.  One CTA
+// per vector: path costs in shared memory, backpointers one bit per (step, state).
+__global__ void __launch_bounds__(256) viterbi_kernel(const float* __restrict__ Zs, int n, int R,
+                                                      const float* __restrict__ vals, int L, int32_t* __restrict__ path) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int S = 1 << L, tid = threadIdx.x;
+    float* cost = reinterpret_cast<float*>(smem);          // 2 x S
+    float* v = cost + 2 * S;                                // S
+    uint32_t* back = reinterpret_cast<uint32_t*>(v + S);   // (R-1) x S/32
+    __shared__ float s_best[256];
+    __shared__ int s_arg[256];
+    const int vec = blockIdx.x;
+    const float* x = Zs + (int64_t)vec * R;
+    for (int s = tid; s < S; s += blockDim.x) {
+        v[s] = vals[s];
+        const float d = __fsub_rn(x[0], vals[s]);
+        cost[s] = __fmul_rn(d, d);
+    }
+    __syncthreads();
+    for (int j = 1; j < R; j++) {
+        const float* src = cost + ((j - 1) & 1) * S;
+        float* dst = cost + (j & 1) * S;
+        const float xj = x[j];
+        for (int s = tid; s < S; s += blockDim.x) {  // S is a multiple of 32: whole warps per iteration
+            const int p0 = s >> 1, p1 = p0 | (1 << (L - 1));
+            const float c0 = src[p0], c1 = src[p1];
+            const bool take1 = c1 < c0;
+            const float d = __fsub_rn(xj, v[s]);
+            dst[s] = __fadd_rn(take1 ? c1 : c0, __fmul_rn(d, d));  // no contraction: same rounding as separate ops
+            const uint32_t bits = __ballot_sync(0xffffffffu, take1);
+            if ((tid & 31) == 0) back[(j - 1) * (S / 32) + (s >> 5)] = bits;
+        }
+        __syncthreads();
+    }
+    // argmin of the final costs (lowest state on ties)
+    const float* fin = cost + ((R - 1) & 1) * S;
+    float best = INFINITY;
+    int arg = 0;
+    for (int s = tid; s < S; s += blockDim.x)
+        if (fin[s] < best) {
+            best = fin[s];
+            arg = s;
+        }
+    s_best[tid] = best;
+    s_arg[tid] = arg;
+    __syncthreads();
+    if (tid == 0) {
+        for (int i = 1; i < (int)blockDim.x; i++)
+            if (s_best[i] < best || (s_best[i] == best && s_arg[i] < arg)) {
+                best = s_best[i];
+                arg = s_arg[i];
+            }
+        int s = arg;
+        int32_t* out = path + (int64_t)vec * R;
+        out[R - 1] = s;
+        for (int j = R - 1; j >= 1; j--) {
+            const uint32_t take1 = (back[(j - 1) * (S / 32) + (s >> 5)] >> (s & 31)) & 1u;
+            s = (s >> 1) | ((int)take1 << (L - 1));
+            out[j - 1] = s;
+        }
+    }
+}
+
+}  // namespace fvs
+
+extern "C" int fvs_trellis_tile_rows(void) { return fvs::trellis::TILE_ROWS; }
+
+extern "C" int fvs_trellis_scan(fvs_stream_t stream, int mode, const uint16_t* Qh, int B, int R, const int32_t* qid,
+                                const int32_t* coff, const int32_t* ccnt, const float* qcp, const int32_t* tile_cell,
+                                const int32_t* tile_row0, int ntiles, const int64_t* off, int NC, const int32_t* words,
+                                int W, const float* tab, int L, const uint16_t* scale1, const float* t0, int32_t* cnt,
+                                float* bval, int32_t* bpos, int M, float* bmc, int MB) {
+    using namespace fvs::trellis;
+    FVS_CHECK_ARG(mode == 0 || mode == 1);
+    FVS_CHECK_ARG(R == fvs::trellis::R && B >= 0 && ntiles >= 0 && NC > 0 && L >= 2 && L <= 12);
+    FVS_CHECK_ARG(W >= (R + L - 1 + 31) / 32 && W <= MAXW);
+    FVS_CHECK_ARG(Qh && qid && coff && ccnt && qcp && tile_cell && tile_row0 && off && words && tab && scale1);
+    if (mode == 0) FVS_CHECK_ARG(bmc && MB > 0);
+    if (mode == 1) FVS_CHECK_ARG(t0 && cnt && bval && bpos && M > 0);
+    if (ntiles == 0 || B == 0) return FVS_OK;
+    Params p{(const __half*)Qh, qid, coff, ccnt, qcp, tile_cell, tile_row0, off, (const uint32_t*)words, tab,
+             (const __half*)scale1, t0, cnt, bval, bpos, bmc, W, L, M, MB};
+    const size_t sm = smem_bytes(L);
+    cudaError_t e = mode ? fvs_ensure_smem((const void*)trellis_scan_kernel<1>, sm)
+                         : fvs_ensure_smem((const void*)trellis_scan_kernel<0>, sm);
+    if (e != cudaSuccess) return (int)e;
+    if (mode == 0)
+        trellis_scan_kernel<0><<<ntiles, NTHREADS, sm, stream>>>(p);
+    else
+        trellis_scan_kernel<1><<<ntiles, NTHREADS, sm, stream>>>(p);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_tiered_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
+                                int ldz, int D, int T, const int32_t* tier_s, const int32_t* tier_e,
+                                const int32_t* tier_bits, const float* const* tier_cb,
+                                const uint8_t* const* tier_planes, const uint16_t* scale, const uint16_t* sig,
+                                int64_t N, float* est, float* sd) {
+    FVS_CHECK_ARG(pos && qc && Zq && tier_s && tier_e && tier_bits && tier_cb && tier_planes && scale && sig && est && sd);
+    FVS_CHECK_ARG(B >= 0 && K >= 1 && N > 0 && D > 0 && ldz >= D);
+    if (T < 1 || T > fvs::TG_MAXT) return FVS_ERANGE;
+    fvs::TieredSet ts;
+    ts.T = T;
+    int pb = 0, cbo = 0;
+    for (int t = 0; t < T; t++) {
+        FVS_CHECK_ARG(tier_e[t] > tier_s[t] && (tier_e[t] - tier_s[t]) % 8 == 0 && tier_e[t] <= D);
+        FVS_CHECK_ARG(tier_bits[t] >= 1 && tier_bits[t] <= 8 && tier_cb[t] && tier_planes[t]);
+        ts.s[t] = tier_s[t];
+        ts.kb[t] = (tier_e[t] - tier_s[t]) / 8;
+        ts.bits[t] = tier_bits[t];
+        ts.planes[t] = tier_planes[t];
+        ts.cb[t] = tier_cb[t];
+        ts.cboff[t] = cbo;
+        cbo += 1 << tier_bits[t];
+        ts.pbase[t] = pb;
+        pb += ts.kb[t];
+    }
+    ts.pbase[T] = pb;
+    ts.nbytes = pb;
+    const size_t sm = (size_t)(D + cbo) * 4;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::tiered_score_kernel, sm);  // 256 threads = 8 warps (s_scl)
+    if (e != cudaSuccess) return (int)e;
+    fvs::tiered_score_kernel<<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, ts, (const __half*)scale,
+                                                     (const __half*)sig, N, est, sd);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_route_topk_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe,
+                                     const float* cell_scale, int64_t* probe) {
+    FVS_CHECK_ARG(QM && cell_scale && probe && B >= 0 && NC > 0 && nprobe >= 1 && nprobe <= NC);
+    if (nprobe > 4096) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    int kp = 1;
+    while (kp < nprobe) kp <<= 1;
+    const size_t sm = (size_t)(NC + kp) * 8;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::route_topk_scaled_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::route_topk_scaled_kernel<<<B, 512, sm, stream>>>((const __half*)QM, cell_scale, NC, nprobe, kp, probe);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_viterbi_encode(fvs_stream_t stream, const float* Zs, int n, int R, const float* vals, int L,
+                                  int32_t* path) {
+    FVS_CHECK_ARG(Zs && vals && path && n >= 0 && R >= 2 && L >= 5 && L <= 12);
+    if (n == 0) return FVS_OK;
+    const int S = 1 << L;
+    const size_t sm = (size_t)3 * S * 4 + (size_t)(R - 1) * (S / 32) * 4;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::viterbi_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::viterbi_kernel<<<n, 256, sm, stream>>>(Zs, n, R, vals, L, path);
+    return fvs_launch_status();
+}

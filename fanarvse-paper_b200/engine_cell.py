@@ -1,0 +1,172 @@
+"""Default-engine search (cell-residual trellis stage 1, tiered gather stage 2) on the B200 C library: the drop-in
+for the reference's `EngineS` (`src/engine_cell.py:69-104`).
+
+`search(Qb, K, z, nprobe, k) -> (I [B,k], reads [B], cand_ids [B,K])`, one CUDA graph per (B, K, z, nprobe, k), the
+exactness flag as the only host synchronisation, and a recompute of flagged queries.  Host-side PyTorch keeps the
+dense products the reference computes with cuBLAS (QM = fp16(Q) @ means16^T, q . c, Q @ W1, Q @ VP); routing
+selection, pair lists, the trellis scan passes, threshold, stage-1 top-K, tiered gather scoring, classification,
+exact re-rank and final top-k run in libfanar_b200.  There is no CPU path.
+"""
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import ptr
+from .engine import BN, EngineB200I8, static_tiles
+
+
+class IndexS:
+    """Device-resident default-engine index in the reference's layout.
+
+    s1   : off, order, c, means16, inv_mnorm, W1 [d,R] f32, tab [2^L] f32, words [N,W] int32, scale1 [N] fp16
+           (`src/engine_cell.py:8-32`, `src/rev_fanardb.py:36-60`)
+    code : Lloyd-Max tiered code: TS, planes, scale, sig, VP [d,D] f32 and cbf (per-tier codebook levels)
+           (`src/tiered_fused.py:47-52`)
+    H16  : fp16 full-precision store [N, d] in original-id order
+    """
+
+    def __init__(self, s1, code, H16, device="cuda", L=10):
+        dev = torch.device(device)
+        self.device = dev
+        f = lambda x, dt=None: torch.as_tensor(x).to(device=dev, dtype=dt).contiguous()
+        self.off_np = np.asarray(s1["off"] if "off" in s1 else s1["off_t"].cpu().numpy(), np.int64)
+        self.off = f(self.off_np, torch.int64)
+        self.NC = len(self.off_np) - 1
+        self.N = int(self.off_np[-1])
+        self.order = f(s1["order"], torch.int32)
+        self.c = f(s1["c"], torch.float32)
+        self.means16 = f(s1["means16"], torch.float16)
+        self.inv_mnorm = f(s1["inv_mnorm"], torch.float32)
+        self.mnorm = None                      # pair constants are q . m_c itself (no normalised routing product)
+        self.W1 = f(s1["W1"], torch.float32)
+        self.R = self.W1.shape[1]
+        self.L = int(s1.get("L", L))
+        self.tab = f(s1["tab"], torch.float32)
+        self.words = f(s1["words"], torch.int32)
+        self.W = self.words.shape[1]
+        self.scale1 = f(s1["scale1"], torch.float16)
+        self.TS = [tuple(int(v) for v in t) for t in code["TS"]]
+        self.T = len(self.TS)
+        self.D = self.TS[-1][1]
+        self.planes = [f(p, torch.uint8) for p in code["planes"]]
+        self.cbf = [f(cb, torch.float32) for cb in code["cbf"]]
+        self.scale = f(code["scale"], torch.float16)
+        self.sig = f(code["sig"], torch.float16)
+        self.VP = f(code["VP"], torch.float32)[:, :self.D].contiguous()
+        self.H16 = f(H16, torch.float16)
+        self.d = self.H16.shape[1]
+        tc, tr, self.MB = static_tiles(self.off_np, _lib.lib().fvs_trellis_tile_rows())
+        self.tile_cell, self.tile_row0 = f(tc, torch.int32), f(tr, torch.int32)
+        self.ntiles = len(tc)
+        self._ts_s = _lib.i32_array([s for s, _, _ in self.TS])
+        self._ts_e = _lib.i32_array([e for _, e, _ in self.TS])
+        self._ts_b = _lib.i32_array([b for _, _, b in self.TS])
+        self._ts_cb = _lib.ptr_array(self.cbf)
+        self._ts_p = _lib.ptr_array(self.planes)
+
+    def nbytes_per_vector(self):
+        return 4 * self.W + 2 + sum((e - s) * b for s, e, b in self.TS) / 8 + 4 * self.T
+
+
+class EngineB200S(EngineB200I8):
+    """The reference's EngineS on libfanar_b200: (beta, rho) = (1.1, 0.75) for K <= 400 else (0.7, 0.5),
+    M = max(4096, 16 K) (`src/engine_cell.py:78-79`, `src/s1cell.py:181`).  Graph capture, the flag read and the
+    flagged-row recompute are inherited from EngineB200I8."""
+    M = None
+    FB_M = 65536
+
+    def __init__(self, index: IndexS):
+        super().__init__(index)
+        self.DELTA = None
+
+    def route(self, Qb, nprobe):
+        """QM = fp16(Q) @ means16^T (cuBLAS) and the nprobe cells of largest float(QM) / |m_c| (`src/engine_cell.py:40-42`)."""
+        ix = self.ix
+        QM = (Qb.half() @ ix.means16.T).contiguous()
+        probe = torch.empty(Qb.shape[0], nprobe, dtype=torch.int64, device=Qb.device)
+        self._call("route_topk", self.L.fvs_route_topk_scaled, ptr(QM), Qb.shape[0], ix.NC, nprobe, ptr(ix.inv_mnorm),
+                   ptr(probe))
+        return QM, probe
+
+    def _scan(self, mode, name, Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc):
+        ix = self.ix
+        self._call(name, self.L.fvs_trellis_scan, mode, ptr(Qh), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
+                   ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.words), ix.W,
+                   ptr(ix.tab), ix.L, ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB)
+
+    def stage1_trellis(self, Qb, QM, probe, K, rho_override=None, M_override=None, Qh=None):
+        """`s1cell.search_static` (`src/s1cell.py:176-195`) on the C library: returns pos [B,K] int64, ok [B] bool,
+        est1 [B,K]."""
+        ix, L = self.ix, self.L
+        B = Qb.shape[0]
+        dev = Qb.device
+        if Qh is None:
+            Qh = (Qb @ ix.W1).half().contiguous()
+        beta, rho = (1.1, 0.75) if K <= 400 else (0.7, 0.5)
+        if rho_override:
+            beta, rho = 1.5, rho_override
+        M = M_override or self.M or max(4096, 16 * K)
+        nprobe = probe.shape[1]
+        n1 = min(max(int(np.ceil(beta * K / (ix.N / ix.NC / BN + 1))), 1), nprobe)
+        probe = probe.contiguous()
+        qid, coff, ccnt, qcp, slot = self.pairs(probe, n1, QM, True)
+        bmc = torch.empty(B * n1 * ix.MB, device=dev)
+        self._scan(0, "trellis_scan_first", Qh, B, qid, coff, ccnt, qcp, None, None, None, None, 0, bmc)
+        t0 = torch.empty(B, device=dev)
+        self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), nprobe, n1, ptr(ix.off), B,
+                   int(np.ceil(rho * K)), ptr(t0))
+        qid, coff, ccnt, qcp, _ = self.pairs(probe, nprobe, QM, False)
+        cnt = torch.zeros(B, dtype=torch.int32, device=dev)
+        bval = torch.empty(B, M, device=dev)
+        bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
+        self._scan(1, "trellis_scan_emit", Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None)
+        pos = torch.empty(B, K, dtype=torch.int64, device=dev)
+        est1 = torch.empty(B, K, device=dev)
+        ok = torch.empty(B, dtype=torch.uint8, device=dev)
+        self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
+                   ptr(ok), None, 0.0, 9)
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, Qh=Qh, ccnt=ccnt, npairs=int(qid.numel()), bval=bval,
+                          bpos=bpos, slot=slot)
+        return pos, ok.bool(), est1
+
+    def rotated_query(self, Qb):
+        return (Qb @ self.ix.VP).contiguous()                              # `src/tiered_fused.py:57`
+
+    def score_tiered(self, QC, pos, Zq):
+        """`tiered_fused.score` (`src/tiered_fused.py:54-72`)."""
+        ix = self.ix
+        B, K = pos.shape
+        est = torch.empty(B, K, device=pos.device)
+        sd = torch.empty(B, K, device=pos.device)
+        self._call("tiered_score", self.L.fvs_tiered_score, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D, ix.T,
+                   ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_cb, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N, ptr(est),
+                   ptr(sd))
+        return est, sd
+
+    def _finish_s(self, Qb, QC, pos, z, k):
+        Zq = self.rotated_query(Qb)
+        est, sd = self.score_tiered(QC, pos, Zq)
+        I, reads, ids, score_k = self.refine(Qb, pos, est, sd, z, k)
+        self._last.update(est=est, sd=sd, Zq=Zq, score_k=score_k)
+        return I, reads.long(), ids
+
+    def _gpu(self, Qb, K, z, nprobe, k):
+        """`EngineS._gpu` (`src/engine_cell.py:74-84`)."""
+        if K <= k:
+            raise ValueError("need K > k")
+        QC = (Qb @ self.ix.c).contiguous()
+        QM, probe = self.route(Qb, nprobe)
+        pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K)
+        self._last.update(probe=probe, QM=QM, QC=QC, est1=est1)
+        I, reads, ids = self._finish_s(Qb, QC, pos, z, k)
+        return ok, I, reads, ids
+
+    def _fallback(self, Qb, K, z, nprobe, k):
+        """Recompute of flagged rows: every block maximum of the first-pass cells above the K-th is kept (rho = 1,
+        beta = 1.5), buffer 65536, so that at least K candidates are emitted."""
+        QC = (Qb @ self.ix.c).contiguous()
+        QM, probe = self.route(Qb, nprobe)
+        pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K, rho_override=1.0, M_override=self.FB_M)
+        return self._finish_s(Qb, QC, pos, z, k)

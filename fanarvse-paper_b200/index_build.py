@@ -270,3 +270,86 @@ def build_index(X16, nlist, R=256, refine_bits=None, seed=0, kmeans_sample=200_0
             cl["VP"] = block_rotation(cl)
             codes["lloyd"] = cl
     return s1, i8, codes
+
+
+# ------------------------------------------------------------------------------------------------ default engine code
+def trellis_table(L: int, seed: int = 0):
+    """Fixed Gaussian table of the bitshift trellis (`src/trellis.py:12-15`): T[s] = Phi^-1((perm[s] + 0.5) / 2^L),
+    perm a permutation of the 2^L states drawn from numpy's default_rng(seed)."""
+    from scipy.special import ndtri
+    S = 1 << L
+    perm = np.random.default_rng(seed).permutation(S)
+    return torch.tensor(ndtri((perm + 0.5) / S), dtype=torch.float32)
+
+
+def viterbi_encode(Zs, vals, L):
+    """State paths [n, R] int32 of the rows of Zs (f32, CUDA) through the k = 1 trellis with emitted values vals
+    (`src/trellis_scan.py:21-32`), on the GPU through the library's encoder."""
+    from . import _lib
+    Zs = Zs.float().contiguous()
+    vals = vals.float().contiguous()
+    path = torch.empty(Zs.shape, dtype=torch.int32, device=Zs.device)
+    _lib.check(_lib.lib().fvs_viterbi_encode(_lib.stream_handle(), _lib.ptr(Zs), Zs.shape[0], Zs.shape[1],
+                                             _lib.ptr(vals), L, _lib.ptr(path)), "viterbi_encode")
+    return path
+
+
+def paths_to_words(path, L):
+    """Bit stream of state paths (`src/trellis_scan.py:10-18`) as int32 words [n, ceil((R+L-1)/32)]: the first state's
+    L bits MSB-first, then the low bit of every later state, packed MSB-first."""
+    path = path.long()
+    n, r = path.shape
+    nbits = r + L - 1
+    W = (nbits + 31) // 32
+    bits = torch.zeros(n, W * 32, dtype=torch.int64, device=path.device)
+    bits[:, :L] = (path[:, :1] >> torch.arange(L - 1, -1, -1, device=path.device)) & 1
+    bits[:, L:nbits] = path[:, 1:] & 1
+    w = (bits.reshape(n, W, 32) << torch.arange(31, -1, -1, device=path.device)).sum(2)
+    return (w & 0xFFFFFFFF).to(torch.int64).to(torch.int32)
+
+
+def build_trellis(X16, s1, R=256, L=10, seed=0, chunk=65536):
+    """Stage-1 trellis code of the cell residuals (the reference's default engine): rotation W1 = V[:, :R] @ Haar(R)
+    over the covariance of the first 50k rows (`src/rev_fanardb.py:37-38`), step alpha from a grid by the MSE on
+    Gaussian segments (`src/rev_fanardb.py:39-43`), Viterbi paths of the normalised projected residuals, words and the
+    per-row scale nz / (fip * |y|) (`src/engine_cell.py:8-24`).  Needs CUDA (the encoder runs in the library).
+    Returns dict(W1, tab, alpha, words, scale1, L)."""
+    dev = X16.device
+    if dev.type != "cuda":
+        raise RuntimeError("build_trellis encodes on the GPU")
+    N, d = X16.shape
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        S = X16[:50000].float()
+        _, V = pca_eigh(S - S.mean(0))
+        W1 = (V[:, :R] @ torch.linalg.qr(torch.randn(R, R, generator=g).to(dev))[0]).contiguous()
+        Tt = trellis_table(L).to(dev)
+        G = torch.randn(512, R, generator=g).to(dev)
+        best = None
+        for a in np.linspace(0.6, 1.3, 15):
+            vals = (float(a) * Tt).contiguous()
+            m = float(((G - vals[viterbi_encode(G, vals, L).long()]) ** 2).mean())
+            if best is None or m < best[0]:
+                best = (m, float(a))
+        alpha = best[1]
+        tab = (alpha * Tt).contiguous()
+        off_t = torch.as_tensor(s1["off"], device=dev)
+        cell = cell_of_position(off_t, N)
+        order = s1["order"].long()
+        means = s1["means16"].float()
+        W = (R + L - 1 + 31) // 32
+        words = torch.empty(N, W, dtype=torch.int32, device=dev)
+        scale1 = torch.empty(N, dtype=torch.float16, device=dev)
+        for j in range(0, N, chunk):
+            Rr = X16[order[j:j + chunk]].float() - means[cell[j:j + chunk]]
+            n = len(Rr)
+            Z = Rr @ W1
+            nz = Z.norm(dim=1).clamp(min=1e-6)
+            Zs = Z / nz[:, None] * R ** 0.5
+            path = viterbi_encode(Zs, tab, L).long()
+            words[j:j + n] = paths_to_words(path, L)
+            Y = tab[path]
+            yn = Y.norm(dim=1)
+            fip = (Zs * Y).sum(1) / (yn * R ** 0.5)
+            scale1[j:j + n] = (nz / (fip * yn)).half()
+    return dict(W1=W1, tab=tab, alpha=alpha, words=words, scale1=scale1, L=L)

@@ -182,6 +182,46 @@ int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ord
 int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ids, int B, int k, const float* Q,
                      int ldq, float* score);
 
+/* Rows per work tile of fvs_trellis_scan (tiles start on the cell's first global 32-row boundary). */
+int fvs_trellis_tile_rows(void);
+
+/*
+ * Default engine, stage 1 (`src/s1cell.py:121-154`, `_first_compact_s` / `_emit_loop_s`): same contract as
+ * fvs_i8_scan with the score est = scale1[n] * dot(Qh[q], v_n) + qcp, where v_n is row n's trellis code decoded as
+ * `src/decode2.py:5-17` (words [N, W] uint32, bits MSB-first; value = tab[L-bit window], rounded to fp16) and
+ * Qh [B, 256] = fp16(Q @ W1); fp16 products accumulated in fp32 on the tensor cores.  R = 256, W >= ceil((R+L-1)/32).
+ */
+int fvs_trellis_scan(fvs_stream_t stream, int mode, const uint16_t* Qh, int B, int R,
+                     const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
+                     const int32_t* tile_cell, const int32_t* tile_row0, int ntiles, const int64_t* off, int NC,
+                     const int32_t* words, int W, const float* tab, int L, const uint16_t* scale1,
+                     const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M, float* bmc, int MB);
+
+/*
+ * Default engine, stage 2 (`src/tiered_fused.py:8-41, 54-72`): est = qc[q] + sum_t scale[t*N+n] * sum_x
+ * cb_t[code_x] * Zq[q, x] over the tier's coordinates x (code_x from the tier's bit planes, plane p giving bit b-1-p),
+ * sd = sqrt(sum_t ||Zq[q, s_t:e_t]||^2 * sig[t*N+n]^2); Zq = Q @ VP (f32).  Host arrays of length T: tier_s, tier_e,
+ * tier_bits, tier_cb (device pointers to 2^b codebook levels), tier_planes.  T <= 8.
+ */
+int fvs_tiered_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq, int ldz,
+                     int D, int T, const int32_t* tier_s, const int32_t* tier_e, const int32_t* tier_bits,
+                     const float* const* tier_cb, const uint8_t* const* tier_planes, const uint16_t* scale,
+                     const uint16_t* sig, int64_t N, float* est, float* sd);
+
+/*
+ * Default engine routing (`src/engine_cell.py:40-42`): probe[q, :] = the nprobe cells of largest
+ * float(QM[q, c]) * cell_scale[c] (QM fp16 = fp16(Q) @ means16^T, cell_scale = 1/|m_c|), ordered (score desc, cell asc).
+ */
+int fvs_route_topk_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, const float* cell_scale,
+                          int64_t* probe);
+
+/*
+ * Index build (not the query path): Viterbi encoding of n segments Zs [n, R] f32 with the bitshift trellis (k = 1) of
+ * `src/trellis_scan.py:21-32` (predecessors (s >> 1) | (u << (L-1)), emitted value vals[s], ties to u = 0 and to the
+ * lowest final state) -> path [n, R] int32 of states.
+ */
+int fvs_viterbi_encode(fvs_stream_t stream, const float* Zs, int n, int R, const float* vals, int L, int32_t* path);
+
 /*
  * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
  * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.

@@ -1,0 +1,218 @@
+"""GPU parity of the default-engine path (trellis stage 1, tiered gather stage 2) against the reference's golden
+vectors and the CPU oracle, through the C ABI.
+
+Stage-1 estimates of this path are fp16 products accumulated in fp32 on the tensor cores, in an order that differs
+from the reference's `tl.dot`: they agree within fp32 rounding (TOL), and thresholds, emitted sets and stage-1
+candidates are compared exactly except for items whose estimate lies within that rounding of the decision value.
+Integer work (routing order, pair lists, Viterbi paths and words, candidate ids) is compared bit for bit."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN, pkg
+from oracle import fvs_oracle as O
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+TOL = 2e-5
+
+
+def c(x):
+    return x.detach().cpu().numpy()
+
+
+@pytest.fixture(scope="module")
+def gt():
+    return dict(np.load(os.path.join(GOLDEN, "trellis_reference.npz")))
+
+
+@pytest.fixture(scope="module")
+def ec():
+    pkg("build").build()
+    return pkg("engine_cell")
+
+
+def _index(ec, f):
+    TS = [tuple(int(v) for v in r) for r in f["TS"]]
+    s1 = dict(off=f["off"], order=f["order"], c=f["c"], means16=f["means16"], inv_mnorm=f["inv_mnorm"], W1=f["W1"],
+              tab=f["tab"], words=f["words"], scale1=f["scale1"])
+    code = dict(TS=TS, planes=[f[f"planes{t}"] for t in range(len(TS))], cbf=[f[f"cbf{t}"] for t in range(len(TS))],
+                scale=f["scale"], sig=f["sig"], VP=f["VP"])
+    return ec.IndexS(s1, code, f["H16"], DEV)
+
+
+def _near(v, ref):
+    return np.abs(v - ref) <= TOL * (1 + np.abs(ref))
+
+
+def test_route_scaled_matches_reference_order(gt, ec):
+    f = gt
+    ix = _index(ec, f)
+    E = ec.EngineB200S(ix)
+    K, nprobe, k = (int(v) for v in f["params"])
+    Q = torch.from_numpy(f["Q"]).to(DEV)
+    QM, probe = E.route(Q, nprobe)
+    np.testing.assert_array_equal(c(QM), f["QM"])          # cuBLAS fp16 product equals the reference's CPU product here
+    sc = f["QM"].astype(np.float32) * f["inv_mnorm"][None]
+    want = np.stack([O.topk_desc(sc[q], nprobe) for q in range(len(sc))])
+    np.testing.assert_array_equal(c(probe), want)
+
+
+def test_trellis_scan_first_pass_and_threshold(gt, ec):
+    f = gt
+    ix = _index(ec, f)
+    E = ec.EngineB200S(ix)
+    K, nprobe, k = (int(v) for v in f["params"])
+    B = len(f["Q"])
+    Q = torch.from_numpy(f["Q"]).to(DEV)
+    QM = torch.from_numpy(f["QM"]).to(DEV)
+    probe = torch.from_numpy(f["QM"].astype(np.float32) * f["inv_mnorm"]).topk(nprobe, 1).indices.to(DEV)
+    Qh = torch.from_numpy(f["k_Qh"]).to(DEV)
+    pos, ok, est1 = E.stage1_trellis(Q, QM, probe, K, Qh=Qh)
+    last = E._last
+    n1, MB = last["n1"], int(f["k_MB"])
+    _, _, _, _, o = O.pairs(c(probe)[:, :n1], ix.NC, f["QM"])
+    gb = f["k_bmc"].reshape(-1, MB)[O.pair_slots(o, B, n1)]
+    pb = c(last["bmc"]).reshape(-1, MB)[c(last["slot"])]
+    valid = gb > -1e29
+    np.testing.assert_allclose(pb[valid], gb[valid], rtol=TOL, atol=TOL)
+    np.testing.assert_allclose(c(last["t0"]), f["k_t0"], rtol=TOL, atol=TOL)
+    np.testing.assert_array_equal(c(ok), f["out_ok"])
+    # stage-1 candidates: equal sets up to items tied with the K-th estimate within rounding
+    gpos = f["k_pos"]
+    for q in range(B):
+        a, b = set(c(pos[q]).tolist()), set(gpos[q].tolist())
+        kth = float(np.sort(c(est1[q]))[0])
+        diff = a ^ b
+        if diff:
+            bv, bp = c(last["bval"][q]), c(last["bpos"][q])
+            n = min(int(c(last["cnt"][q])), last["M"])
+            est_of = dict(zip(bp[:n].tolist(), bv[:n].tolist()))
+            for p in diff:
+                assert p in est_of and _near(est_of[p], kth), (q, p)
+
+
+def test_trellis_emit_matches_reference(gt, ec):
+    """the emit pass from the reference's own threshold: same counts and sets except items within rounding of t0."""
+    f = gt
+    ix = _index(ec, f)
+    E = ec.EngineB200S(ix)
+    K, nprobe, k = (int(v) for v in f["params"])
+    B = len(f["Q"])
+    M = int(f["k_M"])
+    d = lambda a, dt: torch.from_numpy(np.ascontiguousarray(a)).to(DEV, dt)
+    t0 = d(f["k_t0"], torch.float32)
+    cnt = torch.zeros(B, dtype=torch.int32, device=DEV)
+    bval = torch.empty(B, M, device=DEV)
+    bpos = torch.empty(B, M, dtype=torch.int32, device=DEV)
+    E._scan(1, "emit", d(f["k_Qh"], torch.float16), B, d(f["k_qid"], torch.int32), d(f["k_coff"], torch.int32),
+            d(f["k_ccnt"], torch.int32), d(f["k_qcp"], torch.float32), t0, cnt, bval, bpos, M, None)
+    cnt, bval, bpos = c(cnt), c(bval), c(bpos)
+    eq, ev, ep = f["k_emit_q"], f["k_emit_val"], f["k_emit_pos"]
+    for q in range(B):
+        n = min(int(cnt[q]), M)
+        sel = eq == q
+        gp, gv = ep[sel], ev[sel]
+        pp, pv = bpos[q, :n], bval[q, :n]
+        tq = f["k_t0"][q]
+        np.testing.assert_array_equal(np.sort(gp[~_near(gv, tq)]), np.sort(pp[~_near(pv, tq)]))
+        common, ia, ib_ = np.intersect1d(gp, pp, return_indices=True)
+        np.testing.assert_allclose(pv[ib_], gv[ia], rtol=TOL, atol=TOL)
+        assert abs(int(cnt[q]) - int(f["k_cnt"][q])) <= int(_near(gv, tq).sum() + _near(pv, tq).sum())
+
+
+def test_tiered_score_matches_reference(gt, ec):
+    f = gt
+    ix = _index(ec, f)
+    E = ec.EngineB200S(ix)
+    Q = torch.from_numpy(f["Q"]).to(DEV)
+    pos = torch.from_numpy(f["k_pos"]).to(DEV)
+    QC = torch.from_numpy(f["k_QC"]).to(DEV)
+    est, sd = E.score_tiered(QC, pos, E.rotated_query(Q))
+    np.testing.assert_allclose(c(est), f["k_est"], rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(c(sd), f["k_sd"], rtol=1e-5, atol=1e-6)
+    # and the oracle on the product's own rotated query
+    oe, osd = O.tiered_score(f["k_pos"], f["k_QC"], c(E.rotated_query(Q)), ix.TS, [f[f"planes{t}"] for t in range(ix.T)],
+                             [f[f"cbf{t}"] for t in range(ix.T)], f["scale"], f["sig"])
+    np.testing.assert_allclose(c(est), oe, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(c(sd), osd, rtol=1e-5, atol=1e-7)
+
+
+def test_viterbi_encoder_reproduces_reference_words(gt, ec):
+    f = gt
+    ib = pkg("index_build")
+    off = torch.as_tensor(f["off"])
+    N = len(f["order"])
+    cell = torch.searchsorted(off, torch.arange(N), right=True) - 1
+    Rr = torch.from_numpy(f["H16"])[torch.from_numpy(f["order"]).long()].float() - \
+        torch.from_numpy(f["means16"]).float()[cell]
+    Z = Rr @ torch.from_numpy(f["W1"])                  # the golden script's CPU product, so inputs are identical
+    nz = Z.norm(dim=1).clamp(min=1e-6)
+    Zs = (Z / nz[:, None] * 256 ** 0.5).to(DEV)
+    path = ib.viterbi_encode(Zs, torch.from_numpy(f["tab"]).to(DEV), 10)
+    words = ib.paths_to_words(path, 10)
+    np.testing.assert_array_equal(c(words), f["words"])
+    np.testing.assert_array_equal(c(path[:64]), O.viterbi_paths(c(Zs[:64]), f["tab"], 10))
+
+
+def test_search_matches_reference_end_to_end(gt, ec):
+    f = gt
+    ix = _index(ec, f)
+    E = ec.EngineB200S(ix)
+    K, nprobe, k = (int(v) for v in f["params"])
+    z = float(f["z"])
+    Q = torch.from_numpy(f["Q"]).to(DEV)
+    out = E.search_eager(Q, K, z, nprobe, k)
+    np.testing.assert_array_equal(c(out["ok"]).astype(bool), f["out_ok"])
+    same = c(out["reads"]) == f["out_reads"]
+    assert same.mean() >= 0.9
+    np.testing.assert_array_equal(c(out["I"])[same], f["out_I"][same])
+    # graph replay gives the eager results
+    I, reads, ids = E.search(Q, K, z, nprobe, k)
+    np.testing.assert_array_equal(c(I), c(out["I"]))
+    np.testing.assert_array_equal(c(ids), c(out["ids"]))
+
+
+@pytest.fixture(scope="module")
+def synth_index(ec):
+    synth, ib = pkg("synth"), pkg("index_build")
+    ds = synth.make_dataset(synth.MixtureSpec(n=60000, d=384, comps=64, nq=300, seed=7), DEV, gt_k=10)
+    X16 = ds["base16"]
+    s1, _, codes = ib.build_index(X16, 128, R=256, refine_bits=960, seed=7, kmeans_sample=60000, uniform=False,
+                                  lloyd=True)
+    tr = ib.build_trellis(X16, s1, seed=7)
+    s1.update(tr)
+    return ds, ec.IndexS(s1, codes["lloyd"], X16, DEV), s1, codes["lloyd"]
+
+
+def _oracle_index(s1, code, X16):
+    t = lambda x: x.detach().cpu().numpy() if torch.is_tensor(x) else np.asarray(x)
+    oc = dict(TS=code["TS"], planes=[t(p) for p in code["planes"]], cbf=[t(x) for x in code["cbf"]],
+              scale=t(code["scale"]), sig=t(code["sig"]), VP=t(code["VP"]))
+    return dict(off=np.asarray(s1["off"], np.int64), order=t(s1["order"]), means16=t(s1["means16"]),
+                inv_mnorm=t(s1["inv_mnorm"]), c=t(s1["c"]), W1=t(s1["W1"]), tab=t(s1["tab"]), words=t(s1["words"]),
+                scale1=t(s1["scale1"]), H16=t(X16), code=oc)
+
+
+@pytest.mark.parametrize("K,nprobe,k", [(60, 16, 10), (500, 40, 100)])
+def test_search_matches_oracle_synthetic(ec, synth_index, K, nprobe, k):
+    ds, ix, s1, code = synth_index
+    E = ec.EngineB200S(ix)
+    Q = ds["queries"][:120].contiguous()
+    out = E.search_eager(Q, K, 2.0, nprobe, k)
+    oi = _oracle_index(s1, code, ds["base16"])
+    ref = O.search_trellis(oi, c(Q), K, 2.0, nprobe, k, QM=c(out["QM"]), probe=c(out["probe"]), Qh=c(out["Qh"]),
+                           Zq=c(out["Zq"]).astype(np.float64))
+    np.testing.assert_array_equal(c(out["t0"]) > -1e29, ref["t0"] > -1e29)
+    np.testing.assert_allclose(c(out["t0"]), ref["t0"], rtol=TOL, atol=TOL)
+    okp = c(out["ok"]).astype(bool)
+    np.testing.assert_array_equal(okp, ref["ok"])
+    rows = np.nonzero(okp & (c(out["reads"]) == ref["reads"]))[0]
+    assert len(rows) >= 0.85 * len(Q)
+    np.testing.assert_array_equal(c(out["I"])[rows], ref["I"][rows])
+    # recall of the full search (fallback included) against brute force
+    I, _, _ = E.search(Q, K, 2.0, nprobe, k)
+    r = pkg("synth").recall(I.long().cpu(), ds["gt"][:120, :min(k, 10)].cpu(), min(k, 10))
+    assert r >= 0.9, r

@@ -104,3 +104,25 @@ def test_search_trellis_end_to_end(gt):
     same = out["reads"] == f["out_reads"]
     assert same.mean() >= 0.9
     np.testing.assert_array_equal(out["I"][same], f["out_I"][same])
+
+
+def test_trellis_encoder_matches_reference_words(gt):
+    """The oracle's table, Viterbi and bit packing re-encode the golden cell residuals to the reference's own words."""
+    f = gt
+    tab = f["tab"]
+    T = O.trellis_table(10)
+    alpha = float(tab[np.argmax(np.abs(T))] / T[np.argmax(np.abs(T))])
+    np.testing.assert_allclose(tab, (np.float32(alpha) * T).astype(np.float32), rtol=1e-6)
+    off = torch.as_tensor(f["off"])
+    N = len(f["order"])
+    cell = torch.searchsorted(off, torch.arange(N), right=True) - 1
+    X16 = torch.from_numpy(f["H16"])
+    rows = torch.arange(0, N, 7)[:160]                   # a spread sample of rows (the encoder is O(R 2^L) per row)
+    Rr = X16[torch.from_numpy(f["order"]).long()[rows]].float() - torch.from_numpy(f["means16"]).float()[cell[rows]]
+    Z = Rr @ torch.from_numpy(f["W1"])
+    nz = Z.norm(dim=1).clamp(min=1e-6)
+    Zs = (Z / nz[:, None] * 256 ** 0.5).numpy()
+    path = O.viterbi_paths(Zs, (np.float32(alpha) * T).astype(np.float32), 10)
+    words = O.paths_to_words(path, 10)
+    same = (words == f["words"][rows.numpy()]).all(1)
+    assert same.all(), same.mean()
