@@ -59,10 +59,15 @@ class ShardedSearch:
         if G == 1:
             ids_all, s_all = gid[None], S[None]
         else:
-            ids_l = [torch.empty_like(gid) for _ in range(G)]
-            s_l = [torch.empty_like(S) for _ in range(G)]
-            dist.all_gather(ids_l, gid.contiguous(), group=self.group)
-            dist.all_gather(s_l, S.contiguous(), group=self.group)
-            ids_all, s_all = torch.stack(ids_l), torch.stack(s_l)
+            # one collective: (id as two int32 words, score bits) per entry, gathered into [G, B, k, 3]
+            B = gid.shape[0]
+            rec = torch.cat([gid.contiguous().view(torch.int32).view(B, k, 2), S.contiguous().view(torch.int32)[..., None]], 2)
+            out = torch.empty((G,) + tuple(rec.shape), dtype=torch.int32, device=rec.device)
+            if out.device.type == "cuda":
+                dist.all_gather_into_tensor(out, rec, group=self.group)
+            else:
+                dist.all_gather(list(out.unbind(0)), rec, group=self.group)
+            ids_all = out[..., :2].contiguous().view(torch.int64).view(G, B, k)
+            s_all = out[..., 2].contiguous().view(torch.float32)
         Ig, Sg = self.merge(ids_all, s_all, k)
         return Ig, Sg, reads
