@@ -40,6 +40,8 @@ SIGNATURES = {
     "fvs_tiered_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P]),
     "fvs_route_topk_scaled": (I32, [P, P, I32, I32, I32, P, P]),
     "fvs_viterbi_encode": (I32, [P, P, I32, I32, P, I32, P]),
+    "fvs_dense_scan_tc": (I32, [P, I32, P, P, I32, I32, P, P, I64, P, P, P, P, I32, P, I64, P]),
+    "fvs_rth_largest": (I32, [P, P, I32, I32, I64, I32, P]),
     "fvs_exact_scores": (I32, [P, P, I32, P, I32, I32, P, I32, P]),
     "fvs_merge_topk": (I32, [P, P, P, I32, I32, I32, I32, P, P]),
 }

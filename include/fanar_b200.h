@@ -223,6 +223,24 @@ int fvs_route_topk_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC
 int fvs_viterbi_encode(fvs_stream_t stream, const float* Zs, int n, int R, const float* vals, int L, int32_t* path);
 
 /*
+ * Routing-free int8 scan (`throughput/brute.py:7-39`, `_scan`): the dense contraction of q8 [B, R] with every row code
+ * Z [N, R] (int32 accumulate on the tensor cores), est[q, n] = (float(acc) * qs[q]) * float(zs[n]) (zs fp16).
+ *   mode 0: out[q * ldo + n] = est (dense scores, used on the fixed row sample), ldo >= N
+ *   mode 1: every n with est >= t0[q] is appended to query q's buffer (bval/bpos [B, M], counter cnt[q]; entries past M
+ *           are counted, not stored), as MODE=1 of the reference.
+ * R a multiple of 128 (<= 8192); q8 and Z 16-byte aligned; N < 2^31.  status: set to 1 if a bounded wait expired.
+ */
+int fvs_dense_scan_tc(fvs_stream_t stream, int mode, const int8_t* q8, const float* qs, int B, int R, const int8_t* Z,
+                      const uint16_t* zs, int64_t N, const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M,
+                      float* out, int64_t ldo, int32_t* status);
+
+/*
+ * out[q] = the r-th largest of vals[q * ld + 0 .. n-1] (`throughput/brute.py:56-57`: `scores(...).topk(r).values[:, -1]`),
+ * 1 <= r <= n.
+ */
+int fvs_rth_largest(fvs_stream_t stream, const float* vals, int B, int n, int64_t ld, int r, float* out);
+
+/*
  * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
  * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.
  */
