@@ -256,6 +256,43 @@ __global__ void __launch_bounds__(512) rth_largest_kernel(const float* __restric
     if (threadIdx.x == 0) out[q] = o2f(k);
 }
 
+// Same result for r <= RM: every thread keeps the RM largest of its strided share in registers (branch-free insertion,
+// taken only by values above its current RM-th), the threads' r best go to shared memory, and one radix select over
+// those blockDim * r candidates (a superset of the row's r largest) gives the answer.
+template <int RM>
+__global__ void __launch_bounds__(512) rth_largest_small_kernel(const float* __restrict__ vals, int n, int64_t ld,
+                                                                int r, float* __restrict__ out) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ SelectScratch ss;
+    uint32_t* keys = reinterpret_cast<uint32_t*>(smem);  // blockDim * r
+    const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
+    const float* v = vals + (int64_t)q * ld;
+    float top[RM];
+#pragma unroll
+    for (int j = 0; j < RM; j++) top[j] = -INFINITY;
+    constexpr int U = 8;  // independent loads in flight per thread
+    for (int i0 = tid; i0 < n; i0 += U * nt) {
+        float xs[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) xs[u] = i0 + u * nt < n ? __ldg(v + i0 + u * nt) : -INFINITY;
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const float x = xs[u];
+            if (x > top[RM - 1]) {
+#pragma unroll
+                for (int j = RM - 1; j > 0; j--) top[j] = x > top[j - 1] ? top[j - 1] : fmaxf(top[j], x);
+                top[0] = fmaxf(top[0], x);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < RM; j++)
+        if (j < r) keys[j * nt + tid] = f2o(top[j]);
+    __syncthreads();
+    const uint32_t k = block_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, nt * r, r, ss);
+    if (tid == 0) out[q] = o2f(k);
+}
+
 }  // namespace dense
 }  // namespace fvs
 
@@ -320,6 +357,19 @@ extern "C" int fvs_dense_scan_tc(fvs_stream_t stream, int mode, const int8_t* q8
 extern "C" int fvs_rth_largest(fvs_stream_t stream, const float* vals, int B, int n, int64_t ld, int r, float* out) {
     FVS_CHECK_ARG(vals && out && B >= 0 && n >= 1 && ld >= n && r >= 1 && r <= n);
     if (B == 0) return FVS_OK;
+    if (r <= 32) {
+        const size_t sk = (size_t)512 * r * 4;
+        if (r <= 16) {
+            cudaError_t e = fvs_ensure_smem((const void*)fvs::dense::rth_largest_small_kernel<16>, sk);
+            if (e != cudaSuccess) return (int)e;
+            fvs::dense::rth_largest_small_kernel<16><<<B, 512, sk, stream>>>(vals, n, ld, r, out);
+        } else {
+            cudaError_t e = fvs_ensure_smem((const void*)fvs::dense::rth_largest_small_kernel<32>, sk);
+            if (e != cudaSuccess) return (int)e;
+            fvs::dense::rth_largest_small_kernel<32><<<B, 512, sk, stream>>>(vals, n, ld, r, out);
+        }
+        return fvs_launch_status();
+    }
     const size_t want = (size_t)n * 4;
     const int staged = want <= 200 * 1024;
     const size_t sm = staged ? want : 0;

@@ -126,3 +126,18 @@ def test_dense_engine_end_to_end(dm):
     r = synth.recall(I.long().cpu(), ds["gt"].cpu(), 10)
     assert r >= 0.95, r
     D.check_status()
+
+
+@pytest.mark.parametrize("r", [1, 7, 16, 17, 32, 33, 200])
+def test_rth_largest_matches_sort(dm, r):
+    lib = pkg("_lib")
+    g = torch.Generator().manual_seed(r)
+    B, n, ld = 37, 5003, 5010
+    v = torch.randn(B, ld, generator=g)
+    v[:, ::7] = v[:, 3:4]                       # ties
+    v[0, :] = 0.5                               # a row of equal values
+    vd = v.to(DEV)
+    out = torch.empty(B, device=DEV)
+    lib.check(lib.lib().fvs_rth_largest(lib.stream_handle(), lib.ptr(vd), B, n, ld, r, lib.ptr(out)), "rth")
+    want = -np.sort(-v[:, :n].numpy(), 1)[:, r - 1]
+    np.testing.assert_array_equal(c(out), want)
