@@ -290,11 +290,13 @@ def variant_trellis(args, dev, steps=20):
     """Default engine (config 4): cell-residual trellis stage 1 + tiered gather stage 2 on 2.25M x 768 (2048
     components, spectrum exponent 1.0), NC = 8192, batch 2000, k = 10."""
     synth, ib, ec = pkg("synth"), pkg("index_build"), pkg("engine_cell")
-    spec = synth.CONFIGS["c4_2m25_768"]
+    import dataclasses
+    spec = dataclasses.replace(synth.CONFIGS["c4_2m25_768"], n=args.trellis_rows)
+    nlist = 8192 if args.trellis_rows >= 2_000_000 else synth.default_nlist(args.trellis_rows)
     t0 = time.time()
     ds = synth.make_dataset(spec, dev, gt_k=10)
     X16 = ds["base16"]
-    s1, _, codes = ib.build_index(X16, 8192, R=256, refine_bits=1920, seed=0, uniform=False, lloyd=True)
+    s1, _, codes = ib.build_index(X16, nlist, R=256, refine_bits=1920, seed=0, uniform=False, lloyd=True)
     s1.update(ib.build_trellis(X16, s1, seed=0))
     ix = ec.IndexS(s1, codes["lloyd"], X16, dev)
     E = ec.EngineB200S(ix)
@@ -322,8 +324,8 @@ def variant_trellis(args, dev, steps=20):
     E.timing = None
     del ds, X16, ix, E
     torch.cuda.empty_cache()
-    return {"config": "2.25M x 768 fp16 (2048 comps, spectrum 1.0), default engine (trellis stage 1 + tiered "
-                      f"gather), NC=8192, batch {len(Q)}, k=10, z={z}",
+    return {"config": f"{args.trellis_rows / 1e6:g}M x 768 fp16 (2048 comps, spectrum 1.0), default engine (trellis "
+                      f"stage 1 + tiered gather), NC={nlist}, batch {len(Q)}, k=10, z={z}",
             "value": round(len(Q) / (ms * 1e-3), 1), "unit": "queries/s", "nprobe": npr, "K": K,
             "recall@10": round(rec, 4), "ms_per_step": round(ms, 4), "grid": rows, "build_s": round(build_s, 1),
             "kernel_ms": {n: round(v, 4) for n, v in kt.items()}}
@@ -343,7 +345,10 @@ def main():
     ap.add_argument("--z", type=float, default=1.25)
     ap.add_argument("--op", default="auto", help="nprobe:K:M or auto")
     ap.add_argument("--cpu-sample", type=int, default=48)
-    ap.add_argument("--no-variants", action="store_true", help="skip the routing-free and default-engine lines")
+    ap.add_argument("--variants", default="dense,trellis",
+                    help="comma list of extra measurements at N=1: dense (routing-free int8), trellis (default "
+                         "engine), or none")
+    ap.add_argument("--trellis-rows", type=int, default=2_250_000, help="rows of the default-engine dataset")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -368,6 +373,7 @@ def main():
         grid_rows = None
     E.MSZ = M
     k, z = 10, args.z
+    E.prewarm(Q0, K, z, npr, k)
     I = search(Q0, K, z, npr, k)
     rec = pkg("synth").recall(I.cpu(), gt.cpu(), 10)
     # ---- timed region: device-resident inputs
@@ -428,10 +434,21 @@ def main():
         q1 = Qs[1][i:i + 1]
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        r = search(q1, K, z, npr, k)
-        r.cpu()
+        if world == 1:
+            E.search_host(q1, K, z, npr, k)           # latency mode: ids land in pinned host memory
+        else:
+            search(q1, K, z, npr, k).cpu()
         lat.append((time.perf_counter() - t0) * 1e3)
     lat = sorted(lat[10:])
+    lat32 = []
+    if world == 1 and args.batch >= 32:
+        for i in range(40):
+            q32 = Qs[2][(32 * i) % (args.batch - 31):][:32]
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            E.search_host(q32, K, z, npr, k)
+            lat32.append((time.perf_counter() - t0) * 1e3)
+        lat32 = sorted(lat32[10:])
     # ---- roofline of the dominant library kernel (eager searches, events on the launching stream)
     kt, ebytes = kernel_timing(E, Qs[0], K, z, npr, k, 5)
     dom = max(kt, key=kt.get)
@@ -449,10 +466,14 @@ def main():
         cpu = {"value": round(qps, 2), "unit": "queries/s", "cores": torch.get_num_threads(), "kind": "port",
                "sample": f"{nq} queries of the timed batch through the numpy oracle of the whole search"}
     variants = None
-    if rank == 0 and world == 1 and not args.no_variants:
+    want = set(v.strip() for v in args.variants.split(",")) - {"none", ""}
+    if rank == 0 and world == 1 and want:
         variants = {}
-        for name, fn in (("dense_int8_routing_free", lambda: variant_dense(args, ds, s1, ix, gt, dev)),
-                         ("default_engine_trellis", lambda: variant_trellis(args, dev))):
+        todo = [("dense", "dense_int8_routing_free", lambda: variant_dense(args, ds, s1, ix, gt, dev)),
+                ("trellis", "default_engine_trellis", lambda: variant_trellis(args, dev))]
+        for key, name, fn in todo:
+            if key not in want:
+                continue
             try:
                 variants[name] = fn()
                 log(name, json.dumps(variants[name]))
@@ -471,6 +492,7 @@ def main():
                                  "batches cycled)", "value_scaling": "queries/s x (database rows / 1M)",
                            "fallback_queries_per_step": round((E.nbad - nbad0) / args.steps, 3),
                            "batch1_p50_ms": round(lat[len(lat) // 2], 4), "batch1_p99_ms": round(lat[-1], 4),
+                           "batch32_p50_ms": round(lat32[len(lat32) // 2], 4) if lat32 else None,
                            "operating_points": grid_rows},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu}
         if variants:

@@ -105,6 +105,7 @@ class EngineB200I8:
     LUTH = True
     BETA = None
     SCAN = "tc"      # "tc": tcgen05 kernel (the product path); "mma": the mma.sync kernel kept as a baseline
+    SMALL = 32       # batches up to this size take the streaming scan (fvs_i8_scan_small) instead of the tile scan
 
     def __init__(self, index: IndexI8):
         self.ix = index
@@ -185,6 +186,8 @@ class EngineB200I8:
         rho = rho_override if rho_override else (self.RHO or (0.75 if K <= 400 else 0.5))
         n1 = self.first_pass_cells(K, probe.shape[1], rho_override)
         probe = probe.contiguous()
+        if B <= self.SMALL and self.SCAN != "mma":
+            return self._stage1_small(q8, qs, B, QM, probe, K, M, rho, n1, rho_override)
         qid, coff, ccnt, qcp, slot = self.pairs(probe, n1, QM, True)
         bmc = torch.empty(B * n1 * ix.MB, device=dev)
         self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt, qcp, None, None, None, None, 0, bmc)
@@ -205,6 +208,43 @@ class EngineB200I8:
                    ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
         self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, npairs=int(qid.numel()),
                           bval=bval, bpos=bpos, slot=slot)
+        return pos, ok.bool(), est1, ncnt
+
+    def _ident(self, n):
+        """slot[i] = i (the streaming scan's pair slots), cached per length."""
+        t = getattr(self, "_ident_cache", None)
+        if t is None or t.numel() < n:
+            t = torch.arange(max(n, 1024), dtype=torch.int32, device=self.ix.device)
+            self._ident_cache = t
+        return t
+
+    def _stage1_small(self, q8, qs, B, QM, probe, K, M, rho, n1, rho_override):
+        """stage 1 for small batches: streaming scan straight from the probe list (no pair sort)."""
+        ix, L = self.ix, self.L
+        dev = q8.device
+        npr = probe.shape[1]
+        common = lambda mode, ncols: (mode, ptr(q8), ptr(qs), B, ix.R, ptr(probe), npr, ncols, ptr(QM), ix.NC,
+                                      ptr(ix.mnorm), ptr(ix.off), ptr(ix.Z), ptr(ix.zs))
+        bmc = torch.empty(B * n1 * ix.MB, device=dev)
+        self._call("i8_scan_first", L.fvs_i8_scan_small, *common(0, n1), None, None, None, None, 0, ptr(bmc), ix.MB)
+        t0 = torch.empty(B, device=dev)
+        slot = self._ident(B * n1)
+        self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), npr, n1, ptr(ix.off), B,
+                   int(np.ceil(rho * K)), ptr(t0))
+        cnt = torch.zeros(B, dtype=torch.int32, device=dev)
+        bval = torch.empty(B, M, device=dev)
+        bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
+        self._call("i8_scan_emit", L.fvs_i8_scan_small, *common(1, npr), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M,
+                   None, ix.MB)
+        pos = torch.empty(B, K, dtype=torch.int64, device=dev)
+        est1 = torch.empty(B, K, device=dev)
+        ok = torch.empty(B, dtype=torch.uint8, device=dev)
+        use_delta = self.DELTA is not None and not rho_override
+        ncnt = torch.empty(B, dtype=torch.int32, device=dev) if use_delta else None
+        self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
+                   ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=None, npairs=B * npr, bval=bval,
+                          bpos=bpos, slot=slot[:B * n1], probe=probe)
         return pos, ok.bool(), est1, ncnt
 
     # ------------------------------------------------------------------ stages 2-3
@@ -328,6 +368,51 @@ class EngineB200I8:
             ids[badd] = c[:, :ids.shape[1]]
         return I, nr, ids
 
+    def search_host(self, Qb, K, z, nprobe, k):
+        """Latency-mode search returning the top-k ids as a host numpy array [B, k] (`EngineT.search_host`,
+        `src/engine_cell.py:121-137`): the graph also copies the exactness flags, the status word and the ids into
+        pinned host memory, so a search is one replay and one stream synchronisation; flagged rows are recomputed."""
+        if not Qb.is_cuda:
+            raise RuntimeError("EngineB200I8.search_host needs CUDA queries (the B200 library has no CPU path)")
+        B = len(Qb)
+        key = ("host", B, K, z, nprobe, k)
+        if key not in self.graphs:
+            qs = Qb.clone()
+            host = torch.empty((B, k + 2), dtype=torch.int32, pin_memory=True)
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+
+            def body():
+                ok, I, nr, ids = self._gpu(qs, K, z, nprobe, k)
+                packed = torch.cat([ok.to(torch.int32)[:, None], self.status.expand(B, 1), I.to(torch.int32)], 1)
+                host.copy_(packed, non_blocking=True)
+
+            with torch.cuda.stream(st):
+                for _ in range(3):
+                    body()
+            torch.cuda.current_stream().wait_stream(st)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            n0 = self.launches
+            with torch.cuda.graph(g):
+                body()
+            self.graph_launches[key] = self.launches - n0
+            self.graphs[key] = (g, qs, host.numpy())
+        g, qs, h = self.graphs[key]
+        qs.copy_(Qb)
+        g.replay()
+        torch.cuda.current_stream().synchronize()
+        self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
+        if h[0, 1] != 0:
+            raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
+        out = h[:, 2:].copy()
+        if not h[:, 0].all():
+            bad = np.nonzero(h[:, 0] == 0)[0]
+            self.nbad += len(bad)
+            a, _, _ = self._fallback_graphed(Qb, torch.from_numpy(bad), K, z, nprobe, k)
+            out[bad] = a.cpu().numpy()
+        return out
+
     FALLBACK_BUCKETS = (8, 16, 32, 64, 128, 256)
 
     def _fallback_graphed(self, Qb, bad, K, z, nprobe, k):
@@ -359,6 +444,14 @@ class EngineB200I8:
         g.replay()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         return a[:nb].clone(), b[:nb].clone(), c[:nb].clone()
+
+    def prewarm(self, Qb, K, z, nprobe, k, buckets=None):
+        """Capture the recompute graphs of every padded batch size up front (a capture costs milliseconds; a timed
+        or latency-critical search should only replay)."""
+        for b in buckets or self.FALLBACK_BUCKETS:
+            if b <= len(Qb):
+                self._fallback_graphed(Qb, torch.arange(b), K, z, nprobe, k)
+        torch.cuda.synchronize()
 
     def search_eager(self, Qb, K, z, nprobe, k):
         """One search without graph capture (same kernels); returns the intermediates for parity tests."""

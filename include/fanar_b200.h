@@ -186,6 +186,19 @@ int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_
 int fvs_trellis_tile_rows(void);
 
 /*
+ * Small-batch int8 scan (B <= 32): same contract and arithmetic as fvs_i8_scan_tc, streamed from HBM with 16-byte loads
+ * and dp4a, one CTA per (query, probe column, 4 blocks), taking the work straight from probe [B, nprobe] (columns
+ * 0..ncols-1) without a pair list: the pair constant is float(QM[q, c]) * mnorm[c] (mnorm may be NULL: the constant is
+ * float(QM[q, c])) and mode 0 writes bmc[(q * ncols + j) * MB + blk - cs/32] (pair slot q * ncols + j, so
+ * fvs_threshold takes slot[i] = i).  Replaces `_first8c` / `_emit8c` (`throughput/ivf8c_kern.py:2-36`) for batches where
+ * a cell is probed by one or two queries.
+ */
+int fvs_i8_scan_small(fvs_stream_t stream, int mode, const int8_t* q8, const float* qs, int B, int R,
+                      const int64_t* probe, int nprobe, int ncols, const uint16_t* QM, int NC, const float* mnorm,
+                      const int64_t* off, const int8_t* Z, const float* zs, const float* t0, int32_t* cnt, float* bval,
+                      int32_t* bpos, int M, float* bmc, int MB);
+
+/*
  * Default engine, stage 1 (`src/s1cell.py:121-154`, `_first_compact_s` / `_emit_loop_s`): same contract as
  * fvs_i8_scan with the score est = scale1[n] * dot(Qh[q], v_n) + qcp, where v_n is row n's trellis code decoded as
  * `src/decode2.py:5-17` (words [N, W] uint32, bits MSB-first; value = tab[L-bit window], rounded to fp16) and

@@ -25,6 +25,13 @@ def eng():
     return pkg("engine")
 
 
+def _set_scan(E, scan):
+    """"tc": the tcgen05 tile scan at every batch size; "small": the streaming scan at every batch size; "mma": the
+    mma.sync baseline."""
+    E.SCAN = "mma" if scan == "mma" else "tc"
+    E.SMALL = 10 ** 9 if scan == "small" else 0
+
+
 def _golden_engine(eng, f, case):
     idx = golden_index(f, case)
     code = idx["code"]
@@ -118,12 +125,12 @@ def _random_index(eng, n, d, nlist, nq, seed, comps=32):
     (20000, 256, 64, 33, 40, 64, 10, 4096),       # every cell probed
     (20000, 256, 64, 1, 40, 12, 10, 4096),        # batch 1
 ])
-@pytest.mark.parametrize("scan", ["tc", "mma"])
+@pytest.mark.parametrize("scan", ["tc", "small", "mma"])
 def test_search_matches_oracle(eng, n, d, nlist, nq, K, nprobe, k, M, scan):
     ds, ix, oi = _random_index(eng, n, d, nlist, nq, seed=7)
     E = eng.EngineB200I8(ix)
     E.MSZ = M
-    E.SCAN = scan
+    _set_scan(E, scan)
     Q = ds["queries"]
     r = E.search_eager(Q, K, 1.25, nprobe, k)
     QM, probe = E.route(Q, nprobe)
@@ -311,3 +318,18 @@ def test_quantize_matches_reference_formula(eng):
     L.check(lib.fvs_quantize(L.stream_handle(), L.ptr(z), 257, 256, 256, L.ptr(q8), L.ptr(qs)), "quantize")
     np.testing.assert_array_equal(c(qs), c(qs_ref))
     np.testing.assert_array_equal(c(q8), c(q8_ref))
+
+
+def test_search_host_matches_search(eng):
+    """latency mode (ids copied to pinned host memory inside the graph) returns the device search's ids"""
+    synth, ib = pkg("synth"), pkg("index_build")
+    ds = synth.make_dataset(synth.MixtureSpec(n=20000, d=256, comps=16, nq=40, seed=3), DEV, gt_k=10)
+    s1, i8, codes = ib.build_index(ds["base16"], 48, R=256, refine_bits=640, seed=3, kmeans_sample=20000)
+    ix = eng.IndexI8(s1, i8, codes["uniform"], ds["base16"], DEV)
+    E = eng.EngineB200I8(ix)
+    E.MSZ = 600                                          # small buffer: some rows take the recompute path
+    Q = ds["queries"]
+    for B in (1, 5, 40):
+        I, _, _ = E.search(Q[:B].contiguous(), 40, 1.5, 12, 10)
+        h = E.search_host(Q[:B].contiguous(), 40, 1.5, 12, 10)
+        np.testing.assert_array_equal(h, c(I))
