@@ -161,7 +161,11 @@ def emit_bytes(E, B, R=256):
     the emitted (value, position) pairs."""
     last = E._last
     off = E.ix.off_np
-    probed = last["ccnt"].cpu().numpy() > 0
+    if last["ccnt"] is not None:
+        probed = last["ccnt"].cpu().numpy() > 0
+    else:                                   # streaming small-batch scan: the cells of the probe list
+        probed = np.zeros(len(off) - 1, bool)
+        probed[np.unique(last["probe"].cpu().numpy())] = True
     rows = int((np.diff(off)[probed]).sum())
     emitted = int(torch.clamp(last["cnt"], max=last["M"]).sum())
     return rows * (R + 4) + last["npairs"] * 8 + B * (R + 12) + emitted * 8
@@ -431,7 +435,7 @@ def main():
     # ---- batch-1 latency (one query per search, graph path), p50
     lat = []
     for i in range(60):
-        q1 = Qs[1][i:i + 1]
+        q1 = Qs[1][i % args.batch:][:1]
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         if world == 1:
