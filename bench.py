@@ -326,13 +326,16 @@ def variant_trellis(args, dev, steps=20):
     torch.cuda.synchronize()
     kt = {n: float(np.mean([a.elapsed_time(b) for a, b in v])) for n, v in E.timing.items()}
     E.timing = None
+    cnt = E._last["cnt"]
+    flags = {"underflow": int((cnt < K).sum()), "overflow": int((cnt > E._last["M"]).sum()),
+             "cnt_median": int(cnt.float().median())}
     del ds, X16, ix, E
     torch.cuda.empty_cache()
     return {"config": f"{args.trellis_rows / 1e6:g}M x 768 fp16 (2048 comps, spectrum 1.0), default engine (trellis "
                       f"stage 1 + tiered gather), NC={nlist}, batch {len(Q)}, k=10, z={z}",
             "value": round(len(Q) / (ms * 1e-3), 1), "unit": "queries/s", "nprobe": npr, "K": K,
             "recall@10": round(rec, 4), "ms_per_step": round(ms, 4), "grid": rows, "build_s": round(build_s, 1),
-            "kernel_ms": {n: round(v, 4) for n, v in kt.items()}}
+            "kernel_ms": {n: round(v, 4) for n, v in kt.items()}, "flagged_last_batch": flags}
 
 
 # ---------------------------------------------------------------------------------------------------- main

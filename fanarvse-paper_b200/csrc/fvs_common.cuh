@@ -51,6 +51,15 @@ __device__ __forceinline__ float o2f(uint32_t k) {
     return __uint_as_float(u);
 }
 
+// atomic max of a float in global memory holding a valid (non-NaN) float: non-negative floats order as signed ints,
+// negative ones in reverse as unsigned ints
+__device__ __forceinline__ void atomic_max_float(float* addr, float v) {
+    if (v >= 0.f)
+        atomicMax(reinterpret_cast<int*>(addr), __float_as_int(v));
+    else
+        atomicMin(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
 __device__ __forceinline__ int next_pow2(int x) {
     int p = 1;
     while (p < x) p <<= 1;

@@ -4,10 +4,11 @@
 // fvs_trellis_scan replaces `_first_compact_s` / `_emit_loop_s` (`src/s1cell.py:121-154`) with the decoder of
 // `src/decode2.py:5-17`: value_j = tab[state_j], state_j = ((w[j/32] << 32 | w[j/32+1]) >> (64 - L - j%32)) & (2^L-1)
 // (bits MSB-first per uint32 word, `src/trellis_scan.py:10-18`), rounded to fp16 as the reference's `.to(fp16)`.
-// One CTA owns 128 code rows of one cell (four of the reference's 32-row blocks): each thread decodes one row through
-// the 1024-entry table held in shared memory into an fp16 tile; queries (fp16 Q @ W1) come in tiles of 64; the dot
-// products run on the tensor cores (mma m16n8k16, fp16 in, fp32 accumulate) and the epilogue computes
-// est = scale1[n] * dot + qcp (fp32, unfused) with the same first-pass / threshold-emit logic as the int8 scan.
+// One CTA owns 128 code rows of one cell (four of the reference's 32-row blocks): each thread decodes one row into an
+// fp16 tile through a shared-memory table of fp16 value pairs indexed by (L+1)-bit windows (two states per lookup);
+// queries (fp16 Q @ W1) come in tiles of 64; the dot products run on the tensor cores (mma m16n8k16, fp16 in, fp32
+// accumulate) and the epilogue computes est = scale1[n] * dot + qcp (fp32, unfused) with the same first-pass /
+// threshold-emit logic as the int8 scan.
 #include <cuda.h>
 
 #include "fvs_common.cuh"
@@ -39,7 +40,7 @@ struct Params {
     float* bval;
     int32_t* bpos;
     float* bmc;
-    int W, L, M, MB;
+    int W, L, M, MB, ntiles;
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -60,192 +61,283 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
     extern __shared__ __align__(16) uint8_t smem[];
     uint8_t* vt = smem;                                        // TILE_ROWS x RS (decoded fp16 values)
     uint8_t* qt = vt + TILE_ROWS * RS;                         // QT x RS (fp16 queries)
-    float* tab = reinterpret_cast<float*>(qt + QT * RS);       // 2^L
-    float* ssc = tab + (1 << p.L);                             // TILE_ROWS row scales
+    uint32_t* tab2 = reinterpret_cast<uint32_t*>(qt + QT * RS);  // 2^(L+1): fp16 value pairs of (L+1)-bit windows
+    float* ssc = reinterpret_cast<float*>(tab2 + (2 << p.L));  // TILE_ROWS row scales
     float* qcs = ssc + TILE_ROWS;                              // QT
     float* thr = qcs + QT;                                     // QT
     int* qids = reinterpret_cast<int*>(thr + QT);              // QT
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int c = p.tile_cell[blockIdx.x];
-    const int qn = p.ccnt[c];
-    if (qn == 0) return;
-    const int64_t cs = p.off[c], ce = p.off[c + 1];
-    const int64_t row0 = p.tile_row0[blockIdx.x];
-    const int qoff = p.coff[c];
     const int L = p.L, W = p.W;
 
-    for (int i = tid; i < (1 << L); i += NTHREADS) tab[i] = p.tab[i];
-    __syncthreads();
-    // ---- decode one row per thread (rows outside the cell: zeros)
+    // pair table: window w of L+1 bits covers two consecutive states (w >> 1, w & (2^L - 1)); entry = their two
+    // values rounded to fp16, first value in the low half (memory order of the decoded row)
     {
-        const int64_t n = row0 + tid;
-        uint32_t* dst = reinterpret_cast<uint32_t*>(vt + tid * RS);
-        if (n >= cs && n < ce) {
-            uint32_t w[R / 32 + 1];
-#pragma unroll
-            for (int i = 0; i <= R / 32; i++) w[i] = (i < W) ? p.words[n * W + i] : 0u;
-            const uint32_t mask = (1u << L) - 1u;
-#pragma unroll
-            for (int wi = 0; wi < R / 32; wi++) {
-                const unsigned long long comb = ((unsigned long long)w[wi] << 32) | w[wi + 1];
-#pragma unroll
-                for (int o = 0; o < 32; o += 2) {
-                    const uint32_t s0 = (uint32_t)(comb >> (64 - L - o)) & mask;
-                    const uint32_t s1 = (uint32_t)(comb >> (64 - L - o - 1)) & mask;
-                    const uint32_t h0 = __half_as_ushort(__float2half_rn(tab[s0]));
-                    const uint32_t h1 = __half_as_ushort(__float2half_rn(tab[s1]));
-                    dst[(wi * 32 + o) >> 1] = h0 | (h1 << 16);
-                }
-            }
-            ssc[tid] = __half2float(p.scale1[n]);
-        } else {
-            for (int j = 0; j < R / 2; j++) dst[j] = 0u;
-            ssc[tid] = 0.f;
+        const uint32_t mask = (1u << L) - 1u;
+        for (int w = tid; w < (2 << L); w += NTHREADS) {
+            const uint32_t h0 = __half_as_ushort(__float2half_rn(__ldg(p.tab + (w >> 1))));
+            const uint32_t h1 = __half_as_ushort(__float2half_rn(__ldg(p.tab + (w & mask))));
+            tab2[w] = h0 | (h1 << 16);
         }
     }
-    const int64_t wrow0 = row0 + 32 * warp;
-    const bool warp_active = wrow0 < ce;
-    const int blk_rel = (int)(wrow0 / 32 - cs / 32);
-    const int g = lane >> 2, t4 = lane & 3;
-
-    for (int qb = 0; qb < qn; qb += QT) {
-        const int nq = min(QT, qn - qb);
-        __syncthreads();
-        if (tid < QT) {
-            if (tid < nq) {
-                const int pi = qoff + qb + tid;
-                const int q = p.qid[pi];
-                qids[tid] = q;
-                qcs[tid] = p.qcp[pi];
-                thr[tid] = MODE ? p.t0[q] : 0.f;
+    __syncthreads();
+    // the CTA walks tiles blockIdx.x, + gridDim.x, ... (with one CTA per tile: exactly one)
+    for (int tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x) {
+        const int c = p.tile_cell[tile];
+        const int qn = p.ccnt[c];
+        if (qn == 0) continue;  // uniform over the CTA
+        const int64_t cs = p.off[c], ce = p.off[c + 1];
+        const int64_t row0 = p.tile_row0[tile];
+        const int qoff = p.coff[c];
+        // ---- decode one row per thread (rows outside the cell: zeros)
+        {
+            const int64_t n = row0 + tid;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(vt + tid * RS);
+            if (n >= cs && n < ce) {
+                uint32_t w[R / 32 + 1];
+#pragma unroll
+                for (int i = 0; i <= R / 32; i++) w[i] = (i < W) ? p.words[n * W + i] : 0u;
+                const uint32_t mask2 = (2u << L) - 1u;
+#pragma unroll
+                for (int wi = 0; wi < R / 32; wi++) {
+                    const unsigned long long comb = ((unsigned long long)w[wi] << 32) | w[wi + 1];
+#pragma unroll
+                    for (int o = 0; o < 32; o += 2)  // states o and o+1 = the L+1 bits starting at bit o
+                        dst[(wi * 32 + o) >> 1] = tab2[(uint32_t)(comb >> (64 - L - 1 - o)) & mask2];
+                }
+                ssc[tid] = __half2float(p.scale1[n]);
             } else {
-                qids[tid] = -1;
+                for (int j = 0; j < R / 2; j++) dst[j] = 0u;
+                ssc[tid] = 0.f;
             }
         }
-        __syncthreads();
-        const int mt = (nq + 15) >> 4;
-        for (int i = tid; i < mt * 16 * (R * 2 / 16); i += NTHREADS) {
-            const int r = i >> 5, ch = i & 31;
-            const int q = qids[r];
-            uint4 v = make_uint4(0, 0, 0, 0);
-            if (q >= 0) v = reinterpret_cast<const uint4*>(p.Qh + (int64_t)q * R)[ch];
-            *reinterpret_cast<uint4*>(qt + r * RS + ch * 16) = v;
-        }
-        __syncthreads();
-        if (!warp_active) continue;
+        const int64_t wrow0 = row0 + 32 * warp;
+        const bool warp_active = wrow0 < ce;
+        const int blk_rel = (int)(wrow0 / 32 - cs / 32);
+        const int g = lane >> 2, t4 = lane & 3;
 
-        float acc[4][4][4];
-#pragma unroll
-        for (int m = 0; m < 4; m++)
-#pragma unroll
-            for (int j = 0; j < 4; j++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) acc[m][j][e] = 0.f;
-#pragma unroll 4
-        for (int kb = 0; kb < R * 2; kb += 32) {  // 16 fp16 = 32 bytes per k-step
-            uint32_t b[4][2];
-#pragma unroll
-            for (int jp = 0; jp < 2; jp++) {
-                const int nrow = 32 * warp + 16 * jp + (lane & 7) + ((lane >> 4) << 3);
-                ldsm_x4(b[2 * jp][0], b[2 * jp][1], b[2 * jp + 1][0], b[2 * jp + 1][1],
-                        vt + nrow * RS + kb + ((lane >> 3) & 1) * 16);
-            }
-#pragma unroll
-            for (int m = 0; m < 4; m++) {
-                if (m < mt) {
-                    uint32_t a[4];
-                    ldsm_x4(a[0], a[1], a[2], a[3], qt + (16 * m + (lane & 15)) * RS + kb + (lane >> 4) * 16);
-#pragma unroll
-                    for (int j = 0; j < 4; j++) mma_f16(acc[m][j], a, b[j][0], b[j][1]);
+        for (int qb = 0; qb < qn; qb += QT) {
+            const int nq = min(QT, qn - qb);
+            __syncthreads();
+            if (tid < QT) {
+                if (tid < nq) {
+                    const int pi = qoff + qb + tid;
+                    const int q = p.qid[pi];
+                    qids[tid] = q;
+                    qcs[tid] = p.qcp[pi];
+                    thr[tid] = MODE == 1 ? p.t0[q] : 0.f;
+                } else {
+                    qids[tid] = -1;
                 }
             }
-        }
-        float sr[4][2];
-        bool rv[4][2];
-#pragma unroll
-        for (int j = 0; j < 4; j++)
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int r = 32 * warp + 8 * j + 2 * t4 + e;
-                const int64_t n = row0 + r;
-                rv[j][e] = n >= cs && n < ce;
-                sr[j][e] = ssc[r];
+            __syncthreads();
+            const int mt = (nq + 15) >> 4;
+            for (int i = tid; i < mt * 16 * (R * 2 / 16); i += NTHREADS) {
+                const int r = i >> 5, ch = i & 31;
+                const int q = qids[r];
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (q >= 0) v = reinterpret_cast<const uint4*>(p.Qh + (int64_t)q * R)[ch];
+                *reinterpret_cast<uint4*>(qt + r * RS + ch * 16) = v;
             }
+            __syncthreads();
+            if (!warp_active) continue;
+
+            float acc[4][4][4];
 #pragma unroll
-        for (int m = 0; m < 4; m++) {
-            if (m >= mt) break;
-#pragma unroll
-            for (int h = 0; h < 2; h++) {
-                const int ql = 16 * m + g + 8 * h;
-                const bool qv = ql < nq;
-                const float qcv = qv ? qcs[ql] : 0.f;
-                float est[4][2];
+            for (int m = 0; m < 4; m++)
 #pragma unroll
                 for (int j = 0; j < 4; j++)
 #pragma unroll
-                    for (int e = 0; e < 2; e++) est[j][e] = __fadd_rn(__fmul_rn(sr[j][e], acc[m][j][2 * h + e]), qcv);
-                if (MODE == 0) {
-                    float mx = -INFINITY;
+                    for (int e = 0; e < 4; e++) acc[m][j][e] = 0.f;
+#pragma unroll 4
+            for (int kb = 0; kb < R * 2; kb += 32) {  // 16 fp16 = 32 bytes per k-step
+                uint32_t b[4][2];
+#pragma unroll
+                for (int jp = 0; jp < 2; jp++) {
+                    const int nrow = 32 * warp + 16 * jp + (lane & 7) + ((lane >> 4) << 3);
+                    ldsm_x4(b[2 * jp][0], b[2 * jp][1], b[2 * jp + 1][0], b[2 * jp + 1][1],
+                            vt + nrow * RS + kb + ((lane >> 3) & 1) * 16);
+                }
+#pragma unroll
+                for (int m = 0; m < 4; m++) {
+                    if (m < mt) {
+                        uint32_t a[4];
+                        ldsm_x4(a[0], a[1], a[2], a[3], qt + (16 * m + (lane & 15)) * RS + kb + (lane >> 4) * 16);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) mma_f16(acc[m][j], a, b[j][0], b[j][1]);
+                    }
+                }
+            }
+            float sr[4][2];
+            bool rv[4][2];
+#pragma unroll
+            for (int j = 0; j < 4; j++)
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int r = 32 * warp + 8 * j + 2 * t4 + e;
+                    const int64_t n = row0 + r;
+                    rv[j][e] = n >= cs && n < ce;
+                    sr[j][e] = ssc[r];
+                }
+#pragma unroll
+            for (int m = 0; m < 4; m++) {
+                if (m >= mt) break;
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const int ql = 16 * m + g + 8 * h;
+                    const bool qv = ql < nq;
+                    const float qcv = qv ? qcs[ql] : 0.f;
+                    float est[4][2];
 #pragma unroll
                     for (int j = 0; j < 4; j++)
 #pragma unroll
-                        for (int e = 0; e < 2; e++)
-                            if (rv[j][e]) mx = fmaxf(mx, est[j][e]);
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                    if (qv && t4 == 0) p.bmc[(int64_t)(qoff + qb + ql) * p.MB + blk_rel] = mx;
-                } else {
-                    const float th = qv ? thr[ql] : INFINITY;
-                    unsigned kmask = 0;
-#pragma unroll
-                    for (int j = 0; j < 4; j++)
-#pragma unroll
-                        for (int e = 0; e < 2; e++)
-                            if (qv && rv[j][e] && est[j][e] >= th) kmask |= 1u << (2 * j + e);
-                    if (__any_sync(0xffffffffu, kmask != 0)) {
-                        const int s = __popc(kmask);
-                        int incl = s;
-                        int v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
-                        if (t4 >= 1) incl += v;
-                        v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
-                        if (t4 >= 2) incl += v;
-                        const int total = __shfl_sync(0xffffffffu, incl, 3, 4);
-                        int base = 0;
-                        const int q = qv ? qids[ql] : 0;
-                        if (t4 == 0 && total > 0) base = atomicAdd(p.cnt + q, total);
-                        base = __shfl_sync(0xffffffffu, base, 0, 4) + incl - s;
+                        for (int e = 0; e < 2; e++) est[j][e] = __fadd_rn(__fmul_rn(sr[j][e], acc[m][j][2 * h + e]), qcv);
+                    if (MODE != 1) {
+                        float mx = -INFINITY;
 #pragma unroll
                         for (int j = 0; j < 4; j++)
 #pragma unroll
                             for (int e = 0; e < 2; e++)
-                                if (kmask & (1u << (2 * j + e))) {
-                                    if (base < p.M) {
-                                        const int64_t o = (int64_t)q * p.M + base;
-                                        p.bval[o] = est[j][e];
-                                        p.bpos[o] = (int32_t)(row0 + 32 * warp + 8 * j + 2 * t4 + e);
+                                if (rv[j][e]) mx = fmaxf(mx, est[j][e]);
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                        if (qv && t4 == 0) {
+                            if (MODE == 0)
+                                p.bmc[(int64_t)(qoff + qb + ql) * p.MB + blk_rel] = mx;
+                            else  // small-batch rule: global block maxima; MB holds the blocks per query row
+                                atomic_max_float(p.bmc + (int64_t)qids[ql] * p.MB + wrow0 / 32, mx);
+                        }
+                    } else {
+                        const float th = qv ? thr[ql] : INFINITY;
+                        unsigned kmask = 0;
+#pragma unroll
+                        for (int j = 0; j < 4; j++)
+#pragma unroll
+                            for (int e = 0; e < 2; e++)
+                                if (qv && rv[j][e] && est[j][e] >= th) kmask |= 1u << (2 * j + e);
+                        if (__any_sync(0xffffffffu, kmask != 0)) {
+                            const int s = __popc(kmask);
+                            int incl = s;
+                            int v = __shfl_up_sync(0xffffffffu, incl, 1, 4);
+                            if (t4 >= 1) incl += v;
+                            v = __shfl_up_sync(0xffffffffu, incl, 2, 4);
+                            if (t4 >= 2) incl += v;
+                            const int total = __shfl_sync(0xffffffffu, incl, 3, 4);
+                            int base = 0;
+                            const int q = qv ? qids[ql] : 0;
+                            if (t4 == 0 && total > 0) base = atomicAdd(p.cnt + q, total);
+                            base = __shfl_sync(0xffffffffu, base, 0, 4) + incl - s;
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+#pragma unroll
+                                for (int e = 0; e < 2; e++)
+                                    if (kmask & (1u << (2 * j + e))) {
+                                        if (base < p.M) {
+                                            const int64_t o = (int64_t)q * p.M + base;
+                                            p.bval[o] = est[j][e];
+                                            p.bpos[o] = (int32_t)(row0 + 32 * warp + 8 * j + 2 * t4 + e);
+                                        }
+                                        base++;
                                     }
-                                    base++;
-                                }
+                        }
                     }
                 }
+            }
+        }
+        __syncthreads();  // every warp is done with this tile's shared memory before the next decode
+    }
+}
+
+constexpr size_t smem_bytes(int L) {
+    return (size_t)TILE_ROWS * RS + (size_t)QT * RS + ((size_t)2 << L) * 4 + TILE_ROWS * 4 + QT * 4 * 3;
+}
+
+}  // namespace trellis
+
+// ------------------------------------------------------------------------------------------------ small batches
+// `_small_scan` (`src/s1small_cell.py:7-28`) for B <= 8: est = (sum_j tab[state_j] * q'[j]) * scale1[n] + qcp with
+// fp32 table values and the fp32 query projection q' = Q @ W1 (no fp16 rounding, no tensor core), work taken straight
+// from the probe list like fvs_i8_scan_small: one CTA per (query, probe column, 4 blocks), a warp per 32-row block,
+// lane = row (its words in registers, the query and the table in shared memory); mode 0 merges the block maximum into
+// bm[q * NBg + global block] with an atomic max (as the reference's `tl.atomic_max` into bm [B, NB]: a block shared by
+// two adjacent first-pass cells holds one value), mode 1 emits est >= t0[q].
+namespace tsmall {
+constexpr int WARPS = 4;
+constexpr int R = 256;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(32 * tsmall::WARPS) trellis_small_kernel(
+    const float* __restrict__ Qr, const int64_t* __restrict__ probe, int nprobe, int ncols,
+    const __half* __restrict__ QM, int NC, const int64_t* __restrict__ off, const uint32_t* __restrict__ words, int W,
+    const float* __restrict__ tab, int L, const __half* __restrict__ scale1, const float* __restrict__ t0,
+    int32_t* __restrict__ cnt, float* __restrict__ bval, int32_t* __restrict__ bpos, int M, float* __restrict__ bm,
+    int NBg, int groups) {
+    using namespace tsmall;
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* qv = reinterpret_cast<float*>(smem);  // R
+    float* tb = qv + R;                           // 2^L
+    const int pair = blockIdx.x / groups, grp = blockIdx.x - pair * groups;
+    const int q = pair / ncols, j = pair - q * ncols;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int c = (int)probe[(int64_t)q * nprobe + j];
+    const int64_t cs = off[c], ce = off[c + 1];
+    if (ce <= cs) return;  // uniform over the CTA
+    const int64_t b0 = cs / 32, nb = (ce - 1) / 32 - b0 + 1;
+    if ((int64_t)grp * WARPS >= nb) return;  // uniform over the CTA
+    for (int i = threadIdx.x; i < R; i += blockDim.x) qv[i] = Qr[(int64_t)q * R + i];
+    for (int i = threadIdx.x; i < (1 << L); i += blockDim.x) tb[i] = tab[i];
+    __syncthreads();
+    const int64_t blk = b0 + (int64_t)grp * WARPS + warp;
+    if (blk - b0 >= nb) return;
+    const float qcp = __half2float(QM[(int64_t)q * NC + c]);
+    const int64_t n = blk * 32 + lane;
+    const bool valid = n >= cs && n < ce;
+    float est = -INFINITY;
+    if (valid) {
+        uint32_t w[R / 32 + 1];
+#pragma unroll
+        for (int i = 0; i <= R / 32; i++) w[i] = i < W ? words[n * W + i] : 0u;
+        const uint32_t mask = (1u << L) - 1u;
+        float acc = 0.f;
+#pragma unroll
+        for (int wi = 0; wi < R / 32; wi++) {
+            const unsigned long long comb = ((unsigned long long)w[wi] << 32) | w[wi + 1];
+#pragma unroll
+            for (int o = 0; o < 32; o++)
+                acc = __fmaf_rn(tb[(uint32_t)(comb >> (64 - L - o)) & mask], qv[wi * 32 + o], acc);
+        }
+        est = __fadd_rn(__fmul_rn(acc, __half2float(scale1[n])), qcp);
+    }
+    if (MODE == 0) {
+        float mx = est;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomic_max_float(bm + (int64_t)q * NBg + blk, mx);
+    } else {
+        const bool keep = valid && est >= t0[q];
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        if (m) {
+            int base = 0;
+            if (lane == 0) base = atomicAdd(cnt + q, __popc(m));
+            base = __shfl_sync(0xffffffffu, base, 0) + __popc(m & ((1u << lane) - 1u));
+            if (keep && base < M) {
+                bval[(int64_t)q * M + base] = est;
+                bpos[(int64_t)q * M + base] = (int32_t)n;
             }
         }
     }
 }
 
-constexpr size_t smem_bytes(int L) {
-    return (size_t)TILE_ROWS * RS + (size_t)QT * RS + ((size_t)1 << L) * 4 + TILE_ROWS * 4 + QT * 4 * 3;
-}
-
-}  // namespace trellis
-
 // ------------------------------------------------------------------------------------------------ tiered gather
 // est = qc + sum_t scale_t <q_t, cb_t[code]>, var = sum_t ||q_t||^2 sig_t^2 (`src/tiered_fused.py:8-41`); code of
 // coordinate 8j+k of tier t = sum_p bit(7-k) of byte j of plane p << (b-1-p).  One CTA per query holds the rotated
-// query (D floats) and every tier's codebook in shared memory; each warp scores one candidate at a time, lane l owning
-// byte positions l, l+32, ... of the candidate (all planes of a position are loaded together), folding scale_t into its
-// partial sum so that a candidate needs one reduction for the estimate and one for the variance.
+// query and every tier's codebook in shared memory; the query is stored interleaved by coordinate-within-byte
+// (zqk[s_t + k*kb_t + j] = Zq[s_t + 8j + k], the reference's qk[8, B, KB] layout) so that lanes over consecutive byte
+// positions j read consecutive words.  Each warp scores one candidate at a time, lane l owning byte positions l,
+// l+32, ... of the candidate over all tiers; the bytes of all b planes of a position are loaded together, then decoded;
+// scale_t is folded into the partial sums so that a candidate needs one reduction for the estimate and one for the
+// variance.
 constexpr int TG_MAXT = 8;
 struct TieredSet {
     int T, nbytes;  // nbytes: byte positions per candidate over all tiers = D / 8
@@ -253,6 +345,30 @@ struct TieredSet {
     const uint8_t* planes[TG_MAXT];
     const float* cb[TG_MAXT];
 };
+
+// codes of the 8 coordinates of one byte position from NB bit planes, as 8 bytes (lo: coordinates 0-3, hi: 4-7):
+// a nibble's 4 bits are spread into 4 bytes by one multiply (n * 0x00204081 places bit i at bit 8i, the partial
+// products do not overlap) and put in coordinate order by a byte permute; planes are combined MSB-first by
+// shift-or (codes < 2^NB <= 256 never carry into the next byte)
+template <int NB>
+__device__ __forceinline__ float tier_pos_dot(const uint8_t* __restrict__ pb, int64_t pstride,
+                                              const float* __restrict__ cbt, const float* __restrict__ z, int kb) {
+    uint32_t by[NB];
+#pragma unroll
+    for (int pl = 0; pl < NB; pl++) by[pl] = __ldg(pb + pl * pstride);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int pl = 0; pl < NB; pl++) {
+        lo = (lo << 1) | __byte_perm(((by[pl] >> 4) * 0x00204081u) & 0x01010101u, 0, 0x0123);
+        hi = (hi << 1) | __byte_perm(((by[pl] & 15u) * 0x00204081u) & 0x01010101u, 0, 0x0123);
+    }
+    float a = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; k++) a += cbt[(lo >> (8 * k)) & 255u] * z[k * kb];
+#pragma unroll
+    for (int k = 0; k < 4; k++) a += cbt[(hi >> (8 * k)) & 255u] * z[(k + 4) * kb];
+    return a;
+}
 
 __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __restrict__ pos, int B, int K,
                                                           const float* __restrict__ qc, const float* __restrict__ Zq,
@@ -262,16 +378,38 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_qn2[TG_MAXT];
     __shared__ float s_scl[8][TG_MAXT];  // per warp: this candidate's scale of every tier
-    float* zq = reinterpret_cast<float*>(smem);  // D
-    float* cbs = zq + D;                         // sum_t 2^b_t
+    __shared__ const uint8_t* s_planes[TG_MAXT];
+    __shared__ int s_s[TG_MAXT], s_kb[TG_MAXT], s_bits[TG_MAXT], s_cbo[TG_MAXT], s_pbase[TG_MAXT];
+    float* zqk = reinterpret_cast<float*>(smem);  // D, interleaved per tier
+    float* cbs = zqk + D;                         // sum_t 2^b_t
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
-    for (int i = tid; i < D; i += blockDim.x) zq[i] = Zq[(int64_t)q * ldz + i];
+    if (tid < ts.T) {
+        s_planes[tid] = ts.planes[tid];
+        s_s[tid] = ts.s[tid];
+        s_kb[tid] = ts.kb[tid];
+        s_bits[tid] = ts.bits[tid];
+        s_cbo[tid] = ts.cboff[tid];
+        s_pbase[tid] = ts.pbase[tid];
+    }
+    __syncthreads();
+    uint8_t* ptier = reinterpret_cast<uint8_t*>(cbs + ts.cboff[ts.T - 1] + (1 << ts.bits[ts.T - 1]));  // nbytes
+    for (int i = tid; i < D; i += blockDim.x) {
+        int t = 0;
+        while (t + 1 < ts.T && i >= s_s[t + 1]) t++;
+        const int loc = i - s_s[t];
+        if (loc < 8 * s_kb[t]) zqk[s_s[t] + (loc & 7) * s_kb[t] + (loc >> 3)] = Zq[(int64_t)q * ldz + i];
+    }
     for (int t = 0; t < ts.T; t++)
-        for (int i = tid; i < (1 << ts.bits[t]); i += blockDim.x) cbs[ts.cboff[t] + i] = ts.cb[t][i];
+        for (int i = tid; i < (1 << s_bits[t]); i += blockDim.x) cbs[s_cbo[t] + i] = ts.cb[t][i];
+    for (int gp = tid; gp < ts.nbytes; gp += blockDim.x) {
+        int t = 0;
+        while (t + 1 < ts.T && gp >= s_pbase[t + 1]) t++;
+        ptier[gp] = (uint8_t)t;
+    }
     __syncthreads();
     if (warp < ts.T) {
         float a = 0.f;
-        for (int i = ts.s[warp] + lane; i < ts.s[warp] + 8 * ts.kb[warp]; i += 32) a += zq[i] * zq[i];
+        for (int i = s_s[warp] + lane; i < s_s[warp] + 8 * s_kb[warp]; i += 32) a += zqk[i] * zqk[i];
         a = warp_sum(a);
         if (lane == 0) s_qn2[warp] = a;
     }
@@ -287,20 +425,23 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
         __syncwarp();
         float part = 0.f;
         for (int gp = lane; gp < ts.nbytes; gp += 32) {
-            int t = 0;
-            while (t + 1 < ts.T && gp >= ts.pbase[t + 1]) t++;
-            const int j = gp - ts.pbase[t], b = ts.bits[t], kb = ts.kb[t];
-            uint32_t code[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            for (int pl = 0; pl < b; pl++) {
-                const uint32_t byt = __ldg(ts.planes[t] + ((int64_t)pl * N + n) * kb + j);
-#pragma unroll
-                for (int k = 0; k < 8; k++) code[k] |= ((byt >> (7 - k)) & 1u) << (b - 1 - pl);
+            const int t = ptier[gp];
+            const int j = gp - s_pbase[t], b = s_bits[t], kb = s_kb[t];
+            const uint8_t* pb = s_planes[t] + n * kb + j;
+            const int64_t pstride = N * kb;
+            const float* cbt = cbs + s_cbo[t];
+            const float* z = zqk + s_s[t] + j;
+            float a;
+            switch (b) {
+                case 1: a = tier_pos_dot<1>(pb, pstride, cbt, z, kb); break;
+                case 2: a = tier_pos_dot<2>(pb, pstride, cbt, z, kb); break;
+                case 3: a = tier_pos_dot<3>(pb, pstride, cbt, z, kb); break;
+                case 4: a = tier_pos_dot<4>(pb, pstride, cbt, z, kb); break;
+                case 5: a = tier_pos_dot<5>(pb, pstride, cbt, z, kb); break;
+                case 6: a = tier_pos_dot<6>(pb, pstride, cbt, z, kb); break;
+                case 7: a = tier_pos_dot<7>(pb, pstride, cbt, z, kb); break;
+                default: a = tier_pos_dot<8>(pb, pstride, cbt, z, kb); break;
             }
-            const float* cbt = cbs + ts.cboff[t];
-            const float* z = zq + ts.s[t] + 8 * j;
-            float a = 0.f;
-#pragma unroll
-            for (int k = 0; k < 8; k++) a += cbt[code[k]] * z[k];
             part += a * s_scl[warp][t];
         }
         __syncwarp();
@@ -425,23 +566,60 @@ extern "C" int fvs_trellis_scan(fvs_stream_t stream, int mode, const uint16_t* Q
                                 int W, const float* tab, int L, const uint16_t* scale1, const float* t0, int32_t* cnt,
                                 float* bval, int32_t* bpos, int M, float* bmc, int MB) {
     using namespace fvs::trellis;
-    FVS_CHECK_ARG(mode == 0 || mode == 1);
+    FVS_CHECK_ARG(mode == 0 || mode == 1 || mode == 2);
     FVS_CHECK_ARG(R == fvs::trellis::R && B >= 0 && ntiles >= 0 && NC > 0 && L >= 2 && L <= 12);
     FVS_CHECK_ARG(W >= (R + L - 1 + 31) / 32 && W <= MAXW);
     FVS_CHECK_ARG(Qh && qid && coff && ccnt && qcp && tile_cell && tile_row0 && off && words && tab && scale1);
-    if (mode == 0) FVS_CHECK_ARG(bmc && MB > 0);
+    if (mode != 1) FVS_CHECK_ARG(bmc && MB > 0);
     if (mode == 1) FVS_CHECK_ARG(t0 && cnt && bval && bpos && M > 0);
     if (ntiles == 0 || B == 0) return FVS_OK;
     Params p{(const __half*)Qh, qid, coff, ccnt, qcp, tile_cell, tile_row0, off, (const uint32_t*)words, tab,
-             (const __half*)scale1, t0, cnt, bval, bpos, bmc, W, L, M, MB};
+             (const __half*)scale1, t0, cnt, bval, bpos, bmc, W, L, M, MB, ntiles};
     const size_t sm = smem_bytes(L);
-    cudaError_t e = mode ? fvs_ensure_smem((const void*)trellis_scan_kernel<1>, sm)
-                         : fvs_ensure_smem((const void*)trellis_scan_kernel<0>, sm);
+    const void* fn = mode == 0 ? (const void*)trellis_scan_kernel<0>
+                               : mode == 1 ? (const void*)trellis_scan_kernel<1> : (const void*)trellis_scan_kernel<2>;
+    cudaError_t e = fvs_ensure_smem(fn, sm);
+    if (e != cudaSuccess) return (int)e;
+    // one CTA per tile (a persistent walk measured slower: the per-tile phases do not overlap within a CTA, so
+    // more resident CTAs hide more latency)
+    const int grid = ntiles;
+    if (mode == 0)
+        trellis_scan_kernel<0><<<grid, NTHREADS, sm, stream>>>(p);
+    else if (mode == 1)
+        trellis_scan_kernel<1><<<grid, NTHREADS, sm, stream>>>(p);
+    else
+        trellis_scan_kernel<2><<<grid, NTHREADS, sm, stream>>>(p);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_trellis_scan_small(fvs_stream_t stream, int mode, const float* Qr, int B, int R,
+                                      const int64_t* probe, int nprobe, int ncols, const uint16_t* QM, int NC,
+                                      const int64_t* off, const int32_t* words, int W, const float* tab, int L,
+                                      const uint16_t* scale1, const float* t0, int32_t* cnt, float* bval,
+                                      int32_t* bpos, int M, float* bm, int NBg, int MB) {
+    using namespace fvs::tsmall;
+    FVS_CHECK_ARG(mode == 0 || mode == 1);
+    FVS_CHECK_ARG(R == fvs::tsmall::R && B >= 0 && nprobe >= 1 && ncols >= 1 && ncols <= nprobe && NC > 0 && MB > 0);
+    FVS_CHECK_ARG(L >= 2 && L <= 12 && W >= (R + L - 1 + 31) / 32 && W <= 16);
+    FVS_CHECK_ARG(Qr && probe && QM && off && words && tab && scale1);
+    if (mode == 0) FVS_CHECK_ARG(bm && NBg > 0);
+    if (mode == 1) FVS_CHECK_ARG(t0 && cnt && bval && bpos && M > 0);
+    if (B == 0) return FVS_OK;
+    const int groups = (MB + WARPS - 1) / WARPS;
+    const int64_t grid = (int64_t)B * ncols * groups;
+    if (grid > INT32_MAX) return FVS_ERANGE;
+    const size_t sm = (size_t)(R + (1 << L)) * 4;
+    cudaError_t e = mode ? fvs_ensure_smem((const void*)fvs::trellis_small_kernel<1>, sm)
+                         : fvs_ensure_smem((const void*)fvs::trellis_small_kernel<0>, sm);
     if (e != cudaSuccess) return (int)e;
     if (mode == 0)
-        trellis_scan_kernel<0><<<ntiles, NTHREADS, sm, stream>>>(p);
+        fvs::trellis_small_kernel<0><<<(unsigned)grid, 32 * WARPS, sm, stream>>>(
+            Qr, probe, nprobe, ncols, (const __half*)QM, NC, off, (const uint32_t*)words, W, tab, L,
+            (const __half*)scale1, t0, cnt, bval, bpos, M, bm, NBg, groups);
     else
-        trellis_scan_kernel<1><<<ntiles, NTHREADS, sm, stream>>>(p);
+        fvs::trellis_small_kernel<1><<<(unsigned)grid, 32 * WARPS, sm, stream>>>(
+            Qr, probe, nprobe, ncols, (const __half*)QM, NC, off, (const uint32_t*)words, W, tab, L,
+            (const __half*)scale1, t0, cnt, bval, bpos, M, bm, NBg, groups);
     return fvs_launch_status();
 }
 
@@ -471,7 +649,7 @@ extern "C" int fvs_tiered_score(fvs_stream_t stream, const int64_t* pos, int B, 
     }
     ts.pbase[T] = pb;
     ts.nbytes = pb;
-    const size_t sm = (size_t)(D + cbo) * 4;
+    const size_t sm = (size_t)(D + cbo) * 4 + (size_t)((pb + 15) & ~15);
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     cudaError_t e = fvs_ensure_smem((const void*)fvs::tiered_score_kernel, sm);  // 256 threads = 8 warps (s_scl)

@@ -76,6 +76,7 @@ class EngineB200S(EngineB200I8):
     flagged-row recompute are inherited from EngineB200I8."""
     M = None
     FB_M = 65536
+    TINY, SMALL, CAP_SMALL = 8, 32, 8192      # `EngineC.TINY/SMALL`, `search_small`/`search_mask` CAP
 
     def __init__(self, index: IndexS):
         super().__init__(index)
@@ -90,11 +91,12 @@ class EngineB200S(EngineB200I8):
                    ptr(probe))
         return QM, probe
 
-    def _scan(self, mode, name, Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc):
+    def _scan(self, mode, name, Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc, mb=None):
         ix = self.ix
         self._call(name, self.L.fvs_trellis_scan, mode, ptr(Qh), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
                    ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.words), ix.W,
-                   ptr(ix.tab), ix.L, ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB)
+                   ptr(ix.tab), ix.L, ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc),
+                   mb or ix.MB)
 
     def stage1_trellis(self, Qb, QM, probe, K, rho_override=None, M_override=None, Qh=None):
         """`s1cell.search_static` (`src/s1cell.py:176-195`) on the C library: returns pos [B,K] int64, ok [B] bool,
@@ -131,6 +133,52 @@ class EngineB200S(EngineB200I8):
                           bpos=bpos, slot=slot)
         return pos, ok.bool(), est1
 
+    def stage1_small(self, Qb, QM, probe, K):
+        """`EngineC._gpu` stage 1 for B <= 32 (`src/engine_cell.py:49-56`): `search_small` (B <= 8: fp32 estimate,
+        streaming kernel straight from the probe list) or `search_mask` (fp16 tensor-core estimate through the pair
+        lists); (beta, rho) = (1.1, 0.75), an 8192-entry buffer, first-pass maxima merged per global 32-row block and
+        t0 = the r-th largest of them (`src/s1small_cell.py:38, 70`)."""
+        ix, L = self.ix, self.L
+        B = Qb.shape[0]
+        dev = Qb.device
+        beta, rho = 1.1, 0.75
+        M = self.CAP_SMALL
+        nprobe = probe.shape[1]
+        n1 = min(max(int(np.ceil(beta * K / (ix.N / ix.NC / BN + 1))), 1), nprobe)
+        r = int(np.ceil(rho * K))
+        NBg = (ix.N + BN - 1) // BN
+        probe = probe.contiguous()
+        bm = torch.full((B, NBg), -1e30, device=dev)
+        cnt = torch.zeros(B, dtype=torch.int32, device=dev)
+        bval = torch.empty(B, M, device=dev)
+        bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
+        t0 = torch.empty(B, device=dev)
+        if B <= self.TINY:
+            Qr = (Qb @ ix.W1).contiguous()
+            common = lambda mode, ncols: (mode, ptr(Qr), B, ix.R, ptr(probe), nprobe, ncols, ptr(QM), ix.NC,
+                                          ptr(ix.off), ptr(ix.words), ix.W, ptr(ix.tab), ix.L, ptr(ix.scale1))
+            self._call("trellis_small_first", L.fvs_trellis_scan_small, *common(0, n1), None, None, None, None, 0,
+                       ptr(bm), NBg, ix.MB)
+            self._call("threshold", L.fvs_rth_largest, ptr(bm), B, NBg, NBg, r, ptr(t0))
+            self._call("trellis_small_emit", L.fvs_trellis_scan_small, *common(1, nprobe), ptr(t0), ptr(cnt),
+                       ptr(bval), ptr(bpos), M, None, NBg, ix.MB)
+            q_used = Qr
+        else:
+            Qh = (Qb @ ix.W1).half().contiguous()
+            qid, coff, ccnt, qcp, _ = self.pairs(probe, n1, QM, False)
+            self._scan(2, "trellis_scan_first", Qh, B, qid, coff, ccnt, qcp, None, None, None, None, 0, bm, mb=NBg)
+            self._call("threshold", L.fvs_rth_largest, ptr(bm), B, NBg, NBg, r, ptr(t0))
+            qid, coff, ccnt, qcp, _ = self.pairs(probe, nprobe, QM, False)
+            self._scan(1, "trellis_scan_emit", Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None)
+            q_used = Qh
+        pos = torch.empty(B, K, dtype=torch.int64, device=dev)
+        est1 = torch.empty(B, K, device=dev)
+        ok = torch.empty(B, dtype=torch.uint8, device=dev)
+        self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
+                   ptr(ok), None, 0.0, 9)
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bm=bm, Qq=q_used, bval=bval, bpos=bpos)
+        return pos, ok.bool(), est1
+
     def rotated_query(self, Qb):
         return (Qb @ self.ix.VP).contiguous()                              # `src/tiered_fused.py:57`
 
@@ -153,12 +201,15 @@ class EngineB200S(EngineB200I8):
         return I, reads.long(), ids
 
     def _gpu(self, Qb, K, z, nprobe, k):
-        """`EngineS._gpu` (`src/engine_cell.py:74-84`)."""
+        """`EngineS._gpu` (`src/engine_cell.py:74-84`), with `EngineC._gpu` for batches up to 32."""
         if K <= k:
             raise ValueError("need K > k")
         QC = (Qb @ self.ix.c).contiguous()
         QM, probe = self.route(Qb, nprobe)
-        pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K)
+        if len(Qb) <= self.SMALL:
+            pos, ok, est1 = self.stage1_small(Qb, QM, probe, K)
+        else:
+            pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K)
         self._last.update(probe=probe, QM=QM, QC=QC, est1=est1)
         I, reads, ids = self._finish_s(Qb, QC, pos, z, k)
         return ok, I, reads, ids

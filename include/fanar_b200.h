@@ -203,12 +203,26 @@ int fvs_i8_scan_small(fvs_stream_t stream, int mode, const int8_t* q8, const flo
  * fvs_i8_scan with the score est = scale1[n] * dot(Qh[q], v_n) + qcp, where v_n is row n's trellis code decoded as
  * `src/decode2.py:5-17` (words [N, W] uint32, bits MSB-first; value = tab[L-bit window], rounded to fp16) and
  * Qh [B, 256] = fp16(Q @ W1); fp16 products accumulated in fp32 on the tensor cores.  R = 256, W >= ceil((R+L-1)/32).
+ * mode 2 (the first pass of `search_mask`, `src/s1small_cell.py:44-71`, batches 9..32): block maxima merged into
+ * bmc[q * MB + global 32-row block] by atomic max, MB then being the blocks per query row (ceil(N / 32)).
  */
 int fvs_trellis_scan(fvs_stream_t stream, int mode, const uint16_t* Qh, int B, int R,
                      const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
                      const int32_t* tile_cell, const int32_t* tile_row0, int ntiles, const int64_t* off, int NC,
                      const int32_t* words, int W, const float* tab, int L, const uint16_t* scale1,
                      const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M, float* bmc, int MB);
+
+/*
+ * Default engine, stage 1 for B <= 8 (`src/s1small_cell.py:7-42`, `_small_scan` / `search_small`): est =
+ * (sum_j tab[state_j] * Qr[q, j]) * scale1[n] + float(QM[q, c]) in fp32 (Qr = Q @ W1 in fp32, table values not rounded
+ * to fp16), work taken straight from probe [B, nprobe] (columns 0..ncols-1): mode 0 merges the block maxima into
+ * bm[q * NBg + global 32-row block] with an atomic max (bm filled with -1e30 by the caller, NBg = ceil(N / 32); the
+ * reference's `tl.atomic_max` into bm [B, NB]), mode 1 appends est >= t0[q].  MB = ceil(largest cell / 32) + 1.
+ */
+int fvs_trellis_scan_small(fvs_stream_t stream, int mode, const float* Qr, int B, int R, const int64_t* probe,
+                           int nprobe, int ncols, const uint16_t* QM, int NC, const int64_t* off, const int32_t* words,
+                           int W, const float* tab, int L, const uint16_t* scale1, const float* t0, int32_t* cnt,
+                           float* bval, int32_t* bpos, int M, float* bm, int NBg, int MB);
 
 /*
  * Default engine, stage 2 (`src/tiered_fused.py:8-41, 54-72`): est = qc[q] + sum_t scale[t*N+n] * sum_x

@@ -1,8 +1,9 @@
 """Golden vectors of the default engine's query path (trellis stage 1 + tiered stage 2) from the reference itself.
 
 Runs the reference's real `engine_cell.EngineS._gpu` (batch > 32: `s1cell.search_static` with `_first_compact_s` /
-`_emit_loop_s` and the `decode2._decode_tile2` decoder, then `tiered_fused.score`, classification, stage 3) on CPU
-tensors under the Triton interpreter.  Stand-ins: `engine3` (base class Engine8 with the reference's `_score` and a
+`_emit_loop_s` and the `decode2._decode_tile2` decoder, then `tiered_fused.score`, classification, stage 3; batch <= 8:
+`s1small_cell.search_small`; 8 < batch <= 32: `s1small_cell.search_mask`) on CPU tensors under the Triton
+interpreter.  Stand-ins: `engine3` (base class Engine8 with the reference's `_score` and a
 stage-3 hook calling `stage3_zc._stage3`; `rf.L = 10`), `tiered` (only its codebook table `CB`, filled with this
 repository's Lloyd-Max levels since faiss is absent), `civf8`; `tiered_fused._HP` (a host-pointer wrapper for
 zero-copy reads of pinned memory) becomes the identity.  The trellis code itself is produced with the
@@ -171,6 +172,33 @@ def main():
     f.update(k_pos=t(a[0]), k_QC=t(a[1]), k_est=t(a[2]), k_sd=t(a[3]), k_qn2=t(a[6]))
     a = mods["s3"].calls[0][0]      # (H, ids, amb, Q, score, KC)
     f.update(k_ids=t(a[1]), k_amb=t(a[2]), k_score=t(a[4]))
+    # small batches (`EngineC._gpu`, `src/engine_cell.py:49-60`): B <= 8 takes `search_small` (fp32 dot), 8 < B <= 32
+    # `search_mask` (fp16 tensor-core dot), both with an 8192-entry buffer and (beta, rho) = (1.1, 0.75)
+    sm = mods["s1small_cell"]
+    for tag, rows, kern in (("s6_", slice(0, 6), "_small_scan"), ("m20_", slice(6, 26), "_mask_scan")):
+        rec = Rec(getattr(sm, kern))
+        setattr(sm, kern, rec)
+        mods["s3"].calls.clear()
+        Qs = Q[rows].contiguous()
+        with torch.no_grad():
+            ok, I, nr, ids = E._gpu(Qs, K, z, nprobe, k)
+        setattr(sm, kern, rec.kern)
+        a0, a1 = rec.calls[0][0], rec.calls[1][0]
+        if kern == "_small_scan":   # (q, probe, off, words, tab, scale, qc, t0, cnt, bval, bpos, bm, NPR, NP_USE, CAP, NB)
+            bm, t0, cnt, bval, bpos, CAP = a0[11], a1[7], a1[8], a1[9], a1[10], int(a1[14])
+            f[tag + "probe"] = t(a1[1])
+        else:                       # (q, pm, off, words, tab, scale, qc, t0, cnt, bval, bpos, bm, B, NC, CAP, NB, LEVEL)
+            bm, t0, cnt, bval, bpos, CAP = a0[11], a1[7], a1[8], a1[9], a1[10], int(a1[14])
+            f[tag + "pm"] = t(a1[1])
+        cntv = t(cnt)
+        used = np.minimum(cntv, CAP)
+        f.update({tag + "Q": t(Qs), tag + "bm": t(bm), tag + "t0": t(t0), tag + "cnt": cntv, tag + "CAP": np.asarray(CAP),
+                  tag + "emit_q": np.repeat(np.arange(len(cntv)), used).astype(np.int32),
+                  tag + "emit_val": np.concatenate([t(bval)[i, :used[i]] for i in range(len(cntv))]).astype(np.float32),
+                  tag + "emit_pos": np.concatenate([t(bpos)[i, :used[i]] for i in range(len(cntv))]).astype(np.int32),
+                  tag + "out_ok": t(ok), tag + "out_I": t(I), tag + "out_reads": t(nr), tag + "out_ids": t(ids),
+                  tag + "ids": t(mods["s3"].calls[0][0][1]), tag + "score": t(mods["s3"].calls[0][0][4])})
+        print(tag, "ok", int(t(ok).sum()), "/", len(Qs), "cnt", cntv.min(), cntv.max())
     path = os.path.join(args.out, "trellis_reference.npz")
     np.savez_compressed(path, **f)
     print("wrote", path, os.path.getsize(path), "bytes; ok", int(t(ok).sum()), "/", len(Q))

@@ -126,3 +126,27 @@ def test_trellis_encoder_matches_reference_words(gt):
     words = O.paths_to_words(path, 10)
     same = (words == f["words"][rows.numpy()]).all(1)
     assert same.all(), same.mean()
+
+
+@pytest.mark.parametrize("tag", ["s6_", "m20_"])
+def test_small_batch_paths_match_reference(gt, tag):
+    """B <= 8 (`search_small`, fp32 estimate) and 8 < B <= 32 (`search_mask`, fp16 tensor-core estimate): threshold,
+    emitted sets, exactness flags and final ids as the reference's `EngineC._gpu`."""
+    f = gt
+    idx = tindex(f)
+    K, nprobe, k = (int(v) for v in f["params"])
+    Q = f[tag + "Q"]
+    QM = (Q.astype(np.float16).astype(np.float32) @ f["means16"].astype(np.float32).T).astype(np.float16)
+    probe = torch.from_numpy(QM.astype(np.float32) * f["inv_mnorm"]).topk(nprobe, 1).indices.numpy()
+    out = O.search_trellis(idx, Q, K, float(f["z"]), nprobe, k, QM=QM, probe=probe)
+    np.testing.assert_allclose(out["t0"], f[tag + "t0"], rtol=TOL, atol=TOL)
+    np.testing.assert_array_equal(out["ok"], f[tag + "out_ok"])
+    eq, ev, ep = f[tag + "emit_q"], f[tag + "emit_val"], f[tag + "emit_pos"]
+    for q in range(len(Q)):
+        sel = eq == q
+        tq = f[tag + "t0"][q]
+        far = lambda v: np.abs(v - tq) > TOL * (1 + abs(tq))
+        np.testing.assert_array_equal(np.sort(ep[sel][far(ev[sel])]), np.sort(out["pos_l"][q][far(out["est_l"][q])]))
+    same = out["reads"] == f[tag + "out_reads"]
+    assert same.mean() >= 0.8
+    np.testing.assert_array_equal(out["I"][same], f[tag + "out_I"][same])
