@@ -10,9 +10,12 @@
 //   warp 0      : TMA loads of the 128 x 256 B code tiles (two 128 B-wide boxes, 128 B swizzle), A_STAGES ahead
 //   warp 1      : TMEM allocation; lane 0 issues tcgen05.mma.kind::i8 (M=128 rows, N=16..64 queries, K=32 x 8) per
 //                 sub-tile into one of T_STAGES accumulators, and releases a code tile when its last MMA completes
+//                 and a query tile as soon as its own MMAs complete
 //   warps 2-7   : gather: warp 2+g fills the sub-tiles nb = g (mod 6) -- the rows of q8 picked by qid, in the
-//                 canonical K-major 128 B-swizzled layout, plus scale / pair constant / threshold -- so six
-//                 sub-tiles' dependent loads are in flight at once
+//                 canonical K-major 128 B-swizzled layout, into query-tile stage g, and the sub-tile's scales / pair
+//                 constants / thresholds / row scales into the metadata slot of its accumulator stage (nb mod
+//                 T_STAGES, freed by the epilogue together with the accumulator) -- so six sub-tiles' dependent
+//                 loads are in flight at once and a query tile is not held through the epilogue
 //   warps 8-23  : four epilogue warpgroups, group e on the sub-tiles nb = e (mod 4): tcgen05.ld of the warp's 32 TMEM
 //                 lanes (= code rows) 32 columns (queries) at a time, est = ((acc * qs) * zs) + qcp in fp32 with
 //                 explicit rounding, then first pass: per-query block maximum by one redux.sync.max, or emit:
@@ -29,11 +32,20 @@ namespace fvs {
 namespace tc {
 using namespace fvs::tcg;
 
+#ifndef FVS_TC_A_STAGES
+#define FVS_TC_A_STAGES 3
+#endif
+#ifndef FVS_TC_GATHER_WARPS
+#define FVS_TC_GATHER_WARPS 6
+#endif
+#ifndef FVS_TC_MAXT
+#define FVS_TC_MAXT 512
+#endif
 constexpr int TILE_ROWS = 128;
 constexpr int QN = 64;  // queries per sub-tile
 constexpr int RB = 256;
-constexpr int A_STAGES = 3;
-constexpr int GATHER_WARPS = 6;
+constexpr int A_STAGES = FVS_TC_A_STAGES;
+constexpr int GATHER_WARPS = FVS_TC_GATHER_WARPS;
 constexpr int B_STAGES = GATHER_WARPS;  // gather warp g owns B stage g
 constexpr int T_STAGES = 8;
 constexpr int EPI_GROUPS = 4;
@@ -45,15 +57,16 @@ constexpr int A_BYTES = 2 * TILE_ROWS * 128;               // one code tile: 2 K
 constexpr int B_BYTES = 2 * QN * 128;                      // one query sub-tile: 2 K-halves x 8 KB
 constexpr int A_OFF = 0;
 constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
-constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;       // B_STAGES x 4 x QN x 4 B
-constexpr int ZS_OFF = META_OFF + B_STAGES * 4 * QN * 4;   // B_STAGES x TILE_ROWS x 4 B (row scales of the sub-tile)
-constexpr int MAXT = 512;                                  // tiles of one round of a CTA's walk
-constexpr int LIST_OFF = ZS_OFF + B_STAGES * TILE_ROWS * 4; // 5 x MAXT int32: row0, cs, ce, qoff, qn
+constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;       // T_STAGES x 4 x QN x 4 B (per accumulator stage)
+constexpr int ZS_OFF = META_OFF + T_STAGES * 4 * QN * 4;   // T_STAGES x TILE_ROWS x 4 B (row scales of the sub-tile)
+constexpr int MAXT = FVS_TC_MAXT;                          // tiles of one round of a CTA's walk
+constexpr int LIST_OFF = ZS_OFF + T_STAGES * TILE_ROWS * 4; // 5 x MAXT int32: row0, cs, ce, qoff, qn
 constexpr int COL_OFF = LIST_OFF + 5 * MAXT * 4;           // per epilogue warp: 32 column masks + 32 bases
 constexpr int BAR_OFF = COL_OFF + 16 * 64 * 4;             // mbarriers
-constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 2 * T_STAGES;
+constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 3 * T_STAGES;
 constexpr int MISC_OFF = BAR_OFF + NBAR * 8;               // tmem base, abort flag, list length, scan scratch
 constexpr int SMEM_BYTES = MISC_OFF + 16 + 64 + 1024;      // + alignment slack
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 
 struct Params {
     const int8_t* q8;
@@ -88,10 +101,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
     auto b_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + B_STAGES + s); };
     auto t_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + s); };
     auto t_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + T_STAGES + s); };
-    int* meta_qid = reinterpret_cast<int*>(smem + META_OFF);          // [B_STAGES][QN]
-    float* meta_qs = reinterpret_cast<float*>(meta_qid + B_STAGES * QN);
-    float* meta_qc = meta_qs + B_STAGES * QN;
-    float* meta_th = meta_qc + B_STAGES * QN;
+    auto m_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + 2 * T_STAGES + s); };
+    int* meta_qid = reinterpret_cast<int*>(smem + META_OFF);          // [T_STAGES][QN]
+    float* meta_qs = reinterpret_cast<float*>(meta_qid + T_STAGES * QN);
+    float* meta_qc = meta_qs + T_STAGES * QN;
+    float* meta_th = meta_qc + T_STAGES * QN;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + MISC_OFF);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + MISC_OFF + 4);
 
@@ -102,11 +116,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
         }
         for (int s = 0; s < B_STAGES; s++) {
             mbar_init(b_full(s), 1);
-            mbar_init(b_empty(s), 4);
+            mbar_init(b_empty(s), 1);  // released by the MMA commit of its sub-tile
         }
         for (int s = 0; s < T_STAGES; s++) {
             mbar_init(t_full(s), 1);
-            mbar_init(t_empty(s), 4);
+            mbar_init(t_empty(s), 4);  // accumulator + metadata slot, released by the epilogue
+            mbar_init(m_full(s), 1);   // metadata slot written by its gather warp
         }
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -219,6 +234,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                                    sw128_desc(bb + h * QN * 128 + kofs), idesc, ks > 0 ? 1u : 0u);
                         }
                         mma_commit(t_full(st));
+                        mma_commit(b_empty(sb));  // the query tile is free once these MMAs complete
                     }
                     if (!ok) break;
                     mma_commit(a_empty(sa));  // the code tile is free once these MMAs complete
@@ -236,7 +252,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                 for (int i = 0; i * QN < qn; i++, nb_g++) {
                     if (nb_g % GATHER_WARPS != gw) continue;
                     const int s = nb_g % B_STAGES;
-                    if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort)) {
+                    const int st = nb_g % T_STAGES;
+                    if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort) ||
+                        !mbar_wait(t_empty(st), ((nb_g / T_STAGES) & 1) ^ 1, abort)) {
                         ok = false;
                         break;
                     }
@@ -246,7 +264,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
 #pragma unroll
                     for (int rr = 0; rr < TILE_ROWS / 32; rr++) {
                         const int row = row0 + 32 * rr + lane;
-                        zsm[s * TILE_ROWS + 32 * rr + lane] = (row >= cs && row < ce) ? p.zs[row] : 0.f;
+                        zsm[st * TILE_ROWS + 32 * rr + lane] = (row >= cs && row < ce) ? p.zs[row] : 0.f;
                     }
                     int qq[2];
 #pragma unroll
@@ -257,10 +275,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                             const int pi = qoff + i * QN + g;
                             const int q = p.qid[pi];
                             qq[rr] = q;
-                            meta_qid[s * QN + g] = q;
-                            meta_qs[s * QN + g] = p.qs[q];
-                            meta_qc[s * QN + g] = p.qcp[pi];
-                            meta_th[s * QN + g] = MODE ? p.t0[q] : 0.f;
+                            meta_qid[st * QN + g] = q;
+                            meta_qs[st * QN + g] = p.qs[q];
+                            meta_qc[st * QN + g] = p.qcp[pi];
+                            meta_th[st * QN + g] = MODE ? p.t0[q] : 0.f;
                         }
                     }
 #pragma unroll
@@ -283,7 +301,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                     }
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(b_full(s));
+                    if (lane == 0) {
+                        mbar_arrive(b_full(s));
+                        mbar_arrive(m_full(st));
+                    }
                 }
                 if (!ok) break;
             }
@@ -301,20 +322,20 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                 bool ok = true;
                 for (int i = 0; i * QN < qn; i++, nb_e++) {
                     if (nb_e % EPI_GROUPS != eg) continue;
-                    const int sb = nb_e % B_STAGES, st = nb_e % T_STAGES;
+                    const int st = nb_e % T_STAGES;
                     if (!mbar_wait(t_full(st), (nb_e / T_STAGES) & 1, abort) ||
-                        !mbar_wait(b_full(sb), (nb_e / B_STAGES) & 1, abort)) {  // b_full: acquire the metadata
+                        !mbar_wait(m_full(st), (nb_e / T_STAGES) & 1, abort)) {  // m_full: acquire the metadata
                         ok = false;
                         break;
                     }
                     tc_fence_after();
                     const int nq = min(QN, qn - i * QN);
                     const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
-                    const int* mq = meta_qid + sb * QN;
-                    const float* ms = meta_qs + sb * QN;
-                    const float* mc = meta_qc + sb * QN;
-                    const float* mt = meta_th + sb * QN;
-                    const float zr = zsm[sb * TILE_ROWS + 32 * ew + lane];
+                    const int* mq = meta_qid + st * QN;
+                    const float* ms = meta_qs + st * QN;
+                    const float* mc = meta_qc + st * QN;
+                    const float* mt = meta_th + st * QN;
+                    const float zr = zsm[st * TILE_ROWS + 32 * ew + lane];
                     uint32_t* colm = reinterpret_cast<uint32_t*>(smem + COL_OFF) + (warp - 2 - GATHER_WARPS) * 64;
                     int* colb = reinterpret_cast<int*>(colm + 32);
                     for (int h = 0; h * 32 < nq; h++) {
@@ -396,7 +417,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                     __syncwarp();
                     if (lane == 0) {
                         mbar_arrive(t_empty(st));
-                        mbar_arrive(b_empty(sb));
                     }
                 }
                 if (!ok) break;

@@ -155,6 +155,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
     float* lut = reinterpret_cast<float*>(smem);
+    int32_t* s_pos = reinterpret_cast<int32_t*>(lut + 128 * GA);  // the query's candidate positions (K)
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const int lim = ncnt ? min(max(ncnt[q], 0), K) : K;
     for (int i = lim + tid; i < K; i += blockDim.x) {
@@ -164,6 +165,8 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     if (lim == 0) return;
     const float* z = Zq + (int64_t)q * ldz;
     const int nblk = D / 32;
+    // positions staged once (coalesced), so that each candidate round trip is the plane words alone
+    for (int i = tid; i < lim; i += blockDim.x) s_pos[i] = (int32_t)pos[(int64_t)q * K + i];
     // one 4-coordinate group per thread (ga fastest across lanes: conflict-free stores); entry v sums the selected
     // coordinates left to right in fp32, as acc += z_i * bit_i does
     for (int gi = tid; gi < 8 * GA; gi += blockDim.x) {
@@ -227,7 +230,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
         for (int c = 0; c < 2; c++) {
             const int i = i0 + c * nw;
             live[c] = i < lim;
-            nn[c] = live[c] ? pos[(int64_t)q * K + i] : 0;
+            nn[c] = live[c] ? s_pos[i] : 0;
         }
 #pragma unroll
         for (int c = 0; c < 2; c++) {
@@ -372,7 +375,7 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
     if (wpl > 12) return FVS_ERANGE;
     const int GA = ((D / 32) + 31) / 32 * 32;
     FVS_CHECK_ARG(D % 32 == 0);
-    const size_t sm = (size_t)128 * GA * 4;
+    const size_t sm = (size_t)128 * GA * 4 + (size_t)K * 4;
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
 #define FVS_LZ(H, W)                                                                                               \

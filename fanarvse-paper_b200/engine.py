@@ -106,6 +106,8 @@ class EngineB200I8:
     BETA = None
     SCAN = "tc"      # "tc": tcgen05 kernel (the product path); "mma": the mma.sync kernel kept as a baseline
     SMALL = 32       # batches up to this size take the streaming scan (fvs_i8_scan_small) instead of the tile scan
+    FB_INGRAPH = 48  # flagged rows recomputed inside the batch's own graph (batches of FB_MIN_BATCH or more)
+    FB_MIN_BATCH = 256
 
     def __init__(self, index: IndexI8):
         self.ix = index
@@ -118,6 +120,7 @@ class EngineB200I8:
         self.L = _lib.lib()
         self.status = torch.zeros(1, dtype=torch.int32, device=index.device)
         self.work = torch.zeros(index.NC, dtype=torch.int32, device=index.device)
+        self._nflag = torch.zeros(1, dtype=torch.int32, device=index.device)   # rows flagged by the main pass
 
     def pairs(self, probe, ncols, QM, want_slot):
         """pair list by cell over the first ncols probe columns (`throughput/enginei8.py:11-16`)."""
@@ -146,8 +149,11 @@ class EngineB200I8:
                        ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z),
                        ptr(ix.zs), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB)
 
+    _tag = ""        # prefix of the timing names (the in-graph recompute times its calls separately)
+
     def _call(self, name, fn, *args):
         """Call one C-ABI entry point on the current stream; count it; optionally bracket it with CUDA events."""
+        name = self._tag + name
         if self.timing is not None:
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
@@ -176,7 +182,7 @@ class EngineB200I8:
             beta = 1.5
         return min(max(int(np.ceil(beta * K / (self.ix.N / self.ix.NC / BN + 1))), 1), nprobe)
 
-    def stage1_i8(self, Qb, QM, probe, K, rho_override=None, M_override=None, q8qs=None):
+    def stage1_i8(self, Qb, QM, probe, K, rho_override=None, M_override=None, q8qs=None, small=None):
         """`throughput/enginei8.py:36-60` on the C library: returns pos [B,K] int64, ok [B] bool, est1 [B,K], n1."""
         ix, L = self.ix, self.L
         B = Qb.shape[0]
@@ -186,7 +192,7 @@ class EngineB200I8:
         rho = rho_override if rho_override else (self.RHO or (0.75 if K <= 400 else 0.5))
         n1 = self.first_pass_cells(K, probe.shape[1], rho_override)
         probe = probe.contiguous()
-        if B <= self.SMALL and self.SCAN != "mma":
+        if (B <= self.SMALL and self.SCAN != "mma") if small is None else small:
             return self._stage1_small(q8, qs, B, QM, probe, K, M, rho, n1, rho_override)
         qid, coff, ccnt, qcp, slot = self.pairs(probe, n1, QM, True)
         bmc = torch.empty(B * n1 * ix.MB, device=dev)
@@ -319,8 +325,45 @@ class EngineB200I8:
             raise ValueError("need K > k and K >= 10 (the delta rule reads the 10th stage-1 estimate)")
         QC = (Qb @ self.ix.c).contiguous()
         QM, probe = self.route(Qb, nprobe)
-        pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K)
-        return self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
+        q8, qs = self.quantize(Qb)
+        pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs))
+        out = self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
+        if self.FB_INGRAPH and len(Qb) >= self.FB_MIN_BATCH:
+            out = self._fallback_ingraph(Qb, QC, QM, probe, q8, qs, *out, K, z, k)
+        return out
+
+    def _fallback_ingraph(self, Qb, QC, QM, probe, q8, qs, ok, I, reads, ids, K, z, k):
+        """The recompute of `throughput/enginei8.py:112-120` for up to FB_INGRAPH flagged rows, inside the batch's own
+        graph (no host round trip): the flagged rows are compacted on the GPU (prefix sum; unused slots point at row
+        0 and write to a discarded row), rerun from the main pass's routing and query codes with rho 1.0 (beta 1.5),
+        M 65536, fp32 LUT, no delta rule, and scattered back.  Rows beyond the capacity stay flagged for the host."""
+        B, FB, dev = len(Qb), self.FB_INGRAPH, Qb.device
+        bad = ~ok
+        self._nflag.copy_(bad.sum().to(torch.int32).reshape(1))
+        c = torch.cumsum(bad.to(torch.int32), 0)
+        slot = torch.where(bad & (c <= FB), c - 1, torch.full_like(c, FB)).long()
+        rows = torch.full((FB + 1,), B, dtype=torch.long, device=dev)
+        rows.scatter_(0, slot, torch.arange(B, device=dev))        # slot FB collects the unused rows (discarded)
+        rows = rows[:FB]
+        valid = rows < B
+        src = torch.where(valid, rows, torch.zeros_like(rows))
+        Qf = Qb[src].contiguous()
+        main_last, self._tag = self._last, "fallback_"
+        try:
+            pos, okf, est1, _ = self.stage1_i8(Qf, QM[src].contiguous(), probe[src].contiguous(), K,
+                                               rho_override=1.0, M_override=65536,
+                                               q8qs=(q8[src].contiguous(), qs[src].contiguous()), small=True)
+            est, sd = self.score_lut_zq(QC[src].contiguous(), pos, self.rotated_query(Qf), None, False)
+            If, rf, idsf, _ = self.refine(Qf, pos, est, sd, z, k)
+        finally:
+            self._last, self._tag = main_last, ""
+        self._last["fallback_rows"] = rows
+        tgt = torch.where(valid, rows, torch.full_like(rows, B))
+        I = torch.cat([I, I[:1]]).index_copy_(0, tgt, If)[:B]
+        reads = torch.cat([reads, reads[:1]]).index_copy_(0, tgt, rf.long())[:B]
+        ids = torch.cat([ids, ids[:1]]).index_copy_(0, tgt, idsf)[:B]
+        handled = torch.zeros(B + 1, dtype=torch.bool, device=dev).index_fill_(0, tgt, True)[:B]
+        return ok | handled, I, reads, ids
 
     def _fallback(self, Qb, K, z, nprobe, k):
         """`throughput/enginei8.py:112-120`: rho 1.0 (beta 1.5), M 65536, fp32 LUT, no delta rule."""
@@ -356,12 +399,16 @@ class EngineB200I8:
         g.replay()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         I, nr, ids = I.clone(), nr.clone(), ids.clone()
-        flags = torch.cat([ok.to(torch.int32), self.status]).cpu()         # the only synchronisation
-        if int(flags[-1]) != 0:
+        flags = torch.cat([ok.to(torch.int32), self.status, self._nflag]).cpu()   # the only synchronisation
+        if int(flags[-2]) != 0:
             raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
-        if not bool(flags[:-1].all()):
-            bad = torch.nonzero(flags[:-1] == 0).flatten()
-            self.nbad += len(bad)
+        in_graph = self.FB_INGRAPH and B >= self.FB_MIN_BATCH
+        if in_graph:
+            self.nbad += int(flags[-1])                # recomputed inside the graph (or below, beyond capacity)
+        if not bool(flags[:-2].all()):
+            bad = torch.nonzero(flags[:-2] == 0).flatten()
+            if not in_graph:
+                self.nbad += len(bad)
             a, b, c = self._fallback_graphed(Qb, bad, K, z, nprobe, k)
             badd = bad.to(Qb.device)
             I[badd], nr[badd] = a, b

@@ -333,3 +333,45 @@ def test_search_host_matches_search(eng):
         I, _, _ = E.search(Q[:B].contiguous(), 40, 1.5, 12, 10)
         h = E.search_host(Q[:B].contiguous(), 40, 1.5, 12, 10)
         np.testing.assert_array_equal(h, c(I))
+
+
+@pytest.mark.parametrize("msz", [600, 160])
+def test_in_graph_recompute(eng, msz):
+    """batches of FB_MIN_BATCH rows or more recompute up to FB_INGRAPH flagged rows inside their own graph (from the
+    main pass's routing and query codes), the rest on the host: the flagged rows equal the oracle's `_fallback` on the
+    same inputs, the other rows the main pass; the ids of the recompute are exact."""
+    ds, ix, oi = _random_index(eng, 30000, 512, 96, 320, seed=13)
+    E = eng.EngineB200I8(ix)
+    E.MSZ = msz                      # 600: a few flagged rows (all in the graph); 160: more than FB_INGRAPH
+    K, z, nprobe, k = 30, 1.5, 20, 10
+    Q = ds["queries"]
+    assert len(Q) >= E.FB_MIN_BATCH
+    I, nr, ids = E.search(Q, K, z, nprobe, k)
+    r = E.search_eager(Q, K, z, nprobe, k)
+    QM, probe = E.route(Q, nprobe)
+    q8, qs = E.quantize(Q)
+
+    class Knobs(O.I8Knobs):
+        MSZ = msz
+
+    o = O.search_i8(oi, c(Q), K, z, nprobe, k, Knobs, QM=c(QM), probe=c(probe), q8qs=(c(q8), c(qs)),
+                    Zq=c(E.rotated_query(Q)), fallback=False)
+    ok = o["ok"]
+    nbad = int((~ok).sum())
+    assert nbad > 0 and E.nbad >= nbad
+    if msz == 160:
+        assert nbad > E.FB_INGRAPH               # some rows take the host path
+    same = ok & (c(nr) == o["reads"])
+    assert same.sum() >= 0.9 * ok.sum()
+    np.testing.assert_array_equal(c(I)[same], o["I"][same])
+    bad = np.nonzero(~ok)[0]
+    Zf = (Q.float() @ ix.VP16.float()).cpu().numpy()                 # recompute LUT input (fp32 LUT path)
+    fb = O._search_i8_core(oi, c(Q)[bad], K, z, nprobe, k, Knobs, c(QM)[bad], c(probe)[bad], (c(q8)[bad], c(qs)[bad]),
+                           c(E.rotated_query(Q))[bad], rho_override=1.0)
+    in_graph = bad[:E.FB_INGRAPH]
+    np.testing.assert_array_equal(c(ids)[in_graph], fb["ids"][:len(in_graph)])
+    sameb = c(nr)[in_graph] == fb["reads"][:len(in_graph)]
+    assert sameb.sum() >= 0.9 * len(in_graph)
+    np.testing.assert_array_equal(c(I)[in_graph][sameb], fb["I"][:len(in_graph)][sameb])
+    I2, _, _ = E.search(Q, K, z, nprobe, k)
+    np.testing.assert_array_equal(c(I2), c(I))
