@@ -217,12 +217,13 @@ class EngineB200I8:
         return pos, ok.bool(), est1, ncnt
 
     def _ident(self, n):
-        """slot[i] = i (the streaming scan's pair slots), cached per length."""
-        t = getattr(self, "_ident_cache", None)
-        if t is None or t.numel() < n:
-            t = torch.arange(max(n, 1024), dtype=torch.int32, device=self.ix.device)
-            self._ident_cache = t
-        return t
+        """slot[i] = i (the streaming scan's pair slots), cached.  A captured graph keeps the address of the tensor it
+        was given, so a tensor handed out is never released (a larger one is added when needed): releasing it would
+        let the allocator reuse its memory under a graph that still reads it."""
+        keep = self.__dict__.setdefault("_ident_keep", [])
+        if not keep or keep[-1].numel() < n:
+            keep.append(torch.arange(max(n, 1024), dtype=torch.int32, device=self.ix.device))
+        return keep[-1]
 
     def _stage1_small(self, q8, qs, B, QM, probe, K, M, rho, n1, rho_override):
         """stage 1 for small batches: streaming scan straight from the probe list (no pair sort)."""
