@@ -44,15 +44,29 @@ class ShardedSearch:
     """search(Qb, K, z, nprobe, k) -> (I [B,k] int64 global ids, S [B,k] exact scores, reads [B] local reads).
 
     `local` is the rank's engine (EngineB200I8 on its shard); `row_offset` the global id of its first row.  The local
-    exact-score and merge steps can be replaced (CPU tests inject the oracle's restatements)."""
+    exact-score and merge steps can be replaced (CPU tests inject the oracle's restatements).
+
+    On CUDA ranks the whole step -- local search (with its in-graph recompute of flagged rows), exact scores of the
+    local winners, the all-gather, the merge, and a sum over ranks of the rows still flagged -- is one CUDA graph per
+    (B, K, z, nprobe, k); the host reads that sum once.  Only when some rank has rows beyond its in-graph recompute
+    capacity do all ranks take the eager path (the rank-local recompute, then the exchange again), so every rank makes
+    the same collective calls in the same order.  `close()` releases the graphs (they hold NCCL calls) and must run
+    before the process group is destroyed."""
 
     def __init__(self, local, row_offset, group=None, exact=None, merge=None):
         self.local, self.row_offset, self.group = local, int(row_offset), group
         self.exact = exact or (lambda Qb, I: exact_scores(self.local, Qb, I))
         self.merge = merge or merge_topk
+        self.graphs = {}
+        self.eager_steps = 0
 
-    def search(self, Qb, K, z, nprobe, k):
-        I, reads, _ = self.local.search(Qb, K, z, nprobe, k)
+    def close(self):
+        self.graphs.clear()
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+
+    def _exchange(self, Qb, I, k):
+        """exact scores of the local top-k, one all-gather, merge (every rank, same order)."""
         S = self.exact(Qb, I)
         gid = I.long() + self.row_offset
         G = dist.get_world_size(self.group) if dist.is_initialized() else 1
@@ -69,5 +83,54 @@ class ShardedSearch:
                 dist.all_gather(list(out.unbind(0)), rec, group=self.group)
             ids_all = out[..., :2].contiguous().view(torch.int64).view(G, B, k)
             s_all = out[..., 2].contiguous().view(torch.float32)
-        Ig, Sg = self.merge(ids_all, s_all, k)
+        return self.merge(ids_all, s_all, k)
+
+    def _graph_body(self, qs, K, z, nprobe, k):
+        ok, I, reads, ids = self.local._gpu(qs, K, z, nprobe, k)
+        Ig, Sg = self._exchange(qs, I, k)
+        left = (~ok).sum().to(torch.int32).reshape(1)
+        flags = torch.cat([left, self.local.status])
+        if dist.is_initialized() and dist.get_world_size(self.group) > 1:
+            dist.all_reduce(flags, op=dist.ReduceOp.SUM, group=self.group)
+        flags = torch.cat([flags, self.local._nflag])          # + this rank's rows flagged by its main pass
+        return ok, I, reads, ids, Ig, Sg, flags
+
+    def search(self, Qb, K, z, nprobe, k):
+        if not Qb.is_cuda or not hasattr(self.local, "_gpu"):
+            I, reads, _ = self.local.search(Qb, K, z, nprobe, k)
+            Ig, Sg = self._exchange(Qb, I, k)
+            return Ig, Sg, reads
+        key = (len(Qb), K, z, nprobe, k)
+        if key not in self.graphs:
+            qs = Qb.clone()
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(st):
+                for _ in range(3):
+                    self._graph_body(qs, K, z, nprobe, k)
+            torch.cuda.current_stream().wait_stream(st)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                outs = self._graph_body(qs, K, z, nprobe, k)
+            self.graphs[key] = (g, qs, outs)
+        g, qs, (ok, I, reads, ids, Ig, Sg, flags) = self.graphs[key]
+        qs.copy_(Qb)
+        g.replay()
+        f = flags.cpu()                                        # the only synchronisation
+        self.local.nbad += int(f[2])
+        if int(f[1]) != 0:
+            raise _lib.FvsError("sharded search: a bounded device wait expired on some rank (status flag set)")
+        if int(f[0]) == 0:
+            return Ig.clone(), Sg.clone(), reads.clone()
+        # some rank has flagged rows left: every rank recomputes its own (possibly none) and exchanges again
+        self.eager_steps += 1
+        E = self.local
+        I, reads = I.clone(), reads.clone()
+        bad = torch.nonzero(~ok).flatten().cpu()
+        if len(bad):
+            a, b, _ = E._fallback_graphed(Qb, bad, K, z, nprobe, k)
+            badd = bad.to(Qb.device)
+            I[badd], reads[badd] = a, b
+        Ig, Sg = self._exchange(Qb, I, k)
         return Ig, Sg, reads
