@@ -111,12 +111,14 @@ class ShardedSearch:
             torch.cuda.current_stream().wait_stream(st)
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
+            n0 = self.local.launches
             with torch.cuda.graph(g):
                 outs = self._graph_body(qs, K, z, nprobe, k)
-            self.graphs[key] = (g, qs, outs)
-        g, qs, (ok, I, reads, ids, Ig, Sg, flags) = self.graphs[key]
+            self.graphs[key] = (g, qs, outs, self.local.launches - n0 + 2)   # + exact scores, merge
+        g, qs, (ok, I, reads, ids, Ig, Sg, flags), nl = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
+        self.local.replayed_launches = getattr(self.local, "replayed_launches", 0) + nl
         f = flags.cpu()                                        # the only synchronisation
         self.local.nbad += int(f[2])
         if int(f[1]) != 0:
