@@ -285,11 +285,26 @@ __global__ void __launch_bounds__(512) rth_largest_small_kernel(const float* __r
             }
         }
     }
+    // lower bound: a thread's r-th largest (its r values are all >= it, so the row's r-th largest is too); only
+    // entries >= the largest such bound can matter, and the threads' top-r lists hold at least r of them
+    __shared__ float s_lb[32];
+    __shared__ int s_n;
+    float kth = INFINITY;  // top[] is sorted descending: its r-th entry is the minimum of the first r
 #pragma unroll
     for (int j = 0; j < RM; j++)
-        if (j < r) keys[j * nt + tid] = f2o(top[j]);
+        if (j < r) kth = fminf(kth, top[j]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) kth = fmaxf(kth, __shfl_xor_sync(0xffffffffu, kth, o));
+    if ((tid & 31) == 0) s_lb[tid >> 5] = kth;
+    if (tid == 0) s_n = 0;
     __syncthreads();
-    const uint32_t k = block_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, nt * r, r, ss);
+    float lb = -INFINITY;
+    for (int w = 0; w < (nt >> 5); w++) lb = fmaxf(lb, s_lb[w]);
+#pragma unroll
+    for (int j = 0; j < RM; j++)
+        if (j < r && top[j] >= lb) keys[atomicAdd(&s_n, 1)] = f2o(top[j]);
+    __syncthreads();
+    const uint32_t k = block_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, s_n, r, ss);
     if (tid == 0) out[q] = o2f(k);
 }
 
