@@ -33,7 +33,10 @@ sys.path.insert(0, REPO)
 import importlib  # noqa: E402
 
 METRIC = "QPS at recall@10>=0.99, 1M x 1536 fp16, batch 2000; batch-1 p50 latency"
-GRID = [(96, 100, 4096), (128, 120, 4096), (160, 120, 4096), (192, 150, 4096), (256, 150, 4096), (352, 175, 4096)]
+# operating points: (nprobe, K, M, rho, in-graph recompute capacity); rho 0.6 / M 4096 are the reference's final
+# knobs (`throughput/e_v3final.py:28-32` with M raised to 4096); rho 0.65 with M 8192 flags fewer queries
+GRID = [(64, 90, 8192, 0.65, 16), (80, 100, 8192, 0.65, 16), (96, 100, 4096, 0.6, 48), (96, 100, 8192, 0.65, 16), (128, 120, 4096, 0.6, 48), (128, 120, 8192, 0.65, 16),
+        (160, 120, 8192, 0.65, 16), (192, 150, 8192, 0.65, 16), (256, 150, 8192, 0.65, 16), (352, 175, 8192, 0.65, 16)]
 
 
 def pkg(name):
@@ -136,8 +139,8 @@ def choose_op(args, E, search, Q, gt, world):
     """fastest grid point with recall@10 >= 0.99 (same decision on every rank)."""
     synth = pkg("synth")
     best, rows = None, []
-    for npr, K, M in GRID:
-        E.MSZ = M
+    for npr, K, M, rho, fb in GRID:
+        set_knobs(E, M, rho, fb)
         I = search(Q, K, args.z, npr, 10)
         rec = synth.recall(I.cpu(), gt.cpu(), 10)
         ms = timed(lambda: search(Q, K, args.z, npr, 10), 3)
@@ -146,14 +149,18 @@ def choose_op(args, E, search, Q, gt, world):
             t = torch.tensor([ms], device=Q.device)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t)
-        rows.append(dict(nprobe=npr, K=K, M=M, recall=round(rec, 4), ms=round(ms, 3)))
+        rows.append(dict(nprobe=npr, K=K, M=M, rho=rho, fb=fb, recall=round(rec, 4), ms=round(ms, 3)))
         if rec >= 0.99 and (best is None or ms < best[3]):
-            best = (npr, K, M, ms, rec)
+            best = (npr, K, M, ms, rec, rho, fb)
     log("operating points:", json.dumps(rows))
     if best is None:
-        npr, K, M = GRID[-1]
-        best = (npr, K, M, None, rows[-1]["recall"])
+        npr, K, M, rho, fb = GRID[-1]
+        best = (npr, K, M, None, rows[-1]["recall"], rho, fb)
     return best, rows
+
+
+def set_knobs(E, M, rho, fb):
+    E.MSZ, E.RHO, E.FB_INGRAPH = M, rho, fb
 
 
 # ---------------------------------------------------------------------------------------------------- roofline
@@ -216,11 +223,12 @@ def oracle_index_cpu(s1, i8, code, H16):
     return ge.oracle_index(s1, i8, code, H16)
 
 
-def cpu_oracle_qps(oi, Q, K, z, npr, k, M, nq):
+def cpu_oracle_qps(oi, Q, K, z, npr, k, M, nq, rho=None):
     from oracle import fvs_oracle as O
 
     class Knobs(O.I8Knobs):
         MSZ = M
+        RHO = rho or O.I8Knobs.RHO
 
     Qc = Q[:nq].detach().cpu().numpy()
     t = time.perf_counter()
@@ -351,7 +359,7 @@ def main():
     ap.add_argument("--dim", type=int, default=1536)
     ap.add_argument("--comps", type=int, default=1024)
     ap.add_argument("--z", type=float, default=1.25)
-    ap.add_argument("--op", default="auto", help="nprobe:K:M or auto")
+    ap.add_argument("--op", default="auto", help="nprobe:K:M[:rho[:in-graph rows]] or auto")
     ap.add_argument("--cpu-sample", type=int, default=48)
     ap.add_argument("--variants", default="dense,trellis",
                     help="comma list of extra measurements at N=1: dense (routing-free int8), trellis (default "
@@ -375,11 +383,14 @@ def main():
     Q0 = ds["queries"]
     Qs = [Q0] + [pkg("synth").extra_queries(ds, args.batch, 100 + i) for i in range(3)]
     if args.op == "auto":
-        (npr, K, M, _, rec), grid_rows = choose_op(args, E, search, Q0, gt, world)
+        (npr, K, M, _, rec, rho, fb), grid_rows = choose_op(args, E, search, Q0, gt, world)
     else:
-        npr, K, M = (int(x) for x in args.op.split(":"))
+        f = args.op.split(":")
+        npr, K, M = (int(x) for x in f[:3])
+        rho = float(f[3]) if len(f) > 3 else E.RHO
+        fb = int(f[4]) if len(f) > 4 else E.FB_INGRAPH
         grid_rows = None
-    E.MSZ = M
+    set_knobs(E, M, rho, fb)
     k, z = 10, args.z
     E.prewarm(Q0, K, z, npr, k)
     I = search(Q0, K, z, npr, k)
@@ -486,7 +497,7 @@ def main():
     if rank == 0 and world == 1:
         oi = oracle_index_cpu(s1, i8, code, ds["base16"])
         nq = args.cpu_sample
-        qps = cpu_oracle_qps(oi, Qs[0], K, z, npr, k, M, nq)
+        qps = cpu_oracle_qps(oi, Qs[0], K, z, npr, k, M, nq, rho)
         cpu = {"value": round(qps, 2), "unit": "queries/s", "cores": torch.get_num_threads(), "kind": "port",
                "sample": f"{nq} queries of the timed batch through the numpy oracle of the whole search"}
     variants = None
@@ -511,6 +522,7 @@ def main():
                 "config": {"workload": f"{args.rows * world // 1000000}M x {args.dim} fp16 ({world} shard(s) of "
                                        f"{args.rows}), throughput mode, batch {args.batch}, k=10",
                            "global_batch": args.batch, "rows_per_gpu": args.rows, "nprobe": npr, "K": K, "M": M,
+                           "rho": rho, "in_graph_recompute_rows": fb,
                            "z": z, "recall@10": round(rec, 4), "parallelism": f"row-shard x{world}",
                            "l2": "inputs larger than L2 (262 MB of int8 codes + 3 GB fp16 store streamed; 4 query "
                                  "batches cycled)", "value_scaling": "queries/s x (database rows / 1M)",

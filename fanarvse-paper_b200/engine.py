@@ -375,12 +375,17 @@ class EngineB200I8:
         I, reads, ids, _ = self.refine(Qb, pos, est, sd, z, k)
         return I, reads.long(), ids
 
+    def knobs(self):
+        """everything a captured graph bakes in besides the call's arguments (a knob change captures anew)."""
+        return (self.RHO, self.MSZ, self.DELTA, self.LUTH, self.BETA, self.SCAN, self.SMALL, self.FB_INGRAPH,
+                self.FB_MIN_BATCH, getattr(self, "M", None), getattr(self, "OVER", None))
+
     def search(self, Qb, K, z, nprobe, k, ret_est=False):
         """`throughput/enginei8.py:96-111`: returns (I [B,k] int32, reads [B] int64, cand_ids [B,K] int32)."""
         if not Qb.is_cuda:
             raise RuntimeError("EngineB200I8.search needs CUDA queries (the B200 library has no CPU path)")
         B = len(Qb)
-        key = (B, K, z, nprobe, k)
+        key = (B, K, z, nprobe, k, self.knobs())
         if key not in self.graphs:
             qs = Qb.clone()
             st = torch.cuda.Stream()
@@ -423,7 +428,7 @@ class EngineB200I8:
         if not Qb.is_cuda:
             raise RuntimeError("EngineB200I8.search_host needs CUDA queries (the B200 library has no CPU path)")
         B = len(Qb)
-        key = ("host", B, K, z, nprobe, k)
+        key = ("host", B, K, z, nprobe, k, self.knobs())
         if key not in self.graphs:
             qs = Qb.clone()
             host = torch.empty((B, k + 2), dtype=torch.int32, pin_memory=True)
@@ -471,7 +476,7 @@ class EngineB200I8:
         if bucket is None:                                                 # very many flagged rows: eager, chunked
             outs = [self._fallback(Qb[bad[i:i + 256].to(Qb.device)], K, z, nprobe, k) for i in range(0, nb, 256)]
             return tuple(torch.cat(x) for x in zip(*outs))
-        key = ("fb", bucket, K, z, nprobe, k)
+        key = ("fb", bucket, K, z, nprobe, k, self.knobs())
         if key not in self.graphs:
             qs = Qb[:1].repeat(bucket, 1).contiguous()
             st = torch.cuda.Stream()

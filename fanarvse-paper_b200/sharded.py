@@ -100,7 +100,7 @@ class ShardedSearch:
             I, reads, _ = self.local.search(Qb, K, z, nprobe, k)
             Ig, Sg = self._exchange(Qb, I, k)
             return Ig, Sg, reads
-        key = (len(Qb), K, z, nprobe, k)
+        key = (len(Qb), K, z, nprobe, k, self.local.knobs())
         if key not in self.graphs:
             qs = Qb.clone()
             st = torch.cuda.Stream()
