@@ -144,14 +144,22 @@ __global__ void __launch_bounds__(256) lut_score_kernel(const int64_t* __restric
 // (c, v, ga) sits at (c*16 + v)*GA + ga with GA a multiple of 32, so the 32 lanes of a warp, which hold consecutive
 // words, read 32 different banks.  Entries are fp32 slots holding the fp16-rounded value when HALF (the reference's
 // `LUTH` table), otherwise the fp32 value.
-template <bool HALF, int WPL>
+// REC: the candidate's plane words and (scale, sigma) pairs come from its packed record (`src/tiered_fused.py:112-125`:
+// tier t plane p at byte toff[t] + p*KB_t = 4 * word index, then fp16 (scale, sigma) per tier at soff + 4t), one
+// contiguous RB-byte row per vector, instead of b_t separate plane rows and two [T, N] arrays
+struct RecSet {
+    const uint8_t* rec;
+    int RB, soff;
+};
+
+template <bool HALF, int WPL, bool REC>
 __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __restrict__ pos, int B, int K,
                                                            const float* __restrict__ qc, const float* __restrict__ Zq,
                                                            int ldz, int D, int GA, TierSet ts,
                                                            const __half* __restrict__ scale,
                                                            const __half* __restrict__ sig, int64_t N,
                                                            const int32_t* __restrict__ ncnt, float* __restrict__ est,
-                                                           float* __restrict__ sd) {
+                                                           float* __restrict__ sd, RecSet rs) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
     float* lut = reinterpret_cast<float*>(smem);
@@ -239,12 +247,23 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
                 wv[c][u] = 0;
                 if (live[c] && wt[u] >= 0) {
                     const int t = wt[u];
-                    wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(ts.planes[t] +
-                                                                        ((int64_t)wp[u] * N + nn[c]) * ts.kb[t] + wj[u]));
+                    if (REC)
+                        wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(rs.rec + nn[c] * rs.RB) + lane + 32 * u);
+                    else
+                        wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(
+                            ts.planes[t] + ((int64_t)wp[u] * N + nn[c]) * ts.kb[t] + wj[u]));
                 }
             }
-            scl[c] = (live[c] && lane < ts.T) ? __half2float(scale[(int64_t)lane * N + nn[c]]) : 0.f;
-            sgl[c] = (live[c] && lane < ts.T) ? __half2float(sig[(int64_t)lane * N + nn[c]]) : 0.f;
+            if (REC) {
+                const uint32_t sp = (live[c] && lane < ts.T)
+                                        ? __ldg(reinterpret_cast<const uint32_t*>(rs.rec + nn[c] * rs.RB + rs.soff) + lane)
+                                        : 0u;
+                scl[c] = __half2float(__ushort_as_half((unsigned short)(sp & 0xffffu)));
+                sgl[c] = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
+            } else {
+                scl[c] = (live[c] && lane < ts.T) ? __half2float(scale[(int64_t)lane * N + nn[c]]) : 0.f;
+                sgl[c] = (live[c] && lane < ts.T) ? __half2float(sig[(int64_t)lane * N + nn[c]]) : 0.f;
+            }
         }
 #pragma unroll
         for (int c = 0; c < 2; c++) {
@@ -378,13 +397,14 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
     const size_t sm = (size_t)128 * GA * 4 + (size_t)K * 4;
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
+    const fvs::RecSet rs{nullptr, 0, 0};
 #define FVS_LZ(H, W)                                                                                               \
     do {                                                                                                           \
-        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W>, sm);                         \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false>, sm);                  \
         if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,                 \
-                                                              (const __half*)scale, (const __half*)sig, N, ncnt,    \
-                                                              est, sd);                                             \
+        fvs::lut_score_zq_kernel<H, W, false><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,          \
+                                                                     (const __half*)scale, (const __half*)sig, N,  \
+                                                                     ncnt, est, sd, rs);                           \
     } while (0)
     if (half) {
         if (wpl <= 4) FVS_LZ(true, 4); else if (wpl <= 8) FVS_LZ(true, 8); else FVS_LZ(true, 12);
@@ -392,5 +412,45 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
         if (wpl <= 4) FVS_LZ(false, 4); else if (wpl <= 8) FVS_LZ(false, 8); else FVS_LZ(false, 12);
     }
 #undef FVS_LZ
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc,
+                                 const float* Zq, int ldz, int D, int half, int T, const int32_t* tier_s,
+                                 const int32_t* tier_e, const int32_t* tier_bits, const float* tier_delta,
+                                 const uint8_t* rec, int RB, int soff, int64_t N, const int32_t* ncnt, float* est,
+                                 float* sd) {
+    FVS_CHECK_ARG(pos && qc && Zq && tier_s && tier_e && tier_bits && tier_delta && rec && est && sd);
+    FVS_CHECK_ARG(B >= 0 && K >= 1 && N > 0 && D > 0 && D % 32 == 0 && ldz >= D && ldz % 4 == 0);
+    FVS_CHECK_ARG(((uintptr_t)Zq & 15) == 0 && ((uintptr_t)rec & 15) == 0 && RB > 0 && RB % 16 == 0);
+    fvs::TierSet ts;
+    int rc = fvs::make_tiers(ts, T, tier_s, tier_e, tier_bits, tier_delta, nullptr);
+    if (rc) return rc;
+    for (int t = 0; t < T; t++) {
+        FVS_CHECK_ARG(tier_e[t] <= D && (tier_e[t] - tier_s[t]) % 32 == 0);
+        if (t > 0) FVS_CHECK_ARG(tier_s[t] == tier_e[t - 1]);
+    }
+    FVS_CHECK_ARG(tier_s[0] == 0);
+    FVS_CHECK_ARG(soff == 4 * ts.nwords && soff + 4 * T <= RB);
+    const int wpl = (ts.nwords + 31) / 32;
+    if (wpl > 12) return FVS_ERANGE;
+    const int GA = ((D / 32) + 31) / 32 * 32;
+    const size_t sm = (size_t)128 * GA * 4 + (size_t)K * 4;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    const fvs::RecSet rs{rec, RB, soff};
+#define FVS_LR(H, W)                                                                                               \
+    do {                                                                                                           \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true>, sm);                   \
+        if (e != cudaSuccess) return (int)e;                                                                       \
+        fvs::lut_score_zq_kernel<H, W, true><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts, nullptr,  \
+                                                                    nullptr, N, ncnt, est, sd, rs);                \
+    } while (0)
+    if (half) {
+        if (wpl <= 4) FVS_LR(true, 4); else if (wpl <= 8) FVS_LR(true, 8); else FVS_LR(true, 12);
+    } else {
+        if (wpl <= 4) FVS_LR(false, 4); else if (wpl <= 8) FVS_LR(false, 8); else FVS_LR(false, 12);
+    }
+#undef FVS_LR
     return fvs_launch_status();
 }

@@ -27,7 +27,21 @@ __global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* 
     for (int c = tid; c < NC; c += nt) keys[c] = (h2o(row[c]) << 16) | (uint32_t)(0xffff - c);
     if (tid == 0) s_fill = 0;
     __syncthreads();
-    const uint32_t T = block_select_rth_largest<32, uint32_t>([&](int i) { return keys[i]; }, NC, nprobe, ss);
+    // the nprobe-th largest score (16-bit order key, two radix passes); the cell half of the key only where scores
+    // tied with it straddle the cut
+    const uint32_t Th = block_select_rth_largest<16, uint32_t>([&](int i) { return keys[i] >> 16; }, NC, nprobe, ss);
+    int gt = 0, eq = 0;
+    for (int c = tid; c < NC; c += nt) {
+        gt += (keys[c] >> 16) > Th;
+        eq += (keys[c] >> 16) == Th;
+    }
+    __shared__ int s_red[32];
+    gt = block_sum_int(gt, s_red);
+    eq = block_sum_int(eq, s_red);
+    uint32_t T = Th << 16;
+    if (eq > nprobe - gt)
+        T |= block_select_rth_largest<16, uint32_t>(
+            [&](int i) { return (keys[i] >> 16) == Th ? (keys[i] & 0xffffu) : 0u; }, NC, nprobe - gt, ss);
     for (int c = tid; c < NC; c += nt)
         if (keys[c] >= T) {
             const int slot = atomicAdd(&s_fill, 1);
@@ -35,7 +49,8 @@ __global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* 
         }
     for (int i = nprobe + tid; i < kp; i += nt) sb[i] = 0ull;
     __syncthreads();
-    block_bitonic_desc(sb, kp);
+    if (tid < 32) warp_bitonic_desc(sb, kp);  // <= a few hundred entries: one warp, no block barriers
+    __syncthreads();
     for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = 0xffff - (int64_t)(sb[i] & 0xffffu);
 }
 

@@ -342,8 +342,11 @@ constexpr int TG_MAXT = 8;
 struct TieredSet {
     int T, nbytes;  // nbytes: byte positions per candidate over all tiers = D / 8
     int s[TG_MAXT], kb[TG_MAXT], bits[TG_MAXT], cboff[TG_MAXT], pbase[TG_MAXT + 1];
+    int toff[TG_MAXT];  // byte offset of the tier in a packed record (sum of the earlier tiers' b * KB)
     const uint8_t* planes[TG_MAXT];
     const float* cb[TG_MAXT];
+    const uint8_t* rec;  // packed records [N, RB] (`src/tiered_fused.py:112-125`), or null: separate planes
+    int RB, soff;
 };
 
 // codes of the 8 coordinates of one byte position from NB bit planes, as 8 bytes (lo: coordinates 0-3, hi: 4-7):
@@ -379,7 +382,7 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
     __shared__ float s_qn2[TG_MAXT];
     __shared__ float s_scl[8][TG_MAXT];  // per warp: this candidate's scale of every tier
     __shared__ const uint8_t* s_planes[TG_MAXT];
-    __shared__ int s_s[TG_MAXT], s_kb[TG_MAXT], s_bits[TG_MAXT], s_cbo[TG_MAXT], s_pbase[TG_MAXT];
+    __shared__ int s_s[TG_MAXT], s_kb[TG_MAXT], s_bits[TG_MAXT], s_cbo[TG_MAXT], s_pbase[TG_MAXT], s_toff[TG_MAXT];
     float* zqk = reinterpret_cast<float*>(smem);  // D, interleaved per tier
     float* cbs = zqk + D;                         // sum_t 2^b_t
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
@@ -390,6 +393,7 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
         s_bits[tid] = ts.bits[tid];
         s_cbo[tid] = ts.cboff[tid];
         s_pbase[tid] = ts.pbase[tid];
+        s_toff[tid] = ts.toff[tid];
     }
     __syncthreads();
     uint8_t* ptier = reinterpret_cast<uint8_t*>(cbs + ts.cboff[ts.T - 1] + (1 << ts.bits[ts.T - 1]));  // nbytes
@@ -419,16 +423,25 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
     const float qn2l = s_qn2[tl];
     for (int i = warp; i < K; i += nw) {
         const int64_t n = pos[(int64_t)q * K + i];
-        const float scl = lane < ts.T ? __half2float(scale[(int64_t)lane * N + n]) : 0.f;
-        const float sgl = lane < ts.T ? __half2float(sig[(int64_t)lane * N + n]) : 0.f;
+        float scl = 0.f, sgl = 0.f;
+        if (lane < ts.T) {
+            if (ts.rec) {
+                const uint32_t sp = __ldg(reinterpret_cast<const uint32_t*>(ts.rec + n * ts.RB + ts.soff) + lane);
+                scl = __half2float(__ushort_as_half((unsigned short)(sp & 0xffffu)));
+                sgl = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
+            } else {
+                scl = __half2float(scale[(int64_t)lane * N + n]);
+                sgl = __half2float(sig[(int64_t)lane * N + n]);
+            }
+        }
         if (lane < ts.T) s_scl[warp][lane] = scl;
         __syncwarp();
         float part = 0.f;
         for (int gp = lane; gp < ts.nbytes; gp += 32) {
             const int t = ptier[gp];
             const int j = gp - s_pbase[t], b = s_bits[t], kb = s_kb[t];
-            const uint8_t* pb = s_planes[t] + n * kb + j;
-            const int64_t pstride = N * kb;
+            const uint8_t* pb = ts.rec ? ts.rec + n * ts.RB + s_toff[t] + j : s_planes[t] + n * kb + j;
+            const int64_t pstride = ts.rec ? (int64_t)kb : N * kb;
             const float* cbt = cbs + s_cbo[t];
             const float* z = zqk + s_s[t] + j;
             float a;
@@ -623,6 +636,38 @@ extern "C" int fvs_trellis_scan_small(fvs_stream_t stream, int mode, const float
     return fvs_launch_status();
 }
 
+namespace fvs {
+static int make_tiered_set(TieredSet& ts, int T, int D, const int32_t* tier_s, const int32_t* tier_e,
+                           const int32_t* tier_bits, const float* const* tier_cb, const uint8_t* const* tier_planes,
+                           const uint8_t* rec, int RB, int soff) {
+    if (T < 1 || T > TG_MAXT) return FVS_ERANGE;
+    ts.T = T;
+    int pb = 0, cbo = 0, to = 0;
+    for (int t = 0; t < T; t++) {
+        FVS_CHECK_ARG(tier_e[t] > tier_s[t] && (tier_e[t] - tier_s[t]) % 8 == 0 && tier_e[t] <= D);
+        FVS_CHECK_ARG(tier_bits[t] >= 1 && tier_bits[t] <= 8 && tier_cb[t] && (rec || tier_planes[t]));
+        ts.s[t] = tier_s[t];
+        ts.kb[t] = (tier_e[t] - tier_s[t]) / 8;
+        ts.bits[t] = tier_bits[t];
+        ts.planes[t] = tier_planes ? tier_planes[t] : nullptr;
+        ts.cb[t] = tier_cb[t];
+        ts.cboff[t] = cbo;
+        cbo += 1 << tier_bits[t];
+        ts.pbase[t] = pb;
+        pb += ts.kb[t];
+        ts.toff[t] = to;
+        to += tier_bits[t] * ts.kb[t];
+    }
+    ts.pbase[T] = pb;
+    ts.nbytes = pb;
+    ts.rec = rec;
+    ts.RB = RB;
+    ts.soff = soff;
+    if (rec) FVS_CHECK_ARG(soff == to && soff + 4 * T <= RB && RB % 4 == 0 && ((uintptr_t)rec & 3) == 0);
+    return FVS_OK;
+}
+}  // namespace fvs
+
 extern "C" int fvs_tiered_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
                                 int ldz, int D, int T, const int32_t* tier_s, const int32_t* tier_e,
                                 const int32_t* tier_bits, const float* const* tier_cb,
@@ -632,23 +677,9 @@ extern "C" int fvs_tiered_score(fvs_stream_t stream, const int64_t* pos, int B, 
     FVS_CHECK_ARG(B >= 0 && K >= 1 && N > 0 && D > 0 && ldz >= D);
     if (T < 1 || T > fvs::TG_MAXT) return FVS_ERANGE;
     fvs::TieredSet ts;
-    ts.T = T;
-    int pb = 0, cbo = 0;
-    for (int t = 0; t < T; t++) {
-        FVS_CHECK_ARG(tier_e[t] > tier_s[t] && (tier_e[t] - tier_s[t]) % 8 == 0 && tier_e[t] <= D);
-        FVS_CHECK_ARG(tier_bits[t] >= 1 && tier_bits[t] <= 8 && tier_cb[t] && tier_planes[t]);
-        ts.s[t] = tier_s[t];
-        ts.kb[t] = (tier_e[t] - tier_s[t]) / 8;
-        ts.bits[t] = tier_bits[t];
-        ts.planes[t] = tier_planes[t];
-        ts.cb[t] = tier_cb[t];
-        ts.cboff[t] = cbo;
-        cbo += 1 << tier_bits[t];
-        ts.pbase[t] = pb;
-        pb += ts.kb[t];
-    }
-    ts.pbase[T] = pb;
-    ts.nbytes = pb;
+    int rc = fvs::make_tiered_set(ts, T, D, tier_s, tier_e, tier_bits, tier_cb, tier_planes, nullptr, 0, 0);
+    if (rc) return rc;
+    const int pb = ts.nbytes, cbo = ts.cboff[T - 1] + (1 << ts.bits[T - 1]);
     const size_t sm = (size_t)(D + cbo) * 4 + (size_t)((pb + 15) & ~15);
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
@@ -684,5 +715,24 @@ extern "C" int fvs_viterbi_encode(fvs_stream_t stream, const float* Zs, int n, i
     cudaError_t e = fvs_ensure_smem((const void*)fvs::viterbi_kernel, sm);
     if (e != cudaSuccess) return (int)e;
     fvs::viterbi_kernel<<<n, 256, sm, stream>>>(Zs, n, R, vals, L, path);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_tiered_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc,
+                                    const float* Zq, int ldz, int D, int T, const int32_t* tier_s,
+                                    const int32_t* tier_e, const int32_t* tier_bits, const float* const* tier_cb,
+                                    const uint8_t* rec, int RB, int soff, int64_t N, float* est, float* sd) {
+    FVS_CHECK_ARG(pos && qc && Zq && tier_s && tier_e && tier_bits && tier_cb && rec && est && sd);
+    FVS_CHECK_ARG(B >= 0 && K >= 1 && N > 0 && D > 0 && ldz >= D);
+    fvs::TieredSet ts;
+    int rc = fvs::make_tiered_set(ts, T, D, tier_s, tier_e, tier_bits, tier_cb, nullptr, rec, RB, soff);
+    if (rc) return rc;
+    const int pb = ts.nbytes, cbo = ts.cboff[T - 1] + (1 << ts.bits[T - 1]);
+    const size_t sm = (size_t)(D + cbo) * 4 + (size_t)((pb + 15) & ~15);
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::tiered_score_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    fvs::tiered_score_kernel<<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, ts, nullptr, nullptr, N, est, sd);
     return fvs_launch_status();
 }

@@ -44,7 +44,7 @@ class IndexI8:
     H16  : fp16 full-precision store [N, d] in original-id order (HBM-resident here; pinned host RAM in the reference)
     """
 
-    def __init__(self, s1, i8, code, H16, device="cuda"):
+    def __init__(self, s1, i8, code, H16, device="cuda", packed=True):
         dev = torch.device(device)
         self.device = dev
         f = lambda x, dt=None: torch.as_tensor(x).to(device=dev, dtype=dt).contiguous()
@@ -92,6 +92,11 @@ class IndexI8:
         self._ts_b = _lib.i32_array([b for _, _, b in self.TS])
         self._ts_d = _lib.f32_array(self.deltas)
         self._ts_p = _lib.ptr_array(self.planes)
+        # packed refinement records (one coalesced row per candidate in stage 2), the reference's `tiered_fused.pack`
+        self.rec = None
+        if packed:
+            from .index_build import pack_records
+            self.rec, self.RB, self.soff, _ = pack_records(self.TS, self.planes, self.scale, self.sig)
 
     def nbytes_per_vector(self):
         return self.R + 4 + sum((e - s) * b for s, e, b in self.TS) / 8 + 4 * self.T
@@ -284,9 +289,14 @@ class EngineB200I8:
         B, K = pos.shape
         est = torch.empty(B, K, device=pos.device)
         sd = torch.empty(B, K, device=pos.device)
-        self._call("lut_score", self.L.fvs_lut_score_zq, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D, int(half),
-                   ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N, ptr(ncnt),
-                   ptr(est), ptr(sd))
+        if ix.rec is not None:
+            self._call("lut_score", self.L.fvs_lut_score_rec, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D,
+                       int(half), ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ptr(ix.rec), ix.RB, ix.soff, ix.N,
+                       ptr(ncnt), ptr(est), ptr(sd))
+        else:
+            self._call("lut_score", self.L.fvs_lut_score_zq, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D,
+                       int(half), ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig),
+                       ix.N, ptr(ncnt), ptr(est), ptr(sd))
         return est, sd
 
     def rotated_query(self, Qb):

@@ -27,7 +27,7 @@ class IndexS:
     H16  : fp16 full-precision store [N, d] in original-id order
     """
 
-    def __init__(self, s1, code, H16, device="cuda", L=10):
+    def __init__(self, s1, code, H16, device="cuda", L=10, packed=True):
         dev = torch.device(device)
         self.device = dev
         f = lambda x, dt=None: torch.as_tensor(x).to(device=dev, dtype=dt).contiguous()
@@ -65,6 +65,10 @@ class IndexS:
         self._ts_b = _lib.i32_array([b for _, _, b in self.TS])
         self._ts_cb = _lib.ptr_array(self.cbf)
         self._ts_p = _lib.ptr_array(self.planes)
+        self.rec = None
+        if packed:
+            from .index_build import pack_records
+            self.rec, self.RB, self.soff, _ = pack_records(self.TS, self.planes, self.scale, self.sig)
 
     def nbytes_per_vector(self):
         return 4 * self.W + 2 + sum((e - s) * b for s, e, b in self.TS) / 8 + 4 * self.T
@@ -188,9 +192,14 @@ class EngineB200S(EngineB200I8):
         B, K = pos.shape
         est = torch.empty(B, K, device=pos.device)
         sd = torch.empty(B, K, device=pos.device)
-        self._call("tiered_score", self.L.fvs_tiered_score, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D, ix.T,
-                   ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_cb, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N, ptr(est),
-                   ptr(sd))
+        if ix.rec is not None:
+            self._call("tiered_score", self.L.fvs_tiered_score_rec, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1],
+                       ix.D, ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_cb, ptr(ix.rec), ix.RB, ix.soff, ix.N, ptr(est),
+                       ptr(sd))
+        else:
+            self._call("tiered_score", self.L.fvs_tiered_score, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D,
+                       ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_cb, ix._ts_p, ptr(ix.scale), ptr(ix.sig), ix.N,
+                       ptr(est), ptr(sd))
         return est, sd
 
     def _finish_s(self, Qb, QC, pos, z, k):

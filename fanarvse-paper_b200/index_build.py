@@ -353,3 +353,24 @@ def build_trellis(X16, s1, R=256, L=10, seed=0, chunk=65536):
             fip = (Zs * Y).sum(1) / (yn * R ** 0.5)
             scale1[j:j + n] = (nz / (fip * yn)).half()
     return dict(W1=W1, tab=tab, alpha=alpha, words=words, scale1=scale1, L=L)
+
+
+def pack_records(TS, planes, scale, sig):
+    """Packed refinement records, the layout of the reference's `tiered_fused.pack` (`src/tiered_fused.py:112-125`):
+    [N, RB] uint8, tier t plane p at byte toff[t] + p*KB_t (KB_t = (e-s)/8), then the fp16 (scale, sigma) pair of
+    every tier at soff + 4t; RB rounded up to 64 bytes.  Built on the device of the planes.  Returns
+    (rec, RB, soff, toff)."""
+    N = planes[0].shape[1]
+    toff, o = [], 0
+    for s, e, b in TS:
+        toff.append(o)
+        o += b * (e - s) // 8
+    soff = o
+    RB = (o + 4 * len(TS) + 63) // 64 * 64
+    rec = torch.zeros(N, RB, dtype=torch.uint8, device=planes[0].device)
+    for t, (s, e, b) in enumerate(TS):
+        KB = (e - s) // 8
+        rec[:, toff[t]:toff[t] + b * KB] = planes[t].permute(1, 0, 2).reshape(N, b * KB)
+    ss = torch.stack([scale.to(torch.float16), sig.to(torch.float16)], 2)          # [T, N, 2]
+    rec[:, soff:soff + 4 * len(TS)] = ss.permute(1, 0, 2).contiguous().view(torch.uint8).reshape(N, 4 * len(TS))
+    return rec, RB, soff, toff

@@ -268,6 +268,26 @@ int fvs_dense_scan_tc(fvs_stream_t stream, int mode, const int8_t* q8, const flo
 int fvs_rth_largest(fvs_stream_t stream, const float* vals, int B, int n, int64_t ld, int r, float* out);
 
 /*
+ * fvs_lut_score_zq reading each candidate from its packed record instead of the separate planes / scale / sig arrays:
+ * rec [N, RB] uint8 as `tiered_fused.pack` (`src/tiered_fused.py:112-125`) lays it out -- tier t plane p at byte
+ * toff[t] + p * KB_t, then fp16 (scale, sigma) per tier at soff + 4t, RB a multiple of 16 (64 in the reference).  One
+ * coalesced row read per candidate; same arithmetic and results as fvs_lut_score_zq.
+ */
+int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
+                      int ldz, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e,
+                      const int32_t* tier_bits, const float* tier_delta, const uint8_t* rec, int RB, int soff,
+                      int64_t N, const int32_t* ncnt, float* est, float* sd);
+
+/*
+ * fvs_tiered_score reading each candidate from its packed record (layout as fvs_lut_score_rec; the reference's
+ * `score_rec` / `_tiered_score_rec`, `src/tiered_fused.py:74-111, 127-142`).
+ */
+int fvs_tiered_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
+                         int ldz, int D, int T, const int32_t* tier_s, const int32_t* tier_e,
+                         const int32_t* tier_bits, const float* const* tier_cb, const uint8_t* rec, int RB, int soff,
+                         int64_t N, float* est, float* sd);
+
+/*
  * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
  * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.
  */

@@ -375,3 +375,25 @@ def test_in_graph_recompute(eng, msz):
     np.testing.assert_array_equal(c(I)[in_graph][sameb], fb["I"][:len(in_graph)][sameb])
     I2, _, _ = E.search(Q, K, z, nprobe, k)
     np.testing.assert_array_equal(c(I2), c(I))
+
+
+def test_packed_records_match_planes(golden_i8, eng):
+    """stage 2 from packed records (one row per candidate) equals stage 2 from the separate planes, bit for bit"""
+    f = golden_i8
+    E, ix, idx, K, nprobe, k, M = _golden_engine(eng, f, "A_")
+    assert ix.rec is not None
+    B = int(f["A_nq"])
+    Q = torch.from_numpy(f["Q"][:B]).to(DEV)
+    QC = (Q @ ix.c).contiguous()
+    g = torch.Generator().manual_seed(5)
+    pos = torch.randint(0, ix.N, (B, K), generator=g).to(DEV)
+    Zq = E.rotated_query(Q)
+    ncnt = torch.randint(1, K + 1, (B,), generator=g, dtype=torch.int32).to(DEV)
+    for half in (True, False):
+        for nc in (None, ncnt):
+            a = E.score_lut_zq(QC, pos, Zq, nc, half)
+            rec, ix.rec = ix.rec, None
+            b = E.score_lut_zq(QC, pos, Zq, nc, half)
+            ix.rec = rec
+            np.testing.assert_array_equal(c(a[0]), c(b[0]))
+            np.testing.assert_array_equal(c(a[1]), c(b[1]))

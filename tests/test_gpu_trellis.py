@@ -295,3 +295,20 @@ def test_small_batch_matches_oracle_synthetic(ec, synth_index, B):
         for j in bad:
             a, b = sc[int(Ip[r, j])], sc[int(ref["I"][r, j])]
             assert abs(a - b) <= 1e-5 * (1 + abs(b)), (r, j, a, b)
+
+
+def test_packed_records_match_planes_tiered(gt, ec):
+    f = gt
+    ix = _index(ec, f)
+    E = ec.EngineB200S(ix)
+    assert ix.rec is not None
+    Q = torch.from_numpy(f["Q"]).to(DEV)
+    pos = torch.from_numpy(f["k_pos"]).to(DEV)
+    QC = torch.from_numpy(f["k_QC"]).to(DEV)
+    Zq = E.rotated_query(Q)
+    a = E.score_tiered(QC, pos, Zq)
+    rec, ix.rec = ix.rec, None
+    b = E.score_tiered(QC, pos, Zq)
+    ix.rec = rec
+    np.testing.assert_array_equal(c(a[0]), c(b[0]))
+    np.testing.assert_array_equal(c(a[1]), c(b[1]))
