@@ -13,7 +13,10 @@ namespace fvs {
 
 __device__ __forceinline__ uint32_t h2o(uint16_t u) { return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u); }
 
-constexpr int RT_THREADS = 512;
+#ifndef FVS_RT_THREADS
+#define FVS_RT_THREADS 512
+#endif
+constexpr int RT_THREADS = FVS_RT_THREADS;
 
 __global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* __restrict__ QM, int NC, int nprobe,
                                                                 int kp, int64_t* __restrict__ probe) {
@@ -47,11 +50,21 @@ __global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* 
             const int slot = atomicAdd(&s_fill, 1);
             if (slot < nprobe) sb[slot] = keys[c];
         }
-    for (int i = nprobe + tid; i < kp; i += nt) sb[i] = 0ull;
     __syncthreads();
-    if (tid < 32) warp_bitonic_desc(sb, kp);  // <= a few hundred entries: one warp, no block barriers
-    __syncthreads();
-    for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = 0xffff - (int64_t)(sb[i] & 0xffffu);
+    if (nprobe <= 1024) {
+        // order by rank (keys are unique): entry i goes to place #{keys greater than it}; no sorting network
+        for (int i = tid; i < nprobe; i += nt) {
+            const unsigned long long ki = sb[i];
+            int rank = 0;
+            for (int j = 0; j < nprobe; j++) rank += sb[j] > ki;
+            probe[(int64_t)q * nprobe + rank] = 0xffff - (int64_t)(ki & 0xffffu);
+        }
+    } else {
+        for (int i = nprobe + tid; i < kp; i += nt) sb[i] = 0ull;
+        __syncthreads();
+        block_bitonic_desc(sb, kp);
+        for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = 0xffff - (int64_t)(sb[i] & 0xffffu);
+    }
 }
 
 __global__ void pair_hist_kernel(const int64_t* __restrict__ probe, int B, int nprobe, int ncols,

@@ -134,17 +134,35 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
         for (int i = K + tid; i < Kp; i += nt) sb[i] = 0ull;
         __syncthreads();
     }
-    block_bitonic_desc(sb, Kp);
-    for (int i = tid; i < K; i += nt) {
-        const unsigned long long k = sb[i];
-        est1[(int64_t)q * K + i] = o2f((uint32_t)(k >> 32));
-        pos[(int64_t)q * K + i] = (int64_t)(0xffffffffu - (uint32_t)k);
+    __shared__ float s_dval;
+    if (K <= 1024) {
+        // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal); no
+        // sorting network
+        for (int i = tid; i < K; i += nt) {
+            const unsigned long long ki = sb[i];
+            int rank = 0;
+            for (int j = 0; j < K; j++) {
+                const unsigned long long kj = sb[j];
+                rank += (kj > ki) || (kj == ki && j < i);
+            }
+            est1[(int64_t)q * K + rank] = o2f((uint32_t)(ki >> 32));
+            pos[(int64_t)q * K + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+            if (rank == didx) s_dval = o2f((uint32_t)(ki >> 32));
+        }
+    } else {
+        block_bitonic_desc(sb, Kp);
+        for (int i = tid; i < K; i += nt) {
+            const unsigned long long k = sb[i];
+            est1[(int64_t)q * K + i] = o2f((uint32_t)(k >> 32));
+            pos[(int64_t)q * K + i] = (int64_t)(0xffffffffu - (uint32_t)k);
+        }
+        if (tid == 0 && ncnt != nullptr) s_dval = o2f((uint32_t)(sb[didx] >> 32));
     }
     if (tid == 0) ok[q] = (c >= K && c <= M) ? 1 : 0;
     if (ncnt != nullptr) {
         if (tid == 0) s_ncnt = 0;
         __syncthreads();
-        const float thr = __fsub_rn(o2f((uint32_t)(sb[didx] >> 32)), delta);
+        const float thr = __fsub_rn(s_dval, delta);
         int m = 0;
         for (int i = tid; i < K; i += nt) m += o2f((uint32_t)(sb[i] >> 32)) >= thr;
         atomicAdd(&s_ncnt, m);
@@ -301,6 +319,21 @@ __global__ void merge_kernel(const int64_t* __restrict__ ids_g, const float* __r
         }
     }
     __syncthreads();
+    if (n <= 1024) {  // place the k best by rank (ties of equal keys by index), no sorting network
+        for (int i = tid; i < n; i += nt) {
+            const unsigned long long ki = sb[i];
+            int rank = 0;
+            for (int j = 0; j < n; j++) {
+                const unsigned long long kj = sb[j];
+                rank += (kj > ki) || (kj == ki && j < i);
+            }
+            if (rank < k) {
+                I[(int64_t)q * k + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+                if (S) S[(int64_t)q * k + rank] = o2f((uint32_t)(ki >> 32));
+            }
+        }
+        return;
+    }
     block_bitonic_desc(sb, Kp);
     for (int i = tid; i < k; i += nt) {
         const unsigned long long key = sb[i];

@@ -498,6 +498,16 @@ __global__ void __launch_bounds__(512) route_topk_scaled_kernel(const __half* __
             const int slot = atomicAdd(&s_fill, 1);
             if (slot < nprobe) sb[slot] = keys[c];
         }
+    __syncthreads();
+    if (nprobe <= 1024) {  // unique keys: place each by its rank, no sorting network
+        for (int i = tid; i < nprobe; i += nt) {
+            const unsigned long long ki = sb[i];
+            int rank = 0;
+            for (int j = 0; j < nprobe; j++) rank += sb[j] > ki;
+            probe[(int64_t)q * nprobe + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+        }
+        return;
+    }
     for (int i = nprobe + tid; i < kp; i += nt) sb[i] = 0ull;
     __syncthreads();
     block_bitonic_desc(sb, kp);
