@@ -41,8 +41,20 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
     }
     if (tid == 0) s_namb = 0;
     __syncthreads();
-    // (k+1)-th largest hi on warp 0, k-th largest lo on warp 1
-    if (warp == 0) {
+    // (k+1)-th largest hi, k-th largest lo: by ranks when K is small (one pass, every thread), else warp selects
+    if (K <= 1024) {
+        for (int i = tid; i < K; i += nt) {
+            const uint32_t hi = khi[i], lo = klo[i];
+            int rh = 0, rl = 0;
+            for (int j = 0; j < K; j++) {
+                const uint32_t hj = khi[j], lj = klo[j];
+                rh += (hj > hi) || (hj == hi && j < i);
+                rl += (lj > lo) || (lj == lo && j < i);
+            }
+            if (rh == k) s_bounds[0] = hi;
+            if (rl == k - 1) s_bounds[1] = lo;
+        }
+    } else if (warp == 0) {
         const uint32_t v = warp_select_rth_largest<32, uint32_t>([&](int i) { return khi[i]; }, K, k + 1, hist[0]);
         if (lane == 0) s_bounds[0] = v;
     } else if (warp == 1) {
@@ -80,8 +92,24 @@ __global__ void __launch_bounds__(REF_THREADS) refine_kernel(const __half* __res
         if (lane == 0) score[i] = acc;
     }
     __syncthreads();
-    // final top-k by (score desc, id asc) on warp 0: the k-th largest score key, then id order among ties
-    if (warp == 0) {
+    // final top-k by (score desc, id asc): by ranks when K is small (ties of equal keys by index), else on warp 0 the
+    // k-th largest score key, then id order among ties
+    if (K <= 1024) {
+        for (int i = tid; i < K; i += nt) {
+            const unsigned long long ki =
+                ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
+            int r = 0;
+            for (int j = 0; j < K && r < k; j++) {
+                const unsigned long long kj =
+                    ((unsigned long long)f2o(score[j]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[j]);
+                r += (kj > ki) || (kj == ki && j < i);
+            }
+            if (r < k) {
+                I[(int64_t)q * k + r] = cid[i];
+                if (score_k) score_k[(int64_t)q * k + r] = score[i];
+            }
+        }
+    } else if (warp == 0) {
         auto key = [&](int i) {
             return ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
         };
