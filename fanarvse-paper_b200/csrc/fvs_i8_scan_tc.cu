@@ -253,32 +253,51 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                     if (nb_g % GATHER_WARPS != gw) continue;
                     const int s = nb_g % B_STAGES;
                     const int st = nb_g % T_STAGES;
+                    const int nq = min(QN, qn - i * QN);
+                    const int n16 = (nq + 15) & ~15;
+                    // the sub-tile's scalars are loaded before waiting for its slots (they do not depend on them), so
+                    // their latency overlaps the wait: row scales (rows outside the cell read as 0), query ids, then
+                    // the per-query scale / pair constant / threshold
+                    float zv[TILE_ROWS / 32];
+#pragma unroll
+                    for (int rr = 0; rr < TILE_ROWS / 32; rr++) {
+                        const int row = row0 + 32 * rr + lane;
+                        zv[rr] = (row >= cs && row < ce) ? p.zs[row] : 0.f;
+                    }
+                    int qq[2];
+                    float qsv[2], qcv[2], thv[2];
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++) {
+                        const int g = lane + 32 * rr;
+                        qq[rr] = -1;
+                        qsv[rr] = qcv[rr] = thv[rr] = 0.f;
+                        if (g < nq) {
+                            const int pi = qoff + i * QN + g;
+                            qq[rr] = p.qid[pi];
+                            qcv[rr] = p.qcp[pi];
+                        }
+                    }
+#pragma unroll
+                    for (int rr = 0; rr < 2; rr++)
+                        if (qq[rr] >= 0) {
+                            qsv[rr] = p.qs[qq[rr]];
+                            thv[rr] = MODE ? p.t0[qq[rr]] : 0.f;
+                        }
                     if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort) ||
                         !mbar_wait(t_empty(st), ((nb_g / T_STAGES) & 1) ^ 1, abort)) {
                         ok = false;
                         break;
                     }
-                    const int nq = min(QN, qn - i * QN);
-                    const int n16 = (nq + 15) & ~15;
-                    // row scales of the tile (rows outside the cell read as 0)
 #pragma unroll
-                    for (int rr = 0; rr < TILE_ROWS / 32; rr++) {
-                        const int row = row0 + 32 * rr + lane;
-                        zsm[st * TILE_ROWS + 32 * rr + lane] = (row >= cs && row < ce) ? p.zs[row] : 0.f;
-                    }
-                    int qq[2];
+                    for (int rr = 0; rr < TILE_ROWS / 32; rr++) zsm[st * TILE_ROWS + 32 * rr + lane] = zv[rr];
 #pragma unroll
                     for (int rr = 0; rr < 2; rr++) {
                         const int g = lane + 32 * rr;
-                        qq[rr] = -1;
                         if (g < nq) {
-                            const int pi = qoff + i * QN + g;
-                            const int q = p.qid[pi];
-                            qq[rr] = q;
-                            meta_qid[st * QN + g] = q;
-                            meta_qs[st * QN + g] = p.qs[q];
-                            meta_qc[st * QN + g] = p.qcp[pi];
-                            meta_th[st * QN + g] = MODE ? p.t0[q] : 0.f;
+                            meta_qid[st * QN + g] = qq[rr];
+                            meta_qs[st * QN + g] = qsv[rr];
+                            meta_qc[st * QN + g] = qcv[rr];
+                            meta_th[st * QN + g] = thv[rr];
                         }
                     }
 #pragma unroll
