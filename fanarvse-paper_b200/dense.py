@@ -120,6 +120,7 @@ class EngineB200Dense(EngineB200I8):
     then the throughput engine's LUT stage 2, classification, exact re-rank and final top-k.  Flagged queries rerun
     stage 1 with 4x the oversampling and a 65,536-entry buffer."""
     OVER = 2.0
+    FB_INGRAPH = 0        # flagged rows are recomputed from the host
 
     def __init__(self, index, dense: DenseB200):
         super().__init__(index)

@@ -80,6 +80,7 @@ class EngineB200S(EngineB200I8):
     flagged-row recompute are inherited from EngineB200I8."""
     M = None
     FB_M = 65536
+    FB_INGRAPH = 0        # flagged rows are recomputed from the host (no in-graph recompute on this path)
     TINY, SMALL, CAP_SMALL = 8, 32, 8192      # `EngineC.TINY/SMALL`, `search_small`/`search_mask` CAP
 
     def __init__(self, index: IndexS):
