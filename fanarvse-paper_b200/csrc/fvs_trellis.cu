@@ -20,7 +20,7 @@ constexpr int TILE_ROWS = 128;
 constexpr int QT = 64;
 constexpr int R = 256;
 constexpr int RS = R * 2 + 16;  // fp16 row stride in bytes (ldmatrix bank-conflict free)
-constexpr int NTHREADS = 128;
+constexpr int NTHREADS = 256;  // two threads decode a row; warp w: rows 32*(w%4).., queries of half w/4
 constexpr int MAXW = 16;         // words per row (R + L - 1 <= 512 bits)
 
 struct Params {
@@ -89,29 +89,34 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
         const int64_t cs = p.off[c], ce = p.off[c + 1];
         const int64_t row0 = p.tile_row0[tile];
         const int qoff = p.coff[c];
-        // ---- decode one row per thread (rows outside the cell: zeros)
+        // ---- decode: thread pair (2r, 2r+1) decodes row r, halves [0, R/2) and [R/2, R) (rows outside the cell: 0)
         {
-            const int64_t n = row0 + tid;
-            uint32_t* dst = reinterpret_cast<uint32_t*>(vt + tid * RS);
+            const int r = tid >> 1, hf = tid & 1;
+            const int64_t n = row0 + r;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(vt + r * RS) + hf * (R / 4);
             if (n >= cs && n < ce) {
-                uint32_t w[R / 32 + 1];
+                uint32_t w[R / 64 + 1];
 #pragma unroll
-                for (int i = 0; i <= R / 32; i++) w[i] = (i < W) ? p.words[n * W + i] : 0u;
+                for (int i = 0; i <= R / 64; i++) {
+                    const int wi = hf * (R / 64) + i;
+                    w[i] = (wi < W) ? p.words[n * W + wi] : 0u;
+                }
                 const uint32_t mask2 = (2u << L) - 1u;
 #pragma unroll
-                for (int wi = 0; wi < R / 32; wi++) {
+                for (int wi = 0; wi < R / 64; wi++) {
                     const unsigned long long comb = ((unsigned long long)w[wi] << 32) | w[wi + 1];
 #pragma unroll
                     for (int o = 0; o < 32; o += 2)  // states o and o+1 = the L+1 bits starting at bit o
                         dst[(wi * 32 + o) >> 1] = tab2[(uint32_t)(comb >> (64 - L - 1 - o)) & mask2];
                 }
-                ssc[tid] = __half2float(p.scale1[n]);
+                if (hf == 0) ssc[r] = __half2float(p.scale1[n]);
             } else {
-                for (int j = 0; j < R / 2; j++) dst[j] = 0u;
-                ssc[tid] = 0.f;
+                for (int j = 0; j < R / 4; j++) dst[j] = 0u;
+                if (hf == 0) ssc[r] = 0.f;
             }
         }
-        const int64_t wrow0 = row0 + 32 * warp;
+        const int rw = warp & 3, qh = warp >> 2;
+        const int64_t wrow0 = row0 + 32 * rw;
         const bool warp_active = wrow0 < ce;
         const int blk_rel = (int)(wrow0 / 32 - cs / 32);
         const int g = lane >> 2, t4 = lane & 3;
@@ -140,11 +145,12 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
                 *reinterpret_cast<uint4*>(qt + r * RS + ch * 16) = v;
             }
             __syncthreads();
-            if (!warp_active) continue;
+            const int m0 = 2 * qh;  // this warp's two 16-query m-tiles
+            if (!warp_active || m0 >= mt) continue;
 
-            float acc[4][4][4];
+            float acc[2][4][4];
 #pragma unroll
-            for (int m = 0; m < 4; m++)
+            for (int m = 0; m < 2; m++)
 #pragma unroll
                 for (int j = 0; j < 4; j++)
 #pragma unroll
@@ -154,17 +160,18 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
                 uint32_t b[4][2];
 #pragma unroll
                 for (int jp = 0; jp < 2; jp++) {
-                    const int nrow = 32 * warp + 16 * jp + (lane & 7) + ((lane >> 4) << 3);
+                    const int nrow = 32 * rw + 16 * jp + (lane & 7) + ((lane >> 4) << 3);
                     ldsm_x4(b[2 * jp][0], b[2 * jp][1], b[2 * jp + 1][0], b[2 * jp + 1][1],
                             vt + nrow * RS + kb + ((lane >> 3) & 1) * 16);
                 }
 #pragma unroll
-                for (int m = 0; m < 4; m++) {
+                for (int mm = 0; mm < 2; mm++) {
+                    const int m = m0 + mm;
                     if (m < mt) {
                         uint32_t a[4];
                         ldsm_x4(a[0], a[1], a[2], a[3], qt + (16 * m + (lane & 15)) * RS + kb + (lane >> 4) * 16);
 #pragma unroll
-                        for (int j = 0; j < 4; j++) mma_f16(acc[m][j], a, b[j][0], b[j][1]);
+                        for (int j = 0; j < 4; j++) mma_f16(acc[mm][j], a, b[j][0], b[j][1]);
                     }
                 }
             }
@@ -174,13 +181,14 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
             for (int j = 0; j < 4; j++)
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    const int r = 32 * warp + 8 * j + 2 * t4 + e;
+                    const int r = 32 * rw + 8 * j + 2 * t4 + e;
                     const int64_t n = row0 + r;
                     rv[j][e] = n >= cs && n < ce;
                     sr[j][e] = ssc[r];
                 }
 #pragma unroll
-            for (int m = 0; m < 4; m++) {
+            for (int mm = 0; mm < 2; mm++) {
+                const int m = m0 + mm;
                 if (m >= mt) break;
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
@@ -191,7 +199,7 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
 #pragma unroll
                     for (int j = 0; j < 4; j++)
 #pragma unroll
-                        for (int e = 0; e < 2; e++) est[j][e] = __fadd_rn(__fmul_rn(sr[j][e], acc[m][j][2 * h + e]), qcv);
+                        for (int e = 0; e < 2; e++) est[j][e] = __fadd_rn(__fmul_rn(sr[j][e], acc[mm][j][2 * h + e]), qcv);
                     if (MODE != 1) {
                         float mx = -INFINITY;
 #pragma unroll
@@ -235,7 +243,7 @@ __global__ void __launch_bounds__(NTHREADS) trellis_scan_kernel(Params p) {
                                         if (base < p.M) {
                                             const int64_t o = (int64_t)q * p.M + base;
                                             p.bval[o] = est[j][e];
-                                            p.bpos[o] = (int32_t)(row0 + 32 * warp + 8 * j + 2 * t4 + e);
+                                            p.bpos[o] = (int32_t)(row0 + 32 * rw + 8 * j + 2 * t4 + e);
                                         }
                                         base++;
                                     }
