@@ -47,6 +47,8 @@ SIGNATURES = {
     "fvs_rth_largest": (I32, [P, P, I32, I32, I64, I32, P]),
     "fvs_lut_score_rec": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, I32, I32, I64, P, P, P]),
     "fvs_tiered_score_rec": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, I32, I32, I64, P, P]),
+    "fvs_flagged_gather": (I32, [P, P, I32, I32, P, P, I32, P, P, P]),
+    "fvs_rows_scatter": (I32, [P, P, I32, I32, P, I32, P, P, P]),
     "fvs_exact_scores": (I32, [P, P, I32, P, I32, I32, P, I32, P]),
     "fvs_merge_topk": (I32, [P, P, P, I32, I32, I32, I32, P, P]),
 }

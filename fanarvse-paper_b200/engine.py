@@ -345,36 +345,32 @@ class EngineB200I8:
 
     def _fallback_ingraph(self, Qb, QC, QM, probe, q8, qs, ok, I, reads, ids, K, z, k):
         """The recompute of `throughput/enginei8.py:112-120` for up to FB_INGRAPH flagged rows, inside the batch's own
-        graph (no host round trip): the flagged rows are compacted on the GPU (prefix sum; unused slots point at row
-        0 and write to a discarded row), rerun from the main pass's routing and query codes with rho 1.0 (beta 1.5),
-        M 65536, fp32 LUT, no delta rule, and scattered back.  Rows beyond the capacity stay flagged for the host."""
+        graph (no host round trip): `fvs_flagged_gather` compacts the flagged rows on the GPU (stable order; unused
+        slots repeat row 0) and gathers their query, routing product, probe list and query codes; they rerun with
+        rho 1.0 (beta 1.5), M 65536, fp32 LUT, no delta rule; `fvs_rows_scatter` writes the results back and marks
+        them done.  Rows beyond the capacity stay flagged for the host."""
         B, FB, dev = len(Qb), self.FB_INGRAPH, Qb.device
-        bad = ~ok
-        self._nflag.copy_(bad.sum().to(torch.int32).reshape(1))
-        c = torch.cumsum(bad.to(torch.int32), 0)
-        slot = torch.where(bad & (c <= FB), c - 1, torch.full_like(c, FB)).long()
-        rows = torch.full((FB + 1,), B, dtype=torch.long, device=dev)
-        rows.scatter_(0, slot, torch.arange(B, device=dev))        # slot FB collects the unused rows (discarded)
-        rows = rows[:FB]
-        valid = rows < B
-        src = torch.where(valid, rows, torch.zeros_like(rows))
-        Qf = Qb[src].contiguous()
+        rows = torch.empty(FB, dtype=torch.int32, device=dev)
+        bufs = [torch.empty((FB,) + tuple(t.shape[1:]), dtype=t.dtype, device=dev) for t in (Qb, QM, probe, q8, qs, QC)]
+        srcs = [Qb, QM, probe, q8, qs, QC]
+        rb = [t[0].numel() * t.element_size() for t in srcs]
+        self._call("fallback_gather", self.L.fvs_flagged_gather, ptr(ok), B, FB, ptr(rows), ptr(self._nflag),
+                   len(srcs), _lib.ptr_array(srcs), _lib.ptr_array(bufs), _lib.i32_array(rb))
+        Qf, QMf, probef, q8f, qsf, QCf = bufs
         main_last, self._tag = self._last, "fallback_"
         try:
-            pos, okf, est1, _ = self.stage1_i8(Qf, QM[src].contiguous(), probe[src].contiguous(), K,
-                                               rho_override=1.0, M_override=65536,
-                                               q8qs=(q8[src].contiguous(), qs[src].contiguous()), small=True)
-            est, sd = self.score_lut_zq(QC[src].contiguous(), pos, self.rotated_query(Qf), None, False)
+            pos, okf, est1, _ = self.stage1_i8(Qf, QMf, probef, K, rho_override=1.0, M_override=65536,
+                                               q8qs=(q8f, qsf), small=True)
+            est, sd = self.score_lut_zq(QCf, pos, self.rotated_query(Qf), None, False)
             If, rf, idsf, _ = self.refine(Qf, pos, est, sd, z, k)
         finally:
             self._last, self._tag = main_last, ""
         self._last["fallback_rows"] = rows
-        tgt = torch.where(valid, rows, torch.full_like(rows, B))
-        I = torch.cat([I, I[:1]]).index_copy_(0, tgt, If)[:B]
-        reads = torch.cat([reads, reads[:1]]).index_copy_(0, tgt, rf.long())[:B]
-        ids = torch.cat([ids, ids[:1]]).index_copy_(0, tgt, idsf)[:B]
-        handled = torch.zeros(B + 1, dtype=torch.bool, device=dev).index_fill_(0, tgt, True)[:B]
-        return ok | handled, I, reads, ids
+        rf = rf.long()
+        outs, res = [I, reads, ids], [If, rf, idsf]
+        self._call("fallback_scatter", self.L.fvs_rows_scatter, ptr(rows), FB, B, ptr(ok), 3, _lib.ptr_array(res),
+                   _lib.ptr_array(outs), _lib.i32_array([t[0].numel() * t.element_size() for t in outs]))
+        return ok, I, reads, ids
 
     def _fallback(self, Qb, K, z, nprobe, k):
         """`throughput/enginei8.py:112-120`: rho 1.0 (beta 1.5), M 65536, fp32 LUT, no delta rule."""

@@ -288,6 +288,22 @@ int fvs_tiered_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, 
                          int64_t N, float* est, float* sd);
 
 /*
+ * Compaction of flagged rows for a recompute inside the batch's own graph (new; the reference recomputes them from the
+ * host, `throughput/enginei8.py:108-111`): rows[0..FB) = the first FB indices i with ok[i] == 0 in order (B for unused
+ * slots), *nflag = the number of flagged rows; then row rows[s] (row 0 for an unused slot) of each of the G <= 8
+ * arrays src[g] (row_bytes[g] bytes per row, a multiple of 4) is copied to row s of dst[g].  B >= 1, 1 <= FB <= 1024.
+ */
+int fvs_flagged_gather(fvs_stream_t stream, const uint8_t* ok, int B, int FB, int32_t* rows, int32_t* nflag, int G,
+                       const void* const* src, void* const* dst, const int32_t* row_bytes);
+
+/*
+ * Inverse of fvs_flagged_gather's copies: for every slot s with 0 <= rows[s] < B, row s of src[g] goes to row rows[s] of
+ * dst[g] for each array, and ok[rows[s]] = 1 (ok may be NULL).
+ */
+int fvs_rows_scatter(fvs_stream_t stream, const int32_t* rows, int FB, int B, uint8_t* ok, int G, const void* const* src,
+                     void* const* dst, const int32_t* row_bytes);
+
+/*
  * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
  * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.
  */
