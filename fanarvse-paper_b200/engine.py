@@ -390,7 +390,13 @@ class EngineB200I8:
         """`throughput/enginei8.py:96-111`: returns (I [B,k] int32, reads [B] int64, cand_ids [B,K] int32)."""
         if not Qb.is_cuda:
             raise RuntimeError("EngineB200I8.search needs CUDA queries (the B200 library has no CPU path)")
+        if K <= k:
+            raise ValueError("need K > k")
         B = len(Qb)
+        if B == 0:
+            dev = Qb.device
+            return (torch.empty(0, k, dtype=torch.int32, device=dev), torch.empty(0, dtype=torch.int64, device=dev),
+                    torch.empty(0, K, dtype=torch.int32, device=dev))
         key = (B, K, z, nprobe, k, self.knobs())
         if key not in self.graphs:
             qs = Qb.clone()
@@ -434,6 +440,8 @@ class EngineB200I8:
         if not Qb.is_cuda:
             raise RuntimeError("EngineB200I8.search_host needs CUDA queries (the B200 library has no CPU path)")
         B = len(Qb)
+        if B == 0:
+            return np.empty((0, k), np.int32)
         key = ("host", B, K, z, nprobe, k, self.knobs())
         if key not in self.graphs:
             qs = Qb.clone()

@@ -397,3 +397,17 @@ def test_packed_records_match_planes(golden_i8, eng):
             ix.rec = rec
             np.testing.assert_array_equal(c(a[0]), c(b[0]))
             np.testing.assert_array_equal(c(a[1]), c(b[1]))
+
+
+def test_empty_batch_and_argument_errors(eng):
+    """a batch of zero queries returns empty results; bad arguments raise before any device work"""
+    ds, ix, oi = _random_index(eng, 20000, 256, 64, 8, seed=17)
+    E = eng.EngineB200I8(ix)
+    Q = ds["queries"]
+    I, nr, ids = E.search(Q[:0], 40, 1.5, 12, 10)
+    assert I.shape == (0, 10) and nr.shape == (0,) and ids.shape == (0, 40)
+    with pytest.raises(ValueError):
+        E.search(Q, 10, 1.5, 12, 10)                      # K must exceed k
+    L = pkg("_lib")
+    with pytest.raises(L.FvsError):
+        E.route(Q, ix.NC + 1)                             # more probes than cells
