@@ -313,7 +313,7 @@ def variant_trellis(args, dev, steps=20):
     s1.update(ib.build_trellis(X16, s1, seed=0))
     ix = ec.IndexS(s1, codes["lloyd"], X16, dev)
     E = ec.EngineB200S(ix)
-    E.M = 16384           # emit buffer: the reference's max(4096, 16K) overflows for ~3 % of these queries
+    E.M = 65536           # emit buffer: the reference's max(4096, 16K) overflows for ~3 % of these queries
     build_s = time.time() - t0
     Q = ds["queries"]
     z, k = 2.0, 10

@@ -366,7 +366,7 @@ __device__ __forceinline__ float tier_pos_dot(const uint8_t* __restrict__ pb, in
                                               const float* __restrict__ cbt, const float* __restrict__ z, int kb) {
     uint32_t by[NB];
 #pragma unroll
-    for (int pl = 0; pl < NB; pl++) by[pl] = __ldg(pb + pl * pstride);
+    for (int pl = 0; pl < NB; pl++) by[pl] = pb[pl * pstride];  // global planes or the warp's staged record
     uint32_t lo = 0, hi = 0;
 #pragma unroll
     for (int pl = 0; pl < NB; pl++) {
@@ -429,12 +429,28 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
     const float qcv = qc[q];
     const int tl = lane < ts.T ? lane : 0;
     const float qn2l = s_qn2[tl];
+    // packed records of at most 512 bytes are staged per warp in shared memory: the next candidate's record (one
+    // coalesced 16-byte load per lane, held in registers) is in flight while the current one is scored
+    const bool staged = ts.rec && ts.RB <= 512;
+    uint8_t* wrec = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ptier + ts.nbytes) + 15) & ~uintptr_t(15)) +
+                    warp * 512;
+    uint4 nxt = make_uint4(0, 0, 0, 0);
+    if (staged && warp < K) {
+        const int64_t n0 = pos[(int64_t)q * K + warp];
+        if (lane * 16 < ts.RB) nxt = __ldg(reinterpret_cast<const uint4*>(ts.rec + n0 * ts.RB) + lane);
+        if (lane * 16 < ts.RB) *reinterpret_cast<uint4*>(wrec + lane * 16) = nxt;
+        __syncwarp();
+    }
     for (int i = warp; i < K; i += nw) {
         const int64_t n = pos[(int64_t)q * K + i];
+        const uint8_t* rb = wrec;
+        if (staged && i + nw < K && lane * 16 < ts.RB)
+            nxt = __ldg(reinterpret_cast<const uint4*>(ts.rec + pos[(int64_t)q * K + i + nw] * ts.RB) + lane);
         float scl = 0.f, sgl = 0.f;
         if (lane < ts.T) {
             if (ts.rec) {
-                const uint32_t sp = __ldg(reinterpret_cast<const uint32_t*>(ts.rec + n * ts.RB + ts.soff) + lane);
+                const uint32_t sp = staged ? reinterpret_cast<const uint32_t*>(rb + ts.soff)[lane]
+                                           : __ldg(reinterpret_cast<const uint32_t*>(ts.rec + n * ts.RB + ts.soff) + lane);
                 scl = __half2float(__ushort_as_half((unsigned short)(sp & 0xffffu)));
                 sgl = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
             } else {
@@ -448,7 +464,8 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
         for (int gp = lane; gp < ts.nbytes; gp += 32) {
             const int t = ptier[gp];
             const int j = gp - s_pbase[t], b = s_bits[t], kb = s_kb[t];
-            const uint8_t* pb = ts.rec ? ts.rec + n * ts.RB + s_toff[t] + j : s_planes[t] + n * kb + j;
+            const uint8_t* pb = staged ? rb + s_toff[t] + j
+                                       : ts.rec ? ts.rec + n * ts.RB + s_toff[t] + j : s_planes[t] + n * kb + j;
             const int64_t pstride = ts.rec ? (int64_t)kb : N * kb;
             const float* cbt = cbs + s_cbo[t];
             const float* z = zqk + s_s[t] + j;
@@ -465,7 +482,11 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
             }
             part += a * s_scl[warp][t];
         }
-        __syncwarp();
+        __syncwarp();  // every lane is done with the staged record
+        if (staged && i + nw < K) {
+            if (lane * 16 < ts.RB) *reinterpret_cast<uint4*>(wrec + lane * 16) = nxt;
+            __syncwarp();
+        }
         part = warp_sum(part);
         const float var = warp_sum(lane < ts.T ? qn2l * sgl * sgl : 0.f);
         if (lane == 0) {
@@ -746,7 +767,7 @@ extern "C" int fvs_tiered_score_rec(fvs_stream_t stream, const int64_t* pos, int
     int rc = fvs::make_tiered_set(ts, T, D, tier_s, tier_e, tier_bits, tier_cb, nullptr, rec, RB, soff);
     if (rc) return rc;
     const int pb = ts.nbytes, cbo = ts.cboff[T - 1] + (1 << ts.bits[T - 1]);
-    const size_t sm = (size_t)(D + cbo) * 4 + (size_t)((pb + 15) & ~15);
+    const size_t sm = (size_t)(D + cbo) * 4 + (size_t)pb + 16 + (RB <= 512 ? (size_t)8 * 512 : 0);
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     cudaError_t e = fvs_ensure_smem((const void*)fvs::tiered_score_kernel, sm);

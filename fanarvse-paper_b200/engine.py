@@ -408,23 +408,26 @@ class EngineB200I8:
             torch.cuda.current_stream().wait_stream(st)
             g = torch.cuda.CUDAGraph()
             n0 = self.launches
+            hflags = torch.empty(B + 2, dtype=torch.int32, pin_memory=True)
             with torch.cuda.graph(g):
                 outs = self._gpu(qs, K, z, nprobe, k)
+                # exactness flags, status word and flagged count land in pinned host memory inside the graph
+                hflags.copy_(torch.cat([outs[0].to(torch.int32), self.status, self._nflag]), non_blocking=True)
             self.graph_launches[key] = self.launches - n0
-            self.graphs[key] = (g, qs, outs)
-        g, qs, (ok, I, nr, ids) = self.graphs[key]
+            self.graphs[key] = (g, qs, outs, hflags.numpy())
+        g, qs, (ok, I, nr, ids), flags = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         I, nr, ids = I.clone(), nr.clone(), ids.clone()
-        flags = torch.cat([ok.to(torch.int32), self.status, self._nflag]).cpu()   # the only synchronisation
+        torch.cuda.current_stream().synchronize()                # the only synchronisation
         if int(flags[-2]) != 0:
             raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
         in_graph = self.FB_INGRAPH and B >= self.FB_MIN_BATCH
         if in_graph:
             self.nbad += int(flags[-1])                # recomputed inside the graph (or below, beyond capacity)
         if not bool(flags[:-2].all()):
-            bad = torch.nonzero(flags[:-2] == 0).flatten()
+            bad = torch.from_numpy(np.nonzero(flags[:-2] == 0)[0])
             if not in_graph:
                 self.nbad += len(bad)
             a, b, c = self._fallback_graphed(Qb, bad, K, z, nprobe, k)
