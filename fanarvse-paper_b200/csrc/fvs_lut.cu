@@ -12,13 +12,11 @@ namespace fvs {
 
 constexpr int MAX_TIERS = 8;
 
-constexpr int MAX_WORDS = 384;  // 12 words per lane
 struct TierSet {
     int T, nwords;  // nwords: 4-byte plane words per candidate over all tiers
     int s[MAX_TIERS], e[MAX_TIERS], bits[MAX_TIERS], kb[MAX_TIERS], loff[MAX_TIERS], wbase[MAX_TIERS + 1];
     float delta[MAX_TIERS], mid[MAX_TIERS], pw[MAX_TIERS][8];
     const uint8_t* planes[MAX_TIERS];
-    int16_t wperm[MAX_WORDS];  // word handled by slot lane + 32u: each round of 32 slots spreads the LUT blocks
 };
 
 // ------------------------------------------------------------------------------------------------ LUT build
@@ -138,14 +136,13 @@ __global__ void __launch_bounds__(256) lut_score_kernel(const int64_t* __restric
 // ------------------------------------------------------------------------------------------------ fused LUT score
 // One CTA per query: the query's table and tier sums are built in shared memory from Zq, then each warp scores
 // candidates.  A candidate's plane bytes are read as 4-byte words (every plane segment is a multiple of 4 bytes): lane
-// l owns slots l, l+32, ... of the candidate's word list (tier-major, then plane, then position), slot -> word through
-// `wperm` so that the words of one round of slots fall in different 32-coordinate blocks (table banks); it issues all
-// its loads before any lookup, and folds delta_t * 2^(b-1-p) * scale_t into its partial sum, so a candidate needs one
-// warp reduction for the estimate and one for the variance.  Two candidates are in flight per warp.
+// l owns words l, l+32, ... of the candidate's word list (tier-major, then plane, then position), issues all its loads
+// before any lookup, and folds delta_t * 2^(b-1-p) * scale_t into its partial sum, so a candidate needs one warp
+// reduction for the estimate and one for the variance.  Two candidates are in flight per warp.
 // Table layout: a plane word covers one block of 32 coordinates, ga = coordinate / 32 (tiers are contiguous 32-wide
 // groups from coordinate 0), and its byte c4 / nibble h select LUT group c = 2*c4 + h (4 coordinates).  Entry
-// (c, v, ga) sits at (c*16 + v)*GA + ga with GA a multiple of 32, so lanes holding words of different blocks read
-// different banks.  Entries are fp32 slots holding the fp16-rounded value when HALF (the reference's
+// (c, v, ga) sits at (c*16 + v)*GA + ga with GA a multiple of 32, so the 32 lanes of a warp, which hold consecutive
+// words, read 32 different banks.  Entries are fp32 slots holding the fp16-rounded value when HALF (the reference's
 // `LUTH` table), otherwise the fp32 value.
 // REC: the candidate's plane words and (scale, sigma) pairs come from its packed record (`src/tiered_fused.py:112-125`:
 // tier t plane p at byte toff[t] + p*KB_t = 4 * word index, then fp16 (scale, sigma) per tier at soff + 4t), one
@@ -219,12 +216,8 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     // per-lane word descriptors (same for every candidate): tier, plane, byte offset in the plane segment, block ga
     int wt[WPL], wp[WPL], wj[WPL], wg[WPL];
 #pragma unroll
-    int ww[WPL];
-#pragma unroll
     for (int u = 0; u < WPL; u++) {
-        const int slot = lane + 32 * u;
-        const int w = slot < ts.nwords ? ts.wperm[slot] : slot;
-        ww[u] = w;
+        const int w = lane + 32 * u;
         int t = 0;
         while (t + 1 < ts.T && w >= ts.wbase[t + 1]) t++;
         const int r = w - ts.wbase[t], wpp = ts.kb[t] / 4;
@@ -255,7 +248,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
                 if (live[c] && wt[u] >= 0) {
                     const int t = wt[u];
                     if (REC)
-                        wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(rs.rec + nn[c] * rs.RB) + ww[u]);
+                        wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(rs.rec + nn[c] * rs.RB) + lane + 32 * u);
                     else
                         wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(
                             ts.planes[t] + ((int64_t)wp[u] * N + nn[c]) * ts.kb[t] + wj[u]));
@@ -328,38 +321,6 @@ static int make_tiers(TierSet& ts, int T, const int32_t* s, const int32_t* e, co
     }
     ts.wbase[T] = w;
     ts.nwords = w;
-    if (w > MAX_WORDS) return FVS_ERANGE;
-    // slot assignment: a word's LUT column is its 32-coordinate block (bank = block mod 32 in the word-minor table),
-    // and planes of one tier share blocks, so plain word order puts up to b lanes on one bank.  Each round of 32
-    // slots takes at most one word per bank while words remain (banks with the most words left first).
-    int bucket[32][MAX_WORDS / 8 + 8], nb[32] = {0};
-    for (int x = 0; x < w; x++) {
-        int t = 0;
-        while (t + 1 < T && x >= ts.wbase[t + 1]) t++;
-        const int r = x - ts.wbase[t], wpp = ts.kb[t] / 4;
-        const int bank = (ts.s[t] / 32 + (r - (r / wpp) * wpp)) & 31;
-        if (nb[bank] >= MAX_WORDS / 8 + 8) return FVS_ERANGE;
-        bucket[bank][nb[bank]++] = x;
-    }
-    int taken[32] = {0}, slot = 0;
-    while (slot < w) {
-        int order[32];
-        for (int b = 0; b < 32; b++) order[b] = b;
-        for (int a = 0; a < 32; a++)  // banks by remaining words, descending
-            for (int b = a + 1; b < 32; b++)
-                if (nb[order[b]] - taken[order[b]] > nb[order[a]] - taken[order[a]]) {
-                    const int tmp = order[a];
-                    order[a] = order[b];
-                    order[b] = tmp;
-                }
-        const int round_end = slot + 32;
-        for (int a = 0; a < 32 && slot < round_end && slot < w; a++) {
-            const int b = order[a];
-            if (taken[b] < nb[b]) ts.wperm[slot++] = (int16_t)bucket[b][taken[b]++];
-        }
-        for (int b = 0; b < 32 && slot < round_end && slot < w; b++)  // a round short of distinct banks
-            while (taken[b] < nb[b] && slot < round_end && slot < w) ts.wperm[slot++] = (int16_t)bucket[b][taken[b]++];
-    }
     return FVS_OK;
 }
 
