@@ -65,8 +65,9 @@ constexpr int COL_OFF = LIST_OFF + 5 * MAXT * 4;           // per epilogue warp:
 constexpr int BAR_OFF = COL_OFF + 16 * 64 * 4;             // mbarriers
 constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 3 * T_STAGES;
 constexpr int MISC_OFF = BAR_OFF + NBAR * 8;               // tmem base, abort flag, list length, scan scratch
-constexpr int SMEM_BYTES = MISC_OFF + 16 + 64 + 1024;      // + alignment slack
+constexpr int SMEM_BYTES = MISC_OFF + 16 + 128 + 1024;     // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+static_assert(NTHREADS / 32 <= 32, "per-warp scratch holds 32 warps");
 
 struct Params {
     const int8_t* q8;
@@ -143,7 +144,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
     int* L_qoff = L_ce + MAXT;
     int* L_qn = L_qoff + MAXT;
     volatile int* L_len = reinterpret_cast<volatile int*>(smem + MISC_OFF + 8);
-    int* wsum = reinterpret_cast<int*>(smem + MISC_OFF + 16);  // 16 warps
+    int* wsum = reinterpret_cast<int*>(smem + MISC_OFF + 16);  // one slot per warp, up to 32 warps
     float* zsm = reinterpret_cast<float*>(smem + ZS_OFF);
     const int nlocal = ntiles > blockIdx.x ? (ntiles - blockIdx.x + G - 1) / G : 0;
 

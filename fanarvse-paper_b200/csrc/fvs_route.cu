@@ -1,9 +1,10 @@
 // Routing and pairing: the probe list of each query and the cell-sorted pair list (CSR) the scan consumes.
 //
 // fvs_route_topk replaces `QM.topk(nprobe, 1).indices` on the fp16 routing product (`throughput/enginei8.py:67-68`):
-// one CTA per query selects the nprobe largest scores with a block radix select on 32-bit keys
-// (ordered fp16 score << 16 | (65535 - cell)), so the order is (score desc, cell asc) -- the reference leaves the order
-// of equal scores to torch.topk.
+// one CTA per query selects the nprobe largest 32-bit keys (ordered fp16 score << 16 | (65535 - cell)), so the order
+// is (score desc, cell asc) -- the reference leaves the order of equal scores to torch.topk.  Up to 16384 cells the
+// keys stay in registers and the cut is found by a bitwise binary search (route_topk_reg_kernel); beyond that they are
+// staged in shared memory for a block radix select (route_topk_kernel).
 // fvs_pairs replaces `pairs_fast` (`throughput/enginei8.py:11-16`): a counting sort of the (query, cell) pairs by cell
 // (histogram, exclusive scan, atomic scatter).  Within a cell the query order is the scatter order; nothing downstream
 // depends on it (block maxima are addressed through `slot`, emitted sets are sets).
@@ -64,6 +65,83 @@ __global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* 
         __syncthreads();
         block_bitonic_desc(sb, kp);
         for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = 0xffff - (int64_t)(sb[i] & 0xffffu);
+    }
+}
+
+// Register-resident variant for NC <= 256 * 8 * V (NC a multiple of 8, 16-byte aligned rows) and nprobe <= 512: each
+// of 256 threads holds 8 * V keys loaded as 16-byte words, the nprobe-th largest key is found by a bitwise binary
+// search over the 32-bit keys (one block count per bit, the cell half only where scores tied with the cut straddle
+// it), and the selected keys are ordered by rank.  Same keys, same result as route_topk_kernel.
+constexpr int RTR_THREADS = 256;
+constexpr int RTR_MAXP = 512;
+template <int V>
+__global__ void __launch_bounds__(RTR_THREADS) route_topk_reg_kernel(const uint16_t* __restrict__ QM, int NC,
+                                                                     int nprobe, int64_t* __restrict__ probe) {
+    __shared__ int s_cnt[2][RTR_THREADS / 32];
+    __shared__ int s_fill;
+    __shared__ uint32_t s_sel[RTR_MAXP];
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint4* row = reinterpret_cast<const uint4*>(QM + (int64_t)q * NC);
+    uint32_t key[8 * V];  // 0 = no cell (real keys are >= 1: a score's order half is 0 only for the NaN 0xffff)
+#pragma unroll
+    for (int v = 0; v < V; v++) {
+        const int u = tid + v * RTR_THREADS;
+        const bool in = u * 8 < NC;
+        const uint4 w = in ? __ldg(row + u) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const uint32_t h = (ws[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+            key[8 * v + e] = in ? ((h2o((uint16_t)h) << 16) | (uint32_t)(0xffff - (u * 8 + e))) : 0u;
+        }
+    }
+    if (tid == 0) s_fill = 0;
+    int buf = 0;
+    auto count_ge = [&](uint32_t cand) {
+        int c = 0;
+#pragma unroll
+        for (int i = 0; i < 8 * V; i++) c += key[i] >= cand;
+        c = __reduce_add_sync(0xffffffffu, c);
+        if (lane == 0) s_cnt[buf][warp] = c;
+        __syncthreads();  // the other buffer is rewritten only after the next barrier, when every read of it is done
+        int tot = 0;
+#pragma unroll
+        for (int w = 0; w < RTR_THREADS / 32; w++) tot += s_cnt[buf][w];
+        buf ^= 1;
+        return tot;
+    };
+    uint32_t T = 0;
+    int cntT = -1;
+#pragma unroll 1
+    for (int bit = 31; bit >= 16; bit--) {
+        const uint32_t cand = T | (1u << bit);
+        const int c = count_ge(cand);
+        if (c >= nprobe) {
+            T = cand;
+            cntT = c;
+        }
+    }
+    if (cntT != nprobe) {
+#pragma unroll 1
+        for (int bit = 15; bit >= 0; bit--) {
+            const uint32_t cand = T | (1u << bit);
+            const int c = count_ge(cand);
+            if (c >= nprobe) T = cand;
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8 * V; i++)
+        if (key[i] != 0u && key[i] >= T) {
+            const int slot = atomicAdd(&s_fill, 1);
+            if (slot < nprobe) s_sel[slot] = key[i];
+        }
+    __syncthreads();
+    // order by rank (keys are unique): entry i goes to place #{keys greater than it}
+    for (int i = tid; i < nprobe; i += RTR_THREADS) {
+        const uint32_t ki = s_sel[i];
+        int rank = 0;
+        for (int j = 0; j < nprobe; j++) rank += s_sel[j] > ki;
+        probe[(int64_t)q * nprobe + rank] = 0xffff - (int64_t)(ki & 0xffffu);
     }
 }
 
@@ -160,6 +238,17 @@ extern "C" int fvs_route_topk(fvs_stream_t stream, const uint16_t* QM, int B, in
     FVS_CHECK_ARG(QM && probe && B >= 0 && NC > 0 && nprobe >= 1 && nprobe <= NC);
     if (NC > 65535 || nprobe > 4096) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
+    if (NC % 8 == 0 && ((uintptr_t)QM & 15) == 0 && nprobe <= fvs::RTR_MAXP) {
+        const int V = (NC + fvs::RTR_THREADS * 8 - 1) / (fvs::RTR_THREADS * 8);
+        if (V <= 8) {
+            const int Vp = V <= 1 ? 1 : V <= 2 ? 2 : V <= 4 ? 4 : 8;
+            if (Vp == 1) fvs::route_topk_reg_kernel<1><<<B, fvs::RTR_THREADS, 0, stream>>>(QM, NC, nprobe, probe);
+            if (Vp == 2) fvs::route_topk_reg_kernel<2><<<B, fvs::RTR_THREADS, 0, stream>>>(QM, NC, nprobe, probe);
+            if (Vp == 4) fvs::route_topk_reg_kernel<4><<<B, fvs::RTR_THREADS, 0, stream>>>(QM, NC, nprobe, probe);
+            if (Vp == 8) fvs::route_topk_reg_kernel<8><<<B, fvs::RTR_THREADS, 0, stream>>>(QM, NC, nprobe, probe);
+            return fvs_launch_status();
+        }
+    }
     int kp = 1;
     while (kp < nprobe) kp <<= 1;
     const size_t sm = (size_t)(NC + (NC & 1)) * 4 + (size_t)kp * 8;

@@ -254,12 +254,14 @@ def test_merge_topk(eng):
     np.testing.assert_array_equal(c(S), os_)
 
 
-def test_route_topk_ties(eng):
-    """top-n_p cells by (fp16 score desc, cell asc), also through many equal scores."""
+@pytest.mark.parametrize("NC,npr", [(4096, 352), (4093, 352), (4096, 600), (16384, 96), (8, 3), (2000, 1)])
+def test_route_topk_ties(eng, NC, npr):
+    """top-n_p cells by (fp16 score desc, cell asc), also through many equal scores; register-resident kernel
+    (NC a multiple of 8 up to 16384, n_p <= 512) and shared-memory kernel (the other shapes)."""
     L = pkg("_lib")
     lib = L.lib()
     rng = np.random.default_rng(3)
-    B, NC, npr = 37, 4096, 352
+    B = 37
     QM = (rng.integers(-200, 200, (B, NC)) / 256).astype(np.float16)     # heavy ties
     tq = torch.from_numpy(QM).to(DEV)
     probe = torch.empty(B, npr, dtype=torch.int64, device=DEV)
