@@ -104,9 +104,7 @@ __global__ void __launch_bounds__(RTR_THREADS) route_topk_reg_kernel(const uint1
         c = __reduce_add_sync(0xffffffffu, c);
         if (lane == 0) s_cnt[buf][warp] = c;
         __syncthreads();  // the other buffer is rewritten only after the next barrier, when every read of it is done
-        int tot = 0;
-#pragma unroll
-        for (int w = 0; w < RTR_THREADS / 32; w++) tot += s_cnt[buf][w];
+        const int tot = (int)__reduce_add_sync(0xffffffffu, lane < RTR_THREADS / 32 ? (unsigned)s_cnt[buf][lane] : 0u);
         buf ^= 1;
         return tot;
     };

@@ -172,6 +172,162 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
 }
 
 
+// Register-resident variant (same contract) for M <= 8192 with M a multiple of 4 and K <= 512: each of 256 threads
+// holds the order keys of 4 * W candidate scores, loaded as 16-byte words, where W (1, 2, 4 or 8 chunks of 1024 keys)
+// is the smallest that covers this query's cnt; the K-th largest score key is found by a bitwise binary search (one
+// block count per bit, starting below the common prefix of the largest and smallest key); positions are read only
+// for the keys at or above it, and where scores tied with the cut straddle it, the cut's position half comes from the
+// block radix select over those ties.
+constexpr int SELR_THREADS = 256;
+constexpr int SELR_MAXK = 512;
+constexpr int SELR_MAXM = 4 * SELR_THREADS * 8;
+struct SelRegShared {
+    SelectScratch ss;
+    int cnt[2][SELR_THREADS / 32];
+    uint32_t mx[SELR_THREADS / 32], mn[SELR_THREADS / 32];
+    int red[32];
+    int fill, ncnt;
+    float dval;
+    unsigned long long sb[SELR_MAXK];
+};
+
+// the K largest (score key, position key) pairs of the n > K candidates, unordered, into sh.sb
+template <int W>
+__device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
+                                               int K, SelRegShared& sh) {
+    constexpr int NW = SELR_THREADS / 32;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    uint32_t hk[4 * W];  // 0 = no candidate (a finite score's key is never 0)
+#pragma unroll
+    for (int v = 0; v < W; v++) {
+        const int u = tid + v * SELR_THREADS;
+        const bool in = 4 * u < n;
+        const float4 w = in ? __ldcg(reinterpret_cast<const float4*>(bv) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        hk[4 * v + 0] = in ? f2o(w.x) : 0u;
+        hk[4 * v + 1] = 4 * u + 1 < n ? f2o(w.y) : 0u;
+        hk[4 * v + 2] = 4 * u + 2 < n ? f2o(w.z) : 0u;
+        hk[4 * v + 3] = 4 * u + 3 < n ? f2o(w.w) : 0u;
+    }
+    // the cut lies between the smallest and the largest key: their common high bits are its high bits
+    uint32_t mx = 0u, mn = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < 4 * W; i++) {
+        mx = max(mx, hk[i]);
+        if (hk[i] != 0u) mn = min(mn, hk[i]);
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    mn = __reduce_min_sync(0xffffffffu, mn);
+    if (lane == 0) {
+        sh.mx[warp] = mx;
+        sh.mn[warp] = mn;
+    }
+    __syncthreads();
+    mx = __reduce_max_sync(0xffffffffu, lane < NW ? sh.mx[lane] : 0u);
+    mn = __reduce_min_sync(0xffffffffu, lane < NW ? sh.mn[lane] : 0xffffffffu);
+    int buf = 0;
+    auto count_ge = [&](uint32_t cand) {
+        int k = 0;
+#pragma unroll
+        for (int i = 0; i < 4 * W; i++) k += hk[i] >= cand;
+        k = __reduce_add_sync(0xffffffffu, k);
+        if (lane == 0) sh.cnt[buf][warp] = k;
+        __syncthreads();  // the other buffer is rewritten only after the next barrier, when its reads are done
+        const int tot = (int)__reduce_add_sync(0xffffffffu, lane < NW ? (unsigned)sh.cnt[buf][lane] : 0u);
+        buf ^= 1;
+        return tot;
+    };
+    const uint32_t diff = mx ^ mn;
+    const int top = diff ? 31 - __clz(diff) : -1;
+    uint32_t Th = top < 0 ? mx : top == 31 ? 0u : (mx & ~((2u << top) - 1u));
+    int cT = -1;
+#pragma unroll 1
+    for (int bit = top; bit >= 0; bit--) {
+        const uint32_t cand = Th | (1u << bit);
+        const int k = count_ge(cand);
+        if (k >= K) {
+            Th = cand;
+            cT = k;
+        }
+    }
+    if (cT < 0) cT = count_ge(Th);
+    uint32_t Tl = 0u;
+    if (cT > K) {
+        // scores equal to the cut straddle it: the largest position keys among them fill the remaining places
+        int gt = 0;
+#pragma unroll
+        for (int i = 0; i < 4 * W; i++) gt += hk[i] > Th;
+        gt = block_sum_int(gt, sh.red);
+        Tl = block_select_rth_largest<32, uint32_t>(
+            [&](int i) { return f2o(bv[i]) == Th ? (0xffffffffu - (uint32_t)bp[i]) : 0u; }, n, K - gt, sh.ss);
+    }
+    const unsigned long long T = ((unsigned long long)Th << 32) | Tl;
+#pragma unroll
+    for (int v = 0; v < W; v++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t h = hk[4 * v + e];
+            if (h != 0u && h >= Th) {
+                const int i = 4 * (tid + v * SELR_THREADS) + e;
+                const unsigned long long k = ((unsigned long long)h << 32) | (0xffffffffu - (uint32_t)bp[i]);
+                if (k >= T) {  // keys are unique (one entry per probed row): exactly K of them
+                    const int slot = atomicAdd(&sh.fill, 1);
+                    if (slot < K) sh.sb[slot] = k;
+                }
+            }
+        }
+}
+
+__global__ void __launch_bounds__(SELR_THREADS) select_topk_reg_kernel(
+    const float* __restrict__ bval, const int32_t* __restrict__ bpos, const int32_t* __restrict__ cnt, int M, int K,
+    int64_t* __restrict__ pos, float* __restrict__ est1, uint8_t* __restrict__ ok, int32_t* __restrict__ ncnt,
+    float delta, int didx) {
+    __shared__ SelRegShared sh;
+    const int q = blockIdx.x, tid = threadIdx.x;
+    const int c = cnt[q];
+    const int n = min(max(c, 0), M);
+    const float* bv = bval + (int64_t)q * M;
+    const int32_t* bp = bpos + (int64_t)q * M;
+    if (tid == 0) sh.fill = 0;
+    if (n <= K) {
+        const unsigned long long filler = cand_key(kNeg, 0);
+        for (int i = tid; i < K; i += SELR_THREADS) sh.sb[i] = i < n ? cand_key(bv[i], bp[i]) : filler;
+    } else {
+        const int nv = (n + 4 * SELR_THREADS - 1) / (4 * SELR_THREADS);  // uniform over the block
+        if (nv <= 1)
+            select_reg_cut<1>(bv, bp, n, K, sh);
+        else if (nv <= 2)
+            select_reg_cut<2>(bv, bp, n, K, sh);
+        else if (nv <= 4)
+            select_reg_cut<4>(bv, bp, n, K, sh);
+        else
+            select_reg_cut<8>(bv, bp, n, K, sh);
+    }
+    __syncthreads();
+    // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal)
+    for (int i = tid; i < K; i += SELR_THREADS) {
+        const unsigned long long ki = sh.sb[i];
+        int rank = 0;
+        for (int j = 0; j < K; j++) {
+            const unsigned long long kj = sh.sb[j];
+            rank += (kj > ki) || (kj == ki && j < i);
+        }
+        est1[(int64_t)q * K + rank] = o2f((uint32_t)(ki >> 32));
+        pos[(int64_t)q * K + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+        if (rank == didx) sh.dval = o2f((uint32_t)(ki >> 32));
+    }
+    if (tid == 0) ok[q] = (c >= K && c <= M) ? 1 : 0;
+    if (ncnt != nullptr) {
+        if (tid == 0) sh.ncnt = 0;
+        __syncthreads();
+        const float thr = __fsub_rn(sh.dval, delta);
+        int m = 0;
+        for (int i = tid; i < K; i += SELR_THREADS) m += o2f((uint32_t)(sh.sb[i] >> 32)) >= thr;
+        atomicAdd(&sh.ncnt, m);
+        __syncthreads();
+        if (tid == 0) ncnt[q] = sh.ncnt;
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ warp-per-query
 constexpr int WQ_WARPS = 8;  // queries per CTA in the warp-per-query kernels
 
@@ -387,6 +543,11 @@ extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int
         if (e != cudaSuccess) return (int)e;
         fvs::select_topk_warp_kernel<<<(B + fvs::WQ_WARPS - 1) / fvs::WQ_WARPS, 32 * fvs::WQ_WARPS, smw, stream>>>(
             bval, bpos, cnt, B, M, K, Kp, pos, est1, ok, ncnt, delta, delta_idx);
+        return fvs_launch_status();
+    }
+    if (K <= fvs::SELR_MAXK && M % 4 == 0 && M <= fvs::SELR_MAXM && ((uintptr_t)bval & 15) == 0) {
+        fvs::select_topk_reg_kernel<<<B, fvs::SELR_THREADS, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt,
+                                                                         delta, delta_idx);
         return fvs_launch_status();
     }
     const size_t sm = (size_t)(Kp + fvs::SEL_SMEM_KEYS) * 8;

@@ -212,15 +212,22 @@ def test_graph_search_and_fallback(eng):
     np.testing.assert_array_equal(c(I2), c(I))
 
 
-def test_select_topk_ties(eng):
-    """stage-1 top-K orders by (estimate desc, position asc), also through ties and cnt < K, cnt > M."""
+@pytest.mark.parametrize("M,K,kind", [(700, 50, "ties"), (701, 50, "ties"), (4000, 100, "ties"), (4000, 100, "cont"),
+                                       (8192, 100, "cont"), (8192, 100, "ties"), (8196, 100, "cont"),
+                                       (1400, 600, "ties")])
+def test_select_topk_ties(eng, M, K, kind):
+    """stage-1 top-K orders by (estimate desc, position asc), also through ties and cnt < K, cnt > M; register-resident
+    kernel (M a multiple of 4 up to 8192, K <= 512) and shared-memory kernel (the other shapes)."""
     L = pkg("_lib")
     lib = L.lib()
     rng = np.random.default_rng(0)
-    B, M, K = 7, 700, 50
-    vals = rng.integers(0, 20, (B, M)).astype(np.float32) / 4       # many ties
+    B = 7
+    if kind == "ties":
+        vals = rng.integers(-20, 20, (B, M)).astype(np.float32) / 4  # many ties
+    else:
+        vals = (rng.standard_normal((B, M)) * 3).astype(np.float32)
     posv = np.stack([rng.permutation(100000)[:M] for _ in range(B)]).astype(np.int32)
-    cnt = np.array([0, 10, 49, 50, 51, 700, 900], np.int32)
+    cnt = np.array([0, 10, K - 1, K, K + 1, M, M + 200], np.int32)
     tv, tp, tc = (torch.from_numpy(x).to(DEV) for x in (vals, posv, cnt))
     pos = torch.empty(B, K, dtype=torch.int64, device=DEV)
     est = torch.empty(B, K, device=DEV)
