@@ -338,16 +338,26 @@ class EngineB200I8:
         QM, probe = self.route(Qb, nprobe)
         q8, qs = self.quantize(Qb)
         pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs))
+        if not (self.FB_INGRAPH and len(Qb) >= self.FB_MIN_BATCH):
+            return self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
+        # the recompute of the flagged rows needs only the stage-1 flags: it runs on a second stream, beside the main
+        # pass's LUT and re-rank stages, and joins before its results are scattered
+        main = torch.cuda.current_stream()
+        side = self.__dict__.get("_side")
+        if side is None:
+            side = self._side = torch.cuda.Stream(device=Qb.device)
+        side.wait_stream(main)
+        with torch.cuda.stream(side):
+            fb = self._fallback_ingraph(Qb, QC, QM, probe, q8, qs, ok, K, z, k)
         out = self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
-        if self.FB_INGRAPH and len(Qb) >= self.FB_MIN_BATCH:
-            out = self._fallback_ingraph(Qb, QC, QM, probe, q8, qs, *out, K, z, k)
-        return out
+        main.wait_stream(side)
+        return self._fallback_scatter(fb, *out)
 
-    def _fallback_ingraph(self, Qb, QC, QM, probe, q8, qs, ok, I, reads, ids, K, z, k):
+    def _fallback_ingraph(self, Qb, QC, QM, probe, q8, qs, ok, K, z, k):
         """The recompute of `throughput/enginei8.py:112-120` for up to FB_INGRAPH flagged rows, inside the batch's own
         graph (no host round trip): `fvs_flagged_gather` compacts the flagged rows on the GPU (stable order; unused
         slots repeat row 0) and gathers their query, routing product, probe list and query codes; they rerun with
-        rho 1.0 (beta 1.5), M 65536, fp32 LUT, no delta rule; `fvs_rows_scatter` writes the results back and marks
+        rho 1.0 (beta 1.5), M 65536, fp32 LUT, no delta rule.  `_fallback_scatter` writes the results back and marks
         them done.  Rows beyond the capacity stay flagged for the host."""
         B, FB, dev = len(Qb), self.FB_INGRAPH, Qb.device
         rows = torch.empty(FB, dtype=torch.int32, device=dev)
@@ -365,11 +375,15 @@ class EngineB200I8:
             If, rf, idsf, _ = self.refine(Qf, pos, est, sd, z, k)
         finally:
             self._last, self._tag = main_last, ""
+        return rows, If, rf.long(), idsf
+
+    def _fallback_scatter(self, fb, ok, I, reads, ids):
+        rows, If, rf, idsf = fb
         self._last["fallback_rows"] = rows
-        rf = rf.long()
         outs, res = [I, reads, ids], [If, rf, idsf]
-        self._call("fallback_scatter", self.L.fvs_rows_scatter, ptr(rows), FB, B, ptr(ok), 3, _lib.ptr_array(res),
-                   _lib.ptr_array(outs), _lib.i32_array([t[0].numel() * t.element_size() for t in outs]))
+        self._call("fallback_scatter", self.L.fvs_rows_scatter, ptr(rows), rows.numel(), len(ok), ptr(ok), 3,
+                   _lib.ptr_array(res), _lib.ptr_array(outs),
+                   _lib.i32_array([t[0].numel() * t.element_size() for t in outs]))
         return ok, I, reads, ids
 
     def _fallback(self, Qb, K, z, nprobe, k):
