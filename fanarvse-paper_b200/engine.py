@@ -338,20 +338,25 @@ class EngineB200I8:
         QM, probe = self.route(Qb, nprobe)
         q8, qs = self.quantize(Qb)
         pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs))
-        if not (self.FB_INGRAPH and len(Qb) >= self.FB_MIN_BATCH):
-            return self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
-        # the recompute of the flagged rows needs only the stage-1 flags: it runs on a second stream, beside the main
-        # pass's LUT and re-rank stages, and joins before its results are scattered
-        main = torch.cuda.current_stream()
-        side = self.__dict__.get("_side")
-        if side is None:
-            side = self._side = torch.cuda.Stream(device=Qb.device)
-        side.wait_stream(main)
-        with torch.cuda.stream(side):
-            fb = self._fallback_ingraph(Qb, QC, QM, probe, q8, qs, ok, K, z, k)
+        fb = None
+        if self.FB_INGRAPH and len(Qb) >= self.FB_MIN_BATCH:
+            # the recompute of the flagged rows needs only the stage-1 flags: it runs on a second stream, beside the
+            # main pass's LUT and re-rank stages, and joins before its results are scattered
+            main, side = torch.cuda.current_stream(), self._side_stream(Qb.device)
+            side.wait_stream(main)
+            with torch.cuda.stream(side):
+                fb = self._fallback_ingraph(Qb, QC, QM, probe, q8, qs, ok, K, z, k)
         out = self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
+        if fb is None:
+            return out
         main.wait_stream(side)
         return self._fallback_scatter(fb, *out)
+
+    def _side_stream(self, dev):
+        side = self.__dict__.get("_side")
+        if side is None:
+            side = self._side = torch.cuda.Stream(device=dev)
+        return side
 
     def _fallback_ingraph(self, Qb, QC, QM, probe, q8, qs, ok, K, z, k):
         """The recompute of `throughput/enginei8.py:112-120` for up to FB_INGRAPH flagged rows, inside the batch's own
