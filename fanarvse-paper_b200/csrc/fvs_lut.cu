@@ -152,16 +152,19 @@ struct RecSet {
     int RB, soff;
 };
 
-template <bool HALF, int WPL, bool REC>
+// GAC: the table stride GA as a compile-time constant (32 or 64), so that a lookup's address is a shift and a mask of
+// the plane word plus an immediate; 0 = GA from the argument.
+template <bool HALF, int WPL, bool REC, int GAC>
 __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __restrict__ pos, int B, int K,
                                                            const float* __restrict__ qc, const float* __restrict__ Zq,
-                                                           int ldz, int D, int GA, TierSet ts,
+                                                           int ldz, int D, int GA_, TierSet ts,
                                                            const __half* __restrict__ scale,
                                                            const __half* __restrict__ sig, int64_t N,
                                                            const int32_t* __restrict__ ncnt, float* __restrict__ est,
                                                            float* __restrict__ sd, RecSet rs) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
+    const int GA = GAC ? GAC : GA_;
     float* lut = reinterpret_cast<float*>(smem);
     int32_t* s_pos = reinterpret_cast<int32_t*>(lut + 128 * GA);  // the query's candidate positions (K)
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
@@ -215,6 +218,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     __syncthreads();
     // per-lane word descriptors (same for every candidate): tier, plane, byte offset in the plane segment, block ga
     int wt[WPL], wp[WPL], wj[WPL], wg[WPL];
+    float wsc[WPL];  // 2^(b-1-p) * delta_t of the word's plane
 #pragma unroll
     for (int u = 0; u < WPL; u++) {
         const int w = lane + 32 * u;
@@ -225,6 +229,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
         wp[u] = r / wpp;
         wj[u] = (r - wp[u] * wpp) * 4;
         wg[u] = ts.s[t] / 32 + wj[u] / 4;
+        wsc[u] = ts.pw[t][wp[u] < 8 ? wp[u] : 0] * ts.delta[t];
     }
     const int tl = lane < ts.T ? lane : 0;
     const float dmq = ts.delta[tl] * ts.mid[tl] * s_qsum[tl], qn2l = s_qn2[tl];
@@ -282,7 +287,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
                         const uint32_t byt = (w >> (8 * bi)) & 0xffu;
                         a += lt[((2 * bi) * 16 + (byt >> 4)) * GA] + lt[((2 * bi + 1) * 16 + (byt & 15u)) * GA];
                     }
-                    part += a * (ts.pw[t][wp[u]] * ts.delta[t]) * st;
+                    part += a * wsc[u] * st;
                 }
             }
             part = warp_sum(part);
@@ -400,9 +405,9 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
     const fvs::RecSet rs{nullptr, 0, 0};
 #define FVS_LZ(H, W)                                                                                               \
     do {                                                                                                           \
-        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false>, sm);                  \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false, 0>, sm);               \
         if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W, false><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,          \
+        fvs::lut_score_zq_kernel<H, W, false, 0><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,       \
                                                                      (const __half*)scale, (const __half*)sig, N,  \
                                                                      ncnt, est, sd, rs);                           \
     } while (0)
@@ -439,12 +444,16 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const fvs::RecSet rs{rec, RB, soff};
+#define FVS_LRG(H, W, G)                                                                                           \
+    do {                                                                                                           \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true, G>, sm);                \
+        if (e != cudaSuccess) return (int)e;                                                                       \
+        fvs::lut_score_zq_kernel<H, W, true, G><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,        \
+                                                                       nullptr, nullptr, N, ncnt, est, sd, rs);    \
+    } while (0)
 #define FVS_LR(H, W)                                                                                               \
     do {                                                                                                           \
-        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true>, sm);                   \
-        if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W, true><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts, nullptr,  \
-                                                                    nullptr, N, ncnt, est, sd, rs);                \
+        if (GA == 64) FVS_LRG(H, W, 64); else if (GA == 32) FVS_LRG(H, W, 32); else FVS_LRG(H, W, 0);            \
     } while (0)
     if (half) {
         if (wpl <= 4) FVS_LR(true, 4); else if (wpl <= 8) FVS_LR(true, 8); else FVS_LR(true, 12);
@@ -452,5 +461,6 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
         if (wpl <= 4) FVS_LR(false, 4); else if (wpl <= 8) FVS_LR(false, 8); else FVS_LR(false, 12);
     }
 #undef FVS_LR
+#undef FVS_LRG
     return fvs_launch_status();
 }
