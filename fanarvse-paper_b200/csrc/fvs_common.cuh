@@ -73,6 +73,100 @@ struct SelectScratch {
     int rem;
 };
 
+// r-th largest (1-based) of the nonzero 32-bit keys held in registers, NK per thread (0 = no key; at least r nonzero
+// keys over the block).  The bits above the highest bit in which the largest and the smallest key differ are common to
+// all keys and taken as found; the rest are found MSB first, up to 8 bits per pass, from a shared-memory histogram of
+// the keys that still match the found prefix.  All threads call it and get the key; *above = #{keys > result} and
+// *equal = #{keys == result} (*equal = n when every key is the same, n unknown here: reported as INT_MAX).
+struct RegSelectScratch {
+    unsigned hist[256];
+    uint32_t mx[32], mn[32];
+    uint32_t prefix;
+    int rem, eq;
+};
+template <int NK>
+__device__ __forceinline__ uint32_t block_rth_largest_reg(const uint32_t (&k)[NK], int r, RegSelectScratch& s,
+                                                          int* above, int* equal) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+    uint32_t mx = 0u, mn = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < NK; i++) {
+        mx = max(mx, k[i]);
+        if (k[i] != 0u) mn = min(mn, k[i]);
+    }
+    mx = __reduce_max_sync(0xffffffffu, mx);
+    mn = __reduce_min_sync(0xffffffffu, mn);
+    if (lane == 0) {
+        s.mx[warp] = mx;
+        s.mn[warp] = mn;
+    }
+    __syncthreads();
+    mx = __reduce_max_sync(0xffffffffu, lane < nw ? s.mx[lane] : 0u);
+    mn = __reduce_min_sync(0xffffffffu, lane < nw ? s.mn[lane] : 0xffffffffu);
+    const uint32_t diff = mx ^ mn;
+    int shift = 32 - __clz(diff);  // bits [shift, 32) are common to every key
+    if (shift == 0) {
+        *above = 0;
+        *equal = 0x7fffffff;
+        return mx;
+    }
+    uint32_t prefix = shift == 32 ? 0u : (mx >> shift) << shift;
+    int rem = r, eq = 0;
+    while (shift > 0) {
+        const int lo = shift > 8 ? shift - 8 : 0;
+        const uint32_t dmask = (1u << (shift - lo)) - 1u;
+        for (int i = tid; i < 256; i += blockDim.x) s.hist[i] = 0u;
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < NK; i++) {
+            const uint32_t key = k[i];
+            if (key != 0u && (shift == 32 || (key >> shift) == (prefix >> shift)))
+                atomicAdd(&s.hist[(key >> lo) & dmask], 1u);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // lane l owns bins 255-8l .. 248-8l (descending)
+            unsigned c[8], sum = 0;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                c[i] = s.hist[255 - 8 * lane - i];
+                sum += c[i];
+            }
+            unsigned incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const unsigned ball = __ballot_sync(0xffffffffu, incl >= (unsigned)rem);
+            const int L = __ffs(ball) - 1;  // always found: the keys matching the prefix number >= rem
+            if (lane == L) {
+                unsigned before = incl - sum;
+                int digit = 0;
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    if (before + c[i] >= (unsigned)rem) {
+                        digit = 255 - 8 * lane - i;
+                        s.eq = (int)c[i];
+                        break;
+                    }
+                    before += c[i];
+                }
+                s.rem = rem - (int)before;
+                s.prefix = prefix | ((uint32_t)digit << lo);
+            }
+        }
+        __syncthreads();
+        prefix = s.prefix;
+        rem = s.rem;
+        eq = s.eq;
+        shift = lo;
+    }
+    *above = r - rem;
+    *equal = eq;
+    return prefix;
+}
+
 // r-th largest (1-based, 1 <= r <= n) of n keys of KBITS bits (32 or 64) produced by key(i); MSB-first radix select,
 // 8 bits per pass.  Histogram updates are aggregated per warp (lanes with the same digit add once), since the leading
 // digits of scores concentrate in one or two bins.  All threads of the block must call it; every thread gets the key.

@@ -69,18 +69,18 @@ __global__ void __launch_bounds__(RT_THREADS) route_topk_kernel(const uint16_t* 
 }
 
 // Register-resident variant for NC <= 256 * 8 * V (NC a multiple of 8, 16-byte aligned rows) and nprobe <= 512: each
-// of 256 threads holds 8 * V keys loaded as 16-byte words, the nprobe-th largest key is found by a bitwise binary
-// search over the 32-bit keys (one block count per bit, the cell half only where scores tied with the cut straddle
-// it), and the selected keys are ordered by rank.  Same keys, same result as route_topk_kernel.
+// of 256 threads holds 8 * V keys loaded as 16-byte words, the nprobe-th largest key is found by histogram passes
+// below the keys' common prefix (block_rth_largest_reg), and the selected keys are ordered by rank.  Same keys, same
+// result as route_topk_kernel.
 constexpr int RTR_THREADS = 256;
 constexpr int RTR_MAXP = 512;
 template <int V>
 __global__ void __launch_bounds__(RTR_THREADS) route_topk_reg_kernel(const uint16_t* __restrict__ QM, int NC,
                                                                      int nprobe, int64_t* __restrict__ probe) {
-    __shared__ int s_cnt[2][RTR_THREADS / 32];
+    __shared__ RegSelectScratch rs;
     __shared__ int s_fill;
     __shared__ uint32_t s_sel[RTR_MAXP];
-    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int q = blockIdx.x, tid = threadIdx.x;
     const uint4* row = reinterpret_cast<const uint4*>(QM + (int64_t)q * NC);
     uint32_t key[8 * V];  // 0 = no cell (real keys are >= 1: a score's order half is 0 only for the NaN 0xffff)
 #pragma unroll
@@ -96,37 +96,8 @@ __global__ void __launch_bounds__(RTR_THREADS) route_topk_reg_kernel(const uint1
         }
     }
     if (tid == 0) s_fill = 0;
-    int buf = 0;
-    auto count_ge = [&](uint32_t cand) {
-        int c = 0;
-#pragma unroll
-        for (int i = 0; i < 8 * V; i++) c += key[i] >= cand;
-        c = __reduce_add_sync(0xffffffffu, c);
-        if (lane == 0) s_cnt[buf][warp] = c;
-        __syncthreads();  // the other buffer is rewritten only after the next barrier, when every read of it is done
-        const int tot = (int)__reduce_add_sync(0xffffffffu, lane < RTR_THREADS / 32 ? (unsigned)s_cnt[buf][lane] : 0u);
-        buf ^= 1;
-        return tot;
-    };
-    uint32_t T = 0;
-    int cntT = -1;
-#pragma unroll 1
-    for (int bit = 31; bit >= 16; bit--) {
-        const uint32_t cand = T | (1u << bit);
-        const int c = count_ge(cand);
-        if (c >= nprobe) {
-            T = cand;
-            cntT = c;
-        }
-    }
-    if (cntT != nprobe) {
-#pragma unroll 1
-        for (int bit = 15; bit >= 0; bit--) {
-            const uint32_t cand = T | (1u << bit);
-            const int c = count_ge(cand);
-            if (c >= nprobe) T = cand;
-        }
-    }
+    int above, equal;
+    const uint32_t T = block_rth_largest_reg<8 * V>(key, nprobe, rs, &above, &equal);  // keys are unique
 #pragma unroll
     for (int i = 0; i < 8 * V; i++)
         if (key[i] != 0u && key[i] >= T) {

@@ -174,18 +174,15 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
 
 // Register-resident variant (same contract) for M <= 8192 with M a multiple of 4 and K <= 512: each of 256 threads
 // holds the order keys of 4 * W candidate scores, loaded as 16-byte words, where W (1, 2, 4 or 8 chunks of 1024 keys)
-// is the smallest that covers this query's cnt; the K-th largest score key is found by a bitwise binary search (one
-// block count per bit, starting below the common prefix of the largest and smallest key); positions are read only
-// for the keys at or above it, and where scores tied with the cut straddle it, the cut's position half comes from the
-// block radix select over those ties.
+// is the smallest that covers this query's cnt; the K-th largest score key is found by histogram passes below the
+// keys' common prefix (block_rth_largest_reg); positions are read only for the keys at or above it, and where scores
+// tied with the cut straddle it, the cut's position half comes from the block radix select over those ties.
 constexpr int SELR_THREADS = 256;
 constexpr int SELR_MAXK = 512;
 constexpr int SELR_MAXM = 4 * SELR_THREADS * 8;
 struct SelRegShared {
     SelectScratch ss;
-    int cnt[2][SELR_THREADS / 32];
-    uint32_t mx[SELR_THREADS / 32], mn[SELR_THREADS / 32];
-    int red[32];
+    RegSelectScratch rs;
     int fill, ncnt;
     float dval;
     unsigned long long sb[SELR_MAXK];
@@ -195,8 +192,7 @@ struct SelRegShared {
 template <int W>
 __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
                                                int K, SelRegShared& sh) {
-    constexpr int NW = SELR_THREADS / 32;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     uint32_t hk[4 * W];  // 0 = no candidate (a finite score's key is never 0)
 #pragma unroll
     for (int v = 0; v < W; v++) {
@@ -208,55 +204,11 @@ __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, con
         hk[4 * v + 2] = 4 * u + 2 < n ? f2o(w.z) : 0u;
         hk[4 * v + 3] = 4 * u + 3 < n ? f2o(w.w) : 0u;
     }
-    // the cut lies between the smallest and the largest key: their common high bits are its high bits
-    uint32_t mx = 0u, mn = 0xffffffffu;
-#pragma unroll
-    for (int i = 0; i < 4 * W; i++) {
-        mx = max(mx, hk[i]);
-        if (hk[i] != 0u) mn = min(mn, hk[i]);
-    }
-    mx = __reduce_max_sync(0xffffffffu, mx);
-    mn = __reduce_min_sync(0xffffffffu, mn);
-    if (lane == 0) {
-        sh.mx[warp] = mx;
-        sh.mn[warp] = mn;
-    }
-    __syncthreads();
-    mx = __reduce_max_sync(0xffffffffu, lane < NW ? sh.mx[lane] : 0u);
-    mn = __reduce_min_sync(0xffffffffu, lane < NW ? sh.mn[lane] : 0xffffffffu);
-    int buf = 0;
-    auto count_ge = [&](uint32_t cand) {
-        int k = 0;
-#pragma unroll
-        for (int i = 0; i < 4 * W; i++) k += hk[i] >= cand;
-        k = __reduce_add_sync(0xffffffffu, k);
-        if (lane == 0) sh.cnt[buf][warp] = k;
-        __syncthreads();  // the other buffer is rewritten only after the next barrier, when its reads are done
-        const int tot = (int)__reduce_add_sync(0xffffffffu, lane < NW ? (unsigned)sh.cnt[buf][lane] : 0u);
-        buf ^= 1;
-        return tot;
-    };
-    const uint32_t diff = mx ^ mn;
-    const int top = diff ? 31 - __clz(diff) : -1;
-    uint32_t Th = top < 0 ? mx : top == 31 ? 0u : (mx & ~((2u << top) - 1u));
-    int cT = -1;
-#pragma unroll 1
-    for (int bit = top; bit >= 0; bit--) {
-        const uint32_t cand = Th | (1u << bit);
-        const int k = count_ge(cand);
-        if (k >= K) {
-            Th = cand;
-            cT = k;
-        }
-    }
-    if (cT < 0) cT = count_ge(Th);
+    int gt, eq;
+    const uint32_t Th = block_rth_largest_reg<4 * W>(hk, K, sh.rs, &gt, &eq);
     uint32_t Tl = 0u;
-    if (cT > K) {
+    if (eq > K - gt) {
         // scores equal to the cut straddle it: the largest position keys among them fill the remaining places
-        int gt = 0;
-#pragma unroll
-        for (int i = 0; i < 4 * W; i++) gt += hk[i] > Th;
-        gt = block_sum_int(gt, sh.red);
         Tl = block_select_rth_largest<32, uint32_t>(
             [&](int i) { return f2o(bv[i]) == Th ? (0xffffffffu - (uint32_t)bp[i]) : 0u; }, n, K - gt, sh.ss);
     }
