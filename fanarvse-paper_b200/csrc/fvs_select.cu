@@ -172,17 +172,19 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
 }
 
 
-// Register-resident variant (same contract) for M <= 8192 with M a multiple of 4 and K <= 512: each of 256 threads
-// holds the order keys of 4 * W candidate scores, loaded as 16-byte words, where W (1, 2, 4 or 8 chunks of 1024 keys)
-// is the smallest that covers this query's cnt; the K-th largest score key is found by histogram passes below the
+// Register-resident variant (same contract) for M a multiple of 4 and K <= 256: for a query with at most 8192
+// candidates each of 256 threads holds the order keys of 4 * W candidate scores, loaded as 16-byte words, where W (1,
+// 2, 4 or 8 chunks of 1024 keys) is the smallest that covers its cnt (more candidates: radix passes over global
+// memory, select_glob_cut); the K-th largest score key is found by histogram passes below the
 // keys' common prefix (block_rth_largest_reg); positions are read only for the keys at or above it, and where scores
 // tied with the cut straddle it, the cut's position half comes from the block radix select over those ties.
 constexpr int SELR_THREADS = 256;
-constexpr int SELR_MAXK = 512;
+constexpr int SELR_MAXK = 256;  // one rank per thread (larger K: the shared-memory kernel, 512 threads)
 constexpr int SELR_MAXM = 4 * SELR_THREADS * 8;
 struct SelRegShared {
     SelectScratch ss;
     RegSelectScratch rs;
+    int red[32];
     int fill, ncnt;
     float dval;
     unsigned long long sb[SELR_MAXK];
@@ -229,7 +231,36 @@ __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, con
         }
 }
 
-__global__ void __launch_bounds__(SELR_THREADS) select_topk_reg_kernel(
+// the same for n > SELR_MAXM candidates: keys read from global memory in every radix pass
+__device__ __forceinline__ void select_glob_cut(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
+                                                int K, SelRegShared& sh) {
+    const int tid = threadIdx.x;
+    const uint32_t Th = block_select_rth_largest<32, uint32_t>([&](int i) { return f2o(bv[i]); }, n, K, sh.ss);
+    int gt = 0, eq = 0;
+    for (int i = tid; i < n; i += SELR_THREADS) {
+        const uint32_t h = f2o(bv[i]);
+        gt += h > Th;
+        eq += h == Th;
+    }
+    gt = block_sum_int(gt, sh.red);
+    eq = block_sum_int(eq, sh.red);
+    unsigned long long T = (unsigned long long)Th << 32;
+    if (eq > K - gt)
+        T |= block_select_rth_largest<32, uint32_t>(
+            [&](int i) { return f2o(bv[i]) == Th ? (0xffffffffu - (uint32_t)bp[i]) : 0u; }, n, K - gt, sh.ss);
+    for (int i = tid; i < n; i += SELR_THREADS) {
+        const float v = bv[i];
+        if (f2o(v) >= Th) {
+            const unsigned long long k = cand_key(v, bp[i]);
+            if (k >= T) {  // unique keys: exactly K of them
+                const int slot = atomicAdd(&sh.fill, 1);
+                if (slot < K) sh.sb[slot] = k;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(SELR_THREADS, 4) select_topk_reg_kernel(
     const float* __restrict__ bval, const int32_t* __restrict__ bpos, const int32_t* __restrict__ cnt, int M, int K,
     int64_t* __restrict__ pos, float* __restrict__ est1, uint8_t* __restrict__ ok, int32_t* __restrict__ ncnt,
     float delta, int didx) {
@@ -245,7 +276,9 @@ __global__ void __launch_bounds__(SELR_THREADS) select_topk_reg_kernel(
         for (int i = tid; i < K; i += SELR_THREADS) sh.sb[i] = i < n ? cand_key(bv[i], bp[i]) : filler;
     } else {
         const int nv = (n + 4 * SELR_THREADS - 1) / (4 * SELR_THREADS);  // uniform over the block
-        if (nv <= 1)
+        if (n > SELR_MAXM)
+            select_glob_cut(bv, bp, n, K, sh);
+        else if (nv <= 1)
             select_reg_cut<1>(bv, bp, n, K, sh);
         else if (nv <= 2)
             select_reg_cut<2>(bv, bp, n, K, sh);
@@ -497,7 +530,7 @@ extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int
             bval, bpos, cnt, B, M, K, Kp, pos, est1, ok, ncnt, delta, delta_idx);
         return fvs_launch_status();
     }
-    if (K <= fvs::SELR_MAXK && M % 4 == 0 && M <= fvs::SELR_MAXM && ((uintptr_t)bval & 15) == 0) {
+    if (K <= fvs::SELR_MAXK && M % 4 == 0 && ((uintptr_t)bval & 15) == 0) {
         fvs::select_topk_reg_kernel<<<B, fvs::SELR_THREADS, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt,
                                                                          delta, delta_idx);
         return fvs_launch_status();

@@ -543,6 +543,72 @@ __global__ void __launch_bounds__(512) route_topk_scaled_kernel(const __half* __
     for (int i = tid; i < nprobe; i += nt) probe[(int64_t)q * nprobe + i] = (int64_t)(0xffffffffu - (uint32_t)sb[i]);
 }
 
+// Register-resident variant for NC <= 2048 * V (NC a multiple of 8, 16-byte aligned QM rows and scales) and
+// nprobe <= 512: each of 256 threads holds the order keys of 8 * V scaled scores, the nprobe-th largest score key is
+// found by histogram passes below the keys' common prefix (block_rth_largest_reg), the cell half of the cut only
+// where scores tied with it straddle it.  Same keys, same result as route_topk_scaled_kernel.
+constexpr int RSR_THREADS = 256;
+constexpr int RSR_MAXP = 512;
+template <int V>
+__global__ void __launch_bounds__(RSR_THREADS) route_topk_scaled_reg_kernel(const __half* __restrict__ QM,
+                                                                            const float* __restrict__ sc, int NC,
+                                                                            int nprobe, int64_t* __restrict__ probe) {
+    __shared__ RegSelectScratch rs;
+    __shared__ SelectScratch ss;
+    __shared__ int s_fill;
+    __shared__ unsigned long long s_sel[RSR_MAXP];
+    const int q = blockIdx.x, tid = threadIdx.x;
+    const __half* qrow = QM + (int64_t)q * NC;
+    uint32_t hk[8 * V];  // 0 = no cell (a finite score's key is never 0)
+#pragma unroll
+    for (int v = 0; v < V; v++) {
+        const int u = tid + v * RSR_THREADS;
+        const bool in = u * 8 < NC;
+        const uint4 w = in ? __ldg(reinterpret_cast<const uint4*>(qrow) + u) : make_uint4(0u, 0u, 0u, 0u);
+        const float4 s0 = in ? __ldg(reinterpret_cast<const float4*>(sc) + 2 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 s1 = in ? __ldg(reinterpret_cast<const float4*>(sc) + 2 * u + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float ss8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const __half h = __ushort_as_half((unsigned short)((ws[e >> 1] >> (16 * (e & 1))) & 0xffffu));
+            hk[8 * v + e] = in ? f2o(__fmul_rn(__half2float(h), ss8[e])) : 0u;
+        }
+    }
+    if (tid == 0) s_fill = 0;
+    int gt, eq;
+    const uint32_t Th = block_rth_largest_reg<8 * V>(hk, nprobe, rs, &gt, &eq);
+    uint32_t Tl = 0u;
+    if (eq > nprobe - gt)
+        Tl = block_select_rth_largest<32, uint32_t>(
+            [&](int i) {
+                return f2o(__fmul_rn(__half2float(qrow[i]), sc[i])) == Th ? (0xffffffffu - (uint32_t)i) : 0u;
+            },
+            NC, nprobe - gt, ss);
+    const unsigned long long T = ((unsigned long long)Th << 32) | Tl;
+#pragma unroll
+    for (int v = 0; v < V; v++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const uint32_t h = hk[8 * v + e];
+            if (h != 0u && h >= Th) {
+                const int c = 8 * (tid + v * RSR_THREADS) + e;
+                const unsigned long long k = ((unsigned long long)h << 32) | (0xffffffffu - (uint32_t)c);
+                if (k >= T) {  // unique keys: exactly nprobe of them
+                    const int slot = atomicAdd(&s_fill, 1);
+                    if (slot < nprobe) s_sel[slot] = k;
+                }
+            }
+        }
+    __syncthreads();
+    for (int i = tid; i < nprobe; i += RSR_THREADS) {
+        const unsigned long long ki = s_sel[i];
+        int rank = 0;
+        for (int j = 0; j < nprobe; j++) rank += s_sel[j] > ki;
+        probe[(int64_t)q * nprobe + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+    }
+}
+
 // ------------------------------------------------------------------------------------------------ Viterbi (build)
 // Encoder of the bitshift trellis (k = 1) as `src/trellis_scan.py:21-32`: predecessors of state s are
 // (s >> 1) | (u << (L-1)); entering s emits vals[s]; ties keep predecessor u = 0 and the lowest final state.  One CTA
@@ -734,6 +800,20 @@ extern "C" int fvs_route_topk_scaled(fvs_stream_t stream, const uint16_t* QM, in
     FVS_CHECK_ARG(QM && cell_scale && probe && B >= 0 && NC > 0 && nprobe >= 1 && nprobe <= NC);
     if (nprobe > 4096) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
+    if (NC % 8 == 0 && NC <= 8 * fvs::RSR_THREADS * 4 && nprobe <= fvs::RSR_MAXP &&
+        (((uintptr_t)QM | (uintptr_t)cell_scale) & 15) == 0) {
+        const int V = (NC + 8 * fvs::RSR_THREADS - 1) / (8 * fvs::RSR_THREADS);
+        if (V <= 1)
+            fvs::route_topk_scaled_reg_kernel<1>
+                <<<B, fvs::RSR_THREADS, 0, stream>>>((const __half*)QM, cell_scale, NC, nprobe, probe);
+        else if (V <= 2)
+            fvs::route_topk_scaled_reg_kernel<2>
+                <<<B, fvs::RSR_THREADS, 0, stream>>>((const __half*)QM, cell_scale, NC, nprobe, probe);
+        else
+            fvs::route_topk_scaled_reg_kernel<4>
+                <<<B, fvs::RSR_THREADS, 0, stream>>>((const __half*)QM, cell_scale, NC, nprobe, probe);
+        return fvs_launch_status();
+    }
     int kp = 1;
     while (kp < nprobe) kp <<= 1;
     const size_t sm = (size_t)(NC + kp) * 8;

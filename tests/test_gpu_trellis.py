@@ -65,6 +65,24 @@ def test_route_scaled_matches_reference_order(gt, ec):
     np.testing.assert_array_equal(np.sort(c(probe)[same], 1), np.sort(gprobe[same], 1))
 
 
+@pytest.mark.parametrize("NC,npr", [(8192, 256), (8190, 256), (4096, 600), (2048, 64), (16, 5)])
+def test_route_scaled_ties(ec, NC, npr):
+    """top-n_p cells by (fp32 score x cell scale desc, cell asc) through the C ABI, also through many equal scores:
+    register-resident kernel (NC a multiple of 8 up to 8192, n_p <= 512) and shared-memory kernel (other shapes)."""
+    L = pkg("_lib")
+    lib = L.lib()
+    rng = np.random.default_rng(5)
+    B = 23
+    QM = (rng.integers(-200, 200, (B, NC)) / 256).astype(np.float16)           # heavy ties
+    sc = np.where(rng.random(NC) < 0.5, 1.0, rng.random(NC) + 0.5).astype(np.float32)
+    tq, ts = torch.from_numpy(QM).to(DEV), torch.from_numpy(sc).to(DEV)
+    probe = torch.empty(B, npr, dtype=torch.int64, device=DEV)
+    L.check(lib.fvs_route_topk_scaled(L.stream_handle(), L.ptr(tq), B, NC, npr, L.ptr(ts), L.ptr(probe)), "route")
+    s32 = QM.astype(np.float32) * sc[None]
+    want = np.stack([O.topk_desc(s32[q], npr) for q in range(B)])
+    np.testing.assert_array_equal(c(probe), want)
+
+
 def test_trellis_scan_first_pass_and_threshold(gt, ec):
     f = gt
     ix = _index(ec, f)
