@@ -24,6 +24,7 @@ SIGNATURES = {
     "fvs_quantize": (I32, [P, P, I32, I32, I32, P, P]),
     "fvs_route_topk": (I32, [P, P, I32, I32, I32, P]),
     "fvs_pairs": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P]),
+    "fvs_pairs_split": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P]),
     "fvs_pairs_noalloc": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P]),
     "fvs_i8_scan": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, P, P, P, P, P, I32, P, I32]),
     "fvs_i8_scan_tc": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I64, P, P, P, P, P, I32, P,

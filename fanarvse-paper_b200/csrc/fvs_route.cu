@@ -122,6 +122,40 @@ __global__ void pair_hist_kernel(const int64_t* __restrict__ probe, int B, int n
     atomicAdd(ccnt + probe[(int64_t)q * nprobe + j], 1);
 }
 
+// both counts of fvs_pairs_split: all nprobe columns, and the first n1 of them
+__global__ void pair_hist_split_kernel(const int64_t* __restrict__ probe, int B, int nprobe, int n1,
+                                       int32_t* __restrict__ ccnt, int32_t* __restrict__ ccnt1) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)B * nprobe) return;
+    const int j = (int)(i % nprobe);
+    const int64_t c = probe[i];
+    atomicAdd(ccnt + c, 1);
+    if (j < n1) atomicAdd(ccnt1 + c, 1);
+}
+
+// columns < n1 fill the front of their cell's range, the others the back
+__global__ void pair_scatter_split_kernel(const int64_t* __restrict__ probe, int B, int nprobe, int n1, int NC,
+                                          const __half* __restrict__ QM, const float* __restrict__ mnorm,
+                                          const int32_t* __restrict__ coff, const int32_t* __restrict__ ccnt1,
+                                          int32_t* __restrict__ cur1, int32_t* __restrict__ cur2,
+                                          int32_t* __restrict__ qid, float* __restrict__ qcp,
+                                          int32_t* __restrict__ slot) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)B * nprobe) return;
+    const int q = (int)(i / nprobe), j = (int)(i - (int64_t)q * nprobe);
+    const int c = (int)probe[i];
+    int pos;
+    if (j < n1) {
+        pos = coff[c] + atomicAdd(cur1 + c, 1);
+        if (slot) slot[(int64_t)q * n1 + j] = pos;
+    } else {
+        pos = coff[c] + ccnt1[c] + atomicAdd(cur2 + c, 1);
+    }
+    qid[pos] = q;
+    const float v = __half2float(QM[(int64_t)q * NC + c]);
+    qcp[pos] = mnorm ? __fmul_rn(v, mnorm[c]) : v;
+}
+
 // exclusive scan of NC counts in one CTA of 1024 threads
 __global__ void __launch_bounds__(1024) pair_scan_kernel(const int32_t* __restrict__ ccnt, int NC,
                                                          int32_t* __restrict__ coff) {
@@ -243,6 +277,25 @@ extern "C" int fvs_pairs(fvs_stream_t stream, const int64_t* probe, int B, int n
     if (n > 0)
         fvs::pair_scatter_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, ncols, NC, (const __half*)QM, mnorm, coff,
                                                            work, qid, qcp, slot);
+    return fvs_launch_status();
+}
+
+extern "C" int fvs_pairs_split(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int n1, int NC,
+                               const uint16_t* QM, const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt,
+                               int32_t* ccnt1, float* qcp, int32_t* slot, int32_t* work) {
+    FVS_CHECK_ARG(probe && QM && qid && coff && ccnt && ccnt1 && qcp && work && B >= 0 && NC > 0);
+    FVS_CHECK_ARG(n1 >= 1 && n1 <= nprobe);
+    cudaError_t e = cudaMemsetAsync(ccnt, 0, (size_t)NC * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(ccnt1, 0, (size_t)NC * 4, stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(work, 0, (size_t)NC * 8, stream);
+    if (e != cudaSuccess) return (int)e;
+    const int64_t n = (int64_t)B * nprobe;
+    const unsigned grid = (unsigned)((n + 255) / 256);
+    if (n > 0) fvs::pair_hist_split_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, n1, ccnt, ccnt1);
+    fvs::pair_scan_kernel<<<1, 1024, 0, stream>>>(ccnt, NC, coff);
+    if (n > 0)
+        fvs::pair_scatter_split_kernel<<<grid, 256, 0, stream>>>(probe, B, nprobe, n1, NC, (const __half*)QM, mnorm,
+                                                                 coff, ccnt1, work, work + NC, qid, qcp, slot);
     return fvs_launch_status();
 }
 

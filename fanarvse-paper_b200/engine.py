@@ -143,6 +143,26 @@ class EngineB200I8:
         self.launches += 2   # fvs_pairs issues three kernels
         return qid, coff, ccnt, qcp, slot
 
+    def pairs_split(self, probe, n1, QM):
+        """both passes' pair lists as one list by cell, first-pass pairs first in each cell (`fvs_pairs_split`)."""
+        ix = self.ix
+        B, npr = probe.shape
+        dev = probe.device
+        n = B * npr
+        qid = torch.empty(n, dtype=torch.int32, device=dev)
+        qcp = torch.empty(n, device=dev)
+        coff = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        ccnt = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        ccnt1 = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        slot = torch.empty(B * n1, dtype=torch.int32, device=dev)
+        work = self.__dict__.get("_work2")
+        if work is None:
+            work = self._work2 = torch.zeros(2 * ix.NC, dtype=torch.int32, device=dev)
+        self._call("pairs", self.L.fvs_pairs_split, ptr(probe), B, npr, n1, ix.NC, ptr(QM), ptr(ix.mnorm), ptr(qid),
+                   ptr(coff), ptr(ccnt), ptr(ccnt1), ptr(qcp), ptr(slot), ptr(work))
+        self.launches += 2   # fvs_pairs_split issues three kernels
+        return qid, coff, ccnt, ccnt1, qcp, slot
+
     def _scan(self, mode, name, q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc):
         ix = self.ix
         if self.SCAN == "tc":
@@ -199,13 +219,13 @@ class EngineB200I8:
         probe = probe.contiguous()
         if (B <= self.SMALL and self.SCAN != "mma") if small is None else small:
             return self._stage1_small(q8, qs, B, QM, probe, K, M, rho, n1, rho_override)
-        qid, coff, ccnt, qcp, slot = self.pairs(probe, n1, QM, True)
-        bmc = torch.empty(B * n1 * ix.MB, device=dev)
-        self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt, qcp, None, None, None, None, 0, bmc)
+        # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
+        qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
+        bmc = torch.empty(qid.numel() * ix.MB, device=dev)   # block-maxima rows addressed by pair position
+        self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc)
         t0 = torch.empty(B, device=dev)
         self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1,
                    ptr(ix.off), B, int(np.ceil(rho * K)), ptr(t0))
-        qid, coff, ccnt, qcp, _ = self.pairs(probe, probe.shape[1], QM, False)
         cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
@@ -299,8 +319,9 @@ class EngineB200I8:
                        ix.N, ptr(ncnt), ptr(est), ptr(sd))
         return est, sd
 
-    def rotated_query(self, Qb):
-        return (Qb.half() @ self.ix.VP16).float().contiguous()             # `throughput/s2lut.py:122`
+    def rotated_query(self, Qb, Qh=None):
+        Qh = Qb.half() if Qh is None else Qh
+        return (Qh @ self.ix.VP16).float().contiguous()                     # `throughput/s2lut.py:122`
 
     def refine(self, Qb, pos, est, sd, z, k):
         ix = self.ix
@@ -314,18 +335,19 @@ class EngineB200I8:
                    float(z), k, ptr(Qf), Qf.shape[1], ptr(ids), ptr(I), ptr(reads), ptr(score_k))
         return I, reads, ids, score_k
 
-    def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None):
+    def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None, Qh=None):
         """`throughput/enginei8.py:80-95`."""
         half = self.LUTH if half is None else half
-        Zq = self.rotated_query(Qb)
+        Zq = self.rotated_query(Qb, Qh)
         est, sd = self.score_lut_zq(QC, pos, Zq, ncnt, half)
         I, reads, ids, score_k = self.refine(Qb, pos, est, sd, z, k)
         self._last.update(est=est, sd=sd, Zq=Zq, score_k=score_k)
         return ok, I, reads.long(), ids
 
-    def route(self, Qb, nprobe):
+    def route(self, Qb, nprobe, Qh=None):
         """QM = fp16(Q) @ meansN^T (cuBLAS) and the nprobe best cells per query (`throughput/enginei8.py:67-68`)."""
-        QM = (Qb.half() @ self.ix.meansN.T).contiguous()
+        Qh = Qb.half() if Qh is None else Qh
+        QM = (Qh @ self.ix.meansN.T).contiguous()
         probe = torch.empty(Qb.shape[0], nprobe, dtype=torch.int64, device=Qb.device)
         self._call("route_topk", self.L.fvs_route_topk, ptr(QM), Qb.shape[0], self.ix.NC, nprobe, ptr(probe))
         return QM, probe
@@ -335,7 +357,8 @@ class EngineB200I8:
         if K <= k or K < 10:
             raise ValueError("need K > k and K >= 10 (the delta rule reads the 10th stage-1 estimate)")
         QC = (Qb @ self.ix.c).contiguous()
-        QM, probe = self.route(Qb, nprobe)
+        Qh = Qb.half()                       # one fp16 copy of the queries for the routing and rotation products
+        QM, probe = self.route(Qb, nprobe, Qh)
         q8, qs = self.quantize(Qb)
         pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs))
         fb = None
@@ -346,7 +369,7 @@ class EngineB200I8:
             side.wait_stream(main)
             with torch.cuda.stream(side):
                 fb = self._fallback_ingraph(Qb, QC, QM, probe, q8, qs, ok, K, z, k)
-        out = self._finish(Qb, QC, pos, ok, ncnt, K, z, k)
+        out = self._finish(Qb, QC, pos, ok, ncnt, K, z, k, Qh=Qh)
         if fb is None:
             return out
         main.wait_stream(side)

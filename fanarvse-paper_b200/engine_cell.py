@@ -118,13 +118,13 @@ class EngineB200S(EngineB200I8):
         nprobe = probe.shape[1]
         n1 = min(max(int(np.ceil(beta * K / (ix.N / ix.NC / BN + 1))), 1), nprobe)
         probe = probe.contiguous()
-        qid, coff, ccnt, qcp, slot = self.pairs(probe, n1, QM, True)
-        bmc = torch.empty(B * n1 * ix.MB, device=dev)
-        self._scan(0, "trellis_scan_first", Qh, B, qid, coff, ccnt, qcp, None, None, None, None, 0, bmc)
+        # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
+        qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
+        bmc = torch.empty(qid.numel() * ix.MB, device=dev)   # block-maxima rows addressed by pair position
+        self._scan(0, "trellis_scan_first", Qh, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc)
         t0 = torch.empty(B, device=dev)
         self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), nprobe, n1, ptr(ix.off), B,
                    int(np.ceil(rho * K)), ptr(t0))
-        qid, coff, ccnt, qcp, _ = self.pairs(probe, nprobe, QM, False)
         cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)

@@ -53,6 +53,18 @@ int fvs_pairs(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int 
               int32_t* work);
 
 /*
+ * Both pair lists of the int8 stage 1 (`throughput/enginei8.py:42,56`: `pairs_fast` over the first n1 columns for
+ * the first pass, over all nprobe columns for the emit pass) as ONE list by cell over all nprobe columns, in which
+ * each cell's pairs from columns < n1 come first: ccnt[c] = #pairs in cell c, ccnt1[c] = #of them from columns < n1,
+ * coff = exclusive prefix of ccnt, qid / qcp as fvs_pairs, slot[q*n1 + j] (j < n1) = position of pair (q, j).  The
+ * first pass reads (coff, ccnt1), the emit pass (coff, ccnt); one histogram, scan and scatter serve both.
+ * 1 <= n1 <= nprobe.  work: 2*NC int32 of scratch.
+ */
+int fvs_pairs_split(fvs_stream_t stream, const int64_t* probe, int B, int nprobe, int n1, int NC, const uint16_t* QM,
+                    const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt, int32_t* ccnt1, float* qcp,
+                    int32_t* slot, int32_t* work);
+
+/*
  * fvs_pairs without the `work` argument, for callers that cannot allocate device memory: host programs that drive
  * the search through a foreign-function binding and own no CUDA allocator, or that must not call cudaMalloc while
  * their stream is being captured into a CUDA graph.  No counterpart in the reference (its pairing is torch code that

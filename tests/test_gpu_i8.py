@@ -313,6 +313,46 @@ def test_pairs_csr(eng, ncols):
     np.testing.assert_array_equal(gqc[gs], want)
 
 
+@pytest.mark.parametrize("n1", [1, 23, 352])
+def test_pairs_split(eng, n1):
+    """one pair list for both passes: in every cell the pairs from the first n1 columns come first and form the first
+    pass's list (coff, ccnt1), the whole range the emit pass's list (coff, ccnt); slots point at the first-pass pairs."""
+    L = pkg("_lib")
+    lib = L.lib()
+    rng = np.random.default_rng(6)
+    B, NC, npr = 300, 4096, 352
+    probe = np.stack([rng.permutation(NC)[:npr] for _ in range(B)]).astype(np.int64)
+    QM = (rng.standard_normal((B, NC)) * 0.3).astype(np.float16)
+    mnorm = (rng.random(NC) + 0.5).astype(np.float32)
+    tp, tq, tm = (torch.from_numpy(x).to(DEV) for x in (probe, QM, mnorm))
+    n = B * npr
+    qid = torch.empty(n, dtype=torch.int32, device=DEV)
+    qcp = torch.empty(n, device=DEV)
+    coff, ccnt, ccnt1 = (torch.empty(NC, dtype=torch.int32, device=DEV) for _ in range(3))
+    slot = torch.empty(B * n1, dtype=torch.int32, device=DEV)
+    work = torch.empty(2 * NC, dtype=torch.int32, device=DEV)
+    L.check(lib.fvs_pairs_split(L.stream_handle(), L.ptr(tp), B, npr, n1, NC, L.ptr(tq), L.ptr(tm), L.ptr(qid),
+                                L.ptr(coff), L.ptr(ccnt), L.ptr(ccnt1), L.ptr(qcp), L.ptr(slot), L.ptr(work)),
+            "pairs_split")
+    oq, oc, on, oqc, o = O.pairs(probe, NC, QM, mnorm)
+    oq1, oc1, on1, _, _ = O.pairs(probe[:, :n1], NC, QM, mnorm)
+    np.testing.assert_array_equal(c(coff), oc)
+    np.testing.assert_array_equal(c(ccnt), on)
+    np.testing.assert_array_equal(c(ccnt1), on1)
+    gq, gqc, gs = c(qid), c(qcp), c(slot)
+    for cc in range(0, NC, 7):
+        a, m, b = oc[cc], oc[cc] + on1[cc], oc[cc] + on[cc]
+        np.testing.assert_array_equal(np.sort(gq[a:m]), np.sort(oq1[oc1[cc]:oc1[cc] + on1[cc]]))
+        np.testing.assert_array_equal(np.sort(gq[a:b]), np.sort(oq[a:b]))
+    qq = np.repeat(np.arange(B), n1)
+    jj = np.tile(np.arange(n1), B)
+    np.testing.assert_array_equal(gq[gs], qq)
+    cells = probe[qq, jj]
+    assert ((gs >= oc[cells]) & (gs < oc[cells] + on1[cells])).all()
+    want = (QM[qq, cells].astype(np.float32) * mnorm[cells]).astype(np.float32)
+    np.testing.assert_array_equal(gqc[gs], want)
+
+
 def test_quantize_matches_reference_formula(eng):
     """the quantisation kernel equals the reference's torch expression on the same projected queries."""
     L = pkg("_lib")
