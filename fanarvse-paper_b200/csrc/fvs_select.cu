@@ -172,33 +172,34 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
 }
 
 
-// Register-resident variant (same contract) for M a multiple of 4 and K <= 256: for a query with at most 8192
-// candidates each of 256 threads holds the order keys of 4 * W candidate scores, loaded as 16-byte words, where W (1,
-// 2, 4 or 8 chunks of 1024 keys) is the smallest that covers its cnt (more candidates: radix passes over global
-// memory, select_glob_cut); the K-th largest score key is found by histogram passes below the
-// keys' common prefix (block_rth_largest_reg); positions are read only for the keys at or above it, and where scores
-// tied with the cut straddle it, the cut's position half comes from the block radix select over those ties.
-constexpr int SELR_THREADS = 256;
-constexpr int SELR_MAXK = 256;  // one rank per thread (larger K: the shared-memory kernel, 512 threads)
-constexpr int SELR_MAXM = 4 * SELR_THREADS * 8;
+// Register-resident variant (same contract) for M a multiple of 4 and K <= NT (NT = 256 threads, or 512 for K up to
+// 512): for a query with at most 8192 candidates each thread holds the order keys of 4 * W candidate scores, loaded as
+// 16-byte words, where W (chunks of 4 * NT keys) is the smallest power of two that covers its cnt (more candidates:
+// radix passes over global memory, select_glob_cut); the K-th largest score key is found by histogram passes below
+// the keys' common prefix (block_rth_largest_reg); positions are read only for the keys at or above it, and where
+// scores tied with the cut straddle it, the cut's position half comes from the block radix select over those ties;
+// the K winners are placed by rank, one per thread.
+constexpr int SELR_MAXK = 512;
+constexpr int SELR_MAXM = 8192;
+template <int NT>
 struct SelRegShared {
     SelectScratch ss;
     RegSelectScratch rs;
     int red[32];
     int fill, ncnt;
     float dval;
-    unsigned long long sb[SELR_MAXK];
+    unsigned long long sb[NT];
 };
 
 // the K largest (score key, position key) pairs of the n > K candidates, unordered, into sh.sb
-template <int W>
+template <int NT, int W>
 __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
-                                               int K, SelRegShared& sh) {
+                                               int K, SelRegShared<NT>& sh) {
     const int tid = threadIdx.x;
     uint32_t hk[4 * W];  // 0 = no candidate (a finite score's key is never 0)
 #pragma unroll
     for (int v = 0; v < W; v++) {
-        const int u = tid + v * SELR_THREADS;
+        const int u = tid + v * NT;
         const bool in = 4 * u < n;
         const float4 w = in ? __ldcg(reinterpret_cast<const float4*>(bv) + u) : make_float4(0.f, 0.f, 0.f, 0.f);
         hk[4 * v + 0] = in ? f2o(w.x) : 0u;
@@ -221,7 +222,7 @@ __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, con
         for (int e = 0; e < 4; e++) {
             const uint32_t h = hk[4 * v + e];
             if (h != 0u && h >= Th) {
-                const int i = 4 * (tid + v * SELR_THREADS) + e;
+                const int i = 4 * (tid + v * NT) + e;
                 const unsigned long long k = ((unsigned long long)h << 32) | (0xffffffffu - (uint32_t)bp[i]);
                 if (k >= T) {  // keys are unique (one entry per probed row): exactly K of them
                     const int slot = atomicAdd(&sh.fill, 1);
@@ -232,12 +233,13 @@ __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, con
 }
 
 // the same for n > SELR_MAXM candidates: keys read from global memory in every radix pass
+template <int NT>
 __device__ __forceinline__ void select_glob_cut(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
-                                                int K, SelRegShared& sh) {
+                                                int K, SelRegShared<NT>& sh) {
     const int tid = threadIdx.x;
     const uint32_t Th = block_select_rth_largest<32, uint32_t>([&](int i) { return f2o(bv[i]); }, n, K, sh.ss);
     int gt = 0, eq = 0;
-    for (int i = tid; i < n; i += SELR_THREADS) {
+    for (int i = tid; i < n; i += NT) {
         const uint32_t h = f2o(bv[i]);
         gt += h > Th;
         eq += h == Th;
@@ -248,7 +250,7 @@ __device__ __forceinline__ void select_glob_cut(const float* __restrict__ bv, co
     if (eq > K - gt)
         T |= block_select_rth_largest<32, uint32_t>(
             [&](int i) { return f2o(bv[i]) == Th ? (0xffffffffu - (uint32_t)bp[i]) : 0u; }, n, K - gt, sh.ss);
-    for (int i = tid; i < n; i += SELR_THREADS) {
+    for (int i = tid; i < n; i += NT) {
         const float v = bv[i];
         if (f2o(v) >= Th) {
             const unsigned long long k = cand_key(v, bp[i]);
@@ -260,11 +262,12 @@ __device__ __forceinline__ void select_glob_cut(const float* __restrict__ bv, co
     }
 }
 
-__global__ void __launch_bounds__(SELR_THREADS, 4) select_topk_reg_kernel(
+template <int NT>
+__global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
     const float* __restrict__ bval, const int32_t* __restrict__ bpos, const int32_t* __restrict__ cnt, int M, int K,
     int64_t* __restrict__ pos, float* __restrict__ est1, uint8_t* __restrict__ ok, int32_t* __restrict__ ncnt,
     float delta, int didx) {
-    __shared__ SelRegShared sh;
+    __shared__ SelRegShared<NT> sh;
     const int q = blockIdx.x, tid = threadIdx.x;
     const int c = cnt[q];
     const int n = min(max(c, 0), M);
@@ -273,23 +276,23 @@ __global__ void __launch_bounds__(SELR_THREADS, 4) select_topk_reg_kernel(
     if (tid == 0) sh.fill = 0;
     if (n <= K) {
         const unsigned long long filler = cand_key(kNeg, 0);
-        for (int i = tid; i < K; i += SELR_THREADS) sh.sb[i] = i < n ? cand_key(bv[i], bp[i]) : filler;
+        for (int i = tid; i < K; i += NT) sh.sb[i] = i < n ? cand_key(bv[i], bp[i]) : filler;
     } else {
-        const int nv = (n + 4 * SELR_THREADS - 1) / (4 * SELR_THREADS);  // uniform over the block
+        const int nv = (n + 4 * NT - 1) / (4 * NT);  // uniform over the block
         if (n > SELR_MAXM)
-            select_glob_cut(bv, bp, n, K, sh);
+            select_glob_cut<NT>(bv, bp, n, K, sh);
         else if (nv <= 1)
-            select_reg_cut<1>(bv, bp, n, K, sh);
+            select_reg_cut<NT, 1>(bv, bp, n, K, sh);
         else if (nv <= 2)
-            select_reg_cut<2>(bv, bp, n, K, sh);
-        else if (nv <= 4)
-            select_reg_cut<4>(bv, bp, n, K, sh);
+            select_reg_cut<NT, 2>(bv, bp, n, K, sh);
+        else if (nv <= 4 || NT == 512)
+            select_reg_cut<NT, 4>(bv, bp, n, K, sh);
         else
-            select_reg_cut<8>(bv, bp, n, K, sh);
+            select_reg_cut<NT, 8>(bv, bp, n, K, sh);
     }
     __syncthreads();
     // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal)
-    for (int i = tid; i < K; i += SELR_THREADS) {
+    for (int i = tid; i < K; i += NT) {
         const unsigned long long ki = sh.sb[i];
         int rank = 0;
         for (int j = 0; j < K; j++) {
@@ -306,7 +309,7 @@ __global__ void __launch_bounds__(SELR_THREADS, 4) select_topk_reg_kernel(
         __syncthreads();
         const float thr = __fsub_rn(sh.dval, delta);
         int m = 0;
-        for (int i = tid; i < K; i += SELR_THREADS) m += o2f((uint32_t)(sh.sb[i] >> 32)) >= thr;
+        for (int i = tid; i < K; i += NT) m += o2f((uint32_t)(sh.sb[i] >> 32)) >= thr;
         atomicAdd(&sh.ncnt, m);
         __syncthreads();
         if (tid == 0) ncnt[q] = sh.ncnt;
@@ -531,8 +534,12 @@ extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int
         return fvs_launch_status();
     }
     if (K <= fvs::SELR_MAXK && M % 4 == 0 && ((uintptr_t)bval & 15) == 0) {
-        fvs::select_topk_reg_kernel<<<B, fvs::SELR_THREADS, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt,
-                                                                         delta, delta_idx);
+        if (K <= 256)
+            fvs::select_topk_reg_kernel<256><<<B, 256, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt, delta,
+                                                                    delta_idx);
+        else
+            fvs::select_topk_reg_kernel<512><<<B, 512, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt, delta,
+                                                                    delta_idx);
         return fvs_launch_status();
     }
     const size_t sm = (size_t)(Kp + fvs::SEL_SMEM_KEYS) * 8;

@@ -214,10 +214,11 @@ def test_graph_search_and_fallback(eng):
 
 @pytest.mark.parametrize("M,K,kind", [(700, 50, "ties"), (701, 50, "ties"), (4000, 100, "ties"), (4000, 100, "cont"),
                                        (8192, 100, "cont"), (8192, 100, "ties"), (8196, 100, "cont"),
-                                       (16384, 100, "cont"), (16384, 250, "ties"), (4000, 400, "ties"), (1400, 600, "ties")])
+                                       (16384, 100, "cont"), (16384, 250, "ties"), (4000, 400, "ties"), (16384, 500, "cont"),
+                                       (1400, 600, "ties")])
 def test_select_topk_ties(eng, M, K, kind):
     """stage-1 top-K orders by (estimate desc, position asc), also through ties and cnt < K, cnt > M; register-resident
-    kernel (M a multiple of 4, K <= 256; more than 8192 candidates by its global-memory branch) and shared-memory
+    kernel (M a multiple of 4, K <= 512; more than 8192 candidates by its global-memory branch) and shared-memory
     kernel (the other shapes)."""
     L = pkg("_lib")
     lib = L.lib()
