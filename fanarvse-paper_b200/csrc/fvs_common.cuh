@@ -20,6 +20,21 @@ static inline int fvs_launch_status() {
     return e == cudaSuccess ? FVS_OK : (int)e;
 }
 
+// Number of SMs of the current device (looked up once per device).
+inline int fvs_sm_count() {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+    static std::mutex mu;
+    static std::map<int, int> cache;
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(dev);
+    if (it != cache.end()) return it->second;
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cache[dev] = n;
+    return n;
+}
+
 // Raise a kernel's dynamic shared-memory limit once per (kernel, device); later calls (including calls made while a
 // stream is being captured into a CUDA graph) only read the cache.
 inline cudaError_t fvs_ensure_smem(const void* func, size_t bytes) {

@@ -169,10 +169,11 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     int32_t* s_pos = reinterpret_cast<int32_t*>(lut + 128 * GA);  // the query's candidate positions (K)
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
     const int lim = ncnt ? min(max(ncnt[q], 0), K) : K;
-    for (int i = lim + tid; i < K; i += blockDim.x) {
-        est[(int64_t)q * K + i] = kNeg;
-        sd[(int64_t)q * K + i] = 0.f;
-    }
+    if (blockIdx.y == 0)
+        for (int i = lim + tid; i < K; i += blockDim.x) {
+            est[(int64_t)q * K + i] = kNeg;
+            sd[(int64_t)q * K + i] = 0.f;
+        }
     if (lim == 0) return;
     const float* z = Zq + (int64_t)q * ldz;
     const int nblk = D / 32;
@@ -234,7 +235,9 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     const int tl = lane < ts.T ? lane : 0;
     const float dmq = ts.delta[tl] * ts.mid[tl] * s_qsum[tl], qn2l = s_qn2[tl];
     const float qcv = qc[q];
-    for (int i0 = warp; i0 < lim; i0 += 2 * nw) {
+    // a small batch splits each query's candidates over gridDim.y CTAs (rounds of 2 * nw candidates, round-robin),
+    // each with its own copy of the table
+    for (int i0 = warp + blockIdx.y * 2 * nw; i0 < lim; i0 += gridDim.y * 2 * nw) {
         int64_t nn[2];
         bool live[2];
         uint32_t wv[2][WPL];
@@ -298,6 +301,15 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
             }
         }
     }
+}
+
+// CTAs per query of the fused LUT kernel: enough for about two per SM when the batch is small, at most one per 16
+// candidates (two rounds of its 8 warps)
+static int lut_split(int B, int K) {
+    if (B <= 0) return 1;
+    const int want = (2 * fvs_sm_count() + B - 1) / B;
+    const int cap = (K + 15) / 16;
+    return want < 1 ? 1 : (want < cap ? want : cap);
 }
 
 static int make_tiers(TierSet& ts, int T, const int32_t* s, const int32_t* e, const int32_t* bits,
@@ -403,11 +415,12 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const fvs::RecSet rs{nullptr, 0, 0};
+    const int S = fvs::lut_split(B, K);
 #define FVS_LZ(H, W)                                                                                               \
     do {                                                                                                           \
         cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false, 0>, sm);               \
         if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W, false, 0><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,       \
+        fvs::lut_score_zq_kernel<H, W, false, 0><<<dim3(B, S), 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,       \
                                                                      (const __half*)scale, (const __half*)sig, N,  \
                                                                      ncnt, est, sd, rs);                           \
     } while (0)
@@ -444,11 +457,12 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const fvs::RecSet rs{rec, RB, soff};
+    const int S = fvs::lut_split(B, K);
 #define FVS_LRG(H, W, G)                                                                                           \
     do {                                                                                                           \
         cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true, G>, sm);                \
         if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W, true, G><<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,        \
+        fvs::lut_score_zq_kernel<H, W, true, G><<<dim3(B, S), 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,        \
                                                                        nullptr, nullptr, N, ncnt, est, sd, rs);    \
     } while (0)
 #define FVS_LR(H, W)                                                                                               \

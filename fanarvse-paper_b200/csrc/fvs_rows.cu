@@ -1,9 +1,9 @@
 // Row compaction / gather / scatter for the in-graph recompute of flagged queries (new; the reference recomputes
 // flagged rows from the host, `throughput/enginei8.py:108-111`).
 //
-// fvs_flagged_gather: one CTA compacts the rows whose flag is 0 (stable order; the first FB of them), writes their
-// indices (B for unused slots) and the number of flagged rows, then copies those rows of up to 8 arrays into dense
-// [FB, row] buffers (unused slots copy row 0, so that the recompute runs on valid inputs).
+// fvs_flagged_gather: compacts the rows whose flag is 0 (stable order; the first FB of them), writes their indices (B
+// for unused slots) and the number of flagged rows, and copies those rows of up to 8 arrays into dense [FB, row]
+// buffers (unused slots copy row 0, so that the recompute runs on valid inputs); one CTA per (slot, array).
 // fvs_rows_scatter: copies the recomputed rows back to their places and sets their flags to 1.
 #include "fvs_common.cuh"
 
@@ -26,15 +26,20 @@ __device__ __forceinline__ void copy_row(uint8_t* __restrict__ d, const uint8_t*
     }
 }
 
-__global__ void __launch_bounds__(1024) flagged_gather_kernel(const uint8_t* __restrict__ ok, int B, int FB,
-                                                              int32_t* __restrict__ rows, int32_t* __restrict__ nflag,
-                                                              RowSet rs) {
-    __shared__ int wsum[32];
-    __shared__ int s_rows[1024];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nt = blockDim.x;
-    for (int i = tid; i < FB; i += nt) s_rows[i] = B;
-    // chunked stable compaction: each thread owns a contiguous run of rows
-    const int per = (B + nt - 1) / nt;
+// grid (FB, max(G, 1)): CTA (slot, g) finds the slot-th row with flag 0 (stable order) by a block-wide count over the
+// flags -- every CTA repeats this small scan, so that the copies of all (slot, array) rows run in parallel -- and
+// copies that row of array g; CTAs (slot, 0) write rows[slot], CTA (0, 0) the number of flagged rows.
+constexpr int GATHER_THREADS = 256;
+__global__ void __launch_bounds__(GATHER_THREADS) flagged_gather_kernel(const uint8_t* __restrict__ ok, int B, int FB,
+                                                                        int32_t* __restrict__ rows,
+                                                                        int32_t* __restrict__ nflag, RowSet rs) {
+    __shared__ int wsum[GATHER_THREADS / 32];
+    __shared__ int s_row;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int slot = blockIdx.x, g = blockIdx.y;
+    if (tid == 0) s_row = B;
+    // each thread owns a contiguous run of rows; exclusive prefix of the flagged counts over the block
+    const int per = (B + GATHER_THREADS - 1) / GATHER_THREADS;
     const int b0 = tid * per, b1 = min(B, b0 + per);
     int local = 0;
     for (int i = b0; i < b1; i++) local += ok[i] == 0;
@@ -47,22 +52,29 @@ __global__ void __launch_bounds__(1024) flagged_gather_kernel(const uint8_t* __r
     if (lane == 31) wsum[warp] = incl;
     __syncthreads();
     int before = 0, total = 0;
-    for (int w = 0; w < (nt >> 5); w++) {
+#pragma unroll
+    for (int w = 0; w < GATHER_THREADS / 32; w++) {
         if (w < warp) before += wsum[w];
         total += wsum[w];
     }
-    int at = before + incl - local;
-    for (int i = b0; i < b1 && at < FB; i++)
-        if (ok[i] == 0) s_rows[at++] = i;
-    __syncthreads();
-    for (int i = tid; i < FB; i += nt) rows[i] = s_rows[i];
-    if (tid == 0) *nflag = total;
-    // one (slot, array) row per warp at a time: the copies are independent, so they are in flight together
-    for (int pg = warp; pg < FB * rs.G; pg += (nt >> 5)) {
-        const int slot = pg / rs.G, g = pg - slot * rs.G;
-        const int r = s_rows[slot] < B ? s_rows[slot] : 0;
-        copy_row(rs.dst[g] + (int64_t)slot * rs.rb[g], rs.src[g] + (int64_t)r * rs.rb[g], rs.rb[g], lane, 32);
+    const int start = before + incl - local;  // flagged rows before this thread's run
+    if (slot >= start && slot < start + local) {
+        int at = start;
+        for (int i = b0; i < b1; i++)
+            if (ok[i] == 0) {
+                if (at == slot) s_row = i;
+                at++;
+            }
     }
+    __syncthreads();
+    const int r = s_row;  // B when fewer than slot + 1 rows are flagged
+    if (tid == 0 && g == 0) {
+        rows[slot] = r;
+        if (slot == 0) *nflag = total;
+    }
+    if (g < rs.G)
+        copy_row(rs.dst[g] + (int64_t)slot * rs.rb[g], rs.src[g] + (int64_t)(r < B ? r : 0) * rs.rb[g], rs.rb[g], tid,
+                 GATHER_THREADS);
 }
 
 __global__ void __launch_bounds__(256) rows_scatter_kernel(const int32_t* __restrict__ rows, int B,
@@ -98,7 +110,8 @@ extern "C" int fvs_flagged_gather(fvs_stream_t stream, const uint8_t* ok, int B,
     fvs::rows::RowSet rs;
     int rc = fvs::rows::make_rowset(rs, G, src, dst, row_bytes);
     if (rc) return rc;
-    fvs::rows::flagged_gather_kernel<<<1, 1024, 0, stream>>>(ok, B, FB, rows, nflag, rs);
+    fvs::rows::flagged_gather_kernel<<<dim3(FB, G > 0 ? G : 1), fvs::rows::GATHER_THREADS, 0, stream>>>(ok, B, FB, rows,
+                                                                                                        nflag, rs);
     return fvs_launch_status();
 }
 

@@ -172,8 +172,8 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
 }
 
 
-// Register-resident variant (same contract) for M a multiple of 4 and K <= NT (NT = 256 threads, or 512 for K up to
-// 512): for a query with at most 8192 candidates each thread holds the order keys of 4 * W candidate scores, loaded as
+// Register-resident variant (same contract) for M a multiple of 4 and K <= NT (NT = 256 threads, 512 for K up to 512,
+// 1024 for batches smaller than the SM count): for a query with at most 8192 candidates each thread holds the order keys of 4 * W candidate scores, loaded as
 // 16-byte words, where W (chunks of 4 * NT keys) is the smallest power of two that covers its cnt (more candidates:
 // radix passes over global memory, select_glob_cut); the K-th largest score key is found by histogram passes below
 // the keys' common prefix (block_rth_largest_reg); positions are read only for the keys at or above it, and where
@@ -285,7 +285,7 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
             select_reg_cut<NT, 1>(bv, bp, n, K, sh);
         else if (nv <= 2)
             select_reg_cut<NT, 2>(bv, bp, n, K, sh);
-        else if (nv <= 4 || NT == 512)
+        else if (nv <= 4 || NT >= 512)
             select_reg_cut<NT, 4>(bv, bp, n, K, sh);
         else
             select_reg_cut<NT, 8>(bv, bp, n, K, sh);
@@ -534,7 +534,10 @@ extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int
         return fvs_launch_status();
     }
     if (K <= fvs::SELR_MAXK && M % 4 == 0 && ((uintptr_t)bval & 15) == 0) {
-        if (K <= 256)
+        if (B < fvs_sm_count())  // a small batch: 32 warps per query
+            fvs::select_topk_reg_kernel<1024><<<B, 1024, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt,
+                                                                      delta, delta_idx);
+        else if (K <= 256)
             fvs::select_topk_reg_kernel<256><<<B, 256, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt, delta,
                                                                     delta_idx);
         else
