@@ -47,7 +47,14 @@ __global__ void __launch_bounds__(32 * WARPS) scan_small_kernel(
     const float th = MODE ? t0[q] : 0.f;
     const int64_t lo = blk * 32 > cs ? blk * 32 : cs, hi = blk * 32 + 32 < ce ? blk * 32 + 32 : ce;
     float mx = -INFINITY;
-    for (int64_t r0 = lo; r0 < hi; r0 += 2 * UNROLL) {
+    // a block has at most 32 rows: 32 / (2 * UNROLL) steps; in the emit pass the rows kept over the whole block are
+    // reserved with one atomicAdd per warp (the candidate counters of a small batch are shared by thousands of CTAs)
+    constexpr int STEPS = 32 / (2 * UNROLL);
+    float kest[STEPS * UNROLL];
+    uint32_t kmask = 0;
+#pragma unroll
+    for (int st = 0; st < STEPS; st++) {
+        const int64_t r0 = lo + (int64_t)st * 2 * UNROLL;
         uint4 zv[UNROLL];
         float zr[UNROLL];
 #pragma unroll
@@ -74,21 +81,30 @@ __global__ void __launch_bounds__(32 * WARPS) scan_small_kernel(
             if (MODE == 0) {
                 if (valid) mx = fmaxf(mx, est);
             } else {
-                const bool keep = valid && hl == 0 && est >= th;
-                const unsigned m = __ballot_sync(0xffffffffu, keep);
-                if (m) {
-                    int base = 0;
-                    if (lane == 0) base = atomicAdd(cnt + q, __popc(m));
-                    base = __shfl_sync(0xffffffffu, base, 0);
-                    if (keep) {
-                        const int idx = base + (half ? __popc(m & 1u) : 0);
-                        if (idx < M) {
-                            bval[(int64_t)q * M + idx] = est;
-                            bpos[(int64_t)q * M + idx] = (int32_t)r;
-                        }
-                    }
-                }
+                kest[st * UNROLL + u] = est;
+                if (valid && est >= th) kmask |= 1u << (st * UNROLL + u);
             }
+        }
+    }
+    if (MODE == 1) {
+        // lanes 0 and 16 (one per half-warp) hold the kept rows of their half
+        const int mine = hl == 0 ? __popc(kmask) : 0;
+        const int other = __shfl_xor_sync(0xffffffffu, mine, 16);
+        int base = 0;
+        if (lane == 0 && mine + other > 0) base = atomicAdd(cnt + q, mine + other);
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (hl == 0 && kmask) {
+            int idx = base + (half ? other : 0);
+#pragma unroll
+            for (int e = 0; e < STEPS * UNROLL; e++)
+                if ((kmask >> e) & 1u) {
+                    if (idx < M) {
+                        const int64_t r = lo + (int64_t)(e / UNROLL) * 2 * UNROLL + 2 * (e % UNROLL) + half;
+                        bval[(int64_t)q * M + idx] = kest[e];
+                        bpos[(int64_t)q * M + idx] = (int32_t)r;
+                    }
+                    idx++;
+                }
         }
     }
     if (MODE == 0) {
