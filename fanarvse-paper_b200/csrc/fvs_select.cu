@@ -316,6 +316,98 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
     }
 }
 
+// threshold (same contract as threshold_kernel) for small batches: one CTA of 256 threads per query; the block
+// maxima of its first-pass cells are located through a prefix of the cells' block counts and loaded all at once
+// (one key per thread and step of NK), then the r-th largest valid key comes from block_rth_largest_reg.
+constexpr int THR_THREADS = 256;
+template <int NK>
+__global__ void __launch_bounds__(THR_THREADS) threshold_reg_kernel(const float* __restrict__ bmc, int MB,
+                                                                    const int32_t* __restrict__ slot,
+                                                                    const int64_t* __restrict__ probe, int nprobe,
+                                                                    int n1, const int64_t* __restrict__ off, int r,
+                                                                    float* __restrict__ t0) {
+    __shared__ int s_base[1024 + 1];
+    __shared__ int s_red[32];
+    __shared__ RegSelectScratch rs;
+    const int q = blockIdx.x, tid = threadIdx.x;
+    // block counts of the first-pass cells, then their exclusive prefix (n1 <= 1024, four cells per thread)
+    int nbl[4], tot = 0;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int j = 4 * tid + u;
+        nbl[u] = 0;
+        if (j < n1) {
+            const int64_t c = probe[(int64_t)q * nprobe + j];
+            const int64_t cs = off[c], ce = off[c + 1];
+            nbl[u] = ce > cs ? (int)((ce - 1) / 32 - cs / 32 + 1) : 0;
+        }
+        tot += nbl[u];
+    }
+    const int lane = tid & 31, warp = tid >> 5;
+    int incl = tot;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_red[warp] = incl;
+    __syncthreads();
+    int before = 0, n = 0;
+#pragma unroll
+    for (int w = 0; w < THR_THREADS / 32; w++) {
+        if (w < warp) before += s_red[w];
+        n += s_red[w];
+    }
+    int run = before + incl - tot;
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+        const int j = 4 * tid + u;
+        if (j < n1) s_base[j] = run;
+        run += nbl[u];
+    }
+    if (tid == 0) s_base[n1] = n;
+    __syncthreads();
+    // key i belongs to the cell j with s_base[j] <= i < s_base[j + 1]
+    uint32_t hk[NK];  // 0 = no key or an empty block (-1e30)
+    int nvalid = 0;
+#pragma unroll
+    for (int u = 0; u < NK; u++) {
+        const int i = tid + THR_THREADS * u;
+        hk[u] = 0u;
+        if (i < n) {
+            int lo = 0, hi = n1 - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (s_base[mid] <= i) lo = mid; else hi = mid - 1;
+            }
+            const float v = bmc[(int64_t)slot[(int64_t)q * n1 + lo] * MB + (i - s_base[lo])];
+            if (v > -1e29f) {
+                hk[u] = f2o(v);
+                nvalid++;
+            }
+        }
+    }
+    nvalid = block_sum_int(nvalid, s_red);
+    float res;
+    if (nvalid >= r) {
+        int above, equal;
+        res = o2f(block_rth_largest_reg<NK>(hk, r, rs, &above, &equal));
+    } else if (nvalid > 0) {
+        uint32_t m = 0xffffffffu;
+#pragma unroll
+        for (int u = 0; u < NK; u++)
+            if (hk[u] != 0u) m = min(m, hk[u]);
+        m = __reduce_min_sync(0xffffffffu, m);
+        if (lane == 0) s_red[warp] = (int)m;
+        __syncthreads();
+        m = __reduce_min_sync(0xffffffffu, lane < THR_THREADS / 32 ? (uint32_t)s_red[lane] : 0xffffffffu);
+        res = o2f(m);
+    } else {
+        res = 1e30f;
+    }
+    if (tid == 0) t0[q] = res;
+}
+
 // ------------------------------------------------------------------------------------------------ warp-per-query
 constexpr int WQ_WARPS = 8;  // queries per CTA in the warp-per-query kernels
 
@@ -501,6 +593,18 @@ extern "C" int fvs_threshold(fvs_stream_t stream, const float* bmc, int MB, cons
     if (n1 > 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const int cap = n1 * MB;
+    if (B < fvs_sm_count() && cap <= 8 * fvs::THR_THREADS) {  // a small batch: one CTA per query
+        const int NK = (cap + fvs::THR_THREADS - 1) / fvs::THR_THREADS;
+        if (NK <= 1)
+            fvs::threshold_reg_kernel<1><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
+        else if (NK <= 2)
+            fvs::threshold_reg_kernel<2><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
+        else if (NK <= 4)
+            fvs::threshold_reg_kernel<4><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
+        else
+            fvs::threshold_reg_kernel<8><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
+        return fvs_launch_status();
+    }
     const size_t smw = (size_t)fvs::WQ_WARPS * (256 + cap) * 4;
     if (smw <= 96 * 1024) {
         cudaError_t e = fvs_ensure_smem((const void*)fvs::threshold_warp_kernel, smw);
