@@ -19,8 +19,9 @@
 //   warps 8-23  : four epilogue warpgroups, group e on the sub-tiles nb = e (mod 4): tcgen05.ld of the warp's 32 TMEM
 //                 lanes (= code rows) 32 columns (queries) at a time, est = ((acc * qs) * zs) + qcp in fp32 with
 //                 explicit rounding, then first pass: per-query block maximum by one redux.sync.max, or emit:
-//                 per-query ballot over the 32 rows, lane j reserving space for column j with one atomicAdd (a chunk's
-//                 32 atomics in flight together), prefix positions by popc.
+//                 per-row kept-column masks transposed across the warp (lane j: the rows keeping column j), lane j
+//                 reserving space for column j with one atomicAdd (a chunk's 32 atomics in flight together), prefix
+//                 positions by popc, each row's kept estimates picked from registers by a select tree.
 // So the loads and MMAs of the next sub-tiles and tiles overlap the epilogues of the current ones.
 // Every mbarrier wait is bounded; on expiry the CTA raises `status`, drains what it issued, frees TMEM and returns.
 #include <cuda.h>
@@ -88,6 +89,35 @@ struct Params {
     int32_t* status;
     int M, MB;
 };
+
+// 32 x 32 bit-matrix transpose across a warp: lane r holds row r (bit c = entry (r, c)); returns row `lane` of the
+// transpose (bit r = entry (r, lane)).  Five butterfly stages swap the off-diagonal blocks of width 16, 8, 4, 2, 1.
+__device__ __forceinline__ uint32_t transpose32(uint32_t x) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t ms[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+    for (int k = 0; k < 5; k++) {
+        const int j = 16 >> k;
+        const uint32_t m = ms[k];
+        const uint32_t y = __shfl_xor_sync(0xffffffffu, x, j);
+        x = (lane & j) ? ((x & ~m) | ((y >> j) & m)) : ((x & m) | ((y & m) << j));
+    }
+    return x;
+}
+
+// a[jj] for a run-time jj without local memory: a five-level select tree on the index bits (31 selects)
+__device__ __forceinline__ uint32_t select32(const uint32_t (&a)[32], int jj) {
+    uint32_t t16[16], t8[8], t4[4], t2[2];
+#pragma unroll
+    for (int i = 0; i < 16; i++) t16[i] = (jj & 1) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+    for (int i = 0; i < 8; i++) t8[i] = (jj & 2) ? t16[2 * i + 1] : t16[2 * i];
+#pragma unroll
+    for (int i = 0; i < 4; i++) t4[i] = (jj & 4) ? t8[2 * i + 1] : t8[2 * i];
+#pragma unroll
+    for (int i = 0; i < 2; i++) t2[i] = (jj & 8) ? t4[2 * i + 1] : t4[2 * i];
+    return (jj & 16) ? t2[1] : t2[0];
+}
 
 template <int MODE>
 __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_constant__ CUtensorMap zmap, Params p,
@@ -385,9 +415,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                                 }
                             }
                         } else {
-                            // ballots of the chunk's columns (lane jj keeps column jj's, every row its own kept
-                            // columns), then lane jj reserves space for column jj: the chunk's atomics are in flight
-                            // together; finally every row writes only its own kept entries
+                            // every row its kept columns (a bit mask), their transpose (lane jj: the rows keeping
+                            // column jj), then lane jj reserves space for column jj: the chunk's atomics are in
+                            // flight together; finally every row writes only its own kept entries
                             const float4* mt4 = reinterpret_cast<const float4*>(mt + 32 * h);
                             uint32_t mymask = 0, rowmask = 0;
 #pragma unroll
@@ -403,12 +433,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                                         const float est =
                                             __fadd_rn(__fmul_rn(__fmul_rn((float)(int32_t)acc[jj], s4[u]), zr), c4[u]);
                                         const bool keep = rvalid && est >= t4[u];
+                                        acc[jj] = __float_as_uint(est);  // the column's estimate from here on
                                         rowmask |= (uint32_t)keep << jj;
-                                        const uint32_t mask = __ballot_sync(0xffffffffu, keep);
-                                        if (lane == jj) mymask = mask;
                                     }
                                 }
                             }
+                            mymask = transpose32(rowmask);  // lane jj: the rows keeping column jj
                             int mybase = 0;
                             if (mymask) mybase = atomicAdd(p.cnt + mq[32 * h + lane], __popc(mymask));
                             colm[lane] = mymask;
@@ -418,11 +448,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                                 const int jj = __ffs(rowmask) - 1;
                                 rowmask &= rowmask - 1;
                                 const int j = 32 * h + jj;
-                                float accj = 0.f;
-#pragma unroll
-                                for (int u = 0; u < 32; u++)
-                                    if (u == jj) accj = (float)(int32_t)acc[u];
-                                const float est = __fadd_rn(__fmul_rn(__fmul_rn(accj, ms[j]), zr), mc[j]);
+                                const float est = __uint_as_float(select32(acc, jj));
                                 const int idx = colb[jj] + __popc(colm[jj] & ((1u << lane) - 1u));
                                 if (idx < p.M) {
                                     const int64_t o = (int64_t)mq[j] * p.M + idx;
