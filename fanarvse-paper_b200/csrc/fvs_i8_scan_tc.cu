@@ -6,17 +6,17 @@
 //
 // Persistent kernel: one CTA per SM walks the tiles b, b + G, b + 2G, ... of the static work list (skipping cells no
 // query probes).  A tile is split into sub-tiles of up to 64 of the cell's queries; sub-tiles are numbered in walk
-// order (nb).  Warp roles (768 threads):
-//   warp 0      : TMA loads of the 128 x 256 B code tiles (two 128 B-wide boxes, 128 B swizzle), A_STAGES ahead
+// order (nb).  Warp roles (672 threads):
+//   warp 0      : TMA loads of the 128 x 256 B code tiles (two 128 B-wide boxes, 128 B swizzle), A_STAGES (4) ahead
 //   warp 1      : TMEM allocation; lane 0 issues tcgen05.mma.kind::i8 (M=128 rows, N=16..64 queries, K=32 x 8) per
 //                 sub-tile into one of T_STAGES accumulators, and releases a code tile when its last MMA completes
 //                 and a query tile as soon as its own MMAs complete
-//   warps 2-7   : gather: warp 2+g fills the sub-tiles nb = g (mod 6) -- the rows of q8 picked by qid, in the
+//   warps 2-4   : gather: warp 2+g fills the sub-tiles nb = g (mod 3) -- the rows of q8 picked by qid, in the
 //                 canonical K-major 128 B-swizzled layout, into query-tile stage g, and the sub-tile's scales / pair
 //                 constants / thresholds / row scales into the metadata slot of its accumulator stage (nb mod
-//                 T_STAGES, freed by the epilogue together with the accumulator) -- so six sub-tiles' dependent
+//                 T_STAGES, freed by the epilogue together with the accumulator) -- so three sub-tiles' dependent
 //                 loads are in flight at once and a query tile is not held through the epilogue
-//   warps 8-23  : four epilogue warpgroups, group e on the sub-tiles nb = e (mod 4): tcgen05.ld of the warp's 32 TMEM
+//   warps 5-20  : four epilogue warpgroups, group e on the sub-tiles nb = e (mod 4): tcgen05.ld of the warp's 32 TMEM
 //                 lanes (= code rows) 32 columns (queries) at a time, est = ((acc * qs) * zs) + qcp in fp32 with
 //                 explicit rounding, then first pass: per-query block maximum by one redux.sync.max, or emit:
 //                 per-row kept-column masks transposed across the warp (lane j: the rows keeping column j), lane j
@@ -34,10 +34,10 @@ namespace tc {
 using namespace fvs::tcg;
 
 #ifndef FVS_TC_A_STAGES
-#define FVS_TC_A_STAGES 3
+#define FVS_TC_A_STAGES 4
 #endif
 #ifndef FVS_TC_GATHER_WARPS
-#define FVS_TC_GATHER_WARPS 6
+#define FVS_TC_GATHER_WARPS 3
 #endif
 #ifndef FVS_TC_MAXT
 #define FVS_TC_MAXT 512
