@@ -66,8 +66,9 @@ int fvs_pairs_split(fvs_stream_t stream, const int64_t* probe, int B, int nprobe
 
 /*
  * fvs_pairs without the `work` argument, for callers that cannot allocate device memory: host programs that drive
- * the search through a foreign-function binding and own no CUDA allocator, or that must not call cudaMalloc while
- * their stream is being captured into a CUDA graph.  No counterpart in the reference (its pairing is torch code that
+ * the search through a foreign-function binding and own no CUDA allocator, or plugins inside another application
+ * (a database engine, a serving process) whose device memory belongs to that application's own pool and may not be
+ * taken behind its back with cudaMalloc.  No counterpart in the reference (its pairing is torch code that
  * allocates freely).  The per-cell scratch is a file-scope device array of FVS_PAIRS_NOALLOC_MAX_CELLS int32 inside
  * this library, held on every GPU that loads the library until the process exits; NC above that returns FVS_ERANGE.
  * This call allocates nothing: it clears the part of the array it uses, then runs the same kernels as fvs_pairs.

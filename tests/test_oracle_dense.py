@@ -19,22 +19,28 @@ def gd():
 def test_dense_codes_and_scan_match_reference(gd, tag):
     f = gd
     R, K, M = (int(v) for v in f[tag + "params"])
-    # the projections themselves are fp32 GEMMs whose summation order belongs to the BLAS; with the reference's own
-    # CPU product as input the quantisation is bit-exact, and with numpy's product it agrees to one fp16 step
+    # the projections themselves are fp32 GEMMs whose summation order belongs to the BLAS (it changes with the CPU's
+    # vector width and thread count): on the machine that made the fixture the quantisation of torch's product was
+    # bit-exact; elsewhere a last-bit difference in a product can move a code by one step or a row scale by one fp16
+    # step, so those are allowed on a handful of entries.  Everything below starts from the reference's own codes.
     V = torch.from_numpy(f["V"])[:, :R]
     mu = torch.from_numpy(f["mu"])
     zx = ((torch.from_numpy(f["X16"]).float() - mu) @ V).numpy()
     Z, a = O._i8code(zx)
-    np.testing.assert_array_equal(Z, f[tag + "Z"])
-    np.testing.assert_array_equal(a.astype(np.float16), f[tag + "zs"])
+    dz = np.abs(Z.astype(np.int32) - f[tag + "Z"].astype(np.int32))
+    assert dz.max() <= 1 and (dz != 0).mean() < 1e-3
+    a16, g16 = a.astype(np.float16), f[tag + "zs"]
+    ulp = np.abs(a16.view(np.int16).astype(np.int32) - g16.view(np.int16).astype(np.int32))
+    assert ulp.max() <= 1 and (ulp != 0).mean() < 2e-3
     Zn, zsn = O.dense_codes(f["X16"], f["mu"], f["V"], R)
     assert (Zn != f[tag + "Z"]).mean() < 1e-3
     np.testing.assert_allclose(zsn.astype(np.float32), f[tag + "zs"].astype(np.float32), rtol=1e-3)
     zq = ((torch.from_numpy(f["Q"]) - mu) @ V).numpy()
     q8, qs = O._i8code(zq)
-    np.testing.assert_array_equal(q8, f[tag + "q8"])
-    np.testing.assert_array_equal(qs, f[tag + "qs"])
-    zs = f[tag + "zs"]
+    dq = np.abs(q8.astype(np.int32) - f[tag + "q8"].astype(np.int32))
+    assert dq.max() <= 1 and (dq != 0).mean() < 1e-3
+    np.testing.assert_allclose(qs, f[tag + "qs"], rtol=2e-6)
+    Z, zs, q8, qs = f[tag + "Z"], f[tag + "zs"], f[tag + "q8"], f[tag + "qs"]
     out = O.dense_search(q8, qs, Z, zs, K, over=float(f[tag + "over"]), M=M)
     np.testing.assert_array_equal(out["sample"], f[tag + "sample_scores"])
     np.testing.assert_array_equal(out["t0"], f[tag + "t0"])

@@ -1,9 +1,9 @@
 """The allocation-free pair builder (fvs_pairs_noalloc) gives the same pair lists as fvs_pairs, on two calls in a row.
 
 It exists for callers that cannot allocate device memory (a host program binding the library through a foreign-
-function interface without a CUDA allocator, or one capturing its stream into a CUDA graph where cudaMalloc is not
-allowed): its per-cell scratch is a device array inside the library instead of a caller buffer.  This file is collected
-last so that a failure here does not stop the rest of a -x run."""
+function interface without a CUDA allocator, or a plugin inside an application whose device memory belongs to that
+application's own pool): its per-cell scratch is a device array inside the library instead of a caller buffer.
+This file is collected last so that a failure here does not stop the rest of a -x run."""
 import numpy as np
 import pytest
 import torch
