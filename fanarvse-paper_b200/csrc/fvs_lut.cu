@@ -154,7 +154,17 @@ struct RecSet {
 
 // GAC: the table stride GA as a compile-time constant (32 or 64), so that a lookup's address is a shift and a mask of
 // the plane word plus an immediate; 0 = GA from the argument.
-template <bool HALF, int WPL, bool REC, int GAC>
+// WCOL: one table column per plane word instead of one per 32-coordinate block.  Column w (stride GA = 32 * WPL)
+// holds the 8 x 16 entries of the block that word w covers, so a block coded with b planes appears in b columns.  In
+// the per-block layout the lanes holding different planes of one block read the same bank at different entries
+// (up to b-way conflicts per lookup); with a column per word, lane l's word lane + 32u sits in bank l and every
+// lookup instruction is conflict-free.  The entries are the same numbers, so the estimates are unchanged.
+// the 4-bit field of w at bits p..p+3, moved to bits 9..12 (p a compile-time constant after unrolling)
+__device__ __forceinline__ uint32_t nibble_at9(uint32_t w, int p) {
+    return (p >= 9 ? (w >> (p - 9)) : (w << (9 - p))) & (15u << 9);
+}
+
+template <bool HALF, int WPL, bool REC, int GAC, bool WCOL = false>
 __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __restrict__ pos, int B, int K,
                                                            const float* __restrict__ qc, const float* __restrict__ Zq,
                                                            int ldz, int D, int GA_, TierSet ts,
@@ -164,7 +174,8 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
                                                            float* __restrict__ sd, RecSet rs) {
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
-    const int GA = GAC ? GAC : GA_;
+    static_assert(!WCOL || WPL == 4, "the column-per-word table is laid out for 4 words per lane (stride 2^9 B)");
+    const int GA = WCOL ? 32 * WPL : (GAC ? GAC : GA_);
     float* lut = reinterpret_cast<float*>(smem);
     int32_t* s_pos = reinterpret_cast<int32_t*>(lut + 128 * GA);  // the query's candidate positions (K)
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nw = blockDim.x >> 5;
@@ -179,10 +190,8 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     const int nblk = D / 32;
     // positions staged once (coalesced), so that each candidate round trip is the plane words alone
     for (int i = tid; i < lim; i += blockDim.x) s_pos[i] = (int32_t)pos[(int64_t)q * K + i];
-    // one 4-coordinate group per thread (ga fastest across lanes: conflict-free stores); entry v sums the selected
-    // coordinates left to right in fp32, as acc += z_i * bit_i does
-    for (int gi = tid; gi < 8 * GA; gi += blockDim.x) {
-        const int ga = gi % GA, cgrp = gi / GA;
+    // entry v of a 4-coordinate group sums the selected coordinates left to right in fp32, as acc += z_i * bit_i does
+    auto entries = [&](int ga, int cgrp, float (&e16)[16]) {
         float z0 = 0.f, z1 = 0.f, z2 = 0.f, z3 = 0.f;
         if (ga < nblk) {
             const float4 zz = *reinterpret_cast<const float4*>(z + 32 * ga + 4 * cgrp);
@@ -191,7 +200,6 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
             z2 = zz.z;
             z3 = zz.w;
         }
-        float* out = lut + (cgrp * 16) * GA + ga;
 #pragma unroll
         for (int v = 0; v < 16; v++) {
             float acc = 0.f;
@@ -199,7 +207,35 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
             if (v & 4) acc = __fadd_rn(acc, z1);
             if (v & 2) acc = __fadd_rn(acc, z2);
             if (v & 1) acc = __fadd_rn(acc, z3);
-            out[v * GA] = HALF ? __half2float(__float2half_rn(acc)) : acc;
+            e16[v] = HALF ? __half2float(__float2half_rn(acc)) : acc;
+        }
+    };
+    if (WCOL) {
+        // one (block, group) per thread, block fastest across lanes; its 16 entries are stored in the column of every
+        // plane word covering the block (tier t, plane p, block j of the tier: column wbase[t] + p * blocks_t + j)
+        for (int gi = tid; gi < 8 * nblk; gi += blockDim.x) {
+            const int ga = gi % nblk, cgrp = gi / nblk;
+            int t = 0;
+            while (t + 1 < ts.T && 32 * ga >= ts.e[t]) t++;
+            if (32 * ga < ts.s[t] || 32 * ga >= ts.e[t]) continue;  // past the last tier: no word reads it
+            float e16[16];
+            entries(ga, cgrp, e16);
+            const int nbt = ts.kb[t] / 4, c0 = ts.wbase[t] + ga - ts.s[t] / 32;
+            for (int pl = 0; pl < ts.bits[t]; pl++) {
+                float* out = lut + (cgrp * 16) * GA + c0 + pl * nbt;
+#pragma unroll
+                for (int v = 0; v < 16; v++) out[v * GA] = e16[v];
+            }
+        }
+    } else {
+        // one 4-coordinate group per thread (ga fastest across lanes: conflict-free stores)
+        for (int gi = tid; gi < 8 * GA; gi += blockDim.x) {
+            const int ga = gi % GA, cgrp = gi / GA;
+            float e16[16];
+            entries(ga, cgrp, e16);
+            float* out = lut + (cgrp * 16) * GA + ga;
+#pragma unroll
+            for (int v = 0; v < 16; v++) out[v * GA] = e16[v];
         }
     }
     if (warp < ts.T) {  // warp t reduces tier t
@@ -237,44 +273,61 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     const float qcv = qc[q];
     // a small batch splits each query's candidates over gridDim.y CTAs (rounds of 2 * nw candidates, round-robin),
     // each with its own copy of the table
-    for (int i0 = warp + blockIdx.y * 2 * nw; i0 < lim; i0 += gridDim.y * 2 * nw) {
-        int64_t nn[2];
-        bool live[2];
-        uint32_t wv[2][WPL];
-        float scl[2], sgl[2];
+    // each warp scores two candidates per round; the next round's plane words are fetched before this round's
+    // lookups, so that a round's load latency overlaps the previous round's table work
+    uint32_t wv[2][WPL], wn[2][WPL];
+    float scl[2], sgl[2], scn[2], sgn[2];
+    const int step = gridDim.y * 2 * nw;
+    auto fetch = [&](int r0, uint32_t (&w)[2][WPL], float (&sc)[2], float (&sg)[2]) {
 #pragma unroll
         for (int c = 0; c < 2; c++) {
-            const int i = i0 + c * nw;
-            live[c] = i < lim;
-            nn[c] = live[c] ? s_pos[i] : 0;
-        }
-#pragma unroll
-        for (int c = 0; c < 2; c++) {
+            const int i = r0 + c * nw;
+            const bool lv = i < lim;
+            const int64_t n = lv ? s_pos[i] : 0;
 #pragma unroll
             for (int u = 0; u < WPL; u++) {
-                wv[c][u] = 0;
-                if (live[c] && wt[u] >= 0) {
+                w[c][u] = 0;
+                if (lv && wt[u] >= 0) {
                     const int t = wt[u];
                     if (REC)
-                        wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(rs.rec + nn[c] * rs.RB) + lane + 32 * u);
+                        w[c][u] = __ldg(reinterpret_cast<const uint32_t*>(rs.rec + n * rs.RB) + lane + 32 * u);
                     else
-                        wv[c][u] = __ldg(reinterpret_cast<const uint32_t*>(
-                            ts.planes[t] + ((int64_t)wp[u] * N + nn[c]) * ts.kb[t] + wj[u]));
+                        w[c][u] = __ldg(reinterpret_cast<const uint32_t*>(
+                            ts.planes[t] + ((int64_t)wp[u] * N + n) * ts.kb[t] + wj[u]));
                 }
             }
             if (REC) {
-                const uint32_t sp = (live[c] && lane < ts.T)
-                                        ? __ldg(reinterpret_cast<const uint32_t*>(rs.rec + nn[c] * rs.RB + rs.soff) + lane)
+                const uint32_t sp = (lv && lane < ts.T)
+                                        ? __ldg(reinterpret_cast<const uint32_t*>(rs.rec + n * rs.RB + rs.soff) + lane)
                                         : 0u;
-                scl[c] = __half2float(__ushort_as_half((unsigned short)(sp & 0xffffu)));
-                sgl[c] = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
+                sc[c] = __half2float(__ushort_as_half((unsigned short)(sp & 0xffffu)));
+                sg[c] = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
             } else {
-                scl[c] = (live[c] && lane < ts.T) ? __half2float(scale[(int64_t)lane * N + nn[c]]) : 0.f;
-                sgl[c] = (live[c] && lane < ts.T) ? __half2float(sig[(int64_t)lane * N + nn[c]]) : 0.f;
+                sc[c] = (lv && lane < ts.T) ? __half2float(scale[(int64_t)lane * N + n]) : 0.f;
+                sg[c] = (lv && lane < ts.T) ? __half2float(sig[(int64_t)lane * N + n]) : 0.f;
             }
+        }
+    };
+    // (with more than 4 words per lane the second set of registers would spill: fetch and score in turn)
+    constexpr bool PREFETCH = WPL <= 4;
+    int i0 = warp + blockIdx.y * 2 * nw;
+    if (PREFETCH && i0 < lim) fetch(i0, wn, scn, sgn);
+    for (; i0 < lim; i0 += step) {
+        if (PREFETCH) {
+#pragma unroll
+            for (int c = 0; c < 2; c++) {
+                scl[c] = scn[c];
+                sgl[c] = sgn[c];
+#pragma unroll
+                for (int u = 0; u < WPL; u++) wv[c][u] = wn[c][u];
+            }
+            if (i0 + step < lim) fetch(i0 + step, wn, scn, sgn);
+        } else {
+            fetch(i0, wv, scl, sgl);
         }
 #pragma unroll
         for (int c = 0; c < 2; c++) {
+            const bool live = i0 + c * nw < lim;
             float part = lane < ts.T ? -dmq * scl[c] : 0.f;
             float var = lane < ts.T ? qn2l * sgl[c] * sgl[c] : 0.f;
 #pragma unroll
@@ -282,20 +335,35 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
                 const int t = wt[u];
                 const float st = __shfl_sync(0xffffffffu, scl[c], t < 0 ? 0 : t);
                 if (t >= 0) {
-                    const float* lt = lut + wg[u];
                     const uint32_t w = wv[c][u];
                     float a = 0.f;
+                    if (WCOL) {
+                        // byte offset of entry (c, v, column) = (c * 16 + v) * GA * 4 + column * 4 with GA * 4 = 2^9:
+                        // the nibble shifted to bits 9..12 and or-ed with the lane's column offset
+                        const uint32_t cb = (uint32_t)(lane + 32 * u) * 4u;
+                        const char* tb = reinterpret_cast<const char*>(lut);
 #pragma unroll
-                    for (int bi = 0; bi < 4; bi++) {
-                        const uint32_t byt = (w >> (8 * bi)) & 0xffu;
-                        a += lt[((2 * bi) * 16 + (byt >> 4)) * GA] + lt[((2 * bi + 1) * 16 + (byt & 15u)) * GA];
+                        for (int bi = 0; bi < 4; bi++) {
+                            const float xh = *reinterpret_cast<const float*>(
+                                tb + (2 * bi) * 16 * GA * 4 + (nibble_at9(w, 8 * bi + 4) | cb));
+                            const float xl = *reinterpret_cast<const float*>(
+                                tb + (2 * bi + 1) * 16 * GA * 4 + (nibble_at9(w, 8 * bi) | cb));
+                            a += xh + xl;
+                        }
+                    } else {
+                        const float* lt = lut + wg[u];
+#pragma unroll
+                        for (int bi = 0; bi < 4; bi++) {
+                            const uint32_t byt = (w >> (8 * bi)) & 0xffu;
+                            a += lt[((2 * bi) * 16 + (byt >> 4)) * GA] + lt[((2 * bi + 1) * 16 + (byt & 15u)) * GA];
+                        }
                     }
                     part += a * wsc[u] * st;
                 }
             }
             part = warp_sum(part);
             var = warp_sum(var);
-            if (lane == 0 && live[c]) {
+            if (lane == 0 && live) {
                 est[(int64_t)q * K + i0 + c * nw] = qcv + part;
                 sd[(int64_t)q * K + i0 + c * nw] = sqrtf(var);
             }
@@ -411,23 +479,24 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
     if (wpl > 12) return FVS_ERANGE;
     const int GA = ((D / 32) + 31) / 32 * 32;
     FVS_CHECK_ARG(D % 32 == 0);
-    const size_t sm = (size_t)128 * GA * 4 + (size_t)K * 4;
+    // up to 128 plane words: one table column per word (conflict-free lookups, 64 KB); more: one column per block
+    const bool wcol = wpl <= 4;
+    const size_t sm = (size_t)128 * (wcol ? 128 : GA) * 4 + (size_t)K * 4;
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const fvs::RecSet rs{nullptr, 0, 0};
     const int S = fvs::lut_split(B, K);
-#define FVS_LZ(H, W)                                                                                               \
+#define FVS_LZ(H, W, C)                                                                                            \
     do {                                                                                                           \
-        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false, 0>, sm);               \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false, 0, C>, sm);            \
         if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W, false, 0><<<dim3(B, S), 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,       \
-                                                                     (const __half*)scale, (const __half*)sig, N,  \
-                                                                     ncnt, est, sd, rs);                           \
+        fvs::lut_score_zq_kernel<H, W, false, 0, C><<<dim3(B, S), 256, sm, stream>>>(                              \
+            pos, B, K, qc, Zq, ldz, D, GA, ts, (const __half*)scale, (const __half*)sig, N, ncnt, est, sd, rs);    \
     } while (0)
     if (half) {
-        if (wpl <= 4) FVS_LZ(true, 4); else if (wpl <= 8) FVS_LZ(true, 8); else FVS_LZ(true, 12);
+        if (wcol) FVS_LZ(true, 4, true); else if (wpl <= 8) FVS_LZ(true, 8, false); else FVS_LZ(true, 12, false);
     } else {
-        if (wpl <= 4) FVS_LZ(false, 4); else if (wpl <= 8) FVS_LZ(false, 8); else FVS_LZ(false, 12);
+        if (wcol) FVS_LZ(false, 4, true); else if (wpl <= 8) FVS_LZ(false, 8, false); else FVS_LZ(false, 12, false);
     }
 #undef FVS_LZ
     return fvs_launch_status();
@@ -453,26 +522,29 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     const int wpl = (ts.nwords + 31) / 32;
     if (wpl > 12) return FVS_ERANGE;
     const int GA = ((D / 32) + 31) / 32 * 32;
-    const size_t sm = (size_t)128 * GA * 4 + (size_t)K * 4;
+    // up to 128 plane words: one table column per word (conflict-free lookups, 64 KB); more: one column per block
+    const bool wcol = wpl <= 4;
+    const size_t sm = (size_t)128 * (wcol ? 128 : GA) * 4 + (size_t)K * 4;
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const fvs::RecSet rs{rec, RB, soff};
     const int S = fvs::lut_split(B, K);
-#define FVS_LRG(H, W, G)                                                                                           \
+#define FVS_LRG(H, W, G, C)                                                                                        \
     do {                                                                                                           \
-        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true, G>, sm);                \
+        cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true, G, C>, sm);             \
         if (e != cudaSuccess) return (int)e;                                                                       \
-        fvs::lut_score_zq_kernel<H, W, true, G><<<dim3(B, S), 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, GA, ts,        \
-                                                                       nullptr, nullptr, N, ncnt, est, sd, rs);    \
+        fvs::lut_score_zq_kernel<H, W, true, G, C><<<dim3(B, S), 256, sm, stream>>>(                               \
+            pos, B, K, qc, Zq, ldz, D, GA, ts, nullptr, nullptr, N, ncnt, est, sd, rs);                            \
     } while (0)
 #define FVS_LR(H, W)                                                                                               \
     do {                                                                                                           \
-        if (GA == 64) FVS_LRG(H, W, 64); else if (GA == 32) FVS_LRG(H, W, 32); else FVS_LRG(H, W, 0);            \
+        if (GA == 64) FVS_LRG(H, W, 64, false); else if (GA == 32) FVS_LRG(H, W, 32, false);                      \
+        else FVS_LRG(H, W, 0, false);                                                                              \
     } while (0)
     if (half) {
-        if (wpl <= 4) FVS_LR(true, 4); else if (wpl <= 8) FVS_LR(true, 8); else FVS_LR(true, 12);
+        if (wcol) FVS_LRG(true, 4, 0, true); else if (wpl <= 8) FVS_LR(true, 8); else FVS_LR(true, 12);
     } else {
-        if (wpl <= 4) FVS_LR(false, 4); else if (wpl <= 8) FVS_LR(false, 8); else FVS_LR(false, 12);
+        if (wcol) FVS_LRG(false, 4, 0, true); else if (wpl <= 8) FVS_LR(false, 8); else FVS_LR(false, 12);
     }
 #undef FVS_LR
 #undef FVS_LRG
