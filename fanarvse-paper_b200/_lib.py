@@ -22,6 +22,7 @@ SIGNATURES = {
     "fvs_arch": (C.c_char_p, []),
     "fvs_i8_tile_rows": (I32, []),
     "fvs_quantize": (I32, [P, P, I32, I32, I32, P, P]),
+    "fvs_query_prep": (I32, [P, P, I32, I32, I32, P, P, P]),
     "fvs_route_topk": (I32, [P, P, I32, I32, I32, P]),
     "fvs_pairs": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P]),
     "fvs_pairs_split": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P]),

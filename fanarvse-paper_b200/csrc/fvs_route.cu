@@ -228,7 +228,39 @@ __global__ void quantize_kernel(const float* __restrict__ z, int B, int R, int l
     if (lane == 0) qs[q] = sc;
 }
 
+// One warp per query row: the row is read once as float4 (16-byte loads), written back as fp16 (round to nearest
+// even, as a tensor's .half() conversion), and dotted with c in fp32 (per-lane partial sums, then a warp reduction).
+__global__ void query_prep_kernel(const float* __restrict__ Q, int B, int d, int ldq, const float* __restrict__ c,
+                                  __half* __restrict__ Qh, float* __restrict__ qc) {
+    const int q = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (q >= B) return;
+    const float4* row = reinterpret_cast<const float4*>(Q + (int64_t)q * ldq);
+    const float4* cv = reinterpret_cast<const float4*>(c);
+    uint2* out = reinterpret_cast<uint2*>(Qh + (int64_t)q * d);
+    float acc = 0.f;
+    for (int i = lane; i < d / 4; i += 32) {
+        const float4 x = row[i], y = cv[i];
+        acc = fmaf(x.x, y.x, acc);
+        acc = fmaf(x.y, y.y, acc);
+        acc = fmaf(x.z, y.z, acc);
+        acc = fmaf(x.w, y.w, acc);
+        const __half2 lo = __floats2half2_rn(x.x, x.y), hi = __floats2half2_rn(x.z, x.w);
+        out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    }
+    acc = warp_sum(acc);
+    if (lane == 0 && qc) qc[q] = acc;
+}
+
 }  // namespace fvs
+
+extern "C" int fvs_query_prep(fvs_stream_t stream, const float* Q, int B, int d, int ldq, const float* c, uint16_t* Qh,
+                              float* qc) {
+    FVS_CHECK_ARG(Q && c && Qh && B >= 0 && d > 0 && d % 4 == 0 && ldq >= d && ldq % 4 == 0);
+    FVS_CHECK_ARG(((uintptr_t)Q & 15) == 0 && ((uintptr_t)c & 15) == 0 && ((uintptr_t)Qh & 7) == 0);
+    if (B == 0) return FVS_OK;
+    fvs::query_prep_kernel<<<(B + 7) / 8, 256, 0, stream>>>(Q, B, d, ldq, c, (__half*)Qh, qc);
+    return fvs_launch_status();
+}
 
 extern "C" int fvs_quantize(fvs_stream_t stream, const float* z, int B, int R, int ldz, int8_t* q8, float* qs) {
     FVS_CHECK_ARG(z && q8 && qs && B >= 0 && R > 0 && ldz >= R);

@@ -192,6 +192,17 @@ class EngineB200I8:
         self.launches += 1
 
     # ------------------------------------------------------------------ stage 1
+    def query_prep(self, Qb):
+        """QC = Qb @ c and Qh = fp16(Qb) (`throughput/enginei8.py:63, 67`) in one pass over the fp32 queries."""
+        B, d = Qb.shape
+        c = self.ix.c
+        if Qb.dtype != torch.float32 or d % 4 or Qb.stride(1) != 1 or Qb.stride(0) % 4 or Qb.data_ptr() % 16:
+            return (Qb @ c).contiguous(), Qb.half()          # shapes the vectorised kernel does not take
+        Qh = torch.empty(B, d, dtype=torch.float16, device=Qb.device)
+        QC = torch.empty(B, device=Qb.device)
+        self._call("query_prep", self.L.fvs_query_prep, ptr(Qb), B, d, Qb.stride(0), ptr(c), ptr(Qh), ptr(QC))
+        return QC, Qh
+
     def quantize(self, Qb):
         """q8, qs (`throughput/enginei8.py:38`): fp32 projection by cuBLAS, then one quantisation kernel."""
         z = (Qb @ self.ix.Vr).contiguous()
@@ -237,9 +248,9 @@ class EngineB200I8:
         ncnt = torch.empty(B, dtype=torch.int32, device=dev) if use_delta else None
         self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
                    ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
-        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, npairs=int(qid.numel()),
-                          bval=bval, bpos=bpos, slot=slot)
-        return pos, ok.bool(), est1, ncnt
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, ccnt1=ccnt1,
+                          npairs=int(qid.numel()), bval=bval, bpos=bpos, slot=slot, ncnt=ncnt)
+        return pos, ok.view(torch.bool), est1, ncnt
 
     def _ident(self, n):
         """slot[i] = i (the streaming scan's pair slots), cached.  A captured graph keeps the address of the tensor it
@@ -277,7 +288,7 @@ class EngineB200I8:
                    ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
         self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=None, npairs=B * npr, bval=bval,
                           bpos=bpos, slot=slot[:B * n1], probe=probe)
-        return pos, ok.bool(), est1, ncnt
+        return pos, ok.view(torch.bool), est1, ncnt
 
     # ------------------------------------------------------------------ stages 2-3
     def luts(self, Qb, half, Zq=None):
@@ -356,8 +367,7 @@ class EngineB200I8:
         """`throughput/enginei8.py:61-70` (NROUTE branch)."""
         if K <= k or K < 10:
             raise ValueError("need K > k and K >= 10 (the delta rule reads the 10th stage-1 estimate)")
-        QC = (Qb @ self.ix.c).contiguous()
-        Qh = Qb.half()                       # one fp16 copy of the queries for the routing and rotation products
+        QC, Qh = self.query_prep(Qb)         # one fp16 copy of the queries for the routing and rotation products
         QM, probe = self.route(Qb, nprobe, Qh)
         q8, qs = self.quantize(Qb)
         pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs))
@@ -450,26 +460,35 @@ class EngineB200I8:
             torch.cuda.current_stream().wait_stream(st)
             g = torch.cuda.CUDAGraph()
             n0 = self.launches
-            hflags = torch.empty(B + 2, dtype=torch.int32, pin_memory=True)
+            hok = torch.empty(B, dtype=torch.uint8, pin_memory=True)
+            hst = torch.empty(2, dtype=torch.int32, pin_memory=True)
             with torch.cuda.graph(g):
-                outs = self._gpu(qs, K, z, nprobe, k)
+                ok, I, nr, ids = self._gpu(qs, K, z, nprobe, k)
+                # the results as one int32 block (reads as int64 first, then I, then the candidate ids), so that a
+                # replay's results leave the graph's buffers in one copy
+                packed = torch.cat([nr.view(torch.int32), I.reshape(-1), ids.reshape(-1)])
                 # exactness flags, status word and flagged count land in pinned host memory inside the graph
-                hflags.copy_(torch.cat([outs[0].to(torch.int32), self.status, self._nflag]), non_blocking=True)
+                hok.copy_(ok.view(torch.uint8), non_blocking=True)
+                hst[0:1].copy_(self.status, non_blocking=True)
+                hst[1:2].copy_(self._nflag, non_blocking=True)
             self.graph_launches[key] = self.launches - n0
-            self.graphs[key] = (g, qs, outs, hflags.numpy())
-        g, qs, (ok, I, nr, ids), flags = self.graphs[key]
+            self.graphs[key] = (g, qs, packed, (I.shape[1], ids.shape[1]), hok.numpy(), hst.numpy())
+        g, qs, packed, (kk, KK), hok, hst = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
-        I, nr, ids = I.clone(), nr.clone(), ids.clone()
+        P = packed.clone()
+        nr = P[:2 * B].view(torch.int64)
+        I = P[2 * B:2 * B + B * kk].view(B, kk)
+        ids = P[2 * B + B * kk:].view(B, KK)
         torch.cuda.current_stream().synchronize()                # the only synchronisation
-        if int(flags[-2]) != 0:
+        if int(hst[0]) != 0:
             raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
         in_graph = self.FB_INGRAPH and B >= self.FB_MIN_BATCH
         if in_graph:
-            self.nbad += int(flags[-1])                # recomputed inside the graph (or below, beyond capacity)
-        if not bool(flags[:-2].all()):
-            bad = torch.from_numpy(np.nonzero(flags[:-2] == 0)[0])
+            self.nbad += int(hst[1])                   # recomputed inside the graph (or below, beyond capacity)
+        if not bool(hok.all()):
+            bad = torch.from_numpy(np.nonzero(hok == 0)[0])
             if not in_graph:
                 self.nbad += len(bad)
             a, b, c = self._fallback_graphed(Qb, bad, K, z, nprobe, k)

@@ -30,6 +30,15 @@ int fvs_version(void);
 const char* fvs_arch(void);
 
 /*
+ * Per-batch query preparation in one pass over the fp32 queries Q [B, ldq]: Qh [B, d] = fp16(Q) (round to nearest
+ * even: the `Qb.half()` operand of the routing and rotation products, `throughput/enginei8.py:67`,
+ * `throughput/s2lut.py:122`) and qc[q] = <Q[q, :d], c> in fp32 (`QC = Qb @ s1["c"]`, `throughput/enginei8.py:63`;
+ * summation order differs from the BLAS product).  qc may be NULL.  d % 4 == 0; Q, c 16-byte aligned, Qh 8-byte.
+ */
+int fvs_query_prep(fvs_stream_t stream, const float* Q, int B, int d, int ldq, const float* c, uint16_t* Qh,
+                   float* qc);
+
+/*
  * Query quantisation (`throughput/enginei8.py:38`): qs[q] = max(max_r |z[q,r]|, 1e-12) / 127,
  * q8[q,r] = clamp(round_half_even(z[q,r] / qs[q]), -127, 127); z [B, ldz] f32 = Q @ Vr.
  */

@@ -371,6 +371,29 @@ def test_quantize_matches_reference_formula(eng):
     np.testing.assert_array_equal(c(q8), c(q8_ref))
 
 
+@pytest.mark.parametrize("B,d,ldq", [(1, 1536, 1536), (257, 768, 768), (33, 1536, 1600)])
+def test_query_prep_matches_torch(eng, B, d, ldq):
+    """fvs_query_prep: the fp16 copy equals `Qb.half()` bit for bit; the centre product equals `Qb @ c` within fp32
+    summation-order rounding."""
+    L = pkg("_lib")
+    lib = L.lib()
+    g = torch.Generator(device=DEV).manual_seed(B)
+    Qfull = torch.randn(B, ldq, device=DEV, generator=g)
+    Qfull[0, :8] = torch.tensor([1e-8, -1e-8, 65504.0, 70000.0, -3.5, 0.0, -0.0, 2.0 ** -24], device=DEV)
+    Q = Qfull[:, :d]
+    cvec = torch.randn(d, device=DEV, generator=g)
+    Qh = torch.empty(B, d, dtype=torch.float16, device=DEV)
+    qc = torch.empty(B, device=DEV)
+    L.check(lib.fvs_query_prep(L.stream_handle(), L.ptr(Qfull), B, d, ldq, L.ptr(cvec), L.ptr(Qh), L.ptr(qc)),
+            "query_prep")
+    np.testing.assert_array_equal(c(Qh.view(torch.int16)), c(Q.half().view(torch.int16)))
+    ref = (Q.double() @ cvec.double()).float()
+    scale = (Q.abs().double() @ cvec.abs().double()).float()
+    assert ((qc - ref).abs() <= 1e-5 * scale + 1e-30).all()
+    assert lib.fvs_query_prep(L.stream_handle(), L.ptr(Qfull), B, d + 2, ldq, L.ptr(cvec), L.ptr(Qh),
+                              L.ptr(qc)) == -1                     # d not a multiple of 4
+
+
 def test_search_host_matches_search(eng):
     """latency mode (ids copied to pinned host memory inside the graph) returns the device search's ids"""
     synth, ib = pkg("synth"), pkg("index_build")
