@@ -203,6 +203,7 @@ extern "C" int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const i
                           int32_t* ids, int32_t* I, int32_t* reads, float* score_k) {
     FVS_CHECK_ARG(H && order && pos && est && sd && Q && ids && I && reads);
     FVS_CHECK_ARG(d > 0 && d % 8 == 0 && ldq >= d && ldq % 4 == 0 && B >= 0 && k >= 1 && K > k);
+    FVS_CHECK_ARG(((uintptr_t)Q & 15) == 0 && ((uintptr_t)H & 15) == 0);   // 16-byte row loads
     if (K > 4096 || k > 256) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     int kp = 1;
