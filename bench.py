@@ -40,6 +40,10 @@ GRID = [(64, 90, 8192, 0.65, 16), (72, 100, 8192, 0.65, 8), (72, 100, 8192, 0.65
         (160, 120, 8192, 0.65, 16), (192, 150, 8192, 0.65, 16), (256, 150, 8192, 0.65, 16), (352, 175, 8192, 0.65, 16)]
 
 
+# (nprobe, K, M, rho) of the reference arm under --op auto: the point the B200 arm's grid selects on the bench data
+REFERENCE_ARM_OP = (72, 100, 8192, 0.65)
+
+
 def pkg(name):
     return importlib.import_module("fanarvse-paper_b200." + name)
 
@@ -592,17 +596,22 @@ def reference_arm(args, rank, world, local):
     ds = synth.make_dataset(spec, dev, gt_k=10)
     s1, i8, codes = ib.build_index(ds["base16"], synth.default_nlist(args.rows), R=256, seed=0)
     oi = oracle_index_cpu(s1, i8, codes["uniform"], ds["base16"])
-    npr, K, M = (int(x) for x in args.op.split(":")) if args.op != "auto" else (192, 150, 3072)
+    if args.op == "auto":       # the operating point the B200 arm's grid selects on this data (recall@10 0.991)
+        npr, K, M, rho = REFERENCE_ARM_OP
+    else:
+        f = args.op.split(":")
+        npr, K, M = (int(x) for x in f[:3])
+        rho = float(f[3]) if len(f) > 3 else None
     Q = ds["queries"]
     nq = 8
-    t8 = 1.0 / cpu_oracle_qps(oi, Q, K, args.z, npr, 10, M, nq) * nq
-    per_step = max(1, min(256, int(round(nq * 150.0 / (args.steps + args.warmup) / max(t8, 1e-6)))))
+    t8 = 1.0 / cpu_oracle_qps(oi, Q, K, args.z, npr, 10, M, nq, rho) * nq
+    per_step = max(1, min(256, args.batch, int(round(nq * 150.0 / (args.steps + args.warmup) / max(t8, 1e-6)))))
     for i in range(args.warmup):
-        cpu_oracle_qps(oi, Q[i * per_step % args.batch:], K, args.z, npr, 10, M, per_step)
+        cpu_oracle_qps(oi, Q[i * per_step % args.batch:], K, args.z, npr, 10, M, per_step, rho)
     t = time.perf_counter()
     for i in range(args.steps):
         s = (i * per_step) % max(1, args.batch - per_step)
-        cpu_oracle_qps(oi, Q[s:], K, args.z, npr, 10, M, per_step)
+        cpu_oracle_qps(oi, Q[s:], K, args.z, npr, 10, M, per_step, rho)
     el = time.perf_counter() - t
     qps = args.steps * per_step / el
     cb = {"value": round(qps, 3), "unit": "queries/s", "cores": torch.get_num_threads(), "kind": "port",
@@ -612,7 +621,7 @@ def reference_arm(args, rank, world, local):
             "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic", "impl": "reference",
             "config": {"workload": f"{args.rows // 1000000}M x {args.dim} fp16, throughput mode (CPU oracle of the "
                                    f"reference path), batch {args.batch} sampled {per_step}/step, k=10",
-                       "global_batch": args.batch, "nprobe": npr, "K": K, "M": M, "z": args.z},
+                       "global_batch": args.batch, "nprobe": npr, "K": K, "M": M, "rho": rho, "z": args.z},
             "cpu_baseline": cb, "e2e": {"value": round(qps, 3), "unit": "queries/s", "h2d_bytes_per_step": 0,
                                         "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
