@@ -189,8 +189,12 @@ def first_bytes(E, B, R=256):
     first-pass pairs (qid, qcp), the queries, and one block maximum per (pair, 32-row block of its cell)."""
     last = E._last
     off = E.ix.off_np
-    c1 = last["ccnt1"].cpu().numpy().astype(np.int64)
     n = np.diff(off)
+    if last.get("ccnt1") is not None:
+        c1 = last["ccnt1"].cpu().numpy().astype(np.int64)
+    else:                                   # streaming small-batch scan: the first n1 cells of each probe list
+        first = last["probe"][:, :last["n1"]].cpu().numpy().ravel()
+        c1 = np.bincount(first, minlength=len(n)).astype(np.int64)
     nblk = np.where(n > 0, (off[1:] - 1) // 32 - off[:-1] // 32 + 1, 0)
     return int(n[c1 > 0].sum()) * (R + 4) + int(c1.sum()) * 8 + B * (R + 12) + int((c1 * nblk).sum()) * 4
 
@@ -218,6 +222,45 @@ def kernel_timing(E, Q, K, z, npr, k, reps):
     out = {n: float(np.mean([a.elapsed_time(b) for a, b in v])) for n, v in E.timing.items()}
     E.timing = None
     return out, {"first": float(np.mean(fb)), "emit": float(np.mean(eb)), "lut": float(np.mean(lb))}
+
+
+def batch1_scan(E, q1, K, z, npr, k, peak, reps=50):
+    """The emit pass of one query's streaming scan (`fvs_i8_scan_small`) alone: one eager search sets up its inputs,
+    then `reps` launches (each after zeroing its counter) are captured in a CUDA graph and replayed between CUDA
+    events on the launching stream."""
+    L, ix = E.L, E.ix
+    E.search_eager(q1, K, z, npr, k)
+    last = dict(E._last)
+    nbytes = emit_bytes(E, 1)
+    QM, probe = E.route(q1, npr)
+    args = (1, ptr(last["q8"]), ptr(last["qs"]), 1, ix.R, ptr(probe), npr, npr, ptr(QM), ix.NC, ptr(ix.mnorm),
+            ptr(ix.off), ptr(ix.Z), ptr(ix.zs), ptr(last["t0"]), ptr(last["cnt"]), ptr(last["bval"]),
+            ptr(last["bpos"]), last["M"], None, ix.MB)
+    cnt = last["cnt"]
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(reps):
+                cnt.zero_()
+                _lib_check(L.fvs_i8_scan_small(pkg("_lib").stream_handle(st), *args), "i8_scan_small")
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    ms = timed(g.replay, 5) / reps
+    emitted = int(cnt.item())
+    del g
+    return {"kernel": "fvs_i8_scan_small (emit pass, 1 query, with its counter reset)", "algorithmic_bytes": nbytes,
+            "launch_ms": round(ms, 5), "achieved": round(nbytes / (ms * 1e-3) / 1e9, 1),
+            "frac": round(nbytes / (ms * 1e-3) / 1e9 / peak, 4), "emitted": emitted}
+
+
+def _lib_check(rc, what):
+    pkg("_lib").check(rc, what)
+
+
+def ptr(t):
+    return pkg("_lib").ptr(t)
 
 
 def load_peaks():
@@ -535,6 +578,9 @@ def main():
                           "achieved": round(ach_l, 1), "frac_of_hbm": round(ach_l / peak, 4),
                           "traffic": load_traffic("lut_score")},
             "kernel_ms": {n: round(v, 4) for n, v in kt.items()}}
+    # ---- the batch-1 scan (streaming small-batch kernel), same operating point: a few MB per launch, so launch and
+    # load latency rather than bandwidth bound it
+    roof["batch1_scan"] = batch1_scan(E, Qs[1][:1], K, z, npr, k, peak)
     cpu = None
     if rank == 0 and world == 1:
         oi = oracle_index_cpu(s1, i8, code, ds["base16"])
