@@ -112,19 +112,29 @@ class ShardedSearch:
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             n0 = self.local.launches
+            hf = torch.empty(3, dtype=torch.int32, pin_memory=True)
             with torch.cuda.graph(g):
                 outs = self._graph_body(qs, K, z, nprobe, k)
-            self.graphs[key] = (g, qs, outs, self.local.launches - n0 + 2)   # + exact scores, merge
-        g, qs, (ok, I, reads, ids, Ig, Sg, flags), nl = self.graphs[key]
+                _, _, reads, _, Ig, Sg, flags = outs
+                # the step's results as one int32 block (reads and global ids as int64 words first, then the scores),
+                # so that one copy takes them out of the graph's buffers; the flags go to pinned host memory
+                packed = torch.cat([reads.view(torch.int32), Ig.reshape(-1).view(torch.int32),
+                                    Sg.reshape(-1).view(torch.int32)])
+                hf.copy_(flags, non_blocking=True)
+            self.graphs[key] = (g, qs, outs, packed, hf.numpy(), self.local.launches - n0 + 2)  # + exact, merge
+        g, qs, (ok, I, reads, ids, Ig, Sg, flags), packed, f, nl = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
         self.local.replayed_launches = getattr(self.local, "replayed_launches", 0) + nl
-        f = flags.cpu()                                        # the only synchronisation
+        P = packed.clone()
+        torch.cuda.current_stream().synchronize()              # the only synchronisation
         self.local.nbad += int(f[2])
         if int(f[1]) != 0:
             raise _lib.FvsError("sharded search: a bounded device wait expired on some rank (status flag set)")
         if int(f[0]) == 0:
-            return Ig.clone(), Sg.clone(), reads.clone()
+            B, n = len(Qb), Ig.numel()
+            return (P[2 * B:2 * B + 2 * n].view(torch.int64).view(B, k),
+                    P[2 * B + 2 * n:].view(torch.float32).view(B, k), P[:2 * B].view(torch.int64))
         # some rank has flagged rows left: every rank recomputes its own (possibly none) and exchanges again
         self.eager_steps += 1
         E = self.local
