@@ -538,8 +538,14 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         e2e_ms = float(t)
+    # the host-to-device copy alone (same pinned buffers, copy stream), which bounds the loop when it is slower than
+    # the search: the link's speed differs between boxes
+    for _ in range(3):
+        Qd[0].copy_(Qh[0], non_blocking=True)
+    h2d_ms = timed(lambda: Qd[0].copy_(Qh[1], non_blocking=True), 20)
     e2e = {"value": args.batch / (e2e_ms / 1e3) * scale_rows, "unit": "queries/s",
-           "h2d_bytes_per_step": int(Q0.numel() * 4), "d2h_bytes_per_step": int(args.batch * k * 4)}
+           "h2d_bytes_per_step": int(Q0.numel() * 4), "d2h_bytes_per_step": int(args.batch * k * 4),
+           "h2d_copy_ms": round(h2d_ms, 4), "h2d_copy_gbs": round(Q0.numel() * 4 / (h2d_ms * 1e-3) / 1e9, 1)}
     # ---- batch-1 latency (one query per search, graph path), p50
     lat = []
     for i in range(60):
