@@ -12,7 +12,7 @@ Every kernel launch (`_first8c`, `_emit8c`, `_lut_kernel`, `_score_lut`, `_stage
 after the launch, so the fixture holds the reference's own intermediate values (pairs, bmc, t0, cnt/bval/bpos, LUT,
 est/sd, scores) next to the final (ok, I, reads, ids).
 
-Usage:  python tests/golden/make_golden.py [--ref /root/reference] [--out tests/golden]
+Usage:  python tests/golden/make_golden.py --ref <checkout of the reference repository> [--out tests/golden]
 """
 from __future__ import annotations
 
@@ -168,7 +168,7 @@ def pack_case(prefix, ds_Q, s1, i8, code, H16, out, recs, nmain, E, K, z, nprobe
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository (read only)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     mods = load_reference(args.ref)

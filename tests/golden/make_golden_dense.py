@@ -5,7 +5,7 @@ threshold-emit kernel `_scan` MODE=1) on CPU tensors under the Triton interprete
 power of two (`tl.arange(0, R)`), so the goldens use R = 128 and R = 256; the B200 kernel's R = 1536 case is checked
 against the oracle restatement pinned here.
 
-Usage:  python tests/golden/make_golden_dense.py [--ref /root/reference] [--out tests/golden]
+Usage:  python tests/golden/make_golden_dense.py --ref <checkout of the reference repository> [--out tests/golden]
 """
 from __future__ import annotations
 
@@ -29,7 +29,7 @@ from make_golden import Rec  # noqa: E402
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository (read only)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     sys.path[:0] = [f"{args.ref}/throughput"]

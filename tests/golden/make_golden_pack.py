@@ -1,7 +1,7 @@
 """Golden packed refinement records from the reference's own `tiered_fused.pack` (`src/tiered_fused.py:112-125`),
 applied to the tiered codes stored in the throughput-mode and default-engine golden files.
 
-Usage:  python tests/golden/make_golden_pack.py [--ref /root/reference] [--out tests/golden]
+Usage:  python tests/golden/make_golden_pack.py --ref <checkout of the reference repository> [--out tests/golden]
 """
 from __future__ import annotations
 
@@ -19,7 +19,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository (read only)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     sys.path[:0] = [f"{args.ref}/src"]

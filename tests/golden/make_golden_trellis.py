@@ -10,7 +10,7 @@ zero-copy reads of pinned memory) becomes the identity.  The trellis code itself
 reference's own encoder functions (`trellis.make_table`, `trellis.viterbi`, `trellis_scan.viterbi_paths`,
 `trellis_scan.paths_to_words`) following `src/rev_fanardb.py:36-58` and `src/engine_cell.py:8-24`.
 
-Usage:  python tests/golden/make_golden_trellis.py [--ref /root/reference] [--out tests/golden]
+Usage:  python tests/golden/make_golden_trellis.py --ref <checkout of the reference repository> [--out tests/golden]
 """
 from __future__ import annotations
 
@@ -111,7 +111,7 @@ def trellis_code(mods, X16, s1, W1, L=10, seed=0):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the reference repository (read only)")
     ap.add_argument("--out", default=HERE)
     args = ap.parse_args()
     n, d, nq, nlist, bits = 1536, 256, 40, 32, 640
