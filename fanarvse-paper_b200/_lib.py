@@ -21,6 +21,7 @@ SIGNATURES = {
     "fvs_version": (I32, []),
     "fvs_arch": (C.c_char_p, []),
     "fvs_i8_tile_rows": (I32, []),
+    "fvs_set_wait_limit": (C.c_uint32, [C.c_uint32]),
     "fvs_quantize": (I32, [P, P, I32, I32, I32, P, P]),
     "fvs_query_prep": (I32, [P, P, I32, I32, I32, P, P, P]),
     "fvs_route_topk": (I32, [P, P, I32, I32, I32, P]),

@@ -53,6 +53,7 @@ struct Params {
     int32_t* status;
     int64_t ldo;
     int B, N, NK, QB, nqb, M;
+    uint32_t wait_limit;  // polls of every pipeline wait (fvs_set_wait_limit)
 };
 
 template <int MODE>
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dense_tc_kernel(const __grid_cons
     auto t_empty = [&](int b) { return sbase + BAR_OFF + 8 * (2 * STAGES + 2 + b); };
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + MISC_OFF);
     volatile int* abort = reinterpret_cast<volatile int*>(smem + MISC_OFF + 4);
+    const uint32_t WL = p.wait_limit;
 
     if (tid == 0) {
         for (int s = 0; s < STAGES; s++) {
@@ -106,7 +108,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dense_tc_kernel(const __grid_cons
                 bool ok = true;
                 for (int kc = 0; kc < p.NK; kc++, it++) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(empty(s), ((it / STAGES) & 1) ^ 1, abort)) {
+                    if (!mbar_wait(empty(s), ((it / STAGES) & 1) ^ 1, abort, WL)) {
                         ok = false;
                         break;
                     }
@@ -127,13 +129,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) dense_tc_kernel(const __grid_cons
                 const int nq16 = (min(p.QB, p.B - q0) + 15) & ~15;
                 const uint32_t idesc = i8_idesc(nq16, TM);
                 const int b = tc & 1;
-                if (!mbar_wait(t_empty(b), ((tc >> 1) & 1) ^ 1, abort)) break;
+                if (!mbar_wait(t_empty(b), ((tc >> 1) & 1) ^ 1, abort, WL)) break;
                 tc_fence_after();
                 const uint32_t d = tmem + (uint32_t)(b * QBMAX);
                 bool ok = true;
                 for (int kc = 0; kc < p.NK; kc++, it++) {
                     const int s = it % STAGES;
-                    if (!mbar_wait(full(s), (it / STAGES) & 1, abort)) {
+                    if (!mbar_wait(full(s), (it / STAGES) & 1, abort, WL)) {
                         ok = false;
                         break;
                     }
@@ -160,7 +162,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dense_tc_kernel(const __grid_cons
             const int row0 = (t / p.nqb) * TM, q0 = (t % p.nqb) * p.QB;
             const int nq = min(p.QB, p.B - q0);
             const int b = tc & 1;
-            if (!mbar_wait(t_full(b), (tc >> 1) & 1, abort)) break;
+            if (!mbar_wait(t_full(b), (tc >> 1) & 1, abort, WL)) break;
             tc_fence_after();
             const int row = row0 + 32 * ew + lane;
             const bool rvalid = row < p.N;
@@ -224,11 +226,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) dense_tc_kernel(const __grid_cons
             if (lane == 0) mbar_arrive(t_empty(b));
         }
     }
-    // drain what this CTA issued (only pending when a wait gave up): the last load of every stage, the last commit
+    // drain what this CTA issued (only pending when a wait gave up; these waits ignore the abort flag): the last load
+    // of every stage, and the commit after the last MMA issued (an MMA is only issued right before such a commit)
     if (warp == 0 && lane == 0)
-        for (int u = last_load; u >= 0 && u > last_load - STAGES; u--) mbar_wait(full(u % STAGES), (u / STAGES) & 1, abort);
+        for (int u = last_load; u >= 0 && u > last_load - STAGES; u--) mbar_drain(full(u % STAGES), (u / STAGES) & 1);
     if (warp == 1 && lane == 0 && last_commit >= 0)
-        mbar_wait(empty(last_commit % STAGES), (last_commit / STAGES) & 1, abort);
+        mbar_drain(empty(last_commit % STAGES), (last_commit / STAGES) & 1);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -350,7 +353,8 @@ extern "C" int fvs_dense_scan_tc(fvs_stream_t stream, int mode, const int8_t* q8
     const int64_t nrb = (N + TM - 1) / TM;
     if (nrb * nqb > INT32_MAX) return FVS_ERANGE;
     const int ntiles = (int)(nrb * nqb);
-    Params p{qs, (const __half*)zs, t0, cnt, bval, bpos, out, status, ldo, B, (int)N, R / KC, QB, nqb, M};
+    Params p{qs, (const __half*)zs, t0, cnt, bval, bpos, out, status, ldo, B, (int)N, R / KC, QB, nqb, M,
+             pipeline_wait_limit()};
     cudaError_t e = mode ? fvs_ensure_smem((const void*)dense_tc_kernel<1>, SMEM_BYTES)
                          : fvs_ensure_smem((const void*)dense_tc_kernel<0>, SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;

@@ -64,7 +64,7 @@ constexpr int MAXT = FVS_TC_MAXT;                          // tiles of one round
 constexpr int LIST_OFF = ZS_OFF + T_STAGES * TILE_ROWS * 4; // 5 x MAXT int32: row0, cs, ce, qoff, qn
 constexpr int COL_OFF = LIST_OFF + 5 * MAXT * 4;           // per epilogue warp: 32 column masks + 32 bases
 constexpr int BAR_OFF = COL_OFF + 16 * 64 * 4;             // mbarriers
-constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 3 * T_STAGES;
+constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 3 * T_STAGES + 1;  // + the MMA drain barrier
 constexpr int MISC_OFF = BAR_OFF + NBAR * 8;               // tmem base, abort flag, list length, scan scratch
 constexpr int SMEM_BYTES = MISC_OFF + 16 + 128 + 1024;     // + alignment slack
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
@@ -88,6 +88,7 @@ struct Params {
     float* bmc;
     int32_t* status;
     int M, MB;
+    uint32_t wait_limit;  // polls of every pipeline wait (fvs_set_wait_limit)
 };
 
 // 32 x 32 bit-matrix transpose across a warp: lane r holds row r (bit c = entry (r, c)); returns row `lane` of the
@@ -133,6 +134,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
     auto t_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + s); };
     auto t_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + T_STAGES + s); };
     auto m_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + 2 * T_STAGES + s); };
+    const uint32_t d_bar = sbase + BAR_OFF + 8 * (2 * A_STAGES + 2 * B_STAGES + 3 * T_STAGES);
+    const uint32_t WL = p.wait_limit;
     int* meta_qid = reinterpret_cast<int*>(smem + META_OFF);          // [T_STAGES][QN]
     float* meta_qs = reinterpret_cast<float*>(meta_qid + T_STAGES * QN);
     float* meta_qc = meta_qs + T_STAGES * QN;
@@ -154,6 +157,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
             mbar_init(t_empty(s), 4);  // accumulator + metadata slot, released by the epilogue
             mbar_init(m_full(s), 1);   // metadata slot written by its gather warp
         }
+        mbar_init(d_bar, 1);           // every MMA this CTA issued has completed (before TMEM is freed)
         *abort = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -179,7 +183,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
     const int nlocal = ntiles > blockIdx.x ? (ntiles - blockIdx.x + G - 1) / G : 0;
 
     // per-role pipeline counters persist across rounds
-    int na_tma = 0, na_mma = 0, nb_mma = 0, last_a = -1, nb_g = 0, nb_e = 0;
+    int na_tma = 0, na_mma = 0, nb_mma = 0, nb_g = 0, nb_e = 0;
+    bool mma_issued = false;
     for (int r0 = 0; r0 < nlocal; r0 += MAXT) {
         // ---- stage this round's tiles (skipping cells no query probes) in shared memory, in walk order
         {
@@ -228,7 +233,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                 if (r0 == 0) asm volatile("prefetch.tensormap [%0];" ::"l"(&zmap) : "memory");
                 for (int t = 0; t < len && !*abort; t++) {
                     const int s = na_tma % A_STAGES;
-                    if (!mbar_wait(a_empty(s), ((na_tma / A_STAGES) & 1) ^ 1, abort)) break;
+                    if (!mbar_wait(a_empty(s), ((na_tma / A_STAGES) & 1) ^ 1, abort, WL)) break;
                     const int row0 = L_row0[t];
                     mbar_expect_tx(a_full(s), A_BYTES);
                     tma_load_2d(sbase + A_OFF + s * A_BYTES, &zmap, 0, row0, a_full(s));
@@ -242,14 +247,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                 for (int t = 0; t < len && !*abort; t++) {
                     const int qn = L_qn[t];
                     const int sa = na_mma % A_STAGES;
-                    if (!mbar_wait(a_full(sa), (na_mma / A_STAGES) & 1, abort)) break;
+                    if (!mbar_wait(a_full(sa), (na_mma / A_STAGES) & 1, abort, WL)) break;
                     tc_fence_after();
                     const uint32_t abase = sbase + A_OFF + sa * A_BYTES;
                     bool ok = true;
                     for (int i = 0; i * QN < qn; i++, nb_mma++) {
                         const int sb = nb_mma % B_STAGES, st = nb_mma % T_STAGES;
-                        if (!mbar_wait(b_full(sb), (nb_mma / B_STAGES) & 1, abort) ||
-                            !mbar_wait(t_empty(st), ((nb_mma / T_STAGES) & 1) ^ 1, abort)) {
+                        if (!mbar_wait(b_full(sb), (nb_mma / B_STAGES) & 1, abort, WL) ||
+                            !mbar_wait(t_empty(st), ((nb_mma / T_STAGES) & 1) ^ 1, abort, WL)) {
                             ok = false;
                             break;
                         }
@@ -264,12 +269,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                             mma_i8(d, sw128_desc(abase + h * TILE_ROWS * 128 + kofs),
                                    sw128_desc(bb + h * QN * 128 + kofs), idesc, ks > 0 ? 1u : 0u);
                         }
+                        mma_issued = true;
                         mma_commit(t_full(st));
                         mma_commit(b_empty(sb));  // the query tile is free once these MMAs complete
                     }
                     if (!ok) break;
                     mma_commit(a_empty(sa));  // the code tile is free once these MMAs complete
-                    last_a = na_mma;
                     na_mma++;
                 }
             }
@@ -314,8 +319,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                             qsv[rr] = p.qs[qq[rr]];
                             thv[rr] = MODE ? p.t0[qq[rr]] : 0.f;
                         }
-                    if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort) ||
-                        !mbar_wait(t_empty(st), ((nb_g / T_STAGES) & 1) ^ 1, abort)) {
+                    if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort, WL) ||
+                        !mbar_wait(t_empty(st), ((nb_g / T_STAGES) & 1) ^ 1, abort, WL)) {
                         ok = false;
                         break;
                     }
@@ -373,8 +378,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                 for (int i = 0; i * QN < qn; i++, nb_e++) {
                     if (nb_e % EPI_GROUPS != eg) continue;
                     const int st = nb_e % T_STAGES;
-                    if (!mbar_wait(t_full(st), (nb_e / T_STAGES) & 1, abort) ||
-                        !mbar_wait(m_full(st), (nb_e / T_STAGES) & 1, abort)) {  // m_full: acquire the metadata
+                    if (!mbar_wait(t_full(st), (nb_e / T_STAGES) & 1, abort, WL) ||
+                        !mbar_wait(m_full(st), (nb_e / T_STAGES) & 1, abort, WL)) {  // m_full: acquire the metadata
                         ok = false;
                         break;
                     }
@@ -470,11 +475,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
         }
         __syncthreads();  // the round's list is consumed by every role before it is overwritten
     }
-    // drain: the most recent load of every A stage has landed, the last code-tile release has arrived
+    // drain (waits that ignore the abort flag): the most recent load of every A stage has landed, and one commit
+    // after the last MMA this thread issued has arrived, i.e. every MMA of this CTA has completed
     if (warp == 0 && lane == 0)
-        for (int u = na_tma - 1; u >= 0 && u >= na_tma - A_STAGES; u--)
-            mbar_wait(a_full(u % A_STAGES), (u / A_STAGES) & 1, abort);
-    if (warp == 1 && lane == 0 && last_a >= 0) mbar_wait(a_empty(last_a % A_STAGES), (last_a / A_STAGES) & 1, abort);
+        for (int u = na_tma - 1; u >= 0 && u >= na_tma - A_STAGES; u--) mbar_drain(a_full(u % A_STAGES), (u / A_STAGES) & 1);
+    if (warp == 1 && lane == 0 && mma_issued) {
+        mma_commit(d_bar);
+        mbar_drain(d_bar, 0);
+    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -509,7 +517,8 @@ extern "C" int fvs_i8_scan_tc(fvs_stream_t stream, int mode, const int8_t* q8, c
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return FVS_EINVAL;
-    Params p{q8, qs, qid, coff, ccnt, qcp, tile_cell, tile_row0, off, zs, t0, cnt, bval, bpos, bmc, status, M, MB};
+    Params p{q8,  qs,  qid, coff, ccnt, qcp,    tile_cell, tile_row0, off, zs,
+             t0,  cnt, bval, bpos, bmc, status, M,         MB,        pipeline_wait_limit()};
     cudaError_t e = mode ? fvs_ensure_smem((const void*)scan_tc_kernel<1>, SMEM_BYTES)
                          : fvs_ensure_smem((const void*)scan_tc_kernel<0>, SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;

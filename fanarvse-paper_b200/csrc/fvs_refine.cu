@@ -191,6 +191,7 @@ __global__ void exact_scores_kernel(const __half* __restrict__ H, int d, const i
 extern "C" int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ids, int B, int k,
                                 const float* Q, int ldq, float* score) {
     FVS_CHECK_ARG(H && ids && Q && score && d > 0 && d % 8 == 0 && ldq >= d && ldq % 4 == 0 && B >= 0 && k >= 1);
+    FVS_CHECK_ARG(((uintptr_t)Q & 15) == 0 && ((uintptr_t)H & 15) == 0);   // 16-byte row loads
     if (B == 0) return FVS_OK;
     const int64_t warps = (int64_t)B * k;
     fvs::exact_scores_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>((const __half*)H, d, ids, B, k, Q, ldq,

@@ -539,42 +539,73 @@ __global__ void __launch_bounds__(32 * WQ_WARPS) select_topk_warp_kernel(
 }
 
 // ------------------------------------------------------------------------------------------------ merge
+// Keys hold (score, slot): the order-preserving score bits above, 0xffffffff - slot below, so equal scores order by
+// slot.  The tie order the merge needs is by the int64 global id (a -1 "no result" id included), which is read back
+// through the slot; ids are never squeezed into the key.
+__device__ __forceinline__ bool merge_before(float si, int64_t ii, int i, float sj, int64_t ij, int j) {
+    // true when entry j ranks ahead of entry i: larger score, then smaller id, then smaller slot
+    return sj > si || (sj == si && (ij < ii || (ij == ii && j < i)));
+}
+
 __global__ void merge_kernel(const int64_t* __restrict__ ids_g, const float* __restrict__ score_g, int G, int B,
                              int kin, int k, int Kp, int64_t* __restrict__ I, float* __restrict__ S) {
     extern __shared__ __align__(16) uint8_t smem[];
     unsigned long long* sb = reinterpret_cast<unsigned long long*>(smem);
     const int q = blockIdx.x, tid = threadIdx.x, nt = blockDim.x;
     const int n = G * kin;
-    for (int i = tid; i < Kp; i += nt) {
-        if (i < n) {
-            const int g = i / kin, j = i - g * kin;
-            const int64_t o = ((int64_t)g * B + q) * kin + j;
-            sb[i] = ((unsigned long long)f2o(score_g[o]) << 32) | (0xffffffffu - (uint32_t)ids_g[o]);
-        } else {
-            sb[i] = 0ull;
-        }
-    }
-    __syncthreads();
-    if (n <= 1024) {  // place the k best by rank (ties of equal keys by index), no sorting network
+    auto src = [&](int i) {  // global offset of slot i of this query: shard g = i / kin, entry j = i % kin
+        const int g = i / kin, j = i - g * kin;
+        return ((int64_t)g * B + q) * kin + j;
+    };
+    if (n <= 1024) {  // place the k best by rank, no sorting network
+        float* ss = reinterpret_cast<float*>(smem);
+        int64_t* si = reinterpret_cast<int64_t*>(smem + 1024 * 4);
         for (int i = tid; i < n; i += nt) {
-            const unsigned long long ki = sb[i];
+            const int64_t o = src(i);
+            ss[i] = score_g[o];
+            si[i] = ids_g[o];
+        }
+        __syncthreads();
+        for (int i = tid; i < n; i += nt) {
+            const float s = ss[i];
+            const int64_t id = si[i];
             int rank = 0;
-            for (int j = 0; j < n; j++) {
-                const unsigned long long kj = sb[j];
-                rank += (kj > ki) || (kj == ki && j < i);
-            }
+            for (int j = 0; j < n; j++) rank += merge_before(s, id, i, ss[j], si[j], j);
             if (rank < k) {
-                I[(int64_t)q * k + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
-                if (S) S[(int64_t)q * k + rank] = o2f((uint32_t)(ki >> 32));
+                I[(int64_t)q * k + rank] = id;
+                if (S) S[(int64_t)q * k + rank] = s;
             }
         }
         return;
     }
-    block_bitonic_desc(sb, Kp);
-    for (int i = tid; i < k; i += nt) {
-        const unsigned long long key = sb[i];
-        I[(int64_t)q * k + i] = (int64_t)(0xffffffffu - (uint32_t)key);
-        if (S) S[(int64_t)q * k + i] = o2f((uint32_t)(key >> 32));
+    for (int i = tid; i < Kp; i += nt)
+        sb[i] = i < n ? ((unsigned long long)f2o(score_g[src(i)]) << 32) | (0xffffffffu - (uint32_t)i) : 0ull;
+    __syncthreads();
+    block_bitonic_desc(sb, Kp);  // by score desc, slot asc
+    // Only entries whose score reaches the k-th best can be kept: sorted positions [0, b), b the end of the run of
+    // entries equal in score to position k-1.  Within a run of equal scores (sorted positions [a, e)) an entry's
+    // final rank is a + #(run entries ahead of it by (id, slot)).
+    const uint32_t sk = (uint32_t)(sb[k - 1] >> 32);
+    for (int i = tid; i < n; i += nt) {
+        const uint32_t si = (uint32_t)(sb[i] >> 32);
+        if (si < sk) continue;
+        int a = i, e = i + 1;
+        while (a > 0 && (uint32_t)(sb[a - 1] >> 32) == si) a--;
+        while (e < n && (uint32_t)(sb[e] >> 32) == si) e++;
+        if (a >= k) continue;
+        const int slot_i = (int)(0xffffffffu - (uint32_t)sb[i]);
+        const int64_t id_i = ids_g[src(slot_i)];
+        int rank = a;
+        for (int j = a; j < e; j++) {
+            if (j == i) continue;
+            const int slot_j = (int)(0xffffffffu - (uint32_t)sb[j]);
+            const int64_t id_j = ids_g[src(slot_j)];
+            rank += id_j < id_i || (id_j == id_i && slot_j < slot_i);
+        }
+        if (rank < k) {
+            I[(int64_t)q * k + rank] = id_i;
+            if (S) S[(int64_t)q * k + rank] = o2f(si);
+        }
     }
 }
 
@@ -662,6 +693,7 @@ extern "C" int fvs_merge_topk(fvs_stream_t stream, const int64_t* ids_g, const f
     if (G * kin > 4096) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const int Kp = fvs::pow2_at_least(G * kin);
-    fvs::merge_kernel<<<B, 256, (size_t)Kp * 8, stream>>>(ids_g, score_g, G, B, kin, k, Kp, I, S);
+    const size_t sm = G * kin <= 1024 ? (size_t)1024 * 12 : (size_t)Kp * 8;
+    fvs::merge_kernel<<<B, 256, sm, stream>>>(ids_g, score_g, G, B, kin, k, Kp, I, S);
     return fvs_launch_status();
 }

@@ -13,6 +13,9 @@ namespace tcg {
 
 constexpr uint32_t WAIT_LIMIT = 1u << 22;
 
+// polls allowed to the pipeline waits of the next launches (fvs_set_wait_limit; WAIT_LIMIT unless a test lowered it)
+uint32_t pipeline_wait_limit();
+
 __device__ __forceinline__ uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
 __device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
@@ -24,9 +27,11 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
 __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
 }
-// bounded wait for the completion of the phase with the given parity; false when the limit expired or the CTA aborted
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
-    for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
+// bounded wait for the completion of the phase with the given parity; false when `limit` polls expired (the CTA is
+// then marked aborted) or when another role of the CTA has already aborted.  Pipeline waits pass the call's limit.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint32_t limit = WAIT_LIMIT) {
+    for (uint32_t it = 0; it < limit; ++it) {
         uint32_t done;
         asm volatile(
             "{\n\t.reg .pred p;\n\t"
@@ -39,6 +44,24 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
         if ((it & 255u) == 255u && *abort) return false;
     }
     *abort = 1;
+    return false;
+}
+
+// wait used while draining before exit: copies and MMAs already issued complete whatever the rest of the CTA did, so
+// this wait ignores the abort flag and always allows the full WAIT_LIMIT polls (a CTA must not leave with a copy into
+// its shared memory, or an MMA into its tensor memory, still in flight)
+__device__ __forceinline__ bool mbar_drain(uint32_t bar, uint32_t parity) {
+    for (uint32_t it = 0; it < WAIT_LIMIT; ++it) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(done)
+            : "r"(bar), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
     return false;
 }
 

@@ -112,6 +112,7 @@ class DenseB200:
 
     def check_status(self):
         if int(self.status.item()) != 0:
+            self.status.zero_()
             raise _lib.FvsError("dense scan: a bounded device wait expired (status flag set)")
 
 

@@ -483,6 +483,7 @@ class EngineB200I8:
         ids = P[2 * B + B * kk:].view(B, KK)
         torch.cuda.current_stream().synchronize()                # the only synchronisation
         if int(hst[0]) != 0:
+            self.status.zero_()                                   # the next search starts clean
             raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
         in_graph = self.FB_INGRAPH and B >= self.FB_MIN_BATCH
         if in_graph:
@@ -535,6 +536,7 @@ class EngineB200I8:
         torch.cuda.current_stream().synchronize()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         if h[0, 1] != 0:
+            self.status.zero_()
             raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
         out = h[:, 2:].copy()
         if not h[:, 0].all():

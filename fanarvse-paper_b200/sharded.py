@@ -68,7 +68,8 @@ class ShardedSearch:
     def _exchange(self, Qb, I, k):
         """exact scores of the local top-k, one all-gather, merge (every rank, same order)."""
         S = self.exact(Qb, I)
-        gid = I.long() + self.row_offset
+        I = I.long()
+        gid = torch.where(I < 0, torch.full_like(I, -1), I + self.row_offset)   # -1 ("no result") stays -1
         G = dist.get_world_size(self.group) if dist.is_initialized() else 1
         if G == 1:
             ids_all, s_all = gid[None], S[None]

@@ -30,6 +30,18 @@ int fvs_version(void);
 const char* fvs_arch(void);
 
 /*
+ * Polls allowed to each pipeline wait (an mbarrier wait between the roles of a CTA) of the tcgen05 kernels
+ * (fvs_i8_scan_tc, fvs_dense_scan_tc) launched from now on in this process; returns the previous value.  No
+ * counterpart in the reference (its Triton kernels have no waits of their own).  When a wait's polls run out, the
+ * CTA stops its work, waits (with the default limit, whatever this setting) for the copies and MMAs it already issued,
+ * frees its tensor memory, sets the call's `status` word to 1 and returns: the search raises instead of hanging.
+ * This knob exists so that tests can make that path run (0: every pipeline wait gives up at once); production code
+ * leaves it at FVS_WAIT_LIMIT_DEFAULT.  Takes effect at launch, so a captured graph keeps the value it was captured with.
+ */
+#define FVS_WAIT_LIMIT_DEFAULT 4194304u
+uint32_t fvs_set_wait_limit(uint32_t polls);
+
+/*
  * Per-batch query preparation in one pass over the fp32 queries Q [B, ldq]: Qh [B, d] = fp16(Q) (round to nearest
  * even: the `Qb.half()` operand of the routing and rotation products, `throughput/enginei8.py:67`,
  * `throughput/s2lut.py:122`) and qc[q] = <Q[q, :d], c> in fp32 (`QC = Qb @ s1["c"]`, `throughput/enginei8.py:63`;
@@ -328,6 +340,7 @@ int fvs_rows_scatter(fvs_stream_t stream, const int32_t* rows, int FB, int B, ui
 /*
  * Exact top-k of each query over G shards' local top-k (new: the row-sharded multi-GPU search).
  * ids_g [G,B,kin] int64 global ids, score_g [G,B,kin] f32 -> I [B,k], S [B,k] by (score desc, id asc).  G*kin <= 4096.
+ * Any int64 id is kept as given (ids of 2^32 and above, and -1 for "no result", come back unchanged).
  */
 int fvs_merge_topk(fvs_stream_t stream, const int64_t* ids_g, const float* score_g, int G, int B, int kin, int k,
                    int64_t* I, float* S);

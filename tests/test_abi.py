@@ -17,7 +17,7 @@ def lib():
 
 def declared():
     src = open(os.path.join(REPO, "include", "fanar_b200.h")).read()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(fvs_\w+)\s*\(", src, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|uint32_t|const char\*)\s+(fvs_\w+)\s*\(", src, re.M)))
 
 
 def test_every_declared_symbol_is_exported(lib):
@@ -45,6 +45,9 @@ def test_argument_errors(lib):
     assert lib.fvs_refine(n, dummy, 1536, dummy, dummy, dummy, dummy, 1, 10, 1.0, 10, dummy, 1536, dummy, dummy,
                           dummy, n) == -1  # K must exceed k
     assert lib.fvs_merge_topk(n, dummy, dummy, 8, 1, 1024, 10, dummy, n) == -2
+    odd = C.c_void_p(20)                                   # not 16-byte aligned: the row loads would fault
+    assert lib.fvs_exact_scores(n, odd, 1536, dummy, 1, 10, dummy, 1536, dummy) == -1
+    assert lib.fvs_exact_scores(n, dummy, 1536, dummy, 1, 10, odd, 1536, dummy) == -1
     T = (C.c_int32 * 9)(*range(9))
     assert lib.fvs_lut_build(n, dummy, 1, 64, 64, 1, dummy, 9, T, T, dummy, dummy) == -2  # more than 8 tiers
 

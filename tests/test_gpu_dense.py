@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, pkg
+from conftest import GOLDEN, assert_end_to_end, pkg
 from oracle import fvs_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -122,10 +122,37 @@ def test_dense_engine_end_to_end(dm):
     E = dm.EngineB200Dense(ix, D)
     E.MSZ = 4096
     Q = ds["queries"]
-    I, reads, ids = E.search(Q, 100, 2.0, 0, 10)
+    K, z, k = 100, 2.0, 10
+    I, reads, ids = E.search(Q, K, z, 0, k)
     r = synth.recall(I.long().cpu(), ds["gt"].cpu(), 10)
     assert r >= 0.95, r
     D.check_status()
+    # against the oracle on the same inputs: stage 1 (`Brute`) from the product's query codes, then the LUT stage 2,
+    # classification, exact re-rank and final top-k of the throughput engine
+    e = E.search_eager(Q, K, z, 0, k)
+    last = D._last
+    q8, qs = c(last["q8"]), c(last["qs"])
+    ref = O.dense_search(q8, qs, c(D.Z), c(D.zs), K, over=E.OVER, M=E.MSZ)
+    np.testing.assert_array_equal(c(last["t0"]), ref["t0"])
+    np.testing.assert_array_equal(c(last["cnt"]), ref["cnt"])
+    ok = ref["ok"]
+    np.testing.assert_array_equal(c(e["ok"]).astype(bool), ok)
+    import __graft_entry__ as ge
+    oi = ge.oracle_index(s1, i8, codes["uniform"], X16)
+    code = oi["code"]
+    TS = code["TS"]
+    Zq = c(e["Zq"])
+    QC = c((Q @ ix.c).contiguous())
+    Lt = O.lut_build(Zq, half=E.LUTH)
+    qsum, qn2 = O.tier_sums(Zq, TS)
+    est, sd = O.lut_score(ref["pos"], QC, Lt, TS, code["planes"], code["deltas"], code["scale"], code["sig"], qsum, qn2)
+    sure, amb = O.classify(est, sd, z, k)
+    oids = np.asarray(oi["order"])[ref["pos"]]
+    oI = O.final_topk(oids, O.stage3(oi["H16"], oids, amb, c(Q), est, sure), k)
+    np.testing.assert_array_equal(c(e["ids"])[ok], oids[ok])
+    np.testing.assert_allclose(c(e["est"])[ok], est[ok], rtol=1e-5, atol=1e-5)
+    g = {key: c(e[key]) for key in ("ok", "ids", "reads", "I", "est", "sd")}
+    assert_end_to_end(g, dict(ok=ok, ids=oids, reads=amb.sum(1), I=oI, est=est, sd=sd), z, k)
 
 
 @pytest.mark.parametrize("r", [1, 7, 16, 17, 32, 33, 200])

@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden_index, pkg
+from conftest import assert_end_to_end, golden_index, pkg
 from oracle import fvs_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -153,10 +153,10 @@ def test_search_matches_oracle(eng, n, d, nlist, nq, K, nprobe, k, M, scan):
     np.testing.assert_array_equal(c(r["reads"])[ok], amb.sum(1)[ok])
     score = O.stage3(oi["H16"], c(r["ids"]), amb, c(Q), c(r["est"]), sure)
     np.testing.assert_array_equal(c(r["I"])[ok], O.final_topk(c(r["ids"]), score, k)[ok])
-    # end to end against the oracle's own stage 2: equal except where a boundary flip changed the reads
-    same = ok & (o["reads"] == c(r["reads"]))
-    assert same.sum() >= 0.9 * ok.sum()
-    np.testing.assert_array_equal(c(r["I"])[same], o["I"][same])
+    # end to end against the oracle's own stage 2: identical final ids wherever the ambiguous sets agree; every other
+    # row differs only by candidates within 1e-5 of a classification boundary
+    g = {key: c(r[key]) for key in ("ok", "t0", "cnt", "ids", "reads", "I", "est", "sd")}
+    assert_end_to_end(g, o, 1.25, k)
     # emitted sets (positions, estimates) equal the oracle's for every query that fit the buffer
     mnorm = (np.float32(1) / oi["inv_mnorm"].astype(np.float32)).astype(np.float32)
     qid, coff, ccnt, qcp, _ = O.pairs(c(probe), len(oi["off"]) - 1, c(QM), mnorm)
@@ -191,11 +191,11 @@ def test_graph_search_and_fallback(eng):
                     Zq=c(r["Zq"]), fallback=False)
     ok = o["ok"]
     np.testing.assert_array_equal(c(r["ok"]), ok)
-    # rows whose fp32 stage-2 sums put the same candidates on the ambiguity boundary must agree exactly (the others
-    # differ by a boundary flip of the last bits of an estimate)
-    same = ok & (c(nr) == o["reads"])
-    assert same.sum() >= 0.9 * ok.sum()
-    np.testing.assert_array_equal(c(I)[same], o["I"][same])
+    # the graph's rows (the main pass on the exact queries) against the oracle: identical final ids wherever the
+    # ambiguous sets agree, other rows only by candidates within 1e-5 of a classification boundary
+    g = dict(ok=c(r["ok"]), t0=c(r["t0"]), cnt=c(r["cnt"]), ids=c(ids), reads=c(nr), I=c(I), est=c(r["est"]),
+             sd=c(r["sd"]))
+    assert_end_to_end(g, o, z, k)
     bad = np.nonzero(~ok)[0]
     Qb = Q[torch.from_numpy(bad).to(DEV)]
     QMb, probeb = E.route(Qb, nprobe)
@@ -204,9 +204,12 @@ def test_graph_search_and_fallback(eng):
     fb = O._search_i8_core(oi, c(Qb), K, z, nprobe, k, Knobs, c(QMb), c(probeb), (c(q8b), c(qsb)), c(Zqb),
                            rho_override=1.0)
     np.testing.assert_array_equal(c(ids)[bad], fb["ids"])          # stage-1 candidates of the recompute: exact
-    same = c(nr)[bad] == fb["reads"]
-    assert same.sum() >= 0.9 * len(bad)
-    np.testing.assert_array_equal(c(I)[bad][same], fb["I"][same])
+    # the recompute's stage 2 on the GPU (same calls as `_fallback`) for the boundary check of its rows
+    QCb = (Qb @ ix.c).contiguous()
+    posb, okb, _, _ = E.stage1_i8(Qb, QMb, probeb, K, rho_override=1.0, M_override=65536, q8qs=(q8b, qsb))
+    estb, sdb = E.score_lut_zq(QCb, posb, Zqb.contiguous(), None, False)
+    gb = dict(ok=c(okb), ids=c(ids)[bad], reads=c(nr)[bad], I=c(I)[bad], est=c(estb), sd=c(sdb))
+    assert_end_to_end(gb, dict(fb, ok=np.ones(len(bad), bool)), z, k)
     # replay with the same inputs is deterministic
     I2, nr2, ids2 = E.search(Q, K, z, nprobe, k)
     np.testing.assert_array_equal(c(I2), c(I))
@@ -261,6 +264,33 @@ def test_merge_topk(eng):
     oi, os_ = O.merge_topk(ids, sc, k)
     np.testing.assert_array_equal(c(I), oi)
     np.testing.assert_array_equal(c(S), os_)
+
+
+@pytest.mark.parametrize("G,kin,k", [(4, 10, 10), (8, 100, 100), (16, 100, 10)])
+def test_merge_topk_wide_ids(eng, G, kin, k):
+    """global ids at and above 2^32 and -1 ("no result") entries come back unchanged, in (score desc, id asc) order,
+    also through equal scores whose ids differ only above bit 31; rank-placement (G*kin <= 1024) and sorting-network
+    (larger) kernels"""
+    L = pkg("_lib")
+    lib = L.lib()
+    rng = np.random.default_rng(G * kin)
+    B = 5
+    ids = (rng.permutation(10 ** 6)[:G * B * kin].astype(np.int64) + (rng.integers(0, 4, G * B * kin) << 32))
+    ids = ids.reshape(G, B, kin)
+    ids[0, 1, :] = ids[0, 1, 0] % (1 << 32) + (np.arange(kin, dtype=np.int64) << 32)   # equal low words
+    sc = (rng.integers(0, 6, (G, B, kin)) / 4).astype(np.float32)                      # many ties
+    ids[:, 2, kin // 2:] = -1
+    sc[:, 2, kin // 2:] = -1e30
+    ids[:, 3, :] = -1
+    sc[:, 3, :] = -1e30
+    ti, ts = torch.from_numpy(ids).to(DEV), torch.from_numpy(sc).to(DEV)
+    I = torch.empty(B, k, dtype=torch.int64, device=DEV)
+    S = torch.empty(B, k, device=DEV)
+    L.check(lib.fvs_merge_topk(L.stream_handle(), L.ptr(ti), L.ptr(ts), G, B, kin, k, L.ptr(I), L.ptr(S)), "merge")
+    oi, os_ = O.merge_topk(ids, sc, k)
+    np.testing.assert_array_equal(c(I), oi)
+    np.testing.assert_array_equal(c(S), os_)
+    assert (c(I)[3] == -1).all()
 
 
 @pytest.mark.parametrize("NC,npr", [(4096, 352), (4093, 352), (4096, 600), (16384, 96), (8, 3), (2000, 1)])
@@ -435,18 +465,25 @@ def test_in_graph_recompute(eng, msz):
     assert nbad > 0 and E.nbad >= nbad
     if msz == 160:
         assert nbad > E.FB_INGRAPH               # some rows take the host path
-    same = ok & (c(nr) == o["reads"])
-    assert same.sum() >= 0.9 * ok.sum()
-    np.testing.assert_array_equal(c(I)[same], o["I"][same])
+    g = dict(ok=c(r["ok"]), t0=c(r["t0"]), cnt=c(r["cnt"]), ids=c(ids), reads=c(nr), I=c(I), est=c(r["est"]),
+             sd=c(r["sd"]))
+    assert_end_to_end(g, o, z, k)
     bad = np.nonzero(~ok)[0]
-    Zf = (Q.float() @ ix.VP16.float()).cpu().numpy()                 # recompute LUT input (fp32 LUT path)
+    Zq = E.rotated_query(Q)
     fb = O._search_i8_core(oi, c(Q)[bad], K, z, nprobe, k, Knobs, c(QM)[bad], c(probe)[bad], (c(q8)[bad], c(qs)[bad]),
-                           c(E.rotated_query(Q))[bad], rho_override=1.0)
+                           c(Zq)[bad], rho_override=1.0)
     in_graph = bad[:E.FB_INGRAPH]
-    np.testing.assert_array_equal(c(ids)[in_graph], fb["ids"][:len(in_graph)])
-    sameb = c(nr)[in_graph] == fb["reads"][:len(in_graph)]
-    assert sameb.sum() >= 0.9 * len(in_graph)
-    np.testing.assert_array_equal(c(I)[in_graph][sameb], fb["I"][:len(in_graph)][sameb])
+    n = len(in_graph)
+    np.testing.assert_array_equal(c(ids)[in_graph], fb["ids"][:n])
+    # the recompute's stage 2 on the GPU (the calls of the in-graph recompute) for the boundary check of its rows
+    bi = torch.from_numpy(in_graph).to(DEV)
+    posb, okb, _, _ = E.stage1_i8(Q[bi], QM[bi], probe[bi].contiguous(), K, rho_override=1.0, M_override=65536,
+                                  q8qs=(q8[bi], qs[bi]), small=True)
+    QC = E.query_prep(Q)[0]                       # the centre products the in-graph recompute gathers
+    estb, sdb = E.score_lut_zq(QC[bi].contiguous(), posb, Zq[bi].contiguous(), None, False)
+    gb = dict(ok=c(okb), ids=c(ids)[in_graph], reads=c(nr)[in_graph], I=c(I)[in_graph], est=c(estb), sd=c(sdb))
+    ob = {key: fb[key][:n] for key in ("ids", "reads", "I", "est", "sd")}
+    assert_end_to_end(gb, dict(ob, ok=np.ones(n, bool)), z, k)
     I2, _, _ = E.search(Q, K, z, nprobe, k)
     np.testing.assert_array_equal(c(I2), c(I))
 

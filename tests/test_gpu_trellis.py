@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import GOLDEN, pkg
+from conftest import GOLDEN, assert_end_to_end, pkg
 from oracle import fvs_oracle as O
 
 pytestmark = pytest.mark.gpu
@@ -189,9 +189,14 @@ def test_search_matches_reference_end_to_end(gt, ec):
     Q = torch.from_numpy(f["Q"]).to(DEV)
     out = E.search_eager(Q, K, z, nprobe, k)
     np.testing.assert_array_equal(c(out["ok"]).astype(bool), f["out_ok"])
-    same = c(out["reads"]) == f["out_reads"]
-    assert same.mean() >= 0.9
-    np.testing.assert_array_equal(c(out["I"])[same], f["out_I"][same])
+    # rows whose stage-1 candidates equal the reference's (the others differ only by candidates tied with the K-th
+    # estimate within fp32 rounding: test_trellis_scan_first_pass_and_threshold): identical final ids wherever the
+    # ambiguous sets agree, other rows only by candidates within 1e-5 of a classification boundary
+    rows = (c(out["ids"]) == f["k_ids"]).all(1)
+    g = {key: c(out[key])[rows] for key in ("ok", "ids", "reads", "I", "est", "sd")}
+    ref = dict(ok=f["out_ok"][rows], ids=f["k_ids"][rows], reads=f["out_reads"][rows], I=f["out_I"][rows],
+               est=f["k_est"][rows], sd=f["k_sd"][rows])
+    assert_end_to_end(g, ref, z, k)
     # graph replay gives the eager results
     I, reads, ids = E.search(Q, K, z, nprobe, k)
     np.testing.assert_array_equal(c(I), c(out["I"]))

@@ -129,3 +129,68 @@ def test_dead_rank_is_detected():
     assert codes[0] == 0
     st = open(os.path.join(outdir, "r0.status")).read()
     assert st.startswith("raised"), st
+
+
+class _ShortLocal:
+    """a shard engine whose local top-k has fewer than k real rows for some queries (-1 = no result)."""
+
+    def __init__(self, I):
+        self.I = I
+
+    def search(self, Qb, K, z, nprobe, k):
+        return self.I.clone(), torch.zeros(len(self.I), dtype=torch.int64), None
+
+
+def _short_worker(rank, world, port, outdir):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    sys.path.insert(0, REPO)
+    import importlib
+    sharded = importlib.import_module("fanarvse-paper_b200.sharded")
+    from oracle import fvs_oracle as O
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=8))
+    rng = np.random.default_rng(rank)
+    B, k, n = 6, 10, 1000
+    I = rng.permutation(n)[:B * k].reshape(B, k).astype(np.int32)
+    I[0, 3:] = -1                       # query 0: 3 rows on this shard
+    I[1, :] = -1                        # query 1: none on this shard
+    if rank == 1:
+        I[2, 1:] = -1                   # query 2: 1 row on shard 1
+    scores = rng.standard_normal((B, k)).astype(np.float32)
+
+    def exact(Qb, Il):
+        s = torch.from_numpy(scores.copy())
+        s[Il < 0] = -1e30               # as fvs_exact_scores scores a -1 id
+        return s
+
+    def merge(ids_g, s_g, k):
+        a, b = O.merge_topk(ids_g.numpy(), s_g.numpy(), k)
+        return torch.from_numpy(a), torch.from_numpy(b)
+
+    S = sharded.ShardedSearch(_ShortLocal(torch.from_numpy(I)), rank * n, exact=exact, merge=merge)
+    Ig, Sg, _ = S.search(torch.zeros(B, 4), 40, 1.25, 10, k)
+    np.savez(os.path.join(outdir, f"s{rank}.npz"), I=Ig.numpy(), S=Sg.numpy())
+    dist.destroy_process_group()
+
+
+def test_no_result_rows_stay_minus_one():
+    """a -1 local id ("no result") is not offset into another shard's id range: it merges as -1, after every real
+    row (global ids are row_offset + local id only for real rows)."""
+    outdir = tempfile.mkdtemp()
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    ps = [ctx.Process(target=_short_worker, args=(r, 2, port, outdir)) for r in range(2)]
+    for p in ps:
+        p.start()
+    for p in ps:
+        p.join(240)
+    assert [p.exitcode for p in ps] == [0, 0]
+    r = np.load(os.path.join(outdir, "s0.npz"))
+    I = r["I"]
+    assert (I[0, :6] >= 0).all() and (I[0, 6:] == -1).all()         # 3 + 3 real rows
+    assert (I[1] == -1).all()                                         # no shard has a row
+    assert (I[2, :k_real(I[2])] >= 0).all() and k_real(I[2]) == 10     # shard 0 fills it
+    assert ((I == -1) | ((I >= 0) & (I < 2000))).all()
+
+
+def k_real(row):
+    return int((row >= 0).sum())
