@@ -4,7 +4,8 @@ The query kernels consume the dicts the reference builds (same keys, dtypes, byt
 with CUDA, torch and faiss (`src/rev_fanardb.py:33-61`, `src/ideas_engine2.py:23-40`, `src/engine_cell.py:8-32`,
 `throughput/enginei8.py:19-27`, `throughput/s2lut.py:9-29`, `src/tiered.py:15-44`).  faiss is not available here, so the
 two places it is used (the 1-D Lloyd-Max codebooks behind `tiered.DIST`/`tiered.CB`, `src/tiered.py:6-10`) are computed
-from the Gaussian density directly; every other step follows the reference's recipe.  Layout produced:
+from the Gaussian density directly (the Lloyd-Max quantiser of N(0,1), then the reference's own sampled MSE on its
+1M samples); every other step follows the reference's recipe.  Layout produced:
 
 s1   : c [d] f32, off (numpy int64 [NC+1]), off_t int64 [NC+1], order int32 [N] (sorted position -> original id),
        means16 [NC,d] f16, inv_mnorm [NC] f32, cen (= inv_mnorm)                              (`src/engine_cell.py:23,26-32`)
@@ -71,20 +72,61 @@ def lloyd_table(bits: int):
     return _LM_CACHE[bits]
 
 
+_DIST_SAMPLES = None
+_DIST_CACHE = {}
+
+
+def lloyd_levels_f32(bits: int):
+    """The 1-D codebook of `bits` bits as the reference holds it: sorted float32 levels (`src/tiered.py:8`, faiss's 1-D
+    k-means fit there; the Lloyd-Max quantiser of N(0,1) here)."""
+    return np.sort(lloyd_table(bits)[0].astype(np.float32))
+
+
 def dist(bits: int) -> float:
-    """Lloyd-Max MSE per bit width (the reference's `tiered.DIST`); DIST[0] = 1."""
-    return 1.0 if bits == 0 else lloyd_table(bits)[1]
+    """The reference's `tiered.DIST[bits]` (`src/tiered.py:6-9`): mean squared error of the codebook over its 1M
+    standard-normal samples (numpy default_rng(1)), each sample taken to the level picked by the midpoints
+    (np.searchsorted), in float32; DIST[0] = 1."""
+    global _DIST_SAMPLES
+    if bits == 0:
+        return 1.0
+    if bits not in _DIST_CACHE:
+        if _DIST_SAMPLES is None:
+            _DIST_SAMPLES = np.random.default_rng(1).standard_normal((1_000_000, 1)).astype(np.float32)
+        g = _DIST_SAMPLES[:, 0]
+        cb = lloyd_levels_f32(bits)
+        th = (cb[1:] + cb[:-1]) / 2
+        _DIST_CACHE[bits] = float(((g - cb[np.searchsorted(th, g)]) ** 2).mean())
+    return _DIST_CACHE[bits]
 
 
 def uniform_delta(bits: int) -> float:
-    """Step of the MSE-best uniform quantiser on the reference's grid linspace(0.02, 2.5, 600) (`throughput/s2lut.py:9-16`);
-    the MSE is evaluated exactly on the Gaussian density instead of on 2M samples."""
+    """Step of the MSE-best uniform quantiser on the reference's grid linspace(0.02, 2.5, 600) (`throughput/s2lut.py:9-16`),
+    the MSE evaluated exactly on the Gaussian density (the reference estimates it from 2M samples of its device's
+    generator: `uniform_delta_sampled`).  Used for host-built indexes."""
     mid = (2 ** bits - 1) / 2
     best = None
     for delta in np.linspace(0.02, 2.5, 600):
         m = _gauss_mse((np.arange(2 ** bits) - mid) * delta)
         if best is None or m < best[0]:
             best = (m, float(delta))
+    return best[1]
+
+
+def uniform_delta_sampled(bits: int, device, n: int = 2_000_000) -> float:
+    """The reference's `uniform_cb` step (`throughput/s2lut.py:9-16`): n standard-normal samples from a generator of
+    `device` seeded 3, levels (k - (2^b - 1)/2) * delta for each delta of linspace(0.02, 2.5, 600), samples taken to
+    the level picked by the midpoints (bucketize), the first delta of least mean squared error.  On the reference's
+    device (CUDA) this is its step; on the host it follows the host generator."""
+    g = torch.randn(n, device=device, generator=torch.Generator(device=device).manual_seed(3))
+    mid = (2 ** bits - 1) / 2
+    k = torch.arange(2 ** bits, device=device).float()
+    best = None
+    for delta in np.linspace(0.02, 2.5, 600):
+        lv = (k - mid) * delta
+        th = (lv[1:] + lv[:-1]) / 2
+        mse = ((g - lv[torch.bucketize(g, th)]) ** 2).mean().item()
+        if best is None or mse < best[0]:
+            best = (mse, float(delta))
     return best[1]
 
 
@@ -148,15 +190,17 @@ def build_i8_codes(X16, order, off_t, means16, V, R=256, chunk=65536):
     return Z, zs, Vr
 
 
-def allocate(lam, B, bmin=1, bmax=8):
-    """MSE water-filling bit allocation over 32-dim groups -> tiers (s, e, bits) (`src/tiered.py:19-27`)."""
+def allocate(lam, B, bmin=1, bmax=8, dist_table=None):
+    """MSE water-filling bit allocation over 32-dim groups -> tiers (s, e, bits) (`src/tiered.py:19-27`).  dist_table
+    (bits -> MSE) defaults to `dist`."""
+    D = dist_table.__getitem__ if dist_table is not None else dist
     d = len(lam)
     NG = d // G
     lamg = lam.reshape(NG, G).sum(1).cpu().numpy()
     b = np.full(NG, bmin)
     left = B - bmin * d
     while left >= G:
-        gain = [lamg[i] * (dist(b[i]) - dist(b[i] + 1)) if b[i] < bmax else -1 for i in range(NG)]
+        gain = [lamg[i] * (D(b[i]) - D(b[i] + 1)) if b[i] < bmax else -1 for i in range(NG)]
         i = int(np.argmax(gain))
         b[i] += 1
         left -= G
@@ -250,7 +294,9 @@ def build_index(X16, nlist, R=256, refine_bits=None, seed=0, kmeans_sample=200_0
         TS = allocate(lam, refine_bits)
         codes = {}
         if uniform:
-            deltas = {b: uniform_delta(b) for b in sorted({bb for _, _, bb in TS})}
+            # the reference's sampled step on a CUDA build device (its own device); the exact-density step on the host
+            step = (lambda b: uniform_delta_sampled(b, dev)) if dev.type == "cuda" else uniform_delta
+            deltas = {b: step(b) for b in sorted({bb for _, _, bb in TS})}
             CBu = {}
             for b, dl in deltas.items():
                 lv = ((torch.arange(2 ** b, device=dev).float() - (2 ** b - 1) / 2) * dl)
@@ -263,8 +309,8 @@ def build_index(X16, nlist, R=256, refine_bits=None, seed=0, kmeans_sample=200_0
         if lloyd:
             CBl = {}
             for b in sorted({bb for _, _, bb in TS}):
-                lv = torch.as_tensor(lloyd_table(b)[0], device=dev)
-                CBl[b] = (lv, (lv[1:] + lv[:-1]) / 2)
+                lv = lloyd_levels_f32(b)                          # levels and midpoints in float32 (`src/tiered.py:8-10`)
+                CBl[b] = (torch.from_numpy(lv).to(dev), torch.from_numpy((lv[1:] + lv[:-1]) / 2).to(dev))
             cl = tiered_build(X16, order, c, V, TS, CBl, seed)
             cl["cbf"] = [CBl[bb][0].contiguous() for _, _, bb in TS]
             cl["VP"] = block_rotation(cl)
