@@ -31,6 +31,9 @@ SIGNATURES = {
     "fvs_i8_scan": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, P, P, P, P, P, I32, P, I32]),
     "fvs_i8_scan_tc": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I64, P, P, P, P, P, I32, P,
                               I32, P]),
+    "fvs_i8_scan_cells": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I64, P, P, P, P, P, I32, P,
+                                 I32, P, P]),
+    "fvs_cell_lists": (I32, [P, P, I32, P, P, P, P, P]),
     "fvs_threshold": (I32, [P, P, I32, P, P, I32, I32, P, I32, I32, P]),
     "fvs_select_topk": (I32, [P, P, P, P, I32, I32, I32, P, P, P, P, F32, I32]),
     "fvs_lut_build": (I32, [P, P, I32, I32, I32, I32, P, I32, P, P, P, P]),

@@ -162,7 +162,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) dense_tc_kernel(const __grid_cons
             const int row0 = (t / p.nqb) * TM, q0 = (t % p.nqb) * p.QB;
             const int nq = min(p.QB, p.B - q0);
             const int b = tc & 1;
-            if (!mbar_wait(t_full(b), (tc >> 1) & 1, abort, WL)) break;
+            if (!warp_wait(t_full(b), (tc >> 1) & 1, abort, WL)) break;
             tc_fence_after();
             const int row = row0 + 32 * ew + lane;
             const bool rvalid = row < p.N;

@@ -319,8 +319,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                             qsv[rr] = p.qs[qq[rr]];
                             thv[rr] = MODE ? p.t0[qq[rr]] : 0.f;
                         }
-                    if (!mbar_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort, WL) ||
-                        !mbar_wait(t_empty(st), ((nb_g / T_STAGES) & 1) ^ 1, abort, WL)) {
+                    if (!warp_wait(b_empty(s), ((nb_g / B_STAGES) & 1) ^ 1, abort, WL) ||
+                        !warp_wait(t_empty(st), ((nb_g / T_STAGES) & 1) ^ 1, abort, WL)) {
                         ok = false;
                         break;
                     }
@@ -378,8 +378,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_tc_kernel(const __grid_const
                 for (int i = 0; i * QN < qn; i++, nb_e++) {
                     if (nb_e % EPI_GROUPS != eg) continue;
                     const int st = nb_e % T_STAGES;
-                    if (!mbar_wait(t_full(st), (nb_e / T_STAGES) & 1, abort, WL) ||
-                        !mbar_wait(m_full(st), (nb_e / T_STAGES) & 1, abort, WL)) {  // m_full: acquire the metadata
+                    if (!warp_wait(t_full(st), (nb_e / T_STAGES) & 1, abort, WL) ||
+                        !warp_wait(m_full(st), (nb_e / T_STAGES) & 1, abort, WL)) {  // m_full: acquire the metadata
                         ok = false;
                         break;
                     }

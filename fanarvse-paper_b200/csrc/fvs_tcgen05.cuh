@@ -47,6 +47,15 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     return false;
 }
 
+// the same wait made by every lane of a warp, with one outcome for the whole warp (false when any lane's wait gave
+// up), so that a warp never splits at a wait: warp-collective instructions after it (tcgen05.ld, shuffles) are reached
+// by all lanes or by none
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort,
+                                          uint32_t limit = WAIT_LIMIT) {
+    const bool r = mbar_wait(bar, parity, abort, limit);
+    return __all_sync(0xffffffffu, r);
+}
+
 // wait used while draining before exit: copies and MMAs already issued complete whatever the rest of the CTA did, so
 // this wait ignores the abort flag and always allows the full WAIT_LIMIT polls (a CTA must not leave with a copy into
 // its shared memory, or an MMA into its tensor memory, still in flight)

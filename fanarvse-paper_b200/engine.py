@@ -82,6 +82,9 @@ class IndexI8:
         self.VP16 = VP16[:, :self.D].contiguous()
         self.H16 = f(H16, torch.float16)
         self.d = self.H16.shape[1]
+        sizes = np.diff(self.off_np)
+        # cells largest first: the order in which the cell-major scan hands cells out (big cells early, small at the end)
+        self.cell_order = f(np.argsort(-sizes, kind="stable").astype(np.int32), torch.int32)
         tc, tr, self.MB = static_tiles(self.off_np, _lib.lib().fvs_i8_tile_rows())
         self.tile_cell, self.tile_row0 = f(tc, torch.int32), f(tr, torch.int32)
         self.ntiles = len(tc)
@@ -109,7 +112,8 @@ class EngineB200I8:
     DELTA = 0.07
     LUTH = True
     BETA = None
-    SCAN = "tc"      # "tc": tcgen05 kernel (the product path); "mma": the mma.sync kernel kept as a baseline
+    SCAN = "cells"   # "cells": cell-major tcgen05 scan (the product path); "tc": tile-major tcgen05 scan; "mma": the
+    #                  mma.sync scan, kept as measured baselines
     SMALL = 32       # batches up to this size take the streaming scan (fvs_i8_scan_small) instead of the tile scan
     FB_INGRAPH = 48  # flagged rows recomputed inside the batch's own graph (batches of FB_MIN_BATCH or more)
     FB_MIN_BATCH = 256
@@ -126,6 +130,9 @@ class EngineB200I8:
         self.status = torch.zeros(1, dtype=torch.int32, device=index.device)
         self.work = torch.zeros(index.NC, dtype=torch.int32, device=index.device)
         self._nflag = torch.zeros(1, dtype=torch.int32, device=index.device)   # rows flagged by the main pass
+        # work counter of the cell-major scan (left at zero by every launch); like `status`, it belongs to one search
+        # at a time: an engine's searches run one after another
+        self.sched = torch.zeros(2, dtype=torch.int32, device=index.device)
 
     def pairs(self, probe, ncols, QM, want_slot):
         """pair list by cell over the first ncols probe columns (`throughput/enginei8.py:11-16`)."""
@@ -163,9 +170,26 @@ class EngineB200I8:
         self.launches += 2   # fvs_pairs_split issues three kernels
         return qid, coff, ccnt, ccnt1, qcp, slot
 
-    def _scan(self, mode, name, q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc):
+    def cell_lists(self, ccnt1, ccnt):
+        """the two passes' work lists for the cell-major scan: (list1, list, nlist [2] on the device)."""
         ix = self.ix
-        if self.SCAN == "tc":
+        dev = ccnt.device
+        list1 = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        lst = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        nl = torch.empty(2, dtype=torch.int32, device=dev)
+        self._call("cell_lists", self.L.fvs_cell_lists, ptr(ix.cell_order), ix.NC, ptr(ccnt1), ptr(ccnt), ptr(list1),
+                   ptr(lst), ptr(nl))
+        return list1, lst, nl
+
+    def _scan(self, mode, name, q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc, lists=None):
+        ix = self.ix
+        if self.SCAN == "cells":
+            lst, nl = lists
+            self._call(name, self.L.fvs_i8_scan_cells, mode, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff),
+                       ptr(ccnt), ptr(qcp), ptr(lst), ptr(nl), ix.NC, ptr(ix.off), ix.NC, ptr(ix.Z), ix.N, ptr(ix.zs),
+                       ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB, ptr(self.sched),
+                       ptr(self.status))
+        elif self.SCAN == "tc":
             self._call(name, self.L.fvs_i8_scan_tc, mode, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
                        ptr(qcp), ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.Z), ix.N,
                        ptr(ix.zs), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB, ptr(self.status))
@@ -232,15 +256,19 @@ class EngineB200I8:
             return self._stage1_small(q8, qs, B, QM, probe, K, M, rho, n1, rho_override)
         # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
         qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
+        l1 = l2 = None
+        if self.SCAN == "cells":
+            list1, lst, nl = self.cell_lists(ccnt1, ccnt)
+            l1, l2 = (list1, nl[0:1]), (lst, nl[1:2])
         bmc = torch.empty(qid.numel() * ix.MB, device=dev)   # block-maxima rows addressed by pair position
-        self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc)
+        self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc, l1)
         t0 = torch.empty(B, device=dev)
         self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1,
                    ptr(ix.off), B, int(np.ceil(rho * K)), ptr(t0))
         cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
-        self._scan(1, "i8_scan_emit", q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None)
+        self._scan(1, "i8_scan_emit", q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None, l2)
         pos = torch.empty(B, K, dtype=torch.int64, device=dev)
         est1 = torch.empty(B, K, device=dev)
         ok = torch.empty(B, dtype=torch.uint8, device=dev)

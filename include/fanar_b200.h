@@ -220,6 +220,29 @@ int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_
 int fvs_trellis_tile_rows(void);
 
 /*
+ * The int8 stage-1 scan organised by cells (same contract and results as fvs_i8_scan_tc; replaces the same reference
+ * kernels, `throughput/ivf8c_kern.py:2-36`): the CTAs take the cells of `list` (nlist[0] of them, a device count) one at
+ * a time with an atomicAdd on sched[0]; a cell's queries are gathered once and held while all of its code tiles are
+ * scanned; a tile is fetched as the 32-row blocks the cell occupies.  maxlist >= the count (sizes the grid: NC).
+ * sched: 2 int32, zero before the first launch; every launch leaves them zero (the last CTA resets them), so calls on
+ * one stream can share them, while calls that may run at the same time need their own.  Other arguments as
+ * fvs_i8_scan_tc (mode 0 reads the first pass's per-cell counts, mode 1 the emit pass's).
+ */
+int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8, const float* qs, int B, int R,
+                      const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
+                      const int32_t* list, const int32_t* nlist, int maxlist, const int64_t* off, int NC,
+                      const int8_t* Z, int64_t N, const float* zs, const float* t0, int32_t* cnt, float* bval,
+                      int32_t* bpos, int M, float* bmc, int MB, int32_t* sched, int32_t* status);
+
+/*
+ * The work lists of fvs_i8_scan_cells for both passes (new; the reference launches one program per (cell, block)):
+ * the cells of `order` [NC] (a permutation of the cells, largest first) with ccnt1[c] > 0 into list1 and with
+ * ccnt[c] > 0 into list, in that order; nlist[0], nlist[1] = their lengths (device).  ccnt1 may be NULL (no list1).
+ */
+int fvs_cell_lists(fvs_stream_t stream, const int32_t* order, int NC, const int32_t* ccnt1, const int32_t* ccnt,
+                   int32_t* list1, int32_t* list, int32_t* nlist);
+
+/*
  * Small-batch int8 scan (B <= 32): same contract and arithmetic as fvs_i8_scan_tc, streamed from HBM with 16-byte loads
  * and dp4a, one CTA per (query, probe column, 4 blocks), taking the work straight from probe [B, nprobe] (columns
  * 0..ncols-1) without a pair list: the pair constant is float(QM[q, c]) * mnorm[c] (mnorm may be NULL: the constant is

@@ -26,9 +26,9 @@ def eng():
 
 
 def _set_scan(E, scan):
-    """"tc": the tcgen05 tile scan at every batch size; "small": the streaming scan at every batch size; "mma": the
-    mma.sync baseline."""
-    E.SCAN = "mma" if scan == "mma" else "tc"
+    """"cells": the cell-major tcgen05 scan at every batch size (the product path); "tc": the tile-major tcgen05 scan;
+    "small": the streaming scan at every batch size; "mma": the mma.sync baseline."""
+    E.SCAN = scan if scan in ("mma", "tc", "cells") else "cells"
     E.SMALL = 10 ** 9 if scan == "small" else 0
 
 
@@ -44,7 +44,7 @@ def _golden_engine(eng, f, case):
     return E, ix, idx, K, nprobe, k, M
 
 
-@pytest.mark.parametrize("scan", ["tc", "mma"])
+@pytest.mark.parametrize("scan", ["cells", "tc", "mma"])
 @pytest.mark.parametrize("case", ["A_", "B_"])
 def test_stage1_matches_reference_golden(golden_i8, eng, case, scan):
     f = golden_i8
@@ -124,12 +124,14 @@ def _random_index(eng, n, d, nlist, nq, seed, comps=32):
     (30000, 1536, 96, 48, 60, 16, 10, 1024),
     (20000, 256, 64, 33, 40, 64, 10, 4096),       # every cell probed
     (20000, 256, 64, 1, 40, 12, 10, 4096),        # batch 1
+    (12000, 256, 16, 450, 40, 12, 10, 4096),      # up to 450 queries per cell: cells scanned in several query groups
 ])
-@pytest.mark.parametrize("scan", ["tc", "small", "mma"])
+@pytest.mark.parametrize("scan", ["cells", "tc", "small", "mma"])
 def test_search_matches_oracle(eng, n, d, nlist, nq, K, nprobe, k, M, scan):
     ds, ix, oi = _random_index(eng, n, d, nlist, nq, seed=7)
     E = eng.EngineB200I8(ix)
     E.MSZ = M
+    E.FB_INGRAPH = 0           # the main pass alone (its recompute is checked in test_in_graph_recompute)
     _set_scan(E, scan)
     Q = ds["queries"]
     r = E.search_eager(Q, K, 1.25, nprobe, k)

@@ -26,9 +26,10 @@ def setup():
     return ds, ix, eng
 
 
-def _engine(eng, ix):
+def _engine(eng, ix, scan="cells"):
     E = eng.EngineB200I8(ix)
-    E.SMALL = 0          # the tcgen05 tile scan at every batch size
+    E.SCAN = scan        # a tcgen05 scan (cell-major or tile-major) at every batch size
+    E.SMALL = 0
     E.FB_INGRAPH = 0
     return E
 
@@ -43,34 +44,36 @@ def _with_limit(polls, fn):
         lib.fvs_set_wait_limit(prev)
 
 
-def test_expired_wait_raises_and_device_stays_usable(setup):
+@pytest.mark.parametrize("scan", ["cells", "tc"])
+def test_expired_wait_raises_and_device_stays_usable(setup, scan):
     ds, ix, eng = setup
     L = pkg("_lib")
     Q = ds["queries"]
     K, z, nprobe, k = 40, 1.5, 16, 10
-    I0, nr0, ids0 = _engine(eng, ix).search(Q, K, z, nprobe, k)
+    mk = lambda e, i: _engine(e, i, scan)
+    I0, nr0, ids0 = mk(eng, ix).search(Q, K, z, nprobe, k)
     torch.cuda.synchronize()
     prev = L.lib().fvs_set_wait_limit(0)
     assert L.lib().fvs_set_wait_limit(prev) == 0 and prev == 4194304          # the default, restored
 
     # every pipeline wait gives up at once: the search raises (graph path) and the eager scan reports through status
-    E = _engine(eng, ix)
+    E = mk(eng, ix)
     with pytest.raises(L.FvsError, match="bounded device wait"):
         _with_limit(0, lambda: E.search(Q, K, z, nprobe, k))
-    E2 = _engine(eng, ix)
+    E2 = mk(eng, ix)
     _with_limit(0, lambda: E2.search_eager(Q, K, z, nprobe, k))
     torch.cuda.synchronize()
     assert int(E2.status) == 1
 
     # small budgets: some waits give up with copies / MMAs in flight (drain path), others finish; every call returns
     for polls in (1, 4, 32, 256):
-        E3 = _engine(eng, ix)
+        E3 = mk(eng, ix)
         _with_limit(polls, lambda: E3.search_eager(Q, K, z, nprobe, k))
         torch.cuda.synchronize()
         assert int(E3.status) in (0, 1)
 
     # the same device afterwards: a normal search gives the results of before, status clear
-    E4 = _engine(eng, ix)
+    E4 = mk(eng, ix)
     I4, nr4, ids4 = E4.search(Q, K, z, nprobe, k)
     torch.cuda.synchronize()
     assert int(E4.status) == 0
