@@ -33,12 +33,13 @@ SIGNATURES = {
                               I32, P]),
     "fvs_i8_scan_cells": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I64, P, P, P, P, P, I32, P,
                                  I32, P, P]),
-    "fvs_cell_lists": (I32, [P, P, I32, P, P, P, P, P]),
+    "fvs_route_pairs": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P]),
+    "fvs_cell_lists": (I32, [P, P, I32, P, P, P, P, P, P, I32]),
     "fvs_threshold": (I32, [P, P, I32, P, P, I32, I32, P, I32, I32, P]),
     "fvs_select_topk": (I32, [P, P, P, P, I32, I32, I32, P, P, P, P, F32, I32]),
     "fvs_lut_build": (I32, [P, P, I32, I32, I32, I32, P, I32, P, P, P, P]),
     "fvs_lut_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P, P, P]),
-    "fvs_lut_score_zq": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P]),
+    "fvs_lut_score_zq": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P]),
     "fvs_refine": (I32, [P, P, I32, P, P, P, P, I32, I32, F32, I32, P, I32, P, P, P, P]),
     "fvs_i8_scan_small": (I32, [P, I32, P, P, I32, I32, P, I32, I32, P, I32, P, P, P, P, P, P, P, P, I32, P, I32]),
     "fvs_trellis_tile_rows": (I32, []),
@@ -51,7 +52,8 @@ SIGNATURES = {
     "fvs_viterbi_encode": (I32, [P, P, I32, I32, P, I32, P]),
     "fvs_dense_scan_tc": (I32, [P, I32, P, P, I32, I32, P, P, I64, P, P, P, P, I32, P, I64, P]),
     "fvs_rth_largest": (I32, [P, P, I32, I32, I64, I32, P]),
-    "fvs_lut_score_rec": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, P, P, P, P, P, I32, I32, I64, P, P, P]),
+    "fvs_lut_score_rec": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, I32, I32, I64, P, P,
+                                 P]),
     "fvs_tiered_score_rec": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, I32, I32, I64, P, P]),
     "fvs_flagged_gather": (I32, [P, P, I32, I32, P, P, I32, P, P, P]),
     "fvs_rows_scatter": (I32, [P, P, I32, I32, P, I32, P, P, P]),

@@ -575,14 +575,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
 }
 
 // Compact lists of the cells a pass visits, in the order given (largest first): cells with ccnt1 > 0 (first pass) and
-// with ccnt > 0 (emit pass).  One CTA; nlist[0], nlist[1] = the lengths.
+// with ccnt > 0 (emit pass).  One CTA; nlist[0], nlist[1] = the lengths; zero[0..nzero) is cleared on the way (the
+// emit pass's counters, so that they need no fill of their own).
 __global__ void __launch_bounds__(1024) cell_lists_kernel(const int32_t* __restrict__ order, int NC,
                                                           const int32_t* __restrict__ ccnt1,
                                                           const int32_t* __restrict__ ccnt, int32_t* __restrict__ list1,
-                                                          int32_t* __restrict__ list, int32_t* __restrict__ nlist) {
+                                                          int32_t* __restrict__ list, int32_t* __restrict__ nlist,
+                                                          int32_t* __restrict__ zero, int nzero) {
     __shared__ int wsum[2][32];
     __shared__ int base[2];
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    for (int i = tid; i < nzero; i += 1024) zero[i] = 0;
     if (tid == 0) base[0] = base[1] = 0;
     __syncthreads();
     for (int c0 = 0; c0 < NC; c0 += 1024) {
@@ -625,10 +628,12 @@ __global__ void __launch_bounds__(1024) cell_lists_kernel(const int32_t* __restr
 }  // namespace fvs
 
 extern "C" int fvs_cell_lists(fvs_stream_t stream, const int32_t* order, int NC, const int32_t* ccnt1,
-                              const int32_t* ccnt, int32_t* list1, int32_t* list, int32_t* nlist) {
-    FVS_CHECK_ARG(order && ccnt && list && nlist && NC > 0);
+                              const int32_t* ccnt, int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero,
+                              int nzero) {
+    FVS_CHECK_ARG(order && ccnt && list && nlist && NC > 0 && nzero >= 0);
     FVS_CHECK_ARG(ccnt1 == nullptr || list1 != nullptr);
-    fvs::cells::cell_lists_kernel<<<1, 1024, 0, stream>>>(order, NC, ccnt1, ccnt, list1, list, nlist);
+    FVS_CHECK_ARG(nzero == 0 || zero != nullptr);
+    fvs::cells::cell_lists_kernel<<<1, 1024, 0, stream>>>(order, NC, ccnt1, ccnt, list1, list, nlist, zero, nzero);
     return fvs_launch_status();
 }
 

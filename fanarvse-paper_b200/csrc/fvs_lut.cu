@@ -166,8 +166,8 @@ __device__ __forceinline__ uint32_t nibble_at9(uint32_t w, int p) {
 
 template <bool HALF, int WPL, bool REC, int GAC, bool WCOL = false>
 __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __restrict__ pos, int B, int K,
-                                                           const float* __restrict__ qc, const float* __restrict__ Zq,
-                                                           int ldz, int D, int GA_, TierSet ts,
+                                                           const float* __restrict__ qc, const void* __restrict__ Zq,
+                                                           int ldz, int zh, int D, int GA_, TierSet ts,
                                                            const __half* __restrict__ scale,
                                                            const __half* __restrict__ sig, int64_t N,
                                                            const int32_t* __restrict__ ncnt, float* __restrict__ est,
@@ -186,7 +186,10 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
             sd[(int64_t)q * K + i] = 0.f;
         }
     if (lim == 0) return;
-    const float* z = Zq + (int64_t)q * ldz;
+    // the rotated query row: fp32, or the fp16 product itself (converted here, the same values as its .float())
+    const float* z = zh ? nullptr : reinterpret_cast<const float*>(Zq) + (int64_t)q * ldz;
+    const __half* zhr = zh ? reinterpret_cast<const __half*>(Zq) + (int64_t)q * ldz : nullptr;
+    auto zat = [&](int i) { return zhr ? __half2float(zhr[i]) : z[i]; };
     const int nblk = D / 32;
     // positions staged once (coalesced), so that each candidate round trip is the plane words alone
     for (int i = tid; i < lim; i += blockDim.x) s_pos[i] = (int32_t)pos[(int64_t)q * K + i];
@@ -194,11 +197,21 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     auto entries = [&](int ga, int cgrp, float (&e16)[16]) {
         float z0 = 0.f, z1 = 0.f, z2 = 0.f, z3 = 0.f;
         if (ga < nblk) {
-            const float4 zz = *reinterpret_cast<const float4*>(z + 32 * ga + 4 * cgrp);
-            z0 = zz.x;
-            z1 = zz.y;
-            z2 = zz.z;
-            z3 = zz.w;
+            if (zhr) {
+                const uint2 u = *reinterpret_cast<const uint2*>(zhr + 32 * ga + 4 * cgrp);
+                const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+                const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+                z0 = a.x;
+                z1 = a.y;
+                z2 = b.x;
+                z3 = b.y;
+            } else {
+                const float4 zz = *reinterpret_cast<const float4*>(z + 32 * ga + 4 * cgrp);
+                z0 = zz.x;
+                z1 = zz.y;
+                z2 = zz.z;
+                z3 = zz.w;
+            }
         }
 #pragma unroll
         for (int v = 0; v < 16; v++) {
@@ -241,7 +254,7 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     if (warp < ts.T) {  // warp t reduces tier t
         float a = 0.f, b = 0.f;
         for (int i = ts.s[warp] + lane; i < ts.e[warp]; i += 32) {
-            const float x = z[i];
+            const float x = zat(i);
             a += x;
             b += x * x;
         }
@@ -459,8 +472,8 @@ extern "C" int fvs_lut_score(fvs_stream_t stream, const int64_t* pos, int B, int
     return fvs_launch_status();
 }
 
-extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
-                                int ldz, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e,
+extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const void* Zq,
+                                int ldz, int zq_half, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e,
                                 const int32_t* tier_bits, const float* tier_delta, const uint8_t* const* tier_planes,
                                 const uint16_t* scale, const uint16_t* sig, int64_t N, const int32_t* ncnt, float* est,
                                 float* sd) {
@@ -491,7 +504,8 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
         cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, false, 0, C>, sm);            \
         if (e != cudaSuccess) return (int)e;                                                                       \
         fvs::lut_score_zq_kernel<H, W, false, 0, C><<<dim3(B, S), 256, sm, stream>>>(                              \
-            pos, B, K, qc, Zq, ldz, D, GA, ts, (const __half*)scale, (const __half*)sig, N, ncnt, est, sd, rs);    \
+            pos, B, K, qc, Zq, ldz, zq_half, D, GA, ts, (const __half*)scale, (const __half*)sig, N, ncnt, est, sd,   \
+            rs);                                                                                                   \
     } while (0)
     if (half) {
         if (wcol) FVS_LZ(true, 4, true); else if (wpl <= 8) FVS_LZ(true, 8, false); else FVS_LZ(true, 12, false);
@@ -503,7 +517,7 @@ extern "C" int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, 
 }
 
 extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc,
-                                 const float* Zq, int ldz, int D, int half, int T, const int32_t* tier_s,
+                                 const void* Zq, int ldz, int zq_half, int D, int half, int T, const int32_t* tier_s,
                                  const int32_t* tier_e, const int32_t* tier_bits, const float* tier_delta,
                                  const uint8_t* rec, int RB, int soff, int64_t N, const int32_t* ncnt, float* est,
                                  float* sd) {
@@ -534,7 +548,7 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
         cudaError_t e = fvs_ensure_smem((const void*)fvs::lut_score_zq_kernel<H, W, true, G, C>, sm);             \
         if (e != cudaSuccess) return (int)e;                                                                       \
         fvs::lut_score_zq_kernel<H, W, true, G, C><<<dim3(B, S), 256, sm, stream>>>(                               \
-            pos, B, K, qc, Zq, ldz, D, GA, ts, nullptr, nullptr, N, ncnt, est, sd, rs);                            \
+            pos, B, K, qc, Zq, ldz, zq_half, D, GA, ts, nullptr, nullptr, N, ncnt, est, sd, rs);                   \
     } while (0)
 #define FVS_LR(H, W)                                                                                               \
     do {                                                                                                           \

@@ -1,0 +1,235 @@
+// Routing selection and pairing in two launches (the reference's routing top-n_p and `pairs_fast`,
+// `throughput/enginei8.py:11-16, 64-70`, which it runs as torch topk + a stable sort + scatter_add + cumsum + gathers).
+//
+// Launch 1, one CTA per query: the nprobe cells of largest fp16 routing score, ordered by (score desc, cell asc) as
+// fvs_route_topk orders them; while placing selected cell c at rank j, the CTA also takes the pair's rank inside the
+// cell's list with one atomicAdd on a per-cell cursor (first-pass columns j < n1 on cur1, the others on cur2).  The
+// probe row holds (rank in cell << 32 | cell) until launch 2 rewrites it.
+// Launch 2, a grid over the pairs: every CTA scans the per-cell counts (cur1 + cur2) into offsets in shared memory,
+// then places its pairs: first-pass pairs of cell c at coff[c] + r, the others at coff[c] + cur1[c] + r (each cell's
+// first-pass pairs first, the layout of fvs_pairs_split), writes qid, the pair constant float(QM[q, c]) * mnorm[c] and
+// the first pass's pair slots, and the plain cell into probe.  CTA 0 also writes coff / ccnt / ccnt1, the two
+// passes' cell lists for fvs_i8_scan_cells (order given, non-empty cells) and clears the caller's counters.  The last
+// CTA to finish clears the cursors, so every call leaves them zero for the next.
+#include "fvs_common.cuh"
+
+namespace fvs {
+namespace rp {
+
+__device__ __forceinline__ uint32_t h2o(uint16_t u) { return (u & 0x8000u) ? (~u & 0xffffu) : (u | 0x8000u); }
+
+constexpr int THREADS = 256;
+constexpr int MAXP = 512;
+constexpr int PLACE_THREADS = 1024;
+constexpr int MAX_CELLS = 16384;  // per-cell offsets held in shared memory by every placing CTA
+
+template <int V>
+__global__ void __launch_bounds__(THREADS) route_rank_kernel(const uint16_t* __restrict__ QM, int NC, int nprobe,
+                                                             int n1, int32_t* __restrict__ cur1,
+                                                             int32_t* __restrict__ cur2, int64_t* __restrict__ probe) {
+    __shared__ RegSelectScratch rs;
+    __shared__ int s_fill;
+    __shared__ uint32_t s_sel[MAXP];
+    const int q = blockIdx.x, tid = threadIdx.x;
+    const uint4* row = reinterpret_cast<const uint4*>(QM + (int64_t)q * NC);
+    uint32_t key[8 * V];  // (order-preserving score << 16) | (65535 - cell); 0 = no cell
+#pragma unroll
+    for (int v = 0; v < V; v++) {
+        const int u = tid + v * THREADS;
+        const bool in = u * 8 < NC;
+        const uint4 w = in ? __ldg(row + u) : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const uint32_t h = (ws[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+            key[8 * v + e] = in ? ((h2o((uint16_t)h) << 16) | (uint32_t)(0xffff - (u * 8 + e))) : 0u;
+        }
+    }
+    if (tid == 0) s_fill = 0;
+    int above, equal;
+    const uint32_t T = block_rth_largest_reg<8 * V>(key, nprobe, rs, &above, &equal);  // keys are unique
+#pragma unroll
+    for (int i = 0; i < 8 * V; i++)
+        if (key[i] != 0u && key[i] >= T) {
+            const int slot = atomicAdd(&s_fill, 1);
+            if (slot < nprobe) s_sel[slot] = key[i];
+        }
+    __syncthreads();
+    for (int i = tid; i < nprobe; i += THREADS) {
+        const uint32_t ki = s_sel[i];
+        int rank = 0;
+        for (int j = 0; j < nprobe; j++) rank += s_sel[j] > ki;
+        const int c = 0xffff - (int)(ki & 0xffffu);
+        const int r = atomicAdd(rank < n1 ? cur1 + c : cur2 + c, 1);
+        probe[(int64_t)q * nprobe + rank] = ((int64_t)r << 32) | (int64_t)c;
+    }
+}
+
+// exclusive scan of cur1[c] + cur2[c] over the NC cells into coff (shared memory), by one block of PLACE_THREADS
+__device__ void scan_counts(const int32_t* __restrict__ cur1, const int32_t* __restrict__ cur2, int NC, int* coff) {
+    __shared__ int wsum[32];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int per = (NC + PLACE_THREADS - 1) / PLACE_THREADS;
+    const int b0 = tid * per;
+    int local = 0;
+    for (int i = 0; i < per; i++)
+        if (b0 + i < NC) local += cur1[b0 + i] + cur2[b0 + i];
+    int incl = local;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+    }
+    if (lane == 31) wsum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+        int w = wsum[lane];
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, w, o);
+            if (lane >= o) w += v;
+        }
+        wsum[lane] = w;
+    }
+    __syncthreads();
+    int run = incl - local + (warp > 0 ? wsum[warp - 1] : 0);
+    for (int i = 0; i < per; i++)
+        if (b0 + i < NC) {
+            coff[b0 + i] = run;
+            run += cur1[b0 + i] + cur2[b0 + i];
+        }
+    __syncthreads();
+}
+
+struct PlaceOut {
+    int32_t *qid, *coff, *ccnt, *ccnt1, *slot, *list1, *list, *nlist, *zero, *done;
+    float* qcp;
+    int nzero;
+};
+
+__global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __restrict__ probe, int B, int nprobe,
+                                                                    int n1, int NC, const __half* __restrict__ QM,
+                                                                    const float* __restrict__ mnorm,
+                                                                    const int32_t* __restrict__ order,
+                                                                    int32_t* __restrict__ cur1,
+                                                                    int32_t* __restrict__ cur2, PlaceOut o) {
+    extern __shared__ int s_coff[];  // NC
+    __shared__ int s_last;
+    const int tid = threadIdx.x;
+    scan_counts(cur1, cur2, NC, s_coff);
+    const int64_t n = (int64_t)B * nprobe;
+    for (int64_t i = (int64_t)blockIdx.x * PLACE_THREADS + tid; i < n; i += (int64_t)gridDim.x * PLACE_THREADS) {
+        const int64_t v = probe[i];
+        const int c = (int)(v & 0xffff), r = (int)(v >> 32);
+        const int q = (int)(i / nprobe), j = (int)(i - (int64_t)q * nprobe);
+        const int pos = s_coff[c] + (j < n1 ? r : cur1[c] + r);
+        o.qid[pos] = q;
+        const float s = __half2float(QM[(int64_t)q * NC + c]);
+        o.qcp[pos] = mnorm ? __fmul_rn(s, mnorm[c]) : s;
+        if (j < n1 && o.slot) o.slot[(int64_t)q * n1 + j] = pos;
+        probe[i] = c;
+    }
+    if (blockIdx.x == 0) {
+        for (int c = tid; c < NC; c += PLACE_THREADS) {
+            const int a = cur1[c], b = cur2[c];
+            o.coff[c] = s_coff[c];
+            o.ccnt[c] = a + b;
+            o.ccnt1[c] = a;
+        }
+        for (int i = tid; i < o.nzero; i += PLACE_THREADS) o.zero[i] = 0;
+        if (o.list) {
+            // the cells of `order` with first-pass pairs / with any pairs, in that order
+            __shared__ int wsum[2][32];
+            __shared__ int base[2];
+            const int lane = tid & 31, warp = tid >> 5;
+            if (tid == 0) base[0] = base[1] = 0;
+            __syncthreads();
+            for (int c0 = 0; c0 < NC; c0 += PLACE_THREADS) {
+                const int ii = c0 + tid;
+                const int c = ii < NC ? order[ii] : -1;
+                const bool k1 = c >= 0 && cur1[c] > 0;
+                const bool k2 = c >= 0 && cur1[c] + cur2[c] > 0;
+                const unsigned m1 = __ballot_sync(0xffffffffu, k1), m2 = __ballot_sync(0xffffffffu, k2);
+                if (lane == 0) {
+                    wsum[0][warp] = __popc(m1);
+                    wsum[1][warp] = __popc(m2);
+                }
+                __syncthreads();
+                int b1 = base[0], b2 = base[1], t1 = 0, t2 = 0;
+                for (int w = 0; w < PLACE_THREADS / 32; w++) {
+                    if (w < warp) {
+                        b1 += wsum[0][w];
+                        b2 += wsum[1][w];
+                    }
+                    t1 += wsum[0][w];
+                    t2 += wsum[1][w];
+                }
+                const unsigned below = (1u << lane) - 1u;
+                if (k1) o.list1[b1 + __popc(m1 & below)] = c;
+                if (k2) o.list[b2 + __popc(m2 & below)] = c;
+                __syncthreads();
+                if (tid == 0) {
+                    base[0] += t1;
+                    base[1] += t2;
+                }
+                __syncthreads();
+            }
+            if (tid == 0) {
+                o.nlist[0] = base[0];
+                o.nlist[1] = base[1];
+            }
+        }
+    }
+    // the last CTA out clears the cursors for the next call (every CTA has read them by then)
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        s_last = atomicAdd(o.done, 1) == (int)gridDim.x - 1;
+    }
+    __syncthreads();
+    if (s_last) {
+        __threadfence();
+        for (int c = tid; c < NC; c += PLACE_THREADS) {
+            cur1[c] = 0;
+            cur2[c] = 0;
+        }
+        if (tid == 0) *o.done = 0;
+    }
+}
+
+}  // namespace rp
+}  // namespace fvs
+
+extern "C" int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
+                               const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid, float* qcp,
+                               int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
+                               int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work) {
+    using namespace fvs::rp;
+    FVS_CHECK_ARG(QM && probe && qid && qcp && coff && ccnt && ccnt1 && work && B >= 0 && NC > 0);
+    FVS_CHECK_ARG(nprobe >= 1 && nprobe <= NC && n1 >= 1 && n1 <= nprobe && nzero >= 0);
+    FVS_CHECK_ARG(order == nullptr || (list1 && list && nlist));
+    FVS_CHECK_ARG(nzero == 0 || zero != nullptr);
+    if (NC % 8 != 0 || ((uintptr_t)QM & 15) != 0 || nprobe > MAXP || NC > MAX_CELLS) return FVS_ERANGE;
+    if (B == 0) return FVS_OK;
+    int32_t *cur1 = work, *cur2 = work + NC, *done = work + 2 * NC;
+    const int V = (NC + THREADS * 8 - 1) / (THREADS * 8);
+    if (V <= 1)
+        route_rank_kernel<1><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+    else if (V <= 2)
+        route_rank_kernel<2><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+    else if (V <= 4)
+        route_rank_kernel<4><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+    else
+        route_rank_kernel<8><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+    const int64_t npairs = (int64_t)B * nprobe;
+    const int nsm = fvs_sm_count();
+    int grid = (int)((npairs + PLACE_THREADS * 2 - 1) / (PLACE_THREADS * 2));
+    grid = grid < 1 ? 1 : grid > nsm ? nsm : grid;
+    const size_t sm = (size_t)NC * sizeof(int);
+    cudaError_t e = fvs_ensure_smem((const void*)pairs_place_kernel, sm);
+    if (e != cudaSuccess) return (int)e;
+    PlaceOut o{qid, coff, ccnt, ccnt1, slot, list1, list, nlist, zero, done, qcp, nzero};
+    pairs_place_kernel<<<grid, PLACE_THREADS, sm, stream>>>(probe, B, nprobe, n1, NC, (const __half*)QM, mnorm, order,
+                                                            cur1, cur2, o);
+    return fvs_launch_status();
+}

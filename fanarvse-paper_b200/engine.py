@@ -170,15 +170,16 @@ class EngineB200I8:
         self.launches += 2   # fvs_pairs_split issues three kernels
         return qid, coff, ccnt, ccnt1, qcp, slot
 
-    def cell_lists(self, ccnt1, ccnt):
-        """the two passes' work lists for the cell-major scan: (list1, list, nlist [2] on the device)."""
+    def cell_lists(self, ccnt1, ccnt, zero=None):
+        """the two passes' work lists for the cell-major scan: (list1, list, nlist [2] on the device); `zero` (the emit
+        pass's counters) is cleared in the same launch."""
         ix = self.ix
         dev = ccnt.device
         list1 = torch.empty(ix.NC, dtype=torch.int32, device=dev)
         lst = torch.empty(ix.NC, dtype=torch.int32, device=dev)
         nl = torch.empty(2, dtype=torch.int32, device=dev)
         self._call("cell_lists", self.L.fvs_cell_lists, ptr(ix.cell_order), ix.NC, ptr(ccnt1), ptr(ccnt), ptr(list1),
-                   ptr(lst), ptr(nl))
+                   ptr(lst), ptr(nl), ptr(zero), 0 if zero is None else zero.numel())
         return list1, lst, nl
 
     def _scan(self, mode, name, q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc, lists=None):
@@ -242,7 +243,36 @@ class EngineB200I8:
             beta = 1.5
         return min(max(int(np.ceil(beta * K / (self.ix.N / self.ix.NC / BN + 1))), 1), nprobe)
 
-    def stage1_i8(self, Qb, QM, probe, K, rho_override=None, M_override=None, q8qs=None, small=None):
+    def fused_routing(self, B, nprobe):
+        """whether routing and pairing run as the two launches of fvs_route_pairs (batches that take the cell-major scan;
+        shapes the fused kernels take)"""
+        NC = self.ix.NC
+        return self.SCAN == "cells" and B > self.SMALL and NC % 8 == 0 and NC <= 16384 and nprobe <= 512
+
+    def route_pairs(self, QM, nprobe, n1):
+        """`QM.topk(nprobe)` and both passes' pair lists (`throughput/enginei8.py:11-16, 67-70`) in two launches; also
+        the scan's cell lists and cleared emit counters.  Returns probe and the pair tuple stage1_i8 takes."""
+        ix = self.ix
+        B = QM.shape[0]
+        dev = QM.device
+        work = self.__dict__.get("_rp_work")
+        if work is None:
+            work = self._rp_work = torch.zeros(2 * ix.NC + 1, dtype=torch.int32, device=dev)
+        probe = torch.empty(B, nprobe, dtype=torch.int64, device=dev)
+        n = B * nprobe
+        qid = torch.empty(n, dtype=torch.int32, device=dev)
+        qcp = torch.empty(n, device=dev)
+        coff, ccnt, ccnt1, list1, lst = (torch.empty(ix.NC, dtype=torch.int32, device=dev) for _ in range(5))
+        slot = torch.empty(B * n1, dtype=torch.int32, device=dev)
+        nl = torch.empty(2, dtype=torch.int32, device=dev)
+        cnt = torch.empty(B, dtype=torch.int32, device=dev)
+        self._call("route_pairs", self.L.fvs_route_pairs, ptr(QM), B, ix.NC, nprobe, n1, ptr(ix.mnorm),
+                   ptr(ix.cell_order), ptr(probe), ptr(qid), ptr(qcp), ptr(coff), ptr(ccnt), ptr(ccnt1), ptr(slot),
+                   ptr(list1), ptr(lst), ptr(nl), ptr(cnt), B, ptr(work))
+        self.launches += 1   # two kernels
+        return probe, (qid, coff, ccnt, ccnt1, qcp, slot, list1, lst, nl, cnt)
+
+    def stage1_i8(self, Qb, QM, probe, K, rho_override=None, M_override=None, q8qs=None, small=None, pairs=None):
         """`throughput/enginei8.py:36-60` on the C library: returns pos [B,K] int64, ok [B] bool, est1 [B,K], n1."""
         ix, L = self.ix, self.L
         B = Qb.shape[0]
@@ -254,18 +284,24 @@ class EngineB200I8:
         probe = probe.contiguous()
         if (B <= self.SMALL and self.SCAN != "mma") if small is None else small:
             return self._stage1_small(q8, qs, B, QM, probe, K, M, rho, n1, rho_override)
-        # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
-        qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
         l1 = l2 = None
-        if self.SCAN == "cells":
-            list1, lst, nl = self.cell_lists(ccnt1, ccnt)
+        if pairs is not None:             # from route_pairs: pair lists, cell lists, cleared counters
+            qid, coff, ccnt, ccnt1, qcp, slot, list1, lst, nl, cnt = pairs
             l1, l2 = (list1, nl[0:1]), (lst, nl[1:2])
+        else:
+            # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
+            qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
+            if self.SCAN == "cells":
+                cnt = torch.empty(B, dtype=torch.int32, device=dev)            # cleared by the list kernel
+                list1, lst, nl = self.cell_lists(ccnt1, ccnt, cnt)
+                l1, l2 = (list1, nl[0:1]), (lst, nl[1:2])
+            else:
+                cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bmc = torch.empty(qid.numel() * ix.MB, device=dev)   # block-maxima rows addressed by pair position
         self._scan(0, "i8_scan_first", q8, qs, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc, l1)
         t0 = torch.empty(B, device=dev)
         self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), probe.shape[1], n1,
                    ptr(ix.off), B, int(np.ceil(rho * K)), ptr(t0))
-        cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
         self._scan(1, "i8_scan_emit", q8, qs, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None, l2)
@@ -348,19 +384,22 @@ class EngineB200I8:
         B, K = pos.shape
         est = torch.empty(B, K, device=pos.device)
         sd = torch.empty(B, K, device=pos.device)
+        zh = int(Zq.dtype == torch.float16)          # the fp16 product itself, or f32
         if ix.rec is not None:
-            self._call("lut_score", self.L.fvs_lut_score_rec, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D,
+            self._call("lut_score", self.L.fvs_lut_score_rec, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], zh, ix.D,
                        int(half), ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ptr(ix.rec), ix.RB, ix.soff, ix.N,
                        ptr(ncnt), ptr(est), ptr(sd))
         else:
-            self._call("lut_score", self.L.fvs_lut_score_zq, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], ix.D,
+            self._call("lut_score", self.L.fvs_lut_score_zq, ptr(pos), B, K, ptr(QC), ptr(Zq), Zq.shape[1], zh, ix.D,
                        int(half), ix.T, ix._ts_s, ix._ts_e, ix._ts_b, ix._ts_d, ix._ts_p, ptr(ix.scale), ptr(ix.sig),
                        ix.N, ptr(ncnt), ptr(est), ptr(sd))
         return est, sd
 
     def rotated_query(self, Qb, Qh=None):
+        """Zq = fp16(Qb) @ VP16 (`throughput/s2lut.py:122`), kept in fp16: the LUT kernels read the product itself and
+        take the same values as its .float()."""
         Qh = Qb.half() if Qh is None else Qh
-        return (Qh @ self.ix.VP16).float().contiguous()                     # `throughput/s2lut.py:122`
+        return (Qh @ self.ix.VP16).contiguous()
 
     def refine(self, Qb, pos, est, sd, z, k):
         ix = self.ix
@@ -396,9 +435,14 @@ class EngineB200I8:
         if K <= k or K < 10:
             raise ValueError("need K > k and K >= 10 (the delta rule reads the 10th stage-1 estimate)")
         QC, Qh = self.query_prep(Qb)         # one fp16 copy of the queries for the routing and rotation products
-        QM, probe = self.route(Qb, nprobe, Qh)
+        pairs = None
+        if self.fused_routing(len(Qb), nprobe):
+            QM = (Qh @ self.ix.meansN.T).contiguous()
+            probe, pairs = self.route_pairs(QM, nprobe, self.first_pass_cells(K, nprobe))
+        else:
+            QM, probe = self.route(Qb, nprobe, Qh)
         q8, qs = self.quantize(Qb)
-        pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs))
+        pos, ok, est1, ncnt = self.stage1_i8(Qb, QM, probe, K, q8qs=(q8, qs), pairs=pairs)
         fb = None
         if self.FB_INGRAPH and len(Qb) >= self.FB_MIN_BATCH:
             # the recompute of the flagged rows needs only the stage-1 flags: it runs on a second stream, beside the

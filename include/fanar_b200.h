@@ -102,6 +102,20 @@ int fvs_pairs_noalloc(fvs_stream_t stream, const int64_t* probe, int B, int npro
                       const uint16_t* QM, const float* mnorm, int32_t* qid, int32_t* coff, int32_t* ccnt, float* qcp,
                       int32_t* slot);
 
+/*
+ * Routing selection and both pair lists in two launches (replaces fvs_route_topk + fvs_pairs_split + fvs_cell_lists
+ * on the throughput path: the reference's `QM.topk(nprobe)` and `pairs_fast`, `throughput/enginei8.py:11-16, 67-70`).
+ * probe [B, nprobe] as fvs_route_topk; qid / qcp / coff / ccnt / ccnt1 / slot as fvs_pairs_split with first-pass
+ * columns j < n1; when order is given (cells largest first), list1 / list / nlist as fvs_cell_lists.  zero[0..nzero)
+ * is cleared.  work: 2*NC + 1 int32 that are zero before the first call; every call leaves them zero (a call's cursors
+ * are cleared by its last CTA), so calls on one stream can share them.  NC % 8 == 0, NC <= 16384, nprobe <= 512, QM
+ * 16-byte aligned; other shapes return FVS_ERANGE (the three separate entry points take them).
+ */
+int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1, const float* mnorm,
+                    const int32_t* order, int64_t* probe, int32_t* qid, float* qcp, int32_t* coff, int32_t* ccnt,
+                    int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero,
+                    int nzero, int32_t* work);
+
 /* Rows per tile of the int8 scan (a multiple of the reference's 32-row block).  Host-side helper. */
 int fvs_i8_tile_rows(void);
 
@@ -185,13 +199,15 @@ int fvs_lut_score(fvs_stream_t stream, const int64_t* pos, int B, int K, const f
                   const int32_t* ncnt, float* est, float* sd);
 
 /*
- * fvs_lut_score with the table built in shared memory: takes the rotated tier query Zq [B, ldz] f32 (the input of
- * fvs_lut_build) instead of L/qsum/qn2, and computes the same est / sd (same fp16 / f32 table rounding).  Tiers must be
- * contiguous from coordinate 0 with widths multiples of 32 (the reference's 32-dim allocation groups,
- * `src/tiered.py:19-27`).  Replaces `luts_fused` + `score_lut` (`throughput/s2lut.py:92-126`) in one launch.
+ * fvs_lut_score with the table built in shared memory: takes the rotated tier query Zq [B, ldz] (the input of
+ * fvs_lut_build) instead of L/qsum/qn2, and computes the same est / sd (same fp16 / f32 table rounding).  Zq is f32, or
+ * with zq_half = 1 the fp16 product `Qb.half() @ VP16` itself (`throughput/s2lut.py:122` takes its .float(): the same
+ * values, without the conversion pass); ldz % 4 == 0, Zq 16-byte aligned.  Tiers must be contiguous from coordinate 0
+ * with widths multiples of 32 (the reference's 32-dim allocation groups, `src/tiered.py:19-27`).  Replaces
+ * `luts_fused` + `score_lut` (`throughput/s2lut.py:92-126`) in one launch.
  */
-int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq, int ldz,
-                     int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e, const int32_t* tier_bits,
+int fvs_lut_score_zq(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const void* Zq, int ldz,
+                     int zq_half, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e, const int32_t* tier_bits,
                      const float* tier_delta, const uint8_t* const* tier_planes, const uint16_t* scale,
                      const uint16_t* sig, int64_t N, const int32_t* ncnt, float* est, float* sd);
 
@@ -238,9 +254,10 @@ int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8, const flo
  * The work lists of fvs_i8_scan_cells for both passes (new; the reference launches one program per (cell, block)):
  * the cells of `order` [NC] (a permutation of the cells, largest first) with ccnt1[c] > 0 into list1 and with
  * ccnt[c] > 0 into list, in that order; nlist[0], nlist[1] = their lengths (device).  ccnt1 may be NULL (no list1).
+ * zero[0..nzero) is set to 0 in the same launch (the emit pass's per-query counters; zero may be NULL when nzero = 0).
  */
 int fvs_cell_lists(fvs_stream_t stream, const int32_t* order, int NC, const int32_t* ccnt1, const int32_t* ccnt,
-                   int32_t* list1, int32_t* list, int32_t* nlist);
+                   int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero, int nzero);
 
 /*
  * Small-batch int8 scan (B <= 32): same contract and arithmetic as fvs_i8_scan_tc, streamed from HBM with 16-byte loads
@@ -330,8 +347,8 @@ int fvs_rth_largest(fvs_stream_t stream, const float* vals, int B, int n, int64_
  * toff[t] + p * KB_t, then fp16 (scale, sigma) per tier at soff + 4t, RB a multiple of 16 (64 in the reference).  One
  * coalesced row read per candidate; same arithmetic and results as fvs_lut_score_zq.
  */
-int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const float* Zq,
-                      int ldz, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e,
+int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B, int K, const float* qc, const void* Zq,
+                      int ldz, int zq_half, int D, int half, int T, const int32_t* tier_s, const int32_t* tier_e,
                       const int32_t* tier_bits, const float* tier_delta, const uint8_t* rec, int RB, int soff,
                       int64_t N, const int32_t* ncnt, float* est, float* sd);
 

@@ -141,7 +141,7 @@ def test_dense_engine_end_to_end(dm):
     oi = ge.oracle_index(s1, i8, codes["uniform"], X16)
     code = oi["code"]
     TS = code["TS"]
-    Zq = c(e["Zq"])
+    Zq = c(e["Zq"]).astype(np.float32)         # the fp16 product, taken as its .float()
     QC = c((Q @ ix.c).contiguous())
     Lt = O.lut_build(Zq, half=E.LUTH)
     qsum, qn2 = O.tier_sums(Zq, TS)

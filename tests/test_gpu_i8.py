@@ -386,6 +386,76 @@ def test_pairs_split(eng, n1):
     np.testing.assert_array_equal(gqc[gs], want)
 
 
+@pytest.mark.parametrize("B,NC,npr,n1", [(300, 4096, 72, 13), (37, 8192, 256, 30), (1000, 16384, 512, 1),
+                                          (64, 8, 8, 8), (513, 4096, 352, 23)])
+def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1):
+    """fvs_route_pairs (routing selection + both pair lists + cell lists in two launches) gives the probe list of
+    fvs_route_topk, the pair layout of fvs_pairs_split and the lists of fvs_cell_lists, also through tied scores; its
+    cursors are left zero, so a second call on the same work buffer gives the same result."""
+    L = pkg("_lib")
+    lib = L.lib()
+    rng = np.random.default_rng(B + NC)
+    QM = (rng.integers(-300, 300, (B, NC)) / 512).astype(np.float16)        # many ties
+    mnorm = (rng.random(NC) + 0.5).astype(np.float32)
+    order = np.argsort(-rng.integers(0, 50, NC), kind="stable").astype(np.int32)
+    tq, tm, to = (torch.from_numpy(x).to(DEV) for x in (QM, mnorm, order))
+    work = torch.zeros(2 * NC + 1, dtype=torch.int32, device=DEV)
+    outs = []
+    for _ in range(2):
+        probe = torch.empty(B, npr, dtype=torch.int64, device=DEV)
+        qid = torch.empty(B * npr, dtype=torch.int32, device=DEV)
+        qcp = torch.empty(B * npr, device=DEV)
+        coff, ccnt, ccnt1, l1, l2 = (torch.empty(NC, dtype=torch.int32, device=DEV) for _ in range(5))
+        slot = torch.empty(B * n1, dtype=torch.int32, device=DEV)
+        nl = torch.empty(2, dtype=torch.int32, device=DEV)
+        zero = torch.ones(B, dtype=torch.int32, device=DEV)
+        L.check(lib.fvs_route_pairs(L.stream_handle(), L.ptr(tq), B, NC, npr, n1, L.ptr(tm), L.ptr(to), L.ptr(probe),
+                                    L.ptr(qid), L.ptr(qcp), L.ptr(coff), L.ptr(ccnt), L.ptr(ccnt1), L.ptr(slot),
+                                    L.ptr(l1), L.ptr(l2), L.ptr(nl), L.ptr(zero), B, L.ptr(work)), "route_pairs")
+        torch.cuda.synchronize()
+        assert int(work.abs().sum()) == 0 and int(zero.abs().sum()) == 0
+        outs.append([c(x) for x in (probe, qid, qcp, coff, ccnt, ccnt1, slot, l1, l2, nl)])
+    for i in (0, 3, 4, 5, 9):                            # everything but the within-cell order of the pairs
+        np.testing.assert_array_equal(outs[0][i], outs[1][i])
+    for i, j in ((7, 0), (8, 1)):                        # the lists up to their lengths
+        np.testing.assert_array_equal(outs[0][i][:outs[0][9][j]], outs[1][i][:outs[1][9][j]])
+    probe, qid, qcp, coff, ccnt, ccnt1, slot, l1, l2, nl = outs[0]
+    # routing: the separate kernel's probe list
+    p2 = torch.empty(B, npr, dtype=torch.int64, device=DEV)
+    L.check(lib.fvs_route_topk(L.stream_handle(), L.ptr(tq), B, NC, npr, L.ptr(p2)), "route")
+    np.testing.assert_array_equal(probe, c(p2))
+    # pairs: counts and offsets exact, each cell's first-pass and other segments equal as sets, slots and constants
+    oq, oc, on, _, _ = O.pairs(probe, NC, QM, mnorm)
+    oq1, oc1, on1, _, _ = O.pairs(probe[:, :n1], NC, QM, mnorm)
+    np.testing.assert_array_equal(coff, oc)
+    np.testing.assert_array_equal(ccnt, on)
+    np.testing.assert_array_equal(ccnt1, on1)
+    for cc in range(0, NC, max(1, NC // 500)):
+        a, m, e = oc[cc], oc[cc] + on1[cc], oc[cc] + on[cc]
+        np.testing.assert_array_equal(np.sort(qid[a:m]), np.sort(oq1[oc1[cc]:oc1[cc] + on1[cc]]))
+        np.testing.assert_array_equal(np.sort(qid[a:e]), np.sort(oq[a:e]))
+    qq = np.repeat(np.arange(B), n1)
+    jj = np.tile(np.arange(n1), B)
+    np.testing.assert_array_equal(qid[slot], qq)
+    cells = probe[qq, jj]
+    assert ((slot >= oc[cells]) & (slot < oc[cells] + on1[cells])).all()
+    qa = np.repeat(np.arange(B), npr)
+    pc = probe.ravel()
+    want = (QM[qa, pc].astype(np.float32) * mnorm[pc]).astype(np.float32)
+    got = np.zeros(B * npr, np.float32)
+    # the constant of every pair sits at the pair's position: match by (query, cell) through the slots' layout
+    pos_of = {}
+    for cc in range(NC):
+        for pos in range(oc[cc], oc[cc] + on[cc]):
+            pos_of[(int(qid[pos]), cc)] = pos
+    got = np.array([qcp[pos_of[(int(q), int(cc))]] for q, cc in zip(qa, pc)], np.float32)
+    np.testing.assert_array_equal(got, want)
+    # cell lists: the cells of `order` with pairs
+    np.testing.assert_array_equal(nl, [int((on1[order] > 0).sum()), int((on[order] > 0).sum())])
+    np.testing.assert_array_equal(l1[:nl[0]], order[on1[order] > 0])
+    np.testing.assert_array_equal(l2[:nl[1]], order[on[order] > 0])
+
+
 def test_quantize_matches_reference_formula(eng):
     """the quantisation kernel equals the reference's torch expression on the same projected queries."""
     L = pkg("_lib")
