@@ -42,6 +42,7 @@ GRID = [(64, 90, 8192, 0.65, 16), (72, 100, 8192, 0.65, 8), (72, 100, 8192, 0.65
 
 # (nprobe, K, M, rho) of the reference arm under --op auto: the point the B200 arm's grid selects on the bench data
 REFERENCE_ARM_OP = (72, 100, 8192, 0.65)
+REFERENCE_ARM_OP5 = (144, 100, 8192, 0.65)     # the sharded configuration's 2M-row shards (8192 cells)
 
 
 def pkg(name):
@@ -140,11 +141,15 @@ def timed(fn, reps):
     return a.elapsed_time(b) / reps
 
 
-def choose_op(args, E, search, Q, gt, world):
+def synth_nlist(rows):
+    return pkg("synth").default_nlist(rows)
+
+
+def choose_op(args, E, search, Q, gt, world, grid=GRID):
     """fastest grid point with recall@10 >= 0.99 (same decision on every rank)."""
     synth = pkg("synth")
     best, rows = None, []
-    for npr, K, M, rho, fb in GRID:
+    for npr, K, M, rho, fb in grid:
         set_knobs(E, M, rho, fb)
         I = search(Q, K, args.z, npr, 10)
         rec = synth.recall(I.cpu(), gt.cpu(), 10)
@@ -159,7 +164,7 @@ def choose_op(args, E, search, Q, gt, world):
             best = (npr, K, M, ms, rec, rho, fb)
     log("operating points:", json.dumps(rows))
     if best is None:
-        npr, K, M, rho, fb = GRID[-1]
+        npr, K, M, rho, fb = grid[-1]
         best = (npr, K, M, None, rows[-1]["recall"], rho, fb)
     return best, rows
 
@@ -427,6 +432,18 @@ def variant_trellis(args, dev, steps=20):
         r = rows[-1]
         best = (r["nprobe"], r["K"], r["recall"], r["ms"])
     npr, K, rec, ms = best
+    # k = 100 (`src/v19_final.py:58` grid), recall@100 against exact top-100
+    gt100 = synth.brute_force_topk(X16, Q, 100)
+    rows100 = []
+    for npr2, K2 in ((512, 1000), (768, 1000), (1024, 1500), (1536, 1500), (1536, 2000), (2048, 2000), (3072, 3000)):
+        I = E.search(Q, K2, z, npr2, 100)[0]
+        rec100 = synth.recall(I.long().cpu(), gt100.cpu(), 100)
+        ms2 = _steps_ms(lambda: E.search(Q, K2, z, npr2, 100), 5)
+        rows100.append(dict(nprobe=npr2, K=K2, recall_at_100=round(rec100, 4), ms=round(ms2, 3),
+                            qps=round(len(Q) / ms2 * 1e3, 1)))
+        log("trellis k100", json.dumps(rows100[-1]))
+        if rec100 >= 0.99:
+            break
     E.timing = {}
     for _ in range(3):
         E.search_eager(Q, K, z, npr, k)
@@ -443,7 +460,190 @@ def variant_trellis(args, dev, steps=20):
                       f"stage 1 + tiered gather), NC={nlist}, batch {len(Q)}, k=10, z={z}",
             "value": round(len(Q) / (ms * 1e-3), 1), "unit": "queries/s", "nprobe": npr, "K": K, "M": Mbuf,
             "recall@10": round(rec, 4), "ms_per_step": round(ms, 4), "grid": rows, "build_s": round(build_s, 1),
-            "kernel_ms": {n: round(v, 4) for n, v in kt.items()}, "flagged_last_batch": flags}
+            "kernel_ms": {n: round(v, 4) for n, v in kt.items()}, "flagged_last_batch": flags, "k100": rows100}
+
+
+def _timed_search(fn, steps=10):
+    for _ in range(3):
+        fn()
+    return timed(fn, steps)
+
+
+def _recall_at(I, gt, k):
+    return pkg("synth").recall(I.long().cpu(), gt.cpu(), k)
+
+
+def variant_batches(args, E, ds, gt, op):
+    """Config 3 at its other sizes: batch 500 and 1000 at the headline operating point (k=10), and batch 2000 with
+    k=100 (K 1000-3000, beta 0.7: `throughput/e_v3final.py:28-32`, grid of `src/v19_final.py:58`) at the first point
+    of the reference's k=100 grid that reaches recall@100 >= 0.99 against exact top-100."""
+    synth = pkg("synth")
+    npr, K, M, rho, fb = op
+    z = args.z
+    Q = ds["queries"]
+    out = {"config": f"{args.rows // 1000}k x {args.dim} fp16, throughput mode", "k10": [], "k100": []}
+    for B in (500, 1000):
+        I = torch.cat([E.search(Q[i:i + B].contiguous(), K, z, npr, 10)[0] for i in range(0, len(Q), B)])
+        ms = _timed_search(lambda: E.search(Q[:B].contiguous(), K, z, npr, 10))
+        out["k10"].append(dict(batch=B, nprobe=npr, K=K, M=M, rho=rho, recall=round(_recall_at(I, gt, 10), 4),
+                               ms=round(ms, 4), qps=round(B / ms * 1e3, 1)))
+    gt100 = synth.brute_force_topk(ds["base16"], Q, 100)
+    msz, fbs = E.MSZ, E.FB_INGRAPH
+    E.MSZ = None                                    # M = max(4096, 16 K), the reference's buffer rule
+    try:
+        for npr2, K2 in ((512, 1000), (768, 1000), (1024, 1500), (1536, 1500), (1536, 2000), (2048, 2000)):
+            if npr2 > E.ix.NC:
+                continue
+            I = E.search(Q, K2, z, npr2, 100)[0]
+            rec100 = _recall_at(I, gt100, 100)
+            ms = _timed_search(lambda: E.search(Q, K2, z, npr2, 100), 5)
+            out["k100"].append(dict(batch=len(Q), nprobe=npr2, K=K2, M=max(4096, 16 * K2), rho=rho,
+                                    recall_at_100=round(rec100, 4), recall_at_10=round(_recall_at(I, gt, 10), 4),
+                                    ms=round(ms, 4), qps=round(len(Q) / ms * 1e3, 1)))
+            log("batches k100", json.dumps(out["k100"][-1]))
+            if rec100 >= 0.99:
+                break
+    finally:
+        E.MSZ, E.FB_INGRAPH = msz, fbs
+    return out
+
+
+def _trellis_oracle_index(s1, code, X16):
+    t = lambda x: x.detach().cpu().numpy() if torch.is_tensor(x) else np.asarray(x)
+    oc = dict(TS=code["TS"], planes=[t(p) for p in code["planes"]], cbf=[t(x) for x in code["cbf"]],
+              scale=t(code["scale"]), sig=t(code["sig"]), VP=t(code["VP"]))
+    return dict(off=np.asarray(s1["off"], np.int64), order=t(s1["order"]), means16=t(s1["means16"]),
+                inv_mnorm=t(s1["inv_mnorm"]), c=t(s1["c"]), W1=t(s1["W1"]), tab=t(s1["tab"]), words=t(s1["words"]),
+                scale1=t(s1["scale1"]), H16=t(X16), code=oc)
+
+
+def _default_engine(X16, nlist, bits):
+    """the reference's default index (cells, Lloyd-Max tiered code, trellis stage-1 code) and its engine"""
+    ib, ec = pkg("index_build"), pkg("engine_cell")
+    s1, _, codes = ib.build_index(X16, nlist, R=256, refine_bits=bits, seed=0, uniform=False, lloyd=True)
+    s1.update(ib.build_trellis(X16, s1, seed=0))
+    ix = ec.IndexS(s1, codes["lloyd"], X16, X16.device)
+    return s1, codes["lloyd"], ix, ec.EngineB200S(ix)
+
+
+def variant_latency(args, ds, gt):
+    """Config 2: the default engine (trellis stage 1, tiered gather) on the 1M x 1536 set, latency mode at batch 1 and
+    32 (`EngineT.search_host`: one graph replay, ids to pinned host memory), z in {1.5, 2, 2.5, 3}, at the (nprobe, K)
+    points of `src/v19_final.py:53` / `src/v21_lat.py:9`; recall@10 over the queries of the run, p50/p99 per search."""
+    t0 = time.time()
+    s1, code, ix, E = _default_engine(ds["base16"], pkg("synth").default_nlist(len(ds["base16"])), int(2.5 * args.dim))
+    build_s = time.time() - t0
+    Q = ds["queries"]
+    rows = []
+    for npr, K in ((256, 200), (384, 200), (384, 400), (512, 400), (768, 400)):
+        for z in (1.5, 2.0, 2.5, 3.0):
+            for B, nrec in ((1, 400), (32, 2000)):
+                n = nrec // B * B
+                I = np.vstack([E.search_host(Q[i:i + B].contiguous(), K, z, npr, 10) for i in range(0, n, B)])
+                rec = pkg("synth").recall(torch.from_numpy(I).long(), gt[:n].cpu(), 10)
+                ts = []
+                for i in range(70):
+                    qb = Q[(i * B) % (len(Q) - B):][:B].contiguous()
+                    torch.cuda.synchronize()
+                    a = time.perf_counter()
+                    E.search_host(qb, K, z, npr, 10)
+                    ts.append((time.perf_counter() - a) * 1e3)
+                ts = np.array(ts[10:])
+                rows.append(dict(nprobe=npr, K=K, z=z, batch=B, recall=round(rec, 4),
+                                 p50_ms=round(float(np.median(ts)), 4), p99_ms=round(float(np.percentile(ts, 99)), 4),
+                                 qps=round(B / float(np.median(ts)) * 1e3, 1)))
+    best1 = min((r for r in rows if r["batch"] == 1 and r["recall"] >= 0.99), key=lambda r: r["p50_ms"], default=None)
+    best32 = min((r for r in rows if r["batch"] == 32 and r["recall"] >= 0.99), key=lambda r: r["p50_ms"],
+                 default=None)
+    del E, ix
+    torch.cuda.empty_cache()
+    return {"config": f"{len(Q)} queries on {len(ds['base16']) // 1000}k x {args.dim} fp16, default engine (trellis "
+                      f"stage 1 + tiered gather), latency mode (one search per call, ids to host)",
+            "build_s": round(build_s, 1), "best_batch1_at_recall_0.99": best1, "best_batch32_at_recall_0.99": best32,
+            "grid": rows}
+
+
+def variant_c1(args, dev):
+    """Config 1: 100k x 768 (256 components), 1000 queries, k=10, batch 1000, the reference's default index
+    (NC=512, 1920 refinement bits, `src/v19_final.py:18-19`) and engine; the fastest point of a small (nprobe, K) grid
+    reaching recall@10 >= 0.99, then the whole run through the CPU oracle of the same engine on the host cores."""
+    synth = pkg("synth")
+    from oracle import fvs_oracle as O
+    ds = synth.make_dataset(synth.CONFIGS["c1_100k_768"], dev, gt_k=10)
+    s1, code, ix, E = _default_engine(ds["base16"], 512, 1920)
+    Q, gt = ds["queries"], ds["gt"]
+    z, best, grid = 2.0, None, []
+    for npr, K in ((32, 100), (64, 100), (64, 200), (128, 200), (128, 400), (256, 400)):
+        I = E.search(Q, K, z, npr, 10)[0]
+        rec = _recall_at(I, gt, 10)
+        ms = _timed_search(lambda: E.search(Q, K, z, npr, 10))
+        grid.append(dict(nprobe=npr, K=K, recall=round(rec, 4), ms=round(ms, 4)))
+        if rec >= 0.99 and (best is None or ms < best[3]):
+            best = (npr, K, rec, ms)
+    if best is None:
+        best = (grid[-1]["nprobe"], grid[-1]["K"], grid[-1]["recall"], grid[-1]["ms"])
+    npr, K, rec, ms = best
+    I = E.search(Q, K, z, npr, 10)[0].cpu().numpy()
+    oi = _trellis_oracle_index(s1, code, ds["base16"])
+    Qc = Q.cpu().numpy()
+    # the whole run when it fits about a minute of host time (projected from the first 50 queries), else a sample
+    t = time.perf_counter()
+    o50 = O.search_trellis(oi, Qc[:50], K, z, npr, 10)
+    per_q = (time.perf_counter() - t) / 50
+    nq = len(Qc) if per_q * len(Qc) <= 90 else max(50, int(60 / per_q))
+    t = time.perf_counter()
+    o = O.search_trellis(oi, Qc[:nq], K, z, npr, 10) if nq > 50 else o50
+    cpu_s = time.perf_counter() - t if nq > 50 else per_q * 50
+    I, gt = I[:nq], gt[:nq]
+    rec_cpu = synth.recall(torch.from_numpy(o["I"]).long(), gt.cpu(), 10)
+    out = {"config": "100k x 768 fp16 (256 comps), default engine, NC=512, 1920 bits, batch 1000, k=10, z=2.0",
+           "nprobe": npr, "K": K, "recall@10": round(rec, 4), "ms_per_step": round(ms, 4),
+           "value": round(len(Q) / ms * 1e3, 1), "unit": "queries/s", "grid": grid,
+           "cpu_full_run": {"queries": nq, "seconds": round(cpu_s, 2), "value": round(nq / cpu_s, 2),
+                            "unit": "queries/s", "cores": oracle_threads(), "recall@10": round(rec_cpu, 4),
+                            "kind": "port (numpy oracle of the default engine, its own products)",
+                            "rows_with_ids_equal_to_gpu": int((o["I"] == I).all(1).sum())}}
+    del E, ix
+    torch.cuda.empty_cache()
+    return out
+
+
+# operating points of the sharded configuration (8192 cells per 2M-row shard: about twice the headline's nprobe)
+GRID5 = [(144, 100, 8192, 0.65, 8), (192, 150, 8192, 0.65, 16), (256, 200, 8192, 0.65, 16),
+         (288, 250, 8192, 0.65, 16), (352, 300, 8192, 0.65, 16), (512, 400, 8192, 0.65, 16)]
+
+
+def variant_c5(args, dev):
+    """Config 5's shard on one GPU: 2M x 1536 (4096 components), NC=8192, batch 2000, k=10; QPS per-row-normalised
+    (x 2M / 1M), the 1-GPU point of the sharded configuration."""
+    synth, ib, eng = pkg("synth"), pkg("index_build"), pkg("engine")
+    t0 = time.time()
+    ds = synth.make_dataset(synth.CONFIGS["c5_shard_2m_1536"], dev, gt_k=10)
+    s1, i8, codes = ib.build_index(ds["base16"], 8192, R=256, seed=0)
+    ix = eng.IndexI8(s1, i8, codes["uniform"], ds["base16"], dev)
+    E = eng.EngineB200I8(ix)
+    build_s = time.time() - t0
+    Q, gt = ds["queries"], ds["gt"]
+    best, grid = None, []
+    for npr, K, M, rho, fb in GRID5:
+        set_knobs(E, M, rho, fb)
+        I = E.search(Q, K, args.z, npr, 10)[0]
+        rec = _recall_at(I, gt, 10)
+        ms = _timed_search(lambda: E.search(Q, K, args.z, npr, 10))
+        grid.append(dict(nprobe=npr, K=K, M=M, rho=rho, fb=fb, recall=round(rec, 4), ms=round(ms, 4)))
+        if rec >= 0.99 and (best is None or ms < best[3]):
+            best = (npr, K, rec, ms)
+            break
+    if best is None:
+        best = (grid[-1]["nprobe"], grid[-1]["K"], grid[-1]["recall"], grid[-1]["ms"])
+    npr, K, rec, ms = best
+    del E, ix, ds
+    torch.cuda.empty_cache()
+    return {"config": "2M x 1536 fp16 (4096 comps), NC=8192, throughput mode, batch 2000, k=10 (one shard of the "
+                      "16M sharded configuration)", "nprobe": npr, "K": K, "recall@10": round(rec, 4),
+            "ms_per_step": round(ms, 4), "qps": round(2000 / ms * 1e3, 1),
+            "value": round(2000 / ms * 1e3 * 2.0, 1), "unit": "queries/s x (rows / 1M)", "grid": grid,
+            "build_s": round(build_s, 1)}
 
 
 # ---------------------------------------------------------------------------------------------------- main
@@ -454,21 +654,28 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--batch", type=int, default=2000)
-    ap.add_argument("--rows", type=int, default=1_000_000)
+    ap.add_argument("--rows", type=int, default=None,
+                    help="database rows per GPU (default: 1M on one GPU, config 3; 2M per GPU on several, config 5)")
     ap.add_argument("--dim", type=int, default=1536)
-    ap.add_argument("--comps", type=int, default=1024)
+    ap.add_argument("--comps", type=int, default=None, help="mixture components (default 1024; 4096 on several GPUs)")
     ap.add_argument("--z", type=float, default=1.25)
     ap.add_argument("--op", default="auto", help="nprobe:K:M[:rho[:in-graph rows]] or auto")
     ap.add_argument("--cpu-sample", type=int, default=48)
-    ap.add_argument("--variants", default="dense,trellis",
-                    help="comma list of extra measurements at N=1: dense (routing-free int8), trellis (default "
-                         "engine), or none")
+    ap.add_argument("--variants", default="dense,trellis,batches,latency,c1,c5",
+                    help="comma list of extra measurements at N=1: dense (routing-free int8, config 3 literal), "
+                         "trellis (default engine, config 4), batches (config 3 at batch 500/1000 and k=100), latency "
+                         "(config 2), c1 (config 1 with its CPU run), c5 (one 2M-row shard of config 5), or none")
     ap.add_argument("--trellis-rows", type=int, default=2_250_000, help="rows of the default-engine dataset")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local = int(os.environ.get("LOCAL_RANK", 0))
+    # one GPU: config 3 (1M x 1536, 1024 components); several: config 5 (2M rows and 8192 cells per GPU, 4096 comps)
+    if args.rows is None:
+        args.rows = 1_000_000 if world == 1 else 2_000_000
+    if args.comps is None:
+        args.comps = 1024 if world == 1 else 4096
     if args.impl == "reference":
         return reference_arm(args, rank, world, local)
     torch.cuda.set_device(local)
@@ -482,7 +689,8 @@ def main():
     Q0 = ds["queries"]
     Qs = [Q0] + [pkg("synth").extra_queries(ds, args.batch, 100 + i) for i in range(3)]
     if args.op == "auto":
-        (npr, K, M, _, rec, rho, fb), grid_rows = choose_op(args, E, search, Q0, gt, world)
+        grid = GRID if synth_nlist(args.rows) <= 4096 else GRID5
+        (npr, K, M, _, rec, rho, fb), grid_rows = choose_op(args, E, search, Q0, gt, world, grid)
     else:
         f = args.op.split(":")
         npr, K, M = (int(x) for x in f[:3])
@@ -519,10 +727,30 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     ms = ms_rank
+    rank_ms = exchange = None
     if world > 1:
         t = torch.tensor([ms_rank], device=dev)
+        tl = [torch.empty_like(t) for _ in range(world)]
+        torch.distributed.all_gather(tl, t)
+        rank_ms = [round(float(x), 4) for x in tl]
+        ms = max(float(x) for x in tl)
+        # the exchange alone (exact scores of the local winners, all-gather, merge), eager, CUDA events on this stream
+        S = E.sharded
+        Il = E.search_eager(Q0, K, z, npr, k)["I"]
+        for _ in range(3):
+            S._exchange(Q0, Il, k)
+        torch.distributed.barrier()
+        a2, b2 = torch.cuda.Event(True), torch.cuda.Event(True)
+        a2.record()
+        for _ in range(10):
+            S._exchange(Q0, Il, k)
+        b2.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a2.elapsed_time(b2) / 10], device=dev)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t)
+        exchange = {"ms": round(float(t), 4), "share_of_step": round(float(t) / ms, 4),
+                    "what": "exact scores of the local top-k, NCCL all-gather of [B, k] records, merge (eager, max "
+                            "over ranks)"}
     scale_rows = world * args.rows / 1e6
     value = args.batch / (ms / 1e3) * scale_rows
     # ---- end to end through the public API: pinned host queries in, host ids out, every step
@@ -646,8 +874,12 @@ def main():
     want = set(v.strip() for v in args.variants.split(",")) - {"none", ""}
     if rank == 0 and world == 1 and want:
         variants = {}
-        todo = [("dense", "dense_int8_routing_free", lambda: variant_dense(args, ds, s1, ix, gt, dev)),
-                ("trellis", "default_engine_trellis", lambda: variant_trellis(args, dev))]
+        todo = [("batches", "config3_batches_and_k100", lambda: variant_batches(args, E, ds, gt, (npr, K, M, rho, fb))),
+                ("dense", "dense_int8_routing_free", lambda: variant_dense(args, ds, s1, ix, gt, dev)),
+                ("latency", "config2_latency_default_engine", lambda: variant_latency(args, ds, gt)),
+                ("trellis", "default_engine_trellis", lambda: variant_trellis(args, dev)),
+                ("c1", "config1_100k_768", lambda: variant_c1(args, dev)),
+                ("c5", "config5_shard_2m", lambda: variant_c5(args, dev))]
         for key, name, fn in todo:
             if key not in want:
                 continue
@@ -673,6 +905,9 @@ def main():
                            "batch32_p50_ms": round(lat32[len(lat32) // 2], 4) if lat32 else None,
                            "operating_points": grid_rows},
                 "clocks": clocks, "e2e": e2e, "gpu_launches": int(launches), "roofline": roof, "cpu_baseline": cpu}
+        if rank_ms:
+            line["rank_ms_per_step"] = rank_ms
+            line["exchange"] = exchange
         if parity:
             line["parity"] = parity
         if variants:
@@ -699,7 +934,7 @@ def reference_arm(args, rank, world, local):
     s1, i8, codes = ib.build_index(ds["base16"], synth.default_nlist(args.rows), R=256, seed=0)
     oi = oracle_index_cpu(s1, i8, codes["uniform"], ds["base16"])
     if args.op == "auto":       # the operating point the B200 arm's grid selects on this data (recall@10 0.991)
-        npr, K, M, rho = REFERENCE_ARM_OP
+        npr, K, M, rho = REFERENCE_ARM_OP if synth.default_nlist(args.rows) <= 4096 else REFERENCE_ARM_OP5
     else:
         f = args.op.split(":")
         npr, K, M = (int(x) for x in f[:3])
