@@ -313,7 +313,8 @@ class EngineB200I8:
         self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
                    ptr(ok), ptr(ncnt), float(self.DELTA or 0.0), 9)
         self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, q8=q8, qs=qs, ccnt=ccnt, ccnt1=ccnt1,
-                          npairs=int(qid.numel()), bval=bval, bpos=bpos, slot=slot, ncnt=ncnt)
+                          npairs=int(qid.numel()), bval=bval, bpos=bpos, slot=slot, ncnt=ncnt,
+                          scan_args=(qid, coff, qcp, l1, l2))
         return pos, ok.view(torch.bool), est1, ncnt
 
     def _ident(self, n):
