@@ -492,13 +492,26 @@ def variant_trellis(args, dev, steps=20):
     flags = {"underflow": int((cnt < K).sum()), "overflow": int((cnt > E._last["M"]).sum()),
              "cnt_median": int(cnt.float().median())}
     Mbuf = E.M
+    # the same operating point on the mma.sync tile scan (the baseline the tcgen05 cell-major scan replaces)
+    E.SCAN = "mma"
+    ms_mma = _steps_ms(lambda: E.search(Q, K, z, npr, k), steps)
+    E.timing = {}
+    for _ in range(3):
+        E.search_eager(Q, K, z, npr, k)
+    torch.cuda.synchronize()
+    kt_mma = {n: round(float(np.mean([a.elapsed_time(b) for a, b in v])), 4) for n, v in E.timing.items()
+              if n.startswith("trellis_scan")}
+    E.timing = None
+    E.SCAN = "cells"
     del ds, X16, ix, E
     torch.cuda.empty_cache()
     return {"config": f"{args.trellis_rows / 1e6:g}M x 768 fp16 (2048 comps, spectrum 1.0), default engine (trellis "
                       f"stage 1 + tiered gather), NC={nlist}, batch {len(Q)}, k=10, z={z}",
             "value": round(len(Q) / (ms * 1e-3), 1), "unit": "queries/s", "nprobe": npr, "K": K, "M": Mbuf,
             "recall@10": round(rec, 4), "ms_per_step": round(ms, 4), "grid": rows, "build_s": round(build_s, 1),
-            "kernel_ms": {n: round(v, 4) for n, v in kt.items()}, "flagged_last_batch": flags, "k100": rows100}
+            "kernel_ms": {n: round(v, 4) for n, v in kt.items()}, "flagged_last_batch": flags, "k100": rows100,
+            "mma_scan_baseline": {"ms_per_step": round(ms_mma, 4), "qps": round(len(Q) / (ms_mma * 1e-3), 1),
+                                  "kernel_ms": kt_mma}}
 
 
 def _timed_search(fn, steps=10):

@@ -45,6 +45,8 @@ SIGNATURES = {
     "fvs_trellis_tile_rows": (I32, []),
     "fvs_trellis_scan": (I32, [P, I32, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I32, P, I32, P, P, P, P, P,
                                 I32, P, I32]),
+    "fvs_trellis_scan_cells": (I32, [P, I32, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I32, P, I32, P, P, P, P,
+                                      P, I32, P, I32, P, P]),
     "fvs_trellis_scan_small": (I32, [P, I32, P, I32, I32, P, I32, I32, P, I32, P, P, I32, P, I32, P, P, P, P, P, I32, P,
                                       I32, I32]),
     "fvs_tiered_score": (I32, [P, P, I32, I32, P, P, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P]),

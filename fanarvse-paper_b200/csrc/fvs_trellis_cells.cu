@@ -1,0 +1,707 @@
+// Default-engine stage-1 scan (cell-residual trellis code) on the 5th-generation tensor cores (tcgen05, sm_100a),
+// cell-major.
+//
+// Same contract and arithmetic as fvs_trellis_scan modes 0 / 1 (the reference's `_first_compact_s` / `_emit_loop_s`
+// with the decoder `_decode_tile2`, `src/s1cell.py:121-154`, `src/decode2.py:5-17`):
+//   value_j = fp16(tab[state_j]),  state_j = ((w[j/32] << 32 | w[j/32+1]) >> (64 - L - j%32)) & (2^L - 1),
+//   est = scale1[n] * dot(fp16 q', value) + qcp   (dot accumulated in fp32, product and sum rounded separately),
+// then block maxima per 32-row block (mode 0, first pass) or the threshold emit est >= t0[q] (mode 1).
+// The work is organised like fvs_i8_scan_cells: cells handed out dynamically (largest first), a cell's queries (groups
+// of up to RSUB sub-tiles of QN) gathered once and held while its 128-row tiles pass, TMEM accumulators in a ring,
+// three epilogue warpgroups.  The code tile is not copied but decoded in the CTA: each decode lane owns one tile row,
+// reads its row's words (prefetched one tile ahead) and writes the row's 256 fp16 values, two per lookup of a table of
+// fp16 value pairs indexed by (L+1)-bit windows, straight into the canonical K-major 128 B-swizzled layout the MMA
+// reads.  The tile is decoded and consumed in K-chunks of 64 values through a ring of AC chunk slots, so the decode of
+// the next tile's first chunks overlaps the MMAs on the last chunks of the current one.
+// Warp roles (640 threads):
+//   warps 0-3   : decode (warp w: tile rows 32w..32w+31); lane 0 of warp 0 also takes cells (atomicAdd on sched[0])
+//                 and publishes the work items one ahead, like the producer of fvs_i8_scan_cells
+//   warp 4      : TMEM allocation; lane 0 issues tcgen05.mma.kind::f16 (M=128 rows, N=16..64 queries, K=16) per
+//                 chunk and sub-tile, commits a chunk slot once its MMAs are done and a sub-tile's accumulator after
+//                 its last chunk
+//   warps 5-6   : gather: fp16 query rows picked by qid into the swizzled layout; column metadata (qid, pair constant,
+//                 threshold) into one of MS slots
+//   warp 7      : idle (the epilogue warpgroups start on a TMEM lane-quarter boundary)
+//   warps 8-19  : three epilogue warpgroups, units alternating between them
+// The last CTA to finish resets sched[0..1].  Every mbarrier wait is bounded; on expiry the CTA raises `status`,
+// drains the MMAs it issued, frees TMEM and returns.
+#include <cuda.h>
+
+#include "fvs_common.cuh"
+#include "fvs_tcgen05.cuh"
+
+namespace fvs {
+namespace tcells {
+using namespace fvs::tcg;
+
+constexpr int TILE_ROWS = 128;
+constexpr int QN = 64;      // queries per sub-tile
+constexpr int R = 256;      // decoded values per row
+constexpr int KCH = 4;      // K-chunks of 64 fp16 values (128 B per row) per tile
+constexpr int NWORDS = R / 32 + 1;
+constexpr int AC = 5;       // chunk slots
+constexpr int B_STAGES = 4;
+constexpr int RSUB = 2;     // sub-tiles of one work item (held through the item's tiles)
+constexpr int T_STAGES = 8;
+constexpr int I_STAGES = 8;
+constexpr int MS = 8;       // column-metadata slots (one per sub-tile, held until the sub-tile's last unit is done)
+constexpr int EPI_GROUPS = 3;
+constexpr int GATHER_WARPS = 2;
+constexpr int DEC_WARPS = 4;
+constexpr int MAX_L = 10;
+constexpr int W_DEC = 0, W_MMA = W_DEC + DEC_WARPS, W_GATHER = W_MMA + 1, W_EPI = 8;
+constexpr int NWARPS = W_EPI + 4 * EPI_GROUPS;
+constexpr int NTHREADS = 32 * NWARPS;
+constexpr uint32_t TMEM_COLS = T_STAGES * QN;
+static_assert(B_STAGES >= 2 * RSUB, "a work item's sub-tiles and the next item's fit together");
+static_assert(W_EPI % 4 == 0 && W_EPI >= W_GATHER + GATHER_WARPS, "epilogue warpgroups start on a TMEM lane quarter");
+static_assert(DEC_WARPS * 32 == TILE_ROWS, "one decode lane per tile row");
+
+struct Item {
+    int cell, cs, ce, first, ntiles, qoff, nq, nsub;  // nsub == 0: no more work
+};
+
+// shared-memory carve-up (offsets from a 1024-byte aligned base)
+constexpr int CH_BYTES = TILE_ROWS * 128;  // one K-chunk of a decoded tile
+constexpr int B_BYTES = KCH * QN * 128;    // one query sub-tile: 4 K-chunks x 8 KB
+constexpr int A_OFF = 0;
+constexpr int B_OFF = A_OFF + AC * CH_BYTES;
+constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;  // per sub-tile slot: qid, qcp, t0 of QN columns
+constexpr int META_W = 3 * QN * 4;
+constexpr int COL_OFF = META_OFF + MS * META_W;               // per epilogue warp: 32 column masks + 32 bases
+constexpr int MCNT_OFF = COL_OFF + 4 * EPI_GROUPS * 64 * 4;   // per metadata slot: epilogue warps done with it
+constexpr int TAB_OFF = MCNT_OFF + MS * 4;                    // pair table: 2^(L+1) fp16 value pairs
+constexpr int ITEM_OFF = TAB_OFF + (2 << MAX_L) * 4;
+constexpr int BAR_OFF = ITEM_OFF + I_STAGES * (int)sizeof(Item);
+constexpr int NBAR = 2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + 2 * MS + 1;
+constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem base, abort flag
+constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
+static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
+// MMA thread, gather warps, decode warps 1.. (warp 0 publishes the items), epilogue warps
+constexpr uint32_t I_CONSUMERS = 1 + GATHER_WARPS + (DEC_WARPS - 1) + 4 * EPI_GROUPS;
+
+struct Params {
+    const __half* Qh;
+    const uint32_t* words;
+    const float* tab;
+    const __half* scale1;
+    const int32_t* qid;
+    const int32_t* coff;
+    const int32_t* ccnt;
+    const float* qcp;
+    const int32_t* list;
+    const int32_t* nlist;
+    const int64_t* off;
+    const float* t0;
+    int32_t* cnt;
+    float* bval;
+    int32_t* bpos;
+    float* bmc;
+    int32_t* sched;
+    int32_t* status;
+    int M, MB, W, L;
+    uint32_t wait_limit;
+};
+
+// instruction descriptor of tcgen05.mma.kind::f16: f32 accumulate, fp16 A and B, both K-major, M rows, N columns
+__device__ __forceinline__ uint32_t f16_idesc(int N, int M = 128) {
+    return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+__device__ __forceinline__ uint32_t transpose32(uint32_t x) {
+    const int lane = threadIdx.x & 31;
+    const uint32_t ms[5] = {0x0000FFFFu, 0x00FF00FFu, 0x0F0F0F0Fu, 0x33333333u, 0x55555555u};
+#pragma unroll
+    for (int k = 0; k < 5; k++) {
+        const int j = 16 >> k;
+        const uint32_t m = ms[k];
+        const uint32_t y = __shfl_xor_sync(0xffffffffu, x, j);
+        x = (lane & j) ? ((x & ~m) | ((y >> j) & m)) : ((x & m) | ((y & m) << j));
+    }
+    return x;
+}
+
+__device__ __forceinline__ uint32_t select32(const uint32_t (&a)[32], int jj) {
+    uint32_t t16[16], t8[8], t4[4], t2[2];
+#pragma unroll
+    for (int i = 0; i < 16; i++) t16[i] = (jj & 1) ? a[2 * i + 1] : a[2 * i];
+#pragma unroll
+    for (int i = 0; i < 8; i++) t8[i] = (jj & 2) ? t16[2 * i + 1] : t16[2 * i];
+#pragma unroll
+    for (int i = 0; i < 4; i++) t4[i] = (jj & 4) ? t8[2 * i + 1] : t8[2 * i];
+#pragma unroll
+    for (int i = 0; i < 2; i++) t2[i] = (jj & 8) ? t4[2 * i + 1] : t4[2 * i];
+    return (jj & 16) ? t2[1] : t2[0];
+}
+
+__device__ __forceinline__ Item bcast_item(const Item& it) {
+    Item o;
+    o.cell = __shfl_sync(0xffffffffu, it.cell, 0);
+    o.cs = __shfl_sync(0xffffffffu, it.cs, 0);
+    o.ce = __shfl_sync(0xffffffffu, it.ce, 0);
+    o.first = __shfl_sync(0xffffffffu, it.first, 0);
+    o.ntiles = __shfl_sync(0xffffffffu, it.ntiles, 0);
+    o.qoff = __shfl_sync(0xffffffffu, it.qoff, 0);
+    o.nq = __shfl_sync(0xffffffffu, it.nq, 0);
+    o.nsub = __shfl_sync(0xffffffffu, it.nsub, 0);
+    return o;
+}
+
+// the fields of one cell the producer needs, loaded in stages so that no load is waited on in the iteration that
+// issues it
+struct CellInfo {
+    int cell, cs, ce, qn, qoff;
+};
+
+template <int MODE>
+__global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t sbase = saddr(smem);
+    auto c_full = [&](int s) { return sbase + BAR_OFF + 8 * s; };
+    auto c_empty = [&](int s) { return sbase + BAR_OFF + 8 * (AC + s); };
+    auto b_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + s); };
+    auto b_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + B_STAGES + s); };
+    auto t_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + s); };
+    auto t_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + T_STAGES + s); };
+    auto i_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + s); };
+    auto i_empty = [&](int s) {
+        return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + I_STAGES + s);
+    };
+    auto m_full = [&](int s) {
+        return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + s);
+    };
+    auto m_empty = [&](int s) {
+        return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + MS + s);
+    };
+    const uint32_t d_bar = sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + 2 * MS);
+    auto meta = [&](int slot) { return reinterpret_cast<int*>(smem + META_OFF + slot * META_W); };
+    Item* items = reinterpret_cast<Item*>(smem + ITEM_OFF);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + MISC_OFF);
+    volatile int* abort = reinterpret_cast<volatile int*>(smem + MISC_OFF + 4);
+    const uint32_t WL = p.wait_limit;
+
+    if (tid == 0) {
+        for (int s = 0; s < AC; s++) {
+            mbar_init(c_full(s), DEC_WARPS);  // every decode warp has written its rows of the chunk
+            mbar_init(c_empty(s), 1);         // the MMAs reading the chunk have completed
+        }
+        for (int s = 0; s < B_STAGES; s++) {
+            mbar_init(b_full(s), 1);
+            mbar_init(b_empty(s), 1);
+        }
+        for (int s = 0; s < T_STAGES; s++) {
+            mbar_init(t_full(s), 1);
+            mbar_init(t_empty(s), 4);
+        }
+        for (int s = 0; s < I_STAGES; s++) {
+            mbar_init(i_full(s), 1);
+            mbar_init(i_empty(s), I_CONSUMERS);
+        }
+        for (int s = 0; s < MS; s++) {
+            mbar_init(m_full(s), 1);   // written by the sub-tile's gather warp
+            mbar_init(m_empty(s), 1);  // released by the last epilogue warp to finish a unit of the sub-tile
+            reinterpret_cast<int*>(smem + MCNT_OFF)[s] = 0;
+        }
+        mbar_init(d_bar, 1);
+        *abort = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    }
+    {
+        // pair table: window w of L+1 bits covers two consecutive states (w >> 1, w & (2^L - 1)); entry = their two
+        // values rounded to fp16, the first in the low half (the memory order of the decoded row)
+        uint32_t* tab2 = reinterpret_cast<uint32_t*>(smem + TAB_OFF);
+        const uint32_t mask = (1u << p.L) - 1u;
+        for (int w = tid; w < (2 << p.L); w += NTHREADS) {
+            const uint32_t h0 = __half_as_ushort(__float2half_rn(__ldg(p.tab + (w >> 1))));
+            const uint32_t h1 = __half_as_ushort(__float2half_rn(__ldg(p.tab + (w & mask))));
+            tab2[w] = h0 | (h1 << 16);
+        }
+    }
+    if (warp == W_MMA) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(tmem_slot)),
+                     "r"(TMEM_COLS));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    // every consumer role reads the items in order: item n sits in slot n % I_STAGES (the MMA thread alone, the
+    // other roles with all lanes and one outcome per warp)
+    auto read_item = [&](int n, Item& it, bool whole_warp) -> bool {
+        const int s = n % I_STAGES;
+        const bool r = whole_warp ? warp_wait(i_full(s), (n / I_STAGES) & 1, abort, WL)
+                                  : mbar_wait(i_full(s), (n / I_STAGES) & 1, abort, WL);
+        if (r) it = items[s];
+        return r;
+    };
+
+    bool mma_issued = false;
+
+    if (warp < W_MMA) {
+        // ---- decode (warp 0, lane 0: also the item producer)
+        const int dw = warp - W_DEC;
+        const uint32_t* tab2 = reinterpret_cast<const uint32_t*>(smem + TAB_OFF);
+        const int sh = 31 - p.L;  // a window is the top L+1 bits of a 32-bit funnel shift
+        const int r = 32 * dw + lane;
+        const int sw = r & 7;
+        const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw * 128);
+
+        // producer state (lane 0 of warp 0 only)
+        const int nl = (dw == 0 && lane == 0) ? *p.nlist : 0;
+        auto grab = [&]() { return atomicAdd(p.sched, 1); };
+        auto cell_of = [&](int idx) { return idx < nl ? p.list[idx] : -1; };
+        auto fields = [&](int c) {
+            CellInfo ci{c, 0, 0, 0, 0};
+            if (c >= 0) {
+                ci.cs = (int)p.off[c];
+                ci.ce = (int)p.off[c + 1];
+                ci.qn = p.ccnt[c];
+                ci.qoff = p.coff[c];
+            }
+            return ci;
+        };
+        CellInfo pre{-1, 0, 0, 0, 0}, cur{-1, 0, 0, 0, 0};
+        int cn = -1, idxn = 0, g = 0, ni = 0;
+        auto next_cell = [&]() {
+            const CellInfo c = pre;
+            pre = fields(cn);
+            cn = cell_of(idxn);
+            idxn = grab();
+            return c;
+        };
+        auto make_item = [&](const CellInfo& ci, int grp) {
+            Item it;
+            if (ci.cell < 0) {
+                it = Item{-1, 0, 0, 0, 0, 0, 0, 0};
+            } else {
+                const int first = ci.cs & ~31;
+                const int q0 = grp * RSUB * QN;
+                const int nq = min(RSUB * QN, ci.qn - q0);
+                it = Item{ci.cell, ci.cs, ci.ce, first, (ci.ce - first + TILE_ROWS - 1) / TILE_ROWS, ci.qoff + q0, nq,
+                          (nq + QN - 1) / QN};
+            }
+            return it;
+        };
+        auto push = [&](const Item& it) -> bool {
+            const int s = ni % I_STAGES;
+            if (!mbar_wait(i_empty(s), ((ni / I_STAGES) & 1) ^ 1, abort, WL)) return false;
+            items[s] = it;
+            mbar_arrive(i_full(s));  // release: the item's fields are visible to whoever acquires the phase
+            ni++;
+            return true;
+        };
+        // cells with no pairs (not listed) or no rows (probed, but nothing to scan) are skipped
+        auto idle = [&](const CellInfo& ci) { return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs); };
+        // the producer's next item: the next group of the current cell, else the first group of the next busy cell
+        auto produce = [&](bool first_call) -> Item {
+            if (first_call) {
+                pre = fields(cell_of(grab()));
+                cn = cell_of(grab());
+                idxn = grab();
+                g = 0;
+                do {
+                    cur = next_cell();
+                } while (idle(cur));
+            } else {
+                g++;
+                if (!(cur.cell >= 0 && g * RSUB * QN < cur.qn)) {
+                    g = 0;
+                    do {
+                        cur = next_cell();
+                    } while (idle(cur));
+                }
+            }
+            return make_item(cur, g);
+        };
+        // item n + 1, one ahead of the tiles of item n: warp 0 produces it, the other decode warps read it
+        int n = 0;
+        auto get_item = [&](bool first_call, Item& it) -> bool {
+            bool ok = true;
+            if (dw == 0) {
+                if (lane == 0) {
+                    it = produce(first_call);
+                    ok = push(it);
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                it = bcast_item(it);
+            } else {
+                ok = read_item(first_call ? 0 : n + 1, it, true);
+                if (ok && lane == 0) mbar_arrive(i_empty((first_call ? 0 : n + 1) % I_STAGES));
+            }
+            return ok;
+        };
+        auto load_words = [&](const Item& it, int t, uint32_t (&w)[NWORDS]) {
+            const int row = it.first + t * TILE_ROWS + r;
+            const bool v = it.nsub > 0 && row >= it.cs && row < it.ce;
+            const uint32_t* src = p.words + (int64_t)(v ? row : 0) * p.W;
+#pragma unroll
+            for (int i = 0; i < NWORDS; i++) w[i] = v ? __ldg(src + i) : 0u;
+        };
+
+        Item it;
+        bool ok = get_item(true, it);
+        int cslot = 0;
+        uint32_t cph = 0;
+        uint32_t w[NWORDS], wn[NWORDS];
+        if (ok) load_words(it, 0, w);
+        while (ok && it.nsub > 0) {
+            Item itn;
+            if (!get_item(false, itn)) break;
+            for (int t = 0; t < it.ntiles; t++) {
+                // words of the tile after this one (this item's next tile, else the next item's first)
+                if (t + 1 < it.ntiles)
+                    load_words(it, t + 1, wn);
+                else
+                    load_words(itn, 0, wn);
+                const int row = it.first + t * TILE_ROWS + r;
+                const bool v = row >= it.cs && row < it.ce;
+#pragma unroll
+                for (int c = 0; c < KCH; c++) {
+                    if (!warp_wait(c_empty(cslot), cph ^ 1u, abort, WL)) {
+                        ok = false;
+                        break;
+                    }
+                    if (v) {
+                        uint8_t* dst = smem + A_OFF + cslot * CH_BYTES + row_off;
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const uint32_t hi = w[2 * c + h], lo = w[2 * c + h + 1];
+#pragma unroll
+                            for (int uu = 0; uu < 4; uu++) {
+                                uint4 q;
+                                q.x = tab2[__funnelshift_l(lo, hi, 8 * uu + 0) >> sh];
+                                q.y = tab2[__funnelshift_l(lo, hi, 8 * uu + 2) >> sh];
+                                q.z = tab2[__funnelshift_l(lo, hi, 8 * uu + 4) >> sh];
+                                q.w = tab2[__funnelshift_l(lo, hi, 8 * uu + 6) >> sh];
+                                *reinterpret_cast<uint4*>(dst + (((h * 4 + uu) ^ sw) << 4)) = q;
+                            }
+                        }
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(c_full(cslot));
+                    if (++cslot == AC) {
+                        cslot = 0;
+                        cph ^= 1u;
+                    }
+                }
+                if (!ok) break;
+#pragma unroll
+                for (int i = 0; i < NWORDS; i++) w[i] = wn[i];
+            }
+            if (!ok) break;
+            it = itn;
+            n++;
+        }
+    } else if (warp == W_MMA) {
+        if (lane == 0) {
+            int nb = 0, nu = 0, cslot = 0;
+            uint32_t cph = 0;
+            for (int n = 0;; n++) {
+                Item it;
+                if (!read_item(n, it, false)) break;
+                mbar_arrive(i_empty(n % I_STAGES));
+                if (it.nsub == 0) break;
+                bool ok = true;
+                for (int t = 0; t < it.ntiles && ok; t++) {
+                    for (int c = 0; c < KCH && ok; c++) {
+                        if (!mbar_wait(c_full(cslot), cph, abort, WL)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t abase = sbase + A_OFF + cslot * CH_BYTES;
+                        for (int s = 0; s < it.nsub; s++) {
+                            const int sb = (nb + s) % B_STAGES, st = (nu + s) % T_STAGES;
+                            if (c == 0) {
+                                if ((t == 0 && !mbar_wait(b_full(sb), ((nb + s) / B_STAGES) & 1, abort, WL)) ||
+                                    !mbar_wait(t_empty(st), (((nu + s) / T_STAGES) & 1) ^ 1, abort, WL)) {
+                                    ok = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                            }
+                            const int nq = min(QN, it.nq - s * QN);
+                            const uint32_t idesc = f16_idesc((nq + 15) & ~15);
+                            const uint32_t d = tmem + (uint32_t)(st * QN);
+                            const uint32_t bb = sbase + B_OFF + sb * B_BYTES + c * QN * 128;
+#pragma unroll
+                            for (int kk = 0; kk < 4; kk++)
+                                mma_f16(d, sw128_desc(abase + kk * 32), sw128_desc(bb + kk * 32), idesc,
+                                        (c > 0 || kk > 0) ? 1u : 0u);
+                            mma_issued = true;
+                            if (c == KCH - 1) mma_commit(t_full(st));
+                        }
+                        if (!ok) break;
+                        mma_commit(c_empty(cslot));  // the chunk slot is free once these MMAs complete
+                        if (++cslot == AC) {
+                            cslot = 0;
+                            cph ^= 1u;
+                        }
+                    }
+                    nu += it.nsub;
+                }
+                if (!ok) break;
+                for (int s = 0; s < it.nsub; s++) mma_commit(b_empty((nb + s) % B_STAGES));
+                nb += it.nsub;
+            }
+        }
+        __syncwarp();
+    } else if (warp < W_GATHER + GATHER_WARPS) {
+        // ---- query gather: the item's sub-tiles alternate between the gather warps; lane l fills rows l, l + 32
+        const int gw = warp - W_GATHER;
+        int nb = 0;
+        for (int n = 0;; n++) {
+            Item it;
+            if (!read_item(n, it, true)) break;
+            if (lane == 0) mbar_arrive(i_empty(n % I_STAGES));
+            if (it.nsub == 0) break;
+            bool ok = true;
+            for (int s = 0; s < it.nsub; s++, nb++) {
+                if (nb % GATHER_WARPS != gw) continue;
+                const int sb = nb % B_STAGES, sm = nb % MS;
+                const int nq = min(QN, it.nq - s * QN);
+                const int n16 = (nq + 15) & ~15;
+                // the sub-tile's query ids, pair constants and thresholds (loaded before the slot waits)
+                int qq[2];
+                float qcv[2], thv[2];
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int gq = lane + 32 * rr;
+                    qq[rr] = gq < nq ? p.qid[it.qoff + s * QN + gq] : -1;
+                    qcv[rr] = gq < nq ? p.qcp[it.qoff + s * QN + gq] : 0.f;
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) thv[rr] = (MODE && qq[rr] >= 0) ? p.t0[qq[rr]] : 0.f;
+                if (!warp_wait(m_empty(sm), ((nb / MS) & 1) ^ 1, abort, WL)) {
+                    ok = false;
+                    break;
+                }
+                int* mq = meta(sm);
+                float* mc = reinterpret_cast<float*>(mq + QN);
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int gq = lane + 32 * rr;
+                    mq[gq] = qq[rr];
+                    mc[gq] = qcv[rr];
+                    mc[QN + gq] = thv[rr];
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(m_full(sm));
+                if (!warp_wait(b_empty(sb), ((nb / B_STAGES) & 1) ^ 1, abort, WL)) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int gq = lane + 32 * rr;
+                    if (gq >= n16) continue;
+                    const int q = qq[rr];
+                    const uint4* src = reinterpret_cast<const uint4*>(p.Qh + (int64_t)(q >= 0 ? q : 0) * R);
+                    uint8_t* bs = smem + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
+#pragma unroll
+                    for (int c = 0; c < KCH; c++) {
+                        uint4 v[8];
+#pragma unroll
+                        for (int cc = 0; cc < 8; cc++)
+                            v[cc] = q >= 0 ? __ldg(src + 8 * c + cc) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+                        for (int cc = 0; cc < 8; cc++)
+                            *reinterpret_cast<uint4*>(bs + c * QN * 128 + ((cc ^ (gq & 7)) << 4)) = v[cc];
+                    }
+                }
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                __syncwarp();
+                if (lane == 0) mbar_arrive(b_full(sb));
+            }
+            if (!ok) break;
+        }
+    } else if (warp >= W_EPI) {
+        // ---- epilogue: group eg takes the units nu = eg (mod EPI_GROUPS); warp ew = warp % 4 reads TMEM lanes
+        //      32*ew .. 32*ew+31 (tile rows)
+        const int we = warp - W_EPI;
+        const int eg = we / 4;
+        const int ew = warp & 3;
+        uint32_t* colm = reinterpret_cast<uint32_t*>(smem + COL_OFF) + we * 64;
+        int* colb = reinterpret_cast<int*>(colm + 32);
+        int nu = 0, nb = 0;
+        for (int n = 0;; n++) {
+            Item it;
+            if (!read_item(n, it, true)) break;
+            if (lane == 0) mbar_arrive(i_empty(n % I_STAGES));
+            if (it.nsub == 0) break;
+            bool ok = true;
+            for (int t = 0; t < it.ntiles && ok; t++) {
+                const int row0 = it.first + t * TILE_ROWS;
+                const int row = row0 + 32 * ew + lane;
+                const bool rvalid = row >= it.cs && row < it.ce;
+                const bool wactive = row0 + 32 * ew < it.ce;
+                const int blk_rel = (row0 + 32 * ew) / 32 - it.cs / 32;
+                for (int s = 0; s < it.nsub; s++, nu++) {
+                    if (nu % EPI_GROUPS != eg) continue;
+                    const int st = nu % T_STAGES;
+                    const int nq = min(QN, it.nq - s * QN);
+                    const int pair0 = it.qoff + s * QN;
+                    const int sm = (nb + s) % MS;
+                    const float sc = rvalid ? __half2float(p.scale1[row]) : 0.f;  // loaded before the waits
+                    if (!warp_wait(m_full(sm), ((nb + s) / MS) & 1, abort, WL) ||
+                        !warp_wait(t_full(st), (nu / T_STAGES) & 1, abort, WL)) {
+                        ok = false;
+                        break;
+                    }
+                    const int* mq = meta(sm);
+                    const float* mc = reinterpret_cast<const float*>(mq + QN);
+                    const float* mt = mc + QN;
+                    tc_fence_after();
+                    const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
+                    for (int h = 0; h * 32 < nq; h++) {
+                        uint32_t acc[32];
+                        tmem_ld32(ta + 32 * h, acc);
+                        tmem_ld_wait();
+                        if (!wactive) continue;
+                        const int nc = min(32, nq - h * 32);
+                        const float4* mc4 = reinterpret_cast<const float4*>(mc + 32 * h);
+                        if (MODE == 0) {
+#pragma unroll
+                            for (int j4 = 0; j4 < 8; j4++) {
+                                if (4 * j4 >= nc) break;
+                                const float4 cv = mc4[j4];
+                                const float c4[4] = {cv.x, cv.y, cv.z, cv.w};
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    const int jj = 4 * j4 + u;
+                                    if (jj < nc) {
+                                        const float est =
+                                            __fadd_rn(__fmul_rn(sc, __uint_as_float(acc[jj])), c4[u]);
+                                        const uint32_t m = __reduce_max_sync(0xffffffffu, rvalid ? f2o(est) : 0u);
+                                        if (lane == 0) p.bmc[(int64_t)(pair0 + 32 * h + jj) * p.MB + blk_rel] = o2f(m);
+                                    }
+                                }
+                            }
+                        } else {
+                            const float4* mt4 = reinterpret_cast<const float4*>(mt + 32 * h);
+                            uint32_t rowmask = 0;
+#pragma unroll
+                            for (int j4 = 0; j4 < 8; j4++) {
+                                if (4 * j4 >= nc) break;
+                                const float4 cv = mc4[j4], tv = mt4[j4];
+                                const float c4[4] = {cv.x, cv.y, cv.z, cv.w};
+                                const float t4[4] = {tv.x, tv.y, tv.z, tv.w};
+#pragma unroll
+                                for (int u = 0; u < 4; u++) {
+                                    const int jj = 4 * j4 + u;
+                                    if (jj < nc) {
+                                        const float est =
+                                            __fadd_rn(__fmul_rn(sc, __uint_as_float(acc[jj])), c4[u]);
+                                        const bool keep = rvalid && est >= t4[u];
+                                        acc[jj] = __float_as_uint(est);
+                                        rowmask |= (uint32_t)keep << jj;
+                                    }
+                                }
+                            }
+                            const uint32_t mymask = transpose32(rowmask);  // lane jj: the rows keeping column jj
+                            int mybase = 0;
+                            if (mymask) mybase = atomicAdd(p.cnt + mq[32 * h + lane], __popc(mymask));
+                            colm[lane] = mymask;
+                            colb[lane] = mybase;
+                            __syncwarp();
+                            while (rowmask) {
+                                const int jj = __ffs(rowmask) - 1;
+                                rowmask &= rowmask - 1;
+                                const int j = 32 * h + jj;
+                                const float est = __uint_as_float(select32(acc, jj));
+                                const int idx = colb[jj] + __popc(colm[jj] & ((1u << lane) - 1u));
+                                if (idx < p.M) {
+                                    const int64_t o = (int64_t)mq[j] * p.M + idx;
+                                    p.bval[o] = est;
+                                    p.bpos[o] = row;
+                                }
+                            }
+                            __syncwarp();
+                        }
+                    }
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(t_empty(st));
+                        // the sub-tile's units (one per tile) are spread over the warpgroups, which finish in any
+                        // order: the slot is free once all 4 * ntiles warps are done with it; the last one to count
+                        // itself resets the count and releases the slot
+                        __threadfence_block();
+                        int* mcount = reinterpret_cast<int*>(smem + MCNT_OFF);
+                        if (atomicAdd(mcount + sm, 1) == 4 * it.ntiles - 1) {
+                            mcount[sm] = 0;
+                            mbar_arrive(m_empty(sm));
+                        }
+                    }
+                }
+            }
+            if (!ok) break;
+            nb += it.nsub;
+        }
+    }
+    // drain (a wait that ignores the abort flag): one commit after the last MMA issued has arrived, i.e. every MMA of
+    // this CTA has completed before its tensor memory is freed and its shared memory released
+    if (warp == W_MMA && lane == 0 && mma_issued) {
+        mma_commit(d_bar);
+        mbar_drain(d_bar, 0);
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == W_MMA) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    if (tid == 0) {
+        if (*abort && p.status) atomicExch(p.status, 1);
+        // the last CTA out resets the work counter for the next launch (every CTA took its last cell before this)
+        __threadfence();
+        if (atomicAdd(p.sched + 1, 1) == (int)gridDim.x - 1) {
+            atomicExch(p.sched, 0);
+            atomicExch(p.sched + 1, 0);
+        }
+    }
+}
+
+}  // namespace tcells
+}  // namespace fvs
+
+extern "C" int fvs_trellis_scan_cells(fvs_stream_t stream, int mode, const uint16_t* Qh, int B, int R,
+                                      const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,
+                                      const int32_t* list, const int32_t* nlist, int maxlist, const int64_t* off,
+                                      int NC, const int32_t* words, int W, const float* tab, int L,
+                                      const uint16_t* scale1, const float* t0, int32_t* cnt, float* bval,
+                                      int32_t* bpos, int M, float* bmc, int MB, int32_t* sched, int32_t* status) {
+    using namespace fvs::tcells;
+    FVS_CHECK_ARG(mode == 0 || mode == 1);
+    FVS_CHECK_ARG(R == fvs::tcells::R && B >= 0 && maxlist >= 0 && NC > 0);
+    FVS_CHECK_ARG(L >= 2 && W >= (R + L - 1 + 31) / 32);
+    FVS_CHECK_ARG(Qh && qid && coff && ccnt && qcp && list && nlist && off && words && tab && scale1 && sched);
+    FVS_CHECK_ARG(((uintptr_t)Qh & 15) == 0);
+    if (mode == 0) FVS_CHECK_ARG(bmc && MB > 0);
+    if (mode == 1) FVS_CHECK_ARG(t0 && cnt && bval && bpos && M > 0);
+    if (L > MAX_L) return FVS_ERANGE;
+    if (maxlist == 0 || B == 0) return FVS_OK;
+    Params p{(const __half*)Qh, (const uint32_t*)words, tab, (const __half*)scale1, qid, coff, ccnt, qcp, list, nlist,
+             off, t0, cnt, bval, bpos, bmc, sched, status, M, MB, W, L, pipeline_wait_limit()};
+    cudaError_t e = mode ? fvs_ensure_smem((const void*)trellis_cells_kernel<1>, SMEM_BYTES)
+                         : fvs_ensure_smem((const void*)trellis_cells_kernel<0>, SMEM_BYTES);
+    if (e != cudaSuccess) return (int)e;
+    const int nsm = fvs_sm_count();
+    const int grid = maxlist < nsm ? maxlist : nsm;
+    if (mode == 0)
+        trellis_cells_kernel<0><<<grid, NTHREADS, SMEM_BYTES, stream>>>(p);
+    else
+        trellis_cells_kernel<1><<<grid, NTHREADS, SMEM_BYTES, stream>>>(p);
+    return fvs_launch_status();
+}

@@ -57,6 +57,9 @@ class IndexS:
         self.VP = f(code["VP"], torch.float32)[:, :self.D].contiguous()
         self.H16 = f(H16, torch.float16)
         self.d = self.H16.shape[1]
+        sizes = np.diff(self.off_np)
+        # cells largest first: the order in which the cell-major scan hands cells out
+        self.cell_order = f(np.argsort(-sizes, kind="stable").astype(np.int32), torch.int32)
         tc, tr, self.MB = static_tiles(self.off_np, _lib.lib().fvs_trellis_tile_rows())
         self.tile_cell, self.tile_row0 = f(tc, torch.int32), f(tr, torch.int32)
         self.ntiles = len(tc)
@@ -74,10 +77,17 @@ class IndexS:
         return 4 * self.W + 2 + sum((e - s) * b for s, e, b in self.TS) / 8 + 4 * self.T
 
 
+TRELLIS_CELLS_MAX_L = 10   # FVS_TRELLIS_CELLS_MAX_L: largest trellis window of the tcgen05 scan
+
+
 class EngineB200S(EngineB200I8):
     """The reference's EngineS on libfanar_b200: (beta, rho) = (1.1, 0.75) for K <= 400 else (0.7, 0.5),
     M = max(4096, 16 K) (`src/engine_cell.py:78-79`, `src/s1cell.py:181`).  Graph capture, the flag read and the
-    flagged-row recompute are inherited from EngineB200I8."""
+    flagged-row recompute are inherited from EngineB200I8.
+
+    SCAN = "cells" (the product path): batches above SMALL scan with the cell-major tcgen05 kernel
+    (fvs_trellis_scan_cells); "mma" keeps the mma.sync tile kernel (fvs_trellis_scan) as the measured baseline, which
+    also takes trellis windows above TRELLIS_CELLS_MAX_L."""
     M = None
     FB_M = 65536
     FB_INGRAPH = 0        # flagged rows are recomputed from the host (no in-graph recompute on this path)
@@ -96,8 +106,18 @@ class EngineB200S(EngineB200I8):
                    ptr(probe))
         return QM, probe
 
-    def _scan(self, mode, name, Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc, mb=None):
+    def cells_scan(self):
+        return self.SCAN == "cells" and self.ix.L <= TRELLIS_CELLS_MAX_L
+
+    def _scan(self, mode, name, Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, bmc, mb=None, lists=None):
         ix = self.ix
+        if lists is not None:
+            lst, nl = lists
+            self._call(name, self.L.fvs_trellis_scan_cells, mode, ptr(Qh), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
+                       ptr(qcp), ptr(lst), ptr(nl), ix.NC, ptr(ix.off), ix.NC, ptr(ix.words), ix.W, ptr(ix.tab), ix.L,
+                       ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB, ptr(self.sched),
+                       ptr(self.status))
+            return
         self._call(name, self.L.fvs_trellis_scan, mode, ptr(Qh), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt), ptr(qcp),
                    ptr(ix.tile_cell), ptr(ix.tile_row0), ix.ntiles, ptr(ix.off), ix.NC, ptr(ix.words), ix.W,
                    ptr(ix.tab), ix.L, ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc),
@@ -120,22 +140,28 @@ class EngineB200S(EngineB200I8):
         probe = probe.contiguous()
         # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
         qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
+        l1 = l2 = None
+        if self.cells_scan():
+            cnt = torch.empty(B, dtype=torch.int32, device=dev)            # cleared by the list kernel
+            list1, lst, nl = self.cell_lists(ccnt1, ccnt, cnt)
+            l1, l2 = (list1, nl[0:1]), (lst, nl[1:2])
+        else:
+            cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bmc = torch.empty(qid.numel() * ix.MB, device=dev)   # block-maxima rows addressed by pair position
-        self._scan(0, "trellis_scan_first", Qh, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc)
+        self._scan(0, "trellis_scan_first", Qh, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc, lists=l1)
         t0 = torch.empty(B, device=dev)
         self._call("threshold", L.fvs_threshold, ptr(bmc), ix.MB, ptr(slot), ptr(probe), nprobe, n1, ptr(ix.off), B,
                    int(np.ceil(rho * K)), ptr(t0))
-        cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bval = torch.empty(B, M, device=dev)
         bpos = torch.empty(B, M, dtype=torch.int32, device=dev)
-        self._scan(1, "trellis_scan_emit", Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None)
+        self._scan(1, "trellis_scan_emit", Qh, B, qid, coff, ccnt, qcp, t0, cnt, bval, bpos, M, None, lists=l2)
         pos = torch.empty(B, K, dtype=torch.int64, device=dev)
         est1 = torch.empty(B, K, device=dev)
         ok = torch.empty(B, dtype=torch.uint8, device=dev)
         self._call("select_topk", L.fvs_select_topk, ptr(bval), ptr(bpos), ptr(cnt), B, M, K, ptr(pos), ptr(est1),
                    ptr(ok), None, 0.0, 9)
-        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, Qh=Qh, ccnt=ccnt, npairs=int(qid.numel()), bval=bval,
-                          bpos=bpos, slot=slot)
+        self._last = dict(t0=t0, cnt=cnt, n1=n1, M=M, bmc=bmc, Qh=Qh, ccnt=ccnt, ccnt1=ccnt1, npairs=int(qid.numel()),
+                          bval=bval, bpos=bpos, slot=slot, scan_args=(qid, coff, qcp, l1, l2))
         return pos, ok.bool(), est1
 
     def stage1_small(self, Qb, QM, probe, K):

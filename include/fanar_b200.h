@@ -287,6 +287,21 @@ int fvs_trellis_scan(fvs_stream_t stream, int mode, const uint16_t* Qh, int B, i
                      const float* t0, int32_t* cnt, float* bval, int32_t* bpos, int M, float* bmc, int MB);
 
 /*
+ * fvs_trellis_scan modes 0 / 1 on the 5th-generation tensor cores, organised by cells (same contract and values;
+ * replaces the same reference kernels, `src/s1cell.py:121-154` with `src/decode2.py:5-17`): the CTAs take the cells of
+ * `list` (nlist[0] of them) with an atomicAdd on sched[0], gather a cell's queries once, decode each 128-row tile of the
+ * cell in shared memory (fp16 values in the tensor cores' operand layout) and run tcgen05.mma.kind::f16 on it.  Lists,
+ * maxlist and sched as fvs_i8_scan_cells (the lists come from fvs_cell_lists); status as fvs_i8_scan_tc.  L above
+ * FVS_TRELLIS_CELLS_MAX_L returns FVS_ERANGE (fvs_trellis_scan takes it).
+ */
+#define FVS_TRELLIS_CELLS_MAX_L 10
+int fvs_trellis_scan_cells(fvs_stream_t stream, int mode, const uint16_t* Qh, int B, int R, const int32_t* qid,
+                           const int32_t* coff, const int32_t* ccnt, const float* qcp, const int32_t* list,
+                           const int32_t* nlist, int maxlist, const int64_t* off, int NC, const int32_t* words, int W,
+                           const float* tab, int L, const uint16_t* scale1, const float* t0, int32_t* cnt,
+                           float* bval, int32_t* bpos, int M, float* bmc, int MB, int32_t* sched, int32_t* status);
+
+/*
  * Default engine, stage 1 for B <= 8 (`src/s1small_cell.py:7-42`, `_small_scan` / `search_small`): est =
  * (sum_j tab[state_j] * Qr[q, j]) * scale1[n] + float(QM[q, c]) in fp32 (Qr = Q @ W1 in fp32, table values not rounded
  * to fp16), work taken straight from probe [B, nprobe] (columns 0..ncols-1): mode 0 merges the block maxima into

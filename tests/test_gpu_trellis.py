@@ -1,8 +1,9 @@
 """GPU parity of the default-engine path (trellis stage 1, tiered gather stage 2) against the reference's golden
 vectors and the CPU oracle, through the C ABI.
 
-Stage-1 estimates of this path are fp16 products accumulated in fp32 on the tensor cores, in an order that differs
-from the reference's `tl.dot`: they agree within fp32 rounding (TOL), and thresholds, emitted sets and stage-1
+Stage 1 runs on two kernels, both tested: the cell-major tcgen05 scan (SCAN = "cells", the product path: codes decoded
+in shared memory, tcgen05.mma.kind::f16) and the mma.sync tile scan (SCAN = "mma", the baseline).  Stage-1 estimates
+are fp16 products accumulated in fp32 on the tensor cores, in an order that differs from the reference's `tl.dot`: they agree within fp32 rounding (TOL), and thresholds, emitted sets and stage-1
 candidates are compared exactly except for items whose estimate lies within that rounding of the decision value.
 Integer work (routing order, pair lists, Viterbi paths and words, candidate ids) is compared bit for bit."""
 import os
@@ -83,10 +84,20 @@ def test_route_scaled_ties(ec, NC, npr):
     np.testing.assert_array_equal(c(probe), want)
 
 
-def test_trellis_scan_first_pass_and_threshold(gt, ec):
+SCANS = ["cells", "mma"]
+
+
+def _engine(ec, ix, scan="cells"):
+    E = ec.EngineB200S(ix)
+    E.SCAN = scan
+    return E
+
+
+@pytest.mark.parametrize("scan", SCANS)
+def test_trellis_scan_first_pass_and_threshold(gt, ec, scan):
     f = gt
     ix = _index(ec, f)
-    E = ec.EngineB200S(ix)
+    E = _engine(ec, ix, scan)
     K, nprobe, k = (int(v) for v in f["params"])
     B = len(f["Q"])
     Q = torch.from_numpy(f["Q"]).to(DEV)
@@ -117,11 +128,12 @@ def test_trellis_scan_first_pass_and_threshold(gt, ec):
                 assert p in est_of and _near(est_of[p], kth), (q, p)
 
 
-def test_trellis_emit_matches_reference(gt, ec):
+@pytest.mark.parametrize("scan", SCANS)
+def test_trellis_emit_matches_reference(gt, ec, scan):
     """the emit pass from the reference's own threshold: same counts and sets except items within rounding of t0."""
     f = gt
     ix = _index(ec, f)
-    E = ec.EngineB200S(ix)
+    E = _engine(ec, ix, scan)
     K, nprobe, k = (int(v) for v in f["params"])
     B = len(f["Q"])
     M = int(f["k_M"])
@@ -130,8 +142,13 @@ def test_trellis_emit_matches_reference(gt, ec):
     cnt = torch.zeros(B, dtype=torch.int32, device=DEV)
     bval = torch.empty(B, M, device=DEV)
     bpos = torch.empty(B, M, dtype=torch.int32, device=DEV)
+    ccnt = d(f["k_ccnt"], torch.int32)
+    lists = None
+    if scan == "cells":
+        _, lst, nl = E.cell_lists(None, ccnt, cnt)
+        lists = (lst, nl[1:2])
     E._scan(1, "emit", d(f["k_Qh"], torch.float16), B, d(f["k_qid"], torch.int32), d(f["k_coff"], torch.int32),
-            d(f["k_ccnt"], torch.int32), d(f["k_qcp"], torch.float32), t0, cnt, bval, bpos, M, None)
+            ccnt, d(f["k_qcp"], torch.float32), t0, cnt, bval, bpos, M, None, lists=lists)
     cnt, bval, bpos = c(cnt), c(bval), c(bpos)
     eq, ev, ep = f["k_emit_q"], f["k_emit_val"], f["k_emit_pos"]
     for q in range(B):
@@ -180,10 +197,11 @@ def test_viterbi_encoder_reproduces_reference_words(gt, ec):
     np.testing.assert_array_equal(c(path[:64]), O.viterbi_paths(c(Zs[:64]), f["tab"], 10))
 
 
-def test_search_matches_reference_end_to_end(gt, ec):
+@pytest.mark.parametrize("scan", SCANS)
+def test_search_matches_reference_end_to_end(gt, ec, scan):
     f = gt
     ix = _index(ec, f)
-    E = ec.EngineB200S(ix)
+    E = _engine(ec, ix, scan)
     K, nprobe, k = (int(v) for v in f["params"])
     z = float(f["z"])
     Q = torch.from_numpy(f["Q"]).to(DEV)
@@ -224,10 +242,11 @@ def _oracle_index(s1, code, X16):
                 scale1=t(s1["scale1"]), H16=t(X16), code=oc)
 
 
+@pytest.mark.parametrize("scan", SCANS)
 @pytest.mark.parametrize("K,nprobe,k", [(100, 32, 10), (500, 40, 100)])
-def test_search_matches_oracle_synthetic(ec, synth_index, K, nprobe, k):
+def test_search_matches_oracle_synthetic(ec, synth_index, K, nprobe, k, scan):
     ds, ix, s1, code = synth_index
-    E = ec.EngineB200S(ix)
+    E = _engine(ec, ix, scan)
     Q = ds["queries"][:120].contiguous()
     out = E.search_eager(Q, K, 2.0, nprobe, k)
     oi = _oracle_index(s1, code, ds["base16"])
@@ -256,6 +275,92 @@ def test_search_matches_oracle_synthetic(ec, synth_index, K, nprobe, k):
     g = ds["gt"][:120, :10].cpu().numpy()
     r = np.mean([len(set(a.tolist()) & set(b.tolist())) / 10 for a, b in zip(c(I), g)])
     assert r >= 0.9, r
+
+
+@pytest.mark.parametrize("B,nprobe", [(300, 64), (300, 128), (40, 128)])
+def test_cells_scan_matches_tile_scan(ec, synth_index, B, nprobe):
+    """the tcgen05 cell-major scan against the mma.sync tile scan on the same pair lists: first-pass block maxima and
+    emitted sets (with values) through cells of several 128-row tiles and cells with more than 128 queries (several
+    query groups); the two accumulate the fp32 dot in different orders, so values agree within TOL and emitted sets
+    are equal except items within TOL of the threshold."""
+    ds, ix, _, _ = synth_index
+    Ec, Em = _engine(ec, ix, "cells"), _engine(ec, ix, "mma")
+    Q = ds["queries"][:B].contiguous()
+    K = 200
+    QM, probe = Ec.route(Q, nprobe)
+    Qh = (Q @ ix.W1).half().contiguous()
+    pc, okc, ec1 = Ec.stage1_trellis(Q, QM, probe, K, Qh=Qh)
+    Lc = Ec._last
+    pm, okm, em1 = Em.stage1_trellis(Q, QM, probe, K, Qh=Qh)
+    Lm = Em._last
+    torch.cuda.synchronize()
+    assert int(Ec.status) == 0
+    if B > 128:
+        assert c(Lc["ccnt"]).max() > 128      # a cell with several query groups
+    MB, n1 = ix.MB, Lc["n1"]
+    # the block maxima of every first-pass pair (q, j < n1), found through each run's own slot (the order of a cell's
+    # pairs is not deterministic); only the blocks of the pair's cell are written and read
+    bc = c(Lc["bmc"]).reshape(-1, MB)[c(Lc["slot"])]
+    bm = c(Lm["bmc"]).reshape(-1, MB)[c(Lm["slot"])]
+    cells = c(probe)[:, :n1].reshape(-1)
+    off = ix.off_np
+    nb = np.where(off[cells + 1] > off[cells], (off[cells + 1] - 1) // 32 - off[cells] // 32 + 1, 0)
+    own = np.arange(MB)[None, :] < nb[:, None]
+    assert own.sum() > 0
+    np.testing.assert_allclose(bc[own], bm[own], rtol=TOL, atol=TOL)
+    t0c, t0m = c(Lc["t0"]), c(Lm["t0"])
+    np.testing.assert_allclose(t0c, t0m, rtol=TOL, atol=TOL)
+    # emitted sets (each pass with its own threshold): an item clearly above both thresholds is emitted by both, and
+    # the items both emitted carry the same estimate within TOL (queries whose buffer overflowed keep an arbitrary
+    # subset and are skipped)
+    M = Lc["M"]
+    cntc, cntm = c(Lc["cnt"]), c(Lm["cnt"])
+    checked = 0
+    for q in range(B):
+        if cntc[q] > M or cntm[q] > M:
+            continue
+        vc, pcq = c(Lc["bval"][q, :cntc[q]]), c(Lc["bpos"][q, :cntc[q]])
+        vm, pmq = c(Lm["bval"][q, :cntm[q]]), c(Lm["bpos"][q, :cntm[q]])
+        hi = max(t0c[q], t0m[q]) + 3 * TOL * (1 + abs(t0c[q]))
+        assert set(pcq[vc >= hi].tolist()) <= set(pmq.tolist())
+        assert set(pmq[vm >= hi].tolist()) <= set(pcq.tolist())
+        common, ia, ib_ = np.intersect1d(pcq, pmq, return_indices=True)
+        np.testing.assert_allclose(vc[ia], vm[ib_], rtol=TOL, atol=TOL)
+        checked += 1
+    assert checked >= 0.9 * B
+
+
+def test_cells_scan_wait_expiry(ec, synth_index):
+    """an expired bounded wait in the tcgen05 trellis scan raises from search(), and the device stays usable (the next
+    search equals the one before); small poll budgets exercise the drain path."""
+    ds, ix, _, _ = synth_index
+    L = pkg("_lib")
+    lib = L.lib()
+    Q = ds["queries"][:200].contiguous()
+    I0, _, ids0 = _engine(ec, ix).search(Q, 100, 2.0, 32, 10)
+    torch.cuda.synchronize()
+
+    def limited(polls, fn):
+        prev = lib.fvs_set_wait_limit(polls)
+        try:
+            return fn()
+        finally:
+            lib.fvs_set_wait_limit(prev)
+
+    E = _engine(ec, ix)
+    with pytest.raises(L.FvsError, match="bounded device wait"):
+        limited(0, lambda: E.search(Q, 100, 2.0, 32, 10))
+    for polls in (1, 8, 64, 512):
+        E2 = _engine(ec, ix)
+        limited(polls, lambda: E2.search_eager(Q, 100, 2.0, 32, 10))
+        torch.cuda.synchronize()
+        assert int(E2.status) in (0, 1)
+    E3 = _engine(ec, ix)
+    I3, _, ids3 = E3.search(Q, 100, 2.0, 32, 10)
+    torch.cuda.synchronize()
+    assert int(E3.status) == 0
+    np.testing.assert_array_equal(c(I3), c(I0))
+    np.testing.assert_array_equal(c(ids3), c(ids0))
 
 
 @pytest.mark.parametrize("tag", ["s6_", "m20_"])
