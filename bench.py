@@ -492,6 +492,15 @@ def variant_trellis(args, dev, steps=20):
     flags = {"underflow": int((cnt < K).sum()), "overflow": int((cnt > E._last["M"]).sum()),
              "cnt_median": int(cnt.float().median())}
     Mbuf = E.M
+    # the same operating point at the reference's own buffer rule M = max(4096, 16 K) (`src/s1cell.py:181`): the
+    # queries whose emit overflows it are flagged and recomputed (with 65536 entries)
+    E.M = None
+    E.nbad = 0
+    I = E.search(Q, K, z, npr, k)[0]
+    ref_m = dict(M=max(4096, 16 * K), recall=round(synth.recall(I.cpu(), ds["gt"].cpu(), 10), 4),
+                 flagged=E.nbad, ms_per_step=round(_steps_ms(lambda: E.search(Q, K, z, npr, k), steps), 4))
+    ref_m["qps"] = round(len(Q) / (ref_m["ms_per_step"] * 1e-3), 1)
+    E.M = Mbuf
     # the same operating point on the mma.sync tile scan (the baseline the tcgen05 cell-major scan replaces)
     E.SCAN = "mma"
     ms_mma = _steps_ms(lambda: E.search(Q, K, z, npr, k), steps)
@@ -511,7 +520,8 @@ def variant_trellis(args, dev, steps=20):
             "recall@10": round(rec, 4), "ms_per_step": round(ms, 4), "grid": rows, "build_s": round(build_s, 1),
             "kernel_ms": {n: round(v, 4) for n, v in kt.items()}, "flagged_last_batch": flags, "k100": rows100,
             "mma_scan_baseline": {"ms_per_step": round(ms_mma, 4), "qps": round(len(Q) / (ms_mma * 1e-3), 1),
-                                  "kernel_ms": kt_mma}}
+                                  "kernel_ms": kt_mma},
+            "reference_buffer_rule": ref_m}
 
 
 def _timed_search(fn, steps=10):
@@ -916,6 +926,9 @@ def main():
     # ---- the batch-1 scan (streaming small-batch kernel), same operating point: a few MB per launch, so launch and
     # load latency rather than bandwidth bound it
     roof["batch1_scan"] = batch1_scan(E, Qs[1][:1], K, z, npr, k, peak)
+    # and at the probe widths of the latency configuration (`src/v19_final.py:53`): tens of MB of codes per launch
+    roof["batch1_scan_wide"] = [dict(nprobe=n_, K=K_, **batch1_scan(E, Qs[1][:1], K_, z, n_, k, peak))
+                                for n_, K_ in ((384, 400), (768, 800)) if n_ <= E.ix.NC]
     cpu = parity = None
     if rank == 0 and world == 1:
         oi = oracle_index_cpu(s1, i8, code, ds["base16"])

@@ -338,6 +338,52 @@ __device__ __forceinline__ void warp_bitonic_desc(unsigned long long* a, int n) 
     }
 }
 
+// Descending bitonic sort of 32 * PER keys held in registers by one warp, element i = lane * PER + j in v[j]
+// (PER a power of two): exchanges at distance >= PER go through shuffles, the shorter ones stay in the lane.
+template <typename T>
+__device__ __forceinline__ T warp_shfl_xor_key(T x, int m) {
+    if constexpr (sizeof(T) == 8) {
+        const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)x, m);
+        const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(x >> 32), m);
+        return ((T)hi << 32) | (T)lo;
+    } else {
+        return __shfl_xor_sync(0xffffffffu, x, m);
+    }
+}
+template <int PER, typename T>
+__device__ __forceinline__ void warp_sort_regs_desc(T (&v)[PER]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int size = 2; size <= 32 * PER; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride >= PER) {
+                const int lx = stride / PER;
+                const bool lower = (lane & lx) == 0;
+#pragma unroll
+                for (int j = 0; j < PER; j++) {
+                    const T o = warp_shfl_xor_key(v[j], lx);
+                    const bool desc = ((lane * PER + j) & size) == 0;
+                    // the lower index of a pair keeps the larger key in a descending block, the smaller otherwise
+                    v[j] = (lower == desc) ? (v[j] > o ? v[j] : o) : (v[j] < o ? v[j] : o);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < PER; j++) {
+                    if (j & stride) continue;
+                    const int j2 = j | stride;
+                    const bool desc = ((lane * PER + j) & size) == 0;
+                    const T a = v[j], b = v[j2];
+                    if (desc ? (a < b) : (a > b)) {
+                        v[j] = b;
+                        v[j2] = a;
+                    }
+                }
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ int warp_sum_int(int v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

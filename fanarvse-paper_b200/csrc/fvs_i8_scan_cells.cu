@@ -14,12 +14,12 @@
 // Warp roles (640 threads):
 //   warp 0      : lane 0 takes cells (atomicAdd on sched[0]; the list entry, bounds and pair range of a cell are
 //                 loaded ahead in stages), publishes each work item (cell, group of sub-tiles) in a ring of I_STAGES
-//                 slots one item ahead, and issues the TMA loads of the item's code tiles into A_STAGES stages
+//                 slots up to AHEAD items ahead, and issues the TMA loads of the item's code tiles into A_STAGES stages
 //   warp 1      : TMEM allocation; lane 0 issues tcgen05.mma.kind::i8 (M=128 rows, N=16..64 queries, K=256 as 8 x 32)
 //                 for every (tile, sub-tile) unit into one of T_STAGES accumulators; releases a code tile after its
 //                 units and the item's query sub-tiles after its last tile
-//   warps 2-3   : gather: the item's sub-tiles alternate between the two warps; rows of q8 picked by qid, written in the
-//                 canonical K-major 128 B-swizzled layout, and the sub-tile's column metadata (qid, qs, pair constant,
+//   warps 2-3   : gather: the item's sub-tiles alternate between the two warps; rows of q8 picked by qid, copied with
+//                 cp.async (a sub-tile's rows in flight at once) into the canonical K-major 128 B-swizzled layout, and the sub-tile's column metadata (qid, qs, pair constant,
 //                 threshold) into one of MS slots, released when every epilogue warp is done with the sub-tile
 //   warps 4-19  : four epilogue warpgroups, units alternating between them; each warp loads its rows' scales before
 //                 waiting for the accumulator, then as fvs_i8_scan_tc: est = ((acc * qs) * zs) + qcp with explicit rounding, first pass: block maximum per
@@ -46,12 +46,14 @@ constexpr int I_STAGES = 8;
 constexpr int MS = 8;    // column-metadata slots (one per sub-tile, held until the sub-tile's last unit is done)
 constexpr int EPI_GROUPS = 4;
 constexpr int GATHER_WARPS = 2;
+constexpr int AHEAD = 4;  // work items published beyond the one whose tiles are being loaded
 constexpr int W_TMA = 0, W_MMA = 1, W_GATHER = 2, W_EPI = W_GATHER + GATHER_WARPS;
 constexpr int NWARPS = W_EPI + 4 * EPI_GROUPS;
 constexpr int NTHREADS = 32 * NWARPS;
 constexpr uint32_t TMEM_COLS = T_STAGES * QN;
 static_assert(B_STAGES >= 2 * RSUB, "a work item's sub-tiles and the next item's fit together");
 static_assert(W_EPI % 4 == 0, "epilogue warpgroups cover TMEM lane quarters 0..3 in order");
+static_assert(AHEAD + 2 <= I_STAGES, "an item's slot is not reused before the producer has loaded its tiles");
 
 struct Item {
     int cell, cs, ce, first, ntiles, qoff, nq, nsub;  // nsub == 0: no more work
@@ -271,16 +273,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                     ci = next_cell();
                 } while (idle(ci));
             };
-            CellInfo cur = next_cell();
-            while (idle(cur)) cur = next_cell();
-            Item it = make_item(cur, g);
-            bool ok = push(it);
-            while (ok && it.nsub > 0) {
-                CellInfo nxt = cur;
-                int gn = g;
-                advance(nxt, gn);
-                const Item itn = make_item(nxt, gn);
-                if (!push(itn)) break;  // the next item is published before this one's tiles are loaded
+            // items are published up to AHEAD beyond the one whose tiles are being loaded, so that the gathers of the
+            // next items start early; the producer reads its own items back from the ring (a slot is reused only
+            // AHEAD + 1 < I_STAGES items later)
+            CellInfo cur{-1, 0, 0, 0, 0};
+            bool more = true, started = false, ok = true;
+            auto publish_until = [&](int upto) -> bool {
+                while (more && ni <= upto) {
+                    if (!started) {
+                        started = true;
+                        cur = next_cell();
+                        while (idle(cur)) cur = next_cell();
+                    } else {
+                        advance(cur, g);
+                    }
+                    const Item nx = make_item(cur, g);
+                    if (!push(nx)) return false;
+                    if (nx.nsub == 0) more = false;
+                }
+                return true;
+            };
+            for (int n = 0; ok; n++) {
+                if (!publish_until(n + AHEAD)) break;
+                const Item it = items[n % I_STAGES];
+                if (it.nsub == 0) break;
                 for (int t = 0; t < it.ntiles && ok; t++) {
                     const int s = na_load % A_STAGES;
                     if (!mbar_wait(a_empty(s), ((na_load / A_STAGES) & 1) ^ 1, abort, WL)) {
@@ -297,9 +313,6 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                     }
                     na_load++;
                 }
-                cur = nxt;
-                g = gn;
-                it = itn;
             }
         }
     } else if (warp == W_MMA) {
@@ -366,7 +379,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                 const int sb = nb % B_STAGES, sm = nb % MS;
                 const int nq = min(QN, it.nq - s * QN);
                 const int n16 = (nq + 15) & ~15;
-                // the sub-tile's query ids, pair constants, scales and thresholds (loaded before the slot waits)
+                // the sub-tile's query ids and pair constants; its rows are copied with cp.async (all of them in flight
+                // at once, zero rows past nq) while the scales and thresholds load and the metadata slot is filled
                 int qq[2];
                 float qcv[2], qsv[2], thv[2];
 #pragma unroll
@@ -375,12 +389,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                     qq[rr] = gq < nq ? p.qid[it.qoff + s * QN + gq] : -1;
                     qcv[rr] = gq < nq ? p.qcp[it.qoff + s * QN + gq] : 0.f;
                 }
+                if (!warp_wait(b_empty(sb), ((nb / B_STAGES) & 1) ^ 1, abort, WL)) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int gq = lane + 32 * rr;
+                    if (gq >= n16) continue;
+                    const int q = qq[rr];
+                    const uint4* src = reinterpret_cast<const uint4*>(p.q8 + (int64_t)(q >= 0 ? q : 0) * RB);
+                    const uint32_t bs = sbase + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
+#pragma unroll
+                    for (int h = 0; h < 2; h++)
+#pragma unroll
+                        for (int cc = 0; cc < 8; cc++)
+                            cp_async16(bs + h * QN * 128 + ((cc ^ (gq & 7)) << 4), src + 8 * h + cc, q >= 0);
+                }
 #pragma unroll
                 for (int rr = 0; rr < 2; rr++) {
                     qsv[rr] = qq[rr] >= 0 ? p.qs[qq[rr]] : 0.f;
                     thv[rr] = (MODE && qq[rr] >= 0) ? p.t0[qq[rr]] : 0.f;
                 }
                 if (!warp_wait(m_empty(sm), ((nb / MS) & 1) ^ 1, abort, WL)) {
+                    cp_async_wait_all();  // no copy into shared memory stays in flight
                     ok = false;
                     break;
                 }
@@ -396,28 +428,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(m_full(sm));
-                if (!warp_wait(b_empty(sb), ((nb / B_STAGES) & 1) ^ 1, abort, WL)) {
-                    ok = false;
-                    break;
-                }
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int gq = lane + 32 * rr;
-                    if (gq >= n16) continue;
-                    const int q = qq[rr];
-                    const uint4* src = reinterpret_cast<const uint4*>(p.q8 + (int64_t)(q >= 0 ? q : 0) * RB);
-                    uint8_t* bs = smem + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
-#pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        uint4 v[8];
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            v[cc] = q >= 0 ? __ldg(src + 8 * h + cc) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            *reinterpret_cast<uint4*>(bs + h * QN * 128 + ((cc ^ (gq & 7)) << 4)) = v[cc];
-                    }
-                }
+                cp_async_wait_all();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(b_full(sb));

@@ -12,6 +12,51 @@ namespace fvs {
 // the row loads better than more loads per warp (measured 0.083 -> 0.070 ms at 2000 queries, NT = 256); a small batch
 // (fewer CTAs than SMs) takes NT = 1024, so that each query's ambiguous rows are spread over 32 warps.
 
+// exact fp32 dot of one fp16 row with the query: lane l owns coordinates 8l + 256c (c = 0..NCH-1, d = 256 NCH), summed
+// in c order with the expression of the generic loop in refine_kernel (so both give the same sums); the row's loads go
+// out in batches of three 16-byte loads, so that a row costs two load latencies instead of one per chunk
+template <int NCH>
+__device__ __forceinline__ float row_dot_fixed(const __half* __restrict__ h, const float* __restrict__ qrow, int lane) {
+    float acc = 0.f;
+#pragma unroll
+    for (int c0 = 0; c0 < NCH; c0 += 3) {
+        uint4 hv[3];
+#pragma unroll
+        for (int u = 0; u < 3; u++)
+            if (c0 + u < NCH) hv[u] = __ldg(reinterpret_cast<const uint4*>(h + (c0 + u) * 256 + lane * 8));
+#pragma unroll
+        for (int u = 0; u < 3; u++) {
+            if (c0 + u >= NCH) break;
+            const int cc = (c0 + u) * 256 + lane * 8;
+            const float4 qa = *reinterpret_cast<const float4*>(qrow + cc);
+            const float4 qb = *reinterpret_cast<const float4*>(qrow + cc + 4);
+            const __half2* h2 = reinterpret_cast<const __half2*>(&hv[u]);
+            float2 f0 = __half22float2(h2[0]), f1 = __half22float2(h2[1]);
+            float2 f2 = __half22float2(h2[2]), f3 = __half22float2(h2[3]);
+            acc += f0.x * qa.x + f0.y * qa.y + f1.x * qa.z + f1.y * qa.w;
+            acc += f2.x * qb.x + f2.y * qb.y + f3.x * qb.z + f3.y * qb.w;
+        }
+    }
+    return acc;
+}
+
+// the keys of entries 0..K-1 sorted in descending order by one warp (K <= 32 * PER; missing entries are key 0, below
+// every key of a float), then key number r (0-based) written to *out by the lane holding it
+template <int PER, typename T, typename KeyFn>
+__device__ __forceinline__ void warp_rth_sorted(KeyFn key, int K, int r, T* out) {
+    const int lane = threadIdx.x & 31;
+    T v[PER];
+#pragma unroll
+    for (int j = 0; j < PER; j++) {
+        const int i = lane * PER + j;
+        v[j] = i < K ? key(i) : (T)0;
+    }
+    warp_sort_regs_desc<PER>(v);
+#pragma unroll
+    for (int j = 0; j < PER; j++)
+        if (lane * PER + j == r) *out = v[j];
+}
+
 template <int NT>
 __global__ void __launch_bounds__(NT, 2048 / NT) refine_kernel(const __half* __restrict__ H, int d,
                                                             const int32_t* __restrict__ order,
@@ -44,9 +89,12 @@ __global__ void __launch_bounds__(NT, 2048 / NT) refine_kernel(const __half* __r
     }
     if (tid == 0) s_namb = 0;
     __syncthreads();
-    // (k+1)-th largest hi, k-th largest lo: by ranks when K is small (one pass, every thread), else warp selects
-    // (the rank loops are O(K^2): measured faster at K = 100, slower at K = 400)
-    if (K <= 256) {
+    // (k+1)-th largest hi, k-th largest lo: by register sorts of one warp each when K <= 128, by ranks when K <= 256,
+    // else warp selects
+    if (K <= 128) {
+        if (warp == 0) warp_rth_sorted<4, uint32_t>([&](int i) { return khi[i]; }, K, k, &s_bounds[0]);
+        if (warp == 1) warp_rth_sorted<4, uint32_t>([&](int i) { return klo[i]; }, K, k - 1, &s_bounds[1]);
+    } else if (K <= 256) {  // ranks, every thread (O(K^2))
         for (int i = tid; i < K; i += nt) {
             const uint32_t hi = khi[i], lo = klo[i];
             int rh = 0, rl = 0;
@@ -78,9 +126,26 @@ __global__ void __launch_bounds__(NT, 2048 / NT) refine_kernel(const __half* __r
     const int namb = s_namb;
     // exact fp32 dot products of the ambiguous rows (one warp per row, 8 halves per lane per step)
     const float* qrow = Q + (int64_t)q * ldq;
+    const int nch = (d & 255) == 0 ? d >> 8 : 0;
     for (int a = warp; a < namb; a += nw) {
         const int i = amb_list[a];
         const __half* h = H + (int64_t)cid[i] * d;
+        if (nch >= 1 && nch <= 8) {
+            float acc;
+            switch (nch) {
+                case 1: acc = row_dot_fixed<1>(h, qrow, lane); break;
+                case 2: acc = row_dot_fixed<2>(h, qrow, lane); break;
+                case 3: acc = row_dot_fixed<3>(h, qrow, lane); break;
+                case 4: acc = row_dot_fixed<4>(h, qrow, lane); break;
+                case 5: acc = row_dot_fixed<5>(h, qrow, lane); break;
+                case 6: acc = row_dot_fixed<6>(h, qrow, lane); break;
+                case 7: acc = row_dot_fixed<7>(h, qrow, lane); break;
+                default: acc = row_dot_fixed<8>(h, qrow, lane); break;
+            }
+            acc = warp_sum(acc);
+            if (lane == 0) score[i] = acc;
+            continue;
+        }
         float acc = 0.f;
         for (int c0 = lane * 8; c0 < d; c0 += 256) {
             const uint4 hv = *reinterpret_cast<const uint4*>(h + c0);
@@ -96,16 +161,34 @@ __global__ void __launch_bounds__(NT, 2048 / NT) refine_kernel(const __half* __r
         if (lane == 0) score[i] = acc;
     }
     __syncthreads();
-    // final top-k by (score desc, id asc): by ranks when K is small (ties of equal keys by index), else on warp 0 the
-    // k-th largest score key, then id order among ties
-    if (K <= 256) {
+    // final top-k by (score desc, id asc; keys are unique): a register sort of one warp when K <= 128, by ranks when
+    // K <= 256, else on warp 0 the k-th largest score key, then id order among ties
+    auto fkey = [&](int i) {
+        return ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
+    };
+    if (K <= 128) {
+        if (warp == 0) {
+            {
+                unsigned long long v[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++) v[j] = lane * 4 + j < K ? fkey(lane * 4 + j) : 0ull;
+                warp_sort_regs_desc<4>(v);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const int r = lane * 4 + j;
+                    if (r < k) {
+                        I[(int64_t)q * k + r] = (int32_t)(0xffffffffu - (uint32_t)v[j]);
+                        if (score_k) score_k[(int64_t)q * k + r] = o2f((uint32_t)(v[j] >> 32));
+                    }
+                }
+            }
+        }
+    } else if (K <= 256) {
         for (int i = tid; i < K; i += nt) {
-            const unsigned long long ki =
-                ((unsigned long long)f2o(score[i]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[i]);
+            const unsigned long long ki = fkey(i);
             int r = 0;
             for (int j = 0; j < K && r < k; j++) {
-                const unsigned long long kj =
-                    ((unsigned long long)f2o(score[j]) << 32) | (unsigned long long)(0xffffffffu - (uint32_t)cid[j]);
+                const unsigned long long kj = fkey(j);
                 r += (kj > ki) || (kj == ki && j < i);
             }
             if (r < k) {

@@ -15,12 +15,13 @@
 // the next tile's first chunks overlaps the MMAs on the last chunks of the current one.
 // Warp roles (640 threads):
 //   warps 0-3   : decode (warp w: tile rows 32w..32w+31); lane 0 of warp 0 also takes cells (atomicAdd on sched[0])
-//                 and publishes the work items one ahead, like the producer of fvs_i8_scan_cells
+//                 and publishes the work items up to AHEAD beyond the one being decoded, so that the gathers of the
+//                 next items start early
 //   warp 4      : TMEM allocation; lane 0 issues tcgen05.mma.kind::f16 (M=128 rows, N=16..64 queries, K=16) per
 //                 chunk and sub-tile, commits a chunk slot once its MMAs are done and a sub-tile's accumulator after
 //                 its last chunk
-//   warps 5-6   : gather: fp16 query rows picked by qid into the swizzled layout; column metadata (qid, pair constant,
-//                 threshold) into one of MS slots
+//   warps 5-6   : gather: fp16 query rows picked by qid, copied with cp.async (a sub-tile's 64 rows in flight at once)
+//                 into the swizzled layout; column metadata (qid, pair constant, threshold) into one of MS slots
 //   warp 7      : idle (the epilogue warpgroups start on a TMEM lane-quarter boundary)
 //   warps 8-19  : three epilogue warpgroups, units alternating between them
 // The last CTA to finish resets sched[0..1].  Every mbarrier wait is bounded; on expiry the CTA raises `status`,
@@ -49,6 +50,7 @@ constexpr int EPI_GROUPS = 3;
 constexpr int GATHER_WARPS = 2;
 constexpr int DEC_WARPS = 4;
 constexpr int MAX_L = 10;
+constexpr int AHEAD = 4;    // work items published ahead of the one being decoded (so that gathers start early)
 constexpr int W_DEC = 0, W_MMA = W_DEC + DEC_WARPS, W_GATHER = W_MMA + 1, W_EPI = 8;
 constexpr int NWARPS = W_EPI + 4 * EPI_GROUPS;
 constexpr int NTHREADS = 32 * NWARPS;
@@ -77,8 +79,9 @@ constexpr int NBAR = 2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + 2 * M
 constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem base, abort flag
 constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
-// MMA thread, gather warps, decode warps 1.. (warp 0 publishes the items), epilogue warps
-constexpr uint32_t I_CONSUMERS = 1 + GATHER_WARPS + (DEC_WARPS - 1) + 4 * EPI_GROUPS;
+// MMA thread, gather warps, decode warps, epilogue warps
+constexpr uint32_t I_CONSUMERS = 1 + GATHER_WARPS + DEC_WARPS + 4 * EPI_GROUPS;
+static_assert(AHEAD + 2 <= I_STAGES, "the publisher never waits for a slot it has yet to consume itself");
 
 struct Params {
     const __half* Qh;
@@ -139,19 +142,6 @@ __device__ __forceinline__ uint32_t select32(const uint32_t (&a)[32], int jj) {
 #pragma unroll
     for (int i = 0; i < 2; i++) t2[i] = (jj & 8) ? t4[2 * i + 1] : t4[2 * i];
     return (jj & 16) ? t2[1] : t2[0];
-}
-
-__device__ __forceinline__ Item bcast_item(const Item& it) {
-    Item o;
-    o.cell = __shfl_sync(0xffffffffu, it.cell, 0);
-    o.cs = __shfl_sync(0xffffffffu, it.cs, 0);
-    o.ce = __shfl_sync(0xffffffffu, it.ce, 0);
-    o.first = __shfl_sync(0xffffffffu, it.first, 0);
-    o.ntiles = __shfl_sync(0xffffffffu, it.ntiles, 0);
-    o.qoff = __shfl_sync(0xffffffffu, it.qoff, 0);
-    o.nq = __shfl_sync(0xffffffffu, it.nq, 0);
-    o.nsub = __shfl_sync(0xffffffffu, it.nsub, 0);
-    return o;
 }
 
 // the fields of one cell the producer needs, loaded in stages so that no load is waited on in the iteration that
@@ -325,22 +315,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
             }
             return make_item(cur, g);
         };
-        // item n + 1, one ahead of the tiles of item n: warp 0 produces it, the other decode warps read it
-        int n = 0;
-        auto get_item = [&](bool first_call, Item& it) -> bool {
-            bool ok = true;
-            if (dw == 0) {
-                if (lane == 0) {
-                    it = produce(first_call);
-                    ok = push(it);
-                }
-                ok = __shfl_sync(0xffffffffu, ok, 0);
-                it = bcast_item(it);
-            } else {
-                ok = read_item(first_call ? 0 : n + 1, it, true);
-                if (ok && lane == 0) mbar_arrive(i_empty((first_call ? 0 : n + 1) % I_STAGES));
+        // warp 0 (lane 0) publishes items up to AHEAD beyond the one being decoded; every decode warp reads them from the
+        // ring in order
+        bool more = true, first_call = true;
+        auto publish_until = [&](int upto) -> bool {
+            while (more && ni <= upto) {
+                const Item nx = produce(first_call);
+                first_call = false;
+                if (!push(nx)) return false;
+                if (nx.nsub == 0) more = false;
             }
-            return ok;
+            return true;
+        };
+        auto publish = [&](int upto) -> bool {
+            bool r = true;
+            if (dw == 0 && lane == 0) r = publish_until(upto);
+            return __shfl_sync(0xffffffffu, r, 0);
+        };
+        auto get_item = [&](int m, Item& itm) -> bool {
+            const bool r = read_item(m, itm, true);
+            if (r && lane == 0) mbar_arrive(i_empty(m % I_STAGES));
+            return r;
         };
         auto load_words = [&](const Item& it, int t, uint32_t (&w)[NWORDS]) {
             const int row = it.first + t * TILE_ROWS + r;
@@ -349,16 +344,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
 #pragma unroll
             for (int i = 0; i < NWORDS; i++) w[i] = v ? __ldg(src + i) : 0u;
         };
-
+        int n = 0;
         Item it;
-        bool ok = get_item(true, it);
+        bool ok = publish(AHEAD) && get_item(0, it);
         int cslot = 0;
         uint32_t cph = 0;
         uint32_t w[NWORDS], wn[NWORDS];
         if (ok) load_words(it, 0, w);
         while (ok && it.nsub > 0) {
             Item itn;
-            if (!get_item(false, itn)) break;
+            if (!publish(n + 1 + AHEAD) || !get_item(n + 1, itn)) break;
             for (int t = 0; t < it.ntiles; t++) {
                 // words of the tile after this one (this item's next tile, else the next item's first)
                 if (t + 1 < it.ntiles)
@@ -474,7 +469,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                 const int sb = nb % B_STAGES, sm = nb % MS;
                 const int nq = min(QN, it.nq - s * QN);
                 const int n16 = (nq + 15) & ~15;
-                // the sub-tile's query ids, pair constants and thresholds (loaded before the slot waits)
+                // the sub-tile's query ids and pair constants; its rows are copied with cp.async (all of them in flight
+                // at once, zero rows past nq) while the thresholds load and the metadata slot is filled
                 int qq[2];
                 float qcv[2], thv[2];
 #pragma unroll
@@ -483,9 +479,27 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                     qq[rr] = gq < nq ? p.qid[it.qoff + s * QN + gq] : -1;
                     qcv[rr] = gq < nq ? p.qcp[it.qoff + s * QN + gq] : 0.f;
                 }
+                if (!warp_wait(b_empty(sb), ((nb / B_STAGES) & 1) ^ 1, abort, WL)) {
+                    ok = false;
+                    break;
+                }
+#pragma unroll
+                for (int rr = 0; rr < 2; rr++) {
+                    const int gq = lane + 32 * rr;
+                    if (gq >= n16) continue;
+                    const int q = qq[rr];
+                    const uint4* src = reinterpret_cast<const uint4*>(p.Qh + (int64_t)(q >= 0 ? q : 0) * R);
+                    const uint32_t bs = sbase + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
+#pragma unroll
+                    for (int c = 0; c < KCH; c++)
+#pragma unroll
+                        for (int cc = 0; cc < 8; cc++)
+                            cp_async16(bs + c * QN * 128 + ((cc ^ (gq & 7)) << 4), src + 8 * c + cc, q >= 0);
+                }
 #pragma unroll
                 for (int rr = 0; rr < 2; rr++) thv[rr] = (MODE && qq[rr] >= 0) ? p.t0[qq[rr]] : 0.f;
                 if (!warp_wait(m_empty(sm), ((nb / MS) & 1) ^ 1, abort, WL)) {
+                    cp_async_wait_all();  // no copy into shared memory stays in flight
                     ok = false;
                     break;
                 }
@@ -500,28 +514,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(m_full(sm));
-                if (!warp_wait(b_empty(sb), ((nb / B_STAGES) & 1) ^ 1, abort, WL)) {
-                    ok = false;
-                    break;
-                }
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int gq = lane + 32 * rr;
-                    if (gq >= n16) continue;
-                    const int q = qq[rr];
-                    const uint4* src = reinterpret_cast<const uint4*>(p.Qh + (int64_t)(q >= 0 ? q : 0) * R);
-                    uint8_t* bs = smem + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
-#pragma unroll
-                    for (int c = 0; c < KCH; c++) {
-                        uint4 v[8];
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            v[cc] = q >= 0 ? __ldg(src + 8 * c + cc) : make_uint4(0, 0, 0, 0);
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            *reinterpret_cast<uint4*>(bs + c * QN * 128 + ((cc ^ (gq & 7)) << 4)) = v[cc];
-                    }
-                }
+                cp_async_wait_all();
                 asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                 __syncwarp();
                 if (lane == 0) mbar_arrive(b_full(sb));

@@ -414,10 +414,11 @@ class EngineB200I8:
                    float(z), k, ptr(Qf), Qf.shape[1], ptr(ids), ptr(I), ptr(reads), ptr(score_k))
         return I, reads, ids, score_k
 
-    def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None, Qh=None):
+    def _finish(self, Qb, QC, pos, ok, ncnt, K, z, k, half=None, Qh=None, Zq=None):
         """`throughput/enginei8.py:80-95`."""
         half = self.LUTH if half is None else half
-        Zq = self.rotated_query(Qb, Qh)
+        if Zq is None:
+            Zq = self.rotated_query(Qb, Qh)
         est, sd = self.score_lut_zq(QC, pos, Zq, ncnt, half)
         I, reads, ids, score_k = self.refine(Qb, pos, est, sd, z, k)
         self._last.update(est=est, sd=sd, Zq=Zq, score_k=score_k)
@@ -557,7 +558,7 @@ class EngineB200I8:
         torch.cuda.current_stream().synchronize()                # the only synchronisation
         if int(hst[0]) != 0:
             self.status.zero_()                                   # the next search starts clean
-            raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
+            raise _lib.FvsError("stage-1 scan: a bounded device wait expired (status flag set)")
         in_graph = self.FB_INGRAPH and B >= self.FB_MIN_BATCH
         if in_graph:
             self.nbad += int(hst[1])                   # recomputed inside the graph (or below, beyond capacity)
@@ -610,7 +611,7 @@ class EngineB200I8:
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         if h[0, 1] != 0:
             self.status.zero_()
-            raise _lib.FvsError("int8 scan: a bounded device wait expired (status flag set)")
+            raise _lib.FvsError("stage-1 scan: a bounded device wait expired (status flag set)")
         out = h[:, 2:].copy()
         if not h[:, 0].all():
             bad = np.nonzero(h[:, 0] == 0)[0]
