@@ -8,9 +8,10 @@
 // Launch 2, a grid over the pairs: every CTA scans the per-cell counts (cur1 + cur2) into offsets in shared memory,
 // then places its pairs: first-pass pairs of cell c at coff[c] + r, the others at coff[c] + cur1[c] + r (each cell's
 // first-pass pairs first, the layout of fvs_pairs_split), writes qid, the pair constant float(QM[q, c]) * mnorm[c] and
-// the first pass's pair slots, and the plain cell into probe.  CTA 0 also writes coff / ccnt / ccnt1, the two
-// passes' cell lists for fvs_i8_scan_cells (order given, non-empty cells) and clears the caller's counters.  The last
-// CTA to finish clears the cursors, so every call leaves them zero for the next.
+// the first pass's pair slots, and the plain cell into probe.  One more CTA (the last) places no pairs: it writes
+// coff / ccnt / ccnt1, the two passes' cell lists for fvs_i8_scan_cells (order given, non-empty cells) and clears the
+// caller's counters, beside the placing CTAs.  The last CTA to finish clears the cursors, so every call leaves them
+// zero for the next.
 #include "fvs_common.cuh"
 
 namespace fvs {
@@ -118,7 +119,9 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
     const int tid = threadIdx.x;
     scan_counts(cur1, cur2, NC, s_coff);
     const int64_t n = (int64_t)B * nprobe;
-    for (int64_t i = (int64_t)blockIdx.x * PLACE_THREADS + tid; i < n; i += (int64_t)gridDim.x * PLACE_THREADS) {
+    const int nplace = gridDim.x - 1;  // placing CTAs; the last one keeps the books
+    for (int64_t i = (int64_t)blockIdx.x * PLACE_THREADS + tid; blockIdx.x < nplace && i < n;
+         i += (int64_t)nplace * PLACE_THREADS) {
         const int64_t v = probe[i];
         const int c = (int)(v & 0xffff), r = (int)(v >> 32);
         const int q = (int)(i / nprobe), j = (int)(i - (int64_t)q * nprobe);
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
         if (j < n1 && o.slot) o.slot[(int64_t)q * n1 + j] = pos;
         probe[i] = c;
     }
-    if (blockIdx.x == 0) {
+    if (blockIdx.x == nplace) {
         for (int c = tid; c < NC; c += PLACE_THREADS) {
             const int a = cur1[c], b = cur2[c];
             o.coff[c] = s_coff[c];
@@ -224,12 +227,13 @@ extern "C" int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, i
     const int64_t npairs = (int64_t)B * nprobe;
     const int nsm = fvs_sm_count();
     int grid = (int)((npairs + PLACE_THREADS * 2 - 1) / (PLACE_THREADS * 2));
-    grid = grid < 1 ? 1 : grid > nsm ? nsm : grid;
+    grid = grid > nsm - 1 ? nsm - 1 : grid;
+    grid = grid < 1 ? 1 : grid;  // placing CTAs, plus the bookkeeping one
     const size_t sm = (size_t)NC * sizeof(int);
     cudaError_t e = fvs_ensure_smem((const void*)pairs_place_kernel, sm);
     if (e != cudaSuccess) return (int)e;
     PlaceOut o{qid, coff, ccnt, ccnt1, slot, list1, list, nlist, zero, done, qcp, nzero};
-    pairs_place_kernel<<<grid, PLACE_THREADS, sm, stream>>>(probe, B, nprobe, n1, NC, (const __half*)QM, mnorm, order,
+    pairs_place_kernel<<<grid + 1, PLACE_THREADS, sm, stream>>>(probe, B, nprobe, n1, NC, (const __half*)QM, mnorm, order,
                                                             cur1, cur2, o);
     return fvs_launch_status();
 }

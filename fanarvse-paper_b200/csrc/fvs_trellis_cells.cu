@@ -6,24 +6,23 @@
 //   value_j = fp16(tab[state_j]),  state_j = ((w[j/32] << 32 | w[j/32+1]) >> (64 - L - j%32)) & (2^L - 1),
 //   est = scale1[n] * dot(fp16 q', value) + qcp   (dot accumulated in fp32, product and sum rounded separately),
 // then block maxima per 32-row block (mode 0, first pass) or the threshold emit est >= t0[q] (mode 1).
-// The work is organised like fvs_i8_scan_cells: cells handed out dynamically (largest first), a cell's queries (groups
-// of up to RSUB sub-tiles of QN) gathered once and held while its 128-row tiles pass, TMEM accumulators in a ring,
-// three epilogue warpgroups.  The code tile is not copied but decoded in the CTA: each decode lane owns one tile row,
-// reads its row's words (prefetched one tile ahead) and writes the row's 256 fp16 values, two per lookup of a table of
+// Work items are (cell, group of up to QN = 128 of its queries), handed out dynamically (cells largest first).  An
+// item's queries are gathered once and held while the cell's 128-row tiles pass; each tile x item is ONE sequence of
+// 16 tcgen05.mma.kind::f16 (M = 128 rows, N = the item's queries rounded up to 16, K = 16 each), since the issue cost of
+// an MMA hardly depends on N.  The code tile is not copied but decoded in the CTA: four decode warps, one tile row per
+// lane, read the row's words (prefetched one tile ahead) and write its 256 fp16 values, two per lookup of a table of
 // fp16 value pairs indexed by (L+1)-bit windows, straight into the canonical K-major 128 B-swizzled layout the MMA
-// reads.  The tile is decoded and consumed in K-chunks of 64 values through a ring of AC chunk slots, so the decode of
-// the next tile's first chunks overlaps the MMAs on the last chunks of the current one.
+// reads.  The tile moves in K-chunks of 64 values through a ring of AC chunk slots, so decode and MMAs overlap chunk by
+// chunk.
 // Warp roles (640 threads):
-//   warps 0-3   : decode (warp w: tile rows 32w..32w+31); lane 0 of warp 0 also takes cells (atomicAdd on sched[0])
-//                 and publishes the work items up to AHEAD beyond the one being decoded, so that the gathers of the
-//                 next items start early
-//   warp 4      : TMEM allocation; lane 0 issues tcgen05.mma.kind::f16 (M=128 rows, N=16..64 queries, K=16) per
-//                 chunk and sub-tile, commits a chunk slot once its MMAs are done and a sub-tile's accumulator after
-//                 its last chunk
-//   warps 5-6   : gather: fp16 query rows picked by qid, copied with cp.async (a sub-tile's 64 rows in flight at once)
-//                 into the swizzled layout; column metadata (qid, pair constant, threshold) into one of MS slots
-//   warp 7      : idle (the epilogue warpgroups start on a TMEM lane-quarter boundary)
-//   warps 8-19  : three epilogue warpgroups, units alternating between them
+//   warps 0-3   : decode
+//   warp 4      : TMEM allocation; lane 0 issues the MMAs per chunk, commits a chunk slot back once its MMAs are done
+//                 and an accumulator after the tile's last chunk
+//   warps 5-6   : gather, items alternating: fp16 query rows picked by qid, copied with cp.async (an item's rows in
+//                 flight at once) into the swizzled layout; column metadata (qid, pair constant, threshold)
+//   warp 7      : lane 0 takes cells (atomicAdd on sched[0], cell fields loaded ahead in stages) and publishes the
+//                 work items in a ring of I_STAGES slots
+//   warps 8-19  : three epilogue warpgroups, tiles alternating between them
 // The last CTA to finish resets sched[0..1].  Every mbarrier wait is bounded; on expiry the CTA raises `status`,
 // drains the MMAs it issued, frees TMEM and returns.
 #include <cuda.h>
@@ -36,39 +35,38 @@ namespace tcells {
 using namespace fvs::tcg;
 
 constexpr int TILE_ROWS = 128;
-constexpr int QN = 64;      // queries per sub-tile
+constexpr int QN = 128;     // queries per work item (one B operand, one accumulator per tile)
 constexpr int R = 256;      // decoded values per row
 constexpr int KCH = 4;      // K-chunks of 64 fp16 values (128 B per row) per tile
-constexpr int NWORDS = R / 32 + 1;
+constexpr int NWORDS = R / 32 + 1;  // words a lane reads for its row
 constexpr int AC = 5;       // chunk slots
-constexpr int B_STAGES = 4;
-constexpr int RSUB = 2;     // sub-tiles of one work item (held through the item's tiles)
-constexpr int T_STAGES = 8;
+constexpr int B_STAGES = 2;
+constexpr int T_STAGES = 4;
 constexpr int I_STAGES = 8;
-constexpr int MS = 8;       // column-metadata slots (one per sub-tile, held until the sub-tile's last unit is done)
+constexpr int MS = 4;       // column-metadata slots (one per item, held until the item's last tile is done)
 constexpr int EPI_GROUPS = 3;
 constexpr int GATHER_WARPS = 2;
 constexpr int DEC_WARPS = 4;
 constexpr int MAX_L = 10;
-constexpr int AHEAD = 4;    // work items published ahead of the one being decoded (so that gathers start early)
-constexpr int W_DEC = 0, W_MMA = W_DEC + DEC_WARPS, W_GATHER = W_MMA + 1, W_EPI = 8;
+constexpr int W_MMA = 4, W_GATHER = 5, W_PROD = 7, W_EPI = 8;
 constexpr int NWARPS = W_EPI + 4 * EPI_GROUPS;
 constexpr int NTHREADS = 32 * NWARPS;
 constexpr uint32_t TMEM_COLS = T_STAGES * QN;
-static_assert(B_STAGES >= 2 * RSUB, "a work item's sub-tiles and the next item's fit together");
-static_assert(W_EPI % 4 == 0 && W_EPI >= W_GATHER + GATHER_WARPS, "epilogue warpgroups start on a TMEM lane quarter");
+static_assert(W_EPI % 4 == 0, "epilogue warpgroups start on a TMEM lane quarter");
 static_assert(DEC_WARPS * 32 == TILE_ROWS, "one decode lane per tile row");
+static_assert(B_STAGES == GATHER_WARPS, "gather warp g fills B stage g");
+static_assert(TMEM_COLS <= 512, "tensor memory columns");
 
 struct Item {
-    int cell, cs, ce, first, ntiles, qoff, nq, nsub;  // nsub == 0: no more work
+    int cell, cs, ce, first, ntiles, qoff, nq, live;  // live == 0: no more work
 };
 
 // shared-memory carve-up (offsets from a 1024-byte aligned base)
 constexpr int CH_BYTES = TILE_ROWS * 128;  // one K-chunk of a decoded tile
-constexpr int B_BYTES = KCH * QN * 128;    // one query sub-tile: 4 K-chunks x 8 KB
+constexpr int B_BYTES = KCH * QN * 128;    // one item's queries: 4 K-chunks x 16 KB
 constexpr int A_OFF = 0;
 constexpr int B_OFF = A_OFF + AC * CH_BYTES;
-constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;  // per sub-tile slot: qid, qcp, t0 of QN columns
+constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;  // per item slot: qid, qcp, t0 of QN columns
 constexpr int META_W = 3 * QN * 4;
 constexpr int COL_OFF = META_OFF + MS * META_W;               // per epilogue warp: 32 column masks + 32 bases
 constexpr int MCNT_OFF = COL_OFF + 4 * EPI_GROUPS * 64 * 4;   // per metadata slot: epilogue warps done with it
@@ -81,7 +79,6 @@ constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
 static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
 // MMA thread, gather warps, decode warps, epilogue warps
 constexpr uint32_t I_CONSUMERS = 1 + GATHER_WARPS + DEC_WARPS + 4 * EPI_GROUPS;
-static_assert(AHEAD + 2 <= I_STAGES, "the publisher never waits for a slot it has yet to consume itself");
 
 struct Params {
     const __half* Qh;
@@ -156,23 +153,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t sbase = saddr(smem);
-    auto c_full = [&](int s) { return sbase + BAR_OFF + 8 * s; };
-    auto c_empty = [&](int s) { return sbase + BAR_OFF + 8 * (AC + s); };
-    auto b_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + s); };
-    auto b_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + B_STAGES + s); };
-    auto t_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + s); };
-    auto t_empty = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + T_STAGES + s); };
-    auto i_full = [&](int s) { return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + s); };
-    auto i_empty = [&](int s) {
-        return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + I_STAGES + s);
-    };
-    auto m_full = [&](int s) {
-        return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + s);
-    };
-    auto m_empty = [&](int s) {
-        return sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + MS + s);
-    };
-    const uint32_t d_bar = sbase + BAR_OFF + 8 * (2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + 2 * MS);
+    auto bar = [&](int i) { return sbase + BAR_OFF + 8 * i; };
+    auto c_full = [&](int s) { return bar(s); };
+    auto c_empty = [&](int s) { return bar(AC + s); };
+    auto b_full = [&](int s) { return bar(2 * AC + s); };
+    auto b_empty = [&](int s) { return bar(2 * AC + B_STAGES + s); };
+    auto t_full = [&](int s) { return bar(2 * AC + 2 * B_STAGES + s); };
+    auto t_empty = [&](int s) { return bar(2 * AC + 2 * B_STAGES + T_STAGES + s); };
+    auto i_full = [&](int s) { return bar(2 * AC + 2 * B_STAGES + 2 * T_STAGES + s); };
+    auto i_empty = [&](int s) { return bar(2 * AC + 2 * B_STAGES + 2 * T_STAGES + I_STAGES + s); };
+    auto m_full = [&](int s) { return bar(2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + s); };
+    auto m_empty = [&](int s) { return bar(2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + MS + s); };
+    const uint32_t d_bar = bar(2 * AC + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + 2 * MS);
     auto meta = [&](int slot) { return reinterpret_cast<int*>(smem + META_OFF + slot * META_W); };
     Item* items = reinterpret_cast<Item*>(smem + ITEM_OFF);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + MISC_OFF);
@@ -182,7 +174,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
     if (tid == 0) {
         for (int s = 0; s < AC; s++) {
             mbar_init(c_full(s), DEC_WARPS);  // every decode warp has written its rows of the chunk
-            mbar_init(c_empty(s), 1);         // the MMAs reading the chunk have completed
+            mbar_init(c_empty(s), 1);  // the MMAs reading the chunk have completed
         }
         for (int s = 0; s < B_STAGES; s++) {
             mbar_init(b_full(s), 1);
@@ -197,8 +189,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
             mbar_init(i_empty(s), I_CONSUMERS);
         }
         for (int s = 0; s < MS; s++) {
-            mbar_init(m_full(s), 1);   // written by the sub-tile's gather warp
-            mbar_init(m_empty(s), 1);  // released by the last epilogue warp to finish a unit of the sub-tile
+            mbar_init(m_full(s), 1);   // written by the item's gather warp
+            mbar_init(m_empty(s), 1);  // released by the last epilogue warp to finish a tile of the item
             reinterpret_cast<int*>(smem + MCNT_OFF)[s] = 0;
         }
         mbar_init(d_bar, 1);
@@ -236,124 +228,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
         if (r) it = items[s];
         return r;
     };
+    auto take_item = [&](int n, Item& it) -> bool {  // whole warp: read and release
+        const bool r = read_item(n, it, true);
+        if (r && lane == 0) mbar_arrive(i_empty(n % I_STAGES));
+        return r;
+    };
 
     bool mma_issued = false;
 
     if (warp < W_MMA) {
-        // ---- decode (warp 0, lane 0: also the item producer)
-        const int dw = warp - W_DEC;
+        // ---- decode: warp w, rows 32 w + lane of each tile
         const uint32_t* tab2 = reinterpret_cast<const uint32_t*>(smem + TAB_OFF);
         const int sh = 31 - p.L;  // a window is the top L+1 bits of a 32-bit funnel shift
-        const int r = 32 * dw + lane;
+        const int r = 32 * warp + lane;
         const int sw = r & 7;
         const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw * 128);
-
-        // producer state (lane 0 of warp 0 only)
-        const int nl = (dw == 0 && lane == 0) ? *p.nlist : 0;
-        auto grab = [&]() { return atomicAdd(p.sched, 1); };
-        auto cell_of = [&](int idx) { return idx < nl ? p.list[idx] : -1; };
-        auto fields = [&](int c) {
-            CellInfo ci{c, 0, 0, 0, 0};
-            if (c >= 0) {
-                ci.cs = (int)p.off[c];
-                ci.ce = (int)p.off[c + 1];
-                ci.qn = p.ccnt[c];
-                ci.qoff = p.coff[c];
-            }
-            return ci;
-        };
-        CellInfo pre{-1, 0, 0, 0, 0}, cur{-1, 0, 0, 0, 0};
-        int cn = -1, idxn = 0, g = 0, ni = 0;
-        auto next_cell = [&]() {
-            const CellInfo c = pre;
-            pre = fields(cn);
-            cn = cell_of(idxn);
-            idxn = grab();
-            return c;
-        };
-        auto make_item = [&](const CellInfo& ci, int grp) {
-            Item it;
-            if (ci.cell < 0) {
-                it = Item{-1, 0, 0, 0, 0, 0, 0, 0};
-            } else {
-                const int first = ci.cs & ~31;
-                const int q0 = grp * RSUB * QN;
-                const int nq = min(RSUB * QN, ci.qn - q0);
-                it = Item{ci.cell, ci.cs, ci.ce, first, (ci.ce - first + TILE_ROWS - 1) / TILE_ROWS, ci.qoff + q0, nq,
-                          (nq + QN - 1) / QN};
-            }
-            return it;
-        };
-        auto push = [&](const Item& it) -> bool {
-            const int s = ni % I_STAGES;
-            if (!mbar_wait(i_empty(s), ((ni / I_STAGES) & 1) ^ 1, abort, WL)) return false;
-            items[s] = it;
-            mbar_arrive(i_full(s));  // release: the item's fields are visible to whoever acquires the phase
-            ni++;
-            return true;
-        };
-        // cells with no pairs (not listed) or no rows (probed, but nothing to scan) are skipped
-        auto idle = [&](const CellInfo& ci) { return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs); };
-        // the producer's next item: the next group of the current cell, else the first group of the next busy cell
-        auto produce = [&](bool first_call) -> Item {
-            if (first_call) {
-                pre = fields(cell_of(grab()));
-                cn = cell_of(grab());
-                idxn = grab();
-                g = 0;
-                do {
-                    cur = next_cell();
-                } while (idle(cur));
-            } else {
-                g++;
-                if (!(cur.cell >= 0 && g * RSUB * QN < cur.qn)) {
-                    g = 0;
-                    do {
-                        cur = next_cell();
-                    } while (idle(cur));
-                }
-            }
-            return make_item(cur, g);
-        };
-        // warp 0 (lane 0) publishes items up to AHEAD beyond the one being decoded; every decode warp reads them from the
-        // ring in order
-        bool more = true, first_call = true;
-        auto publish_until = [&](int upto) -> bool {
-            while (more && ni <= upto) {
-                const Item nx = produce(first_call);
-                first_call = false;
-                if (!push(nx)) return false;
-                if (nx.nsub == 0) more = false;
-            }
-            return true;
-        };
-        auto publish = [&](int upto) -> bool {
-            bool r = true;
-            if (dw == 0 && lane == 0) r = publish_until(upto);
-            return __shfl_sync(0xffffffffu, r, 0);
-        };
-        auto get_item = [&](int m, Item& itm) -> bool {
-            const bool r = read_item(m, itm, true);
-            if (r && lane == 0) mbar_arrive(i_empty(m % I_STAGES));
-            return r;
-        };
         auto load_words = [&](const Item& it, int t, uint32_t (&w)[NWORDS]) {
             const int row = it.first + t * TILE_ROWS + r;
-            const bool v = it.nsub > 0 && row >= it.cs && row < it.ce;
+            const bool v = it.live && row >= it.cs && row < it.ce;
             const uint32_t* src = p.words + (int64_t)(v ? row : 0) * p.W;
 #pragma unroll
             for (int i = 0; i < NWORDS; i++) w[i] = v ? __ldg(src + i) : 0u;
         };
-        int n = 0;
-        Item it;
-        bool ok = publish(AHEAD) && get_item(0, it);
-        int cslot = 0;
+        int n = 0, cslot = 0;
         uint32_t cph = 0;
+        Item it;
+        bool ok = take_item(0, it);
         uint32_t w[NWORDS], wn[NWORDS];
         if (ok) load_words(it, 0, w);
-        while (ok && it.nsub > 0) {
+        while (ok && it.live) {
             Item itn;
-            if (!publish(n + 1 + AHEAD) || !get_item(n + 1, itn)) break;
+            if (!take_item(n + 1, itn)) break;
             for (int t = 0; t < it.ntiles; t++) {
                 // words of the tile after this one (this item's next tile, else the next item's first)
                 if (t + 1 < it.ntiles)
@@ -402,247 +307,274 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
         }
     } else if (warp == W_MMA) {
         if (lane == 0) {
-            int nb = 0, nu = 0, cslot = 0;
+            int nu = 0, cslot = 0;
             uint32_t cph = 0;
             for (int n = 0;; n++) {
                 Item it;
                 if (!read_item(n, it, false)) break;
                 mbar_arrive(i_empty(n % I_STAGES));
-                if (it.nsub == 0) break;
+                if (!it.live) break;
+                const int sb = n % B_STAGES;
+                const uint32_t idesc = f16_idesc((it.nq + 15) & ~15);
+                const uint32_t bbase = sbase + B_OFF + sb * B_BYTES;
                 bool ok = true;
-                for (int t = 0; t < it.ntiles && ok; t++) {
-                    for (int c = 0; c < KCH && ok; c++) {
-                        if (!mbar_wait(c_full(cslot), cph, abort, WL)) {
+                for (int t = 0; t < it.ntiles && ok; t++, nu++) {
+                    const int st = nu % T_STAGES;
+                    const uint32_t d = tmem + (uint32_t)(st * QN);
+                    for (int c = 0; c < KCH; c++) {
+                        if (!mbar_wait(c_full(cslot), cph, abort, WL) ||
+                            (c == 0 && t == 0 && !mbar_wait(b_full(sb), (n / B_STAGES) & 1, abort, WL)) ||
+                            (c == 0 && !mbar_wait(t_empty(st), ((nu / T_STAGES) & 1) ^ 1, abort, WL))) {
                             ok = false;
                             break;
                         }
                         tc_fence_after();
                         const uint32_t abase = sbase + A_OFF + cslot * CH_BYTES;
-                        for (int s = 0; s < it.nsub; s++) {
-                            const int sb = (nb + s) % B_STAGES, st = (nu + s) % T_STAGES;
-                            if (c == 0) {
-                                if ((t == 0 && !mbar_wait(b_full(sb), ((nb + s) / B_STAGES) & 1, abort, WL)) ||
-                                    !mbar_wait(t_empty(st), (((nu + s) / T_STAGES) & 1) ^ 1, abort, WL)) {
-                                    ok = false;
-                                    break;
-                                }
-                                tc_fence_after();
-                            }
-                            const int nq = min(QN, it.nq - s * QN);
-                            const uint32_t idesc = f16_idesc((nq + 15) & ~15);
-                            const uint32_t d = tmem + (uint32_t)(st * QN);
-                            const uint32_t bb = sbase + B_OFF + sb * B_BYTES + c * QN * 128;
+                        const uint32_t bb = bbase + c * QN * 128;
 #pragma unroll
-                            for (int kk = 0; kk < 4; kk++)
-                                mma_f16(d, sw128_desc(abase + kk * 32), sw128_desc(bb + kk * 32), idesc,
-                                        (c > 0 || kk > 0) ? 1u : 0u);
-                            mma_issued = true;
-                            if (c == KCH - 1) mma_commit(t_full(st));
-                        }
-                        if (!ok) break;
+                        for (int kk = 0; kk < 4; kk++)
+                            mma_f16(d, sw128_desc(abase + kk * 32), sw128_desc(bb + kk * 32), idesc,
+                                    (c > 0 || kk > 0) ? 1u : 0u);
+                        mma_issued = true;
+                        if (c == KCH - 1) mma_commit(t_full(st));
                         mma_commit(c_empty(cslot));  // the chunk slot is free once these MMAs complete
                         if (++cslot == AC) {
                             cslot = 0;
                             cph ^= 1u;
                         }
                     }
-                    nu += it.nsub;
                 }
                 if (!ok) break;
-                for (int s = 0; s < it.nsub; s++) mma_commit(b_empty((nb + s) % B_STAGES));
-                nb += it.nsub;
+                mma_commit(b_empty(sb));  // the item's queries are free once its last MMAs complete
             }
         }
         __syncwarp();
-    } else if (warp < W_GATHER + GATHER_WARPS) {
-        // ---- query gather: the item's sub-tiles alternate between the gather warps; lane l fills rows l, l + 32
+    } else if (warp < W_PROD) {
+        // ---- query gather: items alternate between the gather warps (warp g fills B stage g); lane l fills rows
+        //      l + 32 rr
         const int gw = warp - W_GATHER;
-        int nb = 0;
         for (int n = 0;; n++) {
             Item it;
-            if (!read_item(n, it, true)) break;
-            if (lane == 0) mbar_arrive(i_empty(n % I_STAGES));
-            if (it.nsub == 0) break;
-            bool ok = true;
-            for (int s = 0; s < it.nsub; s++, nb++) {
-                if (nb % GATHER_WARPS != gw) continue;
-                const int sb = nb % B_STAGES, sm = nb % MS;
-                const int nq = min(QN, it.nq - s * QN);
-                const int n16 = (nq + 15) & ~15;
-                // the sub-tile's query ids and pair constants; its rows are copied with cp.async (all of them in flight
-                // at once, zero rows past nq) while the thresholds load and the metadata slot is filled
-                int qq[2];
-                float qcv[2], thv[2];
+            if (!take_item(n, it)) break;
+            if (!it.live) break;
+            if (n % GATHER_WARPS != gw) continue;
+            const int sb = n % B_STAGES, sm = n % MS;
+            const int nq = it.nq, n16 = (it.nq + 15) & ~15;
+            // the item's query ids and pair constants; its rows are copied with cp.async (all of them in flight at
+            // once, zero rows past nq) while the thresholds load and the metadata slot is filled
+            int qq[4];
+            float qcv[4], thv[4];
 #pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int gq = lane + 32 * rr;
-                    qq[rr] = gq < nq ? p.qid[it.qoff + s * QN + gq] : -1;
-                    qcv[rr] = gq < nq ? p.qcp[it.qoff + s * QN + gq] : 0.f;
-                }
-                if (!warp_wait(b_empty(sb), ((nb / B_STAGES) & 1) ^ 1, abort, WL)) {
-                    ok = false;
-                    break;
-                }
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int gq = lane + 32 * rr;
-                    if (gq >= n16) continue;
-                    const int q = qq[rr];
-                    const uint4* src = reinterpret_cast<const uint4*>(p.Qh + (int64_t)(q >= 0 ? q : 0) * R);
-                    const uint32_t bs = sbase + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
-#pragma unroll
-                    for (int c = 0; c < KCH; c++)
-#pragma unroll
-                        for (int cc = 0; cc < 8; cc++)
-                            cp_async16(bs + c * QN * 128 + ((cc ^ (gq & 7)) << 4), src + 8 * c + cc, q >= 0);
-                }
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) thv[rr] = (MODE && qq[rr] >= 0) ? p.t0[qq[rr]] : 0.f;
-                if (!warp_wait(m_empty(sm), ((nb / MS) & 1) ^ 1, abort, WL)) {
-                    cp_async_wait_all();  // no copy into shared memory stays in flight
-                    ok = false;
-                    break;
-                }
-                int* mq = meta(sm);
-                float* mc = reinterpret_cast<float*>(mq + QN);
-#pragma unroll
-                for (int rr = 0; rr < 2; rr++) {
-                    const int gq = lane + 32 * rr;
-                    mq[gq] = qq[rr];
-                    mc[gq] = qcv[rr];
-                    mc[QN + gq] = thv[rr];
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(m_full(sm));
-                cp_async_wait_all();
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                __syncwarp();
-                if (lane == 0) mbar_arrive(b_full(sb));
+            for (int rr = 0; rr < 4; rr++) {
+                const int gq = lane + 32 * rr;
+                qq[rr] = gq < nq ? p.qid[it.qoff + gq] : -1;
+                qcv[rr] = gq < nq ? p.qcp[it.qoff + gq] : 0.f;
             }
-            if (!ok) break;
+            if (!warp_wait(b_empty(sb), ((n / B_STAGES) & 1) ^ 1, abort, WL)) break;
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) {
+                const int gq = lane + 32 * rr;
+                if (gq >= n16) continue;
+                const int q = qq[rr];
+                const uint4* src = reinterpret_cast<const uint4*>(p.Qh + (int64_t)(q >= 0 ? q : 0) * R);
+                const uint32_t bs = sbase + B_OFF + sb * B_BYTES + (gq >> 3) * 1024 + (gq & 7) * 128;
+#pragma unroll
+                for (int c = 0; c < KCH; c++)
+#pragma unroll
+                    for (int cc = 0; cc < 8; cc++)
+                        cp_async16(bs + c * QN * 128 + ((cc ^ (gq & 7)) << 4), src + 8 * c + cc, q >= 0);
+            }
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) thv[rr] = (MODE && qq[rr] >= 0) ? p.t0[qq[rr]] : 0.f;
+            if (!warp_wait(m_empty(sm), ((n / MS) & 1) ^ 1, abort, WL)) {
+                cp_async_wait_all();  // no copy into shared memory stays in flight
+                break;
+            }
+            int* mq = meta(sm);
+            float* mc = reinterpret_cast<float*>(mq + QN);
+#pragma unroll
+            for (int rr = 0; rr < 4; rr++) {
+                const int gq = lane + 32 * rr;
+                mq[gq] = qq[rr];
+                mc[gq] = qcv[rr];
+                mc[QN + gq] = thv[rr];
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(m_full(sm));
+            cp_async_wait_all();
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) mbar_arrive(b_full(sb));
         }
-    } else if (warp >= W_EPI) {
-        // ---- epilogue: group eg takes the units nu = eg (mod EPI_GROUPS); warp ew = warp % 4 reads TMEM lanes
+    } else if (warp == W_PROD) {
+        if (lane == 0) {
+            const int nl = *p.nlist;
+            // cell pipeline, refilled by every next_cell(): `pre` (bounds and pair range of the next cell), `cn` (the
+            // cell after it), `idxn` (the list index after that); each call only uses values loaded by the previous
+            // call, so the producer never waits for a load it just issued
+            auto grab = [&]() { return atomicAdd(p.sched, 1); };
+            auto cell_of = [&](int idx) { return idx < nl ? p.list[idx] : -1; };
+            auto fields = [&](int c) {
+                CellInfo ci{c, 0, 0, 0, 0};
+                if (c >= 0) {
+                    ci.cs = (int)p.off[c];
+                    ci.ce = (int)p.off[c + 1];
+                    ci.qn = p.ccnt[c];
+                    ci.qoff = p.coff[c];
+                }
+                return ci;
+            };
+            CellInfo pre = fields(cell_of(grab()));
+            int cn = cell_of(grab());
+            int idxn = grab();
+            auto next_cell = [&]() {
+                const CellInfo c = pre;
+                pre = fields(cn);
+                cn = cell_of(idxn);
+                idxn = grab();
+                return c;
+            };
+            // cells with no pairs (not listed) or no rows (probed, but nothing to scan) are skipped
+            auto idle = [&](const CellInfo& ci) { return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs); };
+            CellInfo cur;
+            do {
+                cur = next_cell();
+            } while (idle(cur));
+            int g = 0;  // group of `cur` the next item covers
+            for (int ni = 0;; ni++) {
+                Item it{-1, 0, 0, 0, 0, 0, 0, 0};
+                if (cur.cell >= 0) {
+                    const int first = cur.cs & ~31;
+                    it = Item{cur.cell, cur.cs, cur.ce, first, (cur.ce - first + TILE_ROWS - 1) / TILE_ROWS,
+                              cur.qoff + g * QN, min(QN, cur.qn - g * QN), 1};
+                }
+                const int s = ni % I_STAGES;
+                if (!mbar_wait(i_empty(s), ((ni / I_STAGES) & 1) ^ 1, abort, WL)) break;
+                items[s] = it;
+                mbar_arrive(i_full(s));  // release: the item's fields are visible to whoever acquires the phase
+                if (!it.live) break;
+                if (++g * QN >= cur.qn) {
+                    g = 0;
+                    do {
+                        cur = next_cell();
+                    } while (idle(cur));
+                }
+            }
+        }
+    } else {
+        // ---- epilogue: group eg takes the tiles nu = eg (mod EPI_GROUPS); warp ew = warp % 4 reads TMEM lanes
         //      32*ew .. 32*ew+31 (tile rows)
         const int we = warp - W_EPI;
         const int eg = we / 4;
         const int ew = warp & 3;
         uint32_t* colm = reinterpret_cast<uint32_t*>(smem + COL_OFF) + we * 64;
         int* colb = reinterpret_cast<int*>(colm + 32);
-        int nu = 0, nb = 0;
+        int nu = 0;
         for (int n = 0;; n++) {
             Item it;
-            if (!read_item(n, it, true)) break;
-            if (lane == 0) mbar_arrive(i_empty(n % I_STAGES));
-            if (it.nsub == 0) break;
+            if (!take_item(n, it)) break;
+            if (!it.live) break;
             bool ok = true;
-            for (int t = 0; t < it.ntiles && ok; t++) {
+            const int nq = it.nq, sm = n % MS;
+            for (int t = 0; t < it.ntiles; t++, nu++) {
+                if (nu % EPI_GROUPS != eg) continue;
                 const int row0 = it.first + t * TILE_ROWS;
                 const int row = row0 + 32 * ew + lane;
                 const bool rvalid = row >= it.cs && row < it.ce;
                 const bool wactive = row0 + 32 * ew < it.ce;
                 const int blk_rel = (row0 + 32 * ew) / 32 - it.cs / 32;
-                for (int s = 0; s < it.nsub; s++, nu++) {
-                    if (nu % EPI_GROUPS != eg) continue;
-                    const int st = nu % T_STAGES;
-                    const int nq = min(QN, it.nq - s * QN);
-                    const int pair0 = it.qoff + s * QN;
-                    const int sm = (nb + s) % MS;
-                    const float sc = rvalid ? __half2float(p.scale1[row]) : 0.f;  // loaded before the waits
-                    if (!warp_wait(m_full(sm), ((nb + s) / MS) & 1, abort, WL) ||
-                        !warp_wait(t_full(st), (nu / T_STAGES) & 1, abort, WL)) {
-                        ok = false;
-                        break;
-                    }
-                    const int* mq = meta(sm);
-                    const float* mc = reinterpret_cast<const float*>(mq + QN);
-                    const float* mt = mc + QN;
-                    tc_fence_after();
-                    const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
-                    for (int h = 0; h * 32 < nq; h++) {
-                        uint32_t acc[32];
-                        tmem_ld32(ta + 32 * h, acc);
-                        tmem_ld_wait();
-                        if (!wactive) continue;
-                        const int nc = min(32, nq - h * 32);
-                        const float4* mc4 = reinterpret_cast<const float4*>(mc + 32 * h);
-                        if (MODE == 0) {
+                const int st = nu % T_STAGES;
+                const float sc = rvalid ? __half2float(p.scale1[row]) : 0.f;  // loaded before the waits
+                if (!warp_wait(m_full(sm), (n / MS) & 1, abort, WL) ||
+                    !warp_wait(t_full(st), (nu / T_STAGES) & 1, abort, WL)) {
+                    ok = false;
+                    break;
+                }
+                const int* mq = meta(sm);
+                const float* mc = reinterpret_cast<const float*>(mq + QN);
+                const float* mt = mc + QN;
+                tc_fence_after();
+                const uint32_t ta = tmem + ((uint32_t)(32 * ew) << 16) + (uint32_t)(st * QN);
+                for (int h = 0; h * 32 < nq; h++) {
+                    uint32_t acc[32];
+                    tmem_ld32(ta + 32 * h, acc);
+                    tmem_ld_wait();
+                    if (!wactive) continue;
+                    const int nc = min(32, nq - h * 32);
+                    const float4* mc4 = reinterpret_cast<const float4*>(mc + 32 * h);
+                    if (MODE == 0) {
 #pragma unroll
-                            for (int j4 = 0; j4 < 8; j4++) {
-                                if (4 * j4 >= nc) break;
-                                const float4 cv = mc4[j4];
-                                const float c4[4] = {cv.x, cv.y, cv.z, cv.w};
+                        for (int j4 = 0; j4 < 8; j4++) {
+                            if (4 * j4 >= nc) break;
+                            const float4 cv = mc4[j4];
+                            const float c4[4] = {cv.x, cv.y, cv.z, cv.w};
 #pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    const int jj = 4 * j4 + u;
-                                    if (jj < nc) {
-                                        const float est =
-                                            __fadd_rn(__fmul_rn(sc, __uint_as_float(acc[jj])), c4[u]);
-                                        const uint32_t m = __reduce_max_sync(0xffffffffu, rvalid ? f2o(est) : 0u);
-                                        if (lane == 0) p.bmc[(int64_t)(pair0 + 32 * h + jj) * p.MB + blk_rel] = o2f(m);
-                                    }
+                            for (int u = 0; u < 4; u++) {
+                                const int jj = 4 * j4 + u;
+                                if (jj < nc) {
+                                    const float est = __fadd_rn(__fmul_rn(sc, __uint_as_float(acc[jj])), c4[u]);
+                                    const uint32_t m = __reduce_max_sync(0xffffffffu, rvalid ? f2o(est) : 0u);
+                                    if (lane == 0) p.bmc[(int64_t)(it.qoff + 32 * h + jj) * p.MB + blk_rel] = o2f(m);
                                 }
                             }
-                        } else {
-                            const float4* mt4 = reinterpret_cast<const float4*>(mt + 32 * h);
-                            uint32_t rowmask = 0;
-#pragma unroll
-                            for (int j4 = 0; j4 < 8; j4++) {
-                                if (4 * j4 >= nc) break;
-                                const float4 cv = mc4[j4], tv = mt4[j4];
-                                const float c4[4] = {cv.x, cv.y, cv.z, cv.w};
-                                const float t4[4] = {tv.x, tv.y, tv.z, tv.w};
-#pragma unroll
-                                for (int u = 0; u < 4; u++) {
-                                    const int jj = 4 * j4 + u;
-                                    if (jj < nc) {
-                                        const float est =
-                                            __fadd_rn(__fmul_rn(sc, __uint_as_float(acc[jj])), c4[u]);
-                                        const bool keep = rvalid && est >= t4[u];
-                                        acc[jj] = __float_as_uint(est);
-                                        rowmask |= (uint32_t)keep << jj;
-                                    }
-                                }
-                            }
-                            const uint32_t mymask = transpose32(rowmask);  // lane jj: the rows keeping column jj
-                            int mybase = 0;
-                            if (mymask) mybase = atomicAdd(p.cnt + mq[32 * h + lane], __popc(mymask));
-                            colm[lane] = mymask;
-                            colb[lane] = mybase;
-                            __syncwarp();
-                            while (rowmask) {
-                                const int jj = __ffs(rowmask) - 1;
-                                rowmask &= rowmask - 1;
-                                const int j = 32 * h + jj;
-                                const float est = __uint_as_float(select32(acc, jj));
-                                const int idx = colb[jj] + __popc(colm[jj] & ((1u << lane) - 1u));
-                                if (idx < p.M) {
-                                    const int64_t o = (int64_t)mq[j] * p.M + idx;
-                                    p.bval[o] = est;
-                                    p.bpos[o] = row;
-                                }
-                            }
-                            __syncwarp();
                         }
-                    }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(t_empty(st));
-                        // the sub-tile's units (one per tile) are spread over the warpgroups, which finish in any
-                        // order: the slot is free once all 4 * ntiles warps are done with it; the last one to count
-                        // itself resets the count and releases the slot
-                        __threadfence_block();
-                        int* mcount = reinterpret_cast<int*>(smem + MCNT_OFF);
-                        if (atomicAdd(mcount + sm, 1) == 4 * it.ntiles - 1) {
-                            mcount[sm] = 0;
-                            mbar_arrive(m_empty(sm));
+                    } else {
+                        const float4* mt4 = reinterpret_cast<const float4*>(mt + 32 * h);
+                        uint32_t rowmask = 0;
+#pragma unroll
+                        for (int j4 = 0; j4 < 8; j4++) {
+                            if (4 * j4 >= nc) break;
+                            const float4 cv = mc4[j4], tv = mt4[j4];
+                            const float c4[4] = {cv.x, cv.y, cv.z, cv.w};
+                            const float t4[4] = {tv.x, tv.y, tv.z, tv.w};
+#pragma unroll
+                            for (int u = 0; u < 4; u++) {
+                                const int jj = 4 * j4 + u;
+                                if (jj < nc) {
+                                    const float est = __fadd_rn(__fmul_rn(sc, __uint_as_float(acc[jj])), c4[u]);
+                                    const bool keep = rvalid && est >= t4[u];
+                                    acc[jj] = __float_as_uint(est);
+                                    rowmask |= (uint32_t)keep << jj;
+                                }
+                            }
                         }
+                        const uint32_t mymask = transpose32(rowmask);  // lane jj: the rows keeping column jj
+                        int mybase = 0;
+                        if (mymask) mybase = atomicAdd(p.cnt + mq[32 * h + lane], __popc(mymask));
+                        colm[lane] = mymask;
+                        colb[lane] = mybase;
+                        __syncwarp();
+                        while (rowmask) {
+                            const int jj = __ffs(rowmask) - 1;
+                            rowmask &= rowmask - 1;
+                            const int j = 32 * h + jj;
+                            const float est = __uint_as_float(select32(acc, jj));
+                            const int idx = colb[jj] + __popc(colm[jj] & ((1u << lane) - 1u));
+                            if (idx < p.M) {
+                                const int64_t o = (int64_t)mq[j] * p.M + idx;
+                                p.bval[o] = est;
+                                p.bpos[o] = row;
+                            }
+                        }
+                        __syncwarp();
+                    }
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(t_empty(st));
+                    // the item's tiles are spread over the warpgroups, which finish in any order: the metadata slot is
+                    // free once all 4 * ntiles warps are done with it; the last one to count itself resets the count
+                    // and releases the slot
+                    __threadfence_block();
+                    int* mcount = reinterpret_cast<int*>(smem + MCNT_OFF);
+                    if (atomicAdd(mcount + sm, 1) == 4 * it.ntiles - 1) {
+                        mcount[sm] = 0;
+                        mbar_arrive(m_empty(sm));
                     }
                 }
             }
             if (!ok) break;
-            nb += it.nsub;
         }
     }
     // drain (a wait that ignores the abort flag): one commit after the last MMA issued has arrived, i.e. every MMA of
