@@ -290,18 +290,48 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
         else
             select_reg_cut<NT, 8>(bv, bp, n, K, sh);
     }
-    __syncthreads();
-    // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal)
-    for (int i = tid; i < K; i += NT) {
-        const unsigned long long ki = sh.sb[i];
-        int rank = 0;
-        for (int j = 0; j < K; j++) {
-            const unsigned long long kj = sh.sb[j];
-            rank += (kj > ki) || (kj == ki && j < i);
+    if (K <= 128) {
+        // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal)
+        __syncthreads();
+        for (int i = tid; i < K; i += NT) {
+            const unsigned long long ki = sh.sb[i];
+            int rank = 0;
+            for (int j = 0; j < K; j++) {
+                const unsigned long long kj = sh.sb[j];
+                rank += (kj > ki) || (kj == ki && j < i);
+            }
+            est1[(int64_t)q * K + rank] = o2f((uint32_t)(ki >> 32));
+            pos[(int64_t)q * K + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+            if (rank == didx) sh.dval = o2f((uint32_t)(ki >> 32));
         }
-        est1[(int64_t)q * K + rank] = o2f((uint32_t)(ki >> 32));
-        pos[(int64_t)q * K + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
-        if (rank == didx) sh.dval = o2f((uint32_t)(ki >> 32));
+    } else {
+        // larger K: a block bitonic sort of the K keys (descending; real keys are unique, the fill entries are equal),
+        // padded to a power of two with key 0, below every candidate key (the rank loop is O(K^2))
+        int kp = 1;
+        while (kp < K) kp <<= 1;
+        for (int i = K + tid; i < kp; i += NT) sh.sb[i] = 0ull;
+        __syncthreads();
+        for (int k2 = 2; k2 <= kp; k2 <<= 1) {
+            for (int j = k2 >> 1; j > 0; j >>= 1) {
+                for (int i = tid; i < kp; i += NT) {
+                    const int ixj = i ^ j;
+                    if (ixj > i) {
+                        const unsigned long long x = sh.sb[i], y = sh.sb[ixj];
+                        if (((i & k2) == 0) ? (x < y) : (x > y)) {
+                            sh.sb[i] = y;
+                            sh.sb[ixj] = x;
+                        }
+                    }
+                }
+                __syncthreads();
+            }
+        }
+        for (int r = tid; r < K; r += NT) {
+            const unsigned long long kr = sh.sb[r];
+            est1[(int64_t)q * K + r] = o2f((uint32_t)(kr >> 32));
+            pos[(int64_t)q * K + r] = (int64_t)(0xffffffffu - (uint32_t)kr);
+            if (r == didx) sh.dval = o2f((uint32_t)(kr >> 32));
+        }
     }
     if (tid == 0) ok[q] = (c >= K && c <= M) ? 1 : 0;
     if (ncnt != nullptr) {

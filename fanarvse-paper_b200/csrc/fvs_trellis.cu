@@ -496,6 +496,119 @@ __global__ void __launch_bounds__(256) tiered_score_kernel(const int64_t* __rest
     }
 }
 
+// Tiered gather on packed records with one candidate per thread: the same estimate as tiered_score_kernel, organised
+// so that every lane of a warp runs the same tier, position and plane at each step (no divergence, no warp
+// reductions).  A CTA of TC_THREADS scores TC_THREADS candidates of one query; each warp stages its 32 records in
+// shared memory with coalesced 16-byte loads, at a word stride SW = RB/4 rounded up to odd, so that the 32 lanes
+// reading the same byte offset of their own records hit 32 different banks.  The rotated query sits in natural order
+// (the four coordinates a byte half covers are one 16-byte broadcast read) and the tiers' codebooks after it (a code
+// of b <= 5 bits indexes at most 32 words: conflict-free).  Per candidate the work is about 6 instructions per
+// coordinate, against ~25 per coordinate in the warp-per-candidate kernel.
+constexpr int TC_THREADS = 128;
+
+template <int NB>
+__device__ __forceinline__ float tier_cand_dot(const uint8_t* __restrict__ pt, int kb, const float* __restrict__ cbt,
+                                               const float* __restrict__ zt) {
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll 2
+    for (int j = 0; j < kb; j++) {
+        uint32_t by[NB];
+#pragma unroll
+        for (int pl = 0; pl < NB; pl++) by[pl] = pt[pl * kb + j];
+        // codes of coordinates 8j .. 8j+7, one per byte of lo (0-3) and hi (4-7): bit 7-k of every plane's byte, planes
+        // combined MSB-first (as tier_pos_dot)
+        uint32_t lo = 0, hi = 0;
+#pragma unroll
+        for (int pl = 0; pl < NB; pl++) {
+            lo = (lo << 1) | __byte_perm(((by[pl] >> 4) * 0x00204081u) & 0x01010101u, 0, 0x0123);
+            hi = (hi << 1) | __byte_perm(((by[pl] & 15u) * 0x00204081u) & 0x01010101u, 0, 0x0123);
+        }
+        const float4 za = *reinterpret_cast<const float4*>(zt + 8 * j);
+        const float4 zb = *reinterpret_cast<const float4*>(zt + 8 * j + 4);
+        a0 += cbt[lo & 255u] * za.x;
+        a1 += cbt[(lo >> 8) & 255u] * za.y;
+        a0 += cbt[(lo >> 16) & 255u] * za.z;
+        a1 += cbt[lo >> 24] * za.w;
+        a0 += cbt[hi & 255u] * zb.x;
+        a1 += cbt[(hi >> 8) & 255u] * zb.y;
+        a0 += cbt[(hi >> 16) & 255u] * zb.z;
+        a1 += cbt[hi >> 24] * zb.w;
+    }
+    return a0 + a1;
+}
+
+__global__ void __launch_bounds__(TC_THREADS) tiered_cand_kernel(const int64_t* __restrict__ pos, int K,
+                                                                 const float* __restrict__ qc,
+                                                                 const float* __restrict__ Zq, int ldz, int D,
+                                                                 TieredSet ts, float* __restrict__ est,
+                                                                 float* __restrict__ sd) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_qn2[TG_MAXT];
+    const int T = ts.T;
+    const int cbn = ts.cboff[T - 1] + (1 << ts.bits[T - 1]);
+    float* z = reinterpret_cast<float*>(smem);             // D (rounded up to 4)
+    float* cbs = z + ((D + 3) & ~3);                       // the tiers' codebooks
+    uint32_t* recs = reinterpret_cast<uint32_t*>(cbs + ((cbn + 3) & ~3));  // TC_THREADS records at word stride SW
+    const int SW = (ts.RB / 4) | 1;
+    const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t qK = (int64_t)q * K;
+    for (int k = tid; k < D; k += TC_THREADS) z[k] = Zq[(int64_t)q * ldz + k];
+    for (int t = 0; t < T; t++)
+        for (int v = tid; v < (1 << ts.bits[t]); v += TC_THREADS) cbs[ts.cboff[t] + v] = ts.cb[t][v];
+    // the warp's 32 records, chunk c of record r by lane (32 r + c) mod 32 of step (32 r + c) / 32
+    const int RC = ts.RB / 16;
+    const int base = blockIdx.y * TC_THREADS + warp * 32;
+    for (int e = lane; e < 32 * RC; e += 32) {
+        const int r = e / RC, c = e - r * RC;
+        if (base + r < K) {
+            const int64_t n = pos[qK + base + r];
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(ts.rec + n * ts.RB) + c);
+            uint32_t* d = recs + (warp * 32 + r) * SW + 4 * c;
+            d[0] = v.x;
+            d[1] = v.y;
+            d[2] = v.z;
+            d[3] = v.w;
+        }
+    }
+    __syncthreads();
+    for (int t = warp; t < T; t += TC_THREADS / 32) {  // ||q_t||^2 per tier
+        float a = 0.f;
+        for (int k = ts.s[t] + lane; k < ts.s[t] + 8 * ts.kb[t]; k += 32) a += z[k] * z[k];
+        a = warp_sum(a);
+        if (lane == 0) s_qn2[t] = a;
+    }
+    __syncthreads();
+    const int i = blockIdx.y * TC_THREADS + tid;
+    if (i >= K) return;
+    const uint8_t* rb = reinterpret_cast<const uint8_t*>(recs + tid * SW);
+    float acc = qc[q], var = 0.f;
+    for (int t = 0; t < T; t++) {
+        const int kb = ts.kb[t];
+        const uint8_t* pt = rb + ts.toff[t];
+        const float* cbt = cbs + ts.cboff[t];
+        const float* zt = z + ts.s[t];
+        float a;
+        switch (ts.bits[t]) {  // uniform over the CTA
+            case 1: a = tier_cand_dot<1>(pt, kb, cbt, zt); break;
+            case 2: a = tier_cand_dot<2>(pt, kb, cbt, zt); break;
+            case 3: a = tier_cand_dot<3>(pt, kb, cbt, zt); break;
+            case 4: a = tier_cand_dot<4>(pt, kb, cbt, zt); break;
+            case 5: a = tier_cand_dot<5>(pt, kb, cbt, zt); break;
+            case 6: a = tier_cand_dot<6>(pt, kb, cbt, zt); break;
+            case 7: a = tier_cand_dot<7>(pt, kb, cbt, zt); break;
+            default: a = tier_cand_dot<8>(pt, kb, cbt, zt); break;
+        }
+        // the tier's fp16 (scale, sigma) pair at soff + 4t, read bytewise (soff need not be 4-aligned)
+        const uint8_t* sp = rb + ts.soff + 4 * t;
+        const float scl = __half2float(__ushort_as_half((unsigned short)(sp[0] | (sp[1] << 8))));
+        const float sgl = __half2float(__ushort_as_half((unsigned short)(sp[2] | (sp[3] << 8))));
+        acc += a * scl;
+        var += s_qn2[t] * sgl * sgl;
+    }
+    est[qK + i] = acc;
+    sd[qK + i] = sqrtf(var);
+}
+
 // ------------------------------------------------------------------------------------------------ routing (fp32)
 // probe = the nprobe largest float(QM[q, c]) * scale[c] (`src/engine_cell.py:40-42`), ordered (score desc, cell asc).
 __global__ void __launch_bounds__(512) route_topk_scaled_kernel(const __half* __restrict__ QM, const float* __restrict__ sc,
@@ -846,12 +959,16 @@ extern "C" int fvs_tiered_score_rec(fvs_stream_t stream, const int64_t* pos, int
     fvs::TieredSet ts;
     int rc = fvs::make_tiered_set(ts, T, D, tier_s, tier_e, tier_bits, tier_cb, nullptr, rec, RB, soff);
     if (rc) return rc;
-    const int pb = ts.nbytes, cbo = ts.cboff[T - 1] + (1 << ts.bits[T - 1]);
-    const size_t sm = (size_t)(D + cbo) * 4 + (size_t)pb + 16 + (RB <= 512 ? (size_t)8 * 512 : 0);
-    if (sm > 200 * 1024) return FVS_ERANGE;
+    const int cbo = ts.cboff[T - 1] + (1 << ts.bits[T - 1]);
     if (B == 0) return FVS_OK;
-    cudaError_t e = fvs_ensure_smem((const void*)fvs::tiered_score_kernel, sm);
+    FVS_CHECK_ARG(RB % 16 == 0 && ((uintptr_t)rec & 15) == 0);   // 16-byte record chunks
+    // one candidate per thread (tiered_cand_kernel): the query, the codebooks and TC_THREADS records in shared memory
+    const size_t sm = (size_t)(((D + 3) & ~3) + ((cbo + 3) & ~3)) * 4 +
+                      (size_t)fvs::TC_THREADS * (size_t)((RB / 4) | 1) * 4;
+    if (sm > 200 * 1024) return FVS_ERANGE;
+    cudaError_t e = fvs_ensure_smem((const void*)fvs::tiered_cand_kernel, sm);
     if (e != cudaSuccess) return (int)e;
-    fvs::tiered_score_kernel<<<B, 256, sm, stream>>>(pos, B, K, qc, Zq, ldz, D, ts, nullptr, nullptr, N, est, sd);
+    const dim3 grid(B, (K + fvs::TC_THREADS - 1) / fvs::TC_THREADS);
+    fvs::tiered_cand_kernel<<<grid, fvs::TC_THREADS, sm, stream>>>(pos, K, qc, Zq, ldz, D, ts, est, sd);
     return fvs_launch_status();
 }

@@ -438,5 +438,7 @@ def test_packed_records_match_planes_tiered(gt, ec):
     rec, ix.rec = ix.rec, None
     b = E.score_tiered(QC, pos, Zq)
     ix.rec = rec
-    np.testing.assert_array_equal(c(a[0]), c(b[0]))
-    np.testing.assert_array_equal(c(a[1]), c(b[1]))
+    # the record kernel (one candidate per thread) and the plane kernel (one warp per candidate) sum the same products
+    # in different orders: equal within fp32 rounding
+    np.testing.assert_allclose(c(a[0]), c(b[0]), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(c(a[1]), c(b[1]), rtol=1e-5, atol=1e-6)
