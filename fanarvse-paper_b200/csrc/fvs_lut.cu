@@ -384,6 +384,141 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
     }
 }
 
+// Fused LUT score with one candidate per thread (large batches): the same estimate as lut_score_zq_kernel on packed
+// records, organised so that every lane of a warp scores its own candidate and all lanes take the same plane word at
+// each step.  The CTA builds the query's table once (entry (block ga, group c, nibble v) at ga*128 + c*16 + v: the 32
+// lanes reading one (ga, c) touch at most 16 consecutive words, conflict-free) and a per-word list (table block,
+// tier, plane weight); each lane then streams its record in 32-byte steps (two steps in flight) and folds each
+// finished tier as delta_t * (a_t - mid_t * qsum_t) * scale_t, the reference's per-tier form.  No warp reduction per
+// candidate; about 40 instructions per plane word.
+constexpr int LC_THREADS = 128;
+
+template <bool HALF>
+__global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __restrict__ pos, int K,
+                                                              const float* __restrict__ qc,
+                                                              const void* __restrict__ Zq, int ldz, int zh, int D,
+                                                              TierSet ts, const int32_t* __restrict__ ncnt,
+                                                              float* __restrict__ est, float* __restrict__ sd,
+                                                              RecSet rs) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
+    const int nblk = D / 32, nwords = ts.nwords;
+    float* tab = reinterpret_cast<float*>(smem);                   // nblk * 128
+    float* zs = tab + nblk * 128;                                  // D
+    uint32_t* wmeta = reinterpret_cast<uint32_t*>(zs + D);         // per word: table offset | tier << 24
+    float* wpw = reinterpret_cast<float*>(wmeta + nwords);         // per word: 2^(b-1-p)
+    const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t qK = (int64_t)q * K;
+    for (int k = tid; k < D; k += LC_THREADS)
+        zs[k] = zh ? __half2float(reinterpret_cast<const __half*>(Zq)[(int64_t)q * ldz + k])
+                   : reinterpret_cast<const float*>(Zq)[(int64_t)q * ldz + k];
+    for (int w = tid; w < nwords; w += LC_THREADS) {
+        int t = 0;
+        while (t + 1 < ts.T && w >= ts.wbase[t + 1]) t++;
+        const int r = w - ts.wbase[t], wpp = ts.kb[t] / 4;
+        const int p = r / wpp, j4 = r - p * wpp;
+        wmeta[w] = (uint32_t)((ts.s[t] / 32 + j4) * 128) | ((uint32_t)t << 24);
+        wpw[w] = ts.pw[t][p];
+    }
+    __syncthreads();
+    // entry v of a 4-coordinate group sums the selected coordinates left to right in fp32, as acc += z_i * bit_i does
+    for (int idx = tid; idx < nblk * 128; idx += LC_THREADS) {
+        const int ga = idx >> 7, c = (idx >> 4) & 7, v = idx & 15;
+        const float* zz = zs + 32 * ga + 4 * c;
+        float acc = 0.f;
+        if (v & 8) acc = __fadd_rn(acc, zz[0]);
+        if (v & 4) acc = __fadd_rn(acc, zz[1]);
+        if (v & 2) acc = __fadd_rn(acc, zz[2]);
+        if (v & 1) acc = __fadd_rn(acc, zz[3]);
+        tab[idx] = HALF ? __half2float(__float2half_rn(acc)) : acc;
+    }
+    for (int t = warp; t < ts.T; t += LC_THREADS / 32) {
+        float a = 0.f, b = 0.f;
+        for (int k = ts.s[t] + lane; k < ts.e[t]; k += 32) {
+            const float x = zs[k];
+            a += x;
+            b += x * x;
+        }
+        a = warp_sum(a);
+        b = warp_sum(b);
+        if (lane == 0) {
+            s_qsum[t] = a;
+            s_qn2[t] = b;
+        }
+    }
+    __syncthreads();
+    const int i = blockIdx.y * LC_THREADS + tid;
+    if (i >= K) return;
+    const int lim = ncnt ? min(max(ncnt[q], 0), K) : K;
+    if (i >= lim) {
+        est[qK + i] = kNeg;
+        sd[qK + i] = 0.f;
+        return;
+    }
+    const int64_t n = pos[qK + i];
+    const uint8_t* rec = rs.rec + n * rs.RB;
+    float sc[MAX_TIERS];
+    float var = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAX_TIERS; t++) {
+        sc[t] = 0.f;
+        if (t < ts.T) {
+            const uint32_t sp = __ldg(reinterpret_cast<const uint32_t*>(rec + rs.soff) + t);
+            sc[t] = __half2float(__ushort_as_half((unsigned short)(sp & 0xffffu)));
+            const float g = __half2float(__ushort_as_half((unsigned short)(sp >> 16)));
+            var = var + s_qn2[t] * g * g;
+        }
+    }
+    float acc = qc[q], at = 0.f;
+    int ct = 0;
+    auto fold = [&](int t, float a) {  // t uniform over the warp
+        float s = 0.f;
+#pragma unroll
+        for (int u = 0; u < MAX_TIERS; u++)
+            if (u == t) s = sc[u];
+        acc = acc + ts.delta[t] * (a - ts.mid[t] * s_qsum[t]) * s;
+    };
+    // the record streams in 32-byte steps (two 16-byte chunks, a whole sector), two steps in flight ahead of the one
+    // being scored
+    const uint4* rp = reinterpret_cast<const uint4*>(rec);
+    const int nst = (nwords + 7) / 8;
+    auto ld = [&](int st, uint4& a, uint4& b) {
+        a = st < nst ? __ldg(rp + 2 * st) : make_uint4(0u, 0u, 0u, 0u);
+        b = st < nst && 8 * st + 4 < nwords ? __ldg(rp + 2 * st + 1) : make_uint4(0u, 0u, 0u, 0u);
+    };
+    uint4 n1a, n1b, n2a, n2b;
+    ld(0, n1a, n1b);
+    ld(1, n2a, n2b);
+    for (int k = 0; k < nst; k++) {
+        const uint32_t wd8[8] = {n1a.x, n1a.y, n1a.z, n1a.w, n1b.x, n1b.y, n1b.z, n1b.w};
+        n1a = n2a;
+        n1b = n2b;
+        ld(k + 2, n2a, n2b);
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int w = 8 * k + u;
+            if (w >= nwords) break;
+            const uint32_t m = wmeta[w];
+            const int t = (int)(m >> 24);
+            if (t != ct) {
+                fold(ct, at);
+                ct = t;
+                at = 0.f;
+            }
+            const float* E = tab + (m & 0xffffffu);
+            const uint32_t wd = wd8[u];
+            float a = 0.f;
+#pragma unroll
+            for (int bi = 0; bi < 4; bi++)
+                a += E[32 * bi + ((wd >> (8 * bi + 4)) & 15u)] + E[32 * bi + 16 + ((wd >> (8 * bi)) & 15u)];
+            at += a * wpw[w];
+        }
+    }
+    fold(ct, at);
+    est[qK + i] = acc;
+    sd[qK + i] = sqrtf(var);
+}
+
 // CTAs per query of the fused LUT kernel: enough for about two per SM when the batch is small, at most one per 16
 // candidates (two rounds of its 8 warps)
 static int lut_split(int B, int K) {
@@ -542,6 +677,21 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     if (sm > 200 * 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const fvs::RecSet rs{rec, RB, soff};
+    if (B >= fvs_sm_count() && ts.T <= fvs::MAX_TIERS && ts.nwords <= 4 * RB / 16) {
+        // large batch: one candidate per thread
+        const size_t smc = ((size_t)(D / 32) * 128 + D) * 4 + (size_t)ts.nwords * 8;
+        const dim3 grid(B, (K + fvs::LC_THREADS - 1) / fvs::LC_THREADS);
+        cudaError_t e = half ? fvs_ensure_smem((const void*)fvs::lut_cand_kernel<true>, smc)
+                             : fvs_ensure_smem((const void*)fvs::lut_cand_kernel<false>, smc);
+        if (e != cudaSuccess) return (int)e;
+        if (half)
+            fvs::lut_cand_kernel<true><<<grid, fvs::LC_THREADS, smc, stream>>>(pos, K, qc, Zq, ldz, zq_half, D, ts,
+                                                                                ncnt, est, sd, rs);
+        else
+            fvs::lut_cand_kernel<false><<<grid, fvs::LC_THREADS, smc, stream>>>(pos, K, qc, Zq, ldz, zq_half, D, ts,
+                                                                                 ncnt, est, sd, rs);
+        return fvs_launch_status();
+    }
     const int S = fvs::lut_split(B, K);
 #define FVS_LRG(H, W, G, C)                                                                                        \
     do {                                                                                                           \
