@@ -42,6 +42,7 @@ SIGNATURES = {
     "fvs_lut_score_zq": (I32, [P, P, I32, I32, P, P, I32, I32, I32, I32, I32, P, P, P, P, P, P, P, I64, P, P, P]),
     "fvs_refine": (I32, [P, P, I32, P, P, P, P, I32, I32, F32, I32, P, I32, P, P, P, P]),
     "fvs_i8_scan_small": (I32, [P, I32, P, P, I32, I32, P, I32, I32, P, I32, P, P, P, P, P, P, P, P, I32, P, I32]),
+    "fvs_project_quantize": (I32, [P, P, I32, I32, I32, P, P, I32, P, P, P, I32, P]),
     "fvs_trellis_tile_rows": (I32, []),
     "fvs_trellis_scan": (I32, [P, I32, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I32, P, I32, P, P, P, P, P,
                                 I32, P, I32]),

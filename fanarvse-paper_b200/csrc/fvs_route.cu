@@ -238,14 +238,29 @@ __global__ void query_prep_kernel(const float* __restrict__ Q, int B, int d, int
     const float4* cv = reinterpret_cast<const float4*>(c);
     uint2* out = reinterpret_cast<uint2*>(Qh + (int64_t)q * d);
     float acc = 0.f;
-    for (int i = lane; i < d / 4; i += 32) {
-        const float4 x = row[i], y = cv[i];
-        acc = fmaf(x.x, y.x, acc);
-        acc = fmaf(x.y, y.y, acc);
-        acc = fmaf(x.z, y.z, acc);
-        acc = fmaf(x.w, y.w, acc);
-        const __half2 lo = __floats2half2_rn(x.x, x.y), hi = __floats2half2_rn(x.z, x.w);
-        out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+    const int nv = d / 4;
+    // four 16-byte slices of the row in flight per lane (the lane's slices are summed in the same order as one at a time)
+    for (int i0 = lane; i0 < nv; i0 += 4 * 32) {
+        float4 x[4], y[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = i0 + 32 * u;
+            if (i < nv) {
+                x[u] = row[i];
+                y[u] = cv[i];
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int i = i0 + 32 * u;
+            if (i >= nv) break;
+            acc = fmaf(x[u].x, y[u].x, acc);
+            acc = fmaf(x[u].y, y[u].y, acc);
+            acc = fmaf(x[u].z, y[u].z, acc);
+            acc = fmaf(x[u].w, y[u].w, acc);
+            const __half2 lo = __floats2half2_rn(x[u].x, x[u].y), hi = __floats2half2_rn(x[u].z, x[u].w);
+            out[i] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+        }
     }
     acc = warp_sum(acc);
     if (lane == 0 && qc) qc[q] = acc;

@@ -61,6 +61,11 @@ class IndexI8:
         self.Z = f(i8["Z"], torch.int8)
         self.zs = f(i8["zs"], torch.float32)
         self.Vr = f(i8["Vr"], torch.float32)
+        # Vr transposed (K-major for the tensor cores) and split into a TF32 part (rounded to nearest at 10 mantissa
+        # bits) and the exact remainder: the two operands of the projection kernel's 3xTF32 products
+        VrT = self.Vr.t().contiguous()
+        self.VrT_big = ((VrT.view(torch.int32) + 0x1000) & ~0x1FFF).view(torch.float32).contiguous()
+        self.VrT_small = (VrT - self.VrT_big).contiguous()
         self.R = self.Z.shape[1]
         self.TS = [tuple(int(v) for v in t) for t in code["TS"]]
         self.T = len(self.TS)
@@ -228,13 +233,23 @@ class EngineB200I8:
         self._call("query_prep", self.L.fvs_query_prep, ptr(Qb), B, d, Qb.stride(0), ptr(c), ptr(Qh), ptr(QC))
         return QC, Qh
 
+    KS_MAX = 16      # K-splits of the projection kernel (its partial-sum buffer is KS_MAX x B x R floats)
+
     def quantize(self, Qb):
-        """q8, qs (`throughput/enginei8.py:38`): fp32 projection by cuBLAS, then one quantisation kernel."""
-        z = (Qb @ self.ix.Vr).contiguous()
-        B, R = z.shape
-        q8 = torch.empty(B, R, dtype=torch.int8, device=z.device)
-        qs = torch.empty(B, device=z.device)
-        self._call("quantize", self.L.fvs_quantize, ptr(z), B, R, R, ptr(q8), ptr(qs))
+        """q8, qs (`throughput/enginei8.py:38`): z = Qb @ Vr in fp32 accuracy (3xTF32 on the tensor cores, split over
+        K), then the reference's quantisation, in `fvs_project_quantize`."""
+        ix = self.ix
+        B, d = Qb.shape
+        R = ix.Vr.shape[1]
+        q8 = torch.empty(B, R, dtype=torch.int8, device=Qb.device)
+        qs = torch.empty(B, device=Qb.device)
+        if Qb.dtype != torch.float32 or Qb.stride(1) != 1 or Qb.stride(0) % 4 or Qb.data_ptr() % 16 or R != 256:
+            z = (Qb @ ix.Vr).contiguous()            # shapes the projection kernel does not take
+            self._call("quantize", self.L.fvs_quantize, ptr(z), B, R, R, ptr(q8), ptr(qs))
+            return q8, qs
+        part = torch.empty(self.KS_MAX * B * R, device=Qb.device)
+        self._call("quantize", self.L.fvs_project_quantize, ptr(Qb), B, d, Qb.stride(0), ptr(ix.VrT_big),
+                   ptr(ix.VrT_small), R, ptr(q8), ptr(qs), ptr(part), self.KS_MAX, ptr(self.status))
         return q8, qs
 
     def first_pass_cells(self, K, nprobe, rho_override=None):

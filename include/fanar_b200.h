@@ -232,6 +232,19 @@ int fvs_refine(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ord
 int fvs_exact_scores(fvs_stream_t stream, const uint16_t* H, int d, const int32_t* ids, int B, int k, const float* Q,
                      int ldq, float* score);
 
+/*
+ * Query codes of the int8 stage 1 (`throughput/enginei8.py:38`: z = Q @ Vr, qs = max|z| / 127,
+ * q8 = clamp(round(z / qs), +-127), the rounding and clamp of fvs_quantize): z is computed on the tensor cores as
+ * three TF32 products (Q and Vr each split into a TF32 part and an exact remainder; error ~2^-21 relative per product,
+ * fp32 accumulation), split over K into ks_max x B x R partial sums in `part` (16-byte aligned; a fixed-order sum then
+ * quantises each row).  vt_big / vt_small: Vr transposed [R, d] row-major, vt_big = Vr^T with the low 13 mantissa bits
+ * cleared, vt_small = Vr^T - vt_big.  R = 256, d % 4 == 0, ldq % 4 == 0, Q 16-byte aligned.  `status` as
+ * fvs_i8_scan_tc.
+ */
+int fvs_project_quantize(fvs_stream_t stream, const float* Q, int B, int d, int ldq, const float* vt_big,
+                         const float* vt_small, int R, int8_t* q8, float* qs, float* part, int ks_max,
+                         int32_t* status);
+
 /* Rows per work tile of fvs_trellis_scan (tiles start on the cell's first global 32-row boundary). */
 int fvs_trellis_tile_rows(void);
 

@@ -473,6 +473,42 @@ def test_quantize_matches_reference_formula(eng):
     np.testing.assert_array_equal(c(q8), c(q8_ref))
 
 
+@pytest.mark.parametrize("B,d,ldq", [(2000, 1536, 1536), (1, 1536, 1536), (257, 768, 768), (33, 1000, 1004),
+                                    (130, 256, 256)])
+def test_project_quantize_fp32_accuracy(eng, B, d, ldq):
+    """fvs_project_quantize (3xTF32 products on the tensor cores, split over K): z within a few 1e-6 relative of the
+    float64 product (the tensor cores' fp32 accumulation over up to ~200 K-steps per split is the larger term; a SIMT
+    fp32 GEMM is near 1e-7), so qs agrees to 5e-6 relative and q8 equals the reference's quantisation of the exact z
+    except where z / qs lies within 1e-3 of a rounding boundary (well under 0.1 % of the codes)."""
+    L = pkg("_lib")
+    lib = L.lib()
+    g = torch.Generator(device=DEV).manual_seed(B + d)
+    Qfull = torch.randn(B, ldq, device=DEV, generator=g)
+    Q = Qfull[:, :d]
+    Vr = torch.randn(d, 256, device=DEV, generator=g) / d ** 0.5
+    Vr[:, 7] *= 1e-3                                          # a column of small values
+    VrT = Vr.t().contiguous()
+    big = ((VrT.view(torch.int32) + 0x1000) & ~0x1FFF).view(torch.float32).contiguous()
+    small = (VrT - big).contiguous()
+    q8 = torch.empty(B, 256, dtype=torch.int8, device=DEV)
+    qs = torch.empty(B, device=DEV)
+    part = torch.empty(16 * B * 256, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    L.check(lib.fvs_project_quantize(L.stream_handle(), L.ptr(Qfull), B, d, ldq, L.ptr(big), L.ptr(small), 256,
+                                     L.ptr(q8), L.ptr(qs), L.ptr(part), 16, L.ptr(status)), "project_quantize")
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    z64 = Q.double() @ Vr.double()
+    qs64 = z64.abs().amax(1).clamp(min=1e-12) / 127
+    np.testing.assert_allclose(c(qs).astype(np.float64), c(qs64), rtol=5e-6)
+    x = c(z64 / qs64[:, None])
+    want = np.clip(np.round(x), -127, 127)
+    near_tie = np.abs(np.abs(x - np.floor(x)) - 0.5) < 1e-3
+    got = c(q8).astype(np.float64)
+    assert np.all((got == want) | near_tie)
+    assert near_tie.mean() < 5e-3
+
+
 @pytest.mark.parametrize("B,d,ldq", [(1, 1536, 1536), (257, 768, 768), (33, 1536, 1600)])
 def test_query_prep_matches_torch(eng, B, d, ldq):
     """fvs_query_prep: the fp16 copy equals `Qb.half()` bit for bit; the centre product equals `Qb @ c` within fp32
