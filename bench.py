@@ -524,6 +524,28 @@ def variant_trellis(args, dev, steps=20):
             "reference_buffer_rule": ref_m}
 
 
+def profile_case_trellis(args, dev):
+    """The default engine on the config-4 generator at --trellis-rows rows: build, three eager searches (nprobe 256,
+    K 400, M 65536), one line of output.  Used as the workload of one-kernel profiler captures."""
+    synth, ib, ec = pkg("synth"), pkg("index_build"), pkg("engine_cell")
+    import dataclasses
+    pkg("build").build()
+    n = args.trellis_rows
+    spec = dataclasses.replace(synth.CONFIGS["c4_2m25_768"], n=n)
+    nlist = 8192 if n >= 2_000_000 else synth.default_nlist(n)
+    ds = synth.make_dataset(spec, dev, gt_k=10)
+    s1, _, codes = ib.build_index(ds["base16"], nlist, R=256, refine_bits=1920, seed=0, uniform=False, lloyd=True)
+    s1.update(ib.build_trellis(ds["base16"], s1, seed=0))
+    ix = ec.IndexS(s1, codes["lloyd"], ds["base16"], dev)
+    E = ec.EngineB200S(ix)
+    E.M = 65536
+    for _ in range(3):
+        E.search_eager(ds["queries"], 400, 2.0, 256, 10)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": "trellis", "rows": n, "cells": nlist,
+                      "cnt_median": int(E._last["cnt"].float().median())}), flush=True)
+
+
 def _timed_search(fn, steps=10):
     for _ in range(3):
         fn()
@@ -727,6 +749,9 @@ def main():
                          "trellis (default engine, config 4), batches (config 3 at batch 500/1000 and k=100), latency "
                          "(config 2), c1 (config 1 with its CPU run), c5 (one 2M-row shard of config 5), or none")
     ap.add_argument("--trellis-rows", type=int, default=2_250_000, help="rows of the default-engine dataset")
+    ap.add_argument("--profile-case", default=None, choices=["trellis"],
+                    help="only build the named case and run three eager searches (a small workload for one-kernel "
+                         "ncu captures): trellis = the default engine at --trellis-rows, nprobe 256, K 400")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -741,6 +766,8 @@ def main():
         return reference_arm(args, rank, world, local)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.profile_case == "trellis":
+        return profile_case_trellis(args, dev)
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
