@@ -35,7 +35,8 @@ import importlib  # noqa: E402
 METRIC = "QPS at recall@10>=0.99, 1M x 1536 fp16, batch 2000; batch-1 p50 latency"
 # operating points: (nprobe, K, M, rho, in-graph recompute capacity); rho 0.6 / M 4096 are the reference's final
 # knobs (`throughput/e_v3final.py:28-32` with M raised to 4096); rho 0.65 with M 8192 flags fewer queries
-GRID = [(64, 90, 8192, 0.65, 16), (72, 100, 8192, 0.65, 8), (72, 100, 8192, 0.65, 16), (80, 100, 8192, 0.65, 8),
+GRID = [(64, 90, 8192, 0.65, 16), (72, 100, 8192, 0.65, 4), (72, 100, 8192, 0.65, 8), (72, 100, 8192, 0.65, 16),
+        (80, 100, 8192, 0.65, 8),
         (80, 100, 8192, 0.65, 16), (96, 100, 4096, 0.6, 48), (96, 100, 8192, 0.65, 16), (128, 120, 4096, 0.6, 48), (128, 120, 8192, 0.65, 16),
         (160, 120, 8192, 0.65, 16), (192, 150, 8192, 0.65, 16), (256, 150, 8192, 0.65, 16), (352, 175, 8192, 0.65, 16)]
 

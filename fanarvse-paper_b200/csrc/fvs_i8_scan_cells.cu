@@ -19,11 +19,14 @@
 //                 for every (tile, sub-tile) unit into one of T_STAGES accumulators; releases a code tile after its
 //                 units and the item's query sub-tiles after its last tile
 //   warps 2-3   : gather: the item's sub-tiles alternate between the two warps; rows of q8 picked by qid, copied with
-//                 cp.async (a sub-tile's rows in flight at once) into the canonical K-major 128 B-swizzled layout, and the sub-tile's column metadata (qid, qs, pair constant,
-//                 threshold) into one of MS slots, released when every epilogue warp is done with the sub-tile
+//                 cp.async (a sub-tile's rows in flight at once) into the canonical K-major 128 B-swizzled layout,
+//                 and the sub-tile's column metadata (qid, qs, pair constant, threshold) into one of MS slots,
+//                 released when every epilogue warp is done with the sub-tile
 //   warps 4-19  : four epilogue warpgroups, units alternating between them; each warp loads its rows' scales before
-//                 waiting for the accumulator, then as fvs_i8_scan_tc: est = ((acc * qs) * zs) + qcp with explicit rounding, first pass: block maximum per
-//                 query by redux.sync.max; emit: kept-column masks transposed across the warp, one atomicAdd per column.
+//                 waiting for the accumulator, returns the TMEM stage as soon as the accumulator is in registers, then
+//                 as fvs_i8_scan_tc: est = ((acc * qs) * zs) + qcp with explicit rounding, first pass: block maximum
+//                 per query by redux.sync.max; emit: kept-column masks transposed across the warp, one atomicAdd per
+//                 column.
 // The last CTA to finish resets sched[0..1], so the next launch starts from zero.
 // Every mbarrier wait is bounded; on expiry the CTA raises `status`, drains what it issued, frees TMEM and returns.
 #include <cuda.h>
@@ -478,6 +481,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                         uint32_t acc[32];
                         tmem_ld32(ta + 32 * h, acc);
                         tmem_ld_wait();
+                        if ((h + 1) * 32 >= nq) {
+                            // accumulator in registers: the TMEM stage goes back to the MMA before the scoring
+                            tc_fence_before();
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive(t_empty(st));
+                        }
                         if (!wactive) continue;
                         const int nc = min(32, nq - h * 32);
                         const float4* ms4 = reinterpret_cast<const float4*>(ms + 32 * h);
@@ -541,10 +550,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                             __syncwarp();
                         }
                     }
-                    tc_fence_before();
                     __syncwarp();
                     if (lane == 0) {
-                        mbar_arrive(t_empty(st));
                         // the sub-tile's units (one per tile) are spread over the warpgroups, which finish in any
                         // order: the slot is free once all 4 * ntiles warps are done with it; the last one to count
                         // itself resets the count and releases the slot
@@ -573,7 +580,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == W_MMA) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    if (warp == W_MMA)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
     if (tid == 0) {
         if (*abort && p.status) atomicExch(p.status, 1);
         // the last CTA out resets the work counter for the next launch (every CTA took its last cell before this)

@@ -8,8 +8,8 @@
 // then block maxima per 32-row block (mode 0, first pass) or the threshold emit est >= t0[q] (mode 1).
 // Work items are (cell, group of up to QN = 128 of its queries), handed out dynamically (cells largest first).  An
 // item's queries are gathered once and held while the cell's 128-row tiles pass; each tile x item is ONE sequence of
-// 16 tcgen05.mma.kind::f16 (M = 128 rows, N = the item's queries rounded up to 16, K = 16 each), since the issue cost of
-// an MMA hardly depends on N.  The code tile is not copied but decoded in the CTA: four decode warps, one tile row per
+// 16 tcgen05.mma.kind::f16 (M = 128 rows, N = the item's queries rounded up to 16, K = 16 each), since the issue cost
+// of an MMA hardly depends on N.  The code tile is not copied but decoded in the CTA: four decode warps, one tile row per
 // lane, read the row's words (prefetched one tile ahead) and write its 256 fp16 values, two per lookup of a table of
 // fp16 value pairs indexed by (L+1)-bit windows, straight into the canonical K-major 128 B-swizzled layout the MMA
 // reads.  The tile moves in K-chunks of 64 values through a ring of AC chunk slots, so decode and MMAs overlap chunk by
@@ -499,6 +499,12 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                     uint32_t acc[32];
                     tmem_ld32(ta + 32 * h, acc);
                     tmem_ld_wait();
+                    if ((h + 1) * 32 >= nq) {
+                        // accumulator in registers: the TMEM stage goes back to the MMA before the scoring
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(t_empty(st));
+                    }
                     if (!wactive) continue;
                     const int nc = min(32, nq - h * 32);
                     const float4* mc4 = reinterpret_cast<const float4*>(mc + 32 * h);
@@ -559,10 +565,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                         __syncwarp();
                     }
                 }
-                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
-                    mbar_arrive(t_empty(st));
                     // the item's tiles are spread over the warpgroups, which finish in any order: the metadata slot is
                     // free once all 4 * ntiles warps are done with it; the last one to count itself resets the count
                     // and releases the slot
@@ -586,7 +590,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if (warp == W_MMA) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
+    if (warp == W_MMA)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
     if (tid == 0) {
         if (*abort && p.status) atomicExch(p.status, 1);
         // the last CTA out resets the work counter for the next launch (every CTA took its last cell before this)
