@@ -35,8 +35,7 @@ import importlib  # noqa: E402
 METRIC = "QPS at recall@10>=0.99, 1M x 1536 fp16, batch 2000; batch-1 p50 latency"
 # operating points: (nprobe, K, M, rho, in-graph recompute capacity); rho 0.6 / M 4096 are the reference's final
 # knobs (`throughput/e_v3final.py:28-32` with M raised to 4096); rho 0.65 with M 8192 flags fewer queries
-GRID = [(64, 90, 8192, 0.65, 16), (72, 100, 8192, 0.65, 4), (72, 100, 8192, 0.65, 8), (72, 100, 8192, 0.65, 16),
-        (80, 100, 8192, 0.65, 8),
+GRID = [(64, 90, 8192, 0.65, 16), (72, 100, 8192, 0.65, 8), (72, 100, 8192, 0.65, 16), (80, 100, 8192, 0.65, 8),
         (80, 100, 8192, 0.65, 16), (96, 100, 4096, 0.6, 48), (96, 100, 8192, 0.65, 16), (128, 120, 4096, 0.6, 48), (128, 120, 8192, 0.65, 16),
         (160, 120, 8192, 0.65, 16), (192, 150, 8192, 0.65, 16), (256, 150, 8192, 0.65, 16), (352, 175, 8192, 0.65, 16)]
 
@@ -490,8 +489,10 @@ def variant_trellis(args, dev, steps=20):
     kt = {n: float(np.mean([a.elapsed_time(b) for a, b in v])) for n, v in E.timing.items()}
     E.timing = None
     cnt = E._last["cnt"]
+    cq = torch.quantile(cnt.float(), torch.tensor([0.5, 0.9, 0.99], device=cnt.device)).tolist()
     flags = {"underflow": int((cnt < K).sum()), "overflow": int((cnt > E._last["M"]).sum()),
-             "cnt_median": int(cnt.float().median())}
+             "cnt_median": int(cq[0]), "cnt_p90": int(cq[1]), "cnt_p99": int(cq[2]), "cnt_max": int(cnt.max()),
+             "cnt_above_8192": int((cnt > 8192).sum())}
     Mbuf = E.M
     # the same operating point at the reference's own buffer rule M = max(4096, 16 K) (`src/s1cell.py:181`): the
     # queries whose emit overflows it are flagged and recomputed (with 65536 entries)

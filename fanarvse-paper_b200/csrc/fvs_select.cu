@@ -654,7 +654,9 @@ extern "C" int fvs_threshold(fvs_stream_t stream, const float* bmc, int MB, cons
     if (n1 > 1024) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     const int cap = n1 * MB;
-    if (B < fvs_sm_count() && cap <= 8 * fvs::THR_THREADS) {  // a small batch: one CTA per query
+    const size_t smw = (size_t)fvs::WQ_WARPS * (256 + cap) * 4;
+    // one CTA per query for a small batch, and for any batch whose key capacity is too large for the warp kernel
+    if ((B < fvs_sm_count() || smw > 96 * 1024) && cap <= 16 * fvs::THR_THREADS) {
         const int NK = (cap + fvs::THR_THREADS - 1) / fvs::THR_THREADS;
         if (NK <= 1)
             fvs::threshold_reg_kernel<1><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
@@ -662,11 +664,13 @@ extern "C" int fvs_threshold(fvs_stream_t stream, const float* bmc, int MB, cons
             fvs::threshold_reg_kernel<2><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
         else if (NK <= 4)
             fvs::threshold_reg_kernel<4><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
-        else
+        else if (NK <= 8)
             fvs::threshold_reg_kernel<8><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r, t0);
+        else
+            fvs::threshold_reg_kernel<16><<<B, fvs::THR_THREADS, 0, stream>>>(bmc, MB, slot, probe, nprobe, n1, off, r,
+                                                                               t0);
         return fvs_launch_status();
     }
-    const size_t smw = (size_t)fvs::WQ_WARPS * (256 + cap) * 4;
     if (smw <= 96 * 1024) {
         cudaError_t e = fvs_ensure_smem((const void*)fvs::threshold_warp_kernel, smw);
         if (e != cudaSuccess) return (int)e;
