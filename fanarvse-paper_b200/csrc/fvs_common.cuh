@@ -384,6 +384,32 @@ __device__ __forceinline__ void warp_sort_regs_desc(T (&v)[PER]) {
     }
 }
 
+// Descending bitonic sort of kp keys (kp a power of two, kp <= blockDim.x) held one per thread, thread t holding
+// position t (threads t >= kp hold 0 and keep 0); exchanges at distances below 32 go through warp shuffles, longer ones
+// through `buf` (kp words of shared memory) with a barrier on each side.  Every thread of the block calls it.
+__device__ __forceinline__ unsigned long long block_bitonic_desc_u64(unsigned long long v, int kp,
+                                                                     unsigned long long* buf) {
+    const int tid = threadIdx.x;
+    for (int size = 2; size <= kp; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            unsigned long long o;
+            if (stride >= 32) {
+                if (tid < kp) buf[tid] = v;
+                __syncthreads();
+                o = tid < kp ? buf[tid ^ stride] : 0ull;
+                __syncthreads();
+            } else {
+                const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, stride);
+                const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), stride);
+                o = ((unsigned long long)hi << 32) | lo;
+            }
+            const bool desc = (tid & size) == 0, lower = (tid & stride) == 0;
+            v = (lower == desc) ? (v > o ? v : o) : (v < o ? v : o);
+        }
+    }
+    return tid < kp ? v : 0ull;
+}
+
 __device__ __forceinline__ int warp_sum_int(int v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -305,32 +305,24 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
             if (rank == didx) sh.dval = o2f((uint32_t)(ki >> 32));
         }
     } else {
-        // larger K: a block bitonic sort of the K keys (descending; real keys are unique, the fill entries are equal),
-        // padded to a power of two with key 0, below every candidate key (the rank loop is O(K^2))
+        // larger K: a bitonic sort of the K keys (descending; real keys are unique, the fill entries are equal), padded
+        // to a power of two kp <= NT with key 0, thread t holding position t: exchanges at distances below 32 go
+        // through warp shuffles, the longer ones through shared memory (10 barrier pairs at kp = 512 instead of a
+        // barrier after each of the 45 stages)
         int kp = 1;
         while (kp < K) kp <<= 1;
-        for (int i = K + tid; i < kp; i += NT) sh.sb[i] = 0ull;
+        __syncthreads();  // the selection's keys are in sh.sb
+        unsigned long long v = tid < K ? sh.sb[tid] : 0ull;
         __syncthreads();
-        for (int k2 = 2; k2 <= kp; k2 <<= 1) {
-            for (int j = k2 >> 1; j > 0; j >>= 1) {
-                for (int i = tid; i < kp; i += NT) {
-                    const int ixj = i ^ j;
-                    if (ixj > i) {
-                        const unsigned long long x = sh.sb[i], y = sh.sb[ixj];
-                        if (((i & k2) == 0) ? (x < y) : (x > y)) {
-                            sh.sb[i] = y;
-                            sh.sb[ixj] = x;
-                        }
-                    }
-                }
-                __syncthreads();
-            }
+        v = block_bitonic_desc_u64(v, kp, sh.sb);
+        if (tid < K) {
+            est1[(int64_t)q * K + tid] = o2f((uint32_t)(v >> 32));
+            pos[(int64_t)q * K + tid] = (int64_t)(0xffffffffu - (uint32_t)v);
+            if (tid == didx) sh.dval = o2f((uint32_t)(v >> 32));
         }
-        for (int r = tid; r < K; r += NT) {
-            const unsigned long long kr = sh.sb[r];
-            est1[(int64_t)q * K + r] = o2f((uint32_t)(kr >> 32));
-            pos[(int64_t)q * K + r] = (int64_t)(0xffffffffu - (uint32_t)kr);
-            if (r == didx) sh.dval = o2f((uint32_t)(kr >> 32));
+        if (ncnt != nullptr) {  // the delta rule below reads the sorted keys from sh.sb
+            __syncthreads();
+            if (tid < K) sh.sb[tid] = v;
         }
     }
     if (tid == 0) ok[q] = (c >= K && c <= M) ? 1 : 0;

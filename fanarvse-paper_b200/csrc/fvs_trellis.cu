@@ -714,6 +714,16 @@ __global__ void __launch_bounds__(RSR_THREADS) route_topk_scaled_reg_kernel(cons
             }
         }
     __syncthreads();
+    if (nprobe > 128 && nprobe <= RSR_THREADS) {
+        // order by a bitonic sort, one key per thread (the O(nprobe^2) rank loop costs more at these sizes)
+        int kp = 1;
+        while (kp < nprobe) kp <<= 1;
+        unsigned long long v = tid < nprobe ? s_sel[tid] : 0ull;
+        __syncthreads();
+        v = block_bitonic_desc_u64(v, kp, s_sel);
+        if (tid < nprobe) probe[(int64_t)q * nprobe + tid] = (int64_t)(0xffffffffu - (uint32_t)v);
+        return;
+    }
     for (int i = tid; i < nprobe; i += RSR_THREADS) {
         const unsigned long long ki = s_sel[i];
         int rank = 0;
