@@ -404,14 +404,10 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
     const int nblk = D / 32, nwords = ts.nwords;
     float* tab = reinterpret_cast<float*>(smem);                   // nblk * 128
-    float* zs = tab + nblk * 128;                                  // D
-    uint32_t* wmeta = reinterpret_cast<uint32_t*>(zs + D);         // per word: table offset | tier << 24
+    uint32_t* wmeta = reinterpret_cast<uint32_t*>(tab + nblk * 128);  // per word: table offset | tier << 24
     float* wpw = reinterpret_cast<float*>(wmeta + nwords);         // per word: 2^(b-1-p)
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t qK = (int64_t)q * K;
-    for (int k = tid; k < D; k += LC_THREADS)
-        zs[k] = zh ? __half2float(reinterpret_cast<const __half*>(Zq)[(int64_t)q * ldz + k])
-                   : reinterpret_cast<const float*>(Zq)[(int64_t)q * ldz + k];
     for (int w = tid; w < nwords; w += LC_THREADS) {
         int t = 0;
         while (t + 1 < ts.T && w >= ts.wbase[t + 1]) t++;
@@ -420,22 +416,44 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
         wmeta[w] = (uint32_t)((ts.s[t] / 32 + j4) * 128) | ((uint32_t)t << 24);
         wpw[w] = ts.pw[t][p];
     }
-    __syncthreads();
-    // entry v of a 4-coordinate group sums the selected coordinates left to right in fp32, as acc += z_i * bit_i does
-    for (int idx = tid; idx < nblk * 128; idx += LC_THREADS) {
-        const int ga = idx >> 7, c = (idx >> 4) & 7, v = idx & 15;
-        const float* zz = zs + 32 * ga + 4 * c;
-        float acc = 0.f;
-        if (v & 8) acc = __fadd_rn(acc, zz[0]);
-        if (v & 4) acc = __fadd_rn(acc, zz[1]);
-        if (v & 2) acc = __fadd_rn(acc, zz[2]);
-        if (v & 1) acc = __fadd_rn(acc, zz[3]);
-        tab[idx] = HALF ? __half2float(__float2half_rn(acc)) : acc;
+    // group g = 4-coordinate group (block g / 8, group g % 8) holds coordinates 4g .. 4g+3.  Entry v sums the selected
+    // coordinates left to right in fp32, as acc += z_i * bit_i does; built incrementally: entry v = entry (v without
+    // its last selected coordinate) + that coordinate, the same additions in the same order.
+    for (int g = tid; g < nblk * 8; g += LC_THREADS) {
+        float z[4];
+        if (zh) {
+            const uint2 h = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(Zq) +
+                                                                  (int64_t)q * ldz + 4 * g));
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+            z[0] = a.x, z[1] = a.y, z[2] = b.x, z[3] = b.y;
+        } else {
+            const float4 f = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(Zq) +
+                                                                    (int64_t)q * ldz + 4 * g));
+            z[0] = f.x, z[1] = f.y, z[2] = f.z, z[3] = f.w;
+        }
+        float e[16];
+        e[0] = 0.f;
+#pragma unroll
+        for (int v = 1; v < 16; v++) {
+            const int lowbit = v & -v;  // the last selected coordinate: bit 8 = z0, 4 = z1, 2 = z2, 1 = z3
+            const int ci = lowbit == 8 ? 0 : lowbit == 4 ? 1 : lowbit == 2 ? 2 : 3;
+            e[v] = __fadd_rn(e[v & (v - 1)], z[ci]);
+        }
+        float4* dst = reinterpret_cast<float4*>(tab + 16 * g);
+#pragma unroll
+        for (int v4 = 0; v4 < 4; v4++) {
+            float o[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) o[u] = HALF ? __half2float(__float2half_rn(e[4 * v4 + u])) : e[4 * v4 + u];
+            dst[v4] = make_float4(o[0], o[1], o[2], o[3]);
+        }
     }
     for (int t = warp; t < ts.T; t += LC_THREADS / 32) {
         float a = 0.f, b = 0.f;
         for (int k = ts.s[t] + lane; k < ts.e[t]; k += 32) {
-            const float x = zs[k];
+            const float x = zh ? __half2float(reinterpret_cast<const __half*>(Zq)[(int64_t)q * ldz + k])
+                                    : reinterpret_cast<const float*>(Zq)[(int64_t)q * ldz + k];
             a += x;
             b += x * x;
         }
@@ -679,7 +697,7 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     const fvs::RecSet rs{rec, RB, soff};
     if (B >= fvs_sm_count() && ts.T <= fvs::MAX_TIERS && ts.nwords <= 4 * RB / 16) {
         // large batch: one candidate per thread
-        const size_t smc = ((size_t)(D / 32) * 128 + D) * 4 + (size_t)ts.nwords * 8;
+        const size_t smc = (size_t)(D / 32) * 128 * 4 + (size_t)ts.nwords * 8;
         const dim3 grid(B, (K + fvs::LC_THREADS - 1) / fvs::LC_THREADS);
         cudaError_t e = half ? fvs_ensure_smem((const void*)fvs::lut_cand_kernel<true>, smc)
                              : fvs_ensure_smem((const void*)fvs::lut_cand_kernel<false>, smc);

@@ -2,9 +2,12 @@
 // `throughput/enginei8.py:11-16, 64-70`, which it runs as torch topk + a stable sort + scatter_add + cumsum + gathers).
 //
 // Launch 1, one CTA per query: the nprobe cells of largest fp16 routing score, ordered by (score desc, cell asc) as
-// fvs_route_topk orders them; while placing selected cell c at rank j, the CTA also takes the pair's rank inside the
-// cell's list with one atomicAdd on a per-cell cursor (first-pass columns j < n1 on cur1, the others on cur2).  The
-// probe row holds (rank in cell << 32 | cell) until launch 2 rewrites it.
+// fvs_route_topk orders them.  The keys (score, cell) sit in registers; a lower bound on the nprobe-th key comes from
+// the lanes' maxima (each warp's r-th largest by r rounds of redux.max), the keys above it (about 2-3 % of 4096) are
+// compacted into shared memory and ranked by count, and rank < nprobe selects; with more than CAND_CAP keys above the
+// bound the cut is found by histogram passes instead.  While placing selected cell c at rank j, the CTA also takes the
+// pair's rank inside the cell's list with one atomicAdd on a per-cell cursor (first-pass columns j < n1 on cur1, the
+// others on cur2).  The probe row holds (rank in cell << 32 | cell) until launch 2 rewrites it.
 // Launch 2, a grid over the pairs: every CTA scans the per-cell counts (cur1 + cur2) into offsets in shared memory,
 // then places its pairs: first-pass pairs of cell c at coff[c] + r, the others at coff[c] + cur1[c] + r (each cell's
 // first-pass pairs first, the layout of fvs_pairs_split), writes qid, the pair constant float(QM[q, c]) * mnorm[c] and
@@ -21,7 +24,9 @@ __device__ __forceinline__ uint32_t h2o(uint16_t u) { return (u & 0x8000u) ? (~u
 
 constexpr int THREADS = 256;
 constexpr int MAXP = 512;
+constexpr int CAND_CAP = 1024;  // candidates above the lower bound ranked by count; more: histogram passes
 constexpr int PLACE_THREADS = 1024;
+constexpr int LB = 4;  // cells per thread whose loads the bookkeeping CTA issues together
 constexpr int MAX_CELLS = 16384;  // per-cell offsets held in shared memory by every placing CTA
 
 template <int V>
@@ -30,8 +35,9 @@ __global__ void __launch_bounds__(THREADS) route_rank_kernel(const uint16_t* __r
                                                              int32_t* __restrict__ cur2, int64_t* __restrict__ probe) {
     __shared__ RegSelectScratch rs;
     __shared__ int s_fill;
-    __shared__ uint32_t s_sel[MAXP];
-    const int q = blockIdx.x, tid = threadIdx.x;
+    __shared__ uint32_t s_wb[THREADS / 32];
+    __shared__ __align__(16) uint32_t s_sel[CAND_CAP + 4];  // candidates (fast path) or the selected keys (radix path)
+    const int q = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const uint4* row = reinterpret_cast<const uint4*>(QM + (int64_t)q * NC);
     uint32_t key[8 * V];  // (order-preserving score << 16) | (65535 - cell); 0 = no cell
 #pragma unroll
@@ -46,6 +52,58 @@ __global__ void __launch_bounds__(THREADS) route_rank_kernel(const uint16_t* __r
             key[8 * v + e] = in ? ((h2o((uint16_t)h) << 16) | (uint32_t)(0xffff - (u * 8 + e))) : 0u;
         }
     }
+    if (tid == 0) s_fill = 0;
+    // Lower bound T0 on the nprobe-th largest key: every warp takes the r-th largest of its lanes' maxima
+    // (r = ceil(nprobe / warps); each lane maximum is a distinct key), so at least warps * r >= nprobe keys are >= the
+    // smallest of those; 0 when a warp has fewer than r lanes with keys.
+    {
+        uint32_t mx = 0u;
+#pragma unroll
+        for (int i = 0; i < 8 * V; i++) mx = max(mx, key[i]);
+        const int r = (nprobe + THREADS / 32 - 1) / (THREADS / 32);
+        uint32_t b = 0u;
+        if (r <= 32)
+            for (int it = 0; it < r; it++) {
+                b = __reduce_max_sync(0xffffffffu, mx);
+                if (mx == b) mx = 0u;
+            }
+        if (lane == 0) s_wb[warp] = b;
+    }
+    __syncthreads();
+    uint32_t T0 = 0xffffffffu;
+#pragma unroll
+    for (int w = 0; w < THREADS / 32; w++) T0 = min(T0, s_wb[w]);
+#pragma unroll
+    for (int i = 0; i < 8 * V; i++)
+        if (key[i] != 0u && key[i] >= T0) {
+            const int slot = atomicAdd(&s_fill, 1);
+            if (slot < CAND_CAP) s_sel[slot] = key[i];
+        }
+    __syncthreads();
+    const int C = s_fill;
+    if (C <= CAND_CAP) {
+        // the candidates' ranks by count (keys are unique): rank < nprobe selects, and the rank is the probe column
+        if (tid < 4) s_sel[C + tid] = 0u;  // pads the last group of four; 0 ranks below every key
+        __syncthreads();
+        const uint4* s4 = reinterpret_cast<const uint4*>(s_sel);
+        const int C4 = (C + 3) >> 2;
+        for (int i = tid; i < C; i += THREADS) {
+            const uint32_t ki = s_sel[i];
+            int rank = 0;
+            for (int j = 0; j < C4; j++) {
+                const uint4 o = s4[j];
+                rank += (int)(o.x > ki) + (int)(o.y > ki) + (int)(o.z > ki) + (int)(o.w > ki);
+            }
+            if (rank < nprobe) {
+                const int c = 0xffff - (int)(ki & 0xffffu);
+                const int rr = atomicAdd(rank < n1 ? cur1 + c : cur2 + c, 1);
+                probe[(int64_t)q * nprobe + rank] = ((int64_t)rr << 32) | (int64_t)c;
+            }
+        }
+        return;
+    }
+    // too many candidates above the bound: the exact cut by histogram passes over the register keys
+    __syncthreads();
     if (tid == 0) s_fill = 0;
     int above, equal;
     const uint32_t T = block_rth_largest_reg<8 * V>(key, nprobe, rs, &above, &equal);  // keys are unique
@@ -73,8 +131,21 @@ __device__ void scan_counts(const int32_t* __restrict__ cur1, const int32_t* __r
     const int per = (NC + PLACE_THREADS - 1) / PLACE_THREADS;
     const int b0 = tid * per;
     int local = 0;
-    for (int i = 0; i < per; i++)
-        if (b0 + i < NC) local += cur1[b0 + i] + cur2[b0 + i];
+    // the thread's cells' counts, loads issued four at a time, kept in coff until the offsets replace them
+    for (int i0 = 0; i0 < per; i0 += 4) {
+        int cnt[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            const int c = b0 + i0 + u;
+            cnt[u] = (i0 + u < per && c < NC) ? cur1[c] + cur2[c] : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++)
+            if (i0 + u < per && b0 + i0 + u < NC) {
+                coff[b0 + i0 + u] = cnt[u];
+                local += cnt[u];
+            }
+    }
     int incl = local;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -96,8 +167,9 @@ __device__ void scan_counts(const int32_t* __restrict__ cur1, const int32_t* __r
     int run = incl - local + (warp > 0 ? wsum[warp - 1] : 0);
     for (int i = 0; i < per; i++)
         if (b0 + i < NC) {
+            const int cnt = coff[b0 + i];
             coff[b0 + i] = run;
-            run += cur1[b0 + i] + cur2[b0 + i];
+            run += cnt;
         }
     __syncthreads();
 }
@@ -133,11 +205,23 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
         probe[i] = c;
     }
     if (blockIdx.x == nplace) {
-        for (int c = tid; c < NC; c += PLACE_THREADS) {
-            const int a = cur1[c], b = cur2[c];
-            o.coff[c] = s_coff[c];
-            o.ccnt[c] = a + b;
-            o.ccnt1[c] = a;
+        for (int c0 = 0; c0 < NC; c0 += LB * PLACE_THREADS) {
+            int a[LB], b[LB];
+#pragma unroll
+            for (int u = 0; u < LB; u++) {
+                const int c = c0 + u * PLACE_THREADS + tid;
+                a[u] = c < NC ? cur1[c] : 0;
+                b[u] = c < NC ? cur2[c] : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < LB; u++) {
+                const int c = c0 + u * PLACE_THREADS + tid;
+                if (c < NC) {
+                    o.coff[c] = s_coff[c];
+                    o.ccnt[c] = a[u] + b[u];
+                    o.ccnt1[c] = a[u];
+                }
+            }
         }
         for (int i = tid; i < o.nzero; i += PLACE_THREADS) o.zero[i] = 0;
         if (o.list) {
@@ -147,35 +231,50 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
             const int lane = tid & 31, warp = tid >> 5;
             if (tid == 0) base[0] = base[1] = 0;
             __syncthreads();
-            for (int c0 = 0; c0 < NC; c0 += PLACE_THREADS) {
-                const int ii = c0 + tid;
-                const int c = ii < NC ? order[ii] : -1;
-                const bool k1 = c >= 0 && cur1[c] > 0;
-                const bool k2 = c >= 0 && cur1[c] + cur2[c] > 0;
-                const unsigned m1 = __ballot_sync(0xffffffffu, k1), m2 = __ballot_sync(0xffffffffu, k2);
-                if (lane == 0) {
-                    wsum[0][warp] = __popc(m1);
-                    wsum[1][warp] = __popc(m2);
+            for (int c0 = 0; c0 < NC; c0 += LB * PLACE_THREADS) {
+                // the chunk's order entries, then their counts, loaded together; then one pass per 1024 cells
+                int cc[LB], a1[LB], a2[LB];
+#pragma unroll
+                for (int u = 0; u < LB; u++) {
+                    const int ii = c0 + u * PLACE_THREADS + tid;
+                    cc[u] = ii < NC ? order[ii] : -1;
                 }
-                __syncthreads();
-                int b1 = base[0], b2 = base[1], t1 = 0, t2 = 0;
-                for (int w = 0; w < PLACE_THREADS / 32; w++) {
-                    if (w < warp) {
-                        b1 += wsum[0][w];
-                        b2 += wsum[1][w];
+#pragma unroll
+                for (int u = 0; u < LB; u++) {
+                    a1[u] = cc[u] >= 0 ? cur1[cc[u]] : 0;
+                    a2[u] = cc[u] >= 0 ? cur2[cc[u]] : 0;
+                }
+#pragma unroll
+                for (int u = 0; u < LB; u++) {
+                    if (c0 + u * PLACE_THREADS >= NC) break;  // uniform over the block
+                    const int c = cc[u];
+                    const bool k1 = c >= 0 && a1[u] > 0;
+                    const bool k2 = c >= 0 && a1[u] + a2[u] > 0;
+                    const unsigned m1 = __ballot_sync(0xffffffffu, k1), m2 = __ballot_sync(0xffffffffu, k2);
+                    if (lane == 0) {
+                        wsum[0][warp] = __popc(m1);
+                        wsum[1][warp] = __popc(m2);
                     }
-                    t1 += wsum[0][w];
-                    t2 += wsum[1][w];
+                    __syncthreads();
+                    int b1 = base[0], b2 = base[1], t1 = 0, t2 = 0;
+                    for (int w = 0; w < PLACE_THREADS / 32; w++) {
+                        if (w < warp) {
+                            b1 += wsum[0][w];
+                            b2 += wsum[1][w];
+                        }
+                        t1 += wsum[0][w];
+                        t2 += wsum[1][w];
+                    }
+                    const unsigned below = (1u << lane) - 1u;
+                    if (k1) o.list1[b1 + __popc(m1 & below)] = c;
+                    if (k2) o.list[b2 + __popc(m2 & below)] = c;
+                    __syncthreads();
+                    if (tid == 0) {
+                        base[0] += t1;
+                        base[1] += t2;
+                    }
+                    __syncthreads();
                 }
-                const unsigned below = (1u << lane) - 1u;
-                if (k1) o.list1[b1 + __popc(m1 & below)] = c;
-                if (k2) o.list[b2 + __popc(m2 & below)] = c;
-                __syncthreads();
-                if (tid == 0) {
-                    base[0] += t1;
-                    base[1] += t2;
-                }
-                __syncthreads();
             }
             if (tid == 0) {
                 o.nlist[0] = base[0];

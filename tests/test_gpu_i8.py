@@ -387,7 +387,7 @@ def test_pairs_split(eng, n1):
 
 
 @pytest.mark.parametrize("B,NC,npr,n1", [(300, 4096, 72, 13), (37, 8192, 256, 30), (1000, 16384, 512, 1),
-                                          (64, 8, 8, 8), (513, 4096, 352, 23)])
+                                          (64, 8, 8, 8), (513, 4096, 352, 23), (200, 2048, 128, 64)])
 def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1):
     """fvs_route_pairs (routing selection + both pair lists + cell lists in two launches) gives the probe list of
     fvs_route_topk, the pair layout of fvs_pairs_split and the lists of fvs_cell_lists, also through tied scores; its
@@ -616,6 +616,33 @@ def test_packed_records_match_planes(golden_i8, eng):
             ix.rec = rec
             np.testing.assert_array_equal(c(a[0]), c(b[0]))
             np.testing.assert_array_equal(c(a[1]), c(b[1]))
+
+
+@pytest.mark.parametrize("K", [100, 128, 40, 200])
+def test_packed_records_large_batch_match_planes(golden_i8, eng, K):
+    """the large-batch record kernel (one candidate per thread, one CTA per query and slice of 128 candidates: one
+    partly filled slice at K = 100 and 40, a full one at 128, two at 200) equals stage 2 from the separate planes (one
+    warp per candidate, the same products summed in another order) within fp32 rounding, on a batch above the SM
+    count; rows past ncnt read as no candidate in both"""
+    f = golden_i8
+    E, ix, idx, _, nprobe, k, M = _golden_engine(eng, f, "A_")
+    B = 301
+    Q0 = torch.from_numpy(f["Q"]).to(DEV)
+    g = torch.Generator().manual_seed(11)
+    Q = (Q0[torch.randint(0, Q0.shape[0], (B,), generator=g).to(DEV)]
+         + 0.05 * torch.randn(B, Q0.shape[1], generator=g).to(DEV)).contiguous()
+    QC = (Q @ ix.c).contiguous()
+    pos = torch.randint(0, ix.N, (B, K), generator=g).to(DEV)
+    Zq = E.rotated_query(Q)
+    ncnt = torch.randint(1, K + 1, (B,), generator=g, dtype=torch.int32).to(DEV)
+    for half in (True, False):
+        for nc in (None, ncnt):
+            a = E.score_lut_zq(QC, pos, Zq, nc, half)
+            rec, ix.rec = ix.rec, None
+            b = E.score_lut_zq(QC, pos, Zq, nc, half)
+            ix.rec = rec
+            np.testing.assert_allclose(c(a[0]), c(b[0]), rtol=1e-5, atol=1e-5)
+            np.testing.assert_allclose(c(a[1]), c(b[1]), rtol=1e-5, atol=1e-6)
 
 
 def test_empty_batch_and_argument_errors(eng):
