@@ -1,6 +1,8 @@
 // Selection kernels: first-pass threshold, stage-1 top-K (+ delta rule), top-k merge across shards.
 // One CTA per query; candidates are staged in shared memory, the k-th bound is found by a block-wide MSB-first radix
 // select on order-preserving integer keys, the winners are compacted and sorted with a bitonic network.
+#include <cstddef>
+
 #include "fvs_common.cuh"
 
 namespace fvs {
@@ -181,6 +183,7 @@ __global__ void select_topk_kernel(const float* __restrict__ bval, const int32_t
 // the K winners are placed by rank, one per thread.
 constexpr int SELR_MAXK = 512;
 constexpr int SELR_MAXM = 8192;
+constexpr int SELR_CAND_CAP = 2048;
 template <int NT>
 struct SelRegShared {
     SelectScratch ss;
@@ -189,6 +192,8 @@ struct SelRegShared {
     int fill, ncnt;
     float dval;
     unsigned long long sb[NT];
+    // candidates above the lane-maxima bound (select_rank_bound), read as 16-byte pairs
+    alignas(16) unsigned long long cb[SELR_CAND_CAP + 2];
 };
 
 // the K largest (score key, position key) pairs of the n > K candidates, unordered, into sh.sb
@@ -232,6 +237,73 @@ __device__ __forceinline__ void select_reg_cut(const float* __restrict__ bv, con
         }
 }
 
+// The K <= NT largest of n > K candidates, placed in order: est1 / pos at each key's rank, the keys at sh.sb[rank],
+// sh.dval at rank didx.  A lower bound on the K-th largest score key: every thread keeps the maxima of four disjoint
+// subsets of its scores (one per float4 component), each a distinct candidate, so at least K candidates reach the
+// K-th largest of those 4 * NT maxima (found by histogram passes over four keys per thread; 0 when fewer than K
+// maxima exist).  With 4 * NT well above K the candidates at or above it number about 1.1 K; they are compacted into
+// sh.cb and ranked by count on the unique (score key, position key) pairs.  Two strided passes over the scores (the
+// second from L2), for any n.  Returns false, with nothing written, when more than SELR_CAND_CAP candidates reach
+// the bound (many equal scores).
+template <int NT>
+__device__ __forceinline__ bool select_rank_bound(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
+                                                  int K, SelRegShared<NT>& sh, float* __restrict__ est1q,
+                                                  int64_t* __restrict__ posq, int didx) {
+    const int tid = threadIdx.x;
+    const float4* bv4 = reinterpret_cast<const float4*>(bv);
+    uint32_t mx[4] = {0u, 0u, 0u, 0u};  // subset maxima (0 = empty subset; a finite score's key is never 0)
+    for (int u = tid; 4 * u < n; u += NT) {
+        const float4 w = __ldcg(bv4 + u);
+        mx[0] = max(mx[0], f2o(w.x));
+        if (4 * u + 1 < n) mx[1] = max(mx[1], f2o(w.y));
+        if (4 * u + 2 < n) mx[2] = max(mx[2], f2o(w.z));
+        if (4 * u + 3 < n) mx[3] = max(mx[3], f2o(w.w));
+    }
+    const int nz = block_sum_int((int)(mx[0] != 0u) + (int)(mx[1] != 0u) + (int)(mx[2] != 0u) + (int)(mx[3] != 0u),
+                                 sh.red);
+    uint32_t T0 = 0u;
+    if (nz >= K) {
+        int gt, eq;
+        T0 = block_rth_largest_reg<4>(mx, K, sh.rs, &gt, &eq);
+    }
+    // the scores again, the ones at or above the bound compacted with their positions
+    for (int u = tid; 4 * u < n; u += NT) {
+        const float4 w = __ldcg(bv4 + u);
+        const float f4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const uint32_t h = f2o(f4[e]);
+            if (4 * u + e < n && h >= T0) {
+                const int slot = atomicAdd(&sh.fill, 1);
+                if (slot < SELR_CAND_CAP)
+                    sh.cb[slot] = ((unsigned long long)h << 32) | (0xffffffffu - (uint32_t)bp[4 * u + e]);
+            }
+        }
+    }
+    __syncthreads();
+    const int C = sh.fill;
+    if (C > SELR_CAND_CAP) return false;  // uniform over the block
+    if (tid == 0) sh.cb[C] = 0ull;        // pads an odd count; 0 ranks below every key
+    __syncthreads();
+    const ulonglong2* c2 = reinterpret_cast<const ulonglong2*>(sh.cb);
+    const int C2 = (C + 1) >> 1;
+    for (int i = tid; i < C; i += NT) {
+        const unsigned long long ki = sh.cb[i];
+        int rank = 0;
+        for (int j = 0; j < C2; j++) {
+            const ulonglong2 o = c2[j];
+            rank += (int)(o.x > ki) + (int)(o.y > ki);
+        }
+        if (rank < K) {
+            est1q[rank] = o2f((uint32_t)(ki >> 32));
+            posq[rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
+            sh.sb[rank] = ki;
+            if (rank == didx) sh.dval = o2f((uint32_t)(ki >> 32));
+        }
+    }
+    return true;
+}
+
 // the same for n > SELR_MAXM candidates: keys read from global memory in every radix pass
 template <int NT>
 __device__ __forceinline__ void select_glob_cut(const float* __restrict__ bv, const int32_t* __restrict__ bp, int n,
@@ -267,6 +339,7 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
     const float* __restrict__ bval, const int32_t* __restrict__ bpos, const int32_t* __restrict__ cnt, int M, int K,
     int64_t* __restrict__ pos, float* __restrict__ est1, uint8_t* __restrict__ ok, int32_t* __restrict__ ncnt,
     float delta, int didx) {
+    static_assert(offsetof(SelRegShared<NT>, cb) % 16 == 0, "the candidates are read as 16-byte pairs");
     __shared__ SelRegShared<NT> sh;
     const int q = blockIdx.x, tid = threadIdx.x;
     const int c = cnt[q];
@@ -274,10 +347,20 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
     const float* bv = bval + (int64_t)q * M;
     const int32_t* bp = bpos + (int64_t)q * M;
     if (tid == 0) sh.fill = 0;
+    bool placed = false;  // est1 / pos / sh.sb already in rank order
     if (n <= K) {
         const unsigned long long filler = cand_key(kNeg, 0);
         for (int i = tid; i < K; i += NT) sh.sb[i] = i < n ? cand_key(bv[i], bp[i]) : filler;
     } else {
+        if (K <= NT) {
+            placed = select_rank_bound<NT>(bv, bp, n, K, sh, est1 + (int64_t)q * K, pos + (int64_t)q * K, didx);
+            if (!placed) {
+                __syncthreads();  // every thread has read the candidate count
+                if (tid == 0) sh.fill = 0;
+            }
+        }
+    }
+    if (!placed && n > K) {
         const int nv = (n + 4 * NT - 1) / (4 * NT);  // uniform over the block
         if (n > SELR_MAXM)
             select_glob_cut<NT>(bv, bp, n, K, sh);
@@ -291,9 +374,10 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
             select_reg_cut<NT, 8>(bv, bp, n, K, sh);
     }
     if (K <= 128) {
-        // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal)
+        // order by rank: entry i goes to place #{greater} + #{equal before it} (the fill entries are equal); the
+        // bound-and-rank selection has placed its keys already
         __syncthreads();
-        for (int i = tid; i < K; i += NT) {
+        for (int i = tid; i < K && !placed; i += NT) {
             const unsigned long long ki = sh.sb[i];
             int rank = 0;
             for (int j = 0; j < K; j++) {
@@ -304,7 +388,7 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
             pos[(int64_t)q * K + rank] = (int64_t)(0xffffffffu - (uint32_t)ki);
             if (rank == didx) sh.dval = o2f((uint32_t)(ki >> 32));
         }
-    } else {
+    } else if (!placed) {
         // larger K: a bitonic sort of the K keys (descending; real keys are unique, the fill entries are equal), padded
         // to a power of two kp <= NT with key 0, thread t holding position t: exchanges at distances below 32 go
         // through warp shuffles, the longer ones through shared memory (10 barrier pairs at kp = 512 instead of a

@@ -217,24 +217,30 @@ def test_graph_search_and_fallback(eng):
     np.testing.assert_array_equal(c(I2), c(I))
 
 
-@pytest.mark.parametrize("M,K,kind", [(700, 50, "ties"), (701, 50, "ties"), (4000, 100, "ties"), (4000, 100, "cont"),
-                                       (8192, 100, "cont"), (8192, 100, "ties"), (8196, 100, "cont"),
-                                       (16384, 100, "cont"), (16384, 250, "ties"), (4000, 400, "ties"), (16384, 500, "cont"),
-                                       (1400, 600, "ties")])
-def test_select_topk_ties(eng, M, K, kind):
+@pytest.mark.parametrize("M,K,kind,B", [(700, 50, "ties", 7), (701, 50, "ties", 7), (4000, 100, "ties", 7),
+                                         (4000, 100, "cont", 7), (8192, 100, "cont", 7), (8192, 100, "ties", 7),
+                                         (8196, 100, "cont", 7), (16384, 100, "cont", 7), (16384, 250, "ties", 7),
+                                         (4000, 400, "ties", 7), (16384, 500, "cont", 7), (1400, 600, "ties", 7),
+                                         (4000, 100, "flat", 7), (700, 50, "cont", 300), (4000, 100, "ties", 300),
+                                         (8192, 100, "cont", 300), (8192, 100, "ties", 300), (8192, 128, "cont", 300),
+                                         (4000, 100, "flat", 300), (8192, 100, "flat", 300), (2048, 129, "ties", 300)])
+def test_select_topk_ties(eng, M, K, kind, B):
     """stage-1 top-K orders by (estimate desc, position asc), also through ties and cnt < K, cnt > M; register-resident
-    kernel (M a multiple of 4, K <= 512; more than 8192 candidates by its global-memory branch) and shared-memory
-    kernel (the other shapes)."""
+    kernel (M a multiple of 4, K <= 512; more than 8192 candidates by its global-memory branch; K <= 128 by the
+    bound-and-rank selection, which falls back to histogram passes when more than 1024 candidates reach its bound, as
+    with equal scores) at 1024 threads per query (B below the SM count) and 256 (B = 300), and shared-memory kernel
+    (the other shapes)."""
     L = pkg("_lib")
     lib = L.lib()
     rng = np.random.default_rng(0)
-    B = 7
     if kind == "ties":
         vals = rng.integers(-20, 20, (B, M)).astype(np.float32) / 4  # many ties
+    elif kind == "flat":
+        vals = np.full((B, M), 1.5, np.float32)                     # every score equal
     else:
         vals = (rng.standard_normal((B, M)) * 3).astype(np.float32)
     posv = np.stack([rng.permutation(100000)[:M] for _ in range(B)]).astype(np.int32)
-    cnt = np.array([0, 10, K - 1, K, K + 1, M, M + 200], np.int32)
+    cnt = np.resize(np.array([0, 10, K - 1, K, K + 1, M, M + 200, M // 2, M // 3 + 1, 3 * K], np.int32), B)
     tv, tp, tc = (torch.from_numpy(x).to(DEV) for x in (vals, posv, cnt))
     pos = torch.empty(B, K, dtype=torch.int64, device=DEV)
     est = torch.empty(B, K, device=DEV)
