@@ -124,6 +124,123 @@ __global__ void __launch_bounds__(THREADS) route_rank_kernel(const uint16_t* __r
     }
 }
 
+// Launch 1 with a per-cell routing scale (the default engine's routing, `src/engine_cell.py:40-42`): the nprobe cells
+// of largest float(QM[q, c]) * sc[c] (fp32 product, as fvs_route_topk_scaled), ordered by (score desc, cell asc), on
+// 64-bit keys (score key << 32 | ~cell).  The lower bound comes from four subset maxima per thread (one per cell
+// index mod 4), its K-th largest over the block found by histogram passes; the cells at or above it are compacted and
+// ranked by count.  More than CAND_CAP cells above the bound (many equal scores): the exact cut by histogram passes
+// over the score keys, then over the cell keys of the scores tied with it.  Cursors and probe rows as launch 1.
+template <int V>
+__global__ void __launch_bounds__(THREADS) route_rank_scaled_kernel(const uint16_t* __restrict__ QM,
+                                                                    const float* __restrict__ sc, int NC, int nprobe,
+                                                                    int n1, int32_t* __restrict__ cur1,
+                                                                    int32_t* __restrict__ cur2,
+                                                                    int64_t* __restrict__ probe) {
+    __shared__ RegSelectScratch rs;
+    __shared__ SelectScratch ss;
+    __shared__ int s_red[32];
+    __shared__ int s_fill;
+    __shared__ __align__(16) unsigned long long s_key[CAND_CAP + 2];  // read as 16-byte pairs
+    const int q = blockIdx.x, tid = threadIdx.x;
+    const uint16_t* qrow = QM + (int64_t)q * NC;
+    uint32_t hk[8 * V];  // score keys; 0 = no cell (a finite score's key is never 0)
+#pragma unroll
+    for (int v = 0; v < V; v++) {
+        const int u = tid + v * THREADS;
+        const bool in = u * 8 < NC;
+        const uint4 w = in ? __ldg(reinterpret_cast<const uint4*>(qrow) + u) : make_uint4(0u, 0u, 0u, 0u);
+        const float4 s0 = in ? __ldg(reinterpret_cast<const float4*>(sc) + 2 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 s1 = in ? __ldg(reinterpret_cast<const float4*>(sc) + 2 * u + 1) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+        const float ss8[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const __half h = __ushort_as_half((unsigned short)((ws[e >> 1] >> (16 * (e & 1))) & 0xffffu));
+            hk[8 * v + e] = in ? f2o(__fmul_rn(__half2float(h), ss8[e])) : 0u;
+        }
+    }
+    if (tid == 0) s_fill = 0;
+    uint32_t mx[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int i = 0; i < 8 * V; i++) mx[i & 3] = max(mx[i & 3], hk[i]);
+    const int nz =
+        block_sum_int((int)(mx[0] != 0u) + (int)(mx[1] != 0u) + (int)(mx[2] != 0u) + (int)(mx[3] != 0u), s_red);
+    uint32_t T0 = 0u;
+    if (nz >= nprobe) {
+        int gt, eq;
+        T0 = block_rth_largest_reg<4>(mx, nprobe, rs, &gt, &eq);
+    }
+#pragma unroll
+    for (int v = 0; v < V; v++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const uint32_t h = hk[8 * v + e];
+            if (h != 0u && h >= T0) {
+                const int slot = atomicAdd(&s_fill, 1);
+                if (slot < CAND_CAP)
+                    s_key[slot] = ((unsigned long long)h << 32) | (0xffffffffu - (uint32_t)(8 * (tid + v * THREADS) + e));
+            }
+        }
+    __syncthreads();
+    const int C = s_fill;
+    if (C <= CAND_CAP) {
+        if (tid == 0) s_key[C] = 0ull;  // pads an odd count; 0 ranks below every key
+        __syncthreads();
+        const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(s_key);
+        const int C2 = (C + 1) >> 1;
+        for (int i = tid; i < C; i += THREADS) {
+            const unsigned long long ki = s_key[i];
+            int rank = 0;
+            for (int j = 0; j < C2; j++) {
+                const ulonglong2 o = k2[j];
+                rank += (int)(o.x > ki) + (int)(o.y > ki);
+            }
+            if (rank < nprobe) {
+                const int c = (int)(0xffffffffu - (uint32_t)ki);
+                const int rr = atomicAdd(rank < n1 ? cur1 + c : cur2 + c, 1);
+                probe[(int64_t)q * nprobe + rank] = ((int64_t)rr << 32) | (int64_t)c;
+            }
+        }
+        return;
+    }
+    __syncthreads();
+    if (tid == 0) s_fill = 0;
+    int gt, eq;
+    const uint32_t Th = block_rth_largest_reg<8 * V>(hk, nprobe, rs, &gt, &eq);
+    uint32_t Tl = 0u;
+    if (eq > nprobe - gt)  // scores equal to the cut straddle it: the smallest cells among them fill the places left
+        Tl = block_select_rth_largest<32, uint32_t>(
+            [&](int i) {
+                return f2o(__fmul_rn(__half2float(__ushort_as_half(qrow[i])), sc[i])) == Th ? (0xffffffffu - (uint32_t)i)
+                                                                                           : 0u;
+            },
+            NC, nprobe - gt, ss);
+    const unsigned long long T = ((unsigned long long)Th << 32) | Tl;
+#pragma unroll
+    for (int v = 0; v < V; v++)
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const uint32_t h = hk[8 * v + e];
+            if (h != 0u && h >= Th) {
+                const unsigned long long k =
+                    ((unsigned long long)h << 32) | (0xffffffffu - (uint32_t)(8 * (tid + v * THREADS) + e));
+                if (k >= T) {  // unique keys: exactly nprobe of them
+                    const int slot = atomicAdd(&s_fill, 1);
+                    if (slot < nprobe) s_key[slot] = k;
+                }
+            }
+        }
+    __syncthreads();
+    for (int i = tid; i < nprobe; i += THREADS) {
+        const unsigned long long ki = s_key[i];
+        int rank = 0;
+        for (int j = 0; j < nprobe; j++) rank += s_key[j] > ki;
+        const int c = (int)(0xffffffffu - (uint32_t)ki);
+        const int rr = atomicAdd(rank < n1 ? cur1 + c : cur2 + c, 1);
+        probe[(int64_t)q * nprobe + rank] = ((int64_t)rr << 32) | (int64_t)c;
+    }
+}
+
 // exclusive scan of cur1[c] + cur2[c] over the NC cells into coff (shared memory), by one block of PLACE_THREADS
 __device__ void scan_counts(const int32_t* __restrict__ cur1, const int32_t* __restrict__ cur2, int NC, int* coff) {
     __shared__ int wsum[32];
@@ -302,27 +419,36 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
 }  // namespace rp
 }  // namespace fvs
 
-extern "C" int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
-                               const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid, float* qcp,
-                               int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
-                               int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work) {
+static int route_pairs_run(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
+                           const float* sc, const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid,
+                           float* qcp, int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
+                           int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work) {
     using namespace fvs::rp;
     FVS_CHECK_ARG(QM && probe && qid && qcp && coff && ccnt && ccnt1 && work && B >= 0 && NC > 0);
     FVS_CHECK_ARG(nprobe >= 1 && nprobe <= NC && n1 >= 1 && n1 <= nprobe && nzero >= 0);
     FVS_CHECK_ARG(order == nullptr || (list1 && list && nlist));
     FVS_CHECK_ARG(nzero == 0 || zero != nullptr);
     if (NC % 8 != 0 || ((uintptr_t)QM & 15) != 0 || nprobe > MAXP || NC > MAX_CELLS) return FVS_ERANGE;
+    if (sc != nullptr && ((uintptr_t)sc & 15) != 0) return FVS_ERANGE;
     if (B == 0) return FVS_OK;
     int32_t *cur1 = work, *cur2 = work + NC, *done = work + 2 * NC;
     const int V = (NC + THREADS * 8 - 1) / (THREADS * 8);
+#define FVS_RR(VV)                                                                                                    \
+    do {                                                                                                              \
+        if (sc)                                                                                                       \
+            route_rank_scaled_kernel<VV><<<B, THREADS, 0, stream>>>(QM, sc, NC, nprobe, n1, cur1, cur2, probe);       \
+        else                                                                                                          \
+            route_rank_kernel<VV><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);                  \
+    } while (0)
     if (V <= 1)
-        route_rank_kernel<1><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+        FVS_RR(1);
     else if (V <= 2)
-        route_rank_kernel<2><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+        FVS_RR(2);
     else if (V <= 4)
-        route_rank_kernel<4><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+        FVS_RR(4);
     else
-        route_rank_kernel<8><<<B, THREADS, 0, stream>>>(QM, NC, nprobe, n1, cur1, cur2, probe);
+        FVS_RR(8);
+#undef FVS_RR
     const int64_t npairs = (int64_t)B * nprobe;
     const int nsm = fvs_sm_count();
     int grid = (int)((npairs + PLACE_THREADS * 2 - 1) / (PLACE_THREADS * 2));
@@ -335,4 +461,22 @@ extern "C" int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, i
     pairs_place_kernel<<<grid + 1, PLACE_THREADS, sm, stream>>>(probe, B, nprobe, n1, NC, (const __half*)QM, mnorm, order,
                                                             cur1, cur2, o);
     return fvs_launch_status();
+}
+
+extern "C" int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
+                               const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid, float* qcp,
+                               int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
+                               int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work) {
+    return route_pairs_run(stream, QM, B, NC, nprobe, n1, nullptr, mnorm, order, probe, qid, qcp, coff, ccnt, ccnt1,
+                           slot, list1, list, nlist, zero, nzero, work);
+}
+
+extern "C" int fvs_route_pairs_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
+                                      const float* sc, const float* mnorm, const int32_t* order, int64_t* probe,
+                                      int32_t* qid, float* qcp, int32_t* coff, int32_t* ccnt, int32_t* ccnt1,
+                                      int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero,
+                                      int nzero, int32_t* work) {
+    FVS_CHECK_ARG(sc != nullptr);
+    return route_pairs_run(stream, QM, B, NC, nprobe, n1, sc, mnorm, order, probe, qid, qcp, coff, ccnt, ccnt1, slot,
+                           list1, list, nlist, zero, nzero, work);
 }

@@ -123,7 +123,40 @@ class EngineB200S(EngineB200I8):
                    ptr(ix.tab), ix.L, ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc),
                    mb or ix.MB)
 
-    def stage1_trellis(self, Qb, QM, probe, K, rho_override=None, M_override=None, Qh=None):
+    def trellis_passes(self, K, nprobe, rho_override=None):
+        """(rho, n1) of the batched trellis stage 1: (beta, rho) = (1.1, 0.75) for K <= 400 else (0.7, 0.5), (1.5,
+        rho_override) for the recompute; n1 = the first pass's probe columns (`src/s1cell.py:176-184`)."""
+        ix = self.ix
+        beta, rho = (1.1, 0.75) if K <= 400 else (0.7, 0.5)
+        if rho_override:
+            beta, rho = 1.5, rho_override
+        return rho, min(max(int(np.ceil(beta * K / (ix.N / ix.NC / BN + 1))), 1), nprobe)
+
+    def route_pairs(self, QM, nprobe, n1):
+        """`(QM.float() * inv_mnorm).topk(nprobe)` (`src/engine_cell.py:40-42`) and both passes' `_pairs_static` lists
+        (`src/s1cell.py:170-175, 184, 192`) in two launches (fvs_route_pairs_scaled), with the scan's cell lists and
+        cleared emit counters.  Returns probe and the pair tuple stage1_trellis takes."""
+        ix = self.ix
+        B = QM.shape[0]
+        dev = QM.device
+        work = self.__dict__.get("_rp_work")
+        if work is None:
+            work = self._rp_work = torch.zeros(2 * ix.NC + 1, dtype=torch.int32, device=dev)
+        probe = torch.empty(B, nprobe, dtype=torch.int64, device=dev)
+        n = B * nprobe
+        qid = torch.empty(n, dtype=torch.int32, device=dev)
+        qcp = torch.empty(n, device=dev)
+        coff, ccnt, ccnt1, list1, lst = (torch.empty(ix.NC, dtype=torch.int32, device=dev) for _ in range(5))
+        slot = torch.empty(B * n1, dtype=torch.int32, device=dev)
+        nl = torch.empty(2, dtype=torch.int32, device=dev)
+        cnt = torch.empty(B, dtype=torch.int32, device=dev)
+        self._call("route_pairs", self.L.fvs_route_pairs_scaled, ptr(QM), B, ix.NC, nprobe, n1, ptr(ix.inv_mnorm),
+                   ptr(ix.mnorm), ptr(ix.cell_order), ptr(probe), ptr(qid), ptr(qcp), ptr(coff), ptr(ccnt), ptr(ccnt1),
+                   ptr(slot), ptr(list1), ptr(lst), ptr(nl), ptr(cnt), B, ptr(work))
+        self.launches += 1   # two kernels
+        return probe, (qid, coff, ccnt, ccnt1, qcp, slot, list1, lst, nl, cnt)
+
+    def stage1_trellis(self, Qb, QM, probe, K, rho_override=None, M_override=None, Qh=None, pairs=None):
         """`s1cell.search_static` (`src/s1cell.py:176-195`) on the C library: returns pos [B,K] int64, ok [B] bool,
         est1 [B,K]."""
         ix, L = self.ix, self.L
@@ -131,22 +164,23 @@ class EngineB200S(EngineB200I8):
         dev = Qb.device
         if Qh is None:
             Qh = (Qb @ ix.W1).half().contiguous()
-        beta, rho = (1.1, 0.75) if K <= 400 else (0.7, 0.5)
-        if rho_override:
-            beta, rho = 1.5, rho_override
         M = M_override or self.M or max(4096, 16 * K)
         nprobe = probe.shape[1]
-        n1 = min(max(int(np.ceil(beta * K / (ix.N / ix.NC / BN + 1))), 1), nprobe)
+        rho, n1 = self.trellis_passes(K, nprobe, rho_override)
         probe = probe.contiguous()
-        # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
-        qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
         l1 = l2 = None
-        if self.cells_scan():
-            cnt = torch.empty(B, dtype=torch.int32, device=dev)            # cleared by the list kernel
-            list1, lst, nl = self.cell_lists(ccnt1, ccnt, cnt)
+        if pairs is not None:             # from route_pairs: pair lists, cell lists, cleared counters
+            qid, coff, ccnt, ccnt1, qcp, slot, list1, lst, nl, cnt = pairs
             l1, l2 = (list1, nl[0:1]), (lst, nl[1:2])
         else:
-            cnt = torch.zeros(B, dtype=torch.int32, device=dev)
+            # one pair list serves both passes: each cell's pairs from the first n1 probe columns come first
+            qid, coff, ccnt, ccnt1, qcp, slot = self.pairs_split(probe, n1, QM)
+            if self.cells_scan():
+                cnt = torch.empty(B, dtype=torch.int32, device=dev)            # cleared by the list kernel
+                list1, lst, nl = self.cell_lists(ccnt1, ccnt, cnt)
+                l1, l2 = (list1, nl[0:1]), (lst, nl[1:2])
+            else:
+                cnt = torch.zeros(B, dtype=torch.int32, device=dev)
         bmc = torch.empty(qid.numel() * ix.MB, device=dev)   # block-maxima rows addressed by pair position
         self._scan(0, "trellis_scan_first", Qh, B, qid, coff, ccnt1, qcp, None, None, None, None, 0, bmc, lists=l1)
         t0 = torch.empty(B, device=dev)
@@ -241,11 +275,16 @@ class EngineB200S(EngineB200I8):
         if K <= k:
             raise ValueError("need K > k")
         QC = (Qb @ self.ix.c).contiguous()
-        QM, probe = self.route(Qb, nprobe)
-        if len(Qb) <= self.SMALL:
-            pos, ok, est1 = self.stage1_small(Qb, QM, probe, K)
+        if len(Qb) > self.SMALL and self.cells_scan() and self.fused_routing(len(Qb), nprobe):
+            QM = (Qb.half() @ self.ix.means16.T).contiguous()
+            probe, pairs = self.route_pairs(QM, nprobe, self.trellis_passes(K, nprobe)[1])
+            pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K, pairs=pairs)
         else:
-            pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K)
+            QM, probe = self.route(Qb, nprobe)
+            if len(Qb) <= self.SMALL:
+                pos, ok, est1 = self.stage1_small(Qb, QM, probe, K)
+            else:
+                pos, ok, est1 = self.stage1_trellis(Qb, QM, probe, K)
         self._last.update(probe=probe, QM=QM, QC=QC, est1=est1)
         I, reads, ids = self._finish_s(Qb, QC, pos, z, k)
         return ok, I, reads, ids

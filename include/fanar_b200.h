@@ -116,6 +116,19 @@ int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int 
                     int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero,
                     int nzero, int32_t* work);
 
+/*
+ * fvs_route_pairs with a per-cell routing scale: the nprobe cells of largest float(QM[q, c]) * sc[c] (fp32 product,
+ * ties by smaller cell), as fvs_route_topk_scaled (the default engine's routing `(QM.float() * inv_mnorm).topk(nprobe)`,
+ * `src/engine_cell.py:40-42`), then the pair lists, cell lists and cleared counters exactly as fvs_route_pairs (pair
+ * constant float(QM[q, c]) * mnorm[c], or float(QM[q, c]) when mnorm is NULL: the default engine's `_pairs_static`
+ * for both passes, `src/s1cell.py:170-175, 184, 192`).  sc 16-byte aligned; the other conditions and the work buffer
+ * as fvs_route_pairs.
+ */
+int fvs_route_pairs_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1, const float* sc,
+                           const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid, float* qcp,
+                           int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list,
+                           int32_t* nlist, int32_t* zero, int nzero, int32_t* work);
+
 /* Rows per tile of the int8 scan (a multiple of the reference's 32-row block).  Host-side helper. */
 int fvs_i8_tile_rows(void);
 

@@ -392,19 +392,28 @@ def test_pairs_split(eng, n1):
     np.testing.assert_array_equal(gqc[gs], want)
 
 
-@pytest.mark.parametrize("B,NC,npr,n1", [(300, 4096, 72, 13), (37, 8192, 256, 30), (1000, 16384, 512, 1),
-                                          (64, 8, 8, 8), (513, 4096, 352, 23), (200, 2048, 128, 64)])
-def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1):
+@pytest.mark.parametrize("B,NC,npr,n1,scaled", [(300, 4096, 72, 13, 0), (37, 8192, 256, 30, 0),
+                                                 (1000, 16384, 512, 1, 0), (64, 8, 8, 8, 0), (513, 4096, 352, 23, 0),
+                                                 (200, 2048, 128, 64, 0), (300, 8192, 256, 40, 1),
+                                                 (300, 8192, 256, 40, 2), (37, 4096, 72, 13, 1),
+                                                 (1000, 16384, 512, 1, 2), (64, 8, 8, 8, 1), (200, 2048, 400, 64, 2)])
+def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1, scaled):
     """fvs_route_pairs (routing selection + both pair lists + cell lists in two launches) gives the probe list of
     fvs_route_topk, the pair layout of fvs_pairs_split and the lists of fvs_cell_lists, also through tied scores; its
-    cursors are left zero, so a second call on the same work buffer gives the same result."""
+    cursors are left zero, so a second call on the same work buffer gives the same result.  fvs_route_pairs_scaled
+    (scaled = 1: pair constants with the norm factor, 2: without, as the default engine) gives the probe list of
+    fvs_route_topk_scaled, also through scores tied after the scaling."""
     L = pkg("_lib")
     lib = L.lib()
     rng = np.random.default_rng(B + NC)
     QM = (rng.integers(-300, 300, (B, NC)) / 512).astype(np.float16)        # many ties
     mnorm = (rng.random(NC) + 0.5).astype(np.float32)
+    if scaled == 2:
+        mnorm = np.ones(NC, np.float32)           # no norm factor: the kernel's constant float(QM) equals QM * 1
+    sc = np.where(rng.random(NC) < 0.5, 1.0, rng.random(NC) + 0.5).astype(np.float32)   # many equal scales
     order = np.argsort(-rng.integers(0, 50, NC), kind="stable").astype(np.int32)
-    tq, tm, to = (torch.from_numpy(x).to(DEV) for x in (QM, mnorm, order))
+    tq, tm, to, tsc = (torch.from_numpy(x).to(DEV) for x in (QM, mnorm, order, sc))
+    mptr = None if scaled == 2 else L.ptr(tm)
     work = torch.zeros(2 * NC + 1, dtype=torch.int32, device=DEV)
     outs = []
     for _ in range(2):
@@ -415,9 +424,13 @@ def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1):
         slot = torch.empty(B * n1, dtype=torch.int32, device=DEV)
         nl = torch.empty(2, dtype=torch.int32, device=DEV)
         zero = torch.ones(B, dtype=torch.int32, device=DEV)
-        L.check(lib.fvs_route_pairs(L.stream_handle(), L.ptr(tq), B, NC, npr, n1, L.ptr(tm), L.ptr(to), L.ptr(probe),
-                                    L.ptr(qid), L.ptr(qcp), L.ptr(coff), L.ptr(ccnt), L.ptr(ccnt1), L.ptr(slot),
-                                    L.ptr(l1), L.ptr(l2), L.ptr(nl), L.ptr(zero), B, L.ptr(work)), "route_pairs")
+        tail = (L.ptr(to), L.ptr(probe), L.ptr(qid), L.ptr(qcp), L.ptr(coff), L.ptr(ccnt), L.ptr(ccnt1), L.ptr(slot),
+                L.ptr(l1), L.ptr(l2), L.ptr(nl), L.ptr(zero), B, L.ptr(work))
+        if scaled:
+            L.check(lib.fvs_route_pairs_scaled(L.stream_handle(), L.ptr(tq), B, NC, npr, n1, L.ptr(tsc), mptr, *tail),
+                    "route_pairs_scaled")
+        else:
+            L.check(lib.fvs_route_pairs(L.stream_handle(), L.ptr(tq), B, NC, npr, n1, L.ptr(tm), *tail), "route_pairs")
         torch.cuda.synchronize()
         assert int(work.abs().sum()) == 0 and int(zero.abs().sum()) == 0
         outs.append([c(x) for x in (probe, qid, qcp, coff, ccnt, ccnt1, slot, l1, l2, nl)])
@@ -428,7 +441,10 @@ def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1):
     probe, qid, qcp, coff, ccnt, ccnt1, slot, l1, l2, nl = outs[0]
     # routing: the separate kernel's probe list
     p2 = torch.empty(B, npr, dtype=torch.int64, device=DEV)
-    L.check(lib.fvs_route_topk(L.stream_handle(), L.ptr(tq), B, NC, npr, L.ptr(p2)), "route")
+    if scaled:
+        L.check(lib.fvs_route_topk_scaled(L.stream_handle(), L.ptr(tq), B, NC, npr, L.ptr(tsc), L.ptr(p2)), "route")
+    else:
+        L.check(lib.fvs_route_topk(L.stream_handle(), L.ptr(tq), B, NC, npr, L.ptr(p2)), "route")
     np.testing.assert_array_equal(probe, c(p2))
     # pairs: counts and offsets exact, each cell's first-pass and other segments equal as sets, slots and constants
     oq, oc, on, _, _ = O.pairs(probe, NC, QM, mnorm)

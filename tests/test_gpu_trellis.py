@@ -330,6 +330,25 @@ def test_cells_scan_matches_tile_scan(ec, synth_index, B, nprobe):
     assert checked >= 0.9 * B
 
 
+@pytest.mark.parametrize("B,nprobe,K", [(300, 64, 200), (120, 32, 100), (40, 128, 500)])
+def test_fused_routing_matches_separate_kernels(ec, synth_index, B, nprobe, K):
+    """the batched path's routing and pair lists by fvs_route_pairs_scaled (two launches) against
+    fvs_route_topk_scaled + fvs_pairs_split + fvs_cell_lists on the same engine: the same probe lists, thresholds,
+    stage-1 candidates and final results, bit for bit (the within-cell order of the pairs differs between the two,
+    which no result depends on)"""
+    ds, ix, _, _ = synth_index
+    E = _engine(ec, ix, "cells")
+    Q = ds["queries"][:B].contiguous()
+    assert E.fused_routing(B, nprobe) and E.cells_scan()
+    a = E.search_eager(Q, K, 2.0, nprobe, 10)
+    E.fused_routing = lambda B_, n_: False
+    b = E.search_eager(Q, K, 2.0, nprobe, 10)
+    torch.cuda.synchronize()
+    assert int(E.status) == 0
+    for key in ("probe", "t0", "cnt", "est1", "ok", "I", "reads", "ids"):
+        np.testing.assert_array_equal(c(a[key]), c(b[key]), err_msg=key)
+
+
 def test_cells_scan_wait_expiry(ec, synth_index):
     """an expired bounded wait in the tcgen05 trellis scan raises from search(), and the device stays usable (the next
     search equals the one before); small poll budgets exercise the drain path."""
