@@ -9,20 +9,20 @@
 // Work items are (cell, group of up to QN = 128 of its queries), handed out dynamically (cells largest first).  An
 // item's queries are gathered once and held while the cell's 128-row tiles pass; each tile x item is ONE sequence of
 // 16 tcgen05.mma.kind::f16 (M = 128 rows, N = the item's queries rounded up to 16, K = 16 each), since the issue cost
-// of an MMA hardly depends on N.  The code tile is not copied but decoded in the CTA: four decode warps, one tile row per
-// lane, read the row's words (prefetched one tile ahead) and write its 256 fp16 values, two per lookup of a table of
-// fp16 value pairs indexed by (L+1)-bit windows, straight into the canonical K-major 128 B-swizzled layout the MMA
-// reads.  The tile moves in K-chunks of 64 values through a ring of AC chunk slots, so decode and MMAs overlap chunk by
-// chunk.
-// Warp roles (640 threads):
-//   warps 0-3   : decode
-//   warp 4      : TMEM allocation; lane 0 issues the MMAs per chunk, commits a chunk slot back once its MMAs are done
+// of an MMA hardly depends on N.  The code tile is not copied but decoded in the CTA: two sets of four decode warps,
+// one tile row per lane, read the row's words (prefetched one tile ahead) and write its fp16 values, two per lookup of
+// a table of fp16 value pairs indexed by (L+1)-bit windows, straight into the canonical K-major 128 B-swizzled layout
+// the MMA reads; set 0 writes values 0-127 of every row (words 0-4), set 1 values 128-255 (words 4-8).  The tile moves
+// in K-chunks of 64 values through a ring of AC chunk slots, so decode and MMAs overlap chunk by chunk.
+// Warp roles (768 threads):
+//   warps 0-7   : decode (warps 0-3 chunks 0-1, warps 4-7 chunks 2-3 of every tile)
+//   warp 8      : TMEM allocation; lane 0 issues the MMAs per chunk, commits a chunk slot back once its MMAs are done
 //                 and an accumulator after the tile's last chunk
-//   warps 5-6   : gather, items alternating: fp16 query rows picked by qid, copied with cp.async (an item's rows in
+//   warps 9-10  : gather, items alternating: fp16 query rows picked by qid, copied with cp.async (an item's rows in
 //                 flight at once) into the swizzled layout; column metadata (qid, pair constant, threshold)
-//   warp 7      : lane 0 takes cells (atomicAdd on sched[0], cell fields loaded ahead in stages) and publishes the
+//   warp 11     : lane 0 takes cells (atomicAdd on sched[0], cell fields loaded ahead in stages) and publishes the
 //                 work items in a ring of I_STAGES slots
-//   warps 8-19  : three epilogue warpgroups, tiles alternating between them
+//   warps 12-23 : three epilogue warpgroups, tiles alternating between them
 // The last CTA to finish resets sched[0..1].  Every mbarrier wait is bounded; on expiry the CTA raises `status`,
 // drains the MMAs it issued, frees TMEM and returns.
 #include <cuda.h>
@@ -38,7 +38,8 @@ constexpr int TILE_ROWS = 128;
 constexpr int QN = 128;     // queries per work item (one B operand, one accumulator per tile)
 constexpr int R = 256;      // decoded values per row
 constexpr int KCH = 4;      // K-chunks of 64 fp16 values (128 B per row) per tile
-constexpr int NWORDS = R / 32 + 1;  // words a lane reads for its row
+constexpr int DEC_SETS = 2;  // decode warp sets, each decoding KCH / DEC_SETS chunks of every tile
+constexpr int SWORDS = 2 * (KCH / DEC_SETS) + 1;  // words a lane of a set reads for its row (from word 4 * set)
 constexpr int AC = 5;       // chunk slots
 constexpr int B_STAGES = 2;
 constexpr int T_STAGES = 4;
@@ -46,14 +47,15 @@ constexpr int I_STAGES = 8;
 constexpr int MS = 4;       // column-metadata slots (one per item, held until the item's last tile is done)
 constexpr int EPI_GROUPS = 3;
 constexpr int GATHER_WARPS = 2;
-constexpr int DEC_WARPS = 4;
+constexpr int DEC_WARPS = 8;
 constexpr int MAX_L = 10;
-constexpr int W_MMA = 4, W_GATHER = 5, W_PROD = 7, W_EPI = 8;
+constexpr int W_MMA = 8, W_GATHER = 9, W_PROD = 11, W_EPI = 12;
 constexpr int NWARPS = W_EPI + 4 * EPI_GROUPS;
 constexpr int NTHREADS = 32 * NWARPS;
 constexpr uint32_t TMEM_COLS = T_STAGES * QN;
 static_assert(W_EPI % 4 == 0, "epilogue warpgroups start on a TMEM lane quarter");
-static_assert(DEC_WARPS * 32 == TILE_ROWS, "one decode lane per tile row");
+static_assert(DEC_WARPS / DEC_SETS * 32 == TILE_ROWS, "one lane of each decode set per tile row");
+static_assert(W_MMA == DEC_WARPS, "decode warps first");
 static_assert(B_STAGES == GATHER_WARPS, "gather warp g fills B stage g");
 static_assert(TMEM_COLS <= 512, "tensor memory columns");
 
@@ -173,7 +175,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
 
     if (tid == 0) {
         for (int s = 0; s < AC; s++) {
-            mbar_init(c_full(s), DEC_WARPS);  // every decode warp has written its rows of the chunk
+            mbar_init(c_full(s), DEC_WARPS / DEC_SETS);  // every warp of the chunk's decode set has written its rows
             mbar_init(c_empty(s), 1);  // the MMAs reading the chunk have completed
         }
         for (int s = 0; s < B_STAGES; s++) {
@@ -237,29 +239,33 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
     bool mma_issued = false;
 
     if (warp < W_MMA) {
-        // ---- decode: warp w, rows 32 w + lane of each tile
+        // ---- decode: set ds = warp / 4 writes chunks KCH / DEC_SETS * ds .. of every tile; warp w % 4, rows
+        //      32 (w % 4) + lane
         const uint32_t* tab2 = reinterpret_cast<const uint32_t*>(smem + TAB_OFF);
         const int sh = 31 - p.L;  // a window is the top L+1 bits of a 32-bit funnel shift
-        const int r = 32 * warp + lane;
+        const int ds = warp / (DEC_WARPS / DEC_SETS);
+        constexpr int SCH = KCH / DEC_SETS;  // chunks per set
+        const int c0 = SCH * ds;             // the set's first chunk; its words start at 2 * c0
+        const int r = 32 * (warp % (DEC_WARPS / DEC_SETS)) + lane;
         const int sw = r & 7;
         const uint32_t row_off = (uint32_t)((r >> 3) * 1024 + sw * 128);
-        auto load_words = [&](const Item& it, int t, uint32_t (&w)[NWORDS]) {
+        auto load_words = [&](const Item& it, int t, uint32_t (&w)[SWORDS]) {
             const int row = it.first + t * TILE_ROWS + r;
             const bool v = it.live && row >= it.cs && row < it.ce;
-            const uint32_t* src = p.words + (int64_t)(v ? row : 0) * p.W;
+            const uint32_t* src = p.words + (int64_t)(v ? row : 0) * p.W + 2 * c0;
 #pragma unroll
-            for (int i = 0; i < NWORDS; i++) w[i] = v ? __ldg(src + i) : 0u;
+            for (int i = 0; i < SWORDS; i++) w[i] = v ? __ldg(src + i) : 0u;
         };
-        int n = 0, cslot = 0;
-        uint32_t cph = 0;
+        int n = 0;
+        uint32_t gtile = 0;  // tiles decoded so far: chunk c of tile gtile is chunk KCH * gtile + c of the ring
         Item it;
         bool ok = take_item(0, it);
-        uint32_t w[NWORDS], wn[NWORDS];
+        uint32_t w[SWORDS], wn[SWORDS];
         if (ok) load_words(it, 0, w);
         while (ok && it.live) {
             Item itn;
             if (!take_item(n + 1, itn)) break;
-            for (int t = 0; t < it.ntiles; t++) {
+            for (int t = 0; t < it.ntiles; t++, gtile++) {
                 // words of the tile after this one (this item's next tile, else the next item's first)
                 if (t + 1 < it.ntiles)
                     load_words(it, t + 1, wn);
@@ -268,8 +274,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                 const int row = it.first + t * TILE_ROWS + r;
                 const bool v = row >= it.cs && row < it.ce;
 #pragma unroll
-                for (int c = 0; c < KCH; c++) {
-                    if (!warp_wait(c_empty(cslot), cph ^ 1u, abort, WL)) {
+                for (int cc = 0; cc < SCH; cc++) {
+                    // the other set fills the ring's other chunks: a set's wait for chunk g starts after its wait
+                    // for its previous chunk (g - 1 or g - KCH + SCH - 1) passed, i.e. after every chunk up to g - 8
+                    // was consumed, so the slot's barrier is never two phases behind the parity waited on
+                    const uint32_t g = KCH * gtile + (uint32_t)(c0 + cc);
+                    const int cslot = (int)(g % AC);
+                    if (!warp_wait(c_empty(cslot), ((g / AC) & 1u) ^ 1u, abort, WL)) {
                         ok = false;
                         break;
                     }
@@ -277,7 +288,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                         uint8_t* dst = smem + A_OFF + cslot * CH_BYTES + row_off;
 #pragma unroll
                         for (int h = 0; h < 2; h++) {
-                            const uint32_t hi = w[2 * c + h], lo = w[2 * c + h + 1];
+                            const uint32_t hi = w[2 * cc + h], lo = w[2 * cc + h + 1];
 #pragma unroll
                             for (int uu = 0; uu < 4; uu++) {
                                 uint4 q;
@@ -292,14 +303,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
                     __syncwarp();
                     if (lane == 0) mbar_arrive(c_full(cslot));
-                    if (++cslot == AC) {
-                        cslot = 0;
-                        cph ^= 1u;
-                    }
                 }
                 if (!ok) break;
 #pragma unroll
-                for (int i = 0; i < NWORDS; i++) w[i] = wn[i];
+                for (int i = 0; i < SWORDS; i++) w[i] = wn[i];
             }
             if (!ok) break;
             it = itn;
