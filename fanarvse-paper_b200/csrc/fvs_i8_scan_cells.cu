@@ -9,8 +9,9 @@
 //     the cell's 128-row code tiles stream past them (a cell of ~250 rows spans 2-3 tiles; the tile scan gathered them
 //     once per tile); cells with more queries are split into groups of RSUB sub-tiles, each group streaming the
 //     cell's tiles again (from L2);
-//   * a code tile is fetched as the 32-row blocks the cell occupies (1 to 4 TMA boxes per K-half), not as a full
-//     128-row box, so the rows past the cell's end are not moved.
+//   * a code tile is fetched as the 32-row blocks the cell occupies, one TMA copy per K-half with a box of 32, 64, 96
+//     or 128 rows (four tensor maps), so the rows past the cell's end are not moved; K-half 1 lands right after
+//     K-half 0's blocks.
 // Warp roles (640 threads):
 //   warp 0      : lane 0 takes cells (atomicAdd on sched[0]; the list entry, bounds and pair range of a cell are
 //                 loaded ahead in stages), publishes each work item (cell, group of sub-tiles) in a ring of I_STAGES
@@ -65,6 +66,12 @@ struct Item {
 // shared-memory carve-up (offsets from a 1024-byte aligned base)
 constexpr int A_BYTES = 2 * TILE_ROWS * 128;  // one code tile: 2 K-halves x 16 KB
 constexpr int BLK_BYTES = 32 * 128;           // one 32-row block of one K-half
+
+// the code matrix as 2D tensor maps whose boxes are one K-half (128 B) of 32, 64, 96 or 128 rows: a tile of nblk
+// 32-row blocks moves as two copies (one per K-half) with map nblk - 1
+struct ZMaps {
+    CUtensorMap m[4];
+};
 constexpr int B_BYTES = 2 * QN * 128;         // one query sub-tile: 2 K-halves x 8 KB
 constexpr int A_OFF = 0;
 constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
@@ -135,7 +142,7 @@ struct CellInfo {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_constant__ CUtensorMap zmap, Params p) {
+__global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_constant__ ZMaps zm, Params p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -215,7 +222,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
 
     if (warp == W_TMA) {
         if (lane == 0) {
-            asm volatile("prefetch.tensormap [%0];" ::"l"(&zmap) : "memory");
+#pragma unroll
+            for (int k = 0; k < 4; k++) asm volatile("prefetch.tensormap [%0];" ::"l"(&zm.m[k]) : "memory");
             const int nl = *p.nlist;
             // cell pipeline, refilled by every next_cell(): `pre` (bounds and pair range of the next cell), `cn` (the
             // cell after it), `idxn` (the list index after that); each call only uses values loaded by the previous
@@ -310,10 +318,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                     const int nblk = min(4, (it.ce - row0 + 31) / 32);
                     mbar_expect_tx(a_full(s), (uint32_t)(nblk * 2 * BLK_BYTES));
                     const uint32_t dst = sbase + A_OFF + s * A_BYTES;
-                    for (int b = 0; b < nblk; b++) {
-                        tma_load_2d(dst + b * BLK_BYTES, &zmap, 0, row0 + 32 * b, a_full(s));
-                        tma_load_2d(dst + TILE_ROWS * 128 + b * BLK_BYTES, &zmap, 128, row0 + 32 * b, a_full(s));
-                    }
+                    // K-half 0 at dst, K-half 1 right after it (nblk * 4 KB on, 1024-byte aligned)
+                    tma_load_2d(dst, &zm.m[nblk - 1], 0, row0, a_full(s));
+                    tma_load_2d(dst + nblk * BLK_BYTES, &zm.m[nblk - 1], 128, row0, a_full(s));
                     na_load++;
                 }
             }
@@ -335,6 +342,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
                     }
                     tc_fence_after();
                     const uint32_t abase = sbase + A_OFF + sa * A_BYTES;
+                    // K-half 1 follows the tile's nblk blocks of K-half 0; the MMA's 128 rows reach past them only in
+                    // rows beyond the cell's end, which the epilogue does not read, and stay inside the stage
+                    const int row0 = it.first + t * TILE_ROWS;
+                    const uint32_t half1 = (uint32_t)(min(4, (it.ce - row0 + 31) / 32) * BLK_BYTES);
                     for (int s = 0; s < it.nsub; s++) {
                         const int sb = (nb + s) % B_STAGES, st = nu % T_STAGES;
                         if ((t == 0 && !mbar_wait(b_full(sb), ((nb + s) / B_STAGES) & 1, abort, WL)) ||
@@ -350,7 +361,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_co
 #pragma unroll
                         for (int ks = 0; ks < RB / 32; ks++) {
                             const int h = ks >> 2, kofs = (ks & 3) * 32;
-                            mma_i8(d, sw128_desc(abase + h * TILE_ROWS * 128 + kofs),
+                            mma_i8(d, sw128_desc(abase + h * half1 + kofs),
                                    sw128_desc(bb + h * QN * 128 + kofs), idesc, ks > 0 ? 1u : 0u);
                         }
                         mma_issued = true;
@@ -672,15 +683,17 @@ extern "C" int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8
     if (maxlist == 0 || B == 0) return FVS_OK;
     EncodeTiledFn enc = encode_fn();
     if (!enc) return (int)cudaErrorNotSupported;
-    CUtensorMap map;
+    ZMaps zm;
     const cuuint64_t dims[2] = {(cuuint64_t)RB, (cuuint64_t)N};
     const cuuint64_t strides[1] = {(cuuint64_t)RB};
-    const cuuint32_t box[2] = {128, 32};  // one 32-row block of one K-half
     const cuuint32_t estr[2] = {1, 1};
-    CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)Z, dims, strides, box, estr,
-                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (cr != CUDA_SUCCESS) return FVS_EINVAL;
+    for (int k = 0; k < 4; k++) {
+        const cuuint32_t box[2] = {128, (cuuint32_t)(32 * (k + 1))};  // one K-half of k + 1 32-row blocks
+        CUresult cr = enc(&zm.m[k], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void*)Z, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+        if (cr != CUDA_SUCCESS) return FVS_EINVAL;
+    }
     Params p{q8, qs, qid, coff, ccnt, qcp, list, nlist, off, zs, t0, cnt, bval, bpos, bmc, sched, status, M, MB,
              pipeline_wait_limit()};
     cudaError_t e = mode ? fvs_ensure_smem((const void*)scan_cells_kernel<1>, SMEM_BYTES)
@@ -689,8 +702,8 @@ extern "C" int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8
     const int nsm = fvs_sm_count();
     const int grid = maxlist < nsm ? maxlist : nsm;
     if (mode == 0)
-        scan_cells_kernel<0><<<grid, NTHREADS, SMEM_BYTES, stream>>>(map, p);
+        scan_cells_kernel<0><<<grid, NTHREADS, SMEM_BYTES, stream>>>(zm, p);
     else
-        scan_cells_kernel<1><<<grid, NTHREADS, SMEM_BYTES, stream>>>(map, p);
+        scan_cells_kernel<1><<<grid, NTHREADS, SMEM_BYTES, stream>>>(zm, p);
     return fvs_launch_status();
 }
