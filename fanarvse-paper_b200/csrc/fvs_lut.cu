@@ -404,8 +404,7 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
     const int nblk = D / 32, nwords = ts.nwords;
     float* tab = reinterpret_cast<float*>(smem);                   // nblk * 128
-    uint32_t* wmeta = reinterpret_cast<uint32_t*>(tab + nblk * 128);  // per word: table offset | tier << 24
-    float* wpw = reinterpret_cast<float*>(wmeta + nwords);         // per word: 2^(b-1-p)
+    uint2* wmeta = reinterpret_cast<uint2*>(tab + nblk * 128);  // per word: (table byte offset | tier << 24, 2^(b-1-p))
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t qK = (int64_t)q * K;
     for (int w = tid; w < nwords; w += LC_THREADS) {
@@ -413,8 +412,8 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
         while (t + 1 < ts.T && w >= ts.wbase[t + 1]) t++;
         const int r = w - ts.wbase[t], wpp = ts.kb[t] / 4;
         const int p = r / wpp, j4 = r - p * wpp;
-        wmeta[w] = (uint32_t)((ts.s[t] / 32 + j4) * 128) | ((uint32_t)t << 24);
-        wpw[w] = ts.pw[t][p];
+        wmeta[w] = make_uint2((uint32_t)((ts.s[t] / 32 + j4) * 128 * 4) | ((uint32_t)t << 24),
+                              __float_as_uint(ts.pw[t][p]));
     }
     // group g = 4-coordinate group (block g / 8, group g % 8) holds coordinates 4g .. 4g+3.  Entry v sums the selected
     // coordinates left to right in fp32, as acc += z_i * bit_i does; built incrementally: entry v = entry (v without
@@ -516,20 +515,24 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
         for (int u = 0; u < 8; u++) {
             const int w = 8 * k + u;
             if (w >= nwords) break;
-            const uint32_t m = wmeta[w];
-            const int t = (int)(m >> 24);
+            const uint2 m = wmeta[w];
+            const int t = (int)(m.x >> 24);
             if (t != ct) {
                 fold(ct, at);
                 ct = t;
                 at = 0.f;
             }
-            const float* E = tab + (m & 0xffffffu);
+            const char* E = reinterpret_cast<const char*>(tab) + (m.x & 0xffffffu);
             const uint32_t wd = wd8[u];
+            // byte bi of ho / lo: 4 x the high / low nibble of the word's byte bi, i.e. the byte offsets of entries
+            // (32 bi + high nibble) and (32 bi + 16 + low nibble) past 128 bi bytes
+            const uint32_t ho = (wd >> 2) & 0x3C3C3C3Cu, lo = (wd << 2) & 0x3C3C3C3Cu;
             float a = 0.f;
 #pragma unroll
             for (int bi = 0; bi < 4; bi++)
-                a += E[32 * bi + ((wd >> (8 * bi + 4)) & 15u)] + E[32 * bi + 16 + ((wd >> (8 * bi)) & 15u)];
-            at += a * wpw[w];
+                a += *reinterpret_cast<const float*>(E + 128 * bi + __byte_perm(ho, 0u, 0x4440u | bi)) +
+                     *reinterpret_cast<const float*>(E + 128 * bi + 64 + __byte_perm(lo, 0u, 0x4440u | bi));
+            at += a * __uint_as_float(m.y);
         }
     }
     fold(ct, at);
