@@ -12,7 +12,7 @@
 //   * a code tile is fetched as the 32-row blocks the cell occupies, one TMA copy per K-half with a box of 32, 64, 96
 //     or 128 rows (four tensor maps), so the rows past the cell's end are not moved; K-half 1 lands right after
 //     K-half 0's blocks.
-// Warp roles (640 threads):
+// Warp roles (emit pass: 640 threads, one CTA per SM; first pass: 384 threads, two CTAs per SM, see Shape):
 //   warp 0      : lane 0 takes cells (atomicAdd on sched[0]; the list entry, bounds and pair range of a cell are
 //                 loaded ahead in stages), publishes each work item (cell, group of sub-tiles) in a ring of I_STAGES
 //                 slots up to AHEAD items ahead, and issues the TMA loads of the item's code tiles into A_STAGES stages
@@ -23,7 +23,7 @@
 //                 cp.async (a sub-tile's rows in flight at once) into the canonical K-major 128 B-swizzled layout,
 //                 and the sub-tile's column metadata (qid, qs, pair constant, threshold) into one of MS slots,
 //                 released when every epilogue warp is done with the sub-tile
-//   warps 4-19  : four epilogue warpgroups, units alternating between them; each warp loads its rows' scales before
+//   warps 4-    : EPI_GROUPS epilogue warpgroups, units alternating between them; each warp loads its rows' scales before
 //                 waiting for the accumulator, returns the TMEM stage as soon as the accumulator is in registers, then
 //                 as fvs_i8_scan_tc: est = ((acc * qs) * zs) + qcp with explicit rounding, first pass: block maximum
 //                 per query by redux.sync.max; emit: kept-column masks transposed across the warp, one atomicAdd per
@@ -42,28 +42,34 @@ using namespace fvs::tcg;
 constexpr int TILE_ROWS = 128;
 constexpr int QN = 64;  // queries per sub-tile
 constexpr int RB = 256;
-constexpr int A_STAGES = 4;
-constexpr int B_STAGES = 4;
-constexpr int RSUB = 2;  // sub-tiles of one work item (held through the item's tiles); B_STAGES >= 2 * RSUB
-constexpr int T_STAGES = 8;
 constexpr int I_STAGES = 8;
 constexpr int MS = 8;    // column-metadata slots (one per sub-tile, held until the sub-tile's last unit is done)
-constexpr int EPI_GROUPS = 4;
 constexpr int GATHER_WARPS = 2;
 constexpr int AHEAD = 4;  // work items published beyond the one whose tiles are being loaded
 constexpr int W_TMA = 0, W_MMA = 1, W_GATHER = 2, W_EPI = W_GATHER + GATHER_WARPS;
-constexpr int NWARPS = W_EPI + 4 * EPI_GROUPS;
-constexpr int NTHREADS = 32 * NWARPS;
-constexpr uint32_t TMEM_COLS = T_STAGES * QN;
-static_assert(B_STAGES >= 2 * RSUB, "a work item's sub-tiles and the next item's fit together");
 static_assert(W_EPI % 4 == 0, "epilogue warpgroups cover TMEM lane quarters 0..3 in order");
 static_assert(AHEAD + 2 <= I_STAGES, "an item's slot is not reused before the producer has loaded its tiles");
+
+// Pipeline shape per pass.  The first pass (block maxima) runs two CTAs per SM, each with 2 code-tile stages, 2
+// query sub-tile stages (one sub-tile per item), 4 TMEM accumulators and 2 epilogue warpgroups: two independent
+// pipelines per SM hide each other's load and handshake latencies (first pass 87 -> 74 us at 1M rows).  The emit pass
+// (heavier epilogue, more queries per cell) keeps one CTA per SM with 4 / 4 stages, two sub-tiles per item, 8
+// accumulators and 4 epilogue warpgroups.
+template <int MODE>
+struct Shape;
+template <>
+struct Shape<0> {
+    static constexpr int A_STAGES = 2, B_STAGES = 2, RSUB = 1, T_STAGES = 4, EPI_GROUPS = 2, CTAS_PER_SM = 2;
+};
+template <>
+struct Shape<1> {
+    static constexpr int A_STAGES = 4, B_STAGES = 4, RSUB = 2, T_STAGES = 8, EPI_GROUPS = 4, CTAS_PER_SM = 1;
+};
 
 struct Item {
     int cell, cs, ce, first, ntiles, qoff, nq, nsub;  // nsub == 0: no more work
 };
 
-// shared-memory carve-up (offsets from a 1024-byte aligned base)
 constexpr int A_BYTES = 2 * TILE_ROWS * 128;  // one code tile: 2 K-halves x 16 KB
 constexpr int BLK_BYTES = 32 * 128;           // one 32-row block of one K-half
 
@@ -73,19 +79,32 @@ struct ZMaps {
     CUtensorMap m[4];
 };
 constexpr int B_BYTES = 2 * QN * 128;         // one query sub-tile: 2 K-halves x 8 KB
-constexpr int A_OFF = 0;
-constexpr int B_OFF = A_OFF + A_STAGES * A_BYTES;
-constexpr int META_OFF = B_OFF + B_STAGES * B_BYTES;      // per sub-tile slot: qid, qs, qcp, t0 of QN columns
 constexpr int META_W = 4 * QN * 4;
-constexpr int COL_OFF = META_OFF + MS * META_W;             // per epilogue warp: 32 column masks + 32 bases
-constexpr int MCNT_OFF = COL_OFF + 4 * EPI_GROUPS * 64 * 4;  // per metadata slot: epilogue warps done with it
-constexpr int ITEM_OFF = MCNT_OFF + MS * 4;
-constexpr int BAR_OFF = ITEM_OFF + I_STAGES * (int)sizeof(Item);
-constexpr int NBAR = 2 * A_STAGES + 2 * B_STAGES + 2 * T_STAGES + 2 * I_STAGES + 2 * MS + 1;
-constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem base, abort flag
-constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
-static_assert(SMEM_BYTES <= 232448, "shared memory per CTA");
-constexpr uint32_t I_CONSUMERS = 1 + GATHER_WARPS + 4 * EPI_GROUPS;  // MMA thread, gather warps, epilogue warps
+
+// the pass's warps, tensor memory and shared-memory carve-up (offsets from a 1024-byte aligned base)
+template <int MODE>
+struct Layout : Shape<MODE> {
+    using S = Shape<MODE>;
+    static constexpr int NWARPS = W_EPI + 4 * S::EPI_GROUPS;
+    static constexpr int NTHREADS = 32 * NWARPS;
+    static constexpr uint32_t TMEM_COLS = S::T_STAGES * QN;
+    static constexpr int A_OFF = 0;
+    static constexpr int B_OFF = A_OFF + S::A_STAGES * A_BYTES;
+    static constexpr int META_OFF = B_OFF + S::B_STAGES * B_BYTES;   // per sub-tile slot: qid, qs, qcp, t0 of QN columns
+    static constexpr int COL_OFF = META_OFF + MS * META_W;           // per epilogue warp: 32 column masks + 32 bases
+    static constexpr int MCNT_OFF = COL_OFF + 4 * S::EPI_GROUPS * 64 * 4;  // per metadata slot: warps done with it
+    static constexpr int ITEM_OFF = MCNT_OFF + MS * 4;
+    static constexpr int BAR_OFF = ITEM_OFF + I_STAGES * (int)sizeof(Item);
+    static constexpr int NBAR = 2 * S::A_STAGES + 2 * S::B_STAGES + 2 * S::T_STAGES + 2 * I_STAGES + 2 * MS + 1;
+    static constexpr int MISC_OFF = BAR_OFF + NBAR * 8;  // tmem base, abort flag
+    static constexpr int SMEM_BYTES = MISC_OFF + 16 + 1024;
+    static constexpr uint32_t I_CONSUMERS = 1 + GATHER_WARPS + 4 * S::EPI_GROUPS;  // MMA thread, gather, epilogue
+    static_assert(S::B_STAGES >= 2 * S::RSUB, "a work item's sub-tiles and the next item's fit together");
+    static_assert((TMEM_COLS & (TMEM_COLS - 1)) == 0 && TMEM_COLS >= 32 && TMEM_COLS * S::CTAS_PER_SM <= 512,
+                  "tensor memory columns: a power of two, the SM's CTAs together within 512");
+    static_assert(SMEM_BYTES * S::CTAS_PER_SM <= 232448 - 1024 * (S::CTAS_PER_SM - 1), "shared memory per SM");
+    static_assert(NTHREADS * S::CTAS_PER_SM <= 2048, "threads per SM");
+};
 
 struct Params {
     const int8_t* q8;
@@ -142,7 +161,14 @@ struct CellInfo {
 };
 
 template <int MODE>
-__global__ void __launch_bounds__(NTHREADS, 1) scan_cells_kernel(const __grid_constant__ ZMaps zm, Params p) {
+__global__ void __launch_bounds__(Layout<MODE>::NTHREADS, Layout<MODE>::CTAS_PER_SM)
+    scan_cells_kernel(const __grid_constant__ ZMaps zm, Params p) {
+    using LY = Layout<MODE>;
+    constexpr int A_STAGES = LY::A_STAGES, B_STAGES = LY::B_STAGES, RSUB = LY::RSUB, T_STAGES = LY::T_STAGES;
+    constexpr int EPI_GROUPS = LY::EPI_GROUPS;
+    constexpr uint32_t TMEM_COLS = LY::TMEM_COLS, I_CONSUMERS = LY::I_CONSUMERS;
+    constexpr int A_OFF = LY::A_OFF, B_OFF = LY::B_OFF, META_OFF = LY::META_OFF, COL_OFF = LY::COL_OFF;
+    constexpr int MCNT_OFF = LY::MCNT_OFF, ITEM_OFF = LY::ITEM_OFF, BAR_OFF = LY::BAR_OFF, MISC_OFF = LY::MISC_OFF;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -696,14 +722,15 @@ extern "C" int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8
     }
     Params p{q8, qs, qid, coff, ccnt, qcp, list, nlist, off, zs, t0, cnt, bval, bpos, bmc, sched, status, M, MB,
              pipeline_wait_limit()};
-    cudaError_t e = mode ? fvs_ensure_smem((const void*)scan_cells_kernel<1>, SMEM_BYTES)
-                         : fvs_ensure_smem((const void*)scan_cells_kernel<0>, SMEM_BYTES);
+    cudaError_t e = mode ? fvs_ensure_smem((const void*)scan_cells_kernel<1>, Layout<1>::SMEM_BYTES)
+                         : fvs_ensure_smem((const void*)scan_cells_kernel<0>, Layout<0>::SMEM_BYTES);
     if (e != cudaSuccess) return (int)e;
     const int nsm = fvs_sm_count();
-    const int grid = maxlist < nsm ? maxlist : nsm;
+    const int slots = nsm * (mode ? Layout<1>::CTAS_PER_SM : Layout<0>::CTAS_PER_SM);  // persistent CTAs
+    const int grid = maxlist < slots ? maxlist : slots;
     if (mode == 0)
-        scan_cells_kernel<0><<<grid, NTHREADS, SMEM_BYTES, stream>>>(zm, p);
+        scan_cells_kernel<0><<<grid, Layout<0>::NTHREADS, Layout<0>::SMEM_BYTES, stream>>>(zm, p);
     else
-        scan_cells_kernel<1><<<grid, NTHREADS, SMEM_BYTES, stream>>>(zm, p);
+        scan_cells_kernel<1><<<grid, Layout<1>::NTHREADS, Layout<1>::SMEM_BYTES, stream>>>(zm, p);
     return fvs_launch_status();
 }
