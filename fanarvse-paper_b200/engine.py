@@ -127,6 +127,7 @@ class EngineB200I8:
         self.ix = index
         self.graphs = {}
         self.graph_launches = {}
+        self._async_slot = {}      # per search shape: the graph the next search_async replays (two alternate)
         self.nbad = 0
         self.nbad2 = 0
         self.launches = 0          # library kernel launches issued (eager) or captured
@@ -529,6 +530,28 @@ class EngineB200I8:
 
     def search(self, Qb, K, z, nprobe, k, ret_est=False):
         """`throughput/enginei8.py:96-111`: returns (I [B,k] int32, reads [B] int64, cand_ids [B,K] int32)."""
+        h = self._launch(Qb, K, z, nprobe, k, 0)
+        if isinstance(h, tuple):
+            return h
+        res = h.result()
+        if h.reads_done is not None:
+            h.reads_done.synchronize()
+        return res
+
+    def search_async(self, Qb, K, z, nprobe, k):
+        """`search` split in two for serving loops: launches the search of Qb (one graph replay) and returns a handle
+        whose `result()` waits for that search alone and returns what `search` returns.  Searches of one shape
+        alternate between two graphs with their own buffers, so one search can be in flight while the host collects
+        the previous one (call `result()` of a handle before launching the search after the next).  Qb must stay
+        unchanged until `result()` has returned and, when the handle's `reads_done` is an event (flagged rows beyond
+        the graph's recompute capacity were recomputed from Qb on the current stream), until that event."""
+        key = (len(Qb), K, z, nprobe, k, self.knobs())
+        slot = self._async_slot.get(key, 0)
+        self._async_slot[key] = slot ^ 1
+        h = self._launch(Qb, K, z, nprobe, k, slot)
+        return _Done(h) if isinstance(h, tuple) else h
+
+    def _launch(self, Qb, K, z, nprobe, k, slot):
         if not Qb.is_cuda:
             raise RuntimeError("EngineB200I8.search needs CUDA queries (the B200 library has no CPU path)")
         if K <= k:
@@ -538,7 +561,7 @@ class EngineB200I8:
             dev = Qb.device
             return (torch.empty(0, k, dtype=torch.int32, device=dev), torch.empty(0, dtype=torch.int64, device=dev),
                     torch.empty(0, K, dtype=torch.int32, device=dev))
-        key = (B, K, z, nprobe, k, self.knobs())
+        key = (B, K, z, nprobe, k, self.knobs()) + ((("slot", slot),) if slot else ())
         if key not in self.graphs:
             qs = Qb.clone()
             st = torch.cuda.Stream()
@@ -562,15 +585,23 @@ class EngineB200I8:
                 hst[1:2].copy_(self._nflag, non_blocking=True)
             self.graph_launches[key] = self.launches - n0
             self.graphs[key] = (g, qs, packed, (I.shape[1], ids.shape[1]), hok.numpy(), hst.numpy())
-        g, qs, packed, (kk, KK), hok, hst = self.graphs[key]
+        g, qs, packed, dims, hok, hst = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
         self.replayed_launches = getattr(self, "replayed_launches", 0) + self.graph_launches[key]
         P = packed.clone()
+        done = torch.cuda.Event()
+        done.record()
+        return _Pending(self, Qb, K, z, nprobe, k, P, dims, hok, hst, done)
+
+    def _collect(self, Qb, K, z, nprobe, k, P, dims, hok, hst):
+        """after a replay has completed: status, flagged-row accounting and the host recompute of rows beyond the
+        graph's capacity; returns the results and whether that recompute ran"""
+        B = len(Qb)
+        kk, KK = dims
         nr = P[:2 * B].view(torch.int64)
         I = P[2 * B:2 * B + B * kk].view(B, kk)
         ids = P[2 * B + B * kk:].view(B, KK)
-        torch.cuda.current_stream().synchronize()                # the only synchronisation
         if int(hst[0]) != 0:
             self.status.zero_()                                   # the next search starts clean
             raise _lib.FvsError("stage-1 scan: a bounded device wait expired (status flag set)")
@@ -585,7 +616,8 @@ class EngineB200I8:
             badd = bad.to(Qb.device)
             I[badd], nr[badd] = a, b
             ids[badd] = c[:, :ids.shape[1]]
-        return I, nr, ids
+            return (I, nr, ids), True
+        return (I, nr, ids), False
 
     def search_host(self, Qb, K, z, nprobe, k):
         """Latency-mode search returning the top-k ids as a host numpy array [B, k] (`EngineT.search_host`,
@@ -679,3 +711,33 @@ class EngineB200I8:
         """One search without graph capture (same kernels); returns the intermediates for parity tests."""
         ok, I, nr, ids = self._gpu(Qb, K, z, nprobe, k)
         return dict(ok=ok, I=I, reads=nr, ids=ids, **self._last)
+
+
+class _Pending:
+    """A launched search (`EngineB200I8.search_async`): result() waits for its replay (its own event, not the whole
+    stream) and collects it; the rows' host recompute, when needed, runs on the caller's current stream."""
+
+    def __init__(self, eng, Qb, K, z, nprobe, k, P, dims, hok, hst, done):
+        self._args = (Qb, K, z, nprobe, k, P, dims, hok, hst)
+        self._eng, self._done, self._res = eng, done, None
+        self.reads_done = None   # after result(): an event once the host recompute has read Qb, or None (none ran)
+
+    def result(self):
+        if self._res is None:
+            self._done.synchronize()                             # the only synchronisation
+            self._res, recomputed = self._eng._collect(*self._args)
+            if recomputed:
+                self.reads_done = torch.cuda.Event()
+                self.reads_done.record()
+        return self._res
+
+
+class _Done:
+    """An empty batch's result, in the handle form of search_async."""
+
+    def __init__(self, res):
+        self._res = res
+        self.reads_done = None
+
+    def result(self):
+        return self._res

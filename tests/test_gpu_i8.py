@@ -173,6 +173,30 @@ def test_search_matches_oracle(eng, n, d, nlist, nq, K, nprobe, k, M, scan):
     assert int(E.status) == 0
 
 
+def test_search_async_matches_search(eng):
+    """search_async: two searches in flight on the two alternating graphs, a third on the first graph again, each
+    result equal to search() on the same batch (flagged rows recomputed from the host included); an empty batch"""
+    ds, ix, oi = _random_index(eng, 30000, 512, 96, 64, seed=11)
+    E = eng.EngineB200I8(ix)
+    E.MSZ = 160                      # small emit buffer: flagged rows beyond the graph's capacity, recomputed
+    K, z, nprobe, k = 30, 1.5, 20, 10
+    Q = ds["queries"]
+    Qa, Qb = Q[:40].contiguous(), Q[20:60].contiguous()
+    want = [E.search(x, K, z, nprobe, k) for x in (Qa, Qb)]
+    h1 = E.search_async(Qa, K, z, nprobe, k)
+    h2 = E.search_async(Qb, K, z, nprobe, k)
+    r1 = h1.result()
+    h3 = E.search_async(Qa, K, z, nprobe, k)
+    r2, r3 = h2.result(), h3.result()
+    assert h1.result() is r1
+    for got, w in ((r1, want[0]), (r2, want[1]), (r3, want[0])):
+        for a, b in zip(got, w):
+            np.testing.assert_array_equal(c(a), c(b))
+    assert E.nbad > 0
+    I0, nr0, ids0 = E.search_async(Q[:0], K, z, nprobe, k).result()
+    assert I0.shape == (0, k) and nr0.shape == (0,) and ids0.shape == (0, K)
+
+
 def test_graph_search_and_fallback(eng):
     """search() (CUDA graph + recompute of flagged queries) equals the oracle's EngineI8 search: the main pass on the
     exact queries, `_fallback` (rho 1, M 65536, fp32 LUT, no delta rule) on the flagged ones."""
