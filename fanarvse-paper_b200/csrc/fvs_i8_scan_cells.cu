@@ -12,7 +12,7 @@
 //   * a code tile is fetched as the 32-row blocks the cell occupies, one TMA copy per K-half with a box of 32, 64, 96
 //     or 128 rows (four tensor maps), so the rows past the cell's end are not moved; K-half 1 lands right after
 //     K-half 0's blocks.
-// Warp roles (emit pass: 640 threads, one CTA per SM; first pass: 384 threads, two CTAs per SM, see Shape):
+// Warp roles (640 threads, one CTA per SM; see Shape):
 //   warp 0      : lane 0 takes cells (atomicAdd on sched[0]; the list entry, bounds and pair range of a cell are
 //                 loaded ahead in stages), publishes each work item (cell, group of sub-tiles) in a ring of I_STAGES
 //                 slots up to AHEAD items ahead, and issues the TMA loads of the item's code tiles into A_STAGES stages
@@ -50,16 +50,15 @@ constexpr int W_TMA = 0, W_MMA = 1, W_GATHER = 2, W_EPI = W_GATHER + GATHER_WARP
 static_assert(W_EPI % 4 == 0, "epilogue warpgroups cover TMEM lane quarters 0..3 in order");
 static_assert(AHEAD + 2 <= I_STAGES, "an item's slot is not reused before the producer has loaded its tiles");
 
-// Pipeline shape per pass.  The first pass (block maxima) runs two CTAs per SM, each with 2 code-tile stages, 2
-// query sub-tile stages (one sub-tile per item), 4 TMEM accumulators and 2 epilogue warpgroups: two independent
-// pipelines per SM hide each other's load and handshake latencies (first pass 87 -> 74 us at 1M rows).  The emit pass
-// (heavier epilogue, more queries per cell) keeps one CTA per SM with 4 / 4 stages, two sub-tiles per item, 8
-// accumulators and 4 epilogue warpgroups.
+// Pipeline shape per pass: one CTA per SM with 4 code-tile stages, 4 query sub-tile stages (two sub-tiles per item),
+// 8 TMEM accumulators and 4 epilogue warpgroups.  (Two CTAs per SM with half of each, measured for the first pass:
+// 87 -> 74 us at 1M rows and 4096 cells, but 0.37 -> 0.63 ms at 2M rows and 8192 cells, where the CTAs that stream
+// the largest cells alone set the pass time and half a pipeline doubles that tail.)
 template <int MODE>
 struct Shape;
 template <>
 struct Shape<0> {
-    static constexpr int A_STAGES = 2, B_STAGES = 2, RSUB = 1, T_STAGES = 4, EPI_GROUPS = 2, CTAS_PER_SM = 2;
+    static constexpr int A_STAGES = 4, B_STAGES = 4, RSUB = 2, T_STAGES = 8, EPI_GROUPS = 4, CTAS_PER_SM = 1;
 };
 template <>
 struct Shape<1> {
