@@ -33,8 +33,10 @@ SIGNATURES = {
                               I32, P]),
     "fvs_i8_scan_cells": (I32, [P, I32, P, P, I32, I32, P, P, P, P, P, P, I32, P, I32, P, I64, P, P, P, P, P, I32, P,
                                  I32, P, P]),
-    "fvs_route_pairs": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P]),
-    "fvs_route_pairs_scaled": (I32, [P, P, I32, I32, I32, I32, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P]),
+    "fvs_route_pairs": (I32, [P, P, I32, I32, I32, I32, P, P, I32, P, P, P, P, P, P, P, P, P, P, P, I32, P]),
+    "fvs_route_pairs_scaled": (I32, [P, P, I32, I32, I32, I32, P, P, P, I32, P, P, P, P, P, P, P, P, P, P, P, I32,
+                                      P]),
+    "fvs_cell_part_tiles": (I32, []),
     "fvs_cell_lists": (I32, [P, P, I32, P, P, P, P, P, P, I32]),
     "fvs_threshold": (I32, [P, P, I32, P, P, I32, I32, P, I32, I32, P]),
     "fvs_select_topk": (I32, [P, P, P, P, I32, I32, I32, P, P, P, P, F32, I32]),

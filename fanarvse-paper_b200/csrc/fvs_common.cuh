@@ -54,6 +54,9 @@ inline cudaError_t fvs_ensure_smem(const void* func, size_t bytes) {
 
 namespace fvs {
 
+// tiles of one cell part in the cell-major scans' work lists (entries `cell | part << 16`)
+constexpr int CELL_PART_TILES = FVS_CELL_PART_TILES;
+
 constexpr float kNeg = -1e30f;  // the reference's "empty" estimate (`throughput/enginei8.py:48,57`)
 
 // float -> uint32 with the same order (larger float, larger key); NaN is not expected on this path.

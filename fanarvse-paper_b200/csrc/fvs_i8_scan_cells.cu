@@ -156,7 +156,7 @@ __device__ __forceinline__ uint32_t select32(const uint32_t (&a)[32], int jj) {
 // the fields of one cell the producer needs, loaded in stages so that no load is waited on in the iteration that
 // issues it
 struct CellInfo {
-    int cell, cs, ce, qn, qoff;
+    int cell, cs, ce, qn, qoff, part;
 };
 
 template <int MODE>
@@ -255,8 +255,9 @@ __global__ void __launch_bounds__(Layout<MODE>::NTHREADS, Layout<MODE>::CTAS_PER
             // call, so the producer never waits for a load it just issued
             auto grab = [&]() { return atomicAdd(p.sched, 1); };
             auto cell_of = [&](int idx) { return idx < nl ? p.list[idx] : -1; };
-            auto fields = [&](int c) {
-                CellInfo ci{c, 0, 0, 0, 0};
+            auto fields = [&](int e) {  // a list entry: cell | part << 16
+                const int c = e >= 0 ? (e & 0xffff) : -1;
+                CellInfo ci{c, 0, 0, 0, 0, e >= 0 ? e >> 16 : 0};
                 if (c >= 0) {
                     ci.cs = (int)p.off[c];
                     ci.ce = (int)p.off[c + 1];
@@ -282,11 +283,13 @@ __global__ void __launch_bounds__(Layout<MODE>::NTHREADS, Layout<MODE>::CTAS_PER
                 if (ci.cell < 0) {
                     it = Item{-1, 0, 0, 0, 0, 0, 0, 0};
                 } else {
-                    const int first = ci.cs & ~31;
+                    // the part's tiles of the cell's tile grid (which starts at the cell's first 32-row block)
+                    const int grid0 = ci.cs & ~31;
+                    const int first = grid0 + ci.part * CELL_PART_TILES * TILE_ROWS;
+                    const int ntiles = min(CELL_PART_TILES, (ci.ce - first + TILE_ROWS - 1) / TILE_ROWS);
                     const int q0 = grp * RSUB * QN;
                     const int nq = min(RSUB * QN, ci.qn - q0);
-                    it = Item{ci.cell, ci.cs, ci.ce, first, (ci.ce - first + TILE_ROWS - 1) / TILE_ROWS, ci.qoff + q0,
-                              nq, (nq + QN - 1) / QN};
+                    it = Item{ci.cell, ci.cs, ci.ce, first, ntiles, ci.qoff + q0, nq, (nq + QN - 1) / QN};
                 }
                 return it;
             };
@@ -300,7 +303,10 @@ __global__ void __launch_bounds__(Layout<MODE>::NTHREADS, Layout<MODE>::CTAS_PER
             };
             // cells with no pairs (not listed) or no rows (probed, but nothing to scan: the reference launches no
             // program for them) are skipped
-            auto idle = [&](const CellInfo& ci) { return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs); };
+            auto idle = [&](const CellInfo& ci) {  // no pairs, no rows, or a part past the cell's last tile
+                return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs ||
+                                        (ci.cs & ~31) + ci.part * CELL_PART_TILES * TILE_ROWS >= ci.ce);
+            };
             auto advance = [&](CellInfo& ci, int& grp) {
                 grp++;
                 if (ci.cell >= 0 && grp * RSUB * QN < ci.qn) return;
@@ -645,7 +651,8 @@ __global__ void __launch_bounds__(1024) cell_lists_kernel(const int32_t* __restr
     __syncthreads();
     for (int c0 = 0; c0 < NC; c0 += 1024) {
         const int i = c0 + tid;
-        const int c = i < NC ? order[i] : -1;
+        const int e = i < NC ? order[i] : -1;  // cell | part << 16
+        const int c = e >= 0 ? (e & 0xffff) : -1;
         const bool k1 = c >= 0 && ccnt1 && ccnt1[c] > 0;
         const bool k2 = c >= 0 && ccnt[c] > 0;
         const unsigned m1 = __ballot_sync(0xffffffffu, k1), m2 = __ballot_sync(0xffffffffu, k2);
@@ -664,8 +671,8 @@ __global__ void __launch_bounds__(1024) cell_lists_kernel(const int32_t* __restr
             t2 += wsum[1][w];
         }
         const unsigned below = (1u << lane) - 1u;
-        if (k1) list1[b1 + __popc(m1 & below)] = c;
-        if (k2) list[b2 + __popc(m2 & below)] = c;
+        if (k1) list1[b1 + __popc(m1 & below)] = e;
+        if (k2) list[b2 + __popc(m2 & below)] = e;
         __syncthreads();
         if (tid == 0) {
             base[0] += t1;
@@ -691,6 +698,8 @@ extern "C" int fvs_cell_lists(fvs_stream_t stream, const int32_t* order, int NC,
     fvs::cells::cell_lists_kernel<<<1, 1024, 0, stream>>>(order, NC, ccnt1, ccnt, list1, list, nlist, zero, nzero);
     return fvs_launch_status();
 }
+
+extern "C" int fvs_cell_part_tiles(void) { return FVS_CELL_PART_TILES; }
 
 extern "C" int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8, const float* qs, int B, int R,
                                  const int32_t* qid, const int32_t* coff, const int32_t* ccnt, const float* qcp,

@@ -12,9 +12,9 @@
 // then places its pairs: first-pass pairs of cell c at coff[c] + r, the others at coff[c] + cur1[c] + r (each cell's
 // first-pass pairs first, the layout of fvs_pairs_split), writes qid, the pair constant float(QM[q, c]) * mnorm[c] and
 // the first pass's pair slots, and the plain cell into probe.  One more CTA (the last) places no pairs: it writes
-// coff / ccnt / ccnt1, the two passes' cell lists for fvs_i8_scan_cells (order given, non-empty cells) and clears the
-// caller's counters, beside the placing CTAs.  The last CTA to finish clears the cursors, so every call leaves them
-// zero for the next.
+// coff / ccnt / ccnt1, the two passes' work lists for the cell-major scans (the cell-part entries of the order given
+// whose cells have pairs) and clears the caller's counters, beside the placing CTAs.  The last CTA to finish clears
+// the cursors, so every call leaves them zero for the next.
 #include "fvs_common.cuh"
 
 namespace fvs {
@@ -300,7 +300,7 @@ struct PlaceOut {
 __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __restrict__ probe, int B, int nprobe,
                                                                     int n1, int NC, const __half* __restrict__ QM,
                                                                     const float* __restrict__ mnorm,
-                                                                    const int32_t* __restrict__ order,
+                                                                    const int32_t* __restrict__ order, int norder,
                                                                     int32_t* __restrict__ cur1,
                                                                     int32_t* __restrict__ cur2, PlaceOut o) {
     extern __shared__ int s_coff[];  // NC
@@ -342,31 +342,31 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
         }
         for (int i = tid; i < o.nzero; i += PLACE_THREADS) o.zero[i] = 0;
         if (o.list) {
-            // the cells of `order` with first-pass pairs / with any pairs, in that order
+            // the entries (cell | part << 16) of `order` whose cell has first-pass pairs / any pairs, in that order
             __shared__ int wsum[2][32];
             __shared__ int base[2];
             const int lane = tid & 31, warp = tid >> 5;
             if (tid == 0) base[0] = base[1] = 0;
             __syncthreads();
-            for (int c0 = 0; c0 < NC; c0 += LB * PLACE_THREADS) {
-                // the chunk's order entries, then their counts, loaded together; then one pass per 1024 cells
+            for (int c0 = 0; c0 < norder; c0 += LB * PLACE_THREADS) {
+                // the chunk's order entries, then their cells' counts, loaded together; then one pass per 1024
                 int cc[LB], a1[LB], a2[LB];
 #pragma unroll
                 for (int u = 0; u < LB; u++) {
                     const int ii = c0 + u * PLACE_THREADS + tid;
-                    cc[u] = ii < NC ? order[ii] : -1;
+                    cc[u] = ii < norder ? order[ii] : -1;
                 }
 #pragma unroll
                 for (int u = 0; u < LB; u++) {
-                    a1[u] = cc[u] >= 0 ? cur1[cc[u]] : 0;
-                    a2[u] = cc[u] >= 0 ? cur2[cc[u]] : 0;
+                    a1[u] = cc[u] >= 0 ? cur1[cc[u] & 0xffff] : 0;
+                    a2[u] = cc[u] >= 0 ? cur2[cc[u] & 0xffff] : 0;
                 }
 #pragma unroll
                 for (int u = 0; u < LB; u++) {
-                    if (c0 + u * PLACE_THREADS >= NC) break;  // uniform over the block
-                    const int c = cc[u];
-                    const bool k1 = c >= 0 && a1[u] > 0;
-                    const bool k2 = c >= 0 && a1[u] + a2[u] > 0;
+                    if (c0 + u * PLACE_THREADS >= norder) break;  // uniform over the block
+                    const int e = cc[u];  // cell | part << 16
+                    const bool k1 = e >= 0 && a1[u] > 0;
+                    const bool k2 = e >= 0 && a1[u] + a2[u] > 0;
                     const unsigned m1 = __ballot_sync(0xffffffffu, k1), m2 = __ballot_sync(0xffffffffu, k2);
                     if (lane == 0) {
                         wsum[0][warp] = __popc(m1);
@@ -383,8 +383,8 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
                         t2 += wsum[1][w];
                     }
                     const unsigned below = (1u << lane) - 1u;
-                    if (k1) o.list1[b1 + __popc(m1 & below)] = c;
-                    if (k2) o.list[b2 + __popc(m2 & below)] = c;
+                    if (k1) o.list1[b1 + __popc(m1 & below)] = e;
+                    if (k2) o.list[b2 + __popc(m2 & below)] = e;
                     __syncthreads();
                     if (tid == 0) {
                         base[0] += t1;
@@ -420,13 +420,14 @@ __global__ void __launch_bounds__(PLACE_THREADS) pairs_place_kernel(int64_t* __r
 }  // namespace fvs
 
 static int route_pairs_run(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
-                           const float* sc, const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid,
+                           const float* sc, const float* mnorm, const int32_t* order, int norder, int64_t* probe,
+                           int32_t* qid,
                            float* qcp, int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
                            int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work) {
     using namespace fvs::rp;
     FVS_CHECK_ARG(QM && probe && qid && qcp && coff && ccnt && ccnt1 && work && B >= 0 && NC > 0);
     FVS_CHECK_ARG(nprobe >= 1 && nprobe <= NC && n1 >= 1 && n1 <= nprobe && nzero >= 0);
-    FVS_CHECK_ARG(order == nullptr || (list1 && list && nlist));
+    FVS_CHECK_ARG(order == nullptr || (list1 && list && nlist && norder >= 0));
     FVS_CHECK_ARG(nzero == 0 || zero != nullptr);
     if (NC % 8 != 0 || ((uintptr_t)QM & 15) != 0 || nprobe > MAXP || NC > MAX_CELLS) return FVS_ERANGE;
     if (sc != nullptr && ((uintptr_t)sc & 15) != 0) return FVS_ERANGE;
@@ -459,24 +460,25 @@ static int route_pairs_run(fvs_stream_t stream, const uint16_t* QM, int B, int N
     if (e != cudaSuccess) return (int)e;
     PlaceOut o{qid, coff, ccnt, ccnt1, slot, list1, list, nlist, zero, done, qcp, nzero};
     pairs_place_kernel<<<grid + 1, PLACE_THREADS, sm, stream>>>(probe, B, nprobe, n1, NC, (const __half*)QM, mnorm, order,
-                                                            cur1, cur2, o);
+                                                            order ? norder : 0, cur1, cur2, o);
     return fvs_launch_status();
 }
 
 extern "C" int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
-                               const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid, float* qcp,
-                               int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
-                               int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work) {
-    return route_pairs_run(stream, QM, B, NC, nprobe, n1, nullptr, mnorm, order, probe, qid, qcp, coff, ccnt, ccnt1,
-                           slot, list1, list, nlist, zero, nzero, work);
+                               const float* mnorm, const int32_t* order, int norder, int64_t* probe, int32_t* qid,
+                               float* qcp, int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot,
+                               int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero, int nzero,
+                               int32_t* work) {
+    return route_pairs_run(stream, QM, B, NC, nprobe, n1, nullptr, mnorm, order, norder, probe, qid, qcp, coff, ccnt,
+                           ccnt1, slot, list1, list, nlist, zero, nzero, work);
 }
 
 extern "C" int fvs_route_pairs_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1,
-                                      const float* sc, const float* mnorm, const int32_t* order, int64_t* probe,
-                                      int32_t* qid, float* qcp, int32_t* coff, int32_t* ccnt, int32_t* ccnt1,
-                                      int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero,
-                                      int nzero, int32_t* work) {
+                                      const float* sc, const float* mnorm, const int32_t* order, int norder,
+                                      int64_t* probe, int32_t* qid, float* qcp, int32_t* coff, int32_t* ccnt,
+                                      int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist,
+                                      int32_t* zero, int nzero, int32_t* work) {
     FVS_CHECK_ARG(sc != nullptr);
-    return route_pairs_run(stream, QM, B, NC, nprobe, n1, sc, mnorm, order, probe, qid, qcp, coff, ccnt, ccnt1, slot,
-                           list1, list, nlist, zero, nzero, work);
+    return route_pairs_run(stream, QM, B, NC, nprobe, n1, sc, mnorm, order, norder, probe, qid, qcp, coff, ccnt,
+                           ccnt1, slot, list1, list, nlist, zero, nzero, work);
 }

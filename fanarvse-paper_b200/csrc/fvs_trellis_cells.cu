@@ -146,7 +146,7 @@ __device__ __forceinline__ uint32_t select32(const uint32_t (&a)[32], int jj) {
 // the fields of one cell the producer needs, loaded in stages so that no load is waited on in the iteration that
 // issues it
 struct CellInfo {
-    int cell, cs, ce, qn, qoff;
+    int cell, cs, ce, qn, qoff, part;
 };
 
 template <int MODE>
@@ -421,8 +421,9 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
             // call, so the producer never waits for a load it just issued
             auto grab = [&]() { return atomicAdd(p.sched, 1); };
             auto cell_of = [&](int idx) { return idx < nl ? p.list[idx] : -1; };
-            auto fields = [&](int c) {
-                CellInfo ci{c, 0, 0, 0, 0};
+            auto fields = [&](int e) {  // a list entry: cell | part << 16
+                const int c = e >= 0 ? (e & 0xffff) : -1;
+                CellInfo ci{c, 0, 0, 0, 0, e >= 0 ? e >> 16 : 0};
                 if (c >= 0) {
                     ci.cs = (int)p.off[c];
                     ci.ce = (int)p.off[c + 1];
@@ -442,7 +443,10 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
                 return c;
             };
             // cells with no pairs (not listed) or no rows (probed, but nothing to scan) are skipped
-            auto idle = [&](const CellInfo& ci) { return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs); };
+            auto idle = [&](const CellInfo& ci) {  // no pairs, no rows, or a part past the cell's last tile
+                return ci.cell >= 0 && (ci.qn <= 0 || ci.ce <= ci.cs ||
+                                        (ci.cs & ~31) + ci.part * CELL_PART_TILES * TILE_ROWS >= ci.ce);
+            };
             CellInfo cur;
             do {
                 cur = next_cell();
@@ -451,9 +455,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) trellis_cells_kernel(Params p) {
             for (int ni = 0;; ni++) {
                 Item it{-1, 0, 0, 0, 0, 0, 0, 0};
                 if (cur.cell >= 0) {
-                    const int first = cur.cs & ~31;
-                    it = Item{cur.cell, cur.cs, cur.ce, first, (cur.ce - first + TILE_ROWS - 1) / TILE_ROWS,
-                              cur.qoff + g * QN, min(QN, cur.qn - g * QN), 1};
+                    // the part's tiles of the cell's tile grid (which starts at the cell's first 32-row block)
+                    const int first = (cur.cs & ~31) + cur.part * CELL_PART_TILES * TILE_ROWS;
+                    it = Item{cur.cell, cur.cs, cur.ce, first,
+                              min(CELL_PART_TILES, (cur.ce - first + TILE_ROWS - 1) / TILE_ROWS), cur.qoff + g * QN,
+                              min(QN, cur.qn - g * QN), 1};
                 }
                 const int s = ni % I_STAGES;
                 if (!mbar_wait(i_empty(s), ((ni / I_STAGES) & 1) ^ 1, abort, WL)) break;

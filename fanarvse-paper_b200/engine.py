@@ -20,6 +20,20 @@ from ._lib import check, ptr
 BN = 32
 
 
+def cell_part_order(off, order, part_tiles, tile_rows=128):
+    """Work-list order of the cell-major scans: the cells of `order` (largest first), each as its parts
+    p = 0 .. ceil(tiles / part_tiles) - 1, entries `cell | p << 16` (FVS_CELL_PART_TILES; a cell's tiles of tile_rows
+    rows start at its first 32-row block), so that several CTAs share a large cell.  int32 numpy array."""
+    off = np.asarray(off, np.int64)
+    order = np.asarray(order, np.int64)
+    assert len(off) - 1 < 65536, "cell ids of the work lists are 16-bit"
+    cs, ce = off[order], off[order + 1]
+    ntiles = np.where(ce > cs, (ce - (cs & ~31) + tile_rows - 1) // tile_rows, 0)
+    parts = np.maximum(1, (ntiles + part_tiles - 1) // part_tiles)
+    within = np.arange(int(parts.sum())) - np.repeat(np.cumsum(parts) - parts, parts)
+    return (np.repeat(order, parts) | (within << 16)).astype(np.int32)
+
+
 def static_tiles(off, tile_rows):
     """Static work list of the int8 scan: for every non-empty cell, tiles of `tile_rows` rows starting on the cell's
     first global 32-row boundary (`src/s1cell.py:157-168` uses 32-row blocks; a tile here is tile_rows/32 of them).
@@ -88,8 +102,12 @@ class IndexI8:
         self.H16 = f(H16, torch.float16)
         self.d = self.H16.shape[1]
         sizes = np.diff(self.off_np)
-        # cells largest first: the order in which the cell-major scan hands cells out (big cells early, small at the end)
-        self.cell_order = f(np.argsort(-sizes, kind="stable").astype(np.int32), torch.int32)
+        # cells largest first: the order in which the cell-major scan hands cells out (big cells early, small at the end);
+        # as work-list entries, a large cell as several parts
+        order = np.argsort(-sizes, kind="stable").astype(np.int32)
+        self.cell_order = f(order, torch.int32)
+        self.cell_parts = f(cell_part_order(self.off_np, order, _lib.lib().fvs_cell_part_tiles()), torch.int32)
+        self.NP = int(self.cell_parts.numel())
         tc, tr, self.MB = static_tiles(self.off_np, _lib.lib().fvs_i8_tile_rows())
         self.tile_cell, self.tile_row0 = f(tc, torch.int32), f(tr, torch.int32)
         self.ntiles = len(tc)
@@ -181,10 +199,10 @@ class EngineB200I8:
         pass's counters) is cleared in the same launch."""
         ix = self.ix
         dev = ccnt.device
-        list1 = torch.empty(ix.NC, dtype=torch.int32, device=dev)
-        lst = torch.empty(ix.NC, dtype=torch.int32, device=dev)
+        list1 = torch.empty(ix.NP, dtype=torch.int32, device=dev)
+        lst = torch.empty(ix.NP, dtype=torch.int32, device=dev)
         nl = torch.empty(2, dtype=torch.int32, device=dev)
-        self._call("cell_lists", self.L.fvs_cell_lists, ptr(ix.cell_order), ix.NC, ptr(ccnt1), ptr(ccnt), ptr(list1),
+        self._call("cell_lists", self.L.fvs_cell_lists, ptr(ix.cell_parts), ix.NP, ptr(ccnt1), ptr(ccnt), ptr(list1),
                    ptr(lst), ptr(nl), ptr(zero), 0 if zero is None else zero.numel())
         return list1, lst, nl
 
@@ -193,7 +211,7 @@ class EngineB200I8:
         if self.SCAN == "cells":
             lst, nl = lists
             self._call(name, self.L.fvs_i8_scan_cells, mode, ptr(q8), ptr(qs), B, ix.R, ptr(qid), ptr(coff),
-                       ptr(ccnt), ptr(qcp), ptr(lst), ptr(nl), ix.NC, ptr(ix.off), ix.NC, ptr(ix.Z), ix.N, ptr(ix.zs),
+                       ptr(ccnt), ptr(qcp), ptr(lst), ptr(nl), ix.NP, ptr(ix.off), ix.NC, ptr(ix.Z), ix.N, ptr(ix.zs),
                        ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB, ptr(self.sched),
                        ptr(self.status))
         elif self.SCAN == "tc":
@@ -278,12 +296,13 @@ class EngineB200I8:
         n = B * nprobe
         qid = torch.empty(n, dtype=torch.int32, device=dev)
         qcp = torch.empty(n, device=dev)
-        coff, ccnt, ccnt1, list1, lst = (torch.empty(ix.NC, dtype=torch.int32, device=dev) for _ in range(5))
+        coff, ccnt, ccnt1 = (torch.empty(ix.NC, dtype=torch.int32, device=dev) for _ in range(3))
+        list1, lst = (torch.empty(ix.NP, dtype=torch.int32, device=dev) for _ in range(2))
         slot = torch.empty(B * n1, dtype=torch.int32, device=dev)
         nl = torch.empty(2, dtype=torch.int32, device=dev)
         cnt = torch.empty(B, dtype=torch.int32, device=dev)
         self._call("route_pairs", self.L.fvs_route_pairs, ptr(QM), B, ix.NC, nprobe, n1, ptr(ix.mnorm),
-                   ptr(ix.cell_order), ptr(probe), ptr(qid), ptr(qcp), ptr(coff), ptr(ccnt), ptr(ccnt1), ptr(slot),
+                   ptr(ix.cell_parts), ix.NP, ptr(probe), ptr(qid), ptr(qcp), ptr(coff), ptr(ccnt), ptr(ccnt1), ptr(slot),
                    ptr(list1), ptr(lst), ptr(nl), ptr(cnt), B, ptr(work))
         self.launches += 1   # two kernels
         return probe, (qid, coff, ccnt, ccnt1, qcp, slot, list1, lst, nl, cnt)

@@ -14,7 +14,7 @@ import torch
 
 from . import _lib
 from ._lib import ptr
-from .engine import BN, EngineB200I8, static_tiles
+from .engine import BN, EngineB200I8, cell_part_order, static_tiles
 
 
 class IndexS:
@@ -58,8 +58,12 @@ class IndexS:
         self.H16 = f(H16, torch.float16)
         self.d = self.H16.shape[1]
         sizes = np.diff(self.off_np)
-        # cells largest first: the order in which the cell-major scan hands cells out
-        self.cell_order = f(np.argsort(-sizes, kind="stable").astype(np.int32), torch.int32)
+        # cells largest first: the order in which the cell-major scan hands cells out; as work-list entries, a large cell
+        # as several parts
+        order = np.argsort(-sizes, kind="stable").astype(np.int32)
+        self.cell_order = f(order, torch.int32)
+        self.cell_parts = f(cell_part_order(self.off_np, order, _lib.lib().fvs_cell_part_tiles()), torch.int32)
+        self.NP = int(self.cell_parts.numel())
         tc, tr, self.MB = static_tiles(self.off_np, _lib.lib().fvs_trellis_tile_rows())
         self.tile_cell, self.tile_row0 = f(tc, torch.int32), f(tr, torch.int32)
         self.ntiles = len(tc)
@@ -114,7 +118,7 @@ class EngineB200S(EngineB200I8):
         if lists is not None:
             lst, nl = lists
             self._call(name, self.L.fvs_trellis_scan_cells, mode, ptr(Qh), B, ix.R, ptr(qid), ptr(coff), ptr(ccnt),
-                       ptr(qcp), ptr(lst), ptr(nl), ix.NC, ptr(ix.off), ix.NC, ptr(ix.words), ix.W, ptr(ix.tab), ix.L,
+                       ptr(qcp), ptr(lst), ptr(nl), ix.NP, ptr(ix.off), ix.NC, ptr(ix.words), ix.W, ptr(ix.tab), ix.L,
                        ptr(ix.scale1), ptr(t0), ptr(cnt), ptr(bval), ptr(bpos), M, ptr(bmc), ix.MB, ptr(self.sched),
                        ptr(self.status))
             return
@@ -146,12 +150,13 @@ class EngineB200S(EngineB200I8):
         n = B * nprobe
         qid = torch.empty(n, dtype=torch.int32, device=dev)
         qcp = torch.empty(n, device=dev)
-        coff, ccnt, ccnt1, list1, lst = (torch.empty(ix.NC, dtype=torch.int32, device=dev) for _ in range(5))
+        coff, ccnt, ccnt1 = (torch.empty(ix.NC, dtype=torch.int32, device=dev) for _ in range(3))
+        list1, lst = (torch.empty(ix.NP, dtype=torch.int32, device=dev) for _ in range(2))
         slot = torch.empty(B * n1, dtype=torch.int32, device=dev)
         nl = torch.empty(2, dtype=torch.int32, device=dev)
         cnt = torch.empty(B, dtype=torch.int32, device=dev)
         self._call("route_pairs", self.L.fvs_route_pairs_scaled, ptr(QM), B, ix.NC, nprobe, n1, ptr(ix.inv_mnorm),
-                   ptr(ix.mnorm), ptr(ix.cell_order), ptr(probe), ptr(qid), ptr(qcp), ptr(coff), ptr(ccnt), ptr(ccnt1),
+                   ptr(ix.mnorm), ptr(ix.cell_parts), ix.NP, ptr(probe), ptr(qid), ptr(qcp), ptr(coff), ptr(ccnt), ptr(ccnt1),
                    ptr(slot), ptr(list1), ptr(lst), ptr(nl), ptr(cnt), B, ptr(work))
         self.launches += 1   # two kernels
         return probe, (qid, coff, ccnt, ccnt1, qcp, slot, list1, lst, nl, cnt)

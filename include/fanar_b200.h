@@ -103,18 +103,29 @@ int fvs_pairs_noalloc(fvs_stream_t stream, const int64_t* probe, int B, int npro
                       int32_t* slot);
 
 /*
+ * Cell parts: the cell-major scans (fvs_i8_scan_cells, fvs_trellis_scan_cells) take their work from lists whose
+ * entries are `cell | part << 16`: part p of a cell covers its 128-row tiles p*FVS_CELL_PART_TILES ..
+ * (p+1)*FVS_CELL_PART_TILES - 1 (tiles start at the cell's first 32-row block), so that several CTAs share a large
+ * cell.  An order that lists every cell once with part 0 (plain cell ids) is a valid order for cells of at most
+ * FVS_CELL_PART_TILES tiles.  Cell ids below 65536.
+ */
+#define FVS_CELL_PART_TILES 8
+int fvs_cell_part_tiles(void);
+
+/*
  * Routing selection and both pair lists in two launches (replaces fvs_route_topk + fvs_pairs_split + fvs_cell_lists
  * on the throughput path: the reference's `QM.topk(nprobe)` and `pairs_fast`, `throughput/enginei8.py:11-16, 67-70`).
  * probe [B, nprobe] as fvs_route_topk; qid / qcp / coff / ccnt / ccnt1 / slot as fvs_pairs_split with first-pass
- * columns j < n1; when order is given (cells largest first), list1 / list / nlist as fvs_cell_lists.  zero[0..nzero)
+ * columns j < n1; when order is given (norder cell-part entries, largest cells first), list1 / list / nlist as
+ * fvs_cell_lists (list capacity norder).  zero[0..nzero)
  * is cleared.  work: 2*NC + 1 int32 that are zero before the first call; every call leaves them zero (a call's cursors
  * are cleared by its last CTA), so calls on one stream can share them.  NC % 8 == 0, NC <= 16384, nprobe <= 512, QM
  * 16-byte aligned; other shapes return FVS_ERANGE (the three separate entry points take them).
  */
 int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1, const float* mnorm,
-                    const int32_t* order, int64_t* probe, int32_t* qid, float* qcp, int32_t* coff, int32_t* ccnt,
-                    int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist, int32_t* zero,
-                    int nzero, int32_t* work);
+                    const int32_t* order, int norder, int64_t* probe, int32_t* qid, float* qcp, int32_t* coff,
+                    int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list, int32_t* nlist,
+                    int32_t* zero, int nzero, int32_t* work);
 
 /*
  * fvs_route_pairs with a per-cell routing scale: the nprobe cells of largest float(QM[q, c]) * sc[c] (fp32 product,
@@ -125,9 +136,9 @@ int fvs_route_pairs(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int 
  * as fvs_route_pairs.
  */
 int fvs_route_pairs_scaled(fvs_stream_t stream, const uint16_t* QM, int B, int NC, int nprobe, int n1, const float* sc,
-                           const float* mnorm, const int32_t* order, int64_t* probe, int32_t* qid, float* qcp,
-                           int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1, int32_t* list,
-                           int32_t* nlist, int32_t* zero, int nzero, int32_t* work);
+                           const float* mnorm, const int32_t* order, int norder, int64_t* probe, int32_t* qid,
+                           float* qcp, int32_t* coff, int32_t* ccnt, int32_t* ccnt1, int32_t* slot, int32_t* list1,
+                           int32_t* list, int32_t* nlist, int32_t* zero, int nzero, int32_t* work);
 
 /* Rows per tile of the int8 scan (a multiple of the reference's 32-row block).  Host-side helper. */
 int fvs_i8_tile_rows(void);
@@ -263,9 +274,10 @@ int fvs_trellis_tile_rows(void);
 
 /*
  * The int8 stage-1 scan organised by cells (same contract and results as fvs_i8_scan_tc; replaces the same reference
- * kernels, `throughput/ivf8c_kern.py:2-36`): the CTAs take the cells of `list` (nlist[0] of them, a device count) one at
- * a time with an atomicAdd on sched[0]; a cell's queries are gathered once and held while all of its code tiles are
- * scanned; a tile is fetched as the 32-row blocks the cell occupies.  maxlist >= the count (sizes the grid: NC).
+ * kernels, `throughput/ivf8c_kern.py:2-36`): the CTAs take the cell parts of `list` (nlist[0] entries
+ * `cell | part << 16`, a device count; see FVS_CELL_PART_TILES) one at a time with an atomicAdd on sched[0]; a part's
+ * queries (the cell's) are gathered once and held while its code tiles are scanned; a tile is fetched as the 32-row
+ * blocks the cell occupies.  maxlist >= the count (sizes the grid: the list's capacity).
  * sched: 2 int32, zero before the first launch; every launch leaves them zero (the last CTA resets them), so calls on
  * one stream can share them, while calls that may run at the same time need their own.  Other arguments as
  * fvs_i8_scan_tc (mode 0 reads the first pass's per-cell counts, mode 1 the emit pass's).
@@ -278,8 +290,9 @@ int fvs_i8_scan_cells(fvs_stream_t stream, int mode, const int8_t* q8, const flo
 
 /*
  * The work lists of fvs_i8_scan_cells for both passes (new; the reference launches one program per (cell, block)):
- * the cells of `order` [NC] (a permutation of the cells, largest first) with ccnt1[c] > 0 into list1 and with
- * ccnt[c] > 0 into list, in that order; nlist[0], nlist[1] = their lengths (device).  ccnt1 may be NULL (no list1).
+ * the entries of `order` [NC] (cell-part entries, see FVS_CELL_PART_TILES: every part of every cell once, largest
+ * cells first) whose cell c has ccnt1[c] > 0 into list1 and ccnt[c] > 0 into list, in that order; nlist[0], nlist[1]
+ * = their lengths (device), the lists' capacity NC entries.  ccnt1 may be NULL (no list1).
  * zero[0..nzero) is set to 0 in the same launch (the emit pass's per-query counters; zero may be NULL when nzero = 0).
  */
 int fvs_cell_lists(fvs_stream_t stream, const int32_t* order, int NC, const int32_t* ccnt1, const int32_t* ccnt,

@@ -125,6 +125,7 @@ def _random_index(eng, n, d, nlist, nq, seed, comps=32):
     (20000, 256, 64, 33, 40, 64, 10, 4096),       # every cell probed
     (20000, 256, 64, 1, 40, 12, 10, 4096),        # batch 1
     (12000, 256, 16, 450, 40, 12, 10, 4096),      # up to 450 queries per cell: cells scanned in several query groups
+    (24000, 256, 8, 200, 40, 4, 10, 8192),        # cells of ~3000 rows: the cell-major scan takes each as 3 parts
 ])
 @pytest.mark.parametrize("scan", ["cells", "tc", "small", "mma"])
 def test_search_matches_oracle(eng, n, d, nlist, nq, K, nprobe, k, M, scan):
@@ -426,7 +427,8 @@ def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1, scaled):
     fvs_route_topk, the pair layout of fvs_pairs_split and the lists of fvs_cell_lists, also through tied scores; its
     cursors are left zero, so a second call on the same work buffer gives the same result.  fvs_route_pairs_scaled
     (scaled = 1: pair constants with the norm factor, 2: without, as the default engine) gives the probe list of
-    fvs_route_topk_scaled, also through scores tied after the scaling."""
+    fvs_route_topk_scaled, also through scores tied after the scaling.  The order is given as cell-part entries
+    (cell | part << 16, some cells in two or three parts): the lists hold the entries whose cells have pairs."""
     L = pkg("_lib")
     lib = L.lib()
     rng = np.random.default_rng(B + NC)
@@ -436,7 +438,11 @@ def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1, scaled):
         mnorm = np.ones(NC, np.float32)           # no norm factor: the kernel's constant float(QM) equals QM * 1
     sc = np.where(rng.random(NC) < 0.5, 1.0, rng.random(NC) + 0.5).astype(np.float32)   # many equal scales
     order = np.argsort(-rng.integers(0, 50, NC), kind="stable").astype(np.int32)
-    tq, tm, to, tsc = (torch.from_numpy(x).to(DEV) for x in (QM, mnorm, order, sc))
+    nparts = np.where(rng.random(NC) < 0.2, rng.integers(2, 4, NC), 1)
+    within = np.arange(int(nparts.sum())) - np.repeat(np.cumsum(nparts) - nparts, nparts)
+    oe = (np.repeat(order, nparts) | (within << 16)).astype(np.int32)   # cell-part entries
+    NP = len(oe)
+    tq, tm, to, tsc = (torch.from_numpy(x).to(DEV) for x in (QM, mnorm, oe, sc))
     mptr = None if scaled == 2 else L.ptr(tm)
     work = torch.zeros(2 * NC + 1, dtype=torch.int32, device=DEV)
     outs = []
@@ -444,11 +450,12 @@ def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1, scaled):
         probe = torch.empty(B, npr, dtype=torch.int64, device=DEV)
         qid = torch.empty(B * npr, dtype=torch.int32, device=DEV)
         qcp = torch.empty(B * npr, device=DEV)
-        coff, ccnt, ccnt1, l1, l2 = (torch.empty(NC, dtype=torch.int32, device=DEV) for _ in range(5))
+        coff, ccnt, ccnt1 = (torch.empty(NC, dtype=torch.int32, device=DEV) for _ in range(3))
+        l1, l2 = (torch.empty(NP, dtype=torch.int32, device=DEV) for _ in range(2))
         slot = torch.empty(B * n1, dtype=torch.int32, device=DEV)
         nl = torch.empty(2, dtype=torch.int32, device=DEV)
         zero = torch.ones(B, dtype=torch.int32, device=DEV)
-        tail = (L.ptr(to), L.ptr(probe), L.ptr(qid), L.ptr(qcp), L.ptr(coff), L.ptr(ccnt), L.ptr(ccnt1), L.ptr(slot),
+        tail = (L.ptr(to), NP, L.ptr(probe), L.ptr(qid), L.ptr(qcp), L.ptr(coff), L.ptr(ccnt), L.ptr(ccnt1), L.ptr(slot),
                 L.ptr(l1), L.ptr(l2), L.ptr(nl), L.ptr(zero), B, L.ptr(work))
         if scaled:
             L.check(lib.fvs_route_pairs_scaled(L.stream_handle(), L.ptr(tq), B, NC, npr, n1, L.ptr(tsc), mptr, *tail),
@@ -497,9 +504,10 @@ def test_route_pairs_matches_separate_kernels(eng, B, NC, npr, n1, scaled):
     got = np.array([qcp[pos_of[(int(q), int(cc))]] for q, cc in zip(qa, pc)], np.float32)
     np.testing.assert_array_equal(got, want)
     # cell lists: the cells of `order` with pairs
-    np.testing.assert_array_equal(nl, [int((on1[order] > 0).sum()), int((on[order] > 0).sum())])
-    np.testing.assert_array_equal(l1[:nl[0]], order[on1[order] > 0])
-    np.testing.assert_array_equal(l2[:nl[1]], order[on[order] > 0])
+    cells = oe & 0xffff
+    np.testing.assert_array_equal(nl, [int((on1[cells] > 0).sum()), int((on[cells] > 0).sum())])
+    np.testing.assert_array_equal(l1[:nl[0]], oe[on1[cells] > 0])
+    np.testing.assert_array_equal(l2[:nl[1]], oe[on[cells] > 0])
 
 
 def test_quantize_matches_reference_formula(eng):

@@ -277,6 +277,18 @@ def test_search_matches_oracle_synthetic(ec, synth_index, K, nprobe, k, scan):
     assert r >= 0.9, r
 
 
+@pytest.fixture(scope="module")
+def synth_index_big_cells(ec):
+    """16 cells of ~3750 rows (about 30 tiles): the cell-major scan's work lists hold each as several parts"""
+    synth, ib = pkg("synth"), pkg("index_build")
+    ds = synth.make_dataset(synth.MixtureSpec(n=60000, d=384, comps=16, nq=200, seed=9), DEV, gt_k=10)
+    X16 = ds["base16"]
+    s1, _, codes = ib.build_index(X16, 16, R=256, refine_bits=960, seed=9, kmeans_sample=60000, uniform=False,
+                                  lloyd=True)
+    s1.update(ib.build_trellis(X16, s1, seed=9))
+    return ds, ec.IndexS(s1, codes["lloyd"], X16, DEV), s1, codes["lloyd"]
+
+
 @pytest.mark.parametrize("B,nprobe", [(300, 64), (300, 128), (40, 128)])
 def test_cells_scan_matches_tile_scan(ec, synth_index, B, nprobe):
     """the tcgen05 cell-major scan against the mma.sync tile scan on the same pair lists: first-pass block maxima and
@@ -284,9 +296,24 @@ def test_cells_scan_matches_tile_scan(ec, synth_index, B, nprobe):
     query groups); the two accumulate the fp32 dot in different orders, so values agree within TOL and emitted sets
     are equal except items within TOL of the threshold."""
     ds, ix, _, _ = synth_index
+    _cells_vs_tile(ec, ds, ix, B, nprobe, 200, groups=B > 128)
+
+
+@pytest.mark.parametrize("B,nprobe", [(200, 4), (40, 8)])
+def test_cells_scan_parts_match_tile_scan(ec, synth_index_big_cells, B, nprobe):
+    """the same comparison on cells of about 30 tiles, which the cell-major scan takes as parts of at most
+    fvs_cell_part_tiles() tiles (several CTAs per cell)"""
+    ds, ix, _, _ = synth_index_big_cells
+    part = pkg("_lib").lib().fvs_cell_part_tiles()
+    sizes = np.diff(ix.off_np)
+    assert sizes.max() > 2 * 128 * part and ix.NP > ix.NC
+    _cells_vs_tile(ec, ds, ix, B, nprobe, 400, M=65536)
+
+
+def _cells_vs_tile(ec, ds, ix, B, nprobe, K, groups=False, M=None):
     Ec, Em = _engine(ec, ix, "cells"), _engine(ec, ix, "mma")
+    Ec.M = Em.M = M
     Q = ds["queries"][:B].contiguous()
-    K = 200
     QM, probe = Ec.route(Q, nprobe)
     Qh = (Q @ ix.W1).half().contiguous()
     pc, okc, ec1 = Ec.stage1_trellis(Q, QM, probe, K, Qh=Qh)
@@ -295,7 +322,7 @@ def test_cells_scan_matches_tile_scan(ec, synth_index, B, nprobe):
     Lm = Em._last
     torch.cuda.synchronize()
     assert int(Ec.status) == 0
-    if B > 128:
+    if groups:
         assert c(Lc["ccnt"]).max() > 128      # a cell with several query groups
     MB, n1 = ix.MB, Lc["n1"]
     # the block maxima of every first-pass pair (q, j < n1), found through each run's own slot (the order of a cell's
