@@ -2,18 +2,20 @@
 //
 // Same contract and arithmetic as fvs_i8_scan_tc (the reference's `_first8c` / `_emit8c`,
 // `throughput/ivf8c_kern.py:2-36`), organised around cells instead of 128-row tiles:
-//   * work items are cells, handed out dynamically: the producer thread of a CTA takes the next entry of a compact list
-//     of the pass's non-empty cells (largest first) with one atomicAdd, so CTAs finish together whatever the cells'
-//     sizes and query counts;
-//   * a cell's queries (up to RSUB sub-tiles of QN) are gathered ONCE into shared memory and stay there while all of
-//     the cell's 128-row code tiles stream past them (a cell of ~250 rows spans 2-3 tiles; the tile scan gathered them
-//     once per tile); cells with more queries are split into groups of RSUB sub-tiles, each group streaming the
-//     cell's tiles again (from L2);
+//   * work items are cell parts, handed out dynamically: the producer thread of a CTA takes the next entry of a
+//     compact list of the pass's non-empty cells (largest first) with one atomicAdd, so CTAs finish together whatever
+//     the cells' sizes and query counts; an entry is `cell | part << 16`, part p covering tiles 8p .. 8p+7 of the
+//     cell, so that a large cell (the index's largest hold thousands of rows) is shared by several CTAs instead of
+//     setting the pass's tail;
+//   * a part's queries (the cell's, up to RSUB sub-tiles of QN) are gathered ONCE into shared memory and stay there
+//     while the part's 128-row code tiles stream past them (a cell of ~250 rows spans 2-3 tiles; the tile scan
+//     gathered them once per tile); cells with more queries are split into groups of RSUB sub-tiles, each group
+//     streaming the part's tiles again (from L2);
 //   * a code tile is fetched as the 32-row blocks the cell occupies, one TMA copy per K-half with a box of 32, 64, 96
 //     or 128 rows (four tensor maps), so the rows past the cell's end are not moved; K-half 1 lands right after
 //     K-half 0's blocks.
 // Warp roles (640 threads, one CTA per SM; see Shape):
-//   warp 0      : lane 0 takes cells (atomicAdd on sched[0]; the list entry, bounds and pair range of a cell are
+//   warp 0      : lane 0 takes cell parts (atomicAdd on sched[0]; the list entry, bounds and pair range of a cell are
 //                 loaded ahead in stages), publishes each work item (cell, group of sub-tiles) in a ring of I_STAGES
 //                 slots up to AHEAD items ahead, and issues the TMA loads of the item's code tiles into A_STAGES stages
 //   warp 1      : TMEM allocation; lane 0 issues tcgen05.mma.kind::i8 (M=128 rows, N=16..64 queries, K=256 as 8 x 32)
@@ -52,8 +54,8 @@ static_assert(AHEAD + 2 <= I_STAGES, "an item's slot is not reused before the pr
 
 // Pipeline shape per pass: one CTA per SM with 4 code-tile stages, 4 query sub-tile stages (two sub-tiles per item),
 // 8 TMEM accumulators and 4 epilogue warpgroups.  (Two CTAs per SM with half of each, measured for the first pass:
-// 87 -> 74 us at 1M rows and 4096 cells, but 0.37 -> 0.63 ms at 2M rows and 8192 cells, where the CTAs that stream
-// the largest cells alone set the pass time and half a pipeline doubles that tail.)
+// 82 -> 68 us at 1M rows and 4096 cells, but 0.19 -> 0.28 ms at 2M rows and 8192 cells, where the last CTAs' parts
+// set the pass time and half a pipeline lengthens that tail.)
 template <int MODE>
 struct Shape;
 template <>

@@ -6,8 +6,9 @@
 //   value_j = fp16(tab[state_j]),  state_j = ((w[j/32] << 32 | w[j/32+1]) >> (64 - L - j%32)) & (2^L - 1),
 //   est = scale1[n] * dot(fp16 q', value) + qcp   (dot accumulated in fp32, product and sum rounded separately),
 // then block maxima per 32-row block (mode 0, first pass) or the threshold emit est >= t0[q] (mode 1).
-// Work items are (cell, group of up to QN = 128 of its queries), handed out dynamically (cells largest first).  An
-// item's queries are gathered once and held while the cell's 128-row tiles pass; each tile x item is ONE sequence of
+// Work items are (cell part, group of up to QN = 128 of its queries), handed out dynamically (cells largest first;
+// list entries `cell | part << 16`, part p covering tiles 8p .. 8p+7 of the cell, so that several CTAs share a large
+// cell).  An item's queries are gathered once and held while the part's 128-row tiles pass; each tile x item is ONE sequence of
 // 16 tcgen05.mma.kind::f16 (M = 128 rows, N = the item's queries rounded up to 16, K = 16 each), since the issue cost
 // of an MMA hardly depends on N.  The code tile is not copied but decoded in the CTA: two sets of four decode warps,
 // one tile row per lane, read the row's words (prefetched one tile ahead) and write its fp16 values, two per lookup of
@@ -20,7 +21,7 @@
 //                 and an accumulator after the tile's last chunk
 //   warps 9-10  : gather, items alternating: fp16 query rows picked by qid, copied with cp.async (an item's rows in
 //                 flight at once) into the swizzled layout; column metadata (qid, pair constant, threshold)
-//   warp 11     : lane 0 takes cells (atomicAdd on sched[0], cell fields loaded ahead in stages) and publishes the
+//   warp 11     : lane 0 takes cell parts (atomicAdd on sched[0], cell fields loaded ahead in stages) and publishes the
 //                 work items in a ring of I_STAGES slots
 //   warps 12-23 : three epilogue warpgroups, tiles alternating between them
 // The last CTA to finish resets sched[0..1].  Every mbarrier wait is bounded; on expiry the CTA raises `status`,
