@@ -4,8 +4,8 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P bench.py --gpus N
 
 A step is one search of a batch of B queries through the engine (one CUDA-graph replay plus the recompute of any
-flagged queries).  On one GPU the timed loops keep two searches in flight (`search_async`: step i is launched before
-step i-1's results are collected), as a serving loop would; every step completes inside the timed region.  Data: the
+flagged queries).  The timed loops keep two searches in flight (`search_async`: step i is launched before step i-1's
+results are collected), as a serving loop would; every step completes inside the timed region.  Data: the
 synthetic Gaussian-mixture stand-in for the reference's 1M x 1536 set (seed 0), index built on the GPU with the
 reference's recipe.  The operating point (nprobe, K, M) is the fastest of a small frontier grid that reaches
 recall@10 >= 0.99 against brute-force ground truth, as the reference picks its frontier rows
@@ -805,17 +805,15 @@ def main():
     E.prewarm(Q0, K, z, npr, k)
     I = search(Q0, K, z, npr, k)
     rec = pkg("synth").recall(I.cpu(), gt.cpu(), 10)
-    # ---- timed region: device-resident inputs.  One GPU: a serving loop with two searches in flight
-    # (search_async: step i is launched before step i-1's results are collected, so the host's collection overlaps the
-    # GPU's next search; every step completes inside the timed region); the sharded search is synchronous.
+    # ---- timed region: device-resident inputs.  A serving loop with two searches in flight (search_async, of the
+    # engine on one GPU and of the sharded search on N: step i is launched before step i-1's results are collected,
+    # so the host's collection overlaps the GPU's next search; every step completes inside the timed region).
+    launcher = E.sharded.search_async if world > 1 else E.search_async
+
     def run_steps(n):
-        if world > 1:
-            for i in range(n):
-                search(Qs[i % 4], K, z, npr, k)
-            return
         pend = None
         for i in range(n):
-            h = E.search_async(Qs[i % 4], K, z, npr, k)
+            h = launcher(Qs[i % 4], K, z, npr, k)
             if pend is not None:
                 pend.result()
             pend = h
@@ -883,10 +881,9 @@ def main():
     consumed = [torch.cuda.Event() for _ in range(2)]
     step_ev = [torch.cuda.Event(True) for _ in range(args.steps + 1)]
 
-    # one GPU: two searches in flight through search_async (step i is launched before step i-1's results are
-    # collected and copied out, so the host's collection overlaps the GPU's next search); the sharded search is
-    # synchronous
-    launch = None if world > 1 else (lambda Q: E.search_async(Q, K, z, npr, k))
+    # two searches in flight through search_async (step i is launched before step i-1's results are collected and
+    # copied out, so the host's collection overlaps the GPU's next search)
+    launch = lambda Q: launcher(Q, K, z, npr, k)
 
     def prefetch(i, n, cur, reads_done=None):
         # the next step's queries into the other buffer, once step i-1 has read it: its graph (consumed) and, when
@@ -909,26 +906,18 @@ def main():
         for i in range(n):
             cur = i % 2
             torch.cuda.current_stream().wait_event(landed[cur])
-            if launch is None:
-                prefetch(i, n, cur)
-                Ir = search(Qd[cur], K, z, npr, k)
-                consumed[cur].record()
-                Ih.copy_(Ir.to(torch.int32), non_blocking=True)
-                if events:
-                    events[i + 1].record()
-                continue
             h = launch(Qd[cur])
             consumed[cur].record()
             rd = None
             if pend is not None:
-                Ih.copy_(pend.result()[0], non_blocking=True)   # step i-1's ids to the host
+                Ih.copy_(pend.result()[0].to(torch.int32), non_blocking=True)   # step i-1's ids to the host
                 rd = pend.reads_done
                 if events:
                     events[i].record()
             prefetch(i, n, cur, rd)
             pend = h
         if pend is not None:
-            Ih.copy_(pend.result()[0], non_blocking=True)
+            Ih.copy_(pend.result()[0].to(torch.int32), non_blocking=True)
             if events:
                 events[n].record()
         torch.cuda.current_stream().wait_stream(cs)

@@ -58,6 +58,7 @@ class ShardedSearch:
         self.exact = exact or (lambda Qb, I: exact_scores(self.local, Qb, I))
         self.merge = merge or merge_topk
         self.graphs = {}
+        self._slot = {}            # per step shape: the graph the next search_async replays (two alternate)
         self.eager_steps = 0
 
     def close(self):
@@ -101,7 +102,29 @@ class ShardedSearch:
             I, reads, _ = self.local.search(Qb, K, z, nprobe, k)
             Ig, Sg = self._exchange(Qb, I, k)
             return Ig, Sg, reads
+        h = self._launch(Qb, K, z, nprobe, k, 0)
+        res = h.result()
+        if h.reads_done is not None:
+            h.reads_done.synchronize()
+        return res
+
+    def search_async(self, Qb, K, z, nprobe, k):
+        """`search` split in two, as EngineB200I8.search_async: launches the step (one graph replay; the steps of one
+        shape alternate between two graphs with their own buffers) and returns a handle whose `result()` waits for
+        that step alone and returns what `search` returns.  Call `result()` of a handle before launching the step
+        after the next.  Every rank must launch and collect its steps in the same order: the collectives inside the
+        graphs, and those of a recompute beyond the graph's capacity (run inside `result()`, on all ranks together),
+        then keep one order across ranks.  Qb stays unchanged until `result()` has returned and, when the handle's
+        `reads_done` is an event, until that event."""
+        if not Qb.is_cuda or not hasattr(self.local, "_gpu"):
+            return _ShardDone(self.search(Qb, K, z, nprobe, k))
         key = (len(Qb), K, z, nprobe, k, self.local.knobs())
+        slot = self._slot.get(key, 0)
+        self._slot[key] = slot ^ 1
+        return self._launch(Qb, K, z, nprobe, k, slot)
+
+    def _launch(self, Qb, K, z, nprobe, k, slot):
+        key = (len(Qb), K, z, nprobe, k, self.local.knobs()) + ((("slot", slot),) if slot else ())
         if key not in self.graphs:
             qs = Qb.clone()
             st = torch.cuda.Stream()
@@ -115,35 +138,76 @@ class ShardedSearch:
             n0 = self.local.launches
             hf = torch.empty(3, dtype=torch.int32, pin_memory=True)
             with torch.cuda.graph(g):
-                outs = self._graph_body(qs, K, z, nprobe, k)
-                _, _, reads, _, Ig, Sg, flags = outs
-                # the step's results as one int32 block (reads and global ids as int64 words first, then the scores),
-                # so that one copy takes them out of the graph's buffers; the flags go to pinned host memory
+                ok, I, reads, _, Ig, Sg, flags = self._graph_body(qs, K, z, nprobe, k)
+                # the step's results as one int32 block: reads and global ids as int64 words, the merged scores, and
+                # for the recompute path the local ids and exactness flags; one copy takes them out of the graph's
+                # buffers.  The flags summed over ranks go to pinned host memory.
                 packed = torch.cat([reads.view(torch.int32), Ig.reshape(-1).view(torch.int32),
-                                    Sg.reshape(-1).view(torch.int32)])
+                                    Sg.reshape(-1).view(torch.int32), I.reshape(-1).to(torch.int32),
+                                    ok.to(torch.int32)])
                 hf.copy_(flags, non_blocking=True)
-            self.graphs[key] = (g, qs, outs, packed, hf.numpy(), self.local.launches - n0 + 2)  # + exact, merge
-        g, qs, (ok, I, reads, ids, Ig, Sg, flags), packed, f, nl = self.graphs[key]
+            self.graphs[key] = (g, qs, packed, hf.numpy(), self.local.launches - n0 + 2)  # + exact, merge
+        g, qs, packed, f, nl = self.graphs[key]
         qs.copy_(Qb)
         g.replay()
         self.local.replayed_launches = getattr(self.local, "replayed_launches", 0) + nl
         P = packed.clone()
-        torch.cuda.current_stream().synchronize()              # the only synchronisation
+        done = torch.cuda.Event()
+        done.record()
+        return _ShardPending(self, (Qb, K, z, nprobe, k, P, f), done)
+
+    def _collect(self, Qb, K, z, nprobe, k, P, f):
+        """after a replay has completed: status, flagged-row accounting, and the eager recompute + exchange when some
+        rank has flagged rows beyond its graph's capacity (every rank takes that path together); returns the results
+        and whether the recompute ran"""
+        B = len(Qb)
+        n = B * k
+        reads = P[:2 * B].view(torch.int64)
+        Ig = P[2 * B:2 * B + 2 * n].view(torch.int64).view(B, k)
+        Sg = P[2 * B + 2 * n:2 * B + 3 * n].view(torch.float32).view(B, k)
         self.local.nbad += int(f[2])
         if int(f[1]) != 0:
             raise _lib.FvsError("sharded search: a bounded device wait expired on some rank (status flag set)")
         if int(f[0]) == 0:
-            B, n = len(Qb), Ig.numel()
-            return (P[2 * B:2 * B + 2 * n].view(torch.int64).view(B, k),
-                    P[2 * B + 2 * n:].view(torch.float32).view(B, k), P[:2 * B].view(torch.int64))
+            return (Ig, Sg, reads), False
         # some rank has flagged rows left: every rank recomputes its own (possibly none) and exchanges again
         self.eager_steps += 1
         E = self.local
-        I, reads = I.clone(), reads.clone()
+        I = P[2 * B + 3 * n:2 * B + 4 * n].view(B, k)
+        ok = P[2 * B + 4 * n:] != 0
         bad = torch.nonzero(~ok).flatten().cpu()
         if len(bad):
             a, b, _ = E._fallback_graphed(Qb, bad, K, z, nprobe, k)
             badd = bad.to(Qb.device)
-            I[badd], reads[badd] = a, b
+            I[badd], reads[badd] = a.to(I.dtype), b
         Ig, Sg = self._exchange(Qb, I, k)
-        return Ig, Sg, reads
+        return (Ig, Sg, reads), True
+
+
+class _ShardPending:
+    """A launched sharded step (`ShardedSearch.search_async`): result() waits for its replay (its own event) and
+    collects it; `reads_done` as in EngineB200I8.search_async."""
+
+    def __init__(self, sh, args, done):
+        self._sh, self._args, self._done, self._res = sh, args, done, None
+        self.reads_done = None
+
+    def result(self):
+        if self._res is None:
+            self._done.synchronize()                             # the only synchronisation
+            self._res, recomputed = self._sh._collect(*self._args)
+            if recomputed:
+                self.reads_done = torch.cuda.Event()
+                self.reads_done.record()
+        return self._res
+
+
+class _ShardDone:
+    """An eager step's result, in the handle form of search_async."""
+
+    def __init__(self, res):
+        self._res = res
+        self.reads_done = None
+
+    def result(self):
+        return self._res

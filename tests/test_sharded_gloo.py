@@ -76,6 +76,8 @@ def _worker(rank, world, port, outdir, fail_rank):
     try:
         I, Sc, reads = S.search(Q, 40, 1.25, 10, 10)
         Il, _, _ = S.local.search(Q, 40, 1.25, 10, 10)
+        Ia, Sa, _ = S.search_async(Q, 40, 1.25, 10, 10).result()      # the handle form takes the same exchange
+        assert torch.equal(Ia, I) and torch.equal(Sa, Sc), "search_async differs from search"
         np.savez(os.path.join(outdir, f"r{rank}.npz"), I=I.numpy(), S=Sc.numpy(), local=Il.numpy() + rank * n,
                  local_s=exact(Q, Il).numpy())
         status = "ok"
