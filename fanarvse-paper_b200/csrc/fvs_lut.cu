@@ -390,8 +390,15 @@ __global__ void __launch_bounds__(256, 3) lut_score_zq_kernel(const int64_t* __r
 // lanes reading one (ga, c) touch at most 16 consecutive words, conflict-free) and a per-word list (table block,
 // tier, plane weight); each lane then streams its record in 32-byte steps (two steps in flight) and folds each
 // finished tier as delta_t * (a_t - mid_t * qsum_t) * scale_t, the reference's per-tier form.  No warp reduction per
-// candidate; about 40 instructions per plane word.
+// candidate.
 constexpr int LC_THREADS = 128;
+
+// fp32 load from a 32-bit address in the shared window
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
 
 template <bool HALF>
 __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __restrict__ pos, int K,
@@ -403,7 +410,12 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
     extern __shared__ __align__(16) uint8_t smem[];
     __shared__ float s_qsum[MAX_TIERS], s_qn2[MAX_TIERS];
     const int nblk = D / 32, nwords = ts.nwords;
-    float* tab = reinterpret_cast<float*>(smem);                   // nblk * 128
+    // the table starts on a 256-byte boundary of the shared window (the launch reserves 256 bytes for it), so that
+    // every lookup address is one byte permutation of a block base and the word's nibble offsets
+    const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(smem);
+    const uint32_t pad = (256u - (sbase & 255u)) & 255u;
+    const uint32_t tab_s = sbase + pad;
+    float* tab = reinterpret_cast<float*>(smem + pad);             // nblk * 128
     uint2* wmeta = reinterpret_cast<uint2*>(tab + nblk * 128);  // per word: (table byte offset | tier << 24, 2^(b-1-p))
     const int q = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t qK = (int64_t)q * K;
@@ -522,16 +534,19 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
                 ct = t;
                 at = 0.f;
             }
-            const char* E = reinterpret_cast<const char*>(tab) + (m.x & 0xffffffu);
+            // the word's table block (512 bytes, groups 0..7 of 16 entries) starts at A, a multiple of 256; the
+            // entries of byte bi sit at A + 128 bi + (high nibble: 4 v, low nibble: 64 + 4 v).  Byte bi of ho / lo is
+            // that offset's low 8 bits (128 (bi & 1) + [64] + 4 v < 256) and A + 256 (bi >> 1) supplies the rest, so
+            // one byte permutation forms each lookup address
+            const uint32_t A = tab_s + (m.x & 0xffffffu);
             const uint32_t wd = wd8[u];
-            // byte bi of ho / lo: 4 x the high / low nibble of the word's byte bi, i.e. the byte offsets of entries
-            // (32 bi + high nibble) and (32 bi + 16 + low nibble) past 128 bi bytes
-            const uint32_t ho = (wd >> 2) & 0x3C3C3C3Cu, lo = (wd << 2) & 0x3C3C3C3Cu;
+            const uint32_t ho = ((wd >> 2) & 0x3C3C3C3Cu) | 0x80008000u, lo = ((wd << 2) & 0x3C3C3C3Cu) | 0xC040C040u;
             float a = 0.f;
 #pragma unroll
-            for (int bi = 0; bi < 4; bi++)
-                a += *reinterpret_cast<const float*>(E + 128 * bi + __byte_perm(ho, 0u, 0x4440u | bi)) +
-                     *reinterpret_cast<const float*>(E + 128 * bi + 64 + __byte_perm(lo, 0u, 0x4440u | bi));
+            for (int bi = 0; bi < 4; bi++) {
+                const uint32_t base = bi < 2 ? A : A + 256u;
+                a += lds_f32(__byte_perm(ho, base, 0x7650u | bi)) + lds_f32(__byte_perm(lo, base, 0x7650u | bi));
+            }
             at += a * __uint_as_float(m.y);
         }
     }
@@ -700,7 +715,7 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     const fvs::RecSet rs{rec, RB, soff};
     if (B >= fvs_sm_count() && ts.T <= fvs::MAX_TIERS && ts.nwords <= 4 * RB / 16) {
         // large batch: one candidate per thread
-        const size_t smc = (size_t)(D / 32) * 128 * 4 + (size_t)ts.nwords * 8;
+        const size_t smc = (size_t)(D / 32) * 128 * 4 + (size_t)ts.nwords * 8 + 256;   // + the table's alignment
         const dim3 grid(B, (K + fvs::LC_THREADS - 1) / fvs::LC_THREADS);
         cudaError_t e = half ? fvs_ensure_smem((const void*)fvs::lut_cand_kernel<true>, smc)
                              : fvs_ensure_smem((const void*)fvs::lut_cand_kernel<false>, smc);
