@@ -428,9 +428,12 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
                               __float_as_uint(ts.pw[t][p]));
     }
     // group g = 4-coordinate group (block g / 8, group g % 8) holds coordinates 4g .. 4g+3.  Entry v sums the selected
-    // coordinates left to right in fp32, as acc += z_i * bit_i does; built incrementally: entry v = entry (v without
-    // its last selected coordinate) + that coordinate, the same additions in the same order.
-    for (int g = tid; g < nblk * 8; g += LC_THREADS) {
+    // coordinates left to right in fp32 from 0, as acc += z_i * bit_i does (bit 8 of v selects z0, 4 z1, 2 z2, 1 z3).
+    // Four threads build a group, thread x its entries 4x .. 4x+3 (z0, z1 selected by x): the prefix p over z0, z1,
+    // then p, p + z3, p + z2, (p + z2) + z3 -- the same additions in the same order; consecutive threads store
+    // consecutive 16-byte quarters (conflict-free).
+    for (int gx = tid; gx < nblk * 32; gx += LC_THREADS) {
+        const int g = gx >> 2, x = gx & 3;
         float z[4];
         if (zh) {
             const uint2 h = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(Zq) +
@@ -443,22 +446,16 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
                                                                     (int64_t)q * ldz + 4 * g));
             z[0] = f.x, z[1] = f.y, z[2] = f.z, z[3] = f.w;
         }
-        float e[16];
-        e[0] = 0.f;
+        float p = 0.f;
+        if (x & 2) p = __fadd_rn(p, z[0]);
+        if (x & 1) p = __fadd_rn(p, z[1]);
+        const float p2 = __fadd_rn(p, z[2]);
+        float o[4] = {p, __fadd_rn(p, z[3]), p2, __fadd_rn(p2, z[3])};
+        if (HALF) {
 #pragma unroll
-        for (int v = 1; v < 16; v++) {
-            const int lowbit = v & -v;  // the last selected coordinate: bit 8 = z0, 4 = z1, 2 = z2, 1 = z3
-            const int ci = lowbit == 8 ? 0 : lowbit == 4 ? 1 : lowbit == 2 ? 2 : 3;
-            e[v] = __fadd_rn(e[v & (v - 1)], z[ci]);
+            for (int u = 0; u < 4; u++) o[u] = __half2float(__float2half_rn(o[u]));
         }
-        float4* dst = reinterpret_cast<float4*>(tab + 16 * g);
-#pragma unroll
-        for (int v4 = 0; v4 < 4; v4++) {
-            float o[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) o[u] = HALF ? __half2float(__float2half_rn(e[4 * v4 + u])) : e[4 * v4 + u];
-            dst[v4] = make_float4(o[0], o[1], o[2], o[3]);
-        }
+        reinterpret_cast<float4*>(tab)[gx] = make_float4(o[0], o[1], o[2], o[3]);
     }
     for (int t = warp; t < ts.T; t += LC_THREADS / 32) {
         float a = 0.f, b = 0.f;
@@ -523,11 +520,13 @@ __global__ void __launch_bounds__(LC_THREADS) lut_cand_kernel(const int64_t* __r
         n1a = n2a;
         n1b = n2b;
         ld(k + 2, n2a, n2b);
+        uint4 mp;
 #pragma unroll
         for (int u = 0; u < 8; u++) {
             const int w = 8 * k + u;
             if (w >= nwords) break;
-            const uint2 m = wmeta[w];
+            if ((u & 1) == 0) mp = reinterpret_cast<const uint4*>(wmeta)[w >> 1];   // the entries of words w, w + 1
+            const uint2 m = (u & 1) ? make_uint2(mp.z, mp.w) : make_uint2(mp.x, mp.y);
             const int t = (int)(m.x >> 24);
             if (t != ct) {
                 fold(ct, at);
@@ -715,7 +714,8 @@ extern "C" int fvs_lut_score_rec(fvs_stream_t stream, const int64_t* pos, int B,
     const fvs::RecSet rs{rec, RB, soff};
     if (B >= fvs_sm_count() && ts.T <= fvs::MAX_TIERS && ts.nwords <= 4 * RB / 16) {
         // large batch: one candidate per thread
-        const size_t smc = (size_t)(D / 32) * 128 * 4 + (size_t)ts.nwords * 8 + 256;   // + the table's alignment
+        // the table, the word list padded to whole 8-word steps (read in pairs), the table's alignment
+        const size_t smc = (size_t)(D / 32) * 128 * 4 + (size_t)((ts.nwords + 7) & ~7) * 8 + 256;
         const dim3 grid(B, (K + fvs::LC_THREADS - 1) / fvs::LC_THREADS);
         cudaError_t e = half ? fvs_ensure_smem((const void*)fvs::lut_cand_kernel<true>, smc)
                              : fvs_ensure_smem((const void*)fvs::lut_cand_kernel<false>, smc);
