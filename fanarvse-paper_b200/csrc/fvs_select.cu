@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(NT, 1024 / NT) select_topk_reg_kernel(
     }
     if (!placed && n > K) {
         const int nv = (n + 4 * NT - 1) / (4 * NT);  // uniform over the block
-        if (n > SELR_MAXM)
+        if (n > SELR_MAXM || n > 32 * NT)  // more than 8 keys per thread: from global memory
             select_glob_cut<NT>(bv, bp, n, K, sh);
         else if (nv <= 1)
             select_reg_cut<NT, 1>(bv, bp, n, K, sh);
@@ -782,6 +782,9 @@ extern "C" int fvs_select_topk(fvs_stream_t stream, const float* bval, const int
         if (B < fvs_sm_count())  // a small batch: 32 warps per query
             fvs::select_topk_reg_kernel<1024><<<B, 1024, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt,
                                                                       delta, delta_idx);
+        else if (K <= 128)
+            fvs::select_topk_reg_kernel<128><<<B, 128, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt, delta,
+                                                                    delta_idx);
         else if (K <= 256)
             fvs::select_topk_reg_kernel<256><<<B, 256, 0, stream>>>(bval, bpos, cnt, M, K, pos, est1, ok, ncnt, delta,
                                                                     delta_idx);
